@@ -1,0 +1,1348 @@
+// C ABI of libfunasr_dec: context, weights, page pool, sequences, the batched
+// decoder forward (captured as CUDA graphs), greedy generation and the
+// kernel-level entry points. See include/funasr_dec.h for the contract.
+//
+// One forward over M rows launches, per layer:
+//   residual_rmsnorm  (x += down-proj partials of the previous layer; f16 norm)
+//   q8_gemm   QKV     (Wq|Wk|Wv concatenated: N = 4096)      -> split-K partials
+//   qknorm_rope_append (sums the partials, writes q and the f16 K/V pages)
+//   paged_attention (+ split combine)                         -> f16 [M][2048]
+//   q8_gemm   o_proj                                          -> partials
+//   residual_rmsnorm  (x += o; f16 post-attention norm)
+//   q8_gemm   gate|up (N = 2*ffn)                             -> partials
+//   swiglu                                                    -> f16 [M][ffn]
+//   q8_gemm   down                                            -> partials
+// then the final residual_rmsnorm, the lm_head GEMM with a fused argmax and
+// the argmax reduce. This is the node list of the reference's per-token ggml
+// graph (compute/llm_ops_gpu.cpp:155-207) with the copies removed and every
+// elementwise op folded into a neighbour.
+#include "fa_kernels.cuh"
+#include "page_alloc.hpp"
+#include "funasr_dec.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_err;
+
+struct LayerW {
+    int8_t* qkv_q = nullptr; __half* qkv_d = nullptr;
+    int8_t* o_q = nullptr;   __half* o_d = nullptr;
+    int8_t* gu_q = nullptr;  __half* gu_d = nullptr;
+    int8_t* dn_q = nullptr;  __half* dn_d = nullptr;
+    float* in_norm = nullptr;
+    float* post_norm = nullptr;
+    float* q_norm = nullptr;
+    float* k_norm = nullptr;
+};
+
+struct Seq {
+    bool open = false;
+    int len = 0;
+    int max_tokens = 0;
+    std::vector<int> pages;
+};
+
+constexpr int kD = 128;
+constexpr int kHq = 16;
+constexpr int kHkv = 8;
+constexpr size_t kPageElems = (size_t)kHkv * 2 * fa::kPageTokens * kD;
+
+std::mutex g_cfg_mu;
+bool g_configured[64] = {};
+
+}  // namespace
+
+// Kernel attribute set-up, once per device (before any graph capture).
+namespace fa {
+void configure_attention();
+void configure_gemm();
+}  // namespace fa
+
+static int ensure_configured() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return FA_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_cfg_mu);
+    if (dev >= 0 && dev < 64 && !g_configured[dev]) {
+        fa::configure_attention();
+        fa::configure_gemm();
+        g_configured[dev] = true;
+    }
+    return FA_OK;
+}
+
+struct fa_ctx {
+    int device = 0;
+    fa_model_desc d{};
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int n_sm = 148;
+    std::string err;
+
+    bool loaded = false;
+    std::vector<LayerW> L;
+    void* embed = nullptr;
+    int embed_type = FA_TYPE_BF16;
+    float* final_norm = nullptr;
+    int8_t* lm_q = nullptr;
+    __half* lm_d = nullptr;
+    std::vector<void*> dev_allocs;
+
+    __half* pool = nullptr;
+    size_t layer_stride = 0;   // elements between layers of the pool
+    int n_pages = 0;
+    int* bt_dev = nullptr;
+    int bt_stride = 0;
+    float2* rope = nullptr;
+    fa::PageAllocator palloc;
+    std::vector<Seq> seqs;
+
+    // step buffers
+    float* x = nullptr;
+    __half* xn16 = nullptr;
+    float* part = nullptr;
+    size_t part_elems = 0;
+    float* q_rot = nullptr;
+    __half* attn16 = nullptr;
+    __half* h16 = nullptr;
+    float* att_po = nullptr;
+    float* att_pml = nullptr;
+    int att_max_splits = 0;
+    float* amax_v = nullptr;
+    int* amax_i = nullptr;
+    float* logits_dev = nullptr;
+    int* row_tok = nullptr;
+    int* row_slot = nullptr;
+    int* row_pos = nullptr;
+    int* next_dev = nullptr;
+    int* upd_idx = nullptr;
+    int* upd_page = nullptr;
+    int max_updates = 0;
+    int* err_dev = nullptr;
+    int* scratch_ints = nullptr;   // compaction / synthetic-fill page lists
+    int scratch_ints_n = 0;
+
+    // pinned host staging
+    int* h_rows = nullptr;     // tok | slot | pos | upd_idx | upd_page
+    int* h_next = nullptr;
+    int* h_err = nullptr;
+
+    bool use_graphs = true;
+    std::map<uint64_t, cudaGraphExec_t> graphs;
+
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_ev;   // pairs per attention launch
+    int prof_n = 0;
+    int last_launches = 0;
+    cudaEvent_t ev_t0 = nullptr, ev_t1 = nullptr;
+};
+
+#define FA_CK(call)                                                                    \
+    do {                                                                               \
+        cudaError_t e_ = (call);                                                       \
+        if (e_ != cudaSuccess) {                                                       \
+            return set_err(ctx, FA_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+        }                                                                              \
+    } while (0)
+
+static int set_err(const fa_ctx* cctx, int code, const std::string& msg) {
+    if (cctx) const_cast<fa_ctx*>(cctx)->err = msg;
+    g_err = msg;
+    return code;
+}
+
+template <typename T>
+static int dev_alloc(fa_ctx* ctx, T** p, size_t bytes) {
+    void* v = nullptr;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(ctx, FA_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + " B): " + cudaGetErrorString(e));
+    }
+    ctx->dev_allocs.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    return FA_OK;
+}
+
+// ------------------------------------------------------------------ basics --
+extern "C" const char* fa_version(void) { return "funasr_dec sm_100a 0.1"; }
+
+extern "C" const char* fa_last_error(const fa_ctx* ctx) { return ctx ? ctx->err.c_str() : g_err.c_str(); }
+
+extern "C" void fa_default_desc(fa_model_desc* d) {
+    if (!d) return;
+    std::memset(d, 0, sizeof(*d));
+    d->n_layers = 28;
+    d->hidden = 1024;
+    d->n_heads = 16;
+    d->n_kv_heads = 8;
+    d->head_dim = 128;
+    d->ffn = 3072;
+    d->vocab = 151936;
+    d->rope_base = 1000000.0f;
+    d->rms_eps = 1e-5f;
+    d->max_ctx = 40960;
+    d->n_pages = 0;
+    d->kv_bytes = (size_t)4 << 30;
+    d->max_seqs = 256;
+    d->max_rows = 512;
+}
+
+static int validate_desc(const fa_model_desc* d) {
+    if (!d) return set_err(nullptr, FA_ERR_INVALID_ARG, "desc is NULL");
+    if (d->head_dim != kD || d->n_heads != kHq || d->n_kv_heads != kHkv)
+        return set_err(nullptr, FA_ERR_INVALID_ARG,
+                       "kernels are built for head_dim 128, 16 query heads, 8 KV heads");
+    if (d->n_layers <= 0 || d->hidden <= 0 || d->hidden % 64 || d->ffn <= 0 || d->ffn % 64 || d->vocab <= 0 ||
+        d->vocab % 64)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "n_layers > 0; hidden, ffn, vocab multiples of 64 required");
+    if (d->max_ctx <= 0 || d->max_seqs <= 0 || d->max_rows <= 0 || d->max_rows > 4096)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "max_ctx, max_seqs > 0 and 0 < max_rows <= 4096 required");
+    if (!(d->rms_eps > 0.0f) || !(d->rope_base > 0.0f))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "rms_eps and rope_base must be positive");
+    return FA_OK;
+}
+
+static int max_split_for(int K) { return std::max(1, K / 128); }
+
+extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
+    if (validate_desc(desc) != FA_OK) return nullptr;
+    int n_dev = 0;
+    cudaError_t e = cudaGetDeviceCount(&n_dev);
+    if (e != cudaSuccess || n_dev == 0) {
+        set_err(nullptr, FA_ERR_CUDA, std::string("no CUDA device: ") + cudaGetErrorString(e));
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (device < 0 || device >= n_dev) {
+        set_err(nullptr, FA_ERR_INVALID_ARG, "device " + std::to_string(device) + " out of range");
+        return nullptr;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        set_err(nullptr, FA_ERR_CUDA, "cudaSetDevice failed");
+        return nullptr;
+    }
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major != 10) {
+        set_err(nullptr, FA_ERR_CUDA,
+                std::string("this library is built for sm_100a (B200); device is ") + prop.name);
+        return nullptr;
+    }
+    if (ensure_configured() != FA_OK) {
+        set_err(nullptr, FA_ERR_CUDA, "kernel configuration failed");
+        return nullptr;
+    }
+    fa_ctx* ctx = new fa_ctx();
+    ctx->device = device;
+    ctx->d = *desc;
+    ctx->n_sm = prop.multiProcessorCount;
+    auto fail = [&](void) -> fa_ctx* {
+        g_err = ctx->err;
+        fa_destroy(ctx);
+        return nullptr;
+    };
+    if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_err(ctx, FA_ERR_CUDA, "cudaStreamCreate failed");
+        return fail();
+    }
+    ctx->stream = ctx->own_stream;
+    const fa_model_desc& d = ctx->d;
+
+    // page pool
+    const size_t page_bytes_all = kPageElems * 2 * (size_t)d.n_layers;
+    int n_pages = d.n_pages;
+    if (n_pages <= 0) n_pages = (int)std::max<size_t>(1, d.kv_bytes / page_bytes_all);
+    ctx->n_pages = n_pages;
+    ctx->layer_stride = (size_t)n_pages * kPageElems;
+    if (dev_alloc(ctx, &ctx->pool, page_bytes_all * n_pages)) return fail();
+    ctx->palloc.init(n_pages);
+    ctx->bt_stride = (d.max_ctx + fa::kPageTokens - 1) / fa::kPageTokens;
+    if (dev_alloc(ctx, &ctx->bt_dev, sizeof(int) * (size_t)d.max_seqs * ctx->bt_stride)) return fail();
+    if (cudaMemset(ctx->bt_dev, 0, sizeof(int) * (size_t)d.max_seqs * ctx->bt_stride) != cudaSuccess) {
+        set_err(ctx, FA_ERR_CUDA, "memset block table");
+        return fail();
+    }
+    ctx->seqs.resize(d.max_seqs);
+
+    // RoPE table: theta = pos * base^(-2i/128) in double, cos/sin in double, f32 once.
+    {
+        std::vector<float2> tab((size_t)d.max_ctx * (kD / 2));
+        double inv[kD / 2];
+        for (int i = 0; i < kD / 2; ++i) inv[i] = std::pow((double)d.rope_base, -2.0 * i / (double)kD);
+        for (int p = 0; p < d.max_ctx; ++p)
+            for (int i = 0; i < kD / 2; ++i) {
+                const double th = (double)p * inv[i];
+                tab[(size_t)p * (kD / 2) + i] = make_float2((float)std::cos(th), (float)std::sin(th));
+            }
+        if (dev_alloc(ctx, &ctx->rope, sizeof(float2) * tab.size())) return fail();
+        if (cudaMemcpy(ctx->rope, tab.data(), sizeof(float2) * tab.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+            set_err(ctx, FA_ERR_CUDA, "rope table upload");
+            return fail();
+        }
+    }
+
+    // step buffers
+    const int R = d.max_rows;
+    const int qkv_n = (kHq + 2 * kHkv) * kD;
+    const size_t part_cols = std::max({(size_t)qkv_n * max_split_for(d.hidden), (size_t)d.hidden * max_split_for(kHq * kD),
+                                       (size_t)2 * d.ffn * max_split_for(d.hidden), (size_t)d.hidden * max_split_for(d.ffn)});
+    ctx->part_elems = part_cols * R;
+    ctx->att_max_splits = 64;
+    ctx->max_updates = R + 64;
+    if (dev_alloc(ctx, &ctx->x, sizeof(float) * R * d.hidden) ||
+        dev_alloc(ctx, &ctx->xn16, sizeof(__half) * R * std::max(d.hidden, d.ffn)) ||
+        dev_alloc(ctx, &ctx->part, sizeof(float) * ctx->part_elems) ||
+        dev_alloc(ctx, &ctx->q_rot, sizeof(float) * R * kHq * kD) ||
+        dev_alloc(ctx, &ctx->attn16, sizeof(__half) * R * kHq * kD) ||
+        dev_alloc(ctx, &ctx->h16, sizeof(__half) * R * d.ffn) ||
+        dev_alloc(ctx, &ctx->att_po, sizeof(float) * (size_t)R * kHq * ctx->att_max_splits * kD) ||
+        dev_alloc(ctx, &ctx->att_pml, sizeof(float) * (size_t)R * kHq * ctx->att_max_splits * 2) ||
+        dev_alloc(ctx, &ctx->amax_v, sizeof(float) * (size_t)R * (d.vocab / 64)) ||
+        dev_alloc(ctx, &ctx->amax_i, sizeof(int) * (size_t)R * (d.vocab / 64)) ||
+        dev_alloc(ctx, &ctx->row_tok, sizeof(int) * R) || dev_alloc(ctx, &ctx->row_slot, sizeof(int) * R) ||
+        dev_alloc(ctx, &ctx->row_pos, sizeof(int) * R) || dev_alloc(ctx, &ctx->next_dev, sizeof(int) * R) ||
+        dev_alloc(ctx, &ctx->upd_idx, sizeof(int) * ctx->max_updates * 64) ||
+        dev_alloc(ctx, &ctx->upd_page, sizeof(int) * ctx->max_updates * 64) ||
+        dev_alloc(ctx, &ctx->err_dev, sizeof(int)))
+        return fail();
+    ctx->max_updates *= 64;
+    if (cudaMemset(ctx->err_dev, 0, sizeof(int)) != cudaSuccess) {
+        set_err(ctx, FA_ERR_CUDA, "memset err");
+        return fail();
+    }
+    const size_t h_ints = 3 * (size_t)R + 2 * (size_t)ctx->max_updates;
+    if (cudaMallocHost(&ctx->h_rows, sizeof(int) * h_ints) != cudaSuccess ||
+        cudaMallocHost(&ctx->h_next, sizeof(int) * (size_t)R * 4096) != cudaSuccess ||
+        cudaMallocHost(&ctx->h_err, sizeof(int)) != cudaSuccess) {
+        set_err(ctx, FA_ERR_OOM, "cudaMallocHost failed");
+        return fail();
+    }
+    if (cudaEventCreate(&ctx->ev_t0) != cudaSuccess || cudaEventCreate(&ctx->ev_t1) != cudaSuccess) {
+        set_err(ctx, FA_ERR_CUDA, "event create");
+        return fail();
+    }
+    return ctx;
+}
+
+static void clear_graphs(fa_ctx* ctx) {
+    for (auto& kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
+    ctx->graphs.clear();
+}
+
+extern "C" void fa_destroy(fa_ctx* ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    clear_graphs(ctx);
+    for (void* p : ctx->dev_allocs) cudaFree(p);
+    if (ctx->logits_dev) cudaFree(ctx->logits_dev);
+    if (ctx->scratch_ints) cudaFree(ctx->scratch_ints);
+    if (ctx->h_rows) cudaFreeHost(ctx->h_rows);
+    if (ctx->h_next) cudaFreeHost(ctx->h_next);
+    if (ctx->h_err) cudaFreeHost(ctx->h_err);
+    for (auto e : ctx->prof_ev) cudaEventDestroy(e);
+    if (ctx->ev_t0) cudaEventDestroy(ctx->ev_t0);
+    if (ctx->ev_t1) cudaEventDestroy(ctx->ev_t1);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+}
+
+extern "C" int fa_set_stream(fa_ctx* ctx, void* stream) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    cudaSetDevice(ctx->device);
+    FA_CK(cudaStreamSynchronize(ctx->stream));
+    ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+    return FA_OK;
+}
+
+extern "C" int fa_set_graphs(fa_ctx* ctx, int enable) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    ctx->use_graphs = enable != 0;
+    return FA_OK;
+}
+
+extern "C" int fa_pool_info(const fa_ctx* ctx, int* n_pages, int* n_free, size_t* page_bytes) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (n_pages) *n_pages = ctx->n_pages;
+    if (n_free) *n_free = ctx->palloc.n_free();
+    if (page_bytes) *page_bytes = kPageElems * 2 * (size_t)ctx->d.n_layers;
+    return FA_OK;
+}
+
+// ----------------------------------------------------------------- weights --
+namespace {
+
+struct TensorSpec {
+    const fa_tensor_view* v = nullptr;
+};
+
+float bf16_to_f32(uint16_t b) {
+    uint32_t u = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+float f16_to_f32_host(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+
+}  // namespace
+
+static int find_tensor(fa_ctx* ctx, const std::unordered_map<std::string, const fa_tensor_view*>& m,
+                       const std::string& name, int type_q8, int64_t ne0, int64_t ne1,
+                       const fa_tensor_view** out) {
+    auto it = m.find(name);
+    if (it == m.end()) return set_err(ctx, FA_ERR_WEIGHTS, "missing tensor " + name);
+    const fa_tensor_view* v = it->second;
+    if (v->ne[0] != ne0 || (ne1 > 0 && v->ne[1] != ne1))
+        return set_err(ctx, FA_ERR_WEIGHTS,
+                       name + ": shape [" + std::to_string(v->ne[0]) + ", " + std::to_string(v->ne[1]) +
+                           "], expected [" + std::to_string(ne0) + ", " + std::to_string(ne1) + "]");
+    if (type_q8 && v->type != FA_TYPE_Q8_0)
+        return set_err(ctx, FA_ERR_WEIGHTS, name + ": expected Q8_0 (type 8), got type " + std::to_string(v->type));
+    if (!type_q8 && v->type != FA_TYPE_F32 && v->type != FA_TYPE_F16 && v->type != FA_TYPE_BF16)
+        return set_err(ctx, FA_ERR_WEIGHTS, name + ": expected F32/F16/BF16");
+    const size_t elems = (size_t)v->ne[0] * (size_t)(v->ne[1] > 0 ? v->ne[1] : 1);
+    const size_t want = type_q8 ? elems / 32 * 34 : elems * (v->type == FA_TYPE_F32 ? 4 : 2);
+    if (v->nbytes != want || !v->data)
+        return set_err(ctx, FA_ERR_WEIGHTS, name + ": " + std::to_string(v->nbytes) + " bytes, expected " +
+                                                std::to_string(want));
+    *out = v;
+    return FA_OK;
+}
+
+static int upload_vec_f32(fa_ctx* ctx, const fa_tensor_view* v, float** dst) {
+    const size_t n = (size_t)v->ne[0];
+    std::vector<float> h(n);
+    for (size_t i = 0; i < n; ++i) {
+        if (v->type == FA_TYPE_F32) h[i] = reinterpret_cast<const float*>(v->data)[i];
+        else if (v->type == FA_TYPE_BF16) h[i] = bf16_to_f32(reinterpret_cast<const uint16_t*>(v->data)[i]);
+        else h[i] = f16_to_f32_host(reinterpret_cast<const uint16_t*>(v->data)[i]);
+    }
+    if (int rc = dev_alloc(ctx, dst, sizeof(float) * n)) return rc;
+    FA_CK(cudaMemcpy(*dst, h.data(), sizeof(float) * n, cudaMemcpyHostToDevice));
+    return FA_OK;
+}
+
+// Repack a GGUF Q8_0 tensor with N rows of K into (q, d) at row offset r0 (d has ldn columns).
+static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, int8_t* q,
+                     __half* dsc, int ldn) {
+    FA_CK(cudaMemcpyAsync(staging, v->data, v->nbytes, cudaMemcpyHostToDevice, ctx->stream));
+    fa::launch_repack_q8(staging, N, K, r0, 0, q, dsc, ldn, ctx->stream);
+    FA_CK(cudaGetLastError());
+    FA_CK(cudaStreamSynchronize(ctx->stream));
+    return FA_OK;
+}
+
+extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n) {
+    if (!ctx || (!tensors && n > 0)) return set_err(ctx, FA_ERR_INVALID_ARG, "bad arguments");
+    if (ctx->loaded) return set_err(ctx, FA_ERR_INVALID_ARG, "weights already loaded");
+    cudaSetDevice(ctx->device);
+    const fa_model_desc& d = ctx->d;
+    std::unordered_map<std::string, const fa_tensor_view*> m;
+    for (int i = 0; i < n; ++i)
+        if (tensors[i].name) m[tensors[i].name] = &tensors[i];
+    const int H = d.hidden, F = d.ffn, V = d.vocab, QD = kHq * kD, KD = kHkv * kD;
+
+    // validate everything first
+    const fa_tensor_view *emb, *fnorm, *lm;
+    int rc;
+    if ((rc = find_tensor(ctx, m, "llm.model.embed_tokens.weight", 0, H, V, &emb))) return rc;
+    if ((rc = find_tensor(ctx, m, "llm.model.norm.weight", 0, H, 0, &fnorm))) return rc;
+    if ((rc = find_tensor(ctx, m, "llm.lm_head.weight", 1, H, V, &lm))) return rc;
+    struct LV { const fa_tensor_view *q, *k, *v, *o, *g, *u, *dn, *qn, *kn, *in, *post; };
+    std::vector<LV> lv(d.n_layers);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const std::string p = "llm.model.layers." + std::to_string(l) + ".";
+        LV& t = lv[l];
+        if ((rc = find_tensor(ctx, m, p + "self_attn.q_proj.weight", 1, H, QD, &t.q))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "self_attn.k_proj.weight", 1, H, KD, &t.k))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "self_attn.v_proj.weight", 1, H, KD, &t.v))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "self_attn.o_proj.weight", 1, QD, H, &t.o))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "mlp.gate_proj.weight", 1, H, F, &t.g))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "mlp.up_proj.weight", 1, H, F, &t.u))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "mlp.down_proj.weight", 1, F, H, &t.dn))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "self_attn.q_norm.weight", 0, kD, 0, &t.qn))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "self_attn.k_norm.weight", 0, kD, 0, &t.kn))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "input_layernorm.weight", 0, H, 0, &t.in))) return rc;
+        if ((rc = find_tensor(ctx, m, p + "post_attention_layernorm.weight", 0, H, 0, &t.post))) return rc;
+    }
+
+    size_t max_q8 = lm->nbytes;
+    for (auto& t : lv)
+        for (auto* v : {t.q, t.k, t.v, t.o, t.g, t.u, t.dn}) max_q8 = std::max(max_q8, v->nbytes);
+    uint8_t* staging = nullptr;
+    {
+        cudaError_t e = cudaMalloc(&staging, max_q8);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_err(ctx, FA_ERR_OOM, "weight staging buffer");
+        }
+    }
+    auto run = [&]() -> int {
+        ctx->L.resize(d.n_layers);
+        const int QKV = QD + 2 * KD;
+        for (int l = 0; l < d.n_layers; ++l) {
+            LayerW& w = ctx->L[l];
+            LV& t = lv[l];
+            int r;
+            if ((r = dev_alloc(ctx, &w.qkv_q, (size_t)QKV * H)) || (r = dev_alloc(ctx, &w.qkv_d, (size_t)QKV * (H / 32) * 2)) ||
+                (r = dev_alloc(ctx, &w.o_q, (size_t)H * QD)) || (r = dev_alloc(ctx, &w.o_d, (size_t)H * (QD / 32) * 2)) ||
+                (r = dev_alloc(ctx, &w.gu_q, (size_t)2 * F * H)) || (r = dev_alloc(ctx, &w.gu_d, (size_t)2 * F * (H / 32) * 2)) ||
+                (r = dev_alloc(ctx, &w.dn_q, (size_t)H * F)) || (r = dev_alloc(ctx, &w.dn_d, (size_t)H * (F / 32) * 2)))
+                return r;
+            if ((r = upload_q8(ctx, t.q, staging, QD, H, 0, w.qkv_q, w.qkv_d, QKV)) ||
+                (r = upload_q8(ctx, t.k, staging, KD, H, QD, w.qkv_q, w.qkv_d, QKV)) ||
+                (r = upload_q8(ctx, t.v, staging, KD, H, QD + KD, w.qkv_q, w.qkv_d, QKV)) ||
+                (r = upload_q8(ctx, t.o, staging, H, QD, 0, w.o_q, w.o_d, H)) ||
+                (r = upload_q8(ctx, t.g, staging, F, H, 0, w.gu_q, w.gu_d, 2 * F)) ||
+                (r = upload_q8(ctx, t.u, staging, F, H, F, w.gu_q, w.gu_d, 2 * F)) ||
+                (r = upload_q8(ctx, t.dn, staging, H, F, 0, w.dn_q, w.dn_d, H)))
+                return r;
+            if ((r = upload_vec_f32(ctx, t.qn, &w.q_norm)) || (r = upload_vec_f32(ctx, t.kn, &w.k_norm)) ||
+                (r = upload_vec_f32(ctx, t.in, &w.in_norm)) || (r = upload_vec_f32(ctx, t.post, &w.post_norm)))
+                return r;
+        }
+        int r;
+        if ((r = dev_alloc(ctx, &ctx->lm_q, (size_t)V * H)) || (r = dev_alloc(ctx, &ctx->lm_d, (size_t)V * (H / 32) * 2)))
+            return r;
+        if ((r = upload_q8(ctx, lm, staging, V, H, 0, ctx->lm_q, ctx->lm_d, V))) return r;
+        if ((r = upload_vec_f32(ctx, fnorm, &ctx->final_norm))) return r;
+        if ((r = dev_alloc(ctx, (uint8_t**)&ctx->embed, emb->nbytes))) return r;
+        FA_CK(cudaMemcpy(ctx->embed, emb->data, emb->nbytes, cudaMemcpyHostToDevice));
+        ctx->embed_type = emb->type;
+        return FA_OK;
+    };
+    rc = run();
+    cudaFree(staging);
+    if (rc == FA_OK) ctx->loaded = true;
+    return rc;
+}
+
+// --------------------------------------------------------------- sequences --
+static int check_seq(const fa_ctx* ctx, int seq_id) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (seq_id < 0 || seq_id >= (int)ctx->seqs.size() || !ctx->seqs[seq_id].open)
+        return set_err(ctx, FA_ERR_SEQ, "sequence " + std::to_string(seq_id) + " is not open");
+    return FA_OK;
+}
+
+extern "C" int fa_seq_open(fa_ctx* ctx, int max_tokens, int* seq_id) {
+    if (!ctx || !seq_id) return set_err(ctx, FA_ERR_INVALID_ARG, "bad arguments");
+    if (max_tokens <= 0 || max_tokens > ctx->d.max_ctx)
+        return set_err(ctx, FA_ERR_CAPACITY, "max_tokens must be in [1, max_ctx]");
+    for (int i = 0; i < (int)ctx->seqs.size(); ++i) {
+        if (!ctx->seqs[i].open) {
+            Seq& s = ctx->seqs[i];
+            s.open = true;
+            s.len = 0;
+            s.max_tokens = max_tokens;
+            s.pages.clear();
+            *seq_id = i;
+            return FA_OK;
+        }
+    }
+    return set_err(ctx, FA_ERR_SEQ, "no free sequence slot (max_seqs reached)");
+}
+
+extern "C" int fa_seq_close(fa_ctx* ctx, int seq_id) {
+    if (int rc = check_seq(ctx, seq_id)) return rc;
+    Seq& s = ctx->seqs[seq_id];
+    for (int p : s.pages) ctx->palloc.release(p);
+    s.pages.clear();
+    s.open = false;
+    s.len = 0;
+    return FA_OK;
+}
+
+extern "C" int fa_seq_length(const fa_ctx* ctx, int seq_id, int* n_tokens) {
+    if (int rc = check_seq(ctx, seq_id)) return rc;
+    if (n_tokens) *n_tokens = ctx->seqs[seq_id].len;
+    return FA_OK;
+}
+
+extern "C" int fa_seq_truncate(fa_ctx* ctx, int seq_id, int n_tokens) {
+    if (int rc = check_seq(ctx, seq_id)) return rc;
+    Seq& s = ctx->seqs[seq_id];
+    if (n_tokens < 0 || n_tokens > s.len)
+        return set_err(ctx, FA_ERR_INVALID_ARG, "truncate length must be in [0, current length]");
+    const size_t keep = (size_t)(n_tokens + fa::kPageTokens - 1) / fa::kPageTokens;
+    while (s.pages.size() > keep) {
+        ctx->palloc.release(s.pages.back());
+        s.pages.pop_back();
+    }
+    s.len = n_tokens;
+    return FA_OK;
+}
+
+extern "C" int fa_seq_block_table(const fa_ctx* ctx, int seq_id, int* pages, int max_pages, int* n_pages) {
+    if (int rc = check_seq(ctx, seq_id)) return rc;
+    const Seq& s = ctx->seqs[seq_id];
+    if (n_pages) *n_pages = (int)s.pages.size();
+    if (pages)
+        for (int i = 0; i < (int)s.pages.size() && i < max_pages; ++i) pages[i] = s.pages[i];
+    return FA_OK;
+}
+
+// Reserve pages so that every sequence in `need` can hold its new length. Records
+// block-table updates; on exhaustion returns every page taken here.
+static int reserve_pages(fa_ctx* ctx, const std::vector<std::pair<int, int>>& need, std::vector<int>& upd_idx,
+                         std::vector<int>& upd_page) {
+    std::vector<std::pair<int, int>> taken;   // (seq, page)
+    for (auto& sn : need) {
+        Seq& s = ctx->seqs[sn.first];
+        const size_t want = (size_t)(sn.second + fa::kPageTokens - 1) / fa::kPageTokens;
+        while (s.pages.size() < want) {
+            const int p = ctx->palloc.alloc();
+            if (p < 0) {
+                for (auto it = taken.rbegin(); it != taken.rend(); ++it) {
+                    ctx->seqs[it->first].pages.pop_back();
+                    ctx->palloc.release(it->second);
+                }
+                upd_idx.clear();
+                upd_page.clear();
+                return set_err(ctx, FA_ERR_POOL_EXHAUSTED, "KV page pool exhausted");
+            }
+            upd_idx.push_back(sn.first * ctx->bt_stride + (int)s.pages.size());
+            upd_page.push_back(p);
+            s.pages.push_back(p);
+            taken.push_back({sn.first, p});
+        }
+    }
+    return FA_OK;
+}
+
+static int upload_updates(fa_ctx* ctx, const std::vector<int>& ui, const std::vector<int>& up) {
+    size_t off = 0;
+    while (off < ui.size()) {
+        const int n = (int)std::min<size_t>(ui.size() - off, (size_t)ctx->max_updates);
+        int* hi = ctx->h_rows + 3 * ctx->d.max_rows;
+        std::memcpy(hi, ui.data() + off, sizeof(int) * n);
+        std::memcpy(hi + ctx->max_updates, up.data() + off, sizeof(int) * n);
+        FA_CK(cudaMemcpyAsync(ctx->upd_idx, hi, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
+        FA_CK(cudaMemcpyAsync(ctx->upd_page, hi + ctx->max_updates, sizeof(int) * n, cudaMemcpyHostToDevice,
+                              ctx->stream));
+        fa::launch_apply_bt_updates(ctx->bt_dev, ctx->upd_idx, ctx->upd_page, n, ctx->stream);
+        FA_CK(cudaGetLastError());
+        off += n;
+        if (off < ui.size()) FA_CK(cudaStreamSynchronize(ctx->stream));   // staging reuse
+    }
+    return FA_OK;
+}
+
+// ----------------------------------------------------------------- forward --
+namespace {
+
+struct StepPlan {
+    int M = 0;
+    int s_qkv = 1, s_o = 1, s_gu = 1, s_dn = 1;
+    int pps = 32;        // attention pages per split
+    int n_splits = 1;
+    bool embeds = false; // input rows already in x
+    bool logits = false;
+    bool prof = false;
+    uint64_t key() const {
+        return (uint64_t)M | ((uint64_t)n_splits << 13) | ((uint64_t)pps << 25) | ((uint64_t)embeds << 33) |
+               ((uint64_t)logits << 34) | ((uint64_t)prof << 35);
+    }
+};
+
+}  // namespace
+
+static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits) {
+    const fa_model_desc& d = ctx->d;
+    StepPlan p;
+    p.M = M;
+    p.s_qkv = fa::gemm_pick_split(M, (kHq + 2 * kHkv) * kD, d.hidden, ctx->n_sm);
+    p.s_o = fa::gemm_pick_split(M, d.hidden, kHq * kD, ctx->n_sm);
+    p.s_gu = fa::gemm_pick_split(M, 2 * d.ffn, d.hidden, ctx->n_sm);
+    p.s_dn = fa::gemm_pick_split(M, d.hidden, d.ffn, ctx->n_sm);
+    long long total_pages = 0;
+    int max_pages = 1;
+    for (int n : row_len) {
+        const int pg = (n + fa::kPageTokens - 1) / fa::kPageTokens;
+        total_pages += pg;
+        max_pages = std::max(max_pages, pg);
+    }
+    // aim for about 4 CTAs per SM over all (page, KV head) work; 4..64 pages per CTA
+    long long target = 4LL * ctx->n_sm;
+    long long pps = (total_pages * kHkv + target - 1) / target;
+    pps = std::min<long long>(64, std::max<long long>(4, pps));
+    pps = std::max<long long>(pps, (max_pages + ctx->att_max_splits - 1) / ctx->att_max_splits);
+    pps = (pps + 3) / 4 * 4;
+    p.pps = (int)pps;
+    p.n_splits = (max_pages + p.pps - 1) / p.pps;
+    p.embeds = embeds;
+    p.logits = logits;
+    p.prof = ctx->prof;
+    return p;
+}
+
+static int ensure_logits(fa_ctx* ctx) {
+    if (ctx->logits_dev) return FA_OK;
+    void* v = nullptr;
+    if (cudaMalloc(&v, sizeof(float) * (size_t)ctx->d.max_rows * ctx->d.vocab) != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(ctx, FA_ERR_OOM, "logits buffer");
+    }
+    ctx->logits_dev = (float*)v;
+    return FA_OK;
+}
+
+static int ensure_prof_events(fa_ctx* ctx) {
+    const size_t want = 2 * (size_t)ctx->d.n_layers;
+    while (ctx->prof_ev.size() < want) {
+        cudaEvent_t e;
+        FA_CK(cudaEventCreate(&e));
+        ctx->prof_ev.push_back(e);
+    }
+    return FA_OK;
+}
+
+static void record_prof(fa_ctx* ctx, int idx, bool capturing) {
+    if (capturing) cudaEventRecordWithFlags(ctx->prof_ev[idx], ctx->stream, cudaEventRecordExternal);
+    else cudaEventRecord(ctx->prof_ev[idx], ctx->stream);
+}
+
+// Enqueue the kernels of one forward step. Returns the number of launches.
+static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
+    const fa_model_desc& d = ctx->d;
+    cudaStream_t s = ctx->stream;
+    const int M = p.M, H = d.hidden, F = d.ffn;
+    const int QKV = (kHq + 2 * kHkv) * kD;
+    int n = 0;
+    if (!p.embeds) {
+        fa::launch_embed(ctx->embed, ctx->embed_type, H, ctx->row_tok, nullptr, M, d.vocab, ctx->x, ctx->err_dev, s);
+        ++n;
+    }
+    const float* prev_part = nullptr;
+    int prev_n = 0;
+    for (int l = 0; l < d.n_layers; ++l) {
+        const LayerW& w = ctx->L[l];
+        __half* pool_l = ctx->pool + (size_t)l * ctx->layer_stride;
+        fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, w.in_norm, d.rms_eps, ctx->xn16, s);
+        fa::GemmArgs g{};
+        g.A = ctx->xn16; g.Wq = w.qkv_q; g.Wd = w.qkv_d; g.M = M; g.N = QKV; g.K = H;
+        g.n_split = p.s_qkv; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
+        fa::launch_q8_gemm(g, s);
+        fa::AppendArgs a{};
+        a.qkv_part = ctx->part; a.n_part = p.s_qkv; a.M = M; a.pos = ctx->row_pos; a.slot = ctx->row_slot;
+        a.block_table = ctx->bt_dev; a.bt_stride = ctx->bt_stride; a.n_pages = ctx->n_pages;
+        a.qn_w = w.q_norm; a.kn_w = w.k_norm; a.Hq = kHq; a.Hkv = kHkv; a.eps = d.rms_eps;
+        a.q_scale = 1.0f / std::sqrt((float)kD);
+        a.rope = ctx->rope; a.max_pos = d.max_ctx; a.pool_layer = pool_l; a.q_out = ctx->q_rot; a.err = ctx->err_dev;
+        fa::launch_qknorm_rope_append(a, s);
+        fa::AttnArgs at{};
+        at.q = ctx->q_rot; at.pool_layer = pool_l; at.block_table = ctx->bt_dev; at.bt_stride = ctx->bt_stride;
+        at.n_pages = ctx->n_pages; at.slot = ctx->row_slot; at.pos = ctx->row_pos; at.M = M; at.Hq = kHq;
+        at.Hkv = kHkv; at.pages_per_split = p.pps; at.n_splits = p.n_splits; at.part_o = ctx->att_po;
+        at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out32 = nullptr; at.err = ctx->err_dev;
+        if (p.prof) record_prof(ctx, 2 * l, capturing);
+        fa::launch_paged_attention(at, s);
+        ++n;
+        if (p.n_splits > 1) {
+            fa::launch_attn_combine(at, s);
+            ++n;
+        }
+        if (p.prof) record_prof(ctx, 2 * l + 1, capturing);
+        g = fa::GemmArgs{};
+        g.A = ctx->attn16; g.Wq = w.o_q; g.Wd = w.o_d; g.M = M; g.N = H; g.K = kHq * kD;
+        g.n_split = p.s_o; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
+        fa::launch_q8_gemm(g, s);
+        fa::launch_residual_rmsnorm(ctx->x, ctx->part, p.s_o, M, H, w.post_norm, d.rms_eps, ctx->xn16, s);
+        g = fa::GemmArgs{};
+        g.A = ctx->xn16; g.Wq = w.gu_q; g.Wd = w.gu_d; g.M = M; g.N = 2 * F; g.K = H;
+        g.n_split = p.s_gu; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
+        fa::launch_q8_gemm(g, s);
+        fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, s);
+        g = fa::GemmArgs{};
+        g.A = ctx->h16; g.Wq = w.dn_q; g.Wd = w.dn_d; g.M = M; g.N = H; g.K = F;
+        g.n_split = p.s_dn; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
+        fa::launch_q8_gemm(g, s);
+        n += 8;
+        prev_part = ctx->part;
+        prev_n = p.s_dn;
+    }
+    fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, s);
+    fa::GemmArgs g{};
+    g.A = ctx->xn16; g.Wq = ctx->lm_q; g.Wd = ctx->lm_d; g.M = M; g.N = d.vocab; g.K = H;
+    g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = p.logits ? ctx->logits_dev : nullptr;
+    g.amax_val = ctx->amax_v; g.amax_idx = ctx->amax_i;
+    fa::launch_q8_gemm(g, s);
+    fa::launch_argmax_reduce(ctx->amax_v, ctx->amax_i, M, d.vocab / 64, ctx->next_dev, ctx->row_tok, ctx->row_pos, s);
+    n += 3;
+    return n;
+}
+
+static int run_step(fa_ctx* ctx, const StepPlan& p) {
+    if (p.prof)
+        if (int rc = ensure_prof_events(ctx)) return rc;
+    if (!ctx->use_graphs) {
+        ctx->last_launches = enqueue_step(ctx, p, false);
+        FA_CK(cudaGetLastError());
+        ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
+        return FA_OK;
+    }
+    auto it = ctx->graphs.find(p.key());
+    if (it == ctx->graphs.end()) {
+        FA_CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+        const int n = enqueue_step(ctx, p, true);
+        cudaGraph_t graph = nullptr;
+        cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
+        if (e != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            return set_err(ctx, FA_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+        }
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return set_err(ctx, FA_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        if (ctx->graphs.size() > 64) clear_graphs(ctx);
+        it = ctx->graphs.emplace(p.key(), exec).first;
+        ctx->last_launches = n;
+    } else {
+        // launch count is a function of the plan
+        ctx->last_launches = (p.embeds ? 0 : 1) + ctx->d.n_layers * (9 + (p.n_splits > 1 ? 1 : 0)) + 3;
+    }
+    FA_CK(cudaGraphLaunch(it->second, ctx->stream));
+    ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
+    return FA_OK;
+}
+
+static int check_device_error(fa_ctx* ctx) {
+    FA_CK(cudaMemcpyAsync(ctx->h_err, ctx->err_dev, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    FA_CK(cudaStreamSynchronize(ctx->stream));
+    if (*ctx->h_err) {
+        const int e = *ctx->h_err;
+        cudaMemsetAsync(ctx->err_dev, 0, sizeof(int), ctx->stream);
+        cudaStreamSynchronize(ctx->stream);
+        if (e & fa::kDevErrTimeout) return set_err(ctx, FA_ERR_TIMEOUT, "a bounded device wait gave up");
+        return set_err(ctx, FA_ERR_DEVICE, "kernel reported error bits " + std::to_string(e) +
+                                               " (2: bad page, 4: bad position / token)");
+    }
+    return FA_OK;
+}
+
+extern "C" int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
+                          int* next_ids, float* logits) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (!ctx->loaded) return set_err(ctx, FA_ERR_NOT_READY, "weights not loaded");
+    if (n_rows <= 0 || n_rows > ctx->d.max_rows || !seq_ids)
+        return set_err(ctx, FA_ERR_CAPACITY, "n_rows must be in [1, max_rows]");
+    if ((token_ids == nullptr) == (embeds == nullptr))
+        return set_err(ctx, FA_ERR_INVALID_ARG, "give exactly one of token_ids and embeds");
+    cudaSetDevice(ctx->device);
+    const fa_model_desc& d = ctx->d;
+    const int M = n_rows;
+    // positions: consecutive per sequence in row order
+    std::unordered_map<int, int> extra;
+    std::vector<int> pos(M), row_len(M);
+    for (int i = 0; i < M; ++i) {
+        if (int rc = check_seq(ctx, seq_ids[i])) return rc;
+        if (token_ids && (token_ids[i] < 0 || token_ids[i] >= d.vocab))
+            return set_err(ctx, FA_ERR_INVALID_ARG, "token id out of range");
+        const Seq& s = ctx->seqs[seq_ids[i]];
+        const int k = extra[seq_ids[i]]++;
+        pos[i] = s.len + k;
+        row_len[i] = pos[i] + 1;
+        if (pos[i] >= s.max_tokens || pos[i] >= d.max_ctx)
+            return set_err(ctx, FA_ERR_CAPACITY, "sequence " + std::to_string(seq_ids[i]) + " is full");
+    }
+    std::vector<std::pair<int, int>> need;
+    for (int i = 0; i < M; ++i) need.push_back({seq_ids[i], pos[i] + 1});
+    std::vector<int> ui, up;
+    if (int rc = reserve_pages(ctx, need, ui, up)) return rc;
+    if (logits)
+        if (int rc = ensure_logits(ctx)) return rc;
+
+    int* h = ctx->h_rows;
+    for (int i = 0; i < M; ++i) {
+        h[i] = token_ids ? token_ids[i] : 0;
+        h[M + i] = seq_ids[i];
+        h[2 * M + i] = pos[i];
+    }
+    int rc = FA_OK;
+    auto body = [&]() -> int {
+        FA_CK(cudaMemcpyAsync(ctx->row_tok, h, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
+        FA_CK(cudaMemcpyAsync(ctx->row_slot, h + M, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
+        FA_CK(cudaMemcpyAsync(ctx->row_pos, h + 2 * M, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
+        if (int r = upload_updates(ctx, ui, up)) return r;
+        if (embeds)
+            FA_CK(cudaMemcpyAsync(ctx->x, embeds, sizeof(float) * M * d.hidden, cudaMemcpyHostToDevice, ctx->stream));
+        StepPlan p = make_plan(ctx, M, row_len, embeds != nullptr, logits != nullptr);
+        if (int r = run_step(ctx, p)) return r;
+        FA_CK(cudaMemcpyAsync(ctx->h_next, ctx->next_dev, sizeof(int) * M, cudaMemcpyDeviceToHost, ctx->stream));
+        if (logits)
+            FA_CK(cudaMemcpyAsync(logits, ctx->logits_dev, sizeof(float) * M * d.vocab, cudaMemcpyDeviceToHost,
+                                  ctx->stream));
+        return check_device_error(ctx);
+    };
+    rc = body();
+    if (rc != FA_OK) {
+        // roll back the page reservations of this call
+        for (size_t k = ui.size(); k-- > 0;) {
+            const int seq = ui[k] / ctx->bt_stride;
+            ctx->seqs[seq].pages.pop_back();
+            ctx->palloc.release(up[k]);
+        }
+        return rc;
+    }
+    for (int i = 0; i < M; ++i) ctx->seqs[seq_ids[i]].len += 1;
+    if (next_ids) std::memcpy(next_ids, ctx->h_next, sizeof(int) * M);
+    return FA_OK;
+}
+
+extern "C" int fa_prefill(fa_ctx* ctx, int seq_id, const float* embeds, int n_tok, int* next_id, float* last_logits) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (int rc = check_seq(ctx, seq_id)) return rc;
+    if (!embeds || n_tok <= 0) return set_err(ctx, FA_ERR_INVALID_ARG, "embeds and n_tok > 0 required");
+    const int R = ctx->d.max_rows;
+    std::vector<int> ids(R, seq_id), nx(R);
+    std::vector<float> lg;
+    for (int off = 0; off < n_tok; off += R) {
+        const int m = std::min(R, n_tok - off);
+        const bool last = off + m == n_tok;
+        if (last && last_logits) lg.resize((size_t)m * ctx->d.vocab);
+        if (int rc = fa_forward(ctx, m, ids.data(), nullptr, embeds + (size_t)off * ctx->d.hidden, nx.data(),
+                                last && last_logits ? lg.data() : nullptr))
+            return rc;
+        if (last) {
+            if (next_id) *next_id = nx[m - 1];
+            if (last_logits)
+                std::memcpy(last_logits, lg.data() + (size_t)(m - 1) * ctx->d.vocab, sizeof(float) * ctx->d.vocab);
+        }
+    }
+    return FA_OK;
+}
+
+extern "C" int fa_decode_step(fa_ctx* ctx, int n_seq, const int* seq_ids, const int* token_ids, int* next_ids,
+                              float* logits) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (!seq_ids || !token_ids) return set_err(ctx, FA_ERR_INVALID_ARG, "seq_ids and token_ids required");
+    for (int i = 0; i < n_seq; ++i)
+        for (int j = 0; j < i; ++j)
+            if (seq_ids[i] == seq_ids[j]) return set_err(ctx, FA_ERR_INVALID_ARG, "decode rows must be distinct sequences");
+    return fa_forward(ctx, n_seq, seq_ids, token_ids, nullptr, next_ids, logits);
+}
+
+extern "C" int fa_generate(fa_ctx* ctx, int n_seq, const int* seq_ids, const int* first_tokens, int n_steps,
+                           int* out_ids, float* device_ms) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (!ctx->loaded) return set_err(ctx, FA_ERR_NOT_READY, "weights not loaded");
+    if (n_seq <= 0 || n_seq > ctx->d.max_rows || !seq_ids || !first_tokens || n_steps <= 0)
+        return set_err(ctx, FA_ERR_INVALID_ARG, "bad arguments");
+    if ((size_t)n_seq * n_steps > (size_t)ctx->d.max_rows * 4096)
+        return set_err(ctx, FA_ERR_CAPACITY, "n_seq * n_steps exceeds the output staging buffer");
+    cudaSetDevice(ctx->device);
+    const fa_model_desc& d = ctx->d;
+    std::vector<int> base(n_seq);
+    std::vector<std::pair<int, int>> need;
+    for (int i = 0; i < n_seq; ++i) {
+        if (int rc = check_seq(ctx, seq_ids[i])) return rc;
+        for (int j = 0; j < i; ++j)
+            if (seq_ids[i] == seq_ids[j]) return set_err(ctx, FA_ERR_INVALID_ARG, "rows must be distinct sequences");
+        if (first_tokens[i] < 0 || first_tokens[i] >= d.vocab) return set_err(ctx, FA_ERR_INVALID_ARG, "token id out of range");
+        const Seq& s = ctx->seqs[seq_ids[i]];
+        base[i] = s.len;
+        if (s.len + n_steps > s.max_tokens || s.len + n_steps > d.max_ctx)
+            return set_err(ctx, FA_ERR_CAPACITY, "sequence " + std::to_string(seq_ids[i]) + " would overflow");
+        need.push_back({seq_ids[i], s.len + n_steps});
+    }
+    std::vector<int> ui, up;
+    if (int rc = reserve_pages(ctx, need, ui, up)) return rc;
+    int* h = ctx->h_rows;
+    for (int i = 0; i < n_seq; ++i) {
+        h[i] = first_tokens[i];
+        h[n_seq + i] = seq_ids[i];
+        h[2 * n_seq + i] = base[i];
+    }
+    auto body = [&]() -> int {
+        FA_CK(cudaMemcpyAsync(ctx->row_tok, h, sizeof(int) * n_seq, cudaMemcpyHostToDevice, ctx->stream));
+        FA_CK(cudaMemcpyAsync(ctx->row_slot, h + n_seq, sizeof(int) * n_seq, cudaMemcpyHostToDevice, ctx->stream));
+        FA_CK(cudaMemcpyAsync(ctx->row_pos, h + 2 * n_seq, sizeof(int) * n_seq, cudaMemcpyHostToDevice, ctx->stream));
+        if (int r = upload_updates(ctx, ui, up)) return r;
+        FA_CK(cudaEventRecord(ctx->ev_t0, ctx->stream));
+        std::vector<int> row_len(n_seq);
+        for (int k = 0; k < n_steps; ++k) {
+            for (int i = 0; i < n_seq; ++i) row_len[i] = base[i] + k + 1;
+            StepPlan p = make_plan(ctx, n_seq, row_len, false, false);
+            if (int r = run_step(ctx, p)) return r;
+            FA_CK(cudaMemcpyAsync(ctx->h_next + (size_t)k * n_seq, ctx->next_dev, sizeof(int) * n_seq,
+                                  cudaMemcpyDeviceToHost, ctx->stream));
+        }
+        FA_CK(cudaEventRecord(ctx->ev_t1, ctx->stream));
+        return check_device_error(ctx);
+    };
+    int rc = body();
+    if (rc != FA_OK) {
+        for (size_t k = ui.size(); k-- > 0;) {
+            const int seq = ui[k] / ctx->bt_stride;
+            ctx->seqs[seq].pages.pop_back();
+            ctx->palloc.release(up[k]);
+        }
+        return rc;
+    }
+    for (int i = 0; i < n_seq; ++i) ctx->seqs[seq_ids[i]].len += n_steps;
+    if (out_ids) std::memcpy(out_ids, ctx->h_next, sizeof(int) * (size_t)n_seq * n_steps);
+    if (device_ms) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, ctx->ev_t0, ctx->ev_t1);
+        *device_ms = ms;
+    }
+    return FA_OK;
+}
+
+// ------------------------------------------------------------------- pages --
+static int ensure_scratch_ints(fa_ctx* ctx, int n) {
+    if (ctx->scratch_ints_n >= n) return FA_OK;
+    if (ctx->scratch_ints) cudaFree(ctx->scratch_ints);
+    ctx->scratch_ints = nullptr;
+    ctx->scratch_ints_n = 0;
+    void* v = nullptr;
+    if (cudaMalloc(&v, sizeof(int) * (size_t)n) != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(ctx, FA_ERR_OOM, "page list buffer");
+    }
+    ctx->scratch_ints = (int*)v;
+    ctx->scratch_ints_n = n;
+    return FA_OK;
+}
+
+extern "C" int fa_kv_read_pages(fa_ctx* ctx, int layer, const int* pages, int n, uint16_t* out) {
+    if (!ctx || !pages || !out || n < 0) return set_err(ctx, FA_ERR_INVALID_ARG, "bad arguments");
+    if (layer < 0 || layer >= ctx->d.n_layers) return set_err(ctx, FA_ERR_INVALID_ARG, "layer out of range");
+    for (int i = 0; i < n; ++i)
+        if (pages[i] < 0 || pages[i] >= ctx->n_pages) return set_err(ctx, FA_ERR_INVALID_ARG, "page out of range");
+    if (n == 0) return FA_OK;
+    cudaSetDevice(ctx->device);
+    if (int rc = ensure_scratch_ints(ctx, n)) return rc;
+    __half* buf = nullptr;
+    FA_CK(cudaMalloc(&buf, kPageElems * 2 * (size_t)n));
+    int rc = FA_OK;
+    auto body = [&]() -> int {
+        FA_CK(cudaMemcpyAsync(ctx->scratch_ints, pages, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
+        fa::launch_read_pages(ctx->pool + (size_t)layer * ctx->layer_stride, ctx->scratch_ints, n, buf, ctx->stream);
+        FA_CK(cudaGetLastError());
+        FA_CK(cudaMemcpyAsync(out, buf, kPageElems * 2 * (size_t)n, cudaMemcpyDeviceToHost, ctx->stream));
+        FA_CK(cudaStreamSynchronize(ctx->stream));
+        return FA_OK;
+    };
+    rc = body();
+    cudaFree(buf);
+    return rc;
+}
+
+extern "C" int fa_kv_append(fa_ctx* ctx, int n_rows, const int* seq_ids, const uint16_t* k, const uint16_t* v) {
+    if (!ctx || !seq_ids || !k || !v || n_rows <= 0) return set_err(ctx, FA_ERR_INVALID_ARG, "bad arguments");
+    cudaSetDevice(ctx->device);
+    const int L = ctx->d.n_layers;
+    std::unordered_map<int, int> extra;
+    std::vector<int> pos(n_rows);
+    std::vector<std::pair<int, int>> need;
+    for (int i = 0; i < n_rows; ++i) {
+        if (int rc = check_seq(ctx, seq_ids[i])) return rc;
+        const Seq& s = ctx->seqs[seq_ids[i]];
+        pos[i] = s.len + extra[seq_ids[i]]++;
+        if (pos[i] >= s.max_tokens) return set_err(ctx, FA_ERR_CAPACITY, "sequence full");
+        need.push_back({seq_ids[i], pos[i] + 1});
+    }
+    std::vector<int> ui, up;
+    if (int rc = reserve_pages(ctx, need, ui, up)) return rc;
+    const size_t bytes = (size_t)n_rows * L * kHkv * kD * 2;
+    __half *kd = nullptr, *vd = nullptr;
+    int *pd = nullptr;
+    auto body = [&]() -> int {
+        FA_CK(cudaMalloc(&kd, bytes));
+        FA_CK(cudaMalloc(&vd, bytes));
+        FA_CK(cudaMalloc(&pd, sizeof(int) * 2 * n_rows));
+        FA_CK(cudaMemcpyAsync(kd, k, bytes, cudaMemcpyHostToDevice, ctx->stream));
+        FA_CK(cudaMemcpyAsync(vd, v, bytes, cudaMemcpyHostToDevice, ctx->stream));
+        std::vector<int> hp(2 * n_rows);
+        for (int i = 0; i < n_rows; ++i) { hp[i] = pos[i]; hp[n_rows + i] = seq_ids[i]; }
+        FA_CK(cudaMemcpyAsync(pd, hp.data(), sizeof(int) * 2 * n_rows, cudaMemcpyHostToDevice, ctx->stream));
+        if (int r = upload_updates(ctx, ui, up)) return r;
+        fa::RawAppendArgs a{};
+        a.k = kd; a.v = vd; a.M = n_rows; a.n_layers = L; a.Hkv = kHkv; a.pos = pd; a.slot = pd + n_rows;
+        a.block_table = ctx->bt_dev; a.bt_stride = ctx->bt_stride; a.n_pages = ctx->n_pages; a.pool = ctx->pool;
+        a.err = ctx->err_dev;
+        fa::launch_kv_append_raw(a, ctx->stream);
+        FA_CK(cudaGetLastError());
+        return check_device_error(ctx);
+    };
+    int rc = body();
+    if (kd) cudaFree(kd);
+    if (vd) cudaFree(vd);
+    if (pd) cudaFree(pd);
+    if (rc != FA_OK) {
+        for (size_t q = ui.size(); q-- > 0;) {
+            ctx->seqs[ui[q] / ctx->bt_stride].pages.pop_back();
+            ctx->palloc.release(up[q]);
+        }
+        return rc;
+    }
+    for (int i = 0; i < n_rows; ++i) ctx->seqs[seq_ids[i]].len += 1;
+    return FA_OK;
+}
+
+extern "C" int fa_kv_fill_synthetic(fa_ctx* ctx, int seq_id, int n_tokens, uint64_t seed) {
+    if (int rc = check_seq(ctx, seq_id)) return rc;
+    if (n_tokens < 0) return set_err(ctx, FA_ERR_INVALID_ARG, "n_tokens < 0");
+    Seq& s = ctx->seqs[seq_id];
+    if (s.len % fa::kPageTokens)
+        return set_err(ctx, FA_ERR_INVALID_ARG, "synthetic fill starts on a page boundary (length % 16 == 0)");
+    if (s.len + n_tokens > s.max_tokens) return set_err(ctx, FA_ERR_CAPACITY, "sequence would overflow");
+    cudaSetDevice(ctx->device);
+    const size_t first_new = s.pages.size();
+    std::vector<int> ui, up;
+    if (int rc = reserve_pages(ctx, {{seq_id, s.len + n_tokens}}, ui, up)) return rc;
+    std::vector<int> fill(s.pages.begin() + first_new, s.pages.end());
+    auto body = [&]() -> int {
+        if (int r = upload_updates(ctx, ui, up)) return r;
+        if (!fill.empty()) {
+            if (int r = ensure_scratch_ints(ctx, (int)fill.size())) return r;
+            FA_CK(cudaMemcpyAsync(ctx->scratch_ints, fill.data(), sizeof(int) * fill.size(), cudaMemcpyHostToDevice,
+                                  ctx->stream));
+            fa::launch_fill_random(ctx->pool, ctx->layer_stride, ctx->d.n_layers, ctx->scratch_ints, (int)fill.size(),
+                                   seed, ctx->stream);
+            FA_CK(cudaGetLastError());
+        }
+        FA_CK(cudaStreamSynchronize(ctx->stream));
+        return FA_OK;
+    };
+    int rc = body();
+    if (rc != FA_OK) {
+        for (size_t q = ui.size(); q-- > 0;) {
+            s.pages.pop_back();
+            ctx->palloc.release(up[q]);
+        }
+        return rc;
+    }
+    s.len += n_tokens;
+    return FA_OK;
+}
+
+extern "C" int fa_pool_compact(fa_ctx* ctx, int* n_moved) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    cudaSetDevice(ctx->device);
+    std::vector<int> src, dst;
+    ctx->palloc.compact(src, dst);
+    if (n_moved) *n_moved = (int)src.size();
+    if (src.empty()) return FA_OK;
+    std::unordered_map<int, int> remap;
+    for (size_t i = 0; i < src.size(); ++i) remap[src[i]] = dst[i];
+    std::vector<int> ui, up;
+    for (int sid = 0; sid < (int)ctx->seqs.size(); ++sid) {
+        Seq& s = ctx->seqs[sid];
+        if (!s.open) continue;
+        for (size_t k = 0; k < s.pages.size(); ++k) {
+            auto it = remap.find(s.pages[k]);
+            if (it != remap.end()) {
+                s.pages[k] = it->second;
+                ui.push_back(sid * ctx->bt_stride + (int)k);
+                up.push_back(it->second);
+            }
+        }
+    }
+    const int n = (int)src.size();
+    if (int rc = ensure_scratch_ints(ctx, 2 * n)) return rc;
+    std::vector<int> both(src);
+    both.insert(both.end(), dst.begin(), dst.end());
+    FA_CK(cudaMemcpyAsync(ctx->scratch_ints, both.data(), sizeof(int) * 2 * n, cudaMemcpyHostToDevice, ctx->stream));
+    fa::launch_page_copy(ctx->pool, ctx->layer_stride, ctx->d.n_layers, ctx->scratch_ints, ctx->scratch_ints + n, n,
+                         ctx->stream);
+    FA_CK(cudaGetLastError());
+    if (int rc = upload_updates(ctx, ui, up)) return rc;
+    FA_CK(cudaStreamSynchronize(ctx->stream));
+    return FA_OK;
+}
+
+// ------------------------------------------------------------- measurement --
+extern "C" int fa_profile(fa_ctx* ctx, int enable) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    ctx->prof = enable != 0;
+    return FA_OK;
+}
+
+extern "C" int fa_profile_attention(fa_ctx* ctx, float* total_ms, int* n_launches) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    FA_CK(cudaStreamSynchronize(ctx->stream));
+    float tot = 0.0f;
+    for (int l = 0; l < ctx->prof_n; ++l) {
+        float ms = 0.0f;
+        FA_CK(cudaEventElapsedTime(&ms, ctx->prof_ev[2 * l], ctx->prof_ev[2 * l + 1]));
+        tot += ms;
+    }
+    if (total_ms) *total_ms = tot;
+    if (n_launches) *n_launches = ctx->prof_n;
+    return FA_OK;
+}
+
+extern "C" int fa_step_launches(const fa_ctx* ctx, int* n) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (n) *n = ctx->last_launches;
+    return FA_OK;
+}
+
+// ------------------------------------------------------------ kernel ops --
+#define OP_CK(call)                                                                                     \
+    do {                                                                                                \
+        cudaError_t e_ = (call);                                                                        \
+        if (e_ != cudaSuccess) return set_err(nullptr, FA_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+extern "C" int fa_op_qknorm_rope_append(const float* qkv, int M, const int* pos, const int* slot, const int* bt,
+                                        int bt_stride, int n_pages, const float* qn, const float* kn, float eps,
+                                        const float* rope, int max_pos, uint16_t* pool_layer, float* q_out, int* err,
+                                        void* stream) {
+    if (!qkv || !pos || !slot || !bt || !qn || !kn || !rope || !pool_layer || !q_out || M <= 0)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "null argument");
+    if (int rc = ensure_configured()) return rc;
+    fa::AppendArgs a{};
+    a.qkv_part = qkv; a.n_part = 1; a.M = M; a.pos = pos; a.slot = slot; a.block_table = bt; a.bt_stride = bt_stride;
+    a.n_pages = n_pages; a.qn_w = qn; a.kn_w = kn; a.Hq = kHq; a.Hkv = kHkv; a.eps = eps;
+    a.q_scale = 1.0f / std::sqrt((float)kD); a.rope = reinterpret_cast<const float2*>(rope); a.max_pos = max_pos;
+    a.pool_layer = reinterpret_cast<__half*>(pool_layer); a.q_out = q_out; a.err = err;
+    fa::launch_qknorm_rope_append(a, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_kv_append(const uint16_t* k, const uint16_t* v, int M, int n_layers, const int* pos,
+                               const int* slot, const int* bt, int bt_stride, int n_pages, uint16_t* pool, int* err,
+                               void* stream) {
+    if (!k || !v || !pos || !slot || !bt || !pool || M <= 0 || n_layers <= 0)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "null argument");
+    fa::RawAppendArgs a{};
+    a.k = reinterpret_cast<const __half*>(k); a.v = reinterpret_cast<const __half*>(v); a.M = M;
+    a.n_layers = n_layers; a.Hkv = kHkv; a.pos = pos; a.slot = slot; a.block_table = bt; a.bt_stride = bt_stride;
+    a.n_pages = n_pages; a.pool = reinterpret_cast<__half*>(pool); a.err = err;
+    fa::launch_kv_append_raw(a, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" size_t fa_op_attention_scratch_bytes(int M, int n_splits) {
+    if (M <= 0 || n_splits <= 1) return 0;
+    return (size_t)M * kHq * n_splits * (kD + 2) * sizeof(float);
+}
+
+extern "C" int fa_op_paged_attention(const float* q, int M, const int* pos, const int* slot, const int* bt,
+                                     int bt_stride, int n_pages, const uint16_t* pool_layer, int pps, int n_splits,
+                                     void* scratch, uint16_t* out16, float* out32, int* err, void* stream) {
+    if (!q || !pos || !slot || !bt || !pool_layer || M <= 0 || pps <= 0 || n_splits <= 0 || (!out16 && !out32))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "null or non-positive argument");
+    if (n_splits > 1 && !scratch) return set_err(nullptr, FA_ERR_INVALID_ARG, "scratch required when n_splits > 1");
+    if (int rc = ensure_configured()) return rc;
+    fa::AttnArgs a{};
+    a.q = q; a.pool_layer = reinterpret_cast<const __half*>(pool_layer); a.block_table = bt; a.bt_stride = bt_stride;
+    a.n_pages = n_pages; a.slot = slot; a.pos = pos; a.M = M; a.Hq = kHq; a.Hkv = kHkv; a.pages_per_split = pps;
+    a.n_splits = n_splits;
+    a.part_o = reinterpret_cast<float*>(scratch);
+    a.part_ml = a.part_o ? a.part_o + (size_t)M * kHq * n_splits * kD : nullptr;
+    a.out16 = reinterpret_cast<__half*>(out16); a.out32 = out32; a.err = err;
+    fa::launch_paged_attention(a, (cudaStream_t)stream);
+    if (n_splits > 1) fa::launch_attn_combine(a, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, int8_t* q, uint16_t* d, void* stream) {
+    if (!raw || !q || !d || N <= 0 || K <= 0 || K % 32) return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
+    fa::launch_repack_q8(raw, N, K, 0, 0, q, reinterpret_cast<__half*>(d), N, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_q8_gemm(const uint16_t* a16, int M, int K, const int8_t* q, const uint16_t* d, int N, int n_split,
+                             float* c, void* stream) {
+    if (!a16 || !q || !d || !c || M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_split <= 0 ||
+        (K / 64) % n_split)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "need N, K multiples of 64 and n_split dividing K/64");
+    if (int rc = ensure_configured()) return rc;
+    fa::GemmArgs g{};
+    g.A = reinterpret_cast<const __half*>(a16); g.Wq = q; g.Wd = reinterpret_cast<const __half*>(d);
+    g.M = M; g.N = N; g.K = K; g.n_split = n_split; g.epilogue = fa::kEpiStoreF32; g.C = c;
+    fa::launch_q8_gemm(g, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" size_t fa_op_argmax_scratch_bytes(int M, int N) {
+    if (M <= 0 || N <= 0) return 0;
+    return (size_t)M * (N / 64) * (sizeof(float) + sizeof(int));
+}
+
+extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, int M, int K, const int8_t* q, const uint16_t* d, int N,
+                                    void* scratch, int* next, float* logits, void* stream) {
+    if (!a16 || !q || !d || !scratch || !next || M <= 0 || N % 64 || K % 64)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
+    if (int rc = ensure_configured()) return rc;
+    fa::GemmArgs g{};
+    g.A = reinterpret_cast<const __half*>(a16); g.Wq = q; g.Wd = reinterpret_cast<const __half*>(d);
+    g.M = M; g.N = N; g.K = K; g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = logits;
+    g.amax_val = reinterpret_cast<float*>(scratch);
+    g.amax_idx = reinterpret_cast<int*>(g.amax_val + (size_t)M * (N / 64));
+    fa::launch_q8_gemm(g, (cudaStream_t)stream);
+    fa::launch_argmax_reduce(g.amax_val, g.amax_idx, M, N / 64, next, nullptr, nullptr, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+// ------------------------------------------------------- host allocator --
+struct fa_palloc {
+    fa::PageAllocator a;
+};
+
+extern "C" fa_palloc* fa_palloc_create(int n_pages) {
+    if (n_pages <= 0) {
+        set_err(nullptr, FA_ERR_INVALID_ARG, "n_pages must be positive");
+        return nullptr;
+    }
+    fa_palloc* p = new fa_palloc();
+    p->a.init(n_pages);
+    return p;
+}
+
+extern "C" void fa_palloc_destroy(fa_palloc* pa) { delete pa; }
+
+extern "C" int fa_palloc_alloc(fa_palloc* pa) {
+    if (!pa) return set_err(nullptr, FA_ERR_INVALID_ARG, "NULL allocator");
+    const int p = pa->a.alloc();
+    if (p < 0) return set_err(nullptr, FA_ERR_POOL_EXHAUSTED, "page pool exhausted");
+    return p;
+}
+
+extern "C" int fa_palloc_free(fa_palloc* pa, int page) {
+    if (!pa) return set_err(nullptr, FA_ERR_INVALID_ARG, "NULL allocator");
+    if (!pa->a.release(page)) return set_err(nullptr, FA_ERR_INVALID_ARG, "page out of range or already free");
+    return FA_OK;
+}
+
+extern "C" int fa_palloc_n_free(const fa_palloc* pa) { return pa ? pa->a.n_free() : FA_ERR_INVALID_ARG; }
+
+extern "C" int fa_palloc_compact(fa_palloc* pa, int* src, int* dst, int max_moves, int* n_moves) {
+    if (!pa) return set_err(nullptr, FA_ERR_INVALID_ARG, "NULL allocator");
+    std::vector<int> s, d;
+    pa->a.compact(s, d);
+    if (n_moves) *n_moves = (int)s.size();
+    for (int i = 0; i < (int)s.size() && i < max_moves; ++i) {
+        if (src) src[i] = s[i];
+        if (dst) dst[i] = d[i];
+    }
+    return (int)s.size() <= max_moves || (!src && !dst) ? FA_OK
+                                                        : set_err(nullptr, FA_ERR_CAPACITY, "more moves than max_moves");
+}

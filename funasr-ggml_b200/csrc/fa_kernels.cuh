@@ -1,0 +1,110 @@
+// Launchers of the decoder kernels (one translation unit each) used by fa_api.cu.
+#pragma once
+
+#include "fa_common.cuh"
+
+namespace fa {
+
+// ---------------------------------------------------------------- k_append.cu --
+// Kernel (1): per-head Q/K RMSNorm + NEOX RoPE + paged f16 K/V append.
+struct AppendArgs {
+    const float* qkv_part;   // [n_part][M][(Hq + 2*Hkv) * 128] f32 split-K partials of Wqkv . x
+    int n_part;
+    int M;
+    const int* pos;          // [M] token position of each row
+    const int* slot;         // [M] sequence slot of each row
+    const int* block_table;  // [slots][bt_stride]
+    int bt_stride;
+    int n_pages;
+    const float* qn_w;       // [128]
+    const float* kn_w;       // [128]
+    int Hq, Hkv;
+    float eps, q_scale;
+    const float2* rope;      // [max_pos][64]
+    int max_pos;
+    __half* pool_layer;      // [n_pages][Hkv][2][16][128]
+    float* q_out;            // [M][Hq][128]
+    int* err;
+};
+void launch_qknorm_rope_append(const AppendArgs& a, cudaStream_t s);
+
+// Raw append of given f16 K/V for several layers (page-table microbenchmark).
+struct RawAppendArgs {
+    const __half* k;         // [M][n_layers][Hkv][128]
+    const __half* v;
+    int M, n_layers, Hkv;
+    const int* pos;
+    const int* slot;
+    const int* block_table;
+    int bt_stride;
+    int n_pages;
+    __half* pool;            // [n_layers][n_pages][Hkv][2][16][128]
+    int* err;
+};
+void launch_kv_append_raw(const RawAppendArgs& a, cudaStream_t s);
+
+// ------------------------------------------------------------- k_attention.cu --
+// Kernel (2): paged GQA decode attention (head_dim 128, 2 query heads per KV head).
+struct AttnArgs {
+    const float* q;          // [M][Hq][128], already scaled by 1/sqrt(128)
+    const __half* pool_layer;
+    const int* block_table;
+    int bt_stride;
+    int n_pages;
+    const int* slot;         // [M]
+    const int* pos;          // [M]; row m attends to tokens [0, pos[m]]
+    int M, Hq, Hkv;
+    int pages_per_split;     // pages one CTA reads
+    int n_splits;            // grid.x; splits beyond a row's length exit at once
+    float* part_o;           // [M][Hq][n_splits][128] un-normalised partial outputs
+    float* part_ml;          // [M][Hq][n_splits][2]   (running max in log2 units, sum)
+    __half* out16;           // [M][Hq*128] final output (f16) or nullptr
+    float* out32;            // [M][Hq*128] final output (f32) or nullptr
+    int* err;
+};
+size_t attn_smem_bytes();
+void launch_paged_attention(const AttnArgs& a, cudaStream_t s);
+// Split combine; only needed when n_splits > 1.
+void launch_attn_combine(const AttnArgs& a, cudaStream_t s);
+
+// ------------------------------------------------------------------ k_gemm.cu --
+// Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T
+enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1 };
+struct GemmArgs {
+    const __half* A;         // [M][K] f16 activations
+    const int8_t* Wq;        // [N][K] int8
+    const __half* Wd;        // [K/32][N] f16 block scales
+    int M, N, K;
+    int n_split;             // split-K factor (grid.z); K/n_split multiple of 64
+    int epilogue;
+    float* C;                // kEpiStoreF32: [n_split][M][N] partials (n_split == 1: the result)
+    float* amax_val;         // kEpiArgmax: [M][N/64] per-tile row maxima
+    int* amax_idx;           //             [M][N/64] first column holding them
+};
+void launch_q8_gemm(const GemmArgs& g, cudaStream_t s);
+int gemm_pick_split(int M, int N, int K, int n_sm);
+
+// ----------------------------------------------------------------- k_small.cu --
+void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds,
+                  int M, int vocab, float* x, int* err, cudaStream_t s);
+// x[m] += sum_s part[s][m] (n_part may be 0); xn16[m] = f16(rmsnorm(x[m]) * w)
+void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w,
+                             float eps, __half* xn16, cudaStream_t s);
+// h16[m][j] = f16(silu(g) * u) with g, u summed over n_part partials of the interleaved gate/up GEMM
+void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h16, cudaStream_t s);
+// next[m] = first column of the row maximum over n_tiles partial maxima; optional feedback
+// of the token into tokens[m] and pos[m] += 1 for device-fed generation.
+void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,
+                          int* feed_pos, cudaStream_t s);
+void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* upd_page, int n, cudaStream_t s);
+// GGUF Q8_0 rows [N][K/32][34 B] -> q [N][K] + d [K/32][ldn]; rows land at dst row
+// (interleave == 0) r0 + n, or (interleave == 1/2: gate/up) (n/8)*16 + (interleave-1)*8 + n%8.
+void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, int interleave, int8_t* dst_q, __half* dst_d,
+                      int ldn, cudaStream_t s);
+void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,
+                      cudaStream_t s);
+void launch_fill_random(__half* pool, size_t layer_stride, int n_layers, const int* pages, int n_pages_list,
+                        unsigned long long seed, cudaStream_t s);
+void launch_read_pages(const __half* pool_layer, const int* pages, int n, __half* out, cudaStream_t s);
+
+}  // namespace fa

@@ -1,0 +1,138 @@
+// Kernel (1): fused per-head Q/K RMSNorm + NEOX RoPE + paged f16 K/V append.
+//
+// Replaces, per layer and step, the ggml node chain of the reference's
+// gpu_gqa_forward (compute/llm_ops_gpu.cpp:57-96): reshape, gpu_rms_norm on q/k
+// (ggml_rms_norm + cast + mul, :16-25), ggml_rope_ext mode 2 (:72-75), and the
+// ggml_cpy of K/V into the f32 cache slot (:84-96). The cache here is paged f16.
+//
+// Arithmetic is written with explicit round-to-nearest intrinsics so that the
+// K page bytes equal those of the CPU oracle given the same f32 inputs:
+//   ss    = sum over 128 of (double)(x*x)      (ggml CPU rms_norm sums in double)
+//   scale = 1 / sqrt((float)(ss/128) + eps)     (correctly rounded div and sqrt)
+//   y     = (x * scale) * w
+//   rope  : y0' = y0*c - y1*s, y1' = y0*s + y1*c, no fused multiply-add
+//   K, V  : f32 -> f16 round-to-nearest-even
+//
+// Grid: (M rows, (Hq + 2*Hkv) / 8 head groups); 8 warps, one warp per 128-wide
+// head vector, lane l owning dims {l, l+32, l+64, l+96} so both NEOX pairs
+// (l, l+64) and (l+32, l+96) stay in one lane. Memory-bound on nothing: a few KB
+// per row; it exists to avoid ~10 ggml launches and the f32 cache round trip.
+#include "fa_kernels.cuh"
+
+namespace fa {
+
+namespace {
+
+constexpr int D = 128;
+
+__global__ void __launch_bounds__(256) qknorm_rope_append_kernel(AppendArgs a) {
+    const int m = blockIdx.x;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int j = blockIdx.y * 8 + warp;          // head vector index in the qkv row
+    const int n_vec = a.Hq + 2 * a.Hkv;
+    if (j >= n_vec) return;
+    const int W = n_vec * D;
+
+    float x[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = 0.0f;
+    for (int s = 0; s < a.n_part; ++s) {
+        const float* row = a.qkv_part + ((size_t)s * a.M + m) * W + (size_t)j * D;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = __fadd_rn(x[k], row[lane + 32 * k]);
+    }
+
+    const int pos = a.pos[m];
+    const bool is_q = j < a.Hq;
+    const bool is_k = !is_q && j < a.Hq + a.Hkv;
+    if (pos < 0 || pos >= a.max_pos) {
+        if (lane == 0) record_error(a.err, kDevErrBadPos);
+        return;
+    }
+
+    if (is_q || is_k) {
+        double ss = 0.0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ss += (double)__fmul_rn(x[k], x[k]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float mean = (float)(ss / (double)D);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        const float* w = is_q ? a.qn_w : a.kn_w;
+        float y[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) y[k] = __fmul_rn(__fmul_rn(x[k], scale), w[lane + 32 * k]);
+        const float2* cs = a.rope + (size_t)pos * (D / 2);
+        // pair (y[0], y[2]) uses rotation index lane, pair (y[1], y[3]) index lane + 32
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const float2 r = cs[lane + 32 * k];
+            const float x0 = y[k], x1 = y[k + 2];
+            y[k] = __fsub_rn(__fmul_rn(x0, r.x), __fmul_rn(x1, r.y));
+            y[k + 2] = __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x));
+        }
+        if (is_q) {
+            float* dst = a.q_out + ((size_t)m * a.Hq + j) * D;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = __fmul_rn(y[k], a.q_scale);
+            return;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) x[k] = y[k];
+    }
+
+    // K (rotated) or V (as projected) into the page of this row's token.
+    const int h = is_k ? (j - a.Hq) : (j - a.Hq - a.Hkv);
+    const int kv = is_k ? 0 : 1;
+    const int page = a.block_table[(size_t)a.slot[m] * a.bt_stride + pos / kPageTokens];
+    if (page < 0 || page >= a.n_pages) {
+        if (lane == 0) record_error(a.err, kDevErrBadPage);
+        return;
+    }
+    __half* dst = a.pool_layer + (size_t)page * a.Hkv * 2 * kPageTokens * D +
+                  ((size_t)(h * 2 + kv) * kPageTokens + pos % kPageTokens) * D;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = __float2half_rn(x[k]);
+}
+
+// Raw append: one warp copies one (row, layer, head) pair of 256 B K and 256 B V rows.
+__global__ void __launch_bounds__(256) kv_append_raw_kernel(RawAppendArgs a) {
+    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int total = a.M * a.n_layers * a.Hkv;
+    if (gw >= total) return;
+    const int h = gw % a.Hkv;
+    const int l = (gw / a.Hkv) % a.n_layers;
+    const int m = gw / (a.Hkv * a.n_layers);
+    const int pos = a.pos[m];
+    const int page = a.block_table[(size_t)a.slot[m] * a.bt_stride + pos / kPageTokens];
+    if (pos < 0 || page < 0 || page >= a.n_pages) {
+        if (lane == 0) record_error(a.err, kDevErrBadPage);
+        return;
+    }
+    const size_t page_elems = (size_t)a.Hkv * 2 * kPageTokens * D;
+    __half* pg = a.pool + ((size_t)l * a.n_pages + page) * page_elems;
+    const size_t src = (((size_t)m * a.n_layers + l) * a.Hkv + h) * D;
+    const int t = pos % kPageTokens;
+    // 128 halves = 16 x 16 B; lanes 0..15 copy K, lanes 16..31 copy V
+    const int c = lane & 15;
+    const __half* s = (lane < 16 ? a.k : a.v) + src;
+    __half* d = pg + ((size_t)(h * 2 + (lane < 16 ? 0 : 1)) * kPageTokens + t) * D;
+    reinterpret_cast<uint4*>(d)[c] = reinterpret_cast<const uint4*>(s)[c];
+}
+
+}  // namespace
+
+void launch_qknorm_rope_append(const AppendArgs& a, cudaStream_t s) {
+    const int n_vec = a.Hq + 2 * a.Hkv;
+    dim3 grid(a.M, (n_vec + 7) / 8);
+    qknorm_rope_append_kernel<<<grid, 256, 0, s>>>(a);
+}
+
+void launch_kv_append_raw(const RawAppendArgs& a, cudaStream_t s) {
+    const int total = a.M * a.n_layers * a.Hkv;
+    kv_append_raw_kernel<<<(total + 7) / 8, 256, 0, s>>>(a);
+}
+
+}  // namespace fa

@@ -1,0 +1,351 @@
+// Kernel (2): paged GQA decode attention over the f16 page pool.
+//
+// Replaces the reference's attention subgraph (compute/llm_ops_gpu.cpp:98-143):
+// the full-cache views, three cont(permute) copies and two ggml_repeat 8->16 GQA
+// expansions of K and V, scores = K.q/sqrt(128), diag_mask_inf, soft_max and the
+// V^T.p matmul. Here each KV head is read from HBM once and serves both of its
+// query heads (query head H uses KV head H/2, as the reference's repeat/permute
+// order gives), and the softmax is an online softmax in fp32.
+//
+// Work split: one CTA per (split of `pages_per_split` pages, KV head, row).
+// 4 warps; warp w owns pages w, w+4, ... of the split. Each warp streams its
+// pages through a private 3-stage shared-memory ring: lane 0 issues one 8 KiB
+// cp.async.bulk (TMA bulk copy, K and V of this head in this page) per stage,
+// completion is counted on an mbarrier, every wait is bounded in time.
+// Compute per page (lane = (token parity par, 8-dim chunk c)):
+//   QK  : 8 x 16 B shared loads, 16 fp32 FMAs each, then a 16-lane transpose
+//         reduction leaves lane r of each half-warp with the score of
+//         (token 2*(r/2)+par, head r%2)
+//   softmax: max and sum by xor shuffles, running (max, sum) per head in log2 units
+//   PV  : p broadcast through 128 B of shared memory, 8 x 16 B loads, 16 FMAs each
+// The 4 warps merge in shared memory; with several splits the un-normalised
+// partials go to the scratch buffer and attn_combine merges them.
+//
+// Roofline: HBM. Algorithmic bytes per (row, layer) = n_kv * 8 heads * 2 * 128 * 2 B
+// = n_kv * 4096 B; compute is 4 flop per byte read.
+#include "fa_kernels.cuh"
+
+#include <cmath>
+
+namespace fa {
+
+namespace {
+
+constexpr int D = 128;
+constexpr int WARPS = 4;
+constexpr int STAGES = 3;
+constexpr int TILE_HALVES = 2 * kPageTokens * D;   // K then V of one head in one page
+constexpr uint32_t TILE_BYTES = TILE_HALVES * 2;   // 8192
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnSmem {
+    __half tiles[WARPS][STAGES][TILE_HALVES];
+    uint64_t bars[WARPS][STAGES];
+    float q[2][D];
+    float pbuf[WARPS][32];
+    float acc[WARPS][2][D];
+    float ml[WARPS][4];
+};
+
+__device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
+    const uint4 v = lds128(p);
+    float2 a = h2_to_f2(v.x), b = h2_to_f2(v.y), c = h2_to_f2(v.z), d = h2_to_f2(v.w);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+    f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+// Reduce 16 values across the 16 lanes of a half-warp so that lane r ends with
+// the total of value index r. Each stage halves the count kept per lane.
+__device__ __forceinline__ float transpose_reduce16(float (&v)[16], int lane) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const bool b = lane & 8;
+        const float keep = b ? v[k + 8] : v[k];
+        const float send = b ? v[k] : v[k + 8];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const bool b = lane & 4;
+        const float keep = b ? v[k + 4] : v[k];
+        const float send = b ? v[k] : v[k + 4];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const bool b = lane & 2;
+        const float keep = b ? v[k + 2] : v[k];
+        const float send = b ? v[k] : v[k + 2];
+        v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    {
+        const bool b = lane & 1;
+        const float keep = b ? v[1] : v[0];
+        const float send = b ? v[0] : v[1];
+        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+    }
+    return v[0];
+}
+
+__global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
+    const int split = blockIdx.x;
+    const int h = blockIdx.y;
+    const int m = blockIdx.z;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    const int n_kv = a.pos[m] + 1;
+    const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
+    const int p_begin = split * a.pages_per_split;
+    if (p_begin >= n_row_pages) return;                 // uniform for the CTA
+    const int p_end = min(n_row_pages, p_begin + a.pages_per_split);
+    const int* bt = a.block_table + (size_t)a.slot[m] * a.bt_stride;
+
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < WARPS; ++w)
+            for (int s = 0; s < STAGES; ++s) mbar_init(&S.bars[w][s], 1);
+        fence_mbar_init();
+    }
+    {
+        const float* qg = a.q + ((size_t)m * a.Hq + 2 * h) * D;
+        S.q[0][threadIdx.x] = qg[threadIdx.x] * kLog2e;
+        S.q[1][threadIdx.x] = qg[D + threadIdx.x] * kLog2e;
+    }
+    __syncthreads();
+
+    const int span = p_end - p_begin;
+    int nw = span > warp ? (span - warp + WARPS - 1) / WARPS : 0;
+    {
+        bool bad = false;
+        for (int i = lane; i < nw; i += 32) {
+            const int pg = bt[p_begin + warp + WARPS * i];
+            bad |= (pg < 0 || pg >= a.n_pages);
+        }
+        if (__any_sync(0xffffffffu, bad)) {
+            if (lane == 0) record_error(a.err, kDevErrBadPage);
+            nw = 0;
+        }
+    }
+
+    const int c = lane & 15;
+    const int par = lane >> 4;
+    float q0[8], q1[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        q0[k] = S.q[0][8 * c + k];
+        q1[k] = S.q[1][8 * c + k];
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    float acc0[8], acc1[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { acc0[k] = 0.0f; acc1[k] = 0.0f; }
+
+    const size_t page_elems = (size_t)a.Hkv * TILE_HALVES;
+    const __half* head_base = a.pool_layer + (size_t)h * TILE_HALVES;
+    int issued = 0;
+    if (lane == 0) {
+        for (; issued < STAGES && issued < nw; ++issued) {
+            const int pg = bt[p_begin + warp + WARPS * issued];
+            mbar_arrive_expect_tx(&S.bars[warp][issued], TILE_BYTES);
+            bulk_copy_g2s(S.tiles[warp][issued], head_base + (size_t)pg * page_elems, TILE_BYTES,
+                          &S.bars[warp][issued]);
+        }
+    }
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+
+    int i = 0;
+    bool ok = true;
+    for (; i < nw; ++i) {
+        const int s = i % STAGES;
+        const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+        const bool got = mbar_wait_bounded(&S.bars[warp][s], ph);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+
+        const int t0 = (p_begin + warp + WARPS * i) * kPageTokens;
+        const int nvalid = min(kPageTokens, n_kv - t0);
+        const __half* Kt = S.tiles[warp][s];
+        const __half* Vt = Kt + kPageTokens * D;
+
+        float part[16];
+#pragma unroll
+        for (int ii = 0; ii < 8; ++ii) {
+            float f[8];
+            load8(Kt + (2 * ii + par) * D + 8 * c, f);
+            float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                s0 = fmaf(q0[k], f[k], s0);
+                s1 = fmaf(q1[k], f[k], s1);
+            }
+            part[2 * ii] = s0;
+            part[2 * ii + 1] = s1;
+        }
+        const float tot = transpose_reduce16(part, lane);
+        const int r = lane & 15;
+        const int hh = r & 1;
+        const int tt = 2 * (r >> 1) + par;
+        const float sc = tt < nvalid ? tot : -INFINITY;
+
+        float mx = sc;
+#pragma unroll
+        for (int o = 2; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mxo = __shfl_xor_sync(0xffffffffu, mx, 1);
+        const float mn0 = fmaxf(m0, hh ? mxo : mx);
+        const float mn1 = fmaxf(m1, hh ? mx : mxo);
+        const float al0 = exp2f(m0 - mn0);
+        const float al1 = exp2f(m1 - mn1);
+        const float p = exp2f(sc - (hh ? mn1 : mn0));
+        float ps = p;
+#pragma unroll
+        for (int o = 2; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        const float pso = __shfl_xor_sync(0xffffffffu, ps, 1);
+        l0 = l0 * al0 + (hh ? pso : ps);
+        l1 = l1 * al1 + (hh ? ps : pso);
+        m0 = mn0;
+        m1 = mn1;
+
+        S.pbuf[warp][lane] = p;   // lane index = par*16 + 2*ii + hh
+        __syncwarp();
+        float pv[16];
+        {
+            const float4* pb = reinterpret_cast<const float4*>(&S.pbuf[warp][par * 16]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 t = pb[k];
+                pv[4 * k] = t.x; pv[4 * k + 1] = t.y; pv[4 * k + 2] = t.z; pv[4 * k + 3] = t.w;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { acc0[k] *= al0; acc1[k] *= al1; }
+#pragma unroll
+        for (int ii = 0; ii < 8; ++ii) {
+            if (2 * ii + par < nvalid) {
+                float f[8];
+                load8(Vt + (2 * ii + par) * D + 8 * c, f);
+                const float pa = pv[2 * ii], pb = pv[2 * ii + 1];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    acc0[k] = fmaf(pa, f[k], acc0[k]);
+                    acc1[k] = fmaf(pb, f[k], acc1[k]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + STAGES < nw) {
+            fence_proxy_async_smem();
+            const int pg = bt[p_begin + warp + WARPS * (i + STAGES)];
+            mbar_arrive_expect_tx(&S.bars[warp][s], TILE_BYTES);
+            bulk_copy_g2s(S.tiles[warp][s], head_base + (size_t)pg * page_elems, TILE_BYTES, &S.bars[warp][s]);
+        }
+        if (i + STAGES < nw) ++issued;
+    }
+
+    if (!ok) {
+        // A wait gave up: flag it, then wait (bounded again) for this warp's
+        // copies still in flight so none lands after the CTA has exited.
+        if (lane == 0) record_error(a.err, kDevErrTimeout);
+        for (int k = i; k < issued; ++k) {
+            const bool done = mbar_wait_bounded(&S.bars[warp][k % STAGES], (uint32_t)(k / STAGES) & 1u);
+            (void)__all_sync(0xffffffffu, done);
+        }
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { acc0[k] = 0.0f; acc1[k] = 0.0f; }
+    }
+
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        acc0[k] += __shfl_xor_sync(0xffffffffu, acc0[k], 16);
+        acc1[k] += __shfl_xor_sync(0xffffffffu, acc1[k], 16);
+    }
+    if (lane < 16) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            S.acc[warp][0][8 * c + k] = acc0[k];
+            S.acc[warp][1][8 * c + k] = acc1[k];
+        }
+    }
+    if (lane == 0) {
+        S.ml[warp][0] = m0; S.ml[warp][1] = m1;
+        S.ml[warp][2] = l0; S.ml[warp][3] = l1;
+    }
+    __syncthreads();
+
+    const int d = threadIdx.x;
+#pragma unroll
+    for (int hq = 0; hq < 2; ++hq) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < WARPS; ++w) M = fmaxf(M, S.ml[w][hq]);
+        float L = 0.0f, O = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < WARPS; ++w) {
+                const float sc = exp2f(S.ml[w][hq] - M);
+                L += S.ml[w][2 + hq] * sc;
+                O += S.acc[w][hq][d] * sc;
+            }
+        }
+        const int H = 2 * h + hq;
+        if (a.n_splits == 1) {
+            const float v = L > 0.0f ? O / L : 0.0f;
+            const size_t o = (size_t)m * a.Hq * D + (size_t)H * D + d;
+            if (a.out16) a.out16[o] = __float2half_rn(v);
+            if (a.out32) a.out32[o] = v;
+        } else {
+            const size_t base = ((size_t)m * a.Hq + H) * a.n_splits + split;
+            a.part_o[base * D + d] = O;
+            if (d == 0) {
+                a.part_ml[base * 2] = M;
+                a.part_ml[base * 2 + 1] = L;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
+    const int m = blockIdx.x / a.Hq;
+    const int H = blockIdx.x % a.Hq;
+    const int d = threadIdx.x;
+    const int n_kv = a.pos[m] + 1;
+    const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
+    const int n_valid = min(a.n_splits, (n_row_pages + a.pages_per_split - 1) / a.pages_per_split);
+    const size_t base = ((size_t)m * a.Hq + H) * a.n_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < n_valid; ++s) M = fmaxf(M, a.part_ml[(base + s) * 2]);
+    float L = 0.0f, O = 0.0f;
+    if (M != -INFINITY) {
+        for (int s = 0; s < n_valid; ++s) {
+            const float sc = exp2f(a.part_ml[(base + s) * 2] - M);
+            L += a.part_ml[(base + s) * 2 + 1] * sc;
+            O += a.part_o[(base + s) * D + d] * sc;
+        }
+    }
+    const float v = L > 0.0f ? O / L : 0.0f;
+    const size_t o = (size_t)m * a.Hq * D + (size_t)H * D + d;
+    if (a.out16) a.out16[o] = __float2half_rn(v);
+    if (a.out32) a.out32[o] = v;
+}
+
+}  // namespace
+
+size_t attn_smem_bytes() { return sizeof(AttnSmem); }
+
+// Opt the kernel into its dynamic shared memory on the current device.
+void configure_attention() {
+    cudaFuncSetAttribute(paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttnSmem));
+}
+
+void launch_paged_attention(const AttnArgs& a, cudaStream_t s) {
+    dim3 grid(a.n_splits, a.Hkv, a.M);
+    paged_attn_kernel<<<grid, 128, sizeof(AttnSmem), s>>>(a);
+}
+
+void launch_attn_combine(const AttnArgs& a, cudaStream_t s) {
+    attn_combine_kernel<<<a.M * a.Hq, 128, 0, s>>>(a);
+}
+
+}  // namespace fa

@@ -1,0 +1,246 @@
+// Small fused kernels around the three big ones:
+//   embed            : token -> f32 hidden row (pipeline/prompt_builder.hpp:93-113, BF16/F16/F32
+//                      tables), done on the device instead of on the host per token
+//   residual_rmsnorm : x += sum of split-K partials of the previous projection
+//                      (ggml_add residual, compute/llm_ops_gpu.cpp:172,182), then
+//                      f16(rms_norm(x) * w) for the next GEMM (gpu_rms_norm, :16-25)
+//   swiglu           : f16(silu(gate) * up) from the gate/up GEMM partials (:177-180)
+//   argmax_reduce    : first maximum over lm_head tiles (compute/gpu_runner.hpp:108-118)
+//   repack_q8        : GGUF Q8_0 blocks -> int8 matrix + transposed f16 scales
+//   page_copy / fill_random / read_pages / apply_bt_updates : page-pool maintenance
+#include "fa_kernels.cuh"
+
+namespace fa {
+
+namespace {
+
+template <int NT>
+__device__ __forceinline__ double block_sum_double(double v, double* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+    if (threadIdx.x < 32) {
+        t = threadIdx.x < NT / 32 ? sh[threadIdx.x] : 0.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        if (threadIdx.x == 0) sh[0] = t;
+    }
+    __syncthreads();
+    t = sh[0];
+    __syncthreads();
+    return t;
+}
+
+__global__ void __launch_bounds__(256) embed_kernel(const void* table, int table_type, int hidden,
+                                                    const int* tokens, const float* embeds, int vocab,
+                                                    float* x, int* err) {
+    const int m = blockIdx.x;
+    float* dst = x + (size_t)m * hidden;
+    if (embeds) {
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = embeds[(size_t)m * hidden + i];
+        return;
+    }
+    const int tok = tokens[m];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0) record_error(err, kDevErrBadPage);
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = 0.0f;
+        return;
+    }
+    const size_t off = (size_t)tok * hidden;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        float v;
+        if (table_type == 30) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(table)[off + i]);
+        else if (table_type == 1) v = __half2float(reinterpret_cast<const __half*>(table)[off + i]);
+        else v = reinterpret_cast<const float*>(table)[off + i];
+        dst[i] = v;
+    }
+}
+
+__global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const float* part, int n_part, int M,
+                                                               int hidden, const float* w, float eps,
+                                                               __half* xn16) {
+    __shared__ double sh[8];
+    const int m = blockIdx.x;
+    float* xr = x + (size_t)m * hidden;
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < hidden; i += 256) {
+        float v = xr[i];
+        if (n_part > 0) {
+            float o = 0.0f;
+            for (int s = 0; s < n_part; ++s) o = __fadd_rn(o, part[((size_t)s * M + m) * hidden + i]);
+            v = __fadd_rn(v, o);
+            xr[i] = v;
+        }
+        ss += (double)__fmul_rn(v, v);
+    }
+    ss = block_sum_double<256>(ss, sh);
+    const float mean = (float)(ss / (double)hidden);
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+    for (int i = threadIdx.x; i < hidden; i += 256)
+        xn16[(size_t)m * hidden + i] = __float2half_rn(__fmul_rn(__fmul_rn(xr[i], scale), w[i]));
+}
+
+__global__ void __launch_bounds__(256) swiglu_kernel(const float* part, int n_part, int M, int ffn,
+                                                     __half* h16) {
+    const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
+    if (idx >= (size_t)M * ffn) return;
+    const int m = (int)(idx / ffn), j = (int)(idx % ffn);
+    float gs = 0.0f, us = 0.0f;
+    for (int s = 0; s < n_part; ++s) {
+        const float* row = part + ((size_t)s * M + m) * 2 * ffn;
+        gs = __fadd_rn(gs, row[j]);
+        us = __fadd_rn(us, row[ffn + j]);
+    }
+    const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
+    h16[idx] = __float2half_rn(__fmul_rn(sg, us));
+}
+
+__global__ void __launch_bounds__(256) argmax_reduce_kernel(const float* val, const int* idx, int n_tiles,
+                                                            int* next, int* feed_tokens, int* feed_pos) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int m = blockIdx.x;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int t = threadIdx.x; t < n_tiles; t += 256) {
+        const float v = val[(size_t)m * n_tiles + t];
+        const int i = idx[(size_t)m * n_tiles + t];
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        // all-NaN or empty rows fall back to index 0, as the reference's scan does
+        if (bi == 0x7fffffff) bi = 0;
+        next[m] = bi;
+        if (feed_tokens) feed_tokens[m] = bi;
+        if (feed_pos) feed_pos[m] += 1;
+    }
+}
+
+__global__ void apply_bt_updates_kernel(int* bt, const int* upd_idx, const int* upd_page, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) bt[upd_idx[i]] = upd_page[i];
+}
+
+__global__ void repack_q8_kernel(const uint8_t* raw, int N, int K, int r0, int interleave, int8_t* dst_q,
+                                 __half* dst_d, int ldn) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = K / kQK;
+    if (i >= (size_t)N * nb) return;
+    const int n = (int)(i / nb), b = (int)(i % nb);
+    const uint8_t* blk = raw + i * kQBytes;
+    const uint16_t dbits = (uint16_t)blk[0] | ((uint16_t)blk[1] << 8);
+    int row;
+    if (interleave == 0) row = r0 + n;
+    else row = (n / 8) * 16 + (interleave - 1) * 8 + n % 8;
+    dst_d[(size_t)b * ldn + row] = __ushort_as_half(dbits);
+    int8_t* q = dst_q + (size_t)row * K + (size_t)b * kQK;
+#pragma unroll
+    for (int j = 0; j < kQK; ++j) q[j] = (int8_t)blk[2 + j];
+}
+
+__global__ void __launch_bounds__(256) page_copy_kernel(__half* pool, size_t layer_stride, const int* src,
+                                                        const int* dst, size_t page_elems) {
+    const int i = blockIdx.x, l = blockIdx.y;
+    const uint4* s = reinterpret_cast<const uint4*>(pool + l * layer_stride + (size_t)src[i] * page_elems);
+    uint4* d = reinterpret_cast<uint4*>(pool + l * layer_stride + (size_t)dst[i] * page_elems);
+    const size_t n16 = page_elems * 2 / 16;
+    for (size_t k = threadIdx.x; k < n16; k += 256) d[k] = s[k];
+}
+
+__device__ __forceinline__ uint32_t hash32(uint64_t x) {
+    x ^= x >> 33;
+    x *= 0xff51afd7ed558ccdull;
+    x ^= x >> 33;
+    x *= 0xc4ceb9fe1a85ec53ull;
+    x ^= x >> 33;
+    return (uint32_t)x;
+}
+
+// Fills whole pages with deterministic values in [-2, 2): synthetic steady-state cache.
+__global__ void __launch_bounds__(256) fill_random_kernel(__half* pool, size_t layer_stride, const int* pages,
+                                                          size_t page_elems, unsigned long long seed) {
+    const int i = blockIdx.x, l = blockIdx.y;
+    __half* d = pool + l * layer_stride + (size_t)pages[i] * page_elems;
+    for (size_t k = threadIdx.x; k < page_elems; k += 256) {
+        const uint32_t h = hash32(seed ^ ((((uint64_t)l << 40) | ((uint64_t)pages[i] << 20)) + k * 0x9e3779b97f4a7c15ull));
+        d[k] = __float2half_rn((float)(h >> 8) * (4.0f / 16777216.0f) - 2.0f);
+    }
+}
+
+__global__ void __launch_bounds__(256) read_pages_kernel(const __half* pool_layer, const int* pages,
+                                                         size_t page_elems, __half* out) {
+    const int i = blockIdx.x;
+    const uint4* s = reinterpret_cast<const uint4*>(pool_layer + (size_t)pages[i] * page_elems);
+    uint4* d = reinterpret_cast<uint4*>(out + (size_t)i * page_elems);
+    const size_t n16 = page_elems * 2 / 16;
+    for (size_t k = threadIdx.x; k < n16; k += 256) d[k] = s[k];
+}
+
+}  // namespace
+
+void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds, int M,
+                  int vocab, float* x, int* err, cudaStream_t s) {
+    embed_kernel<<<M, 256, 0, s>>>(table, table_type, hidden, tokens, embeds, vocab, x, err);
+}
+
+void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w, float eps,
+                             __half* xn16, cudaStream_t s) {
+    residual_rmsnorm_kernel<<<M, 256, 0, s>>>(x, part, n_part, M, hidden, w, eps, xn16);
+}
+
+void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h16, cudaStream_t s) {
+    const size_t n = (size_t)M * ffn;
+    swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, n_part, M, ffn, h16);
+}
+
+void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,
+                          int* feed_pos, cudaStream_t s) {
+    argmax_reduce_kernel<<<M, 256, 0, s>>>(val, idx, n_tiles, next, feed_tokens, feed_pos);
+}
+
+void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* upd_page, int n, cudaStream_t s) {
+    if (n <= 0) return;
+    apply_bt_updates_kernel<<<(n + 255) / 256, 256, 0, s>>>(block_table, upd_idx, upd_page, n);
+}
+
+void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, int interleave, int8_t* dst_q, __half* dst_d,
+                      int ldn, cudaStream_t s) {
+    const size_t n = (size_t)N * (K / kQK);
+    repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, N, K, r0, interleave, dst_q, dst_d, ldn);
+}
+
+void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,
+                      cudaStream_t s) {
+    if (n <= 0) return;
+    const size_t page_elems = (size_t)8 * 2 * kPageTokens * 128;
+    page_copy_kernel<<<dim3(n, n_layers), 256, 0, s>>>(pool, layer_stride, src, dst, page_elems);
+}
+
+void launch_fill_random(__half* pool, size_t layer_stride, int n_layers, const int* pages, int n_pages_list,
+                        unsigned long long seed, cudaStream_t s) {
+    if (n_pages_list <= 0) return;
+    const size_t page_elems = (size_t)8 * 2 * kPageTokens * 128;
+    fill_random_kernel<<<dim3(n_pages_list, n_layers), 256, 0, s>>>(pool, layer_stride, pages, page_elems, seed);
+}
+
+void launch_read_pages(const __half* pool_layer, const int* pages, int n, __half* out, cudaStream_t s) {
+    if (n <= 0) return;
+    const size_t page_elems = (size_t)8 * 2 * kPageTokens * 128;
+    read_pages_kernel<<<n, 256, 0, s>>>(pool_layer, pages, page_elems, out);
+}
+
+}  // namespace fa

@@ -1,0 +1,378 @@
+"""ctypes binding of libfunasr_dec.so (include/funasr_dec.h).
+
+The library is the product: every call here goes to the CUDA path, and a
+failure raises FaError; there is no CPU fallback. `Decoder` mirrors the
+reference's GPUContext / GPURunner / KVCache roles (compute/gpu_context.hpp,
+compute/gpu_runner.hpp, compute/kv_cache.hpp) over one fa_ctx.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+from typing import Dict, Optional, Sequence, Tuple
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libfunasr_dec.so")
+HEADER = os.path.join(ROOT, "include", "funasr_dec.h")
+
+FA_OK = 0
+ERRORS = {
+    -1: "INVALID_ARG", -2: "CUDA", -3: "OOM", -4: "POOL_EXHAUSTED", -5: "SEQ", -6: "CAPACITY",
+    -7: "WEIGHTS", -8: "TIMEOUT", -9: "NOT_READY", -10: "DEVICE",
+}
+FA_ERR_POOL_EXHAUSTED = -4
+FA_ERR_SEQ = -5
+FA_ERR_CAPACITY = -6
+FA_ERR_WEIGHTS = -7
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_BF16 = 0, 1, 8, 30
+PAGE_TOKENS = 16
+
+
+class FaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class _Desc(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("n_heads", ctypes.c_int),
+        ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("ffn", ctypes.c_int),
+        ("vocab", ctypes.c_int), ("rope_base", ctypes.c_float), ("rms_eps", ctypes.c_float),
+        ("max_ctx", ctypes.c_int), ("n_pages", ctypes.c_int), ("kv_bytes", ctypes.c_size_t),
+        ("max_seqs", ctypes.c_int), ("max_rows", ctypes.c_int),
+    ]
+
+
+class _TensorView(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_int), ("ne", ctypes.c_int64 * 2),
+                ("data", ctypes.c_void_p), ("nbytes", ctypes.c_size_t)]
+
+
+_lib = None
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+
+
+def header_functions() -> list:
+    """Names of every function the C header declares."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(fa_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib():
+    """Load the library (build it first with funasr-ggml_b200/build.py)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FaError(-2, f"{LIB_PATH} is missing; run `python funasr-ggml_b200/build.py`")
+    L = ctypes.CDLL(LIB_PATH)
+    sig = {
+        "fa_version": ([], ctypes.c_char_p),
+        "fa_last_error": ([_P], ctypes.c_char_p),
+        "fa_default_desc": ([ctypes.POINTER(_Desc)], None),
+        "fa_create": ([_I, ctypes.POINTER(_Desc)], _P),
+        "fa_destroy": ([_P], None),
+        "fa_load_weights": ([_P, ctypes.POINTER(_TensorView), _I], _I),
+        "fa_set_stream": ([_P, _P], _I),
+        "fa_set_graphs": ([_P, _I], _I),
+        "fa_pool_info": ([_P, _P, _P, _P], _I),
+        "fa_seq_open": ([_P, _I, _P], _I),
+        "fa_seq_close": ([_P, _I], _I),
+        "fa_seq_length": ([_P, _I, _P], _I),
+        "fa_seq_truncate": ([_P, _I, _I], _I),
+        "fa_seq_block_table": ([_P, _I, _P, _I, _P], _I),
+        "fa_forward": ([_P, _I, _P, _P, _P, _P, _P], _I),
+        "fa_prefill": ([_P, _I, _P, _I, _P, _P], _I),
+        "fa_decode_step": ([_P, _I, _P, _P, _P, _P], _I),
+        "fa_generate": ([_P, _I, _P, _P, _I, _P, _P], _I),
+        "fa_kv_read_pages": ([_P, _I, _P, _I, _P], _I),
+        "fa_kv_append": ([_P, _I, _P, _P, _P], _I),
+        "fa_kv_fill_synthetic": ([_P, _I, _I, ctypes.c_uint64], _I),
+        "fa_pool_compact": ([_P, _P], _I),
+        "fa_profile": ([_P, _I], _I),
+        "fa_profile_attention": ([_P, _P, _P], _I),
+        "fa_step_launches": ([_P, _P], _I),
+        "fa_op_qknorm_rope_append": ([_P, _I, _P, _P, _P, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P, _P, _P, _P], _I),
+        "fa_op_kv_append": ([_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P], _I),
+        "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
+        "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
+        "fa_op_repack_q8": ([_P, _I, _I, _P, _P, _P], _I),
+        "fa_op_q8_gemm": ([_P, _I, _I, _P, _P, _I, _I, _P, _P], _I),
+        "fa_op_argmax_scratch_bytes": ([_I, _I], ctypes.c_size_t),
+        "fa_op_q8_gemm_argmax": ([_P, _I, _I, _P, _P, _I, _P, _P, _P, _P], _I),
+        "fa_palloc_create": ([_I], _P),
+        "fa_palloc_destroy": ([_P], None),
+        "fa_palloc_alloc": ([_P], _I),
+        "fa_palloc_free": ([_P, _I], _I),
+        "fa_palloc_n_free": ([_P], _I),
+        "fa_palloc_compact": ([_P, _P, _P, _I, _P], _I),
+    }
+    for name, (args, res) in sig.items():
+        f = getattr(L, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = L
+    return L
+
+
+def last_error(ctx=None) -> str:
+    s = lib().fa_last_error(ctx)
+    return s.decode() if s else ""
+
+
+def _check(rc: int, ctx=None) -> int:
+    if rc < 0:
+        raise FaError(rc, last_error(ctx))
+    return rc
+
+
+def _p(a: Optional[np.ndarray]):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+def default_desc(**over) -> _Desc:
+    d = _Desc()
+    lib().fa_default_desc(ctypes.byref(d))
+    for k, v in over.items():
+        setattr(d, k, v)
+    return d
+
+
+# ------------------------------------------------------------------ Decoder --
+class Decoder:
+    """One fa_ctx on one GPU: weights, the paged KV pool, sequences and steps."""
+
+    def __init__(self, device: int = 0, **desc):
+        self.desc = default_desc(**desc)
+        self.ctx = lib().fa_create(device, ctypes.byref(self.desc))
+        if not self.ctx:
+            raise FaError(-2, last_error(None))
+        self.hidden = self.desc.hidden
+        self.vocab = self.desc.vocab
+        self.n_layers = self.desc.n_layers
+
+    def close(self):
+        if getattr(self, "ctx", None):
+            lib().fa_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _c(self, rc):
+        return _check(rc, self.ctx)
+
+    # weights ----------------------------------------------------------------
+    def load_weights(self, weights: Dict[str, Tuple[int, Sequence[int], np.ndarray]]):
+        views = (_TensorView * len(weights))()
+        keep = []
+        for i, (name, (t, ne, arr)) in enumerate(weights.items()):
+            arr = np.ascontiguousarray(arr)
+            keep.append(arr)
+            nb = name.encode()
+            keep.append(nb)
+            views[i].name = nb
+            views[i].type = t
+            views[i].ne[0] = int(ne[0])
+            views[i].ne[1] = int(ne[1]) if len(ne) > 1 else 1
+            views[i].data = arr.ctypes.data
+            views[i].nbytes = arr.nbytes
+        self._c(lib().fa_load_weights(self.ctx, views, len(weights)))
+
+    def set_stream(self, stream_ptr: Optional[int]):
+        self._c(lib().fa_set_stream(self.ctx, stream_ptr))
+
+    def set_graphs(self, enable: bool):
+        self._c(lib().fa_set_graphs(self.ctx, int(enable)))
+
+    def pool_info(self):
+        n = ctypes.c_int(); f = ctypes.c_int(); b = ctypes.c_size_t()
+        self._c(lib().fa_pool_info(self.ctx, ctypes.byref(n), ctypes.byref(f), ctypes.byref(b)))
+        return n.value, f.value, b.value
+
+    # sequences --------------------------------------------------------------
+    def seq_open(self, max_tokens: int) -> int:
+        sid = ctypes.c_int()
+        self._c(lib().fa_seq_open(self.ctx, int(max_tokens), ctypes.byref(sid)))
+        return sid.value
+
+    def seq_close(self, sid: int):
+        self._c(lib().fa_seq_close(self.ctx, int(sid)))
+
+    def seq_length(self, sid: int) -> int:
+        n = ctypes.c_int()
+        self._c(lib().fa_seq_length(self.ctx, int(sid), ctypes.byref(n)))
+        return n.value
+
+    def seq_truncate(self, sid: int, n: int):
+        self._c(lib().fa_seq_truncate(self.ctx, int(sid), int(n)))
+
+    def block_table(self, sid: int) -> np.ndarray:
+        n = ctypes.c_int()
+        self._c(lib().fa_seq_block_table(self.ctx, int(sid), None, 0, ctypes.byref(n)))
+        out = np.zeros(n.value, np.int32)
+        self._c(lib().fa_seq_block_table(self.ctx, int(sid), _p(out), n.value, ctypes.byref(n)))
+        return out
+
+    # steps ------------------------------------------------------------------
+    def forward(self, seq_ids, tokens=None, embeds=None, want_logits=False):
+        sids = _i32(seq_ids)
+        M = len(sids)
+        tok = None if tokens is None else _i32(tokens)
+        emb = None if embeds is None else np.ascontiguousarray(embeds, np.float32)
+        nxt = np.zeros(M, np.int32)
+        lg = np.zeros((M, self.vocab), np.float32) if want_logits else None
+        self._c(lib().fa_forward(self.ctx, M, _p(sids), _p(tok), _p(emb), _p(nxt), _p(lg)))
+        return nxt, lg
+
+    def decode_step(self, seq_ids, tokens, want_logits=False):
+        sids = _i32(seq_ids)
+        tok = _i32(tokens)
+        nxt = np.zeros(len(sids), np.int32)
+        lg = np.zeros((len(sids), self.vocab), np.float32) if want_logits else None
+        self._c(lib().fa_decode_step(self.ctx, len(sids), _p(sids), _p(tok), _p(nxt), _p(lg)))
+        return nxt, lg
+
+    def prefill(self, sid: int, embeds: np.ndarray, want_logits=False):
+        emb = np.ascontiguousarray(embeds, np.float32)
+        nxt = ctypes.c_int()
+        lg = np.zeros(self.vocab, np.float32) if want_logits else None
+        self._c(lib().fa_prefill(self.ctx, int(sid), _p(emb), emb.shape[0], ctypes.byref(nxt), _p(lg)))
+        return nxt.value, lg
+
+    def generate(self, seq_ids, first_tokens, n_steps: int):
+        sids = _i32(seq_ids)
+        tok = _i32(first_tokens)
+        out = np.zeros((n_steps, len(sids)), np.int32)
+        ms = ctypes.c_float()
+        self._c(lib().fa_generate(self.ctx, len(sids), _p(sids), _p(tok), int(n_steps), _p(out), ctypes.byref(ms)))
+        return out, ms.value
+
+    # pages ------------------------------------------------------------------
+    def kv_read_pages(self, layer: int, pages) -> np.ndarray:
+        pg = _i32(pages)
+        out = np.zeros((len(pg), 8 * 2 * PAGE_TOKENS * 128), np.uint16)
+        self._c(lib().fa_kv_read_pages(self.ctx, int(layer), _p(pg), len(pg), _p(out)))
+        return out
+
+    def kv_append(self, seq_ids, k16: np.ndarray, v16: np.ndarray):
+        sids = _i32(seq_ids)
+        k16 = np.ascontiguousarray(k16, np.uint16)
+        v16 = np.ascontiguousarray(v16, np.uint16)
+        self._c(lib().fa_kv_append(self.ctx, len(sids), _p(sids), _p(k16), _p(v16)))
+
+    def kv_fill_synthetic(self, sid: int, n_tokens: int, seed: int = 0):
+        self._c(lib().fa_kv_fill_synthetic(self.ctx, int(sid), int(n_tokens), ctypes.c_uint64(seed)))
+
+    def pool_compact(self) -> int:
+        n = ctypes.c_int()
+        self._c(lib().fa_pool_compact(self.ctx, ctypes.byref(n)))
+        return n.value
+
+    # measurement --------------------------------------------------------------
+    def profile(self, enable: bool):
+        self._c(lib().fa_profile(self.ctx, int(enable)))
+
+    def profile_attention(self):
+        ms = ctypes.c_float(); n = ctypes.c_int()
+        self._c(lib().fa_profile_attention(self.ctx, ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value
+
+    def step_launches(self) -> int:
+        n = ctypes.c_int()
+        self._c(lib().fa_step_launches(self.ctx, ctypes.byref(n)))
+        return n.value
+
+
+# ------------------------------------------------------- kernel-level ops --
+def op_qknorm_rope_append(qkv, M, pos, slot, bt, bt_stride, n_pages, qn, kn, eps, rope, max_pos, pool, q_out,
+                          err=0, stream=0):
+    _check(lib().fa_op_qknorm_rope_append(qkv, M, pos, slot, bt, bt_stride, n_pages, qn, kn, eps, rope, max_pos,
+                                          pool, q_out, err or None, stream or None))
+
+
+def op_kv_append(k, v, M, n_layers, pos, slot, bt, bt_stride, n_pages, pool, err=0, stream=0):
+    _check(lib().fa_op_kv_append(k, v, M, n_layers, pos, slot, bt, bt_stride, n_pages, pool, err or None,
+                                 stream or None))
+
+
+def op_attention_scratch_bytes(M, n_splits) -> int:
+    return int(lib().fa_op_attention_scratch_bytes(M, n_splits))
+
+
+def op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits, scratch, out16=0, out32=0,
+                       err=0, stream=0):
+    _check(lib().fa_op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits,
+                                       scratch or None, out16 or None, out32 or None, err or None, stream or None))
+
+
+def op_repack_q8(raw, N, K, q, d, stream=0):
+    _check(lib().fa_op_repack_q8(raw, N, K, q, d, stream or None))
+
+
+def op_q8_gemm(a16, M, K, q, d, N, n_split, c, stream=0):
+    _check(lib().fa_op_q8_gemm(a16, M, K, q, d, N, n_split, c, stream or None))
+
+
+def op_argmax_scratch_bytes(M, N) -> int:
+    return int(lib().fa_op_argmax_scratch_bytes(M, N))
+
+
+def op_q8_gemm_argmax(a16, M, K, q, d, N, scratch, nxt, logits=0, stream=0):
+    _check(lib().fa_op_q8_gemm_argmax(a16, M, K, q, d, N, scratch, nxt, logits or None, stream or None))
+
+
+# ------------------------------------------------------ host page allocator --
+class PageAllocator:
+    """Host-only view of the library's page allocation policy (no GPU needed)."""
+
+    def __init__(self, n_pages: int):
+        self.n_pages = int(n_pages)
+        self.h = lib().fa_palloc_create(int(n_pages))
+        if not self.h:
+            raise FaError(-1, last_error(None))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().fa_palloc_destroy(self.h)
+            self.h = None
+
+    def alloc(self) -> int:
+        return _check(lib().fa_palloc_alloc(self.h))
+
+    def free(self, page: int):
+        _check(lib().fa_palloc_free(self.h, int(page)))
+
+    def n_free(self) -> int:
+        return _check(lib().fa_palloc_n_free(self.h))
+
+    def compact_moves(self):
+        """Apply compaction; returns the (src, dst) page moves in order."""
+        src = np.zeros(self.n_pages, np.int32)
+        dst = np.zeros_like(src)
+        n = ctypes.c_int()
+        _check(lib().fa_palloc_compact(self.h, _p(src), _p(dst), len(src), ctypes.byref(n)))
+        return src[: n.value].tolist(), dst[: n.value].tolist()

@@ -1,0 +1,83 @@
+"""Seeded random-init decoder weights and synthetic inputs (no checkpoints, no datasets).
+
+Weights follow the reference's Q8_0 build (tools/hf_convert_ggml_q8.py:312-320):
+every 2-D projection and lm_head is Q8_0, embed_tokens and the norms BF16.
+Q8_0 blocks are drawn directly: int8 values ~ U[-127, 127], f16 scales
+~ U(0.001, 0.02). Tensor names follow model/loader.cpp:91-117,217-227.
+"""
+from __future__ import annotations
+
+from typing import Dict, Tuple
+
+import numpy as np
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_BF16 = 0, 1, 8, 30
+
+# Qwen3-0.6B decoder of FunASR-Nano (funasr_gguf.md header; core/config.hpp:119-136).
+QWEN3_06B = dict(n_layers=28, hidden=1024, n_heads=16, n_kv_heads=8, head_dim=128, ffn=3072, vocab=151936,
+                 eps=1e-5, rope_base=1e6)
+
+
+def small_config(n_layers=2, hidden=256, ffn=512, vocab=2048):
+    """Same attention geometry (16/8 heads x 128), fewer/smaller everything else."""
+    return dict(QWEN3_06B, n_layers=n_layers, hidden=hidden, ffn=ffn, vocab=vocab)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def q8_0_random(rng: np.random.Generator, n: int, k: int, d_lo=0.001, d_hi=0.02) -> np.ndarray:
+    """[n][k/32*34] uint8 Q8_0 rows with random int8 values and f16 scales."""
+    nb = k // 32
+    blocks = np.empty((n, nb, 34), np.uint8)
+    d = rng.uniform(d_lo, d_hi, size=(n, nb)).astype(np.float16)
+    blocks[:, :, :2] = d.view(np.uint8).reshape(n, nb, 2)
+    blocks[:, :, 2:] = rng.integers(-127, 128, size=(n, nb, 32), dtype=np.int8).view(np.uint8)
+    return blocks.reshape(n, nb * 34)
+
+
+def make_weights(cfg: dict, seed: int = 0) -> Dict[str, Tuple[int, Tuple[int, int], np.ndarray]]:
+    """name -> (ggml type, ne (input dim first), data) for one random-init decoder."""
+    rng = np.random.default_rng(seed)
+    H, F, V = cfg["hidden"], cfg["ffn"], cfg["vocab"]
+    QD = cfg["n_heads"] * cfg["head_dim"]
+    KD = cfg["n_kv_heads"] * cfg["head_dim"]
+    D = cfg["head_dim"]
+    w = {}
+
+    def bf16(shape, lo, hi):
+        return f32_to_bf16_bits(rng.uniform(lo, hi, size=shape).astype(np.float32))
+
+    w["llm.model.embed_tokens.weight"] = (TYPE_BF16, (H, V), f32_to_bf16_bits(
+        (rng.standard_normal((V, H), dtype=np.float32) * 0.05)))
+    w["llm.model.norm.weight"] = (TYPE_BF16, (H, 1), bf16(H, 0.8, 1.2))
+    w["llm.lm_head.weight"] = (TYPE_Q8_0, (H, V), q8_0_random(rng, V, H))
+    for i in range(cfg["n_layers"]):
+        p = f"llm.model.layers.{i}."
+        w[p + "self_attn.q_proj.weight"] = (TYPE_Q8_0, (H, QD), q8_0_random(rng, QD, H))
+        w[p + "self_attn.k_proj.weight"] = (TYPE_Q8_0, (H, KD), q8_0_random(rng, KD, H))
+        w[p + "self_attn.v_proj.weight"] = (TYPE_Q8_0, (H, KD), q8_0_random(rng, KD, H))
+        w[p + "self_attn.o_proj.weight"] = (TYPE_Q8_0, (QD, H), q8_0_random(rng, H, QD))
+        w[p + "mlp.gate_proj.weight"] = (TYPE_Q8_0, (H, F), q8_0_random(rng, F, H))
+        w[p + "mlp.up_proj.weight"] = (TYPE_Q8_0, (H, F), q8_0_random(rng, F, H))
+        w[p + "mlp.down_proj.weight"] = (TYPE_Q8_0, (F, H), q8_0_random(rng, H, F))
+        w[p + "self_attn.q_norm.weight"] = (TYPE_BF16, (D, 1), bf16(D, 0.8, 1.2))
+        w[p + "self_attn.k_norm.weight"] = (TYPE_BF16, (D, 1), bf16(D, 0.8, 1.2))
+        w[p + "input_layernorm.weight"] = (TYPE_BF16, (H, 1), bf16(H, 0.8, 1.2))
+        w[p + "post_attention_layernorm.weight"] = (TYPE_BF16, (H, 1), bf16(H, 0.8, 1.2))
+    return w
+
+
+def decoder_desc(cfg: dict, **over) -> dict:
+    """Keyword arguments for fa_dec.Decoder from a config dict."""
+    d = dict(n_layers=cfg["n_layers"], hidden=cfg["hidden"], ffn=cfg["ffn"], vocab=cfg["vocab"],
+             rope_base=cfg.get("rope_base", 1e6), rms_eps=cfg.get("eps", 1e-5))
+    d.update(over)
+    return d
+
+
+def audio_embeds(rng: np.random.Generator, n: int, hidden: int, scale: float = 1.0) -> np.ndarray:
+    """Stand-in for adaptor output frames [n][hidden] (the encoder is out of scope)."""
+    return (rng.standard_normal((n, hidden), dtype=np.float32) * scale).astype(np.float32)

@@ -1,0 +1,219 @@
+/* funasr_dec.h — C ABI of the B200 (sm_100a) FunASR LLM-decoder hot path.
+ *
+ * The library replaces the reference's decoder KV-cache path:
+ *   compute/kv_cache.hpp                 KVCache (f32 [layer][pos][1024], one sequence)
+ *   compute/gpu_context.hpp:66-78,98-122,220-349
+ *                                        GPUKVCache, weight upload, KV alloc/clear
+ *   compute/llm_ops_gpu.cpp:34-207       Qwen3 decoder graph (ggml-cuda)
+ *   compute/gpu_runner.hpp:44-236        warmup / forward / argmax
+ *   pipeline/pipeline.cpp:434-451        greedy decode loop
+ * with a paged f16 KV cache shared by many sequences, batched forwards over
+ * rows (one row = one token of one sequence) and hand-written CUDA kernels.
+ *
+ * Conventions
+ *   - Every call returns FA_OK (0) or a negative FA_ERR_* code; the message of the
+ *     last failure is fa_last_error(ctx) (fa_last_error(NULL) for calls without a
+ *     context). There is no CPU fallback: without a usable GPU, fa_create fails.
+ *   - Host pointers unless the name says _dev. Shapes are row-major C arrays.
+ *   - One fa_ctx per GPU. A context is not thread-safe; use one host thread per
+ *     context (the reference also drives one GPURunner from one thread).
+ *   - Model geometry fixed by the kernels: head_dim 128, 16 query heads, 8 KV heads
+ *     (Qwen3-0.6B as used by FunASR-Nano). n_layers, hidden, ffn, vocab are free
+ *     (hidden, ffn, vocab multiples of 64).
+ */
+#ifndef FUNASR_DEC_H
+#define FUNASR_DEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FA_API __attribute__((visibility("default")))
+#else
+#define FA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA_OK 0
+#define FA_ERR_INVALID_ARG (-1)
+#define FA_ERR_CUDA (-2)
+#define FA_ERR_OOM (-3)            /* device allocation failed */
+#define FA_ERR_POOL_EXHAUSTED (-4) /* no free KV page; nothing of the call was applied */
+#define FA_ERR_SEQ (-5)            /* unknown / closed sequence, or no free slot */
+#define FA_ERR_CAPACITY (-6)       /* beyond max_rows, a sequence's max_tokens or max_ctx */
+#define FA_ERR_WEIGHTS (-7)        /* missing tensor, wrong type or shape */
+#define FA_ERR_TIMEOUT (-8)        /* a bounded device wait gave up */
+#define FA_ERR_NOT_READY (-9)      /* weights not loaded */
+#define FA_ERR_DEVICE (-10)        /* a kernel reported a bad page / position / token */
+
+#define FA_PAGE_TOKENS 16
+
+/* GGML tensor type ids accepted in fa_tensor_view.type. */
+#define FA_TYPE_F32 0
+#define FA_TYPE_F16 1
+#define FA_TYPE_Q8_0 8
+#define FA_TYPE_BF16 30
+
+/* Decoder geometry and runtime sizes. Mirrors LLMConfig (core/config.hpp:119-136)
+ * plus the cache sizing that replaces n_ctx (compute/gpu_context.hpp:315-349). */
+typedef struct fa_model_desc {
+    int n_layers;    /* block_count, 28 */
+    int hidden;      /* embedding_length, 1024 */
+    int n_heads;     /* head_count, 16 */
+    int n_kv_heads;  /* head_count_kv, 8 */
+    int head_dim;    /* key_length, 128 */
+    int ffn;         /* feed_forward_length, 3072 */
+    int vocab;       /* vocab_size, 151936 */
+    float rope_base; /* rope_freq_base, 1e6 */
+    float rms_eps;   /* 1e-5 (compute/llm_ops_gpu.cpp:50) */
+    int max_ctx;     /* longest sequence (RoPE table length), e.g. 40960 */
+    int n_pages;     /* KV page pool size; 0 = derive from kv_bytes */
+    size_t kv_bytes; /* pool budget in bytes when n_pages == 0 */
+    int max_seqs;    /* sequence slots */
+    int max_rows;    /* rows (tokens) per forward call: decode batch + prefill chunk */
+} fa_model_desc;
+
+/* One tensor in GGUF naming and ggml order: ne[0] is the input (fastest) dim.
+ * Replaces the host->device copies of GPUContext::load_weights
+ * (compute/gpu_context.hpp:220-310); names as model/loader.cpp:91-117,217-227. */
+typedef struct fa_tensor_view {
+    const char* name;
+    int type;          /* FA_TYPE_* */
+    int64_t ne[2];     /* ne[1] = 1 for vectors */
+    const void* data;  /* host memory in GGUF layout (Q8_0: rows of [f16 d][32 x int8]) */
+    size_t nbytes;
+} fa_tensor_view;
+
+typedef struct fa_ctx fa_ctx;
+
+/* Qwen3-0.6B decoder of FunASR-Nano with n_ctx 2048-style defaults. */
+FA_API void fa_default_desc(fa_model_desc* desc);
+
+/* ---- context: GPUContext::init / cleanup (compute/gpu_context.hpp:98-169) ---- */
+FA_API fa_ctx* fa_create(int device, const fa_model_desc* desc); /* NULL on failure: fa_last_error(NULL) */
+FA_API void fa_destroy(fa_ctx* ctx);
+FA_API const char* fa_last_error(const fa_ctx* ctx);
+FA_API int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n);
+/* Run the library's work on `cuda_stream` (a cudaStream_t of this device); NULL restores
+ * the library's own stream. */
+FA_API int fa_set_stream(fa_ctx* ctx, void* cuda_stream);
+/* 1 = launch each step as a captured CUDA graph (default), 0 = direct launches. */
+FA_API int fa_set_graphs(fa_ctx* ctx, int enable);
+/* Pool geometry: pages, free pages, bytes of one page across all layers. */
+FA_API int fa_pool_info(const fa_ctx* ctx, int* n_pages, int* n_free, size_t* page_bytes_all_layers);
+
+/* ---- sequences: KVCache::init / clear / n_past / set_n_past (compute/kv_cache.hpp:38-151),
+ *      GPUContext::clear_kv_cache (compute/gpu_context.hpp:116-122) ---- */
+FA_API int fa_seq_open(fa_ctx* ctx, int max_tokens, int* seq_id);
+FA_API int fa_seq_close(fa_ctx* ctx, int seq_id);     /* returns the sequence's pages to the pool */
+FA_API int fa_seq_length(const fa_ctx* ctx, int seq_id, int* n_tokens);
+/* Roll back to n_tokens <= current length (KVCache::set_n_past); whole pages past it are freed. */
+FA_API int fa_seq_truncate(fa_ctx* ctx, int seq_id, int n_tokens);
+/* Copies up to max_pages entries of the sequence's block table; *n_pages = its page count. */
+FA_API int fa_seq_block_table(const fa_ctx* ctx, int seq_id, int* pages, int max_pages, int* n_pages);
+
+/* ---- forward: GPURunner::forward / forward_gpu_tensor (compute/gpu_runner.hpp:82-105,136-236)
+ * One call appends one token per row to its sequence and runs the decoder over all rows.
+ * Rows of one sequence take consecutive positions in row order (chunked prefill);
+ * every row's K/V is in the cache before any row's attention, so a prefill chunk is
+ * causal within itself. Inputs: token_ids [n_rows] (embedding lookup on the device) or
+ * embeds [n_rows][hidden] f32 (audio frames; exactly one of the two).
+ * Outputs (optional): next_ids [n_rows] = argmax of each row's logits (first maximum),
+ * logits [n_rows][vocab] f32. */
+FA_API int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
+               int* next_ids, float* logits);
+/* Prefill n_tok embedding rows of one sequence in chunks of max_rows
+ * (pipeline/pipeline.cpp:405 -> GPURunner::forward_gpu_tensor); next_id/last_logits
+ * describe the last row. */
+FA_API int fa_prefill(fa_ctx* ctx, int seq_id, const float* embeds, int n_tok, int* next_id, float* last_logits);
+/* One greedy decode step for n_seq distinct sequences (pipeline/pipeline.cpp:434-451,
+ * batched): token_ids[i] is appended to seq_ids[i]. */
+FA_API int fa_decode_step(fa_ctx* ctx, int n_seq, const int* seq_ids, const int* token_ids, int* next_ids,
+                   float* logits);
+/* n_steps greedy steps with the argmax fed back on the device (no host round trip per
+ * token; EOS is not checked). out_ids [n_steps][n_seq]. device_ms (optional) = time of the
+ * n_steps steps on the device, CUDA events on the library stream, H2D/D2H excluded. */
+FA_API int fa_generate(fa_ctx* ctx, int n_seq, const int* seq_ids, const int* first_tokens, int n_steps, int* out_ids,
+                float* device_ms);
+
+/* ---- pages ---- */
+/* Copy pages of one layer ([n][kv_heads][2][16][head_dim] f16 bit patterns) to the host. */
+FA_API int fa_kv_read_pages(fa_ctx* ctx, int layer, const int* pages, int n, uint16_t* out);
+/* Append given f16 K/V for all layers: k, v [n_rows][n_layers][kv_heads][head_dim]
+ * (the raw-append microbenchmark; positions follow the sequences' lengths). */
+FA_API int fa_kv_append(fa_ctx* ctx, int n_rows, const int* seq_ids, const uint16_t* k, const uint16_t* v);
+/* Extend a sequence by n_tokens of synthetic cache content (deterministic values in
+ * [-2, 2) from seed) without running the model: steady-state decode benchmarks. */
+FA_API int fa_kv_fill_synthetic(fa_ctx* ctx, int seq_id, int n_tokens, uint64_t seed);
+/* Move live pages down into the lowest free ids (highest live page first) and rewrite
+ * the block tables; afterwards the live pages are exactly [0, n_live). */
+FA_API int fa_pool_compact(fa_ctx* ctx, int* n_moved);
+
+/* ---- measurement ---- */
+/* 1 = bracket every attention launch with CUDA events (taken into graphs when captured). */
+FA_API int fa_profile(fa_ctx* ctx, int enable);
+/* Attention launches of the last forward/generate step: summed device ms and count
+ * (paged-attention kernel plus its split combine). */
+FA_API int fa_profile_attention(fa_ctx* ctx, float* total_ms, int* n_launches);
+/* Kernels launched by the last forward step (all of this library's kernels). */
+FA_API int fa_step_launches(const fa_ctx* ctx, int* n_launches);
+
+/* ---- kernel-level entry points (device pointers, caller's stream) ----
+ * These are the kernels of one decoder layer, exposed for parity tests and
+ * microbenchmarks. `stream` is a cudaStream_t or NULL (legacy default stream). */
+
+/* Kernel (1): per-head Q/K RMSNorm + NEOX RoPE + paged f16 K/V append
+ * (compute/llm_ops_gpu.cpp:57-96). qkv_dev [M][(16+2*8)*128] f32; rope_dev
+ * [max_pos][64][2] f32 (cos, sin); pool_layer_dev [n_pages][8][2][16][128] f16;
+ * q_out_dev [M][16][128] f32 (scaled by 1/sqrt(128)). */
+FA_API int fa_op_qknorm_rope_append(const float* qkv_dev, int M, const int* pos_dev, const int* slot_dev,
+                             const int* block_table_dev, int bt_stride, int n_pages, const float* q_norm_dev,
+                             const float* k_norm_dev, float eps, const float* rope_dev, int max_pos,
+                             uint16_t* pool_layer_dev, float* q_out_dev, int* err_dev, void* stream);
+/* Raw f16 append for n_layers layers: k/v [M][n_layers][8][128]; pool [n_layers][n_pages][page]. */
+FA_API int fa_op_kv_append(const uint16_t* k_dev, const uint16_t* v_dev, int M, int n_layers, const int* pos_dev,
+                    const int* slot_dev, const int* block_table_dev, int bt_stride, int n_pages,
+                    uint16_t* pool_dev, int* err_dev, void* stream);
+/* Kernel (2): paged GQA decode attention (compute/llm_ops_gpu.cpp:98-143). Row m attends
+ * to tokens [0, pos[m]] of sequence slot[m]. q [M][16][128] f32 (pre-scaled).
+ * Output f16 and/or f32 [M][2048]. scratch_dev holds the split-K partials:
+ * fa_op_attention_scratch_bytes(M, n_splits) bytes (may be NULL when n_splits == 1). */
+FA_API size_t fa_op_attention_scratch_bytes(int M, int n_splits);
+FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
+                          const int* block_table_dev, int bt_stride, int n_pages, const uint16_t* pool_layer_dev,
+                          int pages_per_split, int n_splits, void* scratch_dev, uint16_t* out16_dev,
+                          float* out32_dev, int* err_dev, void* stream);
+/* Kernel (4): Q8_0 GEMM C = A . W^T. A [M][K] f16; W in the library's repacked form:
+ * q [N][K] int8 and d [K/32][N] f16 (fa_op_repack_q8 builds it from GGUF blocks).
+ * n_split > 1 writes partials [n_split][M][N]; fa_op_q8_gemm sums them when sum_dev is given. */
+FA_API int fa_op_repack_q8(const uint8_t* gguf_q8_dev, int N, int K, int8_t* q_dev, uint16_t* d_dev, void* stream);
+FA_API int fa_op_q8_gemm(const uint16_t* a16_dev, int M, int K, const int8_t* q_dev, const uint16_t* d_dev, int N,
+                  int n_split, float* c_dev, void* stream);
+/* lm_head with fused argmax: next [M] = first column of each row's maximum; logits optional. */
+FA_API size_t fa_op_argmax_scratch_bytes(int M, int N);
+FA_API int fa_op_q8_gemm_argmax(const uint16_t* a16_dev, int M, int K, const int8_t* q_dev, const uint16_t* d_dev,
+                         int N, void* scratch_dev, int* next_dev, float* logits_dev, void* stream);
+
+/* ---- host-only page allocator (no GPU needed): the policy behind fa_seq_* ----
+ * Lowest free page id first; compaction moves the highest live page into the lowest
+ * free id until the live pages are [0, n_live). */
+typedef struct fa_palloc fa_palloc;
+FA_API fa_palloc* fa_palloc_create(int n_pages);
+FA_API void fa_palloc_destroy(fa_palloc* pa);
+FA_API int fa_palloc_alloc(fa_palloc* pa);              /* page id, or FA_ERR_POOL_EXHAUSTED */
+FA_API int fa_palloc_free(fa_palloc* pa, int page);     /* FA_ERR_INVALID_ARG on double free / range */
+FA_API int fa_palloc_n_free(const fa_palloc* pa);
+/* Applies compaction to the allocator and returns the moves (src[i] -> dst[i]); *n_moves. */
+FA_API int fa_palloc_compact(fa_palloc* pa, int* src, int* dst, int max_moves, int* n_moves);
+
+/* Library version string. */
+FA_API const char* fa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FUNASR_DEC_H */

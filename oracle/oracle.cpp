@@ -1,0 +1,493 @@
+// oracle/oracle.cpp — CPU restatement of the FunASR-GGML LLM-decoder hot path.
+//
+// TEST INFRASTRUCTURE ONLY. This file is the checker for the CUDA path: it is
+// called from tests/, from __graft_entry__.smoke() and from bench.py's
+// cpu_baseline / reference leg, and nowhere else. Nothing in the product
+// library links or calls it.
+//
+// What it restates (reference paths are relative to the FunASR-GGML tree):
+//   compute/llm_ops.cpp:20-29    rms_norm(x, w)  = ggml_rms_norm(x, 1e-5) * cast_f32(w)
+//   compute/llm_ops.cpp:45-176   gqa_forward: Q/K/V projections, per-head Q/K
+//                                RMSNorm, NEOX RoPE (mode 2, base 1e6), KV append,
+//                                GQA 8->16 (query head H reads kv head H/2),
+//                                q * 1/sqrt(128), causal mask, softmax, V^T p, o_proj
+//   compute/llm_ops.cpp:181-210  llm_layer_forward: residual + SwiGLU MLP
+//   compute/llm_ops.cpp:215-238  llm_forward: 28 layers, final norm, lm_head
+//   compute/kv_cache.hpp:93-110  commit: K/V of the step land at [layer][pos]
+//   compute/gpu_runner.hpp:108-118 argmax: first index holding the maximum
+//   pipeline/prompt_builder.hpp:93-113 BF16 embedding row -> f32
+//   tools/hf_convert_ggml_q8.py:354-381 Q8_0 block codec (d = amax/127, f16 d + 32 int8)
+//
+// ggml op semantics restated from the published definitions of the ops
+// (ggml itself is not vendored with the reference):
+//   rms_norm : sum of f32 squares accumulated in double, mean rounded to f32,
+//              scale = 1/sqrtf(mean + eps), y = x*scale
+//   rope_ext mode 2 (NEOX): pairs (i, i+n/2), theta_i = pos * base^(-2i/n)
+//   diag_mask_inf(n_past): key j > n_past + i is masked
+//   soft_max : max-subtracted exponentials normalised by their sum
+//   mul_mat Q8_0 x f32 on the CPU backend: activations quantised to Q8_0
+//              blocks (roundf), integer block dots, f32 sum of
+//              isum * (d_w * d_x) over blocks            (GEMM mode 2)
+//
+// Decisions this oracle defines (shared with the CUDA path, stated in DESIGN.md):
+//   * KV cache is f16 in pages of 16 tokens: page layout per layer is
+//     [kv_head][K|V][token 16][head_dim], 64 KiB at 8 heads x 128 dims.
+//     Token p of a sequence lives in page block_table[slot][p/16], slot p%16.
+//     f32 -> f16 is round-to-nearest-even.
+//   * RoPE cos/sin: theta computed in double, cos/sin in double, rounded to f32
+//     once into a table [pos][i] (the same table the CUDA path uploads).
+//   * GEMM mode 1 (the CUDA path's arithmetic): activations rounded to f16,
+//     weights dequantised as f16(f32(d) * q), products exact, sums in wide precision.
+//     Mode 0 is exact f32 activations x dequantised weights.
+//   * Attention scores, softmax and PV are computed in double here.
+//
+// Parity pins: the Q8_0 codec is pinned byte-for-byte against the reference
+// converter's own quantize_q8_0 (tools/hf_convert_ggml_q8.py) and the decoder
+// math against an independent Qwen3 implementation (transformers), through the
+// fixtures in tests/golden/. The ggml kernels themselves cannot run here (ggml
+// is not vendored), so parity at the ggml boundary is pinned only through
+// those fixtures.
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+#include <algorithm>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+namespace {
+
+// ---------------------------------------------------------------- f16/bf16 ---
+inline uint32_t f_bits(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+inline float bits_f(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+
+inline float h2f(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1f;
+    uint32_t man = h & 0x3ffu;
+    if (exp == 0) {
+        if (man == 0) return bits_f(sign);
+        // subnormal: value = man * 2^-24
+        float v = (float)man * 5.9604644775390625e-08f;
+        return sign ? -v : v;
+    }
+    if (exp == 31) return bits_f(sign | 0x7f800000u | (man << 13));
+    return bits_f(sign | ((exp + 112) << 23) | (man << 13));
+}
+
+// IEEE round-to-nearest-even f32 -> f16.
+inline uint16_t f2h(float f) {
+    uint32_t x = f_bits(f);
+    uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) {                       // inf / nan
+        return sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0u);
+    }
+    if (ax >= 0x477ff000u) return sign | 0x7c00u;  // rounds to >= 65520 -> inf
+    if (ax < 0x38800000u) {                        // below 2^-14: f16 subnormal or zero
+        // value / 2^-24, rounded to nearest even integer
+        float v = bits_f(ax) * 16777216.0f;        // exact scaling by 2^24
+        float r = std::nearbyint(v);               // default rounding mode: nearest-even
+        return sign | (uint16_t)r;
+    }
+    uint32_t exp = (ax >> 23) - 112;
+    uint32_t man = ax & 0x7fffffu;
+    uint32_t hman = man >> 13;
+    uint32_t rem = man & 0x1fffu;
+    uint32_t h = (exp << 10) | hman;
+    if (rem > 0x1000u || (rem == 0x1000u && (hman & 1u))) h += 1;   // carries into exponent correctly
+    return sign | (uint16_t)h;
+}
+
+inline float bf2f(uint16_t b) { return bits_f((uint32_t)b << 16); }
+
+inline float round_f16(float x) { return h2f(f2h(x)); }
+
+constexpr int QK = 32;           // Q8_0 block length
+constexpr int QB = 34;           // Q8_0 block bytes: f16 d + 32 x int8
+
+// ---------------------------------------------------------------- rms_norm ---
+// ggml_rms_norm over n values, then * w (w already f32).
+inline void rms_norm_vec(const float* x, const float* w, int n, float eps, float* y) {
+    double sum = 0.0;
+    for (int i = 0; i < n; ++i) sum += (double)(x[i] * x[i]);
+    const float mean = (float)(sum / (double)n);
+    const float scale = 1.0f / std::sqrt(mean + eps);
+    for (int i = 0; i < n; ++i) {
+        float v = x[i] * scale;
+        y[i] = w ? v * w[i] : v;
+    }
+}
+
+// NEOX rotation in place with the table row cs[i] = (cos, sin) of pair i.
+inline void rope_neox(float* y, int d, const float* cs) {
+    const int half = d / 2;
+    for (int i = 0; i < half; ++i) {
+        const float c = cs[2 * i], s = cs[2 * i + 1];
+        const float x0 = y[i], x1 = y[i + half];
+        const float a = x0 * c;
+        const float b = x1 * s;
+        const float e = x0 * s;
+        const float f = x1 * c;
+        y[i] = a - b;
+        y[i + half] = e + f;
+    }
+}
+
+// ---------------------------------------------------------------- Q8_0 -------
+inline void q8_row_dequant(const uint8_t* row, int K, float* out, int mode_f16) {
+    for (int b = 0; b < K / QK; ++b) {
+        const uint8_t* blk = row + (size_t)b * QB;
+        uint16_t dh; std::memcpy(&dh, blk, 2);
+        const float d = h2f(dh);
+        const int8_t* q = (const int8_t*)(blk + 2);
+        for (int j = 0; j < QK; ++j) {
+            float w = d * (float)q[j];          // exact in f32
+            out[b * QK + j] = mode_f16 ? round_f16(w) : w;
+        }
+    }
+}
+
+// ggml quantize_row_q8_0 (reference scalar form): d = amax/127, q = roundf(x/d).
+inline void q8_quantize_act(const float* x, int K, int8_t* q, uint16_t* d_out) {
+    for (int b = 0; b < K / QK; ++b) {
+        float amax = 0.0f;
+        for (int j = 0; j < QK; ++j) amax = std::max(amax, std::fabs(x[b * QK + j]));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        d_out[b] = f2h(d);
+        for (int j = 0; j < QK; ++j) q[b * QK + j] = (int8_t)std::roundf(x[b * QK + j] * id);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+// ---- element conversions exposed for tests ----------------------------------
+void or_f32_to_f16(const float* x, int64_t n, uint16_t* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = f2h(x[i]);
+}
+void or_f16_to_f32(const uint16_t* x, int64_t n, float* out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = h2f(x[i]);
+}
+
+// ---- RoPE table --------------------------------------------------------------
+// cs[pos][i][0] = cos(pos * base^(-2i/d)), cs[pos][i][1] = sin(...), i < d/2,
+// computed in double and rounded to f32 once.
+void or_rope_table(int max_pos, int head_dim, double base, float* cs) {
+    const int half = head_dim / 2;
+    std::vector<double> inv(half);
+    for (int i = 0; i < half; ++i) inv[i] = std::pow(base, -2.0 * (double)i / (double)head_dim);
+#pragma omp parallel for schedule(static)
+    for (int p = 0; p < max_pos; ++p) {
+        for (int i = 0; i < half; ++i) {
+            const double th = (double)p * inv[i];
+            cs[((size_t)p * half + i) * 2 + 0] = (float)std::cos(th);
+            cs[((size_t)p * half + i) * 2 + 1] = (float)std::sin(th);
+        }
+    }
+}
+
+// ---- Q8_0 codec ----------------------------------------------------------------
+// tools/hf_convert_ggml_q8.py:354-381: blocks of 32, d = amax/127 (f32; 0 -> 1e-8),
+// q = clip(round_half_even(x/d), -127, 127), stored [f16 d][32 int8].
+void or_q8_0_quantize(const float* x, int64_t n, uint8_t* out) {
+    const int64_t nb = n / QK;
+    for (int64_t b = 0; b < nb; ++b) {
+        const float* xb = x + b * QK;
+        float amax = 0.0f;
+        for (int j = 0; j < QK; ++j) amax = std::max(amax, std::fabs(xb[j]));
+        float d = amax / 127.0f;
+        if (d == 0.0f) d = 1e-8f;
+        uint16_t dh = f2h(d);
+        uint8_t* o = out + b * QB;
+        std::memcpy(o, &dh, 2);
+        for (int j = 0; j < QK; ++j) {
+            float r = std::nearbyint(xb[j] / d);    // numpy round: half to even
+            r = std::min(127.0f, std::max(-127.0f, r));
+            o[2 + j] = (uint8_t)(int8_t)r;
+        }
+    }
+}
+
+void or_q8_0_dequant(const uint8_t* blocks, int64_t n, float* out) {
+    const int64_t nb = n / QK;
+    for (int64_t b = 0; b < nb; ++b) q8_row_dequant(blocks + b * QB, QK, out + b * QK, 0);
+}
+
+// ---- rms_norm rows -------------------------------------------------------------
+void or_rmsnorm(const float* x, const float* w, int rows, int n, float eps, float* out) {
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) rms_norm_vec(x + (size_t)r * n, w, n, eps, out + (size_t)r * n);
+}
+
+// ---- Q8_0 matmul: C[M][N] = A[M][K] . W[N][K]^T --------------------------------
+// mode 0: exact f32 activations x dequantised weights, double accumulation.
+// mode 1: f16(activation) x f16(f32(d) * q), double accumulation (CUDA path arithmetic).
+// mode 2: ggml CPU backend: Q8_0 activations, integer block dots, f32 block sum.
+void or_gemm_q8(const float* A, int M, int K, const uint8_t* W, int N, int mode, float* C) {
+    const int nb = K / QK;
+    if (mode == 2) {
+        std::vector<int8_t> aq((size_t)M * K);
+        std::vector<uint16_t> ad((size_t)M * nb);
+        for (int m = 0; m < M; ++m) q8_quantize_act(A + (size_t)m * K, K, aq.data() + (size_t)m * K, ad.data() + (size_t)m * nb);
+#pragma omp parallel for schedule(dynamic, 16)
+        for (int n = 0; n < N; ++n) {
+            const uint8_t* row = W + (size_t)n * nb * QB;
+            for (int m = 0; m < M; ++m) {
+                const int8_t* xq = aq.data() + (size_t)m * K;
+                const uint16_t* xd = ad.data() + (size_t)m * nb;
+                float sumf = 0.0f;
+                for (int b = 0; b < nb; ++b) {
+                    const uint8_t* blk = row + (size_t)b * QB;
+                    uint16_t dh; std::memcpy(&dh, blk, 2);
+                    const int8_t* wq = (const int8_t*)(blk + 2);
+                    int sumi = 0;
+                    for (int j = 0; j < QK; ++j) sumi += (int)wq[j] * (int)xq[b * QK + j];
+                    sumf += (float)sumi * (h2f(dh) * h2f(xd[b]));
+                }
+                C[(size_t)m * N + n] = sumf;
+            }
+        }
+        return;
+    }
+    std::vector<float> Ar;
+    const float* Ause = A;
+    if (mode == 1) {
+        Ar.resize((size_t)M * K);
+        for (size_t i = 0; i < (size_t)M * K; ++i) Ar[i] = round_f16(A[i]);
+        Ause = Ar.data();
+    }
+#pragma omp parallel
+    {
+        std::vector<float> w(K);
+#pragma omp for schedule(dynamic, 16)
+        for (int n = 0; n < N; ++n) {
+            q8_row_dequant(W + (size_t)n * nb * QB, K, w.data(), mode == 1);
+            for (int m = 0; m < M; ++m) {
+                const float* a = Ause + (size_t)m * K;
+                double s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                int k = 0;
+                for (; k + 8 <= K; k += 8)
+                    for (int u = 0; u < 8; ++u) s[u] += (double)a[k + u] * (double)w[k + u];
+                for (; k < K; ++k) s[0] += (double)a[k] * (double)w[k];
+                C[(size_t)m * N + n] = (float)(((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7])));
+            }
+        }
+    }
+}
+
+// ---- fused per-head Q/K RMSNorm + NEOX RoPE + paged f16 KV append ---------------
+// qkv    : [M][(Hq + 2*Hkv) * D] f32, q heads then k heads then v heads
+// q_out  : [M][Hq * D] f32 = rope(rmsnorm(q) * qn_w) * q_scale
+// pool   : one layer's page pool, [n_pages][Hkv][2][PT][D] f16
+// K/V of row m land at page block_table[slot[m]*bt_stride + pos[m]/PT], token pos[m]%PT.
+void or_qknorm_rope_append(const float* qkv, int M, const int* slot, const int* pos,
+                           const int* block_table, int bt_stride,
+                           const float* qn_w, const float* kn_w,
+                           int Hq, int Hkv, int D, int PT, float eps, float q_scale,
+                           const float* rope_cs, uint16_t* pool, float* q_out) {
+    const int W = (Hq + 2 * Hkv) * D;
+    const size_t page_elems = (size_t)Hkv * 2 * PT * D;
+    std::vector<float> y(D);
+    for (int m = 0; m < M; ++m) {
+        const float* row = qkv + (size_t)m * W;
+        const int p = pos[m];
+        const float* cs = rope_cs + (size_t)p * (D / 2) * 2;
+        const int page = block_table[(size_t)slot[m] * bt_stride + p / PT];
+        const int t = p % PT;
+        uint16_t* pg = pool + (size_t)page * page_elems;
+        for (int h = 0; h < Hq; ++h) {
+            rms_norm_vec(row + h * D, qn_w, D, eps, y.data());
+            rope_neox(y.data(), D, cs);
+            for (int d = 0; d < D; ++d) q_out[(size_t)m * Hq * D + h * D + d] = y[d] * q_scale;
+        }
+        for (int h = 0; h < Hkv; ++h) {
+            rms_norm_vec(row + (Hq + h) * D, kn_w, D, eps, y.data());
+            rope_neox(y.data(), D, cs);
+            uint16_t* kdst = pg + ((size_t)h * 2 + 0) * PT * D + (size_t)t * D;
+            for (int d = 0; d < D; ++d) kdst[d] = f2h(y[d]);
+            const float* v = row + (Hq + Hkv + h) * D;
+            uint16_t* vdst = pg + ((size_t)h * 2 + 1) * PT * D + (size_t)t * D;
+            for (int d = 0; d < D; ++d) vdst[d] = f2h(v[d]);
+        }
+    }
+}
+
+// ---- raw paged append of given f16 K/V (append microbenchmark) -------------------
+// k, v: [M][n_layers][Hkv][D] f16; pool: [n_layers][n_pages][Hkv][2][PT][D].
+void or_kv_append_raw(const uint16_t* k, const uint16_t* v, int M, int n_layers,
+                      const int* slot, const int* pos, const int* block_table, int bt_stride,
+                      int n_pages, int Hkv, int D, int PT, uint16_t* pool) {
+    const size_t page_elems = (size_t)Hkv * 2 * PT * D;
+    for (int m = 0; m < M; ++m) {
+        const int p = pos[m];
+        const int page = block_table[(size_t)slot[m] * bt_stride + p / PT];
+        const int t = p % PT;
+        for (int l = 0; l < n_layers; ++l) {
+            uint16_t* pg = pool + ((size_t)l * n_pages + page) * page_elems;
+            for (int h = 0; h < Hkv; ++h) {
+                const size_t src = (((size_t)m * n_layers + l) * Hkv + h) * D;
+                std::memcpy(pg + ((size_t)h * 2 + 0) * PT * D + (size_t)t * D, k + src, D * 2);
+                std::memcpy(pg + ((size_t)h * 2 + 1) * PT * D + (size_t)t * D, v + src, D * 2);
+            }
+        }
+    }
+}
+
+// ---- paged GQA attention ----------------------------------------------------------
+// q: [M][Hq][D] f32 (already scaled by 1/sqrt(D)); row m attends to tokens [0, n_kv[m])
+// of its sequence. Query head H reads kv head H / (Hq/Hkv). out: [M][Hq*D] f32.
+void or_paged_attention(const float* q, int M, const int* slot, const int* n_kv,
+                        const int* block_table, int bt_stride, const uint16_t* pool,
+                        int Hq, int Hkv, int D, int PT, float* out) {
+    const size_t page_elems = (size_t)Hkv * 2 * PT * D;
+    const int G = Hq / Hkv;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+    for (int m = 0; m < M; ++m) {
+        for (int H = 0; H < Hq; ++H) {
+            const int h = H / G;
+            const int n = n_kv[m];
+            const float* qv = q + ((size_t)m * Hq + H) * D;
+            std::vector<double> s(n > 0 ? n : 1);
+            double mx = -INFINITY;
+            for (int t = 0; t < n; ++t) {
+                const int page = block_table[(size_t)slot[m] * bt_stride + t / PT];
+                const uint16_t* kr = pool + (size_t)page * page_elems + ((size_t)h * 2 + 0) * PT * D + (size_t)(t % PT) * D;
+                double acc = 0.0;
+                for (int d = 0; d < D; ++d) acc += (double)qv[d] * (double)h2f(kr[d]);
+                s[t] = acc;
+                mx = std::max(mx, acc);
+            }
+            double l = 0.0;
+            for (int t = 0; t < n; ++t) { s[t] = std::exp(s[t] - mx); l += s[t]; }
+            std::vector<double> o(D, 0.0);
+            for (int t = 0; t < n; ++t) {
+                const int page = block_table[(size_t)slot[m] * bt_stride + t / PT];
+                const uint16_t* vr = pool + (size_t)page * page_elems + ((size_t)h * 2 + 1) * PT * D + (size_t)(t % PT) * D;
+                for (int d = 0; d < D; ++d) o[d] += s[t] * (double)h2f(vr[d]);
+            }
+            float* dst = out + (size_t)m * Hq * D + (size_t)H * D;
+            for (int d = 0; d < D; ++d) dst[d] = n > 0 ? (float)(o[d] / l) : 0.0f;
+        }
+    }
+}
+
+// ---- argmax: first index of the maximum (compute/gpu_runner.hpp:108-118) ---------------
+void or_argmax_rows(const float* logits, int M, int N, int* out) {
+    for (int m = 0; m < M; ++m) {
+        const float* r = logits + (size_t)m * N;
+        float best = -1e30f;
+        int idx = 0;
+        for (int i = 0; i < N; ++i)
+            if (r[i] > best) { best = r[i]; idx = i; }
+        out[m] = idx;
+    }
+}
+
+// ---- whole decoder forward over a batch of rows --------------------------------------
+struct or_model {
+    int n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
+    int page_tokens, n_pages, max_pos;
+    float eps;
+    const uint16_t* embed_bf16;     // [vocab][hidden]
+    const float* final_norm;        // [hidden]
+    const uint8_t* lm_head;         // Q8_0 rows [vocab]
+    const uint8_t* const* wq;       // per layer Q8_0 [Hq*D][hidden]
+    const uint8_t* const* wk;       // [Hkv*D][hidden]
+    const uint8_t* const* wv;       // [Hkv*D][hidden]
+    const uint8_t* const* wo;       // [hidden][Hq*D]
+    const uint8_t* const* wg;       // [ffn][hidden]
+    const uint8_t* const* wu;       // [ffn][hidden]
+    const uint8_t* const* wd;       // [hidden][ffn]
+    const float* const* in_norm;    // [hidden]
+    const float* const* post_norm;  // [hidden]
+    const float* const* q_norm;     // [D]
+    const float* const* k_norm;     // [D]
+    const float* rope_cs;           // [max_pos][D/2][2]
+};
+
+// One forward over M rows (row m = token at position pos[m] of sequence slot[m]).
+// Either tokens (embedding lookup) or embeds [M][hidden] f32 gives the input.
+// All rows' K/V are appended before any row's attention, per layer.
+// pool: [n_layers][n_pages][page] f16, block_table[slot][page index].
+// logits [M][vocab] optional; next [M] optional (argmax).
+void or_decoder_forward(const or_model* mdl, int mode, int M, const int* tokens, const float* embeds,
+                        const int* slot, const int* pos, const int* block_table, int bt_stride,
+                        uint16_t* pool, float* logits, int* next, float* hidden_out) {
+    const int Hd = mdl->hidden, Hq = mdl->n_heads, Hkv = mdl->n_kv_heads, D = mdl->head_dim;
+    const int F = mdl->ffn, V = mdl->vocab, PT = mdl->page_tokens;
+    const size_t page_elems = (size_t)Hkv * 2 * PT * D;
+    const float q_scale = 1.0f / std::sqrt((float)D);
+    std::vector<float> x((size_t)M * Hd), xn((size_t)M * Hd);
+    std::vector<float> q((size_t)M * Hq * D), k((size_t)M * Hkv * D), v((size_t)M * Hkv * D);
+    std::vector<float> qkv((size_t)M * (Hq + 2 * Hkv) * D), qr((size_t)M * Hq * D), att((size_t)M * Hq * D);
+    std::vector<float> o((size_t)M * Hd), g((size_t)M * F), u((size_t)M * F), hh((size_t)M * F);
+    std::vector<int> nkv(M);
+    for (int m = 0; m < M; ++m) nkv[m] = pos[m] + 1;
+    for (int m = 0; m < M; ++m) {
+        if (embeds) {
+            std::memcpy(&x[(size_t)m * Hd], embeds + (size_t)m * Hd, sizeof(float) * Hd);
+        } else {
+            const uint16_t* e = mdl->embed_bf16 + (size_t)tokens[m] * Hd;
+            for (int i = 0; i < Hd; ++i) x[(size_t)m * Hd + i] = bf2f(e[i]);
+        }
+    }
+    for (int l = 0; l < mdl->n_layers; ++l) {
+        uint16_t* lp = pool + (size_t)l * mdl->n_pages * page_elems;
+        or_rmsnorm(x.data(), mdl->in_norm[l], M, Hd, mdl->eps, xn.data());
+        or_gemm_q8(xn.data(), M, Hd, mdl->wq[l], Hq * D, mode, q.data());
+        or_gemm_q8(xn.data(), M, Hd, mdl->wk[l], Hkv * D, mode, k.data());
+        or_gemm_q8(xn.data(), M, Hd, mdl->wv[l], Hkv * D, mode, v.data());
+        const int W = (Hq + 2 * Hkv) * D;
+        for (int m = 0; m < M; ++m) {
+            std::memcpy(&qkv[(size_t)m * W], &q[(size_t)m * Hq * D], sizeof(float) * Hq * D);
+            std::memcpy(&qkv[(size_t)m * W + Hq * D], &k[(size_t)m * Hkv * D], sizeof(float) * Hkv * D);
+            std::memcpy(&qkv[(size_t)m * W + (Hq + Hkv) * D], &v[(size_t)m * Hkv * D], sizeof(float) * Hkv * D);
+        }
+        or_qknorm_rope_append(qkv.data(), M, slot, pos, block_table, bt_stride, mdl->q_norm[l], mdl->k_norm[l],
+                              Hq, Hkv, D, PT, mdl->eps, q_scale, mdl->rope_cs, lp, qr.data());
+        or_paged_attention(qr.data(), M, slot, nkv.data(), block_table, bt_stride, lp, Hq, Hkv, D, PT, att.data());
+        or_gemm_q8(att.data(), M, Hq * D, mdl->wo[l], Hd, mode, o.data());
+        for (size_t i = 0; i < x.size(); ++i) x[i] = x[i] + o[i];
+        or_rmsnorm(x.data(), mdl->post_norm[l], M, Hd, mdl->eps, xn.data());
+        or_gemm_q8(xn.data(), M, Hd, mdl->wg[l], F, mode, g.data());
+        or_gemm_q8(xn.data(), M, Hd, mdl->wu[l], F, mode, u.data());
+        for (size_t i = 0; i < hh.size(); ++i) {
+            const double gd = g[i];
+            const float s = (float)(gd / (1.0 + std::exp(-gd)));
+            hh[i] = s * u[i];
+        }
+        or_gemm_q8(hh.data(), M, F, mdl->wd[l], Hd, mode, o.data());
+        for (size_t i = 0; i < x.size(); ++i) x[i] = x[i] + o[i];
+    }
+    if (hidden_out) std::memcpy(hidden_out, x.data(), sizeof(float) * x.size());
+    or_rmsnorm(x.data(), mdl->final_norm, M, Hd, mdl->eps, xn.data());
+    std::vector<float> lg;
+    float* L = logits;
+    if (!L) { lg.resize((size_t)M * V); L = lg.data(); }
+    or_gemm_q8(xn.data(), M, Hd, mdl->lm_head, V, mode, L);
+    if (next) or_argmax_rows(L, M, V, next);
+}
+
+int or_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+void or_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+}  // extern "C"
