@@ -1,0 +1,301 @@
+#!/usr/bin/env python
+"""Decode throughput of the paged-KV Qwen3-0.6B decoder on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
+
+Workload (one step): one greedy decode step of the full 28-layer Qwen3-0.6B decoder
+(Q8_0 weights, paged f16 KV cache) for 128 sequences that sit at a 2048-token context
+(growing by one token per step): embedding gather, per layer RMSNorm, QKV GEMM,
+QK-norm + RoPE + paged append, paged GQA attention, o_proj, SwiGLU MLP, then the
+final norm, lm_head with fused argmax and the feedback of the argmax as next input.
+Every GPU runs its own 128 streams (independent replicas, weak scaling, no collectives).
+
+Prints one JSON line. `value` = whole-job decode tokens/s timed on the device (CUDA
+events around exactly K steps, inputs resident in HBM, max over ranks); `e2e` = the same
+through fa_decode_step with host token ids in and next ids out every step.
+The KV cache read per step is ~30 GB, far larger than L2, so no L2 flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "funasr-ggml_b200"))
+
+import fa_multi  # noqa: E402
+import fa_synth  # noqa: E402
+
+METRIC = "decode tokens/s per GPU (bs128, 2k ctx) at 1/2/4/8 B200; paged-attn HBM GB/s"
+KV_BYTES_PER_TOKEN_LAYER = 8 * 2 * 128 * 2     # K+V of 8 heads x 128 dims, f16
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--e2e-steps", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.device)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU baseline --
+def cpu_oracle_sample(cfg, w, ctx, budget_s, rows=2, seed=0):
+    """Oracle decode steps (ggml-CPU arithmetic: Q8_0 activations) for `rows` sequences
+    at `ctx` tokens of synthetic cache, repeated for about budget_s seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    pages = (ctx + 16 + 15) // 16
+    od = oracle.OracleDecoder(cfg, w, n_pages=rows * pages, max_seqs=rows, max_pages_per_seq=pages,
+                              max_pos=ctx + 16, mode=oracle.MODE_GGML_CPU)
+    rng = np.random.default_rng(seed)
+    for s in range(rows):
+        od.seq_open(s)
+        od._reserve(s, ctx)
+        od.seq_len[s] = ctx
+    L = od.pool.shape[0]
+    for l in range(L):
+        od.pool[l] = oracle.f32_to_f16_bits(rng.uniform(-2, 2, od.pool.shape[1:]).astype(np.float32))
+    toks = rng.integers(0, cfg["vocab"], rows)
+    n_tok, t0 = 0, time.perf_counter()
+    while True:
+        _, nxt = od.forward(list(range(rows)), tokens=toks, want_logits=False)
+        toks = nxt
+        n_tok += rows
+        el = time.perf_counter() - t0
+        if el >= budget_s or od.seq_len[0] >= ctx + 15:
+            break
+    return n_tok / el, oracle.num_threads(), n_tok, el
+
+
+# ------------------------------------------------------------------- ours --
+def run_ours(a):
+    rank, local, world = fa_multi.init("nccl")
+    import torch
+    torch.cuda.set_device(local)
+    import fa_dec
+
+    cfg = fa_synth.QWEN3_06B
+    B, ctx, K, W, E = a.batch, a.ctx, a.steps, a.warmup, a.e2e_steps
+    w = fa_synth.make_weights(cfg, seed=1)
+    total_new = W + K + 2 + E + 1
+    max_ctx = (ctx + total_new + 31) // 16 * 16
+    pages_per_seq = max_ctx // 16
+    dec = fa_dec.Decoder(local, **fa_synth.decoder_desc(cfg, max_ctx=max_ctx, n_pages=B * pages_per_seq + 16,
+                                                        max_seqs=B, max_rows=B))
+    dec.load_weights(w)
+    sids = [dec.seq_open(max_ctx) for _ in range(B)]
+    for i, s in enumerate(sids):
+        dec.kv_fill_synthetic(s, ctx, seed=rank * 100003 + i)
+    rng = np.random.default_rng(rank)
+    toks = rng.integers(0, cfg["vocab"], B)
+
+    dec.profile(True)
+    ids, _ = dec.generate(sids, toks, W)
+    toks = ids[-1]
+    sampler = ClockSampler(local)
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    sampler.start()
+    ids, dev_ms = dec.generate(sids, toks, K)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    fa_multi.barrier()
+    attn_ms, n_att = dec.profile_attention()
+    launches = dec.step_launches()
+    dec.profile(False)
+    max_ms = fa_multi.reduce(dev_ms, "max")
+    value = B * K * world / (max_ms / 1e3)
+
+    # attention roofline of the last timed step: every row at ctx + W + K tokens
+    n_kv_last = ctx + W + K
+    att_bytes = B * n_kv_last * KV_BYTES_PER_TOKEN_LAYER
+    att_launch_ms = attn_ms / max(n_att, 1)
+    achieved = att_bytes / (att_launch_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "attention_traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            t = json.load(f)
+        # bytes scale with the (row, token) pairs read per launch
+        traffic = t["dram_bytes_per_launch"] * (B * n_kv_last) / (t["rows"] * t["n_kv"])
+
+    # e2e through the public step call, host ids in and out every step
+    toks = ids[-1]
+    for _ in range(2):
+        toks, _ = dec.decode_step(sids, toks)
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    t0 = time.perf_counter()
+    for _ in range(E):
+        toks, _ = dec.decode_step(sids, toks)
+    e2e_s = time.perf_counter() - t0
+    fa_multi.barrier()
+    e2e_s = fa_multi.reduce(e2e_s, "max")
+    e2e_value = B * E * world / e2e_s
+    all_clocks = fa_multi.gather(clocks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        v, cores, n_tok, el = cpu_oracle_sample(cfg, w, ctx, a.cpu_budget_s)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n_tok} decode tokens (2 sequences at {ctx}-token synthetic context, full 28-layer "
+                         f"model, ggml-CPU arithmetic) in {el:.1f} s; CPU restatement of the reference "
+                         f"(ggml unavailable)"}
+    dec.close()
+    if rank == 0:
+        c0 = all_clocks[0]
+        reasons = sorted(set(r for c in all_clocks for r in c.get("reasons", [])))
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": max_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic: seeded random-init Q8_0 Qwen3-0.6B weights, synthetic f16 KV cache, random first tokens",
+            "config": {"workload": f"steady-state paged GQA decode, {B} sequences per GPU at {ctx}-token context "
+                                   f"(grows to {ctx + W + K}), Qwen3-0.6B 28 layers 16q/8kv x 128, Q8_0 weights, f16 KV",
+                       "batch_per_gpu": B, "ctx": ctx, "page_tokens": 16,
+                       "l2": "no flush: inputs larger than L2 (KV read per step ~30 GB)",
+                       "parallelism": f"independent replicas x{world}, no collectives"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "paged_attn_kernel (+attn_combine)", "peak_kind": peak_kind,
+                         "bytes_per_launch": att_bytes, "ms_per_launch": att_launch_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * 12,
+                    "d2h_bytes_per_step": B * 4 + 4, "steps": E},
+            "gpu_launches": launches * K,
+            "clocks": {"sm_mhz": c0.get("sm_mhz"), "sm_max_mhz": c0.get("sm_max_mhz"), "reasons": reasons},
+        }
+        print(json.dumps(line), flush=True)
+    fa_multi.shutdown()
+
+
+# -------------------------------------------------------------- reference --
+def run_reference(a):
+    """The reference's CPU path (ggml) cannot be built here, so its restatement (the
+    oracle, ggml-CPU arithmetic, all host threads) is timed on the same config: each
+    step is one decode step of a 2-sequence sample at the 2048-token context."""
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return
+    cfg = fa_synth.QWEN3_06B
+    w = fa_synth.make_weights(cfg, seed=1)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    rows = 2
+    ctx = a.ctx
+    n_steps = a.warmup + a.steps
+    pages = (ctx + n_steps + 32) // 16
+    od = oracle.OracleDecoder(cfg, w, n_pages=rows * pages, max_seqs=rows, max_pages_per_seq=pages,
+                              max_pos=ctx + n_steps + 32, mode=oracle.MODE_GGML_CPU)
+    rng = np.random.default_rng(0)
+    for s in range(rows):
+        od.seq_open(s)
+        od._reserve(s, ctx)
+        od.seq_len[s] = ctx
+    for l in range(od.pool.shape[0]):
+        od.pool[l] = oracle.f32_to_f16_bits(rng.uniform(-2, 2, od.pool.shape[1:]).astype(np.float32))
+    toks = rng.integers(0, cfg["vocab"], rows)
+    for _ in range(a.warmup):
+        _, toks = od.forward([0, 1], tokens=toks, want_logits=False)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        _, toks = od.forward([0, 1], tokens=toks, want_logits=False)
+    el = time.perf_counter() - t0
+    v = rows * a.steps / el
+    cores = oracle.num_threads()
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": el * 1e3 / a.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (Q8_0 activations x Q8_0 weights)",
+        "data": "synthetic: seeded random-init Q8_0 Qwen3-0.6B weights, synthetic f16 KV cache",
+        "config": {"workload": f"steady-state decode at {ctx}-token context, Qwen3-0.6B 28 layers, "
+                               f"2-sequence sample per step on the host cores", "ctx": ctx, "rows": rows},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{a.steps} steps x {rows} sequences; CPU restatement of the reference "
+                                   f"(ggml unavailable: third_party/ggml is not vendored)"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)

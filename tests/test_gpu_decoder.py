@@ -1,0 +1,243 @@
+"""GPU parity of the whole decoder behind the reference-facing C ABI (fa_ctx).
+
+The oracle runs the same rows with the same arithmetic (GEMM mode 1); logits must be
+within 2e-2 max-abs / 1e-3 relative RMS, greedy ids must agree on >= 99% of steps and
+block tables must be identical. Mirrors the reference's test_llm.cpp flow: prefill
+the prompt, then greedy decode (compute/gpu_runner.hpp, pipeline/pipeline.cpp:434-451).
+"""
+import numpy as np
+import pytest
+
+import fa_dec
+import fa_synth
+import oracle
+from helpers import assert_close, rel_rms
+
+pytestmark = pytest.mark.gpu
+
+CFG = fa_synth.small_config(n_layers=2, hidden=256, ffn=512, vocab=2048)
+MAX_CTX = 4096
+
+
+def _embed_table(w, cfg):
+    return oracle.bf16_bits_to_f32(w["llm.model.embed_tokens.weight"][2]).reshape(cfg["vocab"], cfg["hidden"])
+
+
+def _decoder(w, cfg, **over):
+    desc = dict(max_ctx=MAX_CTX, n_pages=256, max_seqs=16, max_rows=128)
+    desc.update(over)
+    dec = fa_dec.Decoder(0, **fa_synth.decoder_desc(cfg, **desc))
+    dec.load_weights(w)
+    return dec
+
+
+@pytest.fixture(scope="module")
+def small_w():
+    return fa_synth.make_weights(CFG, seed=11)
+
+
+def test_prefill_and_decode_match_oracle(torch_cuda, small_w):
+    w = small_w
+    dec = _decoder(w, CFG)
+    od = oracle.OracleDecoder(CFG, w, n_pages=256, max_seqs=16, max_pages_per_seq=MAX_CTX // 16, max_pos=MAX_CTX,
+                              mode=oracle.MODE_F16)
+    rng = np.random.default_rng(0)
+    emb = _embed_table(w, CFG)
+    sids = [dec.seq_open(MAX_CTX) for _ in range(3)]
+    assert sids == [0, 1, 2]
+    for s in sids:
+        od.seq_open(s)
+    lens = [17, 33, 5]
+    row_seq = sum(([s] * n for s, n in zip(sids, lens)), [])
+    rows = np.concatenate([
+        np.concatenate([emb[rng.integers(0, CFG["vocab"], 3)], rng.standard_normal((n - 3, CFG["hidden"]))])
+        for n in lens]).astype(np.float32)
+    g_next, g_lg = dec.forward(row_seq, embeds=rows, want_logits=True)
+    o_lg, o_next = od.forward(row_seq, embeds=rows)
+    assert_close(g_lg, o_lg, what="prefill logits")
+    agree = [np.mean(g_next == o_next)]
+    for s in sids:
+        bt = dec.block_table(s)
+        assert np.array_equal(bt, od.block_table[s, :len(bt)]), "block tables differ"
+    last = np.cumsum(lens) - 1
+    toks = g_next[last]
+    for step in range(12):
+        g_next, g_lg = dec.decode_step(sids, toks, want_logits=True)
+        o_lg, o_next = od.forward(sids, tokens=toks)
+        assert_close(g_lg, o_lg, what=f"decode step {step} logits")
+        agree.append(np.mean(g_next == o_next))
+        toks = g_next
+    assert np.mean(agree) >= 0.99, agree
+    for s in sids:
+        bt = dec.block_table(s)
+        assert np.array_equal(bt, od.block_table[s, :len(bt)])
+        assert dec.seq_length(s) == od.seq_len[s]
+    # K/V pages: same bytes up to f16 rounding of values whose f32 inputs differ in the last bit
+    used = np.concatenate([dec.block_table(s) for s in sids])
+    for layer in (0, CFG["n_layers"] - 1):
+        got = dec.kv_read_pages(layer, used)
+        ref = od.pool[layer, used]
+        same = np.mean(got == ref)
+        assert same > 0.95, same
+        assert rel_rms(oracle.f16_bits_to_f32(got), oracle.f16_bits_to_f32(ref)) < 1e-3
+    dec.close()
+
+
+def test_generate_equals_stepwise_and_graphs_are_bitwise_stable(torch_cuda, small_w):
+    w = small_w
+    rng = np.random.default_rng(1)
+    prompt = rng.integers(0, CFG["vocab"], (4, 10))
+
+    def run(use_graphs, generate):
+        dec = _decoder(w, CFG)
+        dec.set_graphs(use_graphs)
+        sids = [dec.seq_open(MAX_CTX) for _ in range(4)]
+        nxt, lg = dec.forward(np.repeat(sids, 10), tokens=prompt.reshape(-1), want_logits=True)
+        first = nxt[9::10]
+        if generate:
+            ids, ms = dec.generate(sids, first, 8)
+            assert ms > 0
+        else:
+            ids, t = [], first
+            for _ in range(8):
+                t, _ = dec.decode_step(sids, t)
+                ids.append(t)
+            ids = np.stack(ids)
+        lens = [dec.seq_length(s) for s in sids]
+        dec.close()
+        return lg, ids, lens
+
+    lg_a, ids_a, lens_a = run(True, True)
+    lg_b, ids_b, lens_b = run(False, False)
+    lg_c, ids_c, _ = run(True, False)
+    assert np.array_equal(lg_a.view(np.uint32), lg_b.view(np.uint32))
+    assert np.array_equal(ids_a, ids_b) and np.array_equal(ids_a, ids_c)
+    assert lens_a == lens_b == [18] * 4
+
+
+def test_pool_exhaustion_rolls_back(torch_cuda, small_w):
+    dec = _decoder(small_w, CFG, n_pages=4)
+    a = dec.seq_open(MAX_CTX)
+    b = dec.seq_open(MAX_CTX)
+    toks = np.arange(48) % CFG["vocab"]
+    dec.forward([a] * 48, tokens=toks)
+    assert dec.pool_info()[1] == 1
+    with pytest.raises(fa_dec.FaError) as e:
+        dec.forward([b] * 32, tokens=toks[:32])
+    assert e.value.code == fa_dec.FA_ERR_POOL_EXHAUSTED
+    assert dec.seq_length(b) == 0 and dec.pool_info()[1] == 1 and len(dec.block_table(b)) == 0
+    dec.forward([b] * 16, tokens=toks[:16])
+    assert dec.seq_length(b) == 16 and dec.pool_info()[1] == 0
+    dec.seq_close(a)
+    assert dec.pool_info()[1] == 3
+    dec.close()
+
+
+def test_compaction_moves_pages_and_keeps_results(torch_cuda, small_w):
+    w = small_w
+    toks = np.random.default_rng(2).integers(0, CFG["vocab"], 40)
+
+    def setup():
+        dec = _decoder(w, CFG, n_pages=32)
+        s = [dec.seq_open(MAX_CTX) for _ in range(3)]
+        dec.forward(np.repeat(s, 40), tokens=np.tile(toks, 3))
+        return dec, s
+
+    dec, s = setup()
+    assert [list(dec.block_table(x)) for x in s] == [[0, 1, 2], [3, 4, 5], [6, 7, 8]]
+    dec.seq_close(s[1])
+    before = {x: [dec.kv_read_pages(l, dec.block_table(x)) for l in range(CFG["n_layers"])] for x in (s[0], s[2])}
+    live = list(dec.block_table(s[0])) + list(dec.block_table(s[2]))
+    src, dst = oracle.compaction_plan(live, 32)
+    assert dec.pool_compact() == len(src) == 3
+    remap = dict(zip(src, dst))
+    assert list(dec.block_table(s[2])) == [remap.get(p, p) for p in [6, 7, 8]]
+    for x in (s[0], s[2]):
+        for l in range(CFG["n_layers"]):
+            assert np.array_equal(dec.kv_read_pages(l, dec.block_table(x)), before[x][l])
+    n1, lg1 = dec.decode_step([s[0], s[2]], [5, 6], want_logits=True)
+    ref, rs = setup()
+    ref.seq_close(rs[1])
+    n2, lg2 = ref.decode_step([rs[0], rs[2]], [5, 6], want_logits=True)
+    assert np.array_equal(lg1.view(np.uint32), lg2.view(np.uint32))
+    # the pool's live pages are now [0, n_live) and new pages continue from there
+    assert sorted(np.concatenate([dec.block_table(s[0]), dec.block_table(s[2])])) == list(range(6))
+    dec.close()
+    ref.close()
+
+
+def test_truncate_then_continue(torch_cuda, small_w):
+    dec = _decoder(small_w, CFG)
+    toks = np.random.default_rng(3).integers(0, CFG["vocab"], 41)
+    a = dec.seq_open(MAX_CTX)
+    dec.forward([a] * 40, tokens=toks[:40])
+    _, l1 = dec.decode_step([a], [toks[40]], want_logits=True)
+    dec.seq_truncate(a, 20)
+    assert dec.seq_length(a) == 20 and len(dec.block_table(a)) == 2
+    dec.forward([a] * 20, tokens=toks[20:40])
+    _, l2 = dec.decode_step([a], [toks[40]], want_logits=True)
+    assert_close(l2, l1, max_abs_tol=1e-3, rel_rms_tol=1e-5, what="after truncate")
+    dec.close()
+
+
+def test_error_paths(torch_cuda, small_w):
+    dec = _decoder(small_w, CFG, max_rows=8)
+    a = dec.seq_open(20)
+    with pytest.raises(fa_dec.FaError) as e:
+        dec.decode_step([7], [1])
+    assert e.value.code == fa_dec.FA_ERR_SEQ
+    with pytest.raises(fa_dec.FaError):
+        dec.decode_step([a], [CFG["vocab"]])
+    with pytest.raises(fa_dec.FaError) as e:
+        dec.forward([a] * 9, tokens=np.zeros(9))
+    assert e.value.code == fa_dec.FA_ERR_CAPACITY
+    dec.forward([a] * 8, tokens=np.zeros(8))
+    dec.forward([a] * 8, tokens=np.zeros(8))
+    with pytest.raises(fa_dec.FaError) as e:
+        dec.forward([a] * 8, tokens=np.zeros(8))      # max_tokens 20
+    assert e.value.code == fa_dec.FA_ERR_CAPACITY
+    assert dec.seq_length(a) == 16
+    with pytest.raises(fa_dec.FaError):
+        dec.decode_step([a, a], [1, 2])
+    dec.seq_close(a)
+    with pytest.raises(fa_dec.FaError):
+        dec.seq_length(a)
+    with pytest.raises(fa_dec.FaError) as e:
+        bad = dict(small_w)
+        bad.pop("llm.model.layers.1.mlp.up_proj.weight")
+        d2 = fa_dec.Decoder(0, **fa_synth.decoder_desc(CFG, max_ctx=MAX_CTX, n_pages=8, max_seqs=2, max_rows=8))
+        d2.load_weights(bad)
+    assert e.value.code == fa_dec.FA_ERR_WEIGHTS and "up_proj" in str(e.value)
+    dec.close()
+
+
+def test_qwen3_06b_greedy_decode_batch1(torch_cuda):
+    """Full Qwen3-0.6B geometry (28 layers, vocab 151936): a 112-row prompt (30 token
+    ids around 82 audio-frame embeddings, as LFR T=82 for 5 s of audio) then 32 greedy
+    tokens with EOS ignored, batch 1 — the decoder part of the reference's CPU-runnable
+    case. Teacher-forced with the GPU's tokens so one disagreement does not cascade."""
+    cfg = fa_synth.QWEN3_06B
+    w = fa_synth.make_weights(cfg, seed=5)
+    dec = _decoder(w, cfg, n_pages=64, max_seqs=2, max_rows=128)
+    od = oracle.OracleDecoder(cfg, w, n_pages=64, max_seqs=2, max_pages_per_seq=MAX_CTX // 16, max_pos=MAX_CTX,
+                              mode=oracle.MODE_F16)
+    rng = np.random.default_rng(6)
+    emb = _embed_table(w, cfg)
+    rows = np.concatenate([emb[rng.integers(0, cfg["vocab"], 20)], rng.standard_normal((82, cfg["hidden"])),
+                           emb[rng.integers(0, cfg["vocab"], 10)]]).astype(np.float32)
+    s = dec.seq_open(MAX_CTX)
+    od.seq_open(s)
+    nxt, lg = dec.prefill(s, rows, want_logits=True)
+    o_lg, o_next = od.forward([s] * len(rows), embeds=rows)
+    assert_close(lg, o_lg[-1], what="prefill logits")
+    agree = [nxt == o_next[-1]]
+    tok = nxt
+    for step in range(32):
+        g_next, g_lg = dec.decode_step([s], [tok], want_logits=True)
+        o_lg, o_next = od.forward([s], tokens=[tok])
+        assert_close(g_lg, o_lg, what=f"step {step}")
+        agree.append(g_next[0] == o_next[0])
+        tok = int(g_next[0])
+    assert np.mean(agree) >= 0.99
+    assert dec.seq_length(s) == 112 + 32
+    dec.close()

@@ -1,0 +1,292 @@
+"""GPU parity of the kernel-level C-ABI entry points against the CPU oracle.
+
+Byte identity for the page writes (kernel 1 and the raw append), tolerance for the
+floating-point attention and GEMM outputs, exact indices for the argmax.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import fa_dec
+import fa_synth
+import oracle
+from helpers import assert_close, dev, max_abs, rel_rms
+
+pytestmark = pytest.mark.gpu
+
+PAGE_ELEMS = 8 * 2 * 16 * 128
+
+
+def _bf16_vec(rng, n, lo, hi):
+    return oracle.bf16_bits_to_f32(fa_synth.f32_to_bf16_bits(rng.uniform(lo, hi, n).astype(np.float32)))
+
+
+def _i16(a):
+    return np.ascontiguousarray(a, np.uint16).view(np.int16)
+
+
+def _u16(t):
+    return t.cpu().numpy().view(np.uint16)
+
+
+# ------------------------------------------------------------------- kernel 1 --
+def test_qknorm_rope_append_pages_byte_identical(torch_cuda):
+    torch = torch_cuda
+    rng = np.random.default_rng(10)
+    n_pages, max_pos, n_seq = 2048, 4096, 8
+    bt_stride = max_pos // 16
+    bt = rng.permutation(n_pages)[: n_seq * bt_stride].reshape(n_seq, bt_stride).astype(np.int32)
+    pairs = set()
+    edge = [0, 15, 16, 17, 4095, 2047, 2048]
+    rows = []
+    for p in edge:
+        rows.append((int(rng.integers(n_seq)), p))
+    while len(rows) < 61:
+        rows.append((int(rng.integers(n_seq)), int(rng.integers(max_pos))))
+    rows = [r for r in rows if not (r in pairs or pairs.add(r))]
+    slot = np.array([r[0] for r in rows], np.int32)
+    pos = np.array([r[1] for r in rows], np.int32)
+    M = len(rows)
+    qkv = (rng.standard_normal((M, 32 * 128)) * 3).astype(np.float32)
+    qn, kn = _bf16_vec(rng, 128, 0.8, 1.2), _bf16_vec(rng, 128, 0.8, 1.2)
+    rope = oracle.rope_table(max_pos)
+    pool0 = oracle.f32_to_f16_bits(rng.standard_normal((n_pages, PAGE_ELEMS)).astype(np.float32))
+
+    d_pool = dev(torch, _i16(pool0))
+    d_q = torch.zeros((M, 16 * 128), dtype=torch.float32, device="cuda")
+    d_err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = [dev(torch, a) for a in (qkv, pos, slot, bt, qn, kn, rope)]
+    fa_dec.op_qknorm_rope_append(args[0].data_ptr(), M, args[1].data_ptr(), args[2].data_ptr(), args[3].data_ptr(),
+                                 bt_stride, n_pages, args[4].data_ptr(), args[5].data_ptr(), 1e-5,
+                                 args[6].data_ptr(), max_pos, d_pool.data_ptr(), d_q.data_ptr(), d_err.data_ptr())
+    torch.cuda.synchronize()
+    pool_ref = pool0.copy()
+    q_ref = oracle.qknorm_rope_append(qkv, slot, pos, bt, qn, kn, rope, pool_ref)
+    assert int(d_err.item()) == 0
+    got = _u16(d_pool)
+    assert np.array_equal(got, pool_ref), f"{(got != pool_ref).sum()} f16 values differ"
+    assert np.array_equal(d_q.cpu().numpy().view(np.uint32), q_ref.view(np.uint32))
+
+
+def test_qknorm_rope_append_rejects_bad_page(torch_cuda):
+    torch = torch_cuda
+    n_pages = 4
+    bt = np.array([[0, 1, 7, 2]], np.int32)       # page 7 is outside the pool
+    pos = np.array([40], np.int32)                # page index 2 -> 7
+    slot = np.zeros(1, np.int32)
+    qkv = np.ones((1, 4096), np.float32)
+    rope = oracle.rope_table(64)
+    d_pool = torch.zeros((n_pages, PAGE_ELEMS), dtype=torch.int16, device="cuda")
+    d_q = torch.zeros((1, 2048), dtype=torch.float32, device="cuda")
+    d_err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = [dev(torch, x) for x in (qkv, pos, slot, bt, np.ones(128, np.float32), rope)]
+    fa_dec.op_qknorm_rope_append(a[0].data_ptr(), 1, a[1].data_ptr(), a[2].data_ptr(), a[3].data_ptr(), 4, n_pages,
+                                 a[4].data_ptr(), a[4].data_ptr(), 1e-5, a[5].data_ptr(), 64, d_pool.data_ptr(),
+                                 d_q.data_ptr(), d_err.data_ptr())
+    torch.cuda.synchronize()
+    assert int(d_err.item()) & 2
+    assert int(d_pool.abs().sum().item()) == 0
+
+
+# ----------------------------------------------- raw append (page-table bench) --
+def test_raw_append_cfg1_pages_byte_identical(torch_cuda):
+    """28 layers x 8 heads x 128 f16, page 16, 32 sequences with contexts ~U[64,1024],
+    block tables from a random permutation of a 4096-page pool, 256 append steps with
+    K/V ~ N(0,1) cast to f16: the touched pages equal the oracle's byte for byte."""
+    torch = torch_cuda
+    rng = np.random.default_rng(2024)
+    L, n_pages, n_seq, steps = 28, 4096, 32, 256
+    ctx0 = rng.integers(64, 1025, n_seq).astype(np.int32)
+    bt_stride = (1024 + steps + 15) // 16
+    bt = rng.permutation(n_pages)[: n_seq * bt_stride].reshape(n_seq, bt_stride).astype(np.int32)
+    d_pool = torch.zeros((L, n_pages, PAGE_ELEMS), dtype=torch.int16, device="cuda")
+    pool_ref = np.zeros((L, n_pages, PAGE_ELEMS), np.uint16)
+    d_bt = dev(torch, bt)
+    slot = np.arange(n_seq, dtype=np.int32)
+    d_slot = dev(torch, slot)
+    d_err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for s in range(steps):
+        pos = ctx0 + s
+        k = oracle.f32_to_f16_bits(rng.standard_normal((n_seq, L, 8, 128)).astype(np.float32))
+        v = oracle.f32_to_f16_bits(rng.standard_normal((n_seq, L, 8, 128)).astype(np.float32))
+        dk, dv, dp = dev(torch, _i16(k)), dev(torch, _i16(v)), dev(torch, pos)
+        fa_dec.op_kv_append(dk.data_ptr(), dv.data_ptr(), n_seq, L, dp.data_ptr(), d_slot.data_ptr(),
+                            d_bt.data_ptr(), bt_stride, n_pages, d_pool.data_ptr(), d_err.data_ptr())
+        oracle.kv_append_raw(k, v, slot, pos, bt, pool_ref, L, n_pages)
+    torch.cuda.synchronize()
+    assert int(d_err.item()) == 0
+    touched = np.unique(np.concatenate([bt[i, ctx0[i] // 16:(ctx0[i] + steps - 1) // 16 + 1] for i in range(n_seq)]))
+    idx = torch.from_numpy(touched.astype(np.int64)).cuda()
+    got = d_pool.index_select(1, idx).cpu().numpy().view(np.uint16)
+    assert np.array_equal(got, pool_ref[:, touched])
+    # nothing outside the touched pages was written
+    untouched = np.setdiff1d(np.arange(n_pages), touched)
+    assert int(d_pool.index_select(1, torch.from_numpy(untouched.astype(np.int64)).cuda()).abs().sum().item()) == 0
+
+
+# ------------------------------------------------------------------- kernel 2 --
+def _attention_case(torch, rng, n_kv, pps, n_splits=None, n_pages=1024, q_scale=0.3):
+    M = len(n_kv)
+    n_kv = np.asarray(n_kv, np.int32)
+    max_pg = int(math.ceil(n_kv.max() / 16))
+    bt_stride = max_pg + 1
+    bt = np.stack([rng.choice(n_pages, bt_stride, replace=bt_stride > n_pages) for _ in range(M)]).astype(np.int32)
+    pool = oracle.f32_to_f16_bits(rng.standard_normal((n_pages, PAGE_ELEMS)).astype(np.float32))
+    q = (rng.standard_normal((M, 16, 128)) * q_scale).astype(np.float32)
+    slot = np.arange(M, dtype=np.int32)
+    pos = n_kv - 1
+    if n_splits is None:
+        n_splits = int(math.ceil(max_pg / pps))
+    d = [dev(torch, a) for a in (q, pos, slot, bt, _i16(pool))]
+    out32 = torch.zeros((M, 2048), dtype=torch.float32, device="cuda")
+    out16 = torch.zeros((M, 2048), dtype=torch.int16, device="cuda")
+    nb = fa_dec.op_attention_scratch_bytes(M, n_splits)
+    scratch = torch.zeros(max(nb, 16), dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    fa_dec.op_paged_attention(d[0].data_ptr(), M, d[1].data_ptr(), d[2].data_ptr(), d[3].data_ptr(), bt_stride,
+                              n_pages, d[4].data_ptr(), pps, n_splits, scratch.data_ptr(), out16.data_ptr(),
+                              out32.data_ptr(), err.data_ptr())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = oracle.paged_attention(q, slot, n_kv, bt, pool)
+    return out32.cpu().numpy(), oracle.f16_bits_to_f32(_u16(out16)), ref
+
+
+@pytest.mark.parametrize("n_kv,pps,n_splits", [
+    ([1, 2, 15, 16, 17, 31, 33, 100, 257], 4, None),      # ragged, partial pages, idle warps
+    ([5, 64, 300], 20, 1),                                  # one split: direct output
+    ([2048] * 6 + [1, 2049, 1000], 32, None),               # long contexts, split-K combine
+    ([4000, 3], 64, None),
+])
+def test_paged_attention_matches_oracle(torch_cuda, n_kv, pps, n_splits):
+    rng = np.random.default_rng(sum(n_kv) + pps)
+    o32, o16, ref = _attention_case(torch_cuda, rng, n_kv, pps, n_splits)
+    assert_close(o32, ref, max_abs_tol=1e-4, rel_rms_tol=1e-5, what="attention f32")
+    assert_close(o16, ref, what="attention f16")
+
+
+def test_paged_attention_sharp_softmax(torch_cuda):
+    """Large scores (q scale 3): the online-softmax rescaling is exercised hard."""
+    rng = np.random.default_rng(77)
+    o32, o16, ref = _attention_case(torch_cuda, rng, [700, 1333, 50], 8, None, q_scale=3.0)
+    assert_close(o32, ref, max_abs_tol=1e-3, rel_rms_tol=1e-5, what="attention f32")
+
+
+def test_paged_attention_full_size_batch128_ctx2048(torch_cuda):
+    """B=128 rows at 2048-2175 tokens (one layer of the steady-state decode shape); all
+    rows checked for finiteness, 12 sampled rows against the oracle."""
+    torch = torch_cuda
+    rng = np.random.default_rng(5)
+    M, n_pages = 128, 128 * 137
+    n_kv = (2048 + rng.integers(0, 128, M)).astype(np.int32)
+    bt_stride = 137
+    bt = rng.permutation(n_pages).reshape(M, bt_stride).astype(np.int32)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    d_pool = (torch.randn((n_pages, PAGE_ELEMS), generator=gen, device="cuda", dtype=torch.float32) * 0.5)
+    d_pool = d_pool.to(torch.float16).view(torch.int16)
+    q = (rng.standard_normal((M, 16, 128)) * 0.3).astype(np.float32)
+    slot = np.arange(M, dtype=np.int32)
+    d = [dev(torch, a) for a in (q, n_kv - 1, slot, bt)] + [d_pool]
+    pps, n_splits = 64, 3
+    out32 = torch.zeros((M, 2048), dtype=torch.float32, device="cuda")
+    scratch = torch.zeros(fa_dec.op_attention_scratch_bytes(M, n_splits), dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    fa_dec.op_paged_attention(d[0].data_ptr(), M, d[1].data_ptr(), d[2].data_ptr(), d[3].data_ptr(), bt_stride,
+                              n_pages, d[4].data_ptr(), pps, n_splits, scratch.data_ptr(), 0, out32.data_ptr(),
+                              err.data_ptr())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = out32.cpu().numpy()
+    assert np.isfinite(got).all()
+    rows = rng.choice(M, 12, replace=False)
+    used = np.unique(bt[rows])
+    sub = d_pool.index_select(0, torch.from_numpy(used.astype(np.int64)).cuda()).cpu().numpy().view(np.uint16)
+    remap = np.searchsorted(used, bt[rows]).astype(np.int32)
+    ref = oracle.paged_attention(q[rows], np.arange(12, dtype=np.int32), n_kv[rows], remap, sub)
+    assert_close(got[rows], ref, max_abs_tol=1e-4, rel_rms_tol=1e-5, what="attention full size")
+
+
+# ------------------------------------------------------------------- kernel 4 --
+def _q8_device(torch, rng, N, K):
+    raw = fa_synth.q8_0_random(rng, N, K)
+    d_raw = dev(torch, raw)
+    q = torch.zeros((N, K), dtype=torch.int8, device="cuda")
+    d = torch.zeros((K // 32, N), dtype=torch.int16, device="cuda")
+    fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, q.data_ptr(), d.data_ptr())
+    return raw, q, d
+
+
+def test_repack_layout(torch_cuda):
+    rng = np.random.default_rng(0)
+    raw, q, d = _q8_device(torch_cuda, rng, 128, 256)
+    torch_cuda.cuda.synchronize()
+    blocks = raw.reshape(128, 8, 34)
+    assert np.array_equal(q.cpu().numpy(), blocks[:, :, 2:].view(np.int8).reshape(128, 256))
+    assert np.array_equal(d.cpu().numpy().view(np.uint16).T, blocks[:, :, :2].copy().view(np.uint16)[:, :, 0])
+
+
+@pytest.mark.parametrize("M,N,K,split", [
+    (1, 1024, 1024, 1), (5, 4096, 1024, 4), (16, 1024, 2048, 8), (17, 2048, 1024, 2),
+    (64, 6144, 1024, 4), (128, 1024, 3072, 12), (200, 1024, 1024, 1), (300, 512, 2048, 2),
+])
+def test_q8_gemm_matches_oracle_mode1(torch_cuda, M, N, K, split):
+    torch = torch_cuda
+    rng = np.random.default_rng(M * 7 + N + K)
+    raw, q, d = _q8_device(torch, rng, N, K)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    a16 = oracle.f32_to_f16_bits(a)
+    d_a = dev(torch, _i16(a16))
+    c = torch.zeros((split, M, N), dtype=torch.float32, device="cuda")
+    fa_dec.op_q8_gemm(d_a.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, split, c.data_ptr())
+    torch.cuda.synchronize()
+    got = c.sum(0).cpu().numpy()
+    ref = oracle.gemm_q8(oracle.f16_bits_to_f32(a16), raw, N, oracle.MODE_F16)
+    assert rel_rms(got, ref) < 2e-6, rel_rms(got, ref)
+    assert max_abs(got, ref) < 1e-4 * np.abs(ref).max()
+
+
+def test_lm_head_argmax_full_vocab(torch_cuda):
+    torch = torch_cuda
+    rng = np.random.default_rng(3)
+    M, N, K = 7, 151936, 1024
+    raw, q, d = _q8_device(torch, rng, N, K)
+    a16 = oracle.f32_to_f16_bits(rng.standard_normal((M, K)).astype(np.float32))
+    d_a = dev(torch, _i16(a16))
+    scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
+    nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
+    logits = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, scratch.data_ptr(),
+                             nxt.data_ptr(), logits.data_ptr())
+    torch.cuda.synchronize()
+    ref = oracle.gemm_q8(oracle.f16_bits_to_f32(a16), raw, N, oracle.MODE_F16)
+    assert rel_rms(logits.cpu().numpy(), ref) < 2e-6
+    assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(ref))
+    # the kernel's argmax is the first maximum of its own logits
+    assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(logits.cpu().numpy()))
+
+
+@pytest.mark.parametrize("j1,j2", [(1000, 70000), (64 * 5 + 3, 64 * 5 + 40), (0, 151935)])
+def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2):
+    torch = torch_cuda
+    M, N, K = 3, 151936, 1024
+    nb = K // 32
+    blocks = np.zeros((N, nb, 34), np.uint8)
+    small = np.float16(0.001).view(np.uint8)
+    blocks[:, :, 0:2] = small
+    big = np.float16(0.02).view(np.uint8)
+    for j in (j1, j2):
+        blocks[j, :, 0:2] = big
+        blocks[j, :, 2:] = np.uint8(127)
+    raw = blocks.reshape(N, nb * 34)
+    d_raw = dev(torch, raw)
+    q = torch.zeros((N, K), dtype=torch.int8, device="cuda")
+    d = torch.zeros((nb, N), dtype=torch.int16, device="cuda")
+    fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, q.data_ptr(), d.data_ptr())
+    a16 = oracle.f32_to_f16_bits(np.full((M, K), 0.5, np.float32))
+    d_a = dev(torch, _i16(a16))
+    scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
+    nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
+    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, scratch.data_ptr(), nxt.data_ptr())
+    torch.cuda.synchronize()
+    assert nxt.cpu().numpy().tolist() == [j1] * M

@@ -1,0 +1,100 @@
+"""CPU tests of the C-ABI library: it loads, exports the header's symbols, rejects bad
+descriptors, refuses to run without a GPU, and its page allocator follows the
+restated policy of the oracle (lowest free page first; compaction moves)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import fa_dec
+import oracle
+
+
+def test_library_exports_every_declared_symbol():
+    L = fa_dec.lib()
+    names = fa_dec.header_functions()
+    assert len(names) >= 35
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert b"sm_100a" in L.fa_version()
+
+
+def test_desc_struct_layout_matches_header():
+    # fa_model_desc: 10 ints/floats, one size_t (8-aligned), 2 ints
+    assert ctypes.sizeof(fa_dec._Desc) == 64
+    assert ctypes.sizeof(fa_dec._TensorView) == 48
+
+
+@pytest.mark.parametrize("field,value", [("head_dim", 64), ("n_kv_heads", 4), ("hidden", 1000), ("max_rows", 0)])
+def test_bad_descriptor_is_rejected_before_touching_the_gpu(field, value):
+    d = fa_dec.default_desc(**{field: value})
+    ctx = fa_dec.lib().fa_create(0, ctypes.byref(d))
+    assert not ctx
+    assert fa_dec.last_error(None)
+
+
+def test_no_cpu_fallback_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible; covered by the GPU tests")
+    with pytest.raises(fa_dec.FaError) as e:
+        fa_dec.Decoder(0)
+    assert "CUDA" in str(e.value) or "device" in str(e.value)
+
+
+def test_op_entry_points_validate_arguments():
+    with pytest.raises(fa_dec.FaError):
+        fa_dec.op_q8_gemm(0, 4, 100, 0, 0, 64, 1, 0)
+    assert fa_dec.op_attention_scratch_bytes(128, 1) == 0
+    assert fa_dec.op_attention_scratch_bytes(128, 4) == 128 * 16 * 4 * 130 * 4
+
+
+def test_allocator_matches_oracle_policy():
+    rng = np.random.default_rng(0)
+    n = 300
+    mine = fa_dec.PageAllocator(n)
+    ref = oracle.PageAllocatorOracle(n)
+    live = []
+    for step in range(5000):
+        if live and (rng.random() < 0.45 or len(live) == n):
+            p = live.pop(int(rng.integers(len(live))))
+            mine.free(p)
+            ref.free(p)
+        else:
+            a, b = mine.alloc(), ref.alloc()
+            assert a == b, step
+            live.append(a)
+        assert mine.n_free() == ref.n_free()
+    with pytest.raises(fa_dec.FaError):
+        mine.free(live[0]) if False else mine.free(n + 5)
+
+
+def test_allocator_exhaustion_and_double_free():
+    a = fa_dec.PageAllocator(3)
+    assert [a.alloc(), a.alloc(), a.alloc()] == [0, 1, 2]
+    with pytest.raises(fa_dec.FaError) as e:
+        a.alloc()
+    assert e.value.code == fa_dec.FA_ERR_POOL_EXHAUSTED
+    a.free(1)
+    with pytest.raises(fa_dec.FaError):
+        a.free(1)
+
+
+def test_compaction_matches_oracle_plan():
+    rng = np.random.default_rng(1)
+    for trial in range(20):
+        n = int(rng.integers(5, 200))
+        mine = fa_dec.PageAllocator(n)
+        pages = [mine.alloc() for _ in range(n)]
+        freed = rng.choice(n, size=int(rng.integers(0, n)), replace=False)
+        for p in freed:
+            mine.free(int(p))
+        live = sorted(set(pages) - set(int(p) for p in freed))
+        src, dst = mine.compact_moves()
+        assert (src, dst) == oracle.compaction_plan(live, n)
+        after = sorted((set(live) - set(src)) | set(dst))
+        assert after == list(range(len(live)))
+        # the allocator now hands out exactly the tail
+        assert mine.n_free() == n - len(live)
+        if len(live) < n:
+            assert mine.alloc() == len(live)
