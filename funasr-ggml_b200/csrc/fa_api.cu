@@ -108,12 +108,15 @@ struct fa_ctx {
 
     // step buffers
     float* x = nullptr;
-    __half* xn16 = nullptr;
+    __half* xn16 = nullptr;     // GEMM input activations: hi plane, lo plane at xn_lo
+    __half* xn_lo = nullptr;
     float* part = nullptr;
     size_t part_elems = 0;
     float* q_rot = nullptr;
     __half* attn16 = nullptr;
+    __half* attn_lo = nullptr;
     __half* h16 = nullptr;
+    __half* h_lo = nullptr;
     float* att_po = nullptr;
     float* att_pml = nullptr;
     int att_max_splits = 0;
@@ -301,11 +304,11 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
     ctx->att_max_splits = 64;
     ctx->max_updates = R + 64;
     if (dev_alloc(ctx, &ctx->x, sizeof(float) * R * d.hidden) ||
-        dev_alloc(ctx, &ctx->xn16, sizeof(__half) * R * std::max(d.hidden, d.ffn)) ||
+        dev_alloc(ctx, &ctx->xn16, sizeof(__half) * 2 * R * std::max(d.hidden, d.ffn)) ||
         dev_alloc(ctx, &ctx->part, sizeof(float) * ctx->part_elems) ||
         dev_alloc(ctx, &ctx->q_rot, sizeof(float) * R * kHq * kD) ||
-        dev_alloc(ctx, &ctx->attn16, sizeof(__half) * R * kHq * kD) ||
-        dev_alloc(ctx, &ctx->h16, sizeof(__half) * R * d.ffn) ||
+        dev_alloc(ctx, &ctx->attn16, sizeof(__half) * 2 * R * kHq * kD) ||
+        dev_alloc(ctx, &ctx->h16, sizeof(__half) * 2 * R * d.ffn) ||
         dev_alloc(ctx, &ctx->att_po, sizeof(float) * (size_t)R * kHq * ctx->att_max_splits * kD) ||
         dev_alloc(ctx, &ctx->att_pml, sizeof(float) * (size_t)R * kHq * ctx->att_max_splits * 2) ||
         dev_alloc(ctx, &ctx->amax_v, sizeof(float) * (size_t)R * (d.vocab / 64)) ||
@@ -317,6 +320,9 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
         dev_alloc(ctx, &ctx->err_dev, sizeof(int)))
         return fail();
     ctx->max_updates *= 64;
+    ctx->xn_lo = ctx->xn16 + (size_t)R * std::max(d.hidden, d.ffn);
+    ctx->attn_lo = ctx->attn16 + (size_t)R * kHq * kD;
+    ctx->h_lo = ctx->h16 + (size_t)R * d.ffn;
     if (cudaMemset(ctx->err_dev, 0, sizeof(int)) != cudaSuccess) {
         set_err(ctx, FA_ERR_CUDA, "memset err");
         return fail();
@@ -734,9 +740,9 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     for (int l = 0; l < d.n_layers; ++l) {
         const LayerW& w = ctx->L[l];
         __half* pool_l = ctx->pool + (size_t)l * ctx->layer_stride;
-        fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, w.in_norm, d.rms_eps, ctx->xn16, s);
+        fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, w.in_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         fa::GemmArgs g{};
-        g.A = ctx->xn16; g.Wq = w.qkv_q; g.Wd = w.qkv_d; g.M = M; g.N = QKV; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wq = w.qkv_q; g.Wd = w.qkv_d; g.M = M; g.N = QKV; g.K = H;
         g.n_split = p.s_qkv; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         fa::launch_q8_gemm(g, s);
         fa::AppendArgs a{};
@@ -750,7 +756,8 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         at.q = ctx->q_rot; at.pool_layer = pool_l; at.block_table = ctx->bt_dev; at.bt_stride = ctx->bt_stride;
         at.n_pages = ctx->n_pages; at.slot = ctx->row_slot; at.pos = ctx->row_pos; at.M = M; at.Hq = kHq;
         at.Hkv = kHkv; at.pages_per_split = p.pps; at.n_splits = p.n_splits; at.part_o = ctx->att_po;
-        at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out32 = nullptr; at.err = ctx->err_dev;
+        at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out16_lo = ctx->attn_lo; at.out32 = nullptr;
+        at.err = ctx->err_dev;
         if (p.prof) record_prof(ctx, 2 * l, capturing);
         fa::launch_paged_attention(at, s);
         ++n;
@@ -760,26 +767,26 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         }
         if (p.prof) record_prof(ctx, 2 * l + 1, capturing);
         g = fa::GemmArgs{};
-        g.A = ctx->attn16; g.Wq = w.o_q; g.Wd = w.o_d; g.M = M; g.N = H; g.K = kHq * kD;
+        g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.Wq = w.o_q; g.Wd = w.o_d; g.M = M; g.N = H; g.K = kHq * kD;
         g.n_split = p.s_o; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         fa::launch_q8_gemm(g, s);
-        fa::launch_residual_rmsnorm(ctx->x, ctx->part, p.s_o, M, H, w.post_norm, d.rms_eps, ctx->xn16, s);
+        fa::launch_residual_rmsnorm(ctx->x, ctx->part, p.s_o, M, H, w.post_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         g = fa::GemmArgs{};
-        g.A = ctx->xn16; g.Wq = w.gu_q; g.Wd = w.gu_d; g.M = M; g.N = 2 * F; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wq = w.gu_q; g.Wd = w.gu_d; g.M = M; g.N = 2 * F; g.K = H;
         g.n_split = p.s_gu; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         fa::launch_q8_gemm(g, s);
-        fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, s);
+        fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s);
         g = fa::GemmArgs{};
-        g.A = ctx->h16; g.Wq = w.dn_q; g.Wd = w.dn_d; g.M = M; g.N = H; g.K = F;
+        g.A = ctx->h16; g.A_lo = ctx->h_lo; g.Wq = w.dn_q; g.Wd = w.dn_d; g.M = M; g.N = H; g.K = F;
         g.n_split = p.s_dn; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         fa::launch_q8_gemm(g, s);
         n += 8;
         prev_part = ctx->part;
         prev_n = p.s_dn;
     }
-    fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, s);
+    fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
     fa::GemmArgs g{};
-    g.A = ctx->xn16; g.Wq = ctx->lm_q; g.Wd = ctx->lm_d; g.M = M; g.N = d.vocab; g.K = H;
+    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wq = ctx->lm_q; g.Wd = ctx->lm_d; g.M = M; g.N = d.vocab; g.K = H;
     g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = p.logits ? ctx->logits_dev : nullptr;
     g.amax_val = ctx->amax_v; g.amax_idx = ctx->amax_i;
     fa::launch_q8_gemm(g, s);
@@ -1242,7 +1249,8 @@ extern "C" size_t fa_op_attention_scratch_bytes(int M, int n_splits) {
 
 extern "C" int fa_op_paged_attention(const float* q, int M, const int* pos, const int* slot, const int* bt,
                                      int bt_stride, int n_pages, const uint16_t* pool_layer, int pps, int n_splits,
-                                     void* scratch, uint16_t* out16, float* out32, int* err, void* stream) {
+                                     void* scratch, uint16_t* out16, uint16_t* out16_lo, float* out32, int* err,
+                                     void* stream) {
     if (!q || !pos || !slot || !bt || !pool_layer || M <= 0 || pps <= 0 || n_splits <= 0 || (!out16 && !out32))
         return set_err(nullptr, FA_ERR_INVALID_ARG, "null or non-positive argument");
     if (n_splits > 1 && !scratch) return set_err(nullptr, FA_ERR_INVALID_ARG, "scratch required when n_splits > 1");
@@ -1253,7 +1261,8 @@ extern "C" int fa_op_paged_attention(const float* q, int M, const int* pos, cons
     a.n_splits = n_splits;
     a.part_o = reinterpret_cast<float*>(scratch);
     a.part_ml = a.part_o ? a.part_o + (size_t)M * kHq * n_splits * kD : nullptr;
-    a.out16 = reinterpret_cast<__half*>(out16); a.out32 = out32; a.err = err;
+    a.out16 = reinterpret_cast<__half*>(out16); a.out16_lo = reinterpret_cast<__half*>(out16_lo);
+    a.out32 = out32; a.err = err;
     fa::launch_paged_attention(a, (cudaStream_t)stream);
     if (n_splits > 1) fa::launch_attn_combine(a, (cudaStream_t)stream);
     OP_CK(cudaGetLastError());
@@ -1267,14 +1276,15 @@ extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, int8_t* q, uint
     return FA_OK;
 }
 
-extern "C" int fa_op_q8_gemm(const uint16_t* a16, int M, int K, const int8_t* q, const uint16_t* d, int N, int n_split,
-                             float* c, void* stream) {
+extern "C" int fa_op_q8_gemm(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const int8_t* q,
+                             const uint16_t* d, int N, int n_split, float* c, void* stream) {
     if (!a16 || !q || !d || !c || M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_split <= 0 ||
         (K / 64) % n_split)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "need N, K multiples of 64 and n_split dividing K/64");
     if (int rc = ensure_configured()) return rc;
     fa::GemmArgs g{};
-    g.A = reinterpret_cast<const __half*>(a16); g.Wq = q; g.Wd = reinterpret_cast<const __half*>(d);
+    g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo); g.Wq = q;
+    g.Wd = reinterpret_cast<const __half*>(d);
     g.M = M; g.N = N; g.K = K; g.n_split = n_split; g.epilogue = fa::kEpiStoreF32; g.C = c;
     fa::launch_q8_gemm(g, (cudaStream_t)stream);
     OP_CK(cudaGetLastError());
@@ -1286,13 +1296,15 @@ extern "C" size_t fa_op_argmax_scratch_bytes(int M, int N) {
     return (size_t)M * (N / 64) * (sizeof(float) + sizeof(int));
 }
 
-extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, int M, int K, const int8_t* q, const uint16_t* d, int N,
-                                    void* scratch, int* next, float* logits, void* stream) {
+extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const int8_t* q,
+                                    const uint16_t* d, int N, void* scratch, int* next, float* logits,
+                                    void* stream) {
     if (!a16 || !q || !d || !scratch || !next || M <= 0 || N % 64 || K % 64)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
     if (int rc = ensure_configured()) return rc;
     fa::GemmArgs g{};
-    g.A = reinterpret_cast<const __half*>(a16); g.Wq = q; g.Wd = reinterpret_cast<const __half*>(d);
+    g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo); g.Wq = q;
+    g.Wd = reinterpret_cast<const __half*>(d);
     g.M = M; g.N = N; g.K = K; g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = logits;
     g.amax_val = reinterpret_cast<float*>(scratch);
     g.amax_idx = reinterpret_cast<int*>(g.amax_val + (size_t)M * (N / 64));

@@ -58,7 +58,8 @@ struct AttnArgs {
     int n_splits;            // grid.x; splits beyond a row's length exit at once
     float* part_o;           // [M][Hq][n_splits][128] un-normalised partial outputs
     float* part_ml;          // [M][Hq][n_splits][2]   (running max in log2 units, sum)
-    __half* out16;           // [M][Hq*128] final output (f16) or nullptr
+    __half* out16;           // [M][Hq*128] final output as f16 hi part, or nullptr
+    __half* out16_lo;        // [M][Hq*128] f16 remainder (out - hi), or nullptr
     float* out32;            // [M][Hq*128] final output (f32) or nullptr
     int* err;
 };
@@ -71,7 +72,8 @@ void launch_attn_combine(const AttnArgs& a, cudaStream_t s);
 // Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T
 enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1 };
 struct GemmArgs {
-    const __half* A;         // [M][K] f16 activations
+    const __half* A;         // [M][K] f16 activations (hi part)
+    const __half* A_lo;      // [M][K] f16 remainder x - hi, or nullptr (plain f16 activations)
     const int8_t* Wq;        // [N][K] int8
     const __half* Wd;        // [K/32][N] f16 block scales
     int M, N, K;
@@ -87,11 +89,12 @@ int gemm_pick_split(int M, int N, int K, int n_sm);
 // ----------------------------------------------------------------- k_small.cu --
 void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds,
                   int M, int vocab, float* x, int* err, cudaStream_t s);
-// x[m] += sum_s part[s][m] (n_part may be 0); xn16[m] = f16(rmsnorm(x[m]) * w)
+// Activations for the GEMMs leave their producer as an f16 pair: hi = f16(y), lo = f16(y - hi).
+// x[m] += sum_s part[s][m] (n_part may be 0); (hi, lo)[m] = split(rmsnorm(x[m]) * w)
 void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w,
-                             float eps, __half* xn16, cudaStream_t s);
-// h16[m][j] = f16(silu(g) * u) with g, u summed over n_part partials of the interleaved gate/up GEMM
-void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h16, cudaStream_t s);
+                             float eps, __half* xn_hi, __half* xn_lo, cudaStream_t s);
+// (hi, lo)[m][j] = split(silu(g) * u), g and u summed over n_part partials of the gate|up GEMM
+void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s);
 // next[m] = first column of the row maximum over n_tiles partial maxima; optional feedback
 // of the token into tokens[m] and pos[m] += 1 for device-fed generation.
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,

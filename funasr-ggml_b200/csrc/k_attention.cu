@@ -87,6 +87,16 @@ __device__ __forceinline__ float transpose_reduce16(float (&v)[16], int lane) {
     return v[0];
 }
 
+// Output as f32 and/or as the (hi, lo) f16 pair the o_proj GEMM consumes.
+__device__ __forceinline__ void store_out(const AttnArgs& a, size_t o, float v) {
+    if (a.out16) {
+        const __half h = __float2half_rn(v);
+        a.out16[o] = h;
+        if (a.out16_lo) a.out16_lo[o] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+    }
+    if (a.out32) a.out32[o] = v;
+}
+
 __global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
@@ -292,9 +302,7 @@ __global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
         const int H = 2 * h + hq;
         if (a.n_splits == 1) {
             const float v = L > 0.0f ? O / L : 0.0f;
-            const size_t o = (size_t)m * a.Hq * D + (size_t)H * D + d;
-            if (a.out16) a.out16[o] = __float2half_rn(v);
-            if (a.out32) a.out32[o] = v;
+            store_out(a, (size_t)m * a.Hq * D + (size_t)H * D + d, v);
         } else {
             const size_t base = ((size_t)m * a.Hq + H) * a.n_splits + split;
             a.part_o[base * D + d] = O;
@@ -325,9 +333,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
         }
     }
     const float v = L > 0.0f ? O / L : 0.0f;
-    const size_t o = (size_t)m * a.Hq * D + (size_t)H * D + d;
-    if (a.out16) a.out16[o] = __float2half_rn(v);
-    if (a.out32) a.out32[o] = v;
+    store_out(a, (size_t)m * a.Hq * D + (size_t)H * D + d, v);
 }
 
 }  // namespace

@@ -5,14 +5,18 @@
 // :206 lm_head). At decode batch B the weight stream is read once per step for
 // all B rows, so the op is a skinny GEMM C[B][N] = A[B][K] . W[N][K]^T.
 //
-// Arithmetic (same as the oracle's GEMM mode 1): activations arrive as f16,
-// weights are dequantised once per CTA tile into shared memory as
-// f16(f32(d) * q), products are exact in fp32 and accumulate in fp32 on the
-// tensor cores (mma.sync m16n8k16).
+// Arithmetic (the oracle's exact GEMM mode): activations arrive as an f16 pair
+// (hi, lo) with hi + lo = x to ~22 bits, the int8 weights enter the MMA exactly as
+// f16, and each 32-wide Q8_0 block's partial sum is scaled by its f16 scale d in
+// fp32 before it joins the fp32 accumulator. So the result is the f32 product
+// of the activations with the exactly dequantised weights d*q, like ggml's
+// block-scaled dot, without rounding either operand to 11 bits. (Rounding the
+// activations to a single f16 makes the decoder output jump by ~3e-4 relative
+// under 1e-7 input noise, which no parity tolerance survives.)
 //
-// Pipeline: 3-stage cp.async ring for the A tile (BM x 64 f16), the int8 weight
-// tile (64 x 64) and its two rows of block scales; a dequantisation pass writes
-// the f16 B tile; ldmatrix feeds the MMAs. Split-K over grid.z writes fp32
+// Pipeline: 3-stage cp.async ring for the A tiles (BM x 64 f16, hi and lo), the
+// int8 weight tile (64 x 64) and its two rows of block scales; a conversion pass
+// writes the int8 tile as f16; ldmatrix feeds the MMAs (2 per k16 step). Split-K over grid.z writes fp32
 // partials that the next fused kernel (RoPE/append, residual+RMSNorm, SwiGLU)
 // sums in a fixed order, so results are deterministic.
 // Epilogue kEpiArgmax (lm_head): per-row maximum and its first column over the
@@ -42,8 +46,8 @@ struct Cfg {
     static constexpr int A_STAGE = BM * A_LD;        // halves
     static constexpr int Q_STAGE = BN * BK;          // bytes
     static constexpr int S_STAGE = 2 * BN;           // halves (2 K-blocks x BN scales)
-    static constexpr size_t SMEM = (size_t)STAGES * (A_STAGE * 2 + Q_STAGE + S_STAGE * 2) + (size_t)BN * B_LD * 2 +
-                                   (size_t)BM * WN * 8;
+    static constexpr size_t SMEM = (size_t)STAGES * (2 * A_STAGE * 2 + Q_STAGE + S_STAGE * 2) +
+                                   (size_t)BN * B_LD * 2 + (size_t)BM * WN * 8;
     static_assert(WTM % 16 == 0 && WTN % 8 == 0, "warp tile");
     static_assert(NT % 2 == 0, "B fragments are loaded two n8 tiles at a time");
 };
@@ -75,10 +79,12 @@ template <int BM, int WM, int WN>
 __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const GemmArgs g) {
     using C = Cfg<BM, WM, WN>;
     extern __shared__ __align__(128) unsigned char smem[];
+    // A stage st: hi tile at As + (2*st) * A_STAGE, lo tile right after it
     __half* As = reinterpret_cast<__half*>(smem);
-    int8_t* Qs = reinterpret_cast<int8_t*>(smem + (size_t)STAGES * C::A_STAGE * 2);
-    __half* Ss = reinterpret_cast<__half*>(smem + (size_t)STAGES * (C::A_STAGE * 2 + C::Q_STAGE));
-    __half* Bs = reinterpret_cast<__half*>(smem + (size_t)STAGES * (C::A_STAGE * 2 + C::Q_STAGE + C::S_STAGE * 2));
+    int8_t* Qs = reinterpret_cast<int8_t*>(smem + (size_t)STAGES * 2 * C::A_STAGE * 2);
+    __half* Ss = reinterpret_cast<__half*>(smem + (size_t)STAGES * (2 * C::A_STAGE * 2 + C::Q_STAGE));
+    __half* Bs = reinterpret_cast<__half*>(smem + (size_t)STAGES * (2 * C::A_STAGE * 2 + C::Q_STAGE + C::S_STAGE * 2));
+    const bool has_lo = g.A_lo != nullptr;
     float* red_v = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(Bs) + (size_t)BN * B_LD * 2);
     int* red_i = reinterpret_cast<int*>(red_v + BM * WN);
 
@@ -93,13 +99,14 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
 
     auto load_stage = [&](int it, int st) {
         const int k0 = k_begin + it * BK;
-        __half* a_dst = As + st * C::A_STAGE;
-        for (int ch = tid; ch < BM * 8; ch += C::THREADS) {
-            const int r = ch >> 3, cc = ch & 7;
+        __half* a_dst = As + 2 * st * C::A_STAGE;
+        for (int ch = tid; ch < BM * 8 * (has_lo ? 2 : 1); ch += C::THREADS) {
+            const int pl = ch / (BM * 8);
+            const int r = (ch >> 3) % BM, cc = ch & 7;
             const int gm = m0 + r;
             const bool ok = gm < g.M;
-            const __half* src = g.A + (size_t)(ok ? gm : 0) * g.K + k0 + cc * 8;
-            cp_async16(a_dst + r * A_LD + cc * 8, src, ok);
+            const __half* src = (pl ? g.A_lo : g.A) + (size_t)(ok ? gm : 0) * g.K + k0 + cc * 8;
+            cp_async16(a_dst + pl * C::A_STAGE + r * A_LD + cc * 8, src, ok);
         }
         int8_t* q_dst = Qs + st * C::Q_STAGE;
         for (int ch = tid; ch < BN * 4; ch += C::THREADS) {
@@ -131,20 +138,18 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
         const int st = it % STAGES;
         cp_async_wait<STAGES - 2>();
         __syncthreads();
-        // dequantise the int8 tile of this stage into Bs (f16)
+        // the int8 tile of this stage into Bs as f16 (exact: |q| <= 127)
         {
             const int8_t* q_src = Qs + st * C::Q_STAGE;
-            const __half* s_src = Ss + st * C::S_STAGE;
             for (int ch = tid; ch < BN * 4; ch += C::THREADS) {
                 const int r = ch >> 2, cc = ch & 3;
                 const uint4 w = *reinterpret_cast<const uint4*>(q_src + r * BK + cc * 16);
-                const float d = __half2float(s_src[(cc >> 1) * BN + r]);
                 uint32_t o[8];
                 const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    o[2 * k] = pack_h2(d * s8_at(ws[k], 0), d * s8_at(ws[k], 1));
-                    o[2 * k + 1] = pack_h2(d * s8_at(ws[k], 2), d * s8_at(ws[k], 3));
+                    o[2 * k] = pack_h2(s8_at(ws[k], 0), s8_at(ws[k], 1));
+                    o[2 * k + 1] = pack_h2(s8_at(ws[k], 2), s8_at(ws[k], 3));
                 }
                 uint4* dst = reinterpret_cast<uint4*>(Bs + r * B_LD + cc * 16);
                 dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -157,24 +162,57 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
             if (nx < n_iter) load_stage(nx, nx % STAGES);
             cp_async_commit();
         }
-        const __half* a_st = As + st * C::A_STAGE;
+        const __half* a_hi = As + 2 * st * C::A_STAGE;
+        const __half* a_lo = a_hi + C::A_STAGE;
+        const __half* s_st = Ss + st * C::S_STAGE;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-            uint32_t af[C::MT][4];
+        for (int kb = 0; kb < BK / kQK; ++kb) {
+            float bacc[C::MT][C::NT][4];
 #pragma unroll
-            for (int mt = 0; mt < C::MT; ++mt) {
-                const int r = wm * C::WTM + mt * 16 + (lane & 15);
-                ldmatrix_x4(af[mt], a_st + r * A_LD + kk * 16 + (lane >> 4) * 8);
-            }
+            for (int i = 0; i < C::MT; ++i)
 #pragma unroll
-            for (int np = 0; np < C::NT / 2; ++np) {
-                uint32_t bf[4];
-                const int r = wn * C::WTN + np * 16 + (lane & 7) + ((lane >> 4) << 3);
-                ldmatrix_x4(bf, Bs + r * B_LD + kk * 16 + ((lane >> 3) & 1) * 8);
+                for (int j = 0; j < C::NT; ++j)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) bacc[i][j][k] = 0.0f;
+#pragma unroll
+            for (int k2 = 0; k2 < kQK / 16; ++k2) {
+                const int kk = kb * (kQK / 16) + k2;
+                uint32_t ah[C::MT][4], al[C::MT][4];
 #pragma unroll
                 for (int mt = 0; mt < C::MT; ++mt) {
-                    mma16816(acc[mt][2 * np], af[mt], bf[0], bf[1]);
-                    mma16816(acc[mt][2 * np + 1], af[mt], bf[2], bf[3]);
+                    const int r = wm * C::WTM + mt * 16 + (lane & 15);
+                    ldmatrix_x4(ah[mt], a_hi + r * A_LD + kk * 16 + (lane >> 4) * 8);
+                    if (has_lo) ldmatrix_x4(al[mt], a_lo + r * A_LD + kk * 16 + (lane >> 4) * 8);
+                }
+#pragma unroll
+                for (int np = 0; np < C::NT / 2; ++np) {
+                    uint32_t bf[4];
+                    const int r = wn * C::WTN + np * 16 + (lane & 7) + ((lane >> 4) << 3);
+                    ldmatrix_x4(bf, Bs + r * B_LD + kk * 16 + ((lane >> 3) & 1) * 8);
+#pragma unroll
+                    for (int mt = 0; mt < C::MT; ++mt) {
+                        mma16816(bacc[mt][2 * np], ah[mt], bf[0], bf[1]);
+                        mma16816(bacc[mt][2 * np + 1], ah[mt], bf[2], bf[3]);
+                        if (has_lo) {
+                            mma16816(bacc[mt][2 * np], al[mt], bf[0], bf[1]);
+                            mma16816(bacc[mt][2 * np + 1], al[mt], bf[2], bf[3]);
+                        }
+                    }
+                }
+            }
+            // scale the block partials by d of their columns and accumulate
+            const int tq = lane & 3;
+#pragma unroll
+            for (int nt = 0; nt < C::NT; ++nt) {
+                const int col = wn * C::WTN + nt * 8 + 2 * tq;
+                const float d0 = __half2float(s_st[kb * BN + col]);
+                const float d1 = __half2float(s_st[kb * BN + col + 1]);
+#pragma unroll
+                for (int mt = 0; mt < C::MT; ++mt) {
+                    acc[mt][nt][0] = fmaf(bacc[mt][nt][0], d0, acc[mt][nt][0]);
+                    acc[mt][nt][1] = fmaf(bacc[mt][nt][1], d1, acc[mt][nt][1]);
+                    acc[mt][nt][2] = fmaf(bacc[mt][nt][2], d0, acc[mt][nt][2]);
+                    acc[mt][nt][3] = fmaf(bacc[mt][nt][3], d1, acc[mt][nt][3]);
                 }
             }
         }

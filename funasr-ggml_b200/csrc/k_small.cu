@@ -59,9 +59,15 @@ __global__ void __launch_bounds__(256) embed_kernel(const void* table, int table
     }
 }
 
+__device__ __forceinline__ void split_store(float y, __half* hi, __half* lo, size_t i) {
+    const __half h = __float2half_rn(y);
+    hi[i] = h;
+    if (lo) lo[i] = __float2half_rn(__fsub_rn(y, __half2float(h)));
+}
+
 __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const float* part, int n_part, int M,
                                                                int hidden, const float* w, float eps,
-                                                               __half* xn16) {
+                                                               __half* xn_hi, __half* xn_lo) {
     __shared__ double sh[8];
     const int m = blockIdx.x;
     float* xr = x + (size_t)m * hidden;
@@ -80,11 +86,11 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const f
     const float mean = (float)(ss / (double)hidden);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
     for (int i = threadIdx.x; i < hidden; i += 256)
-        xn16[(size_t)m * hidden + i] = __float2half_rn(__fmul_rn(__fmul_rn(xr[i], scale), w[i]));
+        split_store(__fmul_rn(__fmul_rn(xr[i], scale), w[i]), xn_hi, xn_lo, (size_t)m * hidden + i);
 }
 
 __global__ void __launch_bounds__(256) swiglu_kernel(const float* part, int n_part, int M, int ffn,
-                                                     __half* h16) {
+                                                     __half* h_hi, __half* h_lo) {
     const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
     if (idx >= (size_t)M * ffn) return;
     const int m = (int)(idx / ffn), j = (int)(idx % ffn);
@@ -95,7 +101,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const float* part, int n_pa
         us = __fadd_rn(us, row[ffn + j]);
     }
     const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
-    h16[idx] = __float2half_rn(__fmul_rn(sg, us));
+    split_store(__fmul_rn(sg, us), h_hi, h_lo, idx);
 }
 
 __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float* val, const int* idx, int n_tiles,
@@ -198,13 +204,13 @@ void launch_embed(const void* table, int table_type, int hidden, const int* toke
 }
 
 void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w, float eps,
-                             __half* xn16, cudaStream_t s) {
-    residual_rmsnorm_kernel<<<M, 256, 0, s>>>(x, part, n_part, M, hidden, w, eps, xn16);
+                             __half* xn_hi, __half* xn_lo, cudaStream_t s) {
+    residual_rmsnorm_kernel<<<M, 256, 0, s>>>(x, part, n_part, M, hidden, w, eps, xn_hi, xn_lo);
 }
 
-void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h16, cudaStream_t s) {
+void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s) {
     const size_t n = (size_t)M * ffn;
-    swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, n_part, M, ffn, h16);
+    swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, n_part, M, ffn, h_hi, h_lo);
 }
 
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,

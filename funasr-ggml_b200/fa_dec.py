@@ -102,11 +102,11 @@ def lib():
         "fa_op_qknorm_rope_append": ([_P, _I, _P, _P, _P, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P, _P, _P, _P], _I),
         "fa_op_kv_append": ([_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P], _I),
         "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
-        "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
+        "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P, _P], _I),
-        "fa_op_q8_gemm": ([_P, _I, _I, _P, _P, _I, _I, _P, _P], _I),
+        "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _P, _I, _I, _P, _P], _I),
         "fa_op_argmax_scratch_bytes": ([_I, _I], ctypes.c_size_t),
-        "fa_op_q8_gemm_argmax": ([_P, _I, _I, _P, _P, _I, _P, _P, _P, _P], _I),
+        "fa_op_q8_gemm_argmax": ([_P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _P], _I),
         "fa_palloc_create": ([_I], _P),
         "fa_palloc_destroy": ([_P], None),
         "fa_palloc_alloc": ([_P], _I),
@@ -324,25 +324,27 @@ def op_attention_scratch_bytes(M, n_splits) -> int:
 
 
 def op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits, scratch, out16=0, out32=0,
-                       err=0, stream=0):
+                       err=0, stream=0, out16_lo=0):
     _check(lib().fa_op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits,
-                                       scratch or None, out16 or None, out32 or None, err or None, stream or None))
+                                       scratch or None, out16 or None, out16_lo or None, out32 or None, err or None,
+                                       stream or None))
 
 
 def op_repack_q8(raw, N, K, q, d, stream=0):
     _check(lib().fa_op_repack_q8(raw, N, K, q, d, stream or None))
 
 
-def op_q8_gemm(a16, M, K, q, d, N, n_split, c, stream=0):
-    _check(lib().fa_op_q8_gemm(a16, M, K, q, d, N, n_split, c, stream or None))
+def op_q8_gemm(a16, a16_lo, M, K, q, d, N, n_split, c, stream=0):
+    _check(lib().fa_op_q8_gemm(a16, a16_lo or None, M, K, q, d, N, n_split, c, stream or None))
 
 
 def op_argmax_scratch_bytes(M, N) -> int:
     return int(lib().fa_op_argmax_scratch_bytes(M, N))
 
 
-def op_q8_gemm_argmax(a16, M, K, q, d, N, scratch, nxt, logits=0, stream=0):
-    _check(lib().fa_op_q8_gemm_argmax(a16, M, K, q, d, N, scratch, nxt, logits or None, stream or None))
+def op_q8_gemm_argmax(a16, a16_lo, M, K, q, d, N, scratch, nxt, logits=0, stream=0):
+    _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, q, d, N, scratch, nxt, logits or None,
+                                      stream or None))
 
 
 # ------------------------------------------------------ host page allocator --

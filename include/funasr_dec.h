@@ -179,23 +179,27 @@ FA_API int fa_op_kv_append(const uint16_t* k_dev, const uint16_t* v_dev, int M, 
                     uint16_t* pool_dev, int* err_dev, void* stream);
 /* Kernel (2): paged GQA decode attention (compute/llm_ops_gpu.cpp:98-143). Row m attends
  * to tokens [0, pos[m]] of sequence slot[m]. q [M][16][128] f32 (pre-scaled).
- * Output f16 and/or f32 [M][2048]. scratch_dev holds the split-K partials:
+ * Output [M][2048] as f32 and/or as an f16 pair (out16 = f16(o), out16_lo = f16(o - out16),
+ * the form the next GEMM reads). scratch_dev holds the split-K partials:
  * fa_op_attention_scratch_bytes(M, n_splits) bytes (may be NULL when n_splits == 1). */
 FA_API size_t fa_op_attention_scratch_bytes(int M, int n_splits);
 FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
                           const int* block_table_dev, int bt_stride, int n_pages, const uint16_t* pool_layer_dev,
                           int pages_per_split, int n_splits, void* scratch_dev, uint16_t* out16_dev,
-                          float* out32_dev, int* err_dev, void* stream);
-/* Kernel (4): Q8_0 GEMM C = A . W^T. A [M][K] f16; W in the library's repacked form:
- * q [N][K] int8 and d [K/32][N] f16 (fa_op_repack_q8 builds it from GGUF blocks).
- * n_split > 1 writes partials [n_split][M][N]; fa_op_q8_gemm sums them when sum_dev is given. */
+                          uint16_t* out16_lo_dev, float* out32_dev, int* err_dev, void* stream);
+/* Kernel (4): Q8_0 GEMM C = A . W^T (compute/llm_ops_gpu.cpp:53-55,149,177-180,206).
+ * A [M][K] as an f16 pair a16 + a16_lo (a16_lo may be NULL: plain f16 activations);
+ * W in the library's repacked form q [N][K] int8 and d [K/32][N] f16 (fa_op_repack_q8
+ * builds it from GGUF blocks); each 32-block's partial sum is scaled by d in fp32.
+ * n_split > 1 writes partials [n_split][M][N] (their sum is C). */
 FA_API int fa_op_repack_q8(const uint8_t* gguf_q8_dev, int N, int K, int8_t* q_dev, uint16_t* d_dev, void* stream);
-FA_API int fa_op_q8_gemm(const uint16_t* a16_dev, int M, int K, const int8_t* q_dev, const uint16_t* d_dev, int N,
-                  int n_split, float* c_dev, void* stream);
+FA_API int fa_op_q8_gemm(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K, const int8_t* q_dev,
+                         const uint16_t* d_dev, int N, int n_split, float* c_dev, void* stream);
 /* lm_head with fused argmax: next [M] = first column of each row's maximum; logits optional. */
 FA_API size_t fa_op_argmax_scratch_bytes(int M, int N);
-FA_API int fa_op_q8_gemm_argmax(const uint16_t* a16_dev, int M, int K, const int8_t* q_dev, const uint16_t* d_dev,
-                         int N, void* scratch_dev, int* next_dev, float* logits_dev, void* stream);
+FA_API int fa_op_q8_gemm_argmax(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K,
+                                const int8_t* q_dev, const uint16_t* d_dev, int N, void* scratch_dev, int* next_dev,
+                                float* logits_dev, void* stream);
 
 /* ---- host-only page allocator (no GPU needed): the policy behind fa_seq_* ----
  * Lowest free page id first; compaction moves the highest live page into the lowest

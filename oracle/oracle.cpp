@@ -36,9 +36,10 @@
 //     f32 -> f16 is round-to-nearest-even.
 //   * RoPE cos/sin: theta computed in double, cos/sin in double, rounded to f32
 //     once into a table [pos][i] (the same table the CUDA path uploads).
-//   * GEMM mode 1 (the CUDA path's arithmetic): activations rounded to f16,
-//     weights dequantised as f16(f32(d) * q), products exact, sums in wide precision.
-//     Mode 0 is exact f32 activations x dequantised weights.
+//   * GEMM mode 0 (the CUDA path's arithmetic): f32 activations times the exactly
+//     dequantised weights d*q, sums in wide precision. (The CUDA path carries the
+//     activations as an f16 hi/lo pair, ~22 bits, and scales each 32-block in fp32.)
+//     Mode 2 is the ggml CPU backend's Q8_0-activation arithmetic.
 //   * Attention scores, softmax and PV are computed in double here.
 //
 // Parity pins: the Q8_0 codec is pinned byte-for-byte against the reference
@@ -104,8 +105,6 @@ inline uint16_t f2h(float f) {
 
 inline float bf2f(uint16_t b) { return bits_f((uint32_t)b << 16); }
 
-inline float round_f16(float x) { return h2f(f2h(x)); }
-
 constexpr int QK = 32;           // Q8_0 block length
 constexpr int QB = 34;           // Q8_0 block bytes: f16 d + 32 x int8
 
@@ -138,15 +137,14 @@ inline void rope_neox(float* y, int d, const float* cs) {
 }
 
 // ---------------------------------------------------------------- Q8_0 -------
-inline void q8_row_dequant(const uint8_t* row, int K, float* out, int mode_f16) {
+inline void q8_row_dequant(const uint8_t* row, int K, float* out) {
     for (int b = 0; b < K / QK; ++b) {
         const uint8_t* blk = row + (size_t)b * QB;
         uint16_t dh; std::memcpy(&dh, blk, 2);
         const float d = h2f(dh);
         const int8_t* q = (const int8_t*)(blk + 2);
         for (int j = 0; j < QK; ++j) {
-            float w = d * (float)q[j];          // exact in f32
-            out[b * QK + j] = mode_f16 ? round_f16(w) : w;
+            out[b * QK + j] = d * (float)q[j];  // exact in f32
         }
     }
 }
@@ -216,7 +214,7 @@ void or_q8_0_quantize(const float* x, int64_t n, uint8_t* out) {
 
 void or_q8_0_dequant(const uint8_t* blocks, int64_t n, float* out) {
     const int64_t nb = n / QK;
-    for (int64_t b = 0; b < nb; ++b) q8_row_dequant(blocks + b * QB, QK, out + b * QK, 0);
+    for (int64_t b = 0; b < nb; ++b) q8_row_dequant(blocks + b * QB, QK, out + b * QK);
 }
 
 // ---- rms_norm rows -------------------------------------------------------------
@@ -226,8 +224,7 @@ void or_rmsnorm(const float* x, const float* w, int rows, int n, float eps, floa
 }
 
 // ---- Q8_0 matmul: C[M][N] = A[M][K] . W[N][K]^T --------------------------------
-// mode 0: exact f32 activations x dequantised weights, double accumulation.
-// mode 1: f16(activation) x f16(f32(d) * q), double accumulation (CUDA path arithmetic).
+// mode 0: f32 activations x exactly dequantised weights, double accumulation (CUDA path).
 // mode 2: ggml CPU backend: Q8_0 activations, integer block dots, f32 block sum.
 void or_gemm_q8(const float* A, int M, int K, const uint8_t* W, int N, int mode, float* C) {
     const int nb = K / QK;
@@ -255,19 +252,13 @@ void or_gemm_q8(const float* A, int M, int K, const uint8_t* W, int N, int mode,
         }
         return;
     }
-    std::vector<float> Ar;
     const float* Ause = A;
-    if (mode == 1) {
-        Ar.resize((size_t)M * K);
-        for (size_t i = 0; i < (size_t)M * K; ++i) Ar[i] = round_f16(A[i]);
-        Ause = Ar.data();
-    }
 #pragma omp parallel
     {
         std::vector<float> w(K);
 #pragma omp for schedule(dynamic, 16)
         for (int n = 0; n < N; ++n) {
-            q8_row_dequant(W + (size_t)n * nb * QB, K, w.data(), mode == 1);
+            q8_row_dequant(W + (size_t)n * nb * QB, K, w.data());
             for (int m = 0; m < M; ++m) {
                 const float* a = Ause + (size_t)m * K;
                 double s[8] = {0, 0, 0, 0, 0, 0, 0, 0};

@@ -19,7 +19,7 @@ def max_abs(a, b) -> float:
 
 
 # The decoder-level tolerance: attention outputs and logits within 2e-2 max-abs and
-# 1e-3 relative RMS of the oracle run with the same arithmetic (GEMM mode 1).
+# 1e-3 relative RMS of the oracle run with the same arithmetic (exact GEMM mode).
 TOL_MAX_ABS = 2e-2
 TOL_REL_RMS = 1e-3
 

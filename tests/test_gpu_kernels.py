@@ -226,24 +226,37 @@ def test_repack_layout(torch_cuda):
     assert np.array_equal(d.cpu().numpy().view(np.uint16).T, blocks[:, :, :2].copy().view(np.uint16)[:, :, 0])
 
 
+def _split_f16(x):
+    """x = hi + lo as two f16 arrays (the form the GEMM reads); returns (hi, lo, hi + lo)."""
+    hi = oracle.f32_to_f16_bits(x)
+    lo = oracle.f32_to_f16_bits(x - oracle.f16_bits_to_f32(hi))
+    return hi, lo, oracle.f16_bits_to_f32(hi) + oracle.f16_bits_to_f32(lo)
+
+
 @pytest.mark.parametrize("M,N,K,split", [
     (1, 1024, 1024, 1), (5, 4096, 1024, 4), (16, 1024, 2048, 8), (17, 2048, 1024, 2),
     (64, 6144, 1024, 4), (128, 1024, 3072, 12), (200, 1024, 1024, 1), (300, 512, 2048, 2),
 ])
-def test_q8_gemm_matches_oracle_mode1(torch_cuda, M, N, K, split):
+def test_q8_gemm_matches_oracle_exact(torch_cuda, M, N, K, split):
     torch = torch_cuda
     rng = np.random.default_rng(M * 7 + N + K)
     raw, q, d = _q8_device(torch, rng, N, K)
-    a = rng.standard_normal((M, K)).astype(np.float32)
-    a16 = oracle.f32_to_f16_bits(a)
-    d_a = dev(torch, _i16(a16))
+    a = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    hi, lo, a_eff = _split_f16(a)
+    d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     c = torch.zeros((split, M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_a.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, split, c.data_ptr())
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, split, c.data_ptr())
     torch.cuda.synchronize()
     got = c.sum(0).cpu().numpy()
-    ref = oracle.gemm_q8(oracle.f16_bits_to_f32(a16), raw, N, oracle.MODE_F16)
+    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_EXACT)
     assert rel_rms(got, ref) < 2e-6, rel_rms(got, ref)
-    assert max_abs(got, ref) < 1e-4 * np.abs(ref).max()
+    assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
+    # without the lo plane the result is the f16-activation product
+    c.zero_()
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), 0, M, K, q.data_ptr(), d.data_ptr(), N, split, c.data_ptr())
+    torch.cuda.synchronize()
+    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, oracle.MODE_EXACT)
+    assert rel_rms(c.sum(0).cpu().numpy(), ref16) < 2e-6
 
 
 def test_lm_head_argmax_full_vocab(torch_cuda):
@@ -251,15 +264,15 @@ def test_lm_head_argmax_full_vocab(torch_cuda):
     rng = np.random.default_rng(3)
     M, N, K = 7, 151936, 1024
     raw, q, d = _q8_device(torch, rng, N, K)
-    a16 = oracle.f32_to_f16_bits(rng.standard_normal((M, K)).astype(np.float32))
-    d_a = dev(torch, _i16(a16))
+    hi, lo, a_eff = _split_f16(rng.standard_normal((M, K)).astype(np.float32))
+    d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
     nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
     logits = torch.zeros((M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, scratch.data_ptr(),
-                             nxt.data_ptr(), logits.data_ptr())
+    fa_dec.op_q8_gemm_argmax(d_hi.data_ptr(), d_lo.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N,
+                             scratch.data_ptr(), nxt.data_ptr(), logits.data_ptr())
     torch.cuda.synchronize()
-    ref = oracle.gemm_q8(oracle.f16_bits_to_f32(a16), raw, N, oracle.MODE_F16)
+    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_EXACT)
     assert rel_rms(logits.cpu().numpy(), ref) < 2e-6
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(ref))
     # the kernel's argmax is the first maximum of its own logits
@@ -272,9 +285,9 @@ def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2):
     M, N, K = 3, 151936, 1024
     nb = K // 32
     blocks = np.zeros((N, nb, 34), np.uint8)
-    small = np.float16(0.001).view(np.uint8)
+    small = np.array([0.001], np.float16).view(np.uint8)
     blocks[:, :, 0:2] = small
-    big = np.float16(0.02).view(np.uint8)
+    big = np.array([0.02], np.float16).view(np.uint8)
     for j in (j1, j2):
         blocks[j, :, 0:2] = big
         blocks[j, :, 2:] = np.uint8(127)
@@ -287,6 +300,7 @@ def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2):
     d_a = dev(torch, _i16(a16))
     scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
     nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
-    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, scratch.data_ptr(), nxt.data_ptr())
+    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), 0, M, K, q.data_ptr(), d.data_ptr(), N, scratch.data_ptr(),
+                             nxt.data_ptr())
     torch.cuda.synchronize()
     assert nxt.cpu().numpy().tolist() == [j1] * M

@@ -58,7 +58,7 @@ def _golden_decoder(mode):
     return h, cfg, w, od
 
 
-@pytest.mark.parametrize("mode,tol", [(oracle.MODE_EXACT, 1e-3), (oracle.MODE_F16, 3e-3)])
+@pytest.mark.parametrize("mode,tol", [(oracle.MODE_EXACT, 1e-3)])
 def test_decoder_logits_match_qwen3(mode, tol):
     h, cfg, w, od = _golden_decoder(mode)
     od.seq_open(0)
@@ -74,8 +74,8 @@ def test_decoder_logits_match_qwen3(mode, tol):
 
 
 def test_prefill_equals_stepwise():
-    h, cfg, w, od = _golden_decoder(oracle.MODE_F16)
-    od2 = oracle.OracleDecoder(cfg, w, n_pages=64, max_seqs=4, max_pages_per_seq=16, max_pos=4096, mode=oracle.MODE_F16)
+    h, cfg, w, od = _golden_decoder(oracle.MODE_EXACT)
+    od2 = oracle.OracleDecoder(cfg, w, n_pages=64, max_seqs=4, max_pages_per_seq=16, max_pos=4096, mode=oracle.MODE_EXACT)
     toks = np.random.default_rng(3).integers(0, cfg["vocab"], 21)
     od.seq_open(1)
     od2.seq_open(1)
