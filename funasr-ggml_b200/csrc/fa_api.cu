@@ -34,11 +34,12 @@ namespace {
 
 thread_local std::string g_err;
 
+// Q8_0 weights on the device: q as exact-integer f16 [N][K], d as f16 [K/32][N].
 struct LayerW {
-    int8_t* qkv_q = nullptr; __half* qkv_d = nullptr;
-    int8_t* o_q = nullptr;   __half* o_d = nullptr;
-    int8_t* gu_q = nullptr;  __half* gu_d = nullptr;
-    int8_t* dn_q = nullptr;  __half* dn_d = nullptr;
+    __half* qkv_q = nullptr; __half* qkv_d = nullptr;
+    __half* o_q = nullptr;   __half* o_d = nullptr;
+    __half* gu_q = nullptr;  __half* gu_d = nullptr;
+    __half* dn_q = nullptr;  __half* dn_d = nullptr;
     float* in_norm = nullptr;
     float* post_norm = nullptr;
     float* q_norm = nullptr;
@@ -66,6 +67,7 @@ bool g_configured[64] = {};
 namespace fa {
 void configure_attention();
 void configure_gemm();
+void configure_gemm_tc();
 }  // namespace fa
 
 static int ensure_configured() {
@@ -75,6 +77,7 @@ static int ensure_configured() {
     if (dev >= 0 && dev < 64 && !g_configured[dev]) {
         fa::configure_attention();
         fa::configure_gemm();
+        fa::configure_gemm_tc();
         g_configured[dev] = true;
     }
     return FA_OK;
@@ -93,7 +96,7 @@ struct fa_ctx {
     void* embed = nullptr;
     int embed_type = FA_TYPE_BF16;
     float* final_norm = nullptr;
-    int8_t* lm_q = nullptr;
+    __half* lm_q = nullptr;
     __half* lm_d = nullptr;
     std::vector<void*> dev_allocs;
 
@@ -140,6 +143,7 @@ struct fa_ctx {
     int* h_err = nullptr;
 
     bool use_graphs = true;
+    int gemm_variant = 0;      // 0: tcgen05 kernel, 1: mma.sync kernel
     std::map<uint64_t, cudaGraphExec_t> graphs;
 
     bool prof = false;
@@ -209,6 +213,8 @@ static int validate_desc(const fa_model_desc* d) {
     if (d->n_layers <= 0 || d->hidden <= 0 || d->hidden % 64 || d->ffn <= 0 || d->ffn % 64 || d->vocab <= 0 ||
         d->vocab % 64)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "n_layers > 0; hidden, ffn, vocab multiples of 64 required");
+    if (d->hidden > 4096)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "hidden above 4096 is not supported by the norm kernel");
     if (d->max_ctx <= 0 || d->max_seqs <= 0 || d->max_rows <= 0 || d->max_rows > 4096)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "max_ctx, max_seqs > 0 and 0 < max_rows <= 4096 required");
     if (!(d->rms_eps > 0.0f) || !(d->rope_base > 0.0f))
@@ -372,6 +378,14 @@ extern "C" int fa_set_stream(fa_ctx* ctx, void* stream) {
     return FA_OK;
 }
 
+extern "C" int fa_set_gemm_variant(fa_ctx* ctx, int variant) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (variant != 0 && variant != 1) return set_err(ctx, FA_ERR_INVALID_ARG, "variant must be 0 or 1");
+    ctx->gemm_variant = variant;
+    clear_graphs(ctx);
+    return FA_OK;
+}
+
 extern "C" int fa_set_graphs(fa_ctx* ctx, int enable) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     ctx->use_graphs = enable != 0;
@@ -445,10 +459,10 @@ static int upload_vec_f32(fa_ctx* ctx, const fa_tensor_view* v, float** dst) {
 }
 
 // Repack a GGUF Q8_0 tensor with N rows of K into (q, d) at row offset r0 (d has ldn columns).
-static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, int8_t* q,
+static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, __half* q,
                      __half* dsc, int ldn) {
     FA_CK(cudaMemcpyAsync(staging, v->data, v->nbytes, cudaMemcpyHostToDevice, ctx->stream));
-    fa::launch_repack_q8(staging, N, K, r0, 0, q, dsc, ldn, ctx->stream);
+    fa::launch_repack_q8(staging, N, K, r0, q, dsc, ldn, ctx->stream);
     FA_CK(cudaGetLastError());
     FA_CK(cudaStreamSynchronize(ctx->stream));
     return FA_OK;
@@ -506,10 +520,10 @@ extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n
             LayerW& w = ctx->L[l];
             LV& t = lv[l];
             int r;
-            if ((r = dev_alloc(ctx, &w.qkv_q, (size_t)QKV * H)) || (r = dev_alloc(ctx, &w.qkv_d, (size_t)QKV * (H / 32) * 2)) ||
-                (r = dev_alloc(ctx, &w.o_q, (size_t)H * QD)) || (r = dev_alloc(ctx, &w.o_d, (size_t)H * (QD / 32) * 2)) ||
-                (r = dev_alloc(ctx, &w.gu_q, (size_t)2 * F * H)) || (r = dev_alloc(ctx, &w.gu_d, (size_t)2 * F * (H / 32) * 2)) ||
-                (r = dev_alloc(ctx, &w.dn_q, (size_t)H * F)) || (r = dev_alloc(ctx, &w.dn_d, (size_t)H * (F / 32) * 2)))
+            if ((r = dev_alloc(ctx, &w.qkv_q, (size_t)QKV * H * 2)) || (r = dev_alloc(ctx, &w.qkv_d, (size_t)QKV * (H / 32) * 2)) ||
+                (r = dev_alloc(ctx, &w.o_q, (size_t)H * QD * 2)) || (r = dev_alloc(ctx, &w.o_d, (size_t)H * (QD / 32) * 2)) ||
+                (r = dev_alloc(ctx, &w.gu_q, (size_t)2 * F * H * 2)) || (r = dev_alloc(ctx, &w.gu_d, (size_t)2 * F * (H / 32) * 2)) ||
+                (r = dev_alloc(ctx, &w.dn_q, (size_t)H * F * 2)) || (r = dev_alloc(ctx, &w.dn_d, (size_t)H * (F / 32) * 2)))
                 return r;
             if ((r = upload_q8(ctx, t.q, staging, QD, H, 0, w.qkv_q, w.qkv_d, QKV)) ||
                 (r = upload_q8(ctx, t.k, staging, KD, H, QD, w.qkv_q, w.qkv_d, QKV)) ||
@@ -524,7 +538,7 @@ extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n
                 return r;
         }
         int r;
-        if ((r = dev_alloc(ctx, &ctx->lm_q, (size_t)V * H)) || (r = dev_alloc(ctx, &ctx->lm_d, (size_t)V * (H / 32) * 2)))
+        if ((r = dev_alloc(ctx, &ctx->lm_q, (size_t)V * H * 2)) || (r = dev_alloc(ctx, &ctx->lm_d, (size_t)V * (H / 32) * 2)))
             return r;
         if ((r = upload_q8(ctx, lm, staging, V, H, 0, ctx->lm_q, ctx->lm_d, V))) return r;
         if ((r = upload_vec_f32(ctx, fnorm, &ctx->final_norm))) return r;
@@ -724,6 +738,14 @@ static void record_prof(fa_ctx* ctx, int idx, bool capturing) {
     else cudaEventRecord(ctx->prof_ev[idx], ctx->stream);
 }
 
+// One Q8_0 GEMM launch on the selected implementation (tcgen05 unless the caller
+// chose the mma.sync cross-check variant or the shape is outside the tcgen05 kernel).
+static void run_gemm(fa_ctx* ctx, const fa::GemmArgs& g) {
+    if (ctx->gemm_variant == 0 && fa::gemm_tc_supported(g) && fa::launch_q8_gemm_tc(g, ctx->err_dev, ctx->stream))
+        return;
+    fa::launch_q8_gemm(g, ctx->stream);
+}
+
 // Enqueue the kernels of one forward step. Returns the number of launches.
 static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     const fa_model_desc& d = ctx->d;
@@ -742,9 +764,9 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         __half* pool_l = ctx->pool + (size_t)l * ctx->layer_stride;
         fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, w.in_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         fa::GemmArgs g{};
-        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wq = w.qkv_q; g.Wd = w.qkv_d; g.M = M; g.N = QKV; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wqh = w.qkv_q; g.Wd = w.qkv_d; g.M = M; g.N = QKV; g.K = H;
         g.n_split = p.s_qkv; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
-        fa::launch_q8_gemm(g, s);
+        run_gemm(ctx, g);
         fa::AppendArgs a{};
         a.qkv_part = ctx->part; a.n_part = p.s_qkv; a.M = M; a.pos = ctx->row_pos; a.slot = ctx->row_slot;
         a.block_table = ctx->bt_dev; a.bt_stride = ctx->bt_stride; a.n_pages = ctx->n_pages;
@@ -767,29 +789,29 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         }
         if (p.prof) record_prof(ctx, 2 * l + 1, capturing);
         g = fa::GemmArgs{};
-        g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.Wq = w.o_q; g.Wd = w.o_d; g.M = M; g.N = H; g.K = kHq * kD;
+        g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.Wqh = w.o_q; g.Wd = w.o_d; g.M = M; g.N = H; g.K = kHq * kD;
         g.n_split = p.s_o; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
-        fa::launch_q8_gemm(g, s);
+        run_gemm(ctx, g);
         fa::launch_residual_rmsnorm(ctx->x, ctx->part, p.s_o, M, H, w.post_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         g = fa::GemmArgs{};
-        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wq = w.gu_q; g.Wd = w.gu_d; g.M = M; g.N = 2 * F; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wqh = w.gu_q; g.Wd = w.gu_d; g.M = M; g.N = 2 * F; g.K = H;
         g.n_split = p.s_gu; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
-        fa::launch_q8_gemm(g, s);
+        run_gemm(ctx, g);
         fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s);
         g = fa::GemmArgs{};
-        g.A = ctx->h16; g.A_lo = ctx->h_lo; g.Wq = w.dn_q; g.Wd = w.dn_d; g.M = M; g.N = H; g.K = F;
+        g.A = ctx->h16; g.A_lo = ctx->h_lo; g.Wqh = w.dn_q; g.Wd = w.dn_d; g.M = M; g.N = H; g.K = F;
         g.n_split = p.s_dn; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
-        fa::launch_q8_gemm(g, s);
+        run_gemm(ctx, g);
         n += 8;
         prev_part = ctx->part;
         prev_n = p.s_dn;
     }
     fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
     fa::GemmArgs g{};
-    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wq = ctx->lm_q; g.Wd = ctx->lm_d; g.M = M; g.N = d.vocab; g.K = H;
+    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wqh = ctx->lm_q; g.Wd = ctx->lm_d; g.M = M; g.N = d.vocab; g.K = H;
     g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = p.logits ? ctx->logits_dev : nullptr;
     g.amax_val = ctx->amax_v; g.amax_idx = ctx->amax_i;
-    fa::launch_q8_gemm(g, s);
+    run_gemm(ctx, g);
     fa::launch_argmax_reduce(ctx->amax_v, ctx->amax_i, M, d.vocab / 64, ctx->next_dev, ctx->row_tok, ctx->row_pos, s);
     n += 3;
     return n;
@@ -1269,26 +1291,36 @@ extern "C" int fa_op_paged_attention(const float* q, int M, const int* pos, cons
     return FA_OK;
 }
 
-extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, int8_t* q, uint16_t* d, void* stream) {
+extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, uint16_t* q, uint16_t* d, void* stream) {
     if (!raw || !q || !d || N <= 0 || K <= 0 || K % 32) return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
-    fa::launch_repack_q8(raw, N, K, 0, 0, q, reinterpret_cast<__half*>(d), N, (cudaStream_t)stream);
+    fa::launch_repack_q8(raw, N, K, 0, reinterpret_cast<__half*>(q), reinterpret_cast<__half*>(d), N,
+                         (cudaStream_t)stream);
     OP_CK(cudaGetLastError());
     return FA_OK;
 }
 
-extern "C" int fa_op_q8_gemm(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const int8_t* q,
-                             const uint16_t* d, int N, int n_split, float* c, void* stream) {
+static int op_gemm(const fa::GemmArgs& g, int variant, cudaStream_t s) {
+    if (variant == 0) {
+        if (!fa::gemm_tc_supported(g)) return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the tcgen05 kernel");
+        if (!fa::launch_q8_gemm_tc(g, nullptr, s)) return set_err(nullptr, FA_ERR_CUDA, "tensor map encoding failed");
+    } else {
+        fa::launch_q8_gemm(g, s);
+    }
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_q8_gemm(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const uint16_t* q,
+                             const uint16_t* d, int N, int n_split, float* c, int variant, void* stream) {
     if (!a16 || !q || !d || !c || M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_split <= 0 ||
         (K / 64) % n_split)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "need N, K multiples of 64 and n_split dividing K/64");
     if (int rc = ensure_configured()) return rc;
     fa::GemmArgs g{};
-    g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo); g.Wq = q;
-    g.Wd = reinterpret_cast<const __half*>(d);
+    g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo);
+    g.Wqh = reinterpret_cast<const __half*>(q); g.Wd = reinterpret_cast<const __half*>(d);
     g.M = M; g.N = N; g.K = K; g.n_split = n_split; g.epilogue = fa::kEpiStoreF32; g.C = c;
-    fa::launch_q8_gemm(g, (cudaStream_t)stream);
-    OP_CK(cudaGetLastError());
-    return FA_OK;
+    return op_gemm(g, variant, (cudaStream_t)stream);
 }
 
 extern "C" size_t fa_op_argmax_scratch_bytes(int M, int N) {
@@ -1296,19 +1328,19 @@ extern "C" size_t fa_op_argmax_scratch_bytes(int M, int N) {
     return (size_t)M * (N / 64) * (sizeof(float) + sizeof(int));
 }
 
-extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const int8_t* q,
-                                    const uint16_t* d, int N, void* scratch, int* next, float* logits,
+extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const uint16_t* q,
+                                    const uint16_t* d, int N, void* scratch, int* next, float* logits, int variant,
                                     void* stream) {
     if (!a16 || !q || !d || !scratch || !next || M <= 0 || N % 64 || K % 64)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
     if (int rc = ensure_configured()) return rc;
     fa::GemmArgs g{};
-    g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo); g.Wq = q;
-    g.Wd = reinterpret_cast<const __half*>(d);
+    g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo);
+    g.Wqh = reinterpret_cast<const __half*>(q); g.Wd = reinterpret_cast<const __half*>(d);
     g.M = M; g.N = N; g.K = K; g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = logits;
     g.amax_val = reinterpret_cast<float*>(scratch);
     g.amax_idx = reinterpret_cast<int*>(g.amax_val + (size_t)M * (N / 64));
-    fa::launch_q8_gemm(g, (cudaStream_t)stream);
+    if (int rc = op_gemm(g, variant, (cudaStream_t)stream)) return rc;
     fa::launch_argmax_reduce(g.amax_val, g.amax_idx, M, N / 64, next, nullptr, nullptr, (cudaStream_t)stream);
     OP_CK(cudaGetLastError());
     return FA_OK;

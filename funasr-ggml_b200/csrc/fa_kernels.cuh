@@ -74,7 +74,7 @@ enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1 };
 struct GemmArgs {
     const __half* A;         // [M][K] f16 activations (hi part)
     const __half* A_lo;      // [M][K] f16 remainder x - hi, or nullptr (plain f16 activations)
-    const int8_t* Wq;        // [N][K] int8
+    const __half* Wqh;       // [N][K] Q8_0 integers q held exactly as f16
     const __half* Wd;        // [K/32][N] f16 block scales
     int M, N, K;
     int n_split;             // split-K factor (grid.z); K/n_split multiple of 64
@@ -83,8 +83,13 @@ struct GemmArgs {
     float* amax_val;         // kEpiArgmax: [M][N/64] per-tile row maxima
     int* amax_idx;           //             [M][N/64] first column holding them
 };
+// mma.sync (m16n8k16) implementation; the cross-check variant.
 void launch_q8_gemm(const GemmArgs& g, cudaStream_t s);
 int gemm_pick_split(int M, int N, int K, int n_sm);
+// tcgen05 / TMEM / TMA implementation (k_gemm_tc.cu); the default.
+bool gemm_tc_supported(const GemmArgs& g);
+bool launch_q8_gemm_tc(const GemmArgs& g, int* err, cudaStream_t s);
+size_t gemm_tc_smem_bytes();
 
 // ----------------------------------------------------------------- k_small.cu --
 void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds,
@@ -100,10 +105,10 @@ void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, 
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,
                           int* feed_pos, cudaStream_t s);
 void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* upd_page, int n, cudaStream_t s);
-// GGUF Q8_0 rows [N][K/32][34 B] -> q [N][K] + d [K/32][ldn]; rows land at dst row
-// (interleave == 0) r0 + n, or (interleave == 1/2: gate/up) (n/8)*16 + (interleave-1)*8 + n%8.
-void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, int interleave, int8_t* dst_q, __half* dst_d,
-                      int ldn, cudaStream_t s);
+// GGUF Q8_0 rows [N][K/32][34 B] -> q as exact f16 [N][K] + d [K/32][ldn], rows landing at
+// destination row r0 + n (Wq, Wk, Wv and gate, up are stacked that way).
+void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_q, __half* dst_d, int ldn,
+                      cudaStream_t s);
 void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,
                       cudaStream_t s);
 void launch_fill_random(__half* pool, size_t layer_stride, int n_layers, const int* pages, int n_pages_list,

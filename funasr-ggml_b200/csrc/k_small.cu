@@ -6,7 +6,7 @@
 //                      f16(rms_norm(x) * w) for the next GEMM (gpu_rms_norm, :16-25)
 //   swiglu           : f16(silu(gate) * up) from the gate/up GEMM partials (:177-180)
 //   argmax_reduce    : first maximum over lm_head tiles (compute/gpu_runner.hpp:108-118)
-//   repack_q8        : GGUF Q8_0 blocks -> int8 matrix + transposed f16 scales
+//   repack_q8        : GGUF Q8_0 blocks -> q as exact f16 matrix + transposed f16 scales
 //   page_copy / fill_random / read_pages / apply_bt_updates : page-pool maintenance
 #include "fa_kernels.cuh"
 
@@ -65,43 +65,87 @@ __device__ __forceinline__ void split_store(float y, __half* hi, __half* lo, siz
     if (lo) lo[i] = __float2half_rn(__fsub_rn(y, __half2float(h)));
 }
 
+// Sum of n_part split-K partials of one float4 column group, in partial order; the
+// loads of a group of 8 partials are all issued before the first add.
+__device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, int n_part) {
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < n_part; s0 += 8) {
+        float4 t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (s0 + u < n_part) t[u] = p[(size_t)(s0 + u) * stride4];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (s0 + u < n_part) {
+                o.x = __fadd_rn(o.x, t[u].x); o.y = __fadd_rn(o.y, t[u].y);
+                o.z = __fadd_rn(o.z, t[u].z); o.w = __fadd_rn(o.w, t[u].w);
+            }
+    }
+    return o;
+}
+
+// One CTA per row; thread t owns float4 groups t, t+256, ... (hidden <= 4096).
 __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const float* part, int n_part, int M,
                                                                int hidden, const float* w, float eps,
                                                                __half* xn_hi, __half* xn_lo) {
     __shared__ double sh[8];
     const int m = blockIdx.x;
-    float* xr = x + (size_t)m * hidden;
+    const int n4 = hidden / 4;
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)m * hidden);
+    float4 v[4];
     double ss = 0.0;
-    for (int i = threadIdx.x; i < hidden; i += 256) {
-        float v = xr[i];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const int i = threadIdx.x + 256 * c;
+        if (i >= n4) break;
+        float4 a = xr[i];
         if (n_part > 0) {
-            float o = 0.0f;
-            for (int s = 0; s < n_part; ++s) o = __fadd_rn(o, part[((size_t)s * M + m) * hidden + i]);
-            v = __fadd_rn(v, o);
-            xr[i] = v;
+            const float4 o = sum_parts4(reinterpret_cast<const float4*>(part) + (size_t)m * n4 + i,
+                                        (size_t)M * n4, n_part);
+            a.x = __fadd_rn(a.x, o.x); a.y = __fadd_rn(a.y, o.y);
+            a.z = __fadd_rn(a.z, o.z); a.w = __fadd_rn(a.w, o.w);
+            xr[i] = a;
         }
-        ss += (double)__fmul_rn(v, v);
+        v[c] = a;
+        ss += (double)__fmul_rn(a.x, a.x) + (double)__fmul_rn(a.y, a.y) + (double)__fmul_rn(a.z, a.z) +
+              (double)__fmul_rn(a.w, a.w);
     }
     ss = block_sum_double<256>(ss, sh);
     const float mean = (float)(ss / (double)hidden);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-    for (int i = threadIdx.x; i < hidden; i += 256)
-        split_store(__fmul_rn(__fmul_rn(xr[i], scale), w[i]), xn_hi, xn_lo, (size_t)m * hidden + i);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const int i = threadIdx.x + 256 * c;
+        if (i >= n4) break;
+        const float4 ww = reinterpret_cast<const float4*>(w)[i];
+        const size_t o = (size_t)m * hidden + 4 * (size_t)i;
+        split_store(__fmul_rn(__fmul_rn(v[c].x, scale), ww.x), xn_hi, xn_lo, o);
+        split_store(__fmul_rn(__fmul_rn(v[c].y, scale), ww.y), xn_hi, xn_lo, o + 1);
+        split_store(__fmul_rn(__fmul_rn(v[c].z, scale), ww.z), xn_hi, xn_lo, o + 2);
+        split_store(__fmul_rn(__fmul_rn(v[c].w, scale), ww.w), xn_hi, xn_lo, o + 3);
+    }
 }
 
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// Thread per float4 group of one row's ffn outputs.
 __global__ void __launch_bounds__(256) swiglu_kernel(const float* part, int n_part, int M, int ffn,
                                                      __half* h_hi, __half* h_lo) {
     const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
-    if (idx >= (size_t)M * ffn) return;
-    const int m = (int)(idx / ffn), j = (int)(idx % ffn);
-    float gs = 0.0f, us = 0.0f;
-    for (int s = 0; s < n_part; ++s) {
-        const float* row = part + ((size_t)s * M + m) * 2 * ffn;
-        gs = __fadd_rn(gs, row[j]);
-        us = __fadd_rn(us, row[ffn + j]);
-    }
-    const float sg = __fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs)));
-    split_store(__fmul_rn(sg, us), h_hi, h_lo, idx);
+    const int f4 = ffn / 4;
+    if (idx >= (size_t)M * f4) return;
+    const int m = (int)(idx / f4), j = (int)(idx % f4);
+    const float4* p = reinterpret_cast<const float4*>(part) + (size_t)m * 2 * f4;
+    const size_t stride4 = (size_t)M * 2 * f4;
+    const float4 g = sum_parts4(p + j, stride4, n_part);
+    const float4 u = sum_parts4(p + f4 + j, stride4, n_part);
+    const size_t o = (size_t)m * ffn + 4 * (size_t)j;
+    split_store(silu_mul(g.x, u.x), h_hi, h_lo, o);
+    split_store(silu_mul(g.y, u.y), h_hi, h_lo, o + 1);
+    split_store(silu_mul(g.z, u.z), h_hi, h_lo, o + 2);
+    split_store(silu_mul(g.w, u.w), h_hi, h_lo, o + 3);
 }
 
 __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float* val, const int* idx, int n_tiles,
@@ -141,21 +185,18 @@ __global__ void apply_bt_updates_kernel(int* bt, const int* upd_idx, const int* 
     if (i < n) bt[upd_idx[i]] = upd_page[i];
 }
 
-__global__ void repack_q8_kernel(const uint8_t* raw, int N, int K, int r0, int interleave, int8_t* dst_q,
-                                 __half* dst_d, int ldn) {
+__global__ void repack_q8_kernel(const uint8_t* raw, int N, int K, int r0, __half* dst_q, __half* dst_d, int ldn) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int nb = K / kQK;
     if (i >= (size_t)N * nb) return;
     const int n = (int)(i / nb), b = (int)(i % nb);
     const uint8_t* blk = raw + i * kQBytes;
     const uint16_t dbits = (uint16_t)blk[0] | ((uint16_t)blk[1] << 8);
-    int row;
-    if (interleave == 0) row = r0 + n;
-    else row = (n / 8) * 16 + (interleave - 1) * 8 + n % 8;
+    const int row = r0 + n;
     dst_d[(size_t)b * ldn + row] = __ushort_as_half(dbits);
-    int8_t* q = dst_q + (size_t)row * K + (size_t)b * kQK;
+    __half* q = dst_q + (size_t)row * K + (size_t)b * kQK;
 #pragma unroll
-    for (int j = 0; j < kQK; ++j) q[j] = (int8_t)blk[2 + j];
+    for (int j = 0; j < kQK; ++j) q[j] = __int2half_rn((int)(int8_t)blk[2 + j]);
 }
 
 __global__ void __launch_bounds__(256) page_copy_kernel(__half* pool, size_t layer_stride, const int* src,
@@ -209,7 +250,7 @@ void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int
 }
 
 void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s) {
-    const size_t n = (size_t)M * ffn;
+    const size_t n = (size_t)M * (ffn / 4);
     swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, n_part, M, ffn, h_hi, h_lo);
 }
 
@@ -223,10 +264,10 @@ void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* up
     apply_bt_updates_kernel<<<(n + 255) / 256, 256, 0, s>>>(block_table, upd_idx, upd_page, n);
 }
 
-void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, int interleave, int8_t* dst_q, __half* dst_d,
-                      int ldn, cudaStream_t s) {
+void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_q, __half* dst_d, int ldn,
+                      cudaStream_t s) {
     const size_t n = (size_t)N * (K / kQK);
-    repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, N, K, r0, interleave, dst_q, dst_d, ldn);
+    repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, N, K, r0, dst_q, dst_d, ldn);
 }
 
 void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,

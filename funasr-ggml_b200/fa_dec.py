@@ -82,6 +82,7 @@ def lib():
         "fa_load_weights": ([_P, ctypes.POINTER(_TensorView), _I], _I),
         "fa_set_stream": ([_P, _P], _I),
         "fa_set_graphs": ([_P, _I], _I),
+        "fa_set_gemm_variant": ([_P, _I], _I),
         "fa_pool_info": ([_P, _P, _P, _P], _I),
         "fa_seq_open": ([_P, _I, _P], _I),
         "fa_seq_close": ([_P, _I], _I),
@@ -104,9 +105,9 @@ def lib():
         "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
         "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P, _P], _I),
-        "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _P, _I, _I, _P, _P], _I),
+        "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _P, _I, _I, _P, _I, _P], _I),
         "fa_op_argmax_scratch_bytes": ([_I, _I], ctypes.c_size_t),
-        "fa_op_q8_gemm_argmax": ([_P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _P], _I),
+        "fa_op_q8_gemm_argmax": ([_P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _I, _P], _I),
         "fa_palloc_create": ([_I], _P),
         "fa_palloc_destroy": ([_P], None),
         "fa_palloc_alloc": ([_P], _I),
@@ -204,6 +205,10 @@ class Decoder:
 
     def set_stream(self, stream_ptr: Optional[int]):
         self._c(lib().fa_set_stream(self.ctx, stream_ptr))
+
+    def set_gemm_variant(self, variant: int):
+        """0: tcgen05 GEMM (default), 1: mma.sync GEMM (cross-check)."""
+        self._c(lib().fa_set_gemm_variant(self.ctx, int(variant)))
 
     def set_graphs(self, enable: bool):
         self._c(lib().fa_set_graphs(self.ctx, int(enable)))
@@ -334,16 +339,16 @@ def op_repack_q8(raw, N, K, q, d, stream=0):
     _check(lib().fa_op_repack_q8(raw, N, K, q, d, stream or None))
 
 
-def op_q8_gemm(a16, a16_lo, M, K, q, d, N, n_split, c, stream=0):
-    _check(lib().fa_op_q8_gemm(a16, a16_lo or None, M, K, q, d, N, n_split, c, stream or None))
+def op_q8_gemm(a16, a16_lo, M, K, q, d, N, n_split, c, variant=0, stream=0):
+    _check(lib().fa_op_q8_gemm(a16, a16_lo or None, M, K, q, d, N, n_split, c, variant, stream or None))
 
 
 def op_argmax_scratch_bytes(M, N) -> int:
     return int(lib().fa_op_argmax_scratch_bytes(M, N))
 
 
-def op_q8_gemm_argmax(a16, a16_lo, M, K, q, d, N, scratch, nxt, logits=0, stream=0):
-    _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, q, d, N, scratch, nxt, logits or None,
+def op_q8_gemm_argmax(a16, a16_lo, M, K, q, d, N, scratch, nxt, logits=0, variant=0, stream=0):
+    _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, q, d, N, scratch, nxt, logits or None, variant,
                                       stream or None))
 
 

@@ -38,9 +38,14 @@ def q8_0_random(rng: np.random.Generator, n: int, k: int, d_lo=0.001, d_hi=0.02)
     return blocks.reshape(n, nb * 34)
 
 
-def make_weights(cfg: dict, seed: int = 0) -> Dict[str, Tuple[int, Tuple[int, int], np.ndarray]]:
-    """name -> (ggml type, ne (input dim first), data) for one random-init decoder."""
+def make_weights(cfg: dict, seed: int = 0, d_range=(0.001, 0.02)) -> Dict[str, Tuple[int, Tuple[int, int], np.ndarray]]:
+    """name -> (ggml type, ne (input dim first), data) for one random-init decoder.
+
+    d_range is the range of the Q8_0 block scales. The default (0.001, 0.02) is the
+    steady-state benchmark's; it gives logits of order +-150. (0.0002, 0.004) gives the
+    +-25 logits of a trained Qwen3."""
     rng = np.random.default_rng(seed)
+    lo, hi = d_range
     H, F, V = cfg["hidden"], cfg["ffn"], cfg["vocab"]
     QD = cfg["n_heads"] * cfg["head_dim"]
     KD = cfg["n_kv_heads"] * cfg["head_dim"]
@@ -53,16 +58,16 @@ def make_weights(cfg: dict, seed: int = 0) -> Dict[str, Tuple[int, Tuple[int, in
     w["llm.model.embed_tokens.weight"] = (TYPE_BF16, (H, V), f32_to_bf16_bits(
         (rng.standard_normal((V, H), dtype=np.float32) * 0.05)))
     w["llm.model.norm.weight"] = (TYPE_BF16, (H, 1), bf16(H, 0.8, 1.2))
-    w["llm.lm_head.weight"] = (TYPE_Q8_0, (H, V), q8_0_random(rng, V, H))
+    w["llm.lm_head.weight"] = (TYPE_Q8_0, (H, V), q8_0_random(rng, V, H, lo, hi))
     for i in range(cfg["n_layers"]):
         p = f"llm.model.layers.{i}."
-        w[p + "self_attn.q_proj.weight"] = (TYPE_Q8_0, (H, QD), q8_0_random(rng, QD, H))
-        w[p + "self_attn.k_proj.weight"] = (TYPE_Q8_0, (H, KD), q8_0_random(rng, KD, H))
-        w[p + "self_attn.v_proj.weight"] = (TYPE_Q8_0, (H, KD), q8_0_random(rng, KD, H))
-        w[p + "self_attn.o_proj.weight"] = (TYPE_Q8_0, (QD, H), q8_0_random(rng, H, QD))
-        w[p + "mlp.gate_proj.weight"] = (TYPE_Q8_0, (H, F), q8_0_random(rng, F, H))
-        w[p + "mlp.up_proj.weight"] = (TYPE_Q8_0, (H, F), q8_0_random(rng, F, H))
-        w[p + "mlp.down_proj.weight"] = (TYPE_Q8_0, (F, H), q8_0_random(rng, H, F))
+        w[p + "self_attn.q_proj.weight"] = (TYPE_Q8_0, (H, QD), q8_0_random(rng, QD, H, lo, hi))
+        w[p + "self_attn.k_proj.weight"] = (TYPE_Q8_0, (H, KD), q8_0_random(rng, KD, H, lo, hi))
+        w[p + "self_attn.v_proj.weight"] = (TYPE_Q8_0, (H, KD), q8_0_random(rng, KD, H, lo, hi))
+        w[p + "self_attn.o_proj.weight"] = (TYPE_Q8_0, (QD, H), q8_0_random(rng, H, QD, lo, hi))
+        w[p + "mlp.gate_proj.weight"] = (TYPE_Q8_0, (H, F), q8_0_random(rng, F, H, lo, hi))
+        w[p + "mlp.up_proj.weight"] = (TYPE_Q8_0, (H, F), q8_0_random(rng, F, H, lo, hi))
+        w[p + "mlp.down_proj.weight"] = (TYPE_Q8_0, (F, H), q8_0_random(rng, H, F, lo, hi))
         w[p + "self_attn.q_norm.weight"] = (TYPE_BF16, (D, 1), bf16(D, 0.8, 1.2))
         w[p + "self_attn.k_norm.weight"] = (TYPE_BF16, (D, 1), bf16(D, 0.8, 1.2))
         w[p + "input_layernorm.weight"] = (TYPE_BF16, (H, 1), bf16(H, 0.8, 1.2))

@@ -44,7 +44,7 @@ def test_no_cpu_fallback_without_gpu():
 
 def test_op_entry_points_validate_arguments():
     with pytest.raises(fa_dec.FaError):
-        fa_dec.op_q8_gemm(0, 0, 4, 100, 0, 0, 64, 1, 0)
+        fa_dec.op_q8_gemm(0, 0, 4, 100, 0, 0, 64, 1, 0, 0)
     assert fa_dec.op_attention_scratch_bytes(128, 1) == 0
     assert fa_dec.op_attention_scratch_bytes(128, 4) == 128 * 16 * 4 * 130 * 4
 
