@@ -677,7 +677,8 @@ struct StepPlan {
     bool prof = false;
     uint64_t key() const {
         return (uint64_t)M | ((uint64_t)n_splits << 13) | ((uint64_t)pps << 25) | ((uint64_t)embeds << 33) |
-               ((uint64_t)logits << 34) | ((uint64_t)prof << 35);
+               ((uint64_t)logits << 34) | ((uint64_t)prof << 35) | ((uint64_t)s_qkv << 36) | ((uint64_t)s_o << 42) |
+               ((uint64_t)s_gu << 48) | ((uint64_t)s_dn << 54);
     }
 };
 
@@ -687,10 +688,14 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     const fa_model_desc& d = ctx->d;
     StepPlan p;
     p.M = M;
-    p.s_qkv = fa::gemm_pick_split(M, (kHq + 2 * kHkv) * kD, d.hidden, ctx->n_sm);
-    p.s_o = fa::gemm_pick_split(M, d.hidden, kHq * kD, ctx->n_sm);
-    p.s_gu = fa::gemm_pick_split(M, 2 * d.ffn, d.hidden, ctx->n_sm);
-    p.s_dn = fa::gemm_pick_split(M, d.hidden, d.ffn, ctx->n_sm);
+    auto pick = [&](int n, int k) {
+        return ctx->gemm_variant == 0 && n % 128 == 0 ? fa::gemm_tc_pick_split(M, n, k, ctx->n_sm)
+                                                       : fa::gemm_pick_split(M, n, k, ctx->n_sm);
+    };
+    p.s_qkv = pick((kHq + 2 * kHkv) * kD, d.hidden);
+    p.s_o = pick(d.hidden, kHq * kD);
+    p.s_gu = pick(2 * d.ffn, d.hidden);
+    p.s_dn = pick(d.hidden, d.ffn);
     long long total_pages = 0;
     int max_pages = 1;
     for (int n : row_len) {

@@ -88,6 +88,7 @@ void launch_q8_gemm(const GemmArgs& g, cudaStream_t s);
 int gemm_pick_split(int M, int N, int K, int n_sm);
 // tcgen05 / TMEM / TMA implementation (k_gemm_tc.cu); the default.
 bool gemm_tc_supported(const GemmArgs& g);
+int gemm_tc_pick_split(int M, int N, int K, int n_sm);
 bool launch_q8_gemm_tc(const GemmArgs& g, int* err, cudaStream_t s);
 size_t gemm_tc_smem_bytes();
 

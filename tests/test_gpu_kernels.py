@@ -228,10 +228,10 @@ def test_repack_layout(torch_cuda):
 
 
 def test_tcgen05_gemm_single_tile(torch_cuda):
-    """One CTA (128 x 64 tile, K = 64) of the tcgen05 kernel: the smallest case."""
+    """One CTA (128 x 128 tile, K = 64) of the tcgen05 kernel: the smallest case."""
     torch = torch_cuda
     rng = np.random.default_rng(42)
-    M, N, K = 128, 64, 64
+    M, N, K = 128, 128, 64
     raw, q, d = _q8_device(torch, rng, N, K)
     a = rng.standard_normal((M, K)).astype(np.float32)
     hi, lo, a_eff = _split_f16(a)
