@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--no-pdl", action="store_true", help="plain stream order between kernels")
     return ap.parse_args()
 
 
@@ -157,6 +158,8 @@ def run_ours(a):
     dec = fa_dec.Decoder(local, **fa_synth.decoder_desc(cfg, max_ctx=max_ctx, n_pages=B * pages_per_seq + 16,
                                                         max_seqs=B, max_rows=B))
     dec.load_weights(w)
+    if a.no_pdl:
+        dec.set_pdl(False)
     sids = [dec.seq_open(max_ctx) for _ in range(B)]
     for i, s in enumerate(sids):
         dec.kv_fill_synthetic(s, ctx, seed=rank * 100003 + i)

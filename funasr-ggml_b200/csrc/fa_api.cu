@@ -63,6 +63,14 @@ bool g_configured[64] = {};
 
 }  // namespace
 
+namespace fa {
+namespace {
+thread_local bool t_launch_pdl = false;
+}
+bool launch_pdl_enabled() { return t_launch_pdl; }
+void set_launch_pdl(bool on) { t_launch_pdl = on; }
+}  // namespace fa
+
 // Kernel attribute set-up, once per device (before any graph capture).
 namespace fa {
 void configure_attention();
@@ -143,6 +151,7 @@ struct fa_ctx {
     int* h_err = nullptr;
 
     bool use_graphs = true;
+    bool use_pdl = true;       // programmatic dependent launch between the step's kernels
     int gemm_variant = 0;      // 0: tcgen05 kernel, 1: mma.sync kernel
     std::map<uint64_t, cudaGraphExec_t> graphs;
 
@@ -389,6 +398,13 @@ extern "C" int fa_set_gemm_variant(fa_ctx* ctx, int variant) {
 extern "C" int fa_set_graphs(fa_ctx* ctx, int enable) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     ctx->use_graphs = enable != 0;
+    return FA_OK;
+}
+
+extern "C" int fa_set_pdl(fa_ctx* ctx, int enable) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    ctx->use_pdl = enable != 0;
+    clear_graphs(ctx);
     return FA_OK;
 }
 
@@ -785,14 +801,15 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         at.Hkv = kHkv; at.pages_per_split = p.pps; at.n_splits = p.n_splits; at.part_o = ctx->att_po;
         at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out16_lo = ctx->attn_lo; at.out32 = nullptr;
         at.err = ctx->err_dev;
-        if (p.prof) record_prof(ctx, 2 * l, capturing);
+        const bool prof_l = p.prof && (l == 0 || l == d.n_layers / 2 || l == d.n_layers - 1);
+        if (prof_l) record_prof(ctx, 2 * l, capturing);
         fa::launch_paged_attention(at, s);
         ++n;
         if (p.n_splits > 1) {
             fa::launch_attn_combine(at, s);
             ++n;
         }
-        if (p.prof) record_prof(ctx, 2 * l + 1, capturing);
+        if (prof_l) record_prof(ctx, 2 * l + 1, capturing);
         g = fa::GemmArgs{};
         g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.Wqh = w.o_q; g.Wd = w.o_d; g.M = M; g.N = H; g.K = kHq * kD;
         g.n_split = p.s_o; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
@@ -822,11 +839,19 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     return n;
 }
 
+// enqueue_step with programmatic dependent launch between its kernels when enabled
+static int enqueue_step_pdl(fa_ctx* ctx, const StepPlan& p, bool capturing) {
+    fa::set_launch_pdl(ctx->use_pdl);
+    const int n = enqueue_step(ctx, p, capturing);
+    fa::set_launch_pdl(false);
+    return n;
+}
+
 static int run_step(fa_ctx* ctx, const StepPlan& p) {
     if (p.prof)
         if (int rc = ensure_prof_events(ctx)) return rc;
     if (!ctx->use_graphs) {
-        ctx->last_launches = enqueue_step(ctx, p, false);
+        ctx->last_launches = enqueue_step_pdl(ctx, p, false);
         FA_CK(cudaGetLastError());
         ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
         return FA_OK;
@@ -834,7 +859,7 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
     auto it = ctx->graphs.find(p.key());
     if (it == ctx->graphs.end()) {
         FA_CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
-        const int n = enqueue_step(ctx, p, true);
+        const int n = enqueue_step_pdl(ctx, p, true);
         cudaGraph_t graph = nullptr;
         cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
         if (e != cudaSuccess) {
@@ -1215,13 +1240,20 @@ extern "C" int fa_profile_attention(fa_ctx* ctx, float* total_ms, int* n_launche
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     FA_CK(cudaStreamSynchronize(ctx->stream));
     float tot = 0.0f;
-    for (int l = 0; l < ctx->prof_n; ++l) {
-        float ms = 0.0f;
-        FA_CK(cudaEventElapsedTime(&ms, ctx->prof_ev[2 * l], ctx->prof_ev[2 * l + 1]));
-        tot += ms;
+    int n = 0;
+    if (ctx->prof_n > 0) {
+        const int L = ctx->d.n_layers;
+        const int layers[3] = {0, L / 2, L - 1};
+        for (int i = 0; i < 3; ++i) {
+            if (i > 0 && layers[i] == layers[i - 1]) continue;
+            float ms = 0.0f;
+            FA_CK(cudaEventElapsedTime(&ms, ctx->prof_ev[2 * layers[i]], ctx->prof_ev[2 * layers[i] + 1]));
+            tot += ms;
+            ++n;
+        }
     }
     if (total_ms) *total_ms = tot;
-    if (n_launches) *n_launches = ctx->prof_n;
+    if (n_launches) *n_launches = n;
     return FA_OK;
 }
 

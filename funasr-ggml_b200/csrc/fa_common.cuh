@@ -9,7 +9,8 @@
 //   block table    : int32 [seq_slot][page_index]; token p of slot s sits in page
 //                    block_table[s][p / 16] at in-page token p % 16.
 //   Q8_0 weights   : repacked at load time from GGUF blocks ([f16 d][32 x int8]) into
-//                    q int8 [N][K] (row-major, 16 B aligned) and d f16 [K/32][N].
+//                    q [N][K] (the int8 values held exactly as f16, row-major, TMA-able)
+//                    and d f16 [K/32][N] (the scales of one K block contiguous over N).
 //   RoPE table     : float2 [pos][head_dim/2] = (cos, sin), computed on the host in double.
 #pragma once
 
@@ -17,6 +18,7 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cstdint>
+#include <utility>
 
 namespace fa {
 
@@ -118,6 +120,35 @@ __device__ __forceinline__ void cp_async_wait() {
 
 __device__ __forceinline__ void record_error(int* err, int code) {
     if (err) atomicOr(err, code);
+}
+
+// Programmatic dependent launch. pdl_trigger lets the next kernel of the stream
+// start its prologue once every CTA of this one has started; pdl_wait blocks
+// until the previous kernel has completed and its writes are visible. Both are
+// no-ops for a kernel launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Host: launches of the decode-step kernels go through launch_k, which adds the
+// programmatic-serialization attribute while launch_pdl_enabled() is set (the
+// step enqueue sets it for its own launches; everything else launches plainly).
+bool launch_pdl_enabled();
+void set_launch_pdl(bool on);
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = launch_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 }  // namespace fa

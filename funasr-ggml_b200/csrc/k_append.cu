@@ -26,6 +26,8 @@ namespace {
 constexpr int D = 128;
 
 __global__ void __launch_bounds__(256) qknorm_rope_append_kernel(AppendArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(256) kv_append_raw_kernel(RawAppendArgs a) {
 void launch_qknorm_rope_append(const AppendArgs& a, cudaStream_t s) {
     const int n_vec = a.Hq + 2 * a.Hkv;
     dim3 grid(a.M, (n_vec + 7) / 8);
-    qknorm_rope_append_kernel<<<grid, 256, 0, s>>>(a);
+    launch_k(qknorm_rope_append_kernel, grid, dim3(256), 0, s, a);
 }
 
 void launch_kv_append_raw(const RawAppendArgs& a, cudaStream_t s) {

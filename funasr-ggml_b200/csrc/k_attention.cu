@@ -105,6 +105,8 @@ __global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
     const int m = blockIdx.z;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();
 
     const int n_kv = a.pos[m] + 1;
     const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
@@ -315,6 +317,8 @@ __global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
 }
 
 __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x / a.Hq;
     const int H = blockIdx.x % a.Hq;
     const int d = threadIdx.x;
@@ -347,11 +351,11 @@ void configure_attention() {
 
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s) {
     dim3 grid(a.n_splits, a.Hkv, a.M);
-    paged_attn_kernel<<<grid, 128, sizeof(AttnSmem), s>>>(a);
+    launch_k(paged_attn_kernel, grid, dim3(128), sizeof(AttnSmem), s, a);
 }
 
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s) {
-    attn_combine_kernel<<<a.M * a.Hq, 128, 0, s>>>(a);
+    launch_k(attn_combine_kernel, dim3(a.M * a.Hq), dim3(128), 0, s, a);
 }
 
 }  // namespace fa

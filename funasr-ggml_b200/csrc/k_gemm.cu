@@ -72,6 +72,8 @@ template <int BM, int WM, int WN>
 __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const GemmArgs g) {
     using C = Cfg<BM, WM, WN>;
     extern __shared__ __align__(128) unsigned char smem[];
+    pdl_trigger();
+    pdl_wait();
     // A stage st: hi tile at As + (2*st) * A_STAGE, lo tile right after it
     __half* As = reinterpret_cast<__half*>(smem);
     unsigned char* Qs = smem + (size_t)STAGES * 2 * C::A_STAGE * 2;
@@ -262,7 +264,7 @@ template <int BM, int WM, int WN>
 void launch_cfg(const GemmArgs& g, cudaStream_t s) {
     using C = Cfg<BM, WM, WN>;
     dim3 grid(g.N / BN, (g.M + BM - 1) / BM, g.n_split);
-    q8_gemm_kernel<BM, WM, WN><<<grid, C::THREADS, C::SMEM, s>>>(g);
+    launch_k(q8_gemm_kernel<BM, WM, WN>, grid, dim3(C::THREADS), C::SMEM, s, g);
 }
 
 template <int BM, int WM, int WN>

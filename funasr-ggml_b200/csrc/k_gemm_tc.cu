@@ -180,28 +180,53 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = S.tmem_base;
+    pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {
             const uint32_t bytes = A_BYTES * (g.has_lo ? 2 : 1) + B_BYTES + SC_BYTES;
-            int it = 0;
+            int my_units = 0;
+            for (int u = blockIdx.x; u < g.n_units; u += gridDim.x) ++my_units;
+            const int total = my_units * n_iters;
+            auto coords = [&](int it, int& k, int& m0, int& n0) {
+                const Unit w = unit_of(g, blockIdx.x + (it / n_iters) * gridDim.x);
+                k = w.k_begin + (it % n_iters) * BK;
+                m0 = w.m0;
+                n0 = w.n0;
+            };
+            // The weights and scales do not depend on the previous kernel: the first
+            // stages' copies go out before waiting for it; the activations after.
+            const int pre = total < STAGES ? total : STAGES;
+            for (int it = 0; it < pre; ++it) {
+                int k, m0, n0;
+                coords(it, k, m0, n0);
+                mbar_arrive_expect_tx(&S.full[it], bytes);
+                tma_load_2d(S.b[it], &tm_b, k, n0, &S.full[it]);
+                tma_load_2d(S.scale[it], &tm_sc, n0, k / kQK, &S.full[it]);
+            }
+            pdl_wait();
+            for (int it = 0; it < pre; ++it) {
+                int k, m0, n0;
+                coords(it, k, m0, n0);
+                tma_load_2d(S.a_hi[it], &tm_a_hi, k, m0, &S.full[it]);
+                if (g.has_lo) tma_load_2d(S.a_lo[it], &tm_a_lo, k, m0, &S.full[it]);
+            }
+            S.issued = pre;
             bool ok = true;
-            for (int u = blockIdx.x; u < g.n_units && ok; u += gridDim.x) {
-                const Unit w = unit_of(g, u);
-                for (int i = 0; i < n_iters; ++i, ++it) {
-                    const int s = it % STAGES;
-                    if (it >= STAGES && !mbar_wait_bounded(&S.empty[s], (uint32_t)((it / STAGES) & 1) ^ 1u)) {
-                        ok = false;
-                        break;
-                    }
-                    const int k = w.k_begin + i * BK;
-                    mbar_arrive_expect_tx(&S.full[s], bytes);
-                    tma_load_2d(S.a_hi[s], &tm_a_hi, k, w.m0, &S.full[s]);
-                    if (g.has_lo) tma_load_2d(S.a_lo[s], &tm_a_lo, k, w.m0, &S.full[s]);
-                    tma_load_2d(S.b[s], &tm_b, k, w.n0, &S.full[s]);
-                    tma_load_2d(S.scale[s], &tm_sc, w.n0, k / kQK, &S.full[s]);
-                    S.issued = it + 1;
+            for (int it = pre; it < total; ++it) {
+                const int s = it % STAGES;
+                if (!mbar_wait_bounded(&S.empty[s], (uint32_t)((it / STAGES) & 1) ^ 1u)) {
+                    ok = false;
+                    break;
                 }
+                int k, m0, n0;
+                coords(it, k, m0, n0);
+                mbar_arrive_expect_tx(&S.full[s], bytes);
+                tma_load_2d(S.a_hi[s], &tm_a_hi, k, m0, &S.full[s]);
+                if (g.has_lo) tma_load_2d(S.a_lo[s], &tm_a_lo, k, m0, &S.full[s]);
+                tma_load_2d(S.b[s], &tm_b, k, n0, &S.full[s]);
+                tma_load_2d(S.scale[s], &tm_sc, n0, k / kQK, &S.full[s]);
+                S.issued = it + 1;
             }
             if (!ok) S.err = 1;
         }
@@ -404,7 +429,7 @@ bool launch_q8_gemm_tc(const GemmArgs& g, int* err, cudaStream_t s) {
     a.C = g.C; a.amax_val = g.amax_val; a.amax_idx = g.amax_idx; a.err = err;
     const int sms = (dev >= 0 && dev < 64 && n_sm[dev] > 0) ? n_sm[dev] : 148;
     const int grid = a.n_units < sms ? a.n_units : sms;
-    q8_gemm_tc_kernel<<<grid, THREADS, gemm_tc_smem_bytes(), s>>>(ta, tl, tb, tsc, a);
+    launch_k(q8_gemm_tc_kernel, dim3(grid), dim3(THREADS), gemm_tc_smem_bytes(), s, ta, tl, tb, tsc, a);
     return true;
 }
 

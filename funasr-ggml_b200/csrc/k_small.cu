@@ -37,6 +37,8 @@ __device__ __forceinline__ double block_sum_double(double v, double* sh) {
 __global__ void __launch_bounds__(256) embed_kernel(const void* table, int table_type, int hidden,
                                                     const int* tokens, const float* embeds, int vocab,
                                                     float* x, int* err) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     float* dst = x + (size_t)m * hidden;
     if (embeds) {
@@ -89,6 +91,8 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const f
                                                                int hidden, const float* w, float eps,
                                                                __half* xn_hi, __half* xn_lo) {
     __shared__ double sh[8];
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const int n4 = hidden / 4;
     float4* xr = reinterpret_cast<float4*>(x + (size_t)m * hidden);
@@ -133,6 +137,8 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // Thread per float4 group of one row's ffn outputs.
 __global__ void __launch_bounds__(256) swiglu_kernel(const float* part, int n_part, int M, int ffn,
                                                      __half* h_hi, __half* h_lo) {
+    pdl_trigger();
+    pdl_wait();
     const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
     const int f4 = ffn / 4;
     if (idx >= (size_t)M * f4) return;
@@ -152,6 +158,8 @@ __global__ void __launch_bounds__(256) argmax_reduce_kernel(const float* val, co
                                                             int* next, int* feed_tokens, int* feed_pos) {
     __shared__ float sv[8];
     __shared__ int si[8];
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -241,22 +249,22 @@ __global__ void __launch_bounds__(256) read_pages_kernel(const __half* pool_laye
 
 void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds, int M,
                   int vocab, float* x, int* err, cudaStream_t s) {
-    embed_kernel<<<M, 256, 0, s>>>(table, table_type, hidden, tokens, embeds, vocab, x, err);
+    launch_k(embed_kernel, dim3(M), dim3(256), 0, s, table, table_type, hidden, tokens, embeds, vocab, x, err);
 }
 
 void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w, float eps,
                              __half* xn_hi, __half* xn_lo, cudaStream_t s) {
-    residual_rmsnorm_kernel<<<M, 256, 0, s>>>(x, part, n_part, M, hidden, w, eps, xn_hi, xn_lo);
+    launch_k(residual_rmsnorm_kernel, dim3(M), dim3(256), 0, s, x, part, n_part, M, hidden, w, eps, xn_hi, xn_lo);
 }
 
 void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s) {
     const size_t n = (size_t)M * (ffn / 4);
-    swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, n_part, M, ffn, h_hi, h_lo);
+    launch_k(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part, n_part, M, ffn, h_hi, h_lo);
 }
 
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,
                           int* feed_pos, cudaStream_t s) {
-    argmax_reduce_kernel<<<M, 256, 0, s>>>(val, idx, n_tiles, next, feed_tokens, feed_pos);
+    launch_k(argmax_reduce_kernel, dim3(M), dim3(256), 0, s, val, idx, n_tiles, next, feed_tokens, feed_pos);
 }
 
 void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* upd_page, int n, cudaStream_t s) {

@@ -83,6 +83,7 @@ def lib():
         "fa_set_stream": ([_P, _P], _I),
         "fa_set_graphs": ([_P, _I], _I),
         "fa_set_gemm_variant": ([_P, _I], _I),
+        "fa_set_pdl": ([_P, _I], _I),
         "fa_pool_info": ([_P, _P, _P, _P], _I),
         "fa_seq_open": ([_P, _I, _P], _I),
         "fa_seq_close": ([_P, _I], _I),
@@ -209,6 +210,9 @@ class Decoder:
     def set_gemm_variant(self, variant: int):
         """0: tcgen05 GEMM (default), 1: mma.sync GEMM (cross-check)."""
         self._c(lib().fa_set_gemm_variant(self.ctx, int(variant)))
+
+    def set_pdl(self, enable: bool):
+        self._c(lib().fa_set_pdl(self.ctx, int(enable)))
 
     def set_graphs(self, enable: bool):
         self._c(lib().fa_set_graphs(self.ctx, int(enable)))

@@ -103,6 +103,9 @@ FA_API int fa_set_stream(fa_ctx* ctx, void* cuda_stream);
 /* GEMM implementation: 0 = tcgen05/TMEM/TMA kernel (default), 1 = mma.sync kernel (same
  * arithmetic; kept to cross-check the default). */
 FA_API int fa_set_gemm_variant(fa_ctx* ctx, int variant);
+/* 1 = programmatic dependent launch between a step's kernels (default): each kernel's
+ * prologue overlaps the previous kernel's tail. 0 = plain stream order. */
+FA_API int fa_set_pdl(fa_ctx* ctx, int enable);
 /* 1 = launch each step as a captured CUDA graph (default), 0 = direct launches. */
 FA_API int fa_set_graphs(fa_ctx* ctx, int enable);
 /* Pool geometry: pages, free pages, bytes of one page across all layers. */
@@ -156,9 +159,10 @@ FA_API int fa_kv_fill_synthetic(fa_ctx* ctx, int seq_id, int n_tokens, uint64_t 
 FA_API int fa_pool_compact(fa_ctx* ctx, int* n_moved);
 
 /* ---- measurement ---- */
-/* 1 = bracket every attention launch with CUDA events (taken into graphs when captured). */
+/* 1 = bracket the attention launches of layers 0, L/2 and L-1 with CUDA events (taken
+ * into graphs when captured). */
 FA_API int fa_profile(fa_ctx* ctx, int enable);
-/* Attention launches of the last forward/generate step: summed device ms and count
+/* Those attention launches of the last forward/generate step: summed device ms and count
  * (paged-attention kernel plus its split combine). */
 FA_API int fa_profile_attention(fa_ctx* ctx, float* total_ms, int* n_launches);
 /* Kernels launched by the last forward step (all of this library's kernels). */

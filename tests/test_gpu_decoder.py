@@ -83,14 +83,15 @@ def test_prefill_and_decode_match_oracle(torch_cuda, small_w):
     dec.close()
 
 
-def test_generate_equals_stepwise_and_graphs_are_bitwise_stable(torch_cuda, small_w):
+def test_generate_equals_stepwise_and_graphs_pdl_are_bitwise_stable(torch_cuda, small_w):
     w = small_w
     rng = np.random.default_rng(1)
     prompt = rng.integers(0, CFG["vocab"], (4, 10))
 
-    def run(use_graphs, generate):
+    def run(use_graphs, generate, pdl=True):
         dec = _decoder(w, CFG)
         dec.set_graphs(use_graphs)
+        dec.set_pdl(pdl)
         sids = [dec.seq_open(MAX_CTX) for _ in range(4)]
         nxt, lg = dec.forward(np.repeat(sids, 10), tokens=prompt.reshape(-1), want_logits=True)
         first = nxt[9::10]
@@ -110,8 +111,10 @@ def test_generate_equals_stepwise_and_graphs_are_bitwise_stable(torch_cuda, smal
     lg_a, ids_a, lens_a = run(True, True)
     lg_b, ids_b, lens_b = run(False, False)
     lg_c, ids_c, _ = run(True, False)
+    lg_d, ids_d, _ = run(True, True, pdl=False)
     assert np.array_equal(lg_a.view(np.uint32), lg_b.view(np.uint32))
-    assert np.array_equal(ids_a, ids_b) and np.array_equal(ids_a, ids_c)
+    assert np.array_equal(lg_a.view(np.uint32), lg_d.view(np.uint32)), "PDL changes results"
+    assert np.array_equal(ids_a, ids_b) and np.array_equal(ids_a, ids_c) and np.array_equal(ids_a, ids_d)
     assert lens_a == lens_b == [18] * 4
 
 
