@@ -34,12 +34,12 @@ namespace {
 
 thread_local std::string g_err;
 
-// Q8_0 weights on the device: q as exact-integer f16 [N][K], d as f16 [K/32][N].
+// Q8_0 weights on the device as f16(d * q) [N][K].
 struct LayerW {
-    __half* qkv_q = nullptr; __half* qkv_d = nullptr;
-    __half* o_q = nullptr;   __half* o_d = nullptr;
-    __half* gu_q = nullptr;  __half* gu_d = nullptr;
-    __half* dn_q = nullptr;  __half* dn_d = nullptr;
+    __half* qkv_q = nullptr;
+    __half* o_q = nullptr;
+    __half* gu_q = nullptr;
+    __half* dn_q = nullptr;
     float* in_norm = nullptr;
     float* post_norm = nullptr;
     float* q_norm = nullptr;
@@ -105,7 +105,6 @@ struct fa_ctx {
     int embed_type = FA_TYPE_BF16;
     float* final_norm = nullptr;
     __half* lm_q = nullptr;
-    __half* lm_d = nullptr;
     std::vector<void*> dev_allocs;
 
     __half* pool = nullptr;
@@ -474,11 +473,10 @@ static int upload_vec_f32(fa_ctx* ctx, const fa_tensor_view* v, float** dst) {
     return FA_OK;
 }
 
-// Repack a GGUF Q8_0 tensor with N rows of K into (q, d) at row offset r0 (d has ldn columns).
-static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, __half* q,
-                     __half* dsc, int ldn) {
+// Expand a GGUF Q8_0 tensor with N rows of K into f16(d * q) rows at row offset r0.
+static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, __half* w) {
     FA_CK(cudaMemcpyAsync(staging, v->data, v->nbytes, cudaMemcpyHostToDevice, ctx->stream));
-    fa::launch_repack_q8(staging, N, K, r0, q, dsc, ldn, ctx->stream);
+    fa::launch_repack_q8(staging, N, K, r0, w, ctx->stream);
     FA_CK(cudaGetLastError());
     FA_CK(cudaStreamSynchronize(ctx->stream));
     return FA_OK;
@@ -536,27 +534,24 @@ extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n
             LayerW& w = ctx->L[l];
             LV& t = lv[l];
             int r;
-            if ((r = dev_alloc(ctx, &w.qkv_q, (size_t)QKV * H * 2)) || (r = dev_alloc(ctx, &w.qkv_d, (size_t)QKV * (H / 32) * 2)) ||
-                (r = dev_alloc(ctx, &w.o_q, (size_t)H * QD * 2)) || (r = dev_alloc(ctx, &w.o_d, (size_t)H * (QD / 32) * 2)) ||
-                (r = dev_alloc(ctx, &w.gu_q, (size_t)2 * F * H * 2)) || (r = dev_alloc(ctx, &w.gu_d, (size_t)2 * F * (H / 32) * 2)) ||
-                (r = dev_alloc(ctx, &w.dn_q, (size_t)H * F * 2)) || (r = dev_alloc(ctx, &w.dn_d, (size_t)H * (F / 32) * 2)))
+            if ((r = dev_alloc(ctx, &w.qkv_q, (size_t)QKV * H * 2)) || (r = dev_alloc(ctx, &w.o_q, (size_t)H * QD * 2)) ||
+                (r = dev_alloc(ctx, &w.gu_q, (size_t)2 * F * H * 2)) || (r = dev_alloc(ctx, &w.dn_q, (size_t)H * F * 2)))
                 return r;
-            if ((r = upload_q8(ctx, t.q, staging, QD, H, 0, w.qkv_q, w.qkv_d, QKV)) ||
-                (r = upload_q8(ctx, t.k, staging, KD, H, QD, w.qkv_q, w.qkv_d, QKV)) ||
-                (r = upload_q8(ctx, t.v, staging, KD, H, QD + KD, w.qkv_q, w.qkv_d, QKV)) ||
-                (r = upload_q8(ctx, t.o, staging, H, QD, 0, w.o_q, w.o_d, H)) ||
-                (r = upload_q8(ctx, t.g, staging, F, H, 0, w.gu_q, w.gu_d, 2 * F)) ||
-                (r = upload_q8(ctx, t.u, staging, F, H, F, w.gu_q, w.gu_d, 2 * F)) ||
-                (r = upload_q8(ctx, t.dn, staging, H, F, 0, w.dn_q, w.dn_d, H)))
+            if ((r = upload_q8(ctx, t.q, staging, QD, H, 0, w.qkv_q)) ||
+                (r = upload_q8(ctx, t.k, staging, KD, H, QD, w.qkv_q)) ||
+                (r = upload_q8(ctx, t.v, staging, KD, H, QD + KD, w.qkv_q)) ||
+                (r = upload_q8(ctx, t.o, staging, H, QD, 0, w.o_q)) ||
+                (r = upload_q8(ctx, t.g, staging, F, H, 0, w.gu_q)) ||
+                (r = upload_q8(ctx, t.u, staging, F, H, F, w.gu_q)) ||
+                (r = upload_q8(ctx, t.dn, staging, H, F, 0, w.dn_q)))
                 return r;
             if ((r = upload_vec_f32(ctx, t.qn, &w.q_norm)) || (r = upload_vec_f32(ctx, t.kn, &w.k_norm)) ||
                 (r = upload_vec_f32(ctx, t.in, &w.in_norm)) || (r = upload_vec_f32(ctx, t.post, &w.post_norm)))
                 return r;
         }
         int r;
-        if ((r = dev_alloc(ctx, &ctx->lm_q, (size_t)V * H * 2)) || (r = dev_alloc(ctx, &ctx->lm_d, (size_t)V * (H / 32) * 2)))
-            return r;
-        if ((r = upload_q8(ctx, lm, staging, V, H, 0, ctx->lm_q, ctx->lm_d, V))) return r;
+        if ((r = dev_alloc(ctx, &ctx->lm_q, (size_t)V * H * 2))) return r;
+        if ((r = upload_q8(ctx, lm, staging, V, H, 0, ctx->lm_q))) return r;
         if ((r = upload_vec_f32(ctx, fnorm, &ctx->final_norm))) return r;
         if ((r = dev_alloc(ctx, (uint8_t**)&ctx->embed, emb->nbytes))) return r;
         FA_CK(cudaMemcpy(ctx->embed, emb->data, emb->nbytes, cudaMemcpyHostToDevice));
@@ -785,7 +780,7 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         __half* pool_l = ctx->pool + (size_t)l * ctx->layer_stride;
         fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, w.in_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         fa::GemmArgs g{};
-        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wqh = w.qkv_q; g.Wd = w.qkv_d; g.M = M; g.N = QKV; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = w.qkv_q; g.M = M; g.N = QKV; g.K = H;
         g.n_split = p.s_qkv; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         run_gemm(ctx, g);
         fa::AppendArgs a{};
@@ -811,17 +806,17 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         }
         if (prof_l) record_prof(ctx, 2 * l + 1, capturing);
         g = fa::GemmArgs{};
-        g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.Wqh = w.o_q; g.Wd = w.o_d; g.M = M; g.N = H; g.K = kHq * kD;
+        g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.Wh = w.o_q; g.M = M; g.N = H; g.K = kHq * kD;
         g.n_split = p.s_o; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         run_gemm(ctx, g);
         fa::launch_residual_rmsnorm(ctx->x, ctx->part, p.s_o, M, H, w.post_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         g = fa::GemmArgs{};
-        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wqh = w.gu_q; g.Wd = w.gu_d; g.M = M; g.N = 2 * F; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = w.gu_q; g.M = M; g.N = 2 * F; g.K = H;
         g.n_split = p.s_gu; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         run_gemm(ctx, g);
         fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s);
         g = fa::GemmArgs{};
-        g.A = ctx->h16; g.A_lo = ctx->h_lo; g.Wqh = w.dn_q; g.Wd = w.dn_d; g.M = M; g.N = H; g.K = F;
+        g.A = ctx->h16; g.A_lo = ctx->h_lo; g.Wh = w.dn_q; g.M = M; g.N = H; g.K = F;
         g.n_split = p.s_dn; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         run_gemm(ctx, g);
         n += 8;
@@ -830,7 +825,7 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     }
     fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
     fa::GemmArgs g{};
-    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wqh = ctx->lm_q; g.Wd = ctx->lm_d; g.M = M; g.N = d.vocab; g.K = H;
+    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = ctx->lm_q; g.M = M; g.N = d.vocab; g.K = H;
     g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = p.logits ? ctx->logits_dev : nullptr;
     g.amax_val = ctx->amax_v; g.amax_idx = ctx->amax_i;
     run_gemm(ctx, g);
@@ -1328,10 +1323,9 @@ extern "C" int fa_op_paged_attention(const float* q, int M, const int* pos, cons
     return FA_OK;
 }
 
-extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, uint16_t* q, uint16_t* d, void* stream) {
-    if (!raw || !q || !d || N <= 0 || K <= 0 || K % 32) return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
-    fa::launch_repack_q8(raw, N, K, 0, reinterpret_cast<__half*>(q), reinterpret_cast<__half*>(d), N,
-                         (cudaStream_t)stream);
+extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, uint16_t* w16, void* stream) {
+    if (!raw || !w16 || N <= 0 || K <= 0 || K % 32) return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
+    fa::launch_repack_q8(raw, N, K, 0, reinterpret_cast<__half*>(w16), (cudaStream_t)stream);
     OP_CK(cudaGetLastError());
     return FA_OK;
 }
@@ -1347,15 +1341,15 @@ static int op_gemm(const fa::GemmArgs& g, int variant, cudaStream_t s) {
     return FA_OK;
 }
 
-extern "C" int fa_op_q8_gemm(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const uint16_t* q,
-                             const uint16_t* d, int N, int n_split, float* c, int variant, void* stream) {
-    if (!a16 || !q || !d || !c || M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_split <= 0 ||
+extern "C" int fa_op_q8_gemm(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const uint16_t* w16,
+                             int N, int n_split, float* c, int variant, void* stream) {
+    if (!a16 || !w16 || !c || M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_split <= 0 ||
         (K / 64) % n_split)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "need N, K multiples of 64 and n_split dividing K/64");
     if (int rc = ensure_configured()) return rc;
     fa::GemmArgs g{};
     g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo);
-    g.Wqh = reinterpret_cast<const __half*>(q); g.Wd = reinterpret_cast<const __half*>(d);
+    g.Wh = reinterpret_cast<const __half*>(w16);
     g.M = M; g.N = N; g.K = K; g.n_split = n_split; g.epilogue = fa::kEpiStoreF32; g.C = c;
     return op_gemm(g, variant, (cudaStream_t)stream);
 }
@@ -1365,15 +1359,14 @@ extern "C" size_t fa_op_argmax_scratch_bytes(int M, int N) {
     return (size_t)M * (N / 64) * (sizeof(float) + sizeof(int));
 }
 
-extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const uint16_t* q,
-                                    const uint16_t* d, int N, void* scratch, int* next, float* logits, int variant,
-                                    void* stream) {
-    if (!a16 || !q || !d || !scratch || !next || M <= 0 || N % 64 || K % 64)
+extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const uint16_t* w16,
+                                    int N, void* scratch, int* next, float* logits, int variant, void* stream) {
+    if (!a16 || !w16 || !scratch || !next || M <= 0 || N % 64 || K % 64)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
     if (int rc = ensure_configured()) return rc;
     fa::GemmArgs g{};
     g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo);
-    g.Wqh = reinterpret_cast<const __half*>(q); g.Wd = reinterpret_cast<const __half*>(d);
+    g.Wh = reinterpret_cast<const __half*>(w16);
     g.M = M; g.N = N; g.K = K; g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = logits;
     g.amax_val = reinterpret_cast<float*>(scratch);
     g.amax_idx = reinterpret_cast<int*>(g.amax_val + (size_t)M * (N / 64));

@@ -8,9 +8,8 @@
 //                    copy moves it.
 //   block table    : int32 [seq_slot][page_index]; token p of slot s sits in page
 //                    block_table[s][p / 16] at in-page token p % 16.
-//   Q8_0 weights   : repacked at load time from GGUF blocks ([f16 d][32 x int8]) into
-//                    q [N][K] (the int8 values held exactly as f16, row-major, TMA-able)
-//                    and d f16 [K/32][N] (the scales of one K block contiguous over N).
+//   Q8_0 weights   : expanded at load time from GGUF blocks ([f16 d][32 x int8]) into
+//                    W [N][K] f16 = f16(d * q), row-major (K contiguous), TMA-able.
 //   RoPE table     : float2 [pos][head_dim/2] = (cos, sin), computed on the host in double.
 #pragma once
 

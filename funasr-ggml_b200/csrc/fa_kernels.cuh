@@ -74,8 +74,7 @@ enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1 };
 struct GemmArgs {
     const __half* A;         // [M][K] f16 activations (hi part)
     const __half* A_lo;      // [M][K] f16 remainder x - hi, or nullptr (plain f16 activations)
-    const __half* Wqh;       // [N][K] Q8_0 integers q held exactly as f16
-    const __half* Wd;        // [K/32][N] f16 block scales
+    const __half* Wh;        // [N][K] f16(d * q): Q8_0 weights rounded once to f16 at load time
     int M, N, K;
     int n_split;             // split-K factor (grid.z); K/n_split multiple of 64
     int epilogue;
@@ -106,10 +105,9 @@ void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, 
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,
                           int* feed_pos, cudaStream_t s);
 void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* upd_page, int n, cudaStream_t s);
-// GGUF Q8_0 rows [N][K/32][34 B] -> q as exact f16 [N][K] + d [K/32][ldn], rows landing at
+// GGUF Q8_0 rows [N][K/32][34 B] -> W [N][K] f16 with W = f16(f32(d) * q), rows landing at
 // destination row r0 + n (Wq, Wk, Wv and gate, up are stacked that way).
-void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_q, __half* dst_d, int ldn,
-                      cudaStream_t s);
+void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_w, cudaStream_t s);
 void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,
                       cudaStream_t s);
 void launch_fill_random(__half* pool, size_t layer_stride, int n_layers, const int* pages, int n_pages_list,

@@ -5,20 +5,17 @@
 // :206 lm_head). At decode batch B the weight stream is read once per step for
 // all B rows, so the op is a skinny GEMM C[B][N] = A[B][K] . W[N][K]^T.
 //
-// Arithmetic (the oracle's exact GEMM mode): activations arrive as an f16 pair
-// (hi, lo) with hi + lo = x to ~22 bits, the int8 weights enter the MMA exactly as
-// f16, and each 32-wide Q8_0 block's partial sum is scaled by its f16 scale d in
-// fp32 before it joins the fp32 accumulator. So the result is the f32 product
-// of the activations with the exactly dequantised weights d*q, like ggml's
-// block-scaled dot, without rounding either operand to 11 bits. (Rounding the
-// activations to a single f16 makes the decoder output jump by ~3e-4 relative
-// under 1e-7 input noise, which no parity tolerance survives.)
+// Arithmetic (the oracle's GEMM mode 1, same as k_gemm_tc.cu): activations
+// arrive as an f16 pair (hi, lo) with hi + lo = x to ~22 bits, so the product is
+// a smooth function of them (a single f16 rounding of the activations makes the
+// decoder output jump by ~3e-4 relative under 1e-7 input noise, which no parity
+// tolerance survives); the weights are f16(d*q), rounded once at load time;
+// products are exact and accumulate in fp32.
 //
 // This is the legacy-tensor-core (mma.sync m16n8k16) implementation, kept as the
 // cross-check of the tcgen05 kernel in k_gemm_tc.cu, which is the default.
-// Pipeline: 3-stage cp.async ring for the A tiles (BM x 64 f16, hi and lo), the
-// weight tile (64 x 64 exact-integer f16) and its two rows of block scales;
-// ldmatrix feeds the MMAs (2 per k16 step). Split-K over grid.z writes fp32
+// Pipeline: 3-stage cp.async ring for the A tiles (BM x 64 f16, hi and lo) and
+// the weight tile (64 x 64 f16); ldmatrix feeds the MMAs (2 per k16 step). Split-K over grid.z writes fp32
 // partials that the next fused kernel (RoPE/append, residual+RMSNorm, SwiGLU)
 // sums in a fixed order, so results are deterministic.
 // Epilogue kEpiArgmax (lm_head): per-row maximum and its first column over the
@@ -47,9 +44,7 @@ struct Cfg {
     static constexpr int NT = WTN / 8;
     static constexpr int A_STAGE = BM * A_LD;        // halves
     static constexpr int Q_STAGE = BN * B_LD * 2;    // bytes (f16 weight tile, padded rows)
-    static constexpr int S_STAGE = 2 * BN;           // halves (2 K-blocks x BN scales)
-    static constexpr size_t SMEM = (size_t)STAGES * (2 * A_STAGE * 2 + Q_STAGE + S_STAGE * 2) +
-                                   (size_t)BM * WN * 8;
+    static constexpr size_t SMEM = (size_t)STAGES * (2 * A_STAGE * 2 + Q_STAGE) + (size_t)BM * WN * 8;
     static_assert(WTM % 16 == 0 && WTN % 8 == 0, "warp tile");
     static_assert(NT % 2 == 0, "B fragments are loaded two n8 tiles at a time");
 };
@@ -77,9 +72,8 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
     // A stage st: hi tile at As + (2*st) * A_STAGE, lo tile right after it
     __half* As = reinterpret_cast<__half*>(smem);
     unsigned char* Qs = smem + (size_t)STAGES * 2 * C::A_STAGE * 2;
-    __half* Ss = reinterpret_cast<__half*>(smem + (size_t)STAGES * (2 * C::A_STAGE * 2 + C::Q_STAGE));
     const bool has_lo = g.A_lo != nullptr;
-    float* red_v = reinterpret_cast<float*>(smem + (size_t)STAGES * (2 * C::A_STAGE * 2 + C::Q_STAGE + C::S_STAGE * 2));
+    float* red_v = reinterpret_cast<float*>(smem + (size_t)STAGES * (2 * C::A_STAGE * 2 + C::Q_STAGE));
     int* red_i = reinterpret_cast<int*>(red_v + BM * WN);
 
     const int tid = threadIdx.x;
@@ -105,12 +99,7 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
         __half* q_dst = reinterpret_cast<__half*>(Qs + st * C::Q_STAGE);
         for (int ch = tid; ch < BN * 8; ch += C::THREADS) {
             const int r = ch >> 3, cc = ch & 7;
-            cp_async16(q_dst + r * B_LD + cc * 8, g.Wqh + (size_t)(n0 + r) * g.K + k0 + cc * 8, true);
-        }
-        __half* s_dst = Ss + st * C::S_STAGE;
-        for (int ch = tid; ch < 2 * BN / 8; ch += C::THREADS) {
-            const int kb = ch / (BN / 8), cc = ch % (BN / 8);
-            cp_async16(s_dst + kb * BN + cc * 8, g.Wd + (size_t)(k0 / kQK + kb) * g.N + n0 + cc * 8, true);
+            cp_async16(q_dst + r * B_LD + cc * 8, g.Wh + (size_t)(n0 + r) * g.K + k0 + cc * 8, true);
         }
     };
 
@@ -140,55 +129,28 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
         const __half* Bs = reinterpret_cast<const __half*>(Qs + st * C::Q_STAGE);
         const __half* a_hi = As + 2 * st * C::A_STAGE;
         const __half* a_lo = a_hi + C::A_STAGE;
-        const __half* s_st = Ss + st * C::S_STAGE;
 #pragma unroll
-        for (int kb = 0; kb < BK / kQK; ++kb) {
-            float bacc[C::MT][C::NT][4];
+        for (int kk = 0; kk < BK / 16; ++kk) {
+            uint32_t ah[C::MT][4], al[C::MT][4];
 #pragma unroll
-            for (int i = 0; i < C::MT; ++i)
-#pragma unroll
-                for (int j = 0; j < C::NT; ++j)
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) bacc[i][j][k] = 0.0f;
-#pragma unroll
-            for (int k2 = 0; k2 < kQK / 16; ++k2) {
-                const int kk = kb * (kQK / 16) + k2;
-                uint32_t ah[C::MT][4], al[C::MT][4];
-#pragma unroll
-                for (int mt = 0; mt < C::MT; ++mt) {
-                    const int r = wm * C::WTM + mt * 16 + (lane & 15);
-                    ldmatrix_x4(ah[mt], a_hi + r * A_LD + kk * 16 + (lane >> 4) * 8);
-                    if (has_lo) ldmatrix_x4(al[mt], a_lo + r * A_LD + kk * 16 + (lane >> 4) * 8);
-                }
-#pragma unroll
-                for (int np = 0; np < C::NT / 2; ++np) {
-                    uint32_t bf[4];
-                    const int r = wn * C::WTN + np * 16 + (lane & 7) + ((lane >> 4) << 3);
-                    ldmatrix_x4(bf, Bs + r * B_LD + kk * 16 + ((lane >> 3) & 1) * 8);
-#pragma unroll
-                    for (int mt = 0; mt < C::MT; ++mt) {
-                        mma16816(bacc[mt][2 * np], ah[mt], bf[0], bf[1]);
-                        mma16816(bacc[mt][2 * np + 1], ah[mt], bf[2], bf[3]);
-                        if (has_lo) {
-                            mma16816(bacc[mt][2 * np], al[mt], bf[0], bf[1]);
-                            mma16816(bacc[mt][2 * np + 1], al[mt], bf[2], bf[3]);
-                        }
-                    }
-                }
+            for (int mt = 0; mt < C::MT; ++mt) {
+                const int r = wm * C::WTM + mt * 16 + (lane & 15);
+                ldmatrix_x4(ah[mt], a_hi + r * A_LD + kk * 16 + (lane >> 4) * 8);
+                if (has_lo) ldmatrix_x4(al[mt], a_lo + r * A_LD + kk * 16 + (lane >> 4) * 8);
             }
-            // scale the block partials by d of their columns and accumulate
-            const int tq = lane & 3;
 #pragma unroll
-            for (int nt = 0; nt < C::NT; ++nt) {
-                const int col = wn * C::WTN + nt * 8 + 2 * tq;
-                const float d0 = __half2float(s_st[kb * BN + col]);
-                const float d1 = __half2float(s_st[kb * BN + col + 1]);
+            for (int np = 0; np < C::NT / 2; ++np) {
+                uint32_t bf[4];
+                const int r = wn * C::WTN + np * 16 + (lane & 7) + ((lane >> 4) << 3);
+                ldmatrix_x4(bf, Bs + r * B_LD + kk * 16 + ((lane >> 3) & 1) * 8);
 #pragma unroll
                 for (int mt = 0; mt < C::MT; ++mt) {
-                    acc[mt][nt][0] = fmaf(bacc[mt][nt][0], d0, acc[mt][nt][0]);
-                    acc[mt][nt][1] = fmaf(bacc[mt][nt][1], d1, acc[mt][nt][1]);
-                    acc[mt][nt][2] = fmaf(bacc[mt][nt][2], d0, acc[mt][nt][2]);
-                    acc[mt][nt][3] = fmaf(bacc[mt][nt][3], d1, acc[mt][nt][3]);
+                    mma16816(acc[mt][2 * np], ah[mt], bf[0], bf[1]);
+                    mma16816(acc[mt][2 * np + 1], ah[mt], bf[2], bf[3]);
+                    if (has_lo) {
+                        mma16816(acc[mt][2 * np], al[mt], bf[0], bf[1]);
+                        mma16816(acc[mt][2 * np + 1], al[mt], bf[2], bf[3]);
+                    }
                 }
             }
         }

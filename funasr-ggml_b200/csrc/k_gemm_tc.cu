@@ -1,32 +1,30 @@
 // Kernel (4), Blackwell path: Q8_0 weight GEMM on the 5th-generation tensor cores.
 //
-//     C[M][N] = A[M][K] . W[N][K]^T,   W[n][k] = d[k/32][n] * q[n][k]
+//     C[M][N] = A[M][K] . W[N][K]^T,   W = f16(d * q) per Q8_0 block, made at load time
 //
-// Same arithmetic as the mma.sync kernel in k_gemm.cu (and the oracle's exact
-// GEMM mode): A arrives as an f16 pair (hi, lo), q enters the MMA as exact f16
-// integers, and each 32-wide Q8_0 block's partial sum is scaled by its d in
-// fp32 before it joins the fp32 accumulator - ggml's block-scaled dot without
-// rounding either operand.
+// Arithmetic (the oracle's GEMM mode 1): A arrives as an f16 pair (hi, lo) with
+// hi + lo = x to ~22 bits, so the product is a smooth function of the
+// activations; the weights are the Q8_0 values d*q rounded once to f16 (relative
+// error <= 2^-11, fixed per weight); products are exact and accumulate in fp32 in
+// TMEM over the whole K range of a work unit.
 //
 // Persistent kernel: one CTA per SM walks the work units u = blockIdx.x,
 // blockIdx.x + gridDim.x, ... where a unit is one 128 x 128 output tile times one
 // K chunk (split-K). The pipeline never drains between units: the producer runs
-// ahead into the next unit, and the epilogue of one unit overlaps the next
-// unit's MMAs. 10 warps, one role each:
+// ahead into the next unit, and the epilogue of one unit (TMEM buffer u & 1)
+// overlaps the MMAs of the next. 10 warps, one role each:
 //   warp 0      TMA producer: cp.async.bulk.tensor 2-D loads per stage of A hi,
-//               A lo (128 x 64 f16), W (128 x 64 f16), all 128 B swizzled, and the
-//               stage's block scales (2 x 128 f16); 4-stage ring
+//               A lo (128 x 64 f16) and W (128 x 64 f16), 128 B swizzled; 4-stage
+//               ring. The first stages' weight copies go out before the wait on
+//               the previous kernel (programmatic dependent launch).
 //   warp 1      allocates 256 TMEM columns; one lane issues tcgen05.mma
-//               (cta_group::1, kind::f16, M=128, N=128, K=16) for one Q8_0 block
-//               (2 k-steps x hi/lo) into TMEM buffer (block & 1) and commits it
+//               (cta_group::1, kind::f16, M=128, N=128, K=16; hi and lo) and
+//               commits stages back to the producer and units to the epilogue
 //   warps 2..9  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and
-//               columns 64*((w-2)/4).. ; per block acc += partial * d, then the
-//               buffer (and, after a stage's second block, the stage) is released;
-//               at a unit's end the fp32 partials or the tile's row argmax go out
-// A stage is free again when the MMAs that read it have completed (tcgen05.commit)
-// and all 8 epilogue warps have read its scales. Every mbarrier wait is bounded in
-// time; a wait that gives up records an error and the CTA drains its copies and
-// MMAs before freeing TMEM.
+//               columns 64*((w-2)/4).. of the unit's accumulator, releases the
+//               buffer, and writes fp32 split-K partials or the tile's row argmax
+// Every mbarrier wait is bounded in time; a wait that gives up records an error
+// and the CTA drains its copies and MMAs before freeing TMEM.
 #include "fa_kernels.cuh"
 
 #include <cuda.h>
@@ -39,20 +37,18 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int BK = 64;              // K per stage: two Q8_0 blocks
+constexpr int BK = 64;              // K per stage
 constexpr int STAGES = 4;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 constexpr uint32_t B_BYTES = BN * BK * 2;
-constexpr uint32_t SC_BYTES = 2 * BN * 2;
 constexpr uint32_t TMEM_COLS = 2 * BN;  // two fp32 accumulators of 128 columns
 
 struct TcSmem {
     __half a_hi[STAGES][BM * BK];   // 16 KiB each, 1 KiB aligned (128 B swizzle atoms)
     __half a_lo[STAGES][BM * BK];
     __half b[STAGES][BN * BK];      // 16 KiB each
-    __half scale[STAGES][2][BN];    // d of the stage's two K blocks for the tile's columns
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
     uint64_t tfull[2];
@@ -109,6 +105,10 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
         : "memory");
 }
 
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
 #define TMEM_LD_X32(taddr, v)                                                                                  \
     asm volatile(                                                                                              \
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"       \
@@ -145,20 +145,20 @@ __device__ __forceinline__ Unit unit_of(const TcArgs& g, int u) {
 
 __global__ void __launch_bounds__(THREADS, 1)
     q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
-                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_sc,
-                      const TcArgs g) {
+                      const __grid_constant__ CUtensorMap tm_b, const TcArgs g) {
     extern __shared__ unsigned char smem_raw[];
     TcSmem& S = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int k_len = g.K / g.n_split;
-    const int n_iters = k_len / BK;     // stages per unit
-    const int n_blk = k_len / kQK;      // Q8_0 blocks per unit
+    const int n_iters = (g.K / g.n_split) / BK;     // stages per unit
 
     if (threadIdx.x == 0) {
+        tma_prefetch_desc(&tm_a_hi);
+        tma_prefetch_desc(&tm_a_lo);
+        tma_prefetch_desc(&tm_b);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], 1 + EPI_WARPS);
+            mbar_init(&S.empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.tfull[b], 1);
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t bytes = A_BYTES * (g.has_lo ? 2 : 1) + B_BYTES + SC_BYTES;
+            const uint32_t bytes = A_BYTES * (g.has_lo ? 2 : 1) + B_BYTES;
             int my_units = 0;
             for (int u = blockIdx.x; u < g.n_units; u += gridDim.x) ++my_units;
             const int total = my_units * n_iters;
@@ -194,15 +194,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 m0 = w.m0;
                 n0 = w.n0;
             };
-            // The weights and scales do not depend on the previous kernel: the first
-            // stages' copies go out before waiting for it; the activations after.
+            // The weights do not depend on the previous kernel: the first stages'
+            // weight copies go out before waiting for it; the activations after.
             const int pre = total < STAGES ? total : STAGES;
             for (int it = 0; it < pre; ++it) {
                 int k, m0, n0;
                 coords(it, k, m0, n0);
                 mbar_arrive_expect_tx(&S.full[it], bytes);
                 tma_load_2d(S.b[it], &tm_b, k, n0, &S.full[it]);
-                tma_load_2d(S.scale[it], &tm_sc, n0, k / kQK, &S.full[it]);
             }
             pdl_wait();
             for (int it = 0; it < pre; ++it) {
@@ -225,7 +224,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_2d(S.a_hi[s], &tm_a_hi, k, m0, &S.full[s]);
                 if (g.has_lo) tma_load_2d(S.a_lo[s], &tm_a_lo, k, m0, &S.full[s]);
                 tma_load_2d(S.b[s], &tm_b, k, n0, &S.full[s]);
-                tma_load_2d(S.scale[s], &tm_sc, n0, k / kQK, &S.full[s]);
                 S.issued = it + 1;
             }
             if (!ok) S.err = 1;
@@ -235,33 +233,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             bool ok = true;
             int it = 0, j = 0;
-            for (int u = blockIdx.x; u < g.n_units && ok; u += gridDim.x) {
-                for (int b = 0; b < n_blk; ++b, ++j) {
-                    const int half = b & 1, s = it % STAGES;
-                    if (half == 0) {
-                        if (!mbar_wait_bounded(&S.full[s], (uint32_t)(it / STAGES) & 1u)) { ok = false; break; }
-                        S.consumed = it + 1;
-                    }
-                    const int buf = j & 1;
-                    if (j >= 2 && !mbar_wait_bounded(&S.tempty[buf], (uint32_t)((j >> 1) - 1) & 1u)) {
-                        ok = false;
-                        break;
-                    }
+            for (int u = blockIdx.x; u < g.n_units && ok; u += gridDim.x, ++j) {
+                const int buf = j & 1;
+                if (j >= 2 && !mbar_wait_bounded(&S.tempty[buf], (uint32_t)((j >> 1) - 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + (uint32_t)(buf * BN);
+                for (int i = 0; i < n_iters; ++i, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait_bounded(&S.full[s], (uint32_t)(it / STAGES) & 1u)) { ok = false; break; }
+                    S.consumed = it + 1;
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem + (uint32_t)(buf * BN);
 #pragma unroll
-                    for (int kk = 0; kk < 2; ++kk) {
-                        const uint32_t koff = (uint32_t)(half * 64 + kk * 32) >> 4;   // bytes / 16
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint32_t koff = (uint32_t)(kk * 32) >> 4;   // bytes / 16
                         const uint64_t db = smem_desc(S.b[s]) + koff;
-                        tc_mma(d_tmem, smem_desc(S.a_hi[s]) + koff, db, kk > 0 ? 1u : 0u);
+                        tc_mma(d_tmem, smem_desc(S.a_hi[s]) + koff, db, (i > 0 || kk > 0) ? 1u : 0u);
                         if (g.has_lo) tc_mma(d_tmem, smem_desc(S.a_lo[s]) + koff, db, 1u);
                     }
-                    tc_commit(&S.tfull[buf]);
-                    if (half == 1) {
-                        tc_commit(&S.empty[s]);
-                        ++it;
-                    }
+                    tc_commit(&S.empty[s]);
                 }
+                if (!ok) break;
+                tc_commit(&S.tfull[buf]);
             }
             if (!ok) S.err = 1;
             // every MMA issued so far completes before TMEM can be released
@@ -273,43 +268,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int q = warp & 3;                 // TMEM lanes 32q..32q+31 belong to this warp
         const int ch = (warp - 2) >> 2;         // column half of the tile
         const int row = q * 32 + lane;          // accumulator row
-        int it = 0, j = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; u < g.n_units && ok; u += gridDim.x) {
+        int j = 0;
+        for (int u = blockIdx.x; u < g.n_units; u += gridDim.x, ++j) {
             const Unit w = unit_of(g, u);
-            float acc[64];
-#pragma unroll
-            for (int c = 0; c < 64; ++c) acc[c] = 0.0f;
-            for (int b = 0; b < n_blk; ++b, ++j) {
-                const int buf = j & 1, half = b & 1, s = it % STAGES;
-                const bool got = mbar_wait_bounded(&S.tfull[buf], (uint32_t)(j >> 1) & 1u);
-                if (!__all_sync(0xffffffffu, got)) {
-                    if (lane == 0) S.err = 1;
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                uint32_t v[64];
-                const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + ch * 64);
-                TMEM_LD_X32(taddr, v);
-                TMEM_LD_X32(taddr + 32, (v + 32));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                mbar_arrive(&S.tempty[buf]);
-                const __half2* sc = reinterpret_cast<const __half2*>(&S.scale[s][half][ch * 64]);
-#pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const float2 d = __half22float2(sc[c]);
-                    acc[2 * c] = fmaf(__uint_as_float(v[2 * c]), d.x, acc[2 * c]);
-                    acc[2 * c + 1] = fmaf(__uint_as_float(v[2 * c + 1]), d.y, acc[2 * c + 1]);
-                }
-                if (half == 1) {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&S.empty[s]);   // this warp is done with the stage's scales
-                    ++it;
-                }
+            const int buf = j & 1;
+            const bool got = mbar_wait_bounded(&S.tfull[buf], (uint32_t)(j >> 1) & 1u);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) S.err = 1;
+                break;
             }
-            if (!ok) break;
+            tc_fence_after();
+            uint32_t v[64];
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + ch * 64);
+            TMEM_LD_X32(taddr, v);
+            TMEM_LD_X32(taddr + 32, (v + 32));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(&S.tempty[buf]);
             const int gm = w.m0 + row;
             const int c0 = w.n0 + ch * 64;
             if (gm < g.M) {
@@ -318,7 +293,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                                  (size_t)gm * g.N + c0;
 #pragma unroll
                     for (int c = 0; c < 64; c += 4)
-                        *reinterpret_cast<float4*>(out + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+                        *reinterpret_cast<float4*>(out + c) =
+                            make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
+                                        __uint_as_float(v[c + 3]));
                 }
                 if (g.epilogue == kEpiArgmax) {
                     // first maximum of the row within this 64-column half; NaN never wins
@@ -326,7 +303,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     int bi = 0x7fffffff;
 #pragma unroll
                     for (int c = 0; c < 64; ++c)
-                        if (acc[c] > bv) { bv = acc[c]; bi = c0 + c; }
+                        if (__uint_as_float(v[c]) > bv) { bv = __uint_as_float(v[c]); bi = c0 + c; }
                     const int n_tiles = g.N / 64;
                     g.amax_val[(size_t)gm * n_tiles + c0 / 64] = bv;
                     g.amax_idx[(size_t)gm * n_tiles + c0 / 64] = bi;
@@ -390,7 +367,7 @@ void configure_gemm_tc() {
 }
 
 // Split-K factor for the persistent kernel: the divisor S of K/64 (with K/S >= 128)
-// that minimises rounds * (Q8_0 blocks per unit + 2), rounds = ceil(units / SMs).
+// that minimises rounds * (32-wide K blocks per unit + 2), rounds = ceil(units / SMs).
 int gemm_tc_pick_split(int M, int N, int K, int n_sm) {
     const int tiles = (N / BN) * ((M + BM - 1) / BM);
     const int kb = K / BK;
@@ -407,7 +384,7 @@ int gemm_tc_pick_split(int M, int N, int K, int n_sm) {
 }
 
 bool gemm_tc_supported(const GemmArgs& g) {
-    return g.Wqh != nullptr && g.N % BN == 0 && g.K % BK == 0 && g.n_split > 0 && (g.K / g.n_split) % BK == 0 &&
+    return g.Wh != nullptr && g.N % BN == 0 && g.K % BK == 0 && g.n_split > 0 && (g.K / g.n_split) % BK == 0 &&
            encoder() != nullptr;
 }
 
@@ -417,11 +394,10 @@ bool launch_q8_gemm_tc(const GemmArgs& g, int* err, cudaStream_t s) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && n_sm[dev] == 0) cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev);
-    CUtensorMap ta, tl, tb, tsc;
+    CUtensorMap ta, tl, tb;
     if (!make_map(&ta, g.A, g.K, g.M, BK, BM, true)) return false;
     if (!make_map(&tl, g.A_lo ? g.A_lo : g.A, g.K, g.M, BK, BM, true)) return false;
-    if (!make_map(&tb, g.Wqh, g.K, g.N, BK, BN, true)) return false;
-    if (!make_map(&tsc, g.Wd, g.N, g.K / kQK, BN, 2, false)) return false;
+    if (!make_map(&tb, g.Wh, g.K, g.N, BK, BN, true)) return false;
     TcArgs a{};
     a.M = g.M; a.N = g.N; a.K = g.K; a.n_split = g.n_split; a.epilogue = g.epilogue; a.has_lo = g.A_lo != nullptr;
     a.n_tiles_n = g.N / BN;
@@ -429,7 +405,7 @@ bool launch_q8_gemm_tc(const GemmArgs& g, int* err, cudaStream_t s) {
     a.C = g.C; a.amax_val = g.amax_val; a.amax_idx = g.amax_idx; a.err = err;
     const int sms = (dev >= 0 && dev < 64 && n_sm[dev] > 0) ? n_sm[dev] : 148;
     const int grid = a.n_units < sms ? a.n_units : sms;
-    launch_k(q8_gemm_tc_kernel, dim3(grid), dim3(THREADS), gemm_tc_smem_bytes(), s, ta, tl, tb, tsc, a);
+    launch_k(q8_gemm_tc_kernel, dim3(grid), dim3(THREADS), gemm_tc_smem_bytes(), s, ta, tl, tb, a);
     return true;
 }
 

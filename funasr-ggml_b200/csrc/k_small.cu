@@ -6,7 +6,7 @@
 //                      f16(rms_norm(x) * w) for the next GEMM (gpu_rms_norm, :16-25)
 //   swiglu           : f16(silu(gate) * up) from the gate/up GEMM partials (:177-180)
 //   argmax_reduce    : first maximum over lm_head tiles (compute/gpu_runner.hpp:108-118)
-//   repack_q8        : GGUF Q8_0 blocks -> q as exact f16 matrix + transposed f16 scales
+//   repack_q8        : GGUF Q8_0 blocks -> f16(d * q) weight matrix
 //   page_copy / fill_random / read_pages / apply_bt_updates : page-pool maintenance
 #include "fa_kernels.cuh"
 
@@ -193,18 +193,16 @@ __global__ void apply_bt_updates_kernel(int* bt, const int* upd_idx, const int* 
     if (i < n) bt[upd_idx[i]] = upd_page[i];
 }
 
-__global__ void repack_q8_kernel(const uint8_t* raw, int N, int K, int r0, __half* dst_q, __half* dst_d, int ldn) {
+__global__ void repack_q8_kernel(const uint8_t* raw, int N, int K, int r0, __half* dst_w) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int nb = K / kQK;
     if (i >= (size_t)N * nb) return;
     const int n = (int)(i / nb), b = (int)(i % nb);
     const uint8_t* blk = raw + i * kQBytes;
-    const uint16_t dbits = (uint16_t)blk[0] | ((uint16_t)blk[1] << 8);
-    const int row = r0 + n;
-    dst_d[(size_t)b * ldn + row] = __ushort_as_half(dbits);
-    __half* q = dst_q + (size_t)row * K + (size_t)b * kQK;
+    const float d = __half2float(__ushort_as_half((uint16_t)blk[0] | ((uint16_t)blk[1] << 8)));
+    __half* w = dst_w + (size_t)(r0 + n) * K + (size_t)b * kQK;
 #pragma unroll
-    for (int j = 0; j < kQK; ++j) q[j] = __int2half_rn((int)(int8_t)blk[2 + j]);
+    for (int j = 0; j < kQK; ++j) w[j] = __float2half_rn(__fmul_rn(d, (float)(int8_t)blk[2 + j]));
 }
 
 __global__ void __launch_bounds__(256) page_copy_kernel(__half* pool, size_t layer_stride, const int* src,
@@ -272,10 +270,9 @@ void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* up
     apply_bt_updates_kernel<<<(n + 255) / 256, 256, 0, s>>>(block_table, upd_idx, upd_page, n);
 }
 
-void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_q, __half* dst_d, int ldn,
-                      cudaStream_t s) {
+void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_w, cudaStream_t s) {
     const size_t n = (size_t)N * (K / kQK);
-    repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, N, K, r0, dst_q, dst_d, ldn);
+    repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, N, K, r0, dst_w);
 }
 
 void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,

@@ -105,10 +105,10 @@ def lib():
         "fa_op_kv_append": ([_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P], _I),
         "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
         "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P], _I),
-        "fa_op_repack_q8": ([_P, _I, _I, _P, _P, _P], _I),
-        "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _P, _I, _I, _P, _I, _P], _I),
+        "fa_op_repack_q8": ([_P, _I, _I, _P, _P], _I),
+        "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _I, _I, _P, _I, _P], _I),
         "fa_op_argmax_scratch_bytes": ([_I, _I], ctypes.c_size_t),
-        "fa_op_q8_gemm_argmax": ([_P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _I, _P], _I),
+        "fa_op_q8_gemm_argmax": ([_P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _P], _I),
         "fa_palloc_create": ([_I], _P),
         "fa_palloc_destroy": ([_P], None),
         "fa_palloc_alloc": ([_P], _I),
@@ -339,20 +339,20 @@ def op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_spl
                                        stream or None))
 
 
-def op_repack_q8(raw, N, K, q, d, stream=0):
-    _check(lib().fa_op_repack_q8(raw, N, K, q, d, stream or None))
+def op_repack_q8(raw, N, K, w16, stream=0):
+    _check(lib().fa_op_repack_q8(raw, N, K, w16, stream or None))
 
 
-def op_q8_gemm(a16, a16_lo, M, K, q, d, N, n_split, c, variant=0, stream=0):
-    _check(lib().fa_op_q8_gemm(a16, a16_lo or None, M, K, q, d, N, n_split, c, variant, stream or None))
+def op_q8_gemm(a16, a16_lo, M, K, w16, N, n_split, c, variant=0, stream=0):
+    _check(lib().fa_op_q8_gemm(a16, a16_lo or None, M, K, w16, N, n_split, c, variant, stream or None))
 
 
 def op_argmax_scratch_bytes(M, N) -> int:
     return int(lib().fa_op_argmax_scratch_bytes(M, N))
 
 
-def op_q8_gemm_argmax(a16, a16_lo, M, K, q, d, N, scratch, nxt, logits=0, variant=0, stream=0):
-    _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, q, d, N, scratch, nxt, logits or None, variant,
+def op_q8_gemm_argmax(a16, a16_lo, M, K, w16, N, scratch, nxt, logits=0, variant=0, stream=0):
+    _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, w16, N, scratch, nxt, logits or None, variant,
                                       stream or None))
 
 

@@ -196,18 +196,17 @@ FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, 
                           uint16_t* out16_lo_dev, float* out32_dev, int* err_dev, void* stream);
 /* Kernel (4): Q8_0 GEMM C = A . W^T (compute/llm_ops_gpu.cpp:53-55,149,177-180,206).
  * A [M][K] as an f16 pair a16 + a16_lo (a16_lo may be NULL: plain f16 activations);
- * W in the library's repacked form: q [N][K] (the Q8_0 integers held exactly as f16)
- * and d [K/32][N] f16 (fa_op_repack_q8 builds both from GGUF blocks); each 32-block's
- * partial sum is scaled by its d in fp32. n_split > 1 writes partials [n_split][M][N]
- * (their sum is C). variant: 0 = tcgen05 kernel, 1 = mma.sync kernel. */
-FA_API int fa_op_repack_q8(const uint8_t* gguf_q8_dev, int N, int K, uint16_t* q_dev, uint16_t* d_dev, void* stream);
-FA_API int fa_op_q8_gemm(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K, const uint16_t* q_dev,
-                         const uint16_t* d_dev, int N, int n_split, float* c_dev, int variant, void* stream);
+ * W [N][K] f16 = f16(d * q) per Q8_0 block (fa_op_repack_q8 builds it from GGUF blocks).
+ * n_split > 1 writes partials [n_split][M][N] (their sum is C).
+ * variant: 0 = tcgen05 kernel (N a multiple of 128), 1 = mma.sync kernel. */
+FA_API int fa_op_repack_q8(const uint8_t* gguf_q8_dev, int N, int K, uint16_t* w16_dev, void* stream);
+FA_API int fa_op_q8_gemm(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K, const uint16_t* w16_dev,
+                         int N, int n_split, float* c_dev, int variant, void* stream);
 /* lm_head with fused argmax: next [M] = first column of each row's maximum; logits optional. */
 FA_API size_t fa_op_argmax_scratch_bytes(int M, int N);
 FA_API int fa_op_q8_gemm_argmax(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K,
-                                const uint16_t* q_dev, const uint16_t* d_dev, int N, void* scratch_dev, int* next_dev,
-                                float* logits_dev, int variant, void* stream);
+                                const uint16_t* w16_dev, int N, void* scratch_dev, int* next_dev, float* logits_dev,
+                                int variant, void* stream);
 
 /* ---- host-only page allocator (no GPU needed): the policy behind fa_seq_* ----
  * Lowest free page id first; compaction moves the highest live page into the lowest

@@ -36,10 +36,11 @@
 //     f32 -> f16 is round-to-nearest-even.
 //   * RoPE cos/sin: theta computed in double, cos/sin in double, rounded to f32
 //     once into a table [pos][i] (the same table the CUDA path uploads).
-//   * GEMM mode 0 (the CUDA path's arithmetic): f32 activations times the exactly
-//     dequantised weights d*q, sums in wide precision. (The CUDA path carries the
-//     activations as an f16 hi/lo pair, ~22 bits, and scales each 32-block in fp32.)
-//     Mode 2 is the ggml CPU backend's Q8_0-activation arithmetic.
+//   * GEMM mode 1 (the CUDA path's arithmetic): f32 activations times the Q8_0
+//     weights expanded once to f16, W = f16(f32(d) * q), sums in wide precision.
+//     (The CUDA path carries the activations as an f16 hi/lo pair, ~22 bits.)
+//     Mode 0 is the same with the exact weights d*q; mode 2 is the ggml CPU
+//     backend's Q8_0-activation arithmetic.
 //   * Attention scores, softmax and PV are computed in double here.
 //
 // Parity pins: the Q8_0 codec is pinned byte-for-byte against the reference
@@ -137,14 +138,16 @@ inline void rope_neox(float* y, int d, const float* cs) {
 }
 
 // ---------------------------------------------------------------- Q8_0 -------
-inline void q8_row_dequant(const uint8_t* row, int K, float* out) {
+// d*q is exact in f32; with round16 it is then rounded to f16 (nearest-even).
+inline void q8_row_dequant(const uint8_t* row, int K, float* out, bool round16 = false) {
     for (int b = 0; b < K / QK; ++b) {
         const uint8_t* blk = row + (size_t)b * QB;
         uint16_t dh; std::memcpy(&dh, blk, 2);
         const float d = h2f(dh);
         const int8_t* q = (const int8_t*)(blk + 2);
         for (int j = 0; j < QK; ++j) {
-            out[b * QK + j] = d * (float)q[j];  // exact in f32
+            const float w = d * (float)q[j];
+            out[b * QK + j] = round16 ? h2f(f2h(w)) : w;
         }
     }
 }
@@ -224,7 +227,8 @@ void or_rmsnorm(const float* x, const float* w, int rows, int n, float eps, floa
 }
 
 // ---- Q8_0 matmul: C[M][N] = A[M][K] . W[N][K]^T --------------------------------
-// mode 0: f32 activations x exactly dequantised weights, double accumulation (CUDA path).
+// mode 0: f32 activations x exactly dequantised weights d*q, double accumulation.
+// mode 1: f32 activations x f16(d*q) weights, double accumulation (the CUDA path).
 // mode 2: ggml CPU backend: Q8_0 activations, integer block dots, f32 block sum.
 void or_gemm_q8(const float* A, int M, int K, const uint8_t* W, int N, int mode, float* C) {
     const int nb = K / QK;
@@ -258,7 +262,7 @@ void or_gemm_q8(const float* A, int M, int K, const uint8_t* W, int N, int mode,
         std::vector<float> w(K);
 #pragma omp for schedule(dynamic, 16)
         for (int n = 0; n < N; ++n) {
-            q8_row_dequant(W + (size_t)n * nb * QB, K, w.data());
+            q8_row_dequant(W + (size_t)n * nb * QB, K, w.data(), mode == 1);
             for (int m = 0; m < M; ++m) {
                 const float* a = Ause + (size_t)m * K;
                 double s[8] = {0, 0, 0, 0, 0, 0, 0, 0};

@@ -23,7 +23,8 @@ _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 _lib = None
 
 # GEMM arithmetic modes of or_gemm_q8 / or_decoder_forward.
-MODE_EXACT = 0      # f32 activations x exactly dequantised weights (the CUDA path's arithmetic)
+MODE_EXACT = 0      # f32 activations x exactly dequantised weights d*q
+MODE_W16 = 1        # f32 activations x f16(d*q) weights: the CUDA path's arithmetic
 MODE_GGML_CPU = 2   # ggml CPU backend: Q8_0 activations, integer block dots
 
 QK8_0 = 32
@@ -140,7 +141,7 @@ def rmsnorm(x: np.ndarray, w: Optional[np.ndarray], eps: float = 1e-5) -> np.nda
     return out
 
 
-def gemm_q8(a: np.ndarray, w_q8: np.ndarray, n: int, mode: int = MODE_EXACT) -> np.ndarray:
+def gemm_q8(a: np.ndarray, w_q8: np.ndarray, n: int, mode: int = MODE_W16) -> np.ndarray:
     a = _c(a, np.float32)
     M, K = a.shape
     w_q8 = _c(w_q8, np.uint8)
@@ -226,7 +227,7 @@ class OracleDecoder:
     """
 
     def __init__(self, cfg, weights, n_pages: int, max_seqs: int, max_pages_per_seq: int,
-                 max_pos: int, mode: int = MODE_EXACT):
+                 max_pos: int, mode: int = MODE_W16):
         self.cfg = cfg
         self.mode = mode
         L = cfg["n_layers"]

@@ -1,6 +1,6 @@
 """GPU parity of the whole decoder behind the reference-facing C ABI (fa_ctx).
 
-The oracle runs the same rows with the same arithmetic (GEMM mode 0, exact); logits must be
+The oracle runs the same rows with the same arithmetic (GEMM mode 1: f16(d*q) weights, exact activations); logits must be
 within 2e-2 max-abs / 1e-3 relative RMS, greedy ids must agree on >= 99% of steps and
 block tables must be identical. Mirrors the reference's test_llm.cpp flow: prefill
 the prompt, then greedy decode (compute/gpu_runner.hpp, pipeline/pipeline.cpp:434-451).
@@ -40,7 +40,7 @@ def test_prefill_and_decode_match_oracle(torch_cuda, small_w):
     w = small_w
     dec = _decoder(w, CFG)
     od = oracle.OracleDecoder(CFG, w, n_pages=256, max_seqs=16, max_pages_per_seq=MAX_CTX // 16, max_pos=MAX_CTX,
-                              mode=oracle.MODE_EXACT)
+                              mode=oracle.MODE_W16)
     rng = np.random.default_rng(0)
     emb = _embed_table(w, CFG)
     sids = [dec.seq_open(MAX_CTX) for _ in range(3)]
@@ -249,7 +249,7 @@ def test_qwen3_06b_greedy_decode_batch1(torch_cuda):
     w = fa_synth.make_weights(cfg, seed=5, d_range=(0.0002, 0.004))
     dec = _decoder(w, cfg, n_pages=64, max_seqs=2, max_rows=128)
     od = oracle.OracleDecoder(cfg, w, n_pages=64, max_seqs=2, max_pages_per_seq=MAX_CTX // 16, max_pos=MAX_CTX,
-                              mode=oracle.MODE_EXACT)
+                              mode=oracle.MODE_W16)
     rng = np.random.default_rng(6)
     emb = _embed_table(w, cfg)
     rows = np.concatenate([emb[rng.integers(0, cfg["vocab"], 20)], rng.standard_normal((82, cfg["hidden"])),
@@ -279,7 +279,7 @@ def test_qwen3_06b_benchmark_scale_rel_rms(torch_cuda):
     w = fa_synth.make_weights(cfg, seed=8)
     dec = _decoder(w, cfg, n_pages=64, max_seqs=4, max_rows=128)
     od = oracle.OracleDecoder(cfg, w, n_pages=64, max_seqs=4, max_pages_per_seq=MAX_CTX // 16, max_pos=MAX_CTX,
-                              mode=oracle.MODE_EXACT)
+                              mode=oracle.MODE_W16)
     rng = np.random.default_rng(9)
     sids = [dec.seq_open(MAX_CTX) for _ in range(4)]
     for s in sids:

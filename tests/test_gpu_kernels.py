@@ -209,22 +209,23 @@ def test_paged_attention_full_size_batch128_ctx2048(torch_cuda):
 
 # ------------------------------------------------------------------- kernel 4 --
 def _q8_device(torch, rng, N, K):
+    """Random Q8_0 weights: GGUF bytes on the host, f16(d * q) [N][K] on the device."""
     raw = fa_synth.q8_0_random(rng, N, K)
     d_raw = dev(torch, raw)
-    q = torch.zeros((N, K), dtype=torch.int16, device="cuda")       # f16 bit patterns
-    d = torch.zeros((K // 32, N), dtype=torch.int16, device="cuda")
-    fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, q.data_ptr(), d.data_ptr())
-    return raw, q, d
+    w16 = torch.zeros((N, K), dtype=torch.int16, device="cuda")       # f16 bit patterns
+    fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, w16.data_ptr())
+    return raw, w16
 
 
-def test_repack_layout(torch_cuda):
+def test_repack_rounds_d_times_q_to_f16(torch_cuda):
     rng = np.random.default_rng(0)
-    raw, q, d = _q8_device(torch_cuda, rng, 128, 256)
+    raw, w16 = _q8_device(torch_cuda, rng, 128, 256)
     torch_cuda.cuda.synchronize()
     blocks = raw.reshape(128, 8, 34)
-    qf = oracle.f16_bits_to_f32(q.cpu().numpy().view(np.uint16))
-    assert np.array_equal(qf, blocks[:, :, 2:].view(np.int8).reshape(128, 256).astype(np.float32))
-    assert np.array_equal(d.cpu().numpy().view(np.uint16).T, blocks[:, :, :2].copy().view(np.uint16)[:, :, 0])
+    d = oracle.f16_bits_to_f32(blocks[:, :, :2].copy().view(np.uint16)[:, :, 0])
+    q = blocks[:, :, 2:].view(np.int8).astype(np.float32)
+    want = oracle.f32_to_f16_bits((d[:, :, None] * q).reshape(128, 256))
+    assert np.array_equal(w16.cpu().numpy().view(np.uint16), want)
 
 
 def test_tcgen05_gemm_single_tile(torch_cuda):
@@ -232,14 +233,14 @@ def test_tcgen05_gemm_single_tile(torch_cuda):
     torch = torch_cuda
     rng = np.random.default_rng(42)
     M, N, K = 128, 128, 64
-    raw, q, d = _q8_device(torch, rng, N, K)
+    raw, w16 = _q8_device(torch, rng, N, K)
     a = rng.standard_normal((M, K)).astype(np.float32)
     hi, lo, a_eff = _split_f16(a)
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     c = torch.zeros((1, M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, 1, c.data_ptr(), 0)
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, 1, c.data_ptr(), 0)
     torch.cuda.synchronize()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_EXACT)
+    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
     got = c[0].cpu().numpy()
     assert rel_rms(got, ref) < 2e-6, rel_rms(got, ref)
 
@@ -256,26 +257,25 @@ def _split_f16(x):
     (1, 1024, 1024, 1), (5, 4096, 1024, 4), (16, 1024, 2048, 8), (17, 2048, 1024, 2),
     (64, 6144, 1024, 4), (128, 1024, 3072, 12), (200, 1024, 1024, 1), (300, 512, 2048, 2),
 ])
-def test_q8_gemm_matches_oracle_exact(torch_cuda, M, N, K, split, variant):
+def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
     torch = torch_cuda
     rng = np.random.default_rng(M * 7 + N + K)
-    raw, q, d = _q8_device(torch, rng, N, K)
+    raw, w16 = _q8_device(torch, rng, N, K)
     a = (rng.standard_normal((M, K)) * 3).astype(np.float32)
     hi, lo, a_eff = _split_f16(a)
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     c = torch.zeros((split, M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N, split, c.data_ptr(),
-                      variant)
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, split, c.data_ptr(), variant)
     torch.cuda.synchronize()
     got = c.sum(0).cpu().numpy()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_EXACT)
+    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
     assert rel_rms(got, ref) < 2e-6, rel_rms(got, ref)
     assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
     # without the lo plane the result is the f16-activation product
     c.zero_()
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), 0, M, K, q.data_ptr(), d.data_ptr(), N, split, c.data_ptr(), variant)
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), 0, M, K, w16.data_ptr(), N, split, c.data_ptr(), variant)
     torch.cuda.synchronize()
-    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, oracle.MODE_EXACT)
+    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, oracle.MODE_W16)
     assert rel_rms(c.sum(0).cpu().numpy(), ref16) < 2e-6
 
 
@@ -284,16 +284,16 @@ def test_lm_head_argmax_full_vocab(torch_cuda, variant):
     torch = torch_cuda
     rng = np.random.default_rng(3)
     M, N, K = 7, 151936, 1024
-    raw, q, d = _q8_device(torch, rng, N, K)
+    raw, w16 = _q8_device(torch, rng, N, K)
     hi, lo, a_eff = _split_f16(rng.standard_normal((M, K)).astype(np.float32))
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
     nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
     logits = torch.zeros((M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm_argmax(d_hi.data_ptr(), d_lo.data_ptr(), M, K, q.data_ptr(), d.data_ptr(), N,
+    fa_dec.op_q8_gemm_argmax(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N,
                              scratch.data_ptr(), nxt.data_ptr(), logits.data_ptr(), variant)
     torch.cuda.synchronize()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_EXACT)
+    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
     assert rel_rms(logits.cpu().numpy(), ref) < 2e-6
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(ref))
     # the kernel's argmax is the first maximum of its own logits
@@ -315,14 +315,13 @@ def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2, variant):
         blocks[j, :, 2:] = np.uint8(127)
     raw = blocks.reshape(N, nb * 34)
     d_raw = dev(torch, raw)
-    q = torch.zeros((N, K), dtype=torch.int16, device="cuda")
-    d = torch.zeros((nb, N), dtype=torch.int16, device="cuda")
-    fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, q.data_ptr(), d.data_ptr())
+    w16 = torch.zeros((N, K), dtype=torch.int16, device="cuda")
+    fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, w16.data_ptr())
     a16 = oracle.f32_to_f16_bits(np.full((M, K), 0.5, np.float32))
     d_a = dev(torch, _i16(a16))
     scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
     nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
-    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), 0, M, K, q.data_ptr(), d.data_ptr(), N, scratch.data_ptr(),
-                             nxt.data_ptr(), 0, variant)
+    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), 0, M, K, w16.data_ptr(), N, scratch.data_ptr(), nxt.data_ptr(), 0,
+                             variant)
     torch.cuda.synchronize()
     assert nxt.cpu().numpy().tolist() == [j1] * M

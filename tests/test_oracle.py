@@ -58,7 +58,7 @@ def _golden_decoder(mode):
     return h, cfg, w, od
 
 
-@pytest.mark.parametrize("mode,tol", [(oracle.MODE_EXACT, 1e-3)])
+@pytest.mark.parametrize("mode,tol", [(oracle.MODE_EXACT, 1e-3), (oracle.MODE_W16, 2e-3)])
 def test_decoder_logits_match_qwen3(mode, tol):
     h, cfg, w, od = _golden_decoder(mode)
     od.seq_open(0)
@@ -74,8 +74,8 @@ def test_decoder_logits_match_qwen3(mode, tol):
 
 
 def test_prefill_equals_stepwise():
-    h, cfg, w, od = _golden_decoder(oracle.MODE_EXACT)
-    od2 = oracle.OracleDecoder(cfg, w, n_pages=64, max_seqs=4, max_pages_per_seq=16, max_pos=4096, mode=oracle.MODE_EXACT)
+    h, cfg, w, od = _golden_decoder(oracle.MODE_W16)
+    od2 = oracle.OracleDecoder(cfg, w, n_pages=64, max_seqs=4, max_pages_per_seq=16, max_pos=4096, mode=oracle.MODE_W16)
     toks = np.random.default_rng(3).integers(0, cfg["vocab"], 21)
     od.seq_open(1)
     od2.seq_open(1)
@@ -131,3 +131,20 @@ def test_allocator_and_compaction_restatement():
     live = [0, 1, 2, 3, 5]
     src, dst = oracle.compaction_plan(live, 10)
     assert (src, dst) == ([5], [4])
+
+
+def test_f16_weights_stay_close_to_exact_weights():
+    """Mode 1 (the CUDA path: weights rounded once to f16) against mode 0 (exact d*q)
+    on the golden model: the fixed weight rounding moves the logits by far less than
+    the reference's own Q8_0 activation quantisation (mode 2) does."""
+    outs = {}
+    for mode in (oracle.MODE_EXACT, oracle.MODE_W16, oracle.MODE_GGML_CPU):
+        h, cfg, w, od = _golden_decoder(mode)
+        od.seq_open(0)
+        emb = oracle.bf16_bits_to_f32(w["llm.model.embed_tokens.weight"][2]).reshape(cfg["vocab"], cfg["hidden"])
+        rows = np.concatenate([emb[h["pre"]], h["audio"], emb[h["suf"]]], 0)
+        outs[mode], _ = od.forward([0] * 16, embeds=rows)
+    ref = outs[oracle.MODE_EXACT]
+    rr = lambda a: float(np.sqrt(((a - ref) ** 2).mean() / (ref ** 2).mean()))
+    assert rr(outs[oracle.MODE_W16]) < 2e-3
+    assert rr(outs[oracle.MODE_W16]) < 0.2 * rr(outs[oracle.MODE_GGML_CPU])
