@@ -72,13 +72,15 @@ def test_prefill_and_decode_match_oracle(torch_cuda, small_w):
         bt = dec.block_table(s)
         assert np.array_equal(bt, od.block_table[s, :len(bt)])
         assert dec.seq_length(s) == od.seq_len[s]
-    # K/V pages: same bytes up to f16 rounding of values whose f32 inputs differ in the last bit
+    # K/V pages: layer 0 sees identical inputs, so its pages match byte for byte except
+    # where an fp32 accumulation-order difference straddles an f16 rounding boundary;
+    # deeper layers inherit the upstream differences and are compared by value.
     used = np.concatenate([dec.block_table(s) for s in sids])
     for layer in (0, CFG["n_layers"] - 1):
         got = dec.kv_read_pages(layer, used)
         ref = od.pool[layer, used]
-        same = np.mean(got == ref)
-        assert same > 0.95, same
+        if layer == 0:
+            assert np.mean(got == ref) > 0.98, np.mean(got == ref)
         assert rel_rms(oracle.f16_bits_to_f32(got), oracle.f16_bits_to_f32(ref)) < 1e-3
     dec.close()
 

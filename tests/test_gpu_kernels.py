@@ -242,7 +242,7 @@ def test_tcgen05_gemm_single_tile(torch_cuda):
     torch.cuda.synchronize()
     ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
     got = c[0].cpu().numpy()
-    assert rel_rms(got, ref) < 2e-6, rel_rms(got, ref)
+    assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
 
 
 def _split_f16(x):
@@ -269,14 +269,15 @@ def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
     torch.cuda.synchronize()
     got = c.sum(0).cpu().numpy()
     ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
-    assert rel_rms(got, ref) < 2e-6, rel_rms(got, ref)
+    # fp32 accumulation over K (up to 3072) against a double-precision sum: ~sqrt(K) * 2^-24
+    assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
     assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
     # without the lo plane the result is the f16-activation product
     c.zero_()
     fa_dec.op_q8_gemm(d_hi.data_ptr(), 0, M, K, w16.data_ptr(), N, split, c.data_ptr(), variant)
     torch.cuda.synchronize()
     ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, oracle.MODE_W16)
-    assert rel_rms(c.sum(0).cpu().numpy(), ref16) < 2e-6
+    assert rel_rms(c.sum(0).cpu().numpy(), ref16) < 5e-6
 
 
 @pytest.mark.parametrize("variant", [0, 1])
@@ -294,7 +295,7 @@ def test_lm_head_argmax_full_vocab(torch_cuda, variant):
                              scratch.data_ptr(), nxt.data_ptr(), logits.data_ptr(), variant)
     torch.cuda.synchronize()
     ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
-    assert rel_rms(logits.cpu().numpy(), ref) < 2e-6
+    assert rel_rms(logits.cpu().numpy(), ref) < 5e-6
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(ref))
     # the kernel's argmax is the first maximum of its own logits
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(logits.cpu().numpy()))
