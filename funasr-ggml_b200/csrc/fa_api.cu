@@ -175,6 +175,12 @@ static int set_err(const fa_ctx* cctx, int code, const std::string& msg) {
     return code;
 }
 
+namespace fa {
+// Records a context-free error (read back with fa_last_error(NULL)) for entry points
+// defined in other translation units.
+int report_op_error(int code, const char* msg) { return set_err(nullptr, code, msg); }
+}  // namespace fa
+
 template <typename T>
 static int dev_alloc(fa_ctx* ctx, T** p, size_t bytes) {
     void* v = nullptr;

@@ -24,8 +24,11 @@
 // Roofline: HBM. Algorithmic bytes per (row, layer) = n_kv * 8 heads * 2 * 128 * 2 B
 // = n_kv * 4096 B; compute is 4 flop per byte read.
 #include "fa_kernels.cuh"
+#include "funasr_dec.h"
 
 #include <cmath>
+#include <mutex>
+#include <string>
 
 namespace fa {
 
@@ -358,4 +361,80 @@ void launch_attn_combine(const AttnArgs& a, cudaStream_t s) {
     launch_k(attn_combine_kernel, dim3(a.M * a.Hq), dim3(128), 0, s, a);
 }
 
+// ---------------------------------------------------- allocation-free variant --
+// For callers that may not allocate device memory themselves (a host runtime that
+// owns every allocation through its own pool, a plugin loaded into a process that
+// forbids cudaMalloc after start-up, code that must not allocate while a graph is
+// being built around it): the split-K partials live in one buffer compiled into the
+// library. Every GPU that loads the library holds it until the process exits.
+constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;   // 8 MiB: M * n_splits <= 1008
+
+int report_op_error(int code, const char* msg);   // fa_api.cu
+
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};   // device address of g_attn_scratch per device
+}  // namespace
+
 }  // namespace fa
+
+// The first call on a device looks up the buffer's device address there
+// (cudaGetSymbolAddress) and sets the kernel's shared-memory limit; make that first
+// call before any stream capture. All calls share the one buffer, so calls whose
+// work overlaps on the GPU (other streams, other host threads) race on it. Nothing
+// in it needs to start at zero: a call writes every partial it later reads.
+extern "C" FA_API int fa_op_paged_attention_noalloc(const float* q, int M, const int* pos, const int* slot,
+                                                    const int* bt, int bt_stride, int n_pages,
+                                                    const uint16_t* pool_layer, int pps, int n_splits,
+                                                    uint16_t* out16, uint16_t* out16_lo, float* out32, int* err,
+                                                    void* stream) {
+    using namespace fa;
+    if (!q || !pos || !slot || !bt || !pool_layer || M <= 0 || pps <= 0 || n_splits <= 0 || (!out16 && !out32))
+        return report_op_error(FA_ERR_INVALID_ARG, "null or non-positive argument");
+    const int Hq = 16, Hkv = 8;
+    const size_t need = n_splits > 1 ? (size_t)M * Hq * n_splits * (D + 2) * sizeof(float) : 0;
+    if (need > kNoAllocScratchBytes) {
+        const std::string msg = "fa_op_paged_attention_noalloc: " + std::to_string(M) + " rows x " +
+                                std::to_string(n_splits) + " splits need " + std::to_string(need) +
+                                " bytes of split-K scratch; the built-in buffer holds " +
+                                std::to_string(kNoAllocScratchBytes) + " (M * n_splits <= 1008)";
+        return report_op_error(FA_ERR_CAPACITY, msg.c_str());
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return report_op_error(FA_ERR_CUDA, "fa_op_paged_attention_noalloc: no current CUDA device");
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void* p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+            if (e != cudaSuccess || !p) {
+                const std::string msg = std::string("fa_op_paged_attention_noalloc: cudaGetSymbolAddress: ") +
+                                        cudaGetErrorString(e);
+                return report_op_error(FA_ERR_CUDA, msg.c_str());
+            }
+            configure_attention();
+            g_noalloc_ptr[dev] = p;
+        }
+        base = g_noalloc_ptr[dev];
+    }
+    AttnArgs a{};
+    a.q = q; a.pool_layer = reinterpret_cast<const __half*>(pool_layer); a.block_table = bt; a.bt_stride = bt_stride;
+    a.n_pages = n_pages; a.slot = slot; a.pos = pos; a.M = M; a.Hq = Hq; a.Hkv = Hkv; a.pages_per_split = pps;
+    a.n_splits = n_splits;
+    a.part_o = reinterpret_cast<float*>(base);
+    a.part_ml = a.part_o + (size_t)M * Hq * n_splits * D;
+    a.out16 = reinterpret_cast<__half*>(out16); a.out16_lo = reinterpret_cast<__half*>(out16_lo);
+    a.out32 = out32; a.err = err;
+    launch_paged_attention(a, (cudaStream_t)stream);
+    if (n_splits > 1) launch_attn_combine(a, (cudaStream_t)stream);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        const std::string msg = std::string("fa_op_paged_attention_noalloc: launch: ") + cudaGetErrorString(e);
+        return report_op_error(FA_ERR_CUDA, msg.c_str());
+    }
+    return FA_OK;
+}

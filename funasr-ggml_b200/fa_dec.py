@@ -105,6 +105,7 @@ def lib():
         "fa_op_kv_append": ([_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P], _I),
         "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
         "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P], _I),
+        "fa_op_paged_attention_noalloc": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P], _I),
         "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _I, _I, _P, _I, _P], _I),
         "fa_op_argmax_scratch_bytes": ([_I, _I], ctypes.c_size_t),
@@ -337,6 +338,14 @@ def op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_spl
     _check(lib().fa_op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits,
                                        scratch or None, out16 or None, out16_lo or None, out32 or None, err or None,
                                        stream or None))
+
+
+def op_paged_attention_noalloc(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits, out16=0, out32=0,
+                               err=0, stream=0, out16_lo=0):
+    """fa_op_paged_attention with the library's built-in scratch buffer (allocates nothing)."""
+    _check(lib().fa_op_paged_attention_noalloc(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits,
+                                               out16 or None, out16_lo or None, out32 or None, err or None,
+                                               stream or None))
 
 
 def op_repack_q8(raw, N, K, w16, stream=0):

@@ -194,6 +194,19 @@ FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, 
                           const int* block_table_dev, int bt_stride, int n_pages, const uint16_t* pool_layer_dev,
                           int pages_per_split, int n_splits, void* scratch_dev, uint16_t* out16_dev,
                           uint16_t* out16_lo_dev, float* out32_dev, int* err_dev, void* stream);
+/* fa_op_paged_attention without the scratch argument: nothing is allocated, by the
+ * library or the caller. No counterpart in the reference; it exists for callers that
+ * cannot call cudaMalloc (an embedding runtime that owns all device memory, a process
+ * that forbids allocation once started). The split-K partials go to one 8 MiB buffer
+ * built into the library (held on every GPU that loads it until exit), so
+ * M * n_splits <= 1008 (FA_ERR_CAPACITY otherwise). The first call on a device sets
+ * the buffer up; make it before any stream capture. Calls share the buffer: calls
+ * that overlap on the GPU race. */
+FA_API int fa_op_paged_attention_noalloc(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
+                                         const int* block_table_dev, int bt_stride, int n_pages,
+                                         const uint16_t* pool_layer_dev, int pages_per_split, int n_splits,
+                                         uint16_t* out16_dev, uint16_t* out16_lo_dev, float* out32_dev, int* err_dev,
+                                         void* stream);
 /* Kernel (4): Q8_0 GEMM C = A . W^T (compute/llm_ops_gpu.cpp:53-55,149,177-180,206).
  * A [M][K] as an f16 pair a16 + a16_lo (a16_lo may be NULL: plain f16 activations);
  * W [N][K] f16 = f16(d * q) per Q8_0 block (fa_op_repack_q8 builds it from GGUF blocks).
