@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between kernels")
+    ap.add_argument("--workload", default="decode", choices=["decode", "attention"],
+                    help="attention: kernel (2) alone over one layer's pages at the same batch and context")
     return ap.parse_args()
 
 
@@ -247,6 +249,82 @@ def run_ours(a):
     fa_multi.shutdown()
 
 
+# ------------------------------------------------------ attention alone --
+def run_attention(a):
+    """Paged GQA decode attention (plus its split combine) of one layer on its own:
+    B rows at `ctx` tokens, two page pools used alternately (each ~1 GB at B=128,
+    ctx 2048, so nothing stays in L2 between launches), the decoder's split choice,
+    f16 hi/lo output as the decoder writes it. Prints the achieved HBM GB/s."""
+    import torch
+    import fa_dec
+
+    rank, local, world = fa_multi.init("nccl")
+    torch.cuda.set_device(local)
+    B, ctx, K, W = a.batch, a.ctx, a.steps, a.warmup
+    n_kv = np.full(B, ctx, np.int32)
+    pages = (ctx + 15) // 16
+    n_pages = B * pages
+    rng = np.random.default_rng(rank)
+    dev = torch.device("cuda", local)
+    pools = [torch.randn(n_pages * 8 * 2 * 16 * 128, dtype=torch.float16, device=dev).view(torch.int16)
+             for _ in range(2)]
+    bts = [torch.from_numpy(rng.permutation(n_pages).reshape(B, pages).astype(np.int32)).to(dev) for _ in range(2)]
+    q = (torch.randn(B, 16, 128, device=dev) * 0.3).contiguous()
+    pos = torch.from_numpy(n_kv - 1).to(dev)
+    slot = torch.arange(B, dtype=torch.int32, device=dev)
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    pps, n_splits = fa_dec.op_attention_plan(n_kv, n_sm)
+    scratch = torch.empty(max(fa_dec.op_attention_scratch_bytes(B, n_splits), 16), dtype=torch.uint8, device=dev)
+    out16 = torch.empty(B, 2048, dtype=torch.int16, device=dev)
+    out_lo = torch.empty_like(out16)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def launch(i):
+        fa_dec.op_paged_attention(q.data_ptr(), B, pos.data_ptr(), slot.data_ptr(), bts[i % 2].data_ptr(), pages,
+                                  n_pages, pools[i % 2].data_ptr(), pps, n_splits, scratch.data_ptr(),
+                                  out16=out16.data_ptr(), out16_lo=out_lo.data_ptr(), err=err.data_ptr(),
+                                  stream=stream)
+
+    for i in range(W):
+        launch(i)
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        launch(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    fa_multi.barrier()
+    assert int(err.item()) == 0, "attention reported a device error"
+    ms = fa_multi.reduce(e0.elapsed_time(e1), "max")
+    bytes_per_launch = B * ctx * KV_BYTES_PER_TOKEN_LAYER
+    gbs = bytes_per_launch * K * world / (ms / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+    all_clocks = fa_multi.gather(clocks)
+    if rank == 0:
+        reasons = sorted(set(r for c in all_clocks for r in c.get("reasons", [])))
+        print(json.dumps({
+            "metric": "paged-attn HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic: N(0,1) f16 pages, random block tables",
+            "config": {"workload": f"paged GQA decode attention of one layer, {B} rows at {ctx} tokens, "
+                                   f"16q/8kv x 128, f16 pages of 16 tokens", "batch_per_gpu": B, "ctx": ctx,
+                       "pages_per_split": pps, "n_splits": n_splits,
+                       "l2": "no flush: two ~1 GB page pools used alternately"},
+            "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / world / peak, "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch},
+            "gpu_launches": K * (2 if n_splits > 1 else 1),
+            "clocks": {"sm_mhz": all_clocks[0].get("sm_mhz"), "sm_max_mhz": all_clocks[0].get("sm_max_mhz"),
+                       "reasons": reasons},
+        }), flush=True)
+    fa_multi.shutdown()
+
+
 # -------------------------------------------------------------- reference --
 def run_reference(a):
     """The reference's CPU path (ggml) cannot be built here, so its restatement (the
@@ -300,5 +378,7 @@ if __name__ == "__main__":
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "attention":
+        run_attention(args)
     else:
         run_ours(args)

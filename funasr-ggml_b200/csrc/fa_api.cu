@@ -701,6 +701,20 @@ struct StepPlan {
 
 }  // namespace
 
+// Attention work split for rows whose contexts total `total_pages` pages (longest:
+// max_pages): about 4 CTAs per SM over all (page, KV head) work, 4..64 pages per CTA
+// (a multiple of 4), and at most max_splits splits per row.
+static void attention_split(long long total_pages, int max_pages, int n_sm, int max_splits, int* pps_out,
+                            int* n_splits_out) {
+    const long long target = 4LL * n_sm;
+    long long pps = (total_pages * kHkv + target - 1) / target;
+    pps = std::min<long long>(64, std::max<long long>(4, pps));
+    pps = std::max<long long>(pps, (max_pages + max_splits - 1) / max_splits);
+    pps = (pps + 3) / 4 * 4;
+    *pps_out = (int)pps;
+    *n_splits_out = (max_pages + *pps_out - 1) / *pps_out;
+}
+
 static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits) {
     const fa_model_desc& d = ctx->d;
     StepPlan p;
@@ -720,14 +734,7 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
         total_pages += pg;
         max_pages = std::max(max_pages, pg);
     }
-    // aim for about 4 CTAs per SM over all (page, KV head) work; 4..64 pages per CTA
-    long long target = 4LL * ctx->n_sm;
-    long long pps = (total_pages * kHkv + target - 1) / target;
-    pps = std::min<long long>(64, std::max<long long>(4, pps));
-    pps = std::max<long long>(pps, (max_pages + ctx->att_max_splits - 1) / ctx->att_max_splits);
-    pps = (pps + 3) / 4 * 4;
-    p.pps = (int)pps;
-    p.n_splits = (max_pages + p.pps - 1) / p.pps;
+    attention_split(total_pages, max_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits);
     p.embeds = embeds;
     p.logits = logits;
     p.prof = ctx->prof;
@@ -1299,6 +1306,21 @@ extern "C" int fa_op_kv_append(const uint16_t* k, const uint16_t* v, int M, int 
     a.n_pages = n_pages; a.pool = reinterpret_cast<__half*>(pool); a.err = err;
     fa::launch_kv_append_raw(a, (cudaStream_t)stream);
     OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages_per_split, int* n_splits) {
+    if (!n_kv || M <= 0 || n_sm <= 0 || !pages_per_split || !n_splits)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_attention_plan: bad argument");
+    long long total = 0;
+    int max_pages = 1;
+    for (int i = 0; i < M; ++i) {
+        if (n_kv[i] <= 0) return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_attention_plan: n_kv must be > 0");
+        const int pg = (n_kv[i] + fa::kPageTokens - 1) / fa::kPageTokens;
+        total += pg;
+        max_pages = std::max(max_pages, pg);
+    }
+    attention_split(total, max_pages, n_sm, 64, pages_per_split, n_splits);
     return FA_OK;
 }
 

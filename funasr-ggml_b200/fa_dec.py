@@ -105,6 +105,7 @@ def lib():
         "fa_op_kv_append": ([_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P], _I),
         "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
         "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P], _I),
+        "fa_op_attention_plan": ([_P, _I, _I, _P, _P], _I),
         "fa_op_paged_attention_noalloc": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P], _I),
         "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _I, _I, _P, _I, _P], _I),
@@ -338,6 +339,14 @@ def op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_spl
     _check(lib().fa_op_paged_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits,
                                        scratch or None, out16 or None, out16_lo or None, out32 or None, err or None,
                                        stream or None))
+
+
+def op_attention_plan(n_kv, n_sm=148):
+    """(pages_per_split, n_splits) the decoder picks for rows with contexts n_kv."""
+    a = np.ascontiguousarray(n_kv, np.int32)
+    pps, ns = ctypes.c_int(), ctypes.c_int()
+    _check(lib().fa_op_attention_plan(a.ctypes.data, len(a), n_sm, ctypes.byref(pps), ctypes.byref(ns)))
+    return pps.value, ns.value
 
 
 def op_paged_attention_noalloc(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits, out16=0, out32=0,

@@ -190,6 +190,8 @@ FA_API int fa_op_kv_append(const uint16_t* k_dev, const uint16_t* v_dev, int M, 
  * the form the next GEMM reads). scratch_dev holds the split-K partials:
  * fa_op_attention_scratch_bytes(M, n_splits) bytes (may be NULL when n_splits == 1). */
 FA_API size_t fa_op_attention_scratch_bytes(int M, int n_splits);
+/* The split the decoder uses for rows with contexts n_kv[M] on n_sm SMs (host only). */
+FA_API int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages_per_split, int* n_splits);
 FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
                           const int* block_table_dev, int bt_stride, int n_pages, const uint16_t* pool_layer_dev,
                           int pages_per_split, int n_splits, void* scratch_dev, uint16_t* out16_dev,
