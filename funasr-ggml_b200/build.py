@@ -23,7 +23,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libfunasr_dec.so")
 INCLUDE = os.path.join(ROOT, "include")
 
-SOURCES = ["fa_api.cu", "k_append.cu", "k_attention.cu", "k_gemm.cu", "k_gemm_tc.cu", "k_small.cu"]
+SOURCES = ["fa_api.cu", "k_append.cu", "k_attention.cu", "k_gemm.cu", "k_gemm_tc.cu", "k_small.cu", "gguf_file.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I", INCLUDE, "-I", CSRC]
@@ -52,7 +52,7 @@ def _stale(out: str, deps) -> bool:
 
 
 def _compile(src: str, verbose: bool, extra) -> str:
-    obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+    obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
     cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-c", os.path.join(CSRC, src), "-o", obj]
     if verbose:
         print(" ".join(cmd), flush=True)
@@ -66,7 +66,7 @@ def _compile(src: str, verbose: bool, extra) -> str:
 
 def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     os.makedirs(BUILD, exist_ok=True)
-    objs = [os.path.join(BUILD, s.replace(".cu", ".o")) for s in SOURCES]
+    objs = [os.path.join(BUILD, os.path.splitext(s)[0] + ".o") for s in SOURCES]
     todo = [s for s, o in zip(SOURCES, objs) if force or _stale(o, list(_deps(s)))]
     if todo:
         with cf.ThreadPoolExecutor(max_workers=min(8, len(todo))) as ex:

@@ -179,6 +179,7 @@ namespace fa {
 // Records a context-free error (read back with fa_last_error(NULL)) for entry points
 // defined in other translation units.
 int report_op_error(int code, const char* msg) { return set_err(nullptr, code, msg); }
+int report_ctx_error(const fa_ctx* ctx, int code, const char* msg) { return set_err(ctx, code, msg); }
 }  // namespace fa
 
 template <typename T>

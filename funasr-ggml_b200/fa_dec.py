@@ -105,6 +105,9 @@ def lib():
         "fa_op_kv_append": ([_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P], _I),
         "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
         "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P], _I),
+        "fa_gguf_read_desc": ([ctypes.c_char_p, _P], _I),
+        "fa_load_gguf": ([_P, ctypes.c_char_p], _I),
+        "fa_gguf_find_tensor": ([ctypes.c_char_p, ctypes.c_char_p, _P, _P, _P, _P], _I),
         "fa_op_attention_plan": ([_P, _I, _I, _P, _P], _I),
         "fa_op_paged_attention_noalloc": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P], _I),
@@ -156,6 +159,25 @@ def default_desc(**over) -> _Desc:
     return d
 
 
+def gguf_desc(path: str, **over) -> _Desc:
+    """Geometry of the decoder in a GGUF model file (fa_gguf_read_desc) plus runtime sizes."""
+    d = default_desc()
+    _check(lib().fa_gguf_read_desc(os.fsencode(path), ctypes.byref(d)))
+    for k, v in over.items():
+        setattr(d, k, v)
+    return d
+
+
+def gguf_find_tensor(path: str, name: str):
+    """(ggml type, (ne0, rows), file offset, bytes) of one tensor of a GGUF file."""
+    t = ctypes.c_int()
+    ne = (ctypes.c_int64 * 2)()
+    off, nb = ctypes.c_size_t(), ctypes.c_size_t()
+    _check(lib().fa_gguf_find_tensor(os.fsencode(path), name.encode(), ctypes.byref(t), ne, ctypes.byref(off),
+                                     ctypes.byref(nb)))
+    return t.value, (ne[0], ne[1]), off.value, nb.value
+
+
 # ------------------------------------------------------------------ Decoder --
 class Decoder:
     """One fa_ctx on one GPU: weights, the paged KV pool, sequences and steps."""
@@ -205,6 +227,10 @@ class Decoder:
             views[i].data = arr.ctypes.data
             views[i].nbytes = arr.nbytes
         self._c(lib().fa_load_weights(self.ctx, views, len(weights)))
+
+    def load_gguf(self, path: str):
+        """Load the decoder tensors (llm.*) of a GGUF model file."""
+        self._c(lib().fa_load_gguf(self.ctx, os.fsencode(path)))
 
     def set_stream(self, stream_ptr: Optional[int]):
         self._c(lib().fa_set_stream(self.ctx, stream_ptr))

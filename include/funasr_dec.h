@@ -97,6 +97,20 @@ FA_API fa_ctx* fa_create(int device, const fa_model_desc* desc); /* NULL on fail
 FA_API void fa_destroy(fa_ctx* ctx);
 FA_API const char* fa_last_error(const fa_ctx* ctx);
 FA_API int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n);
+/* ---- GGUF model files (decoder part of core/gguf_reader.hpp, ModelConfig::load_from_gguf
+ *      core/config.hpp:191-228 and ModelLoader::load_llm model/loader.cpp:91-117,210-227) ---- */
+/* Fill the geometry fields of *desc (n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn,
+ * vocab, rope_base, max_ctx) from a GGUF file's FunAsr.* keys; the runtime sizes (pages,
+ * sequences, rows) are left as they were. Host only. vocab comes from llm.lm_head.weight
+ * (151936 when the file has none, as the reference fixes it). */
+FA_API int fa_gguf_read_desc(const char* path, fa_model_desc* desc);
+/* Where a tensor sits in a GGUF file: ggml type, ne[0] and the product of the other
+ * dims, byte offset from the start of the file, bytes (0 for types the decoder does not
+ * take). Host only. */
+FA_API int fa_gguf_find_tensor(const char* path, const char* name, int* type, int64_t* ne, size_t* file_offset,
+                               size_t* nbytes);
+/* Map a GGUF file and load its llm.* tensors as fa_load_weights does. */
+FA_API int fa_load_gguf(fa_ctx* ctx, const char* path);
 /* Run the library's work on `cuda_stream` (a cudaStream_t of this device); NULL restores
  * the library's own stream. */
 FA_API int fa_set_stream(fa_ctx* ctx, void* cuda_stream);
