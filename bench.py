@@ -50,8 +50,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between kernels")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attention"],
-                    help="attention: kernel (2) alone over one layer's pages at the same batch and context")
+    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "gemm"],
+                    help="attention: kernel (2) alone over one layer's pages at the same batch and context; "
+                         "gemm: the decode step's weight GEMMs alone")
     return ap.parse_args()
 
 
@@ -325,6 +326,76 @@ def run_attention(a):
     fa_multi.shutdown()
 
 
+# ---------------------------------------------------------- GEMMs alone --
+def run_gemm(a):
+    """The weight GEMMs of one decode step on their own: for each of the 28 layers the
+    QKV (4096 x 1024), o_proj (1024 x 2048), gate/up (6144 x 1024) and down (1024 x 3072)
+    GEMMs, then lm_head (151936 x 1024) with its argmax, all at M = batch rows, with
+    each layer's own f16 weights (1.27 GB in all, so weights come from HBM as in the
+    decoder) and the decoder's split-K choice. Prints the weight-read GB/s."""
+    import torch
+    import fa_dec
+
+    rank, local, world = fa_multi.init("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = fa_synth.QWEN3_06B
+    M, K, W = a.batch, a.steps, a.warmup
+    H, F, V, L = cfg["hidden"], cfg["ffn"], cfg["vocab"], cfg["n_layers"]
+    shapes = [("qkv", 4096, H), ("o", H, 2048), ("gate_up", 2 * F, H), ("down", H, F)]
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    splits = {nm: fa_dec.op_gemm_plan(M, n, k, 0, n_sm) for nm, n, k in shapes}
+    weights = [{nm: (torch.randn(n, k, device=dev) * 0.02).half() for nm, n, k in shapes} for _ in range(L)]
+    lm = (torch.randn(V, H, device=dev) * 0.02).half()
+    a_hi = (torch.randn(M, max(F, 2048), device=dev)).half()
+    a_lo = (torch.randn(M, max(F, 2048), device=dev) * 1e-4).half()
+    part = torch.empty(max(splits.values()) * M * 2 * F, dtype=torch.float32, device=dev)
+    am_scr = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, V), dtype=torch.uint8, device=dev)
+    nxt = torch.empty(M, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def step():
+        for l in range(L):
+            for nm, n, k in shapes:
+                fa_dec.op_q8_gemm(a_hi.data_ptr(), a_lo.data_ptr(), M, k, weights[l][nm].data_ptr(), n, splits[nm],
+                                  part.data_ptr(), 0, stream)
+        fa_dec.op_q8_gemm_argmax(a_hi.data_ptr(), a_lo.data_ptr(), M, H, lm.data_ptr(), V, am_scr.data_ptr(),
+                                 nxt.data_ptr(), 0, 0, stream)
+
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = fa_multi.reduce(e0.elapsed_time(e1), "max") / K
+    wbytes = sum(n * k * 2 for _, n, k in shapes) * L + V * H * 2
+    gbs = wbytes / (ms / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode-step weight GEMMs, weight-read GB/s", "value": gbs * world, "unit": "GB/s",
+            "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 (hi/lo activations x f16(d*q) weights)",
+            "data": "synthetic: random f16 weights and activations",
+            "config": {"workload": f"{L} layers x (QKV, o_proj, gate/up, down) + lm_head with argmax at M={M}",
+                       "splits": splits, "weight_bytes": wbytes,
+                       "l2": "no flush: 1.27 GB of distinct weights per step"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "peak_kind": peak_kind},
+            "gpu_launches": K * (4 * L + 2),
+            "clocks": clocks,
+        }), flush=True)
+    fa_multi.shutdown()
+
+
 # -------------------------------------------------------------- reference --
 def run_reference(a):
     """The reference's CPU path (ggml) cannot be built here, so its restatement (the
@@ -380,5 +451,7 @@ if __name__ == "__main__":
         run_reference(args)
     elif args.workload == "attention":
         run_attention(args)
+    elif args.workload == "gemm":
+        run_gemm(args)
     else:
         run_ours(args)

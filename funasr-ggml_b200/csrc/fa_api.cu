@@ -702,18 +702,35 @@ struct StepPlan {
 
 }  // namespace
 
-// Attention work split for rows whose contexts total `total_pages` pages (longest:
-// max_pages): about 4 CTAs per SM over all (page, KV head) work, 4..64 pages per CTA
-// (a multiple of 4), and at most max_splits splits per row.
-static void attention_split(long long total_pages, int max_pages, int n_sm, int max_splits, int* pps_out,
+// Attention work split for rows of row_pages[i] pages each: the pages per CTA (a
+// multiple of 4, one per warp and round) that minimise the estimated time
+//   waves * (pps + 2) + (2 if any row is split)
+// where waves = ceil(CTAs / (2 * n_sm)) (2 CTAs fit on an SM), a CTA costs its pages
+// plus about 2 pages' worth of set-up, and merging split partials about 2 more; at
+// most max_splits splits per row.
+static void attention_split(const std::vector<int>& row_pages, int n_sm, int max_splits, int* pps_out,
                             int* n_splits_out) {
-    const long long target = 4LL * n_sm;
-    long long pps = (total_pages * kHkv + target - 1) / target;
-    pps = std::min<long long>(64, std::max<long long>(4, pps));
-    pps = std::max<long long>(pps, (max_pages + max_splits - 1) / max_splits);
-    pps = (pps + 3) / 4 * 4;
-    *pps_out = (int)pps;
-    *n_splits_out = (max_pages + *pps_out - 1) / *pps_out;
+    int max_pages = 1;
+    for (int pg : row_pages) max_pages = std::max(max_pages, pg);
+    const long long slots = 2LL * n_sm;
+    long long best_cost = -1;
+    int best = 0;
+    for (int pps = 4; pps <= 256; pps += 4) {
+        const int n_splits = (max_pages + pps - 1) / pps;
+        if (n_splits > max_splits) continue;
+        long long ctas = 0;
+        for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + pps - 1) / pps);
+        const long long waves = (ctas + slots - 1) / slots;
+        const long long cost = waves * (pps + 2) + (n_splits > 1 ? 2 : 0);
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = pps;
+        }
+        if (n_splits == 1) break;   // larger pps change nothing
+    }
+    if (!best) best = (max_pages + max_splits - 1) / max_splits;   // unreachable with pps up to 256
+    *pps_out = best;
+    *n_splits_out = (max_pages + best - 1) / best;
 }
 
 static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits) {
@@ -728,14 +745,9 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     p.s_o = pick(d.hidden, kHq * kD);
     p.s_gu = pick(2 * d.ffn, d.hidden);
     p.s_dn = pick(d.hidden, d.ffn);
-    long long total_pages = 0;
-    int max_pages = 1;
-    for (int n : row_len) {
-        const int pg = (n + fa::kPageTokens - 1) / fa::kPageTokens;
-        total_pages += pg;
-        max_pages = std::max(max_pages, pg);
-    }
-    attention_split(total_pages, max_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits);
+    std::vector<int> row_pages(row_len.size());
+    for (size_t i = 0; i < row_len.size(); ++i) row_pages[i] = (row_len[i] + fa::kPageTokens - 1) / fa::kPageTokens;
+    attention_split(row_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits);
     p.embeds = embeds;
     p.logits = logits;
     p.prof = ctx->prof;
@@ -1313,15 +1325,12 @@ extern "C" int fa_op_kv_append(const uint16_t* k, const uint16_t* v, int M, int 
 extern "C" int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages_per_split, int* n_splits) {
     if (!n_kv || M <= 0 || n_sm <= 0 || !pages_per_split || !n_splits)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_attention_plan: bad argument");
-    long long total = 0;
-    int max_pages = 1;
+    std::vector<int> row_pages((size_t)M);
     for (int i = 0; i < M; ++i) {
         if (n_kv[i] <= 0) return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_attention_plan: n_kv must be > 0");
-        const int pg = (n_kv[i] + fa::kPageTokens - 1) / fa::kPageTokens;
-        total += pg;
-        max_pages = std::max(max_pages, pg);
+        row_pages[i] = (n_kv[i] + fa::kPageTokens - 1) / fa::kPageTokens;
     }
-    attention_split(total, max_pages, n_sm, 64, pages_per_split, n_splits);
+    attention_split(row_pages, n_sm, 64, pages_per_split, n_splits);
     return FA_OK;
 }
 
@@ -1367,6 +1376,13 @@ static int op_gemm(const fa::GemmArgs& g, int variant, cudaStream_t s) {
         fa::launch_q8_gemm(g, s);
     }
     OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_gemm_plan(int M, int N, int K, int variant, int n_sm, int* n_split) {
+    if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_sm <= 0 || !n_split || (variant != 0 && variant != 1))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_gemm_plan: bad argument");
+    *n_split = variant == 0 && N % 128 == 0 ? fa::gemm_tc_pick_split(M, N, K, n_sm) : fa::gemm_pick_split(M, N, K, n_sm);
     return FA_OK;
 }
 

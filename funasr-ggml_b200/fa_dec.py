@@ -109,6 +109,7 @@ def lib():
         "fa_load_gguf": ([_P, ctypes.c_char_p], _I),
         "fa_gguf_find_tensor": ([ctypes.c_char_p, ctypes.c_char_p, _P, _P, _P, _P], _I),
         "fa_op_attention_plan": ([_P, _I, _I, _P, _P], _I),
+        "fa_op_gemm_plan": ([_I, _I, _I, _I, _I, _P], _I),
         "fa_op_paged_attention_noalloc": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P], _I),
         "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _I, _I, _P, _I, _P], _I),
@@ -373,6 +374,13 @@ def op_attention_plan(n_kv, n_sm=148):
     pps, ns = ctypes.c_int(), ctypes.c_int()
     _check(lib().fa_op_attention_plan(a.ctypes.data, len(a), n_sm, ctypes.byref(pps), ctypes.byref(ns)))
     return pps.value, ns.value
+
+
+def op_gemm_plan(M, N, K, variant=0, n_sm=148):
+    """Split-K factor the decoder picks for an M x N x K GEMM."""
+    s = ctypes.c_int()
+    _check(lib().fa_op_gemm_plan(M, N, K, variant, n_sm, ctypes.byref(s)))
+    return s.value
 
 
 def op_paged_attention_noalloc(q, M, pos, slot, bt, bt_stride, n_pages, pool, pps, n_splits, out16=0, out32=0,

@@ -229,6 +229,8 @@ FA_API int fa_op_paged_attention_noalloc(const float* q_dev, int M, const int* p
  * n_split > 1 writes partials [n_split][M][N] (their sum is C).
  * variant: 0 = tcgen05 kernel (N a multiple of 128), 1 = mma.sync kernel. */
 FA_API int fa_op_repack_q8(const uint8_t* gguf_q8_dev, int N, int K, uint16_t* w16_dev, void* stream);
+/* The split-K factor the decoder uses for an M x N x K GEMM of `variant` on n_sm SMs (host only). */
+FA_API int fa_op_gemm_plan(int M, int N, int K, int variant, int n_sm, int* n_split);
 FA_API int fa_op_q8_gemm(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K, const uint16_t* w16_dev,
                          int N, int n_split, float* c_dev, int variant, void* stream);
 /* lm_head with fused argmax: next [M] = first column of each row's maximum; logits optional. */
