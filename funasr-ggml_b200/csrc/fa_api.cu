@@ -86,6 +86,7 @@ static int ensure_configured() {
         fa::configure_attention();
         fa::configure_gemm();
         fa::configure_gemm_tc();
+        fa::configure_prefill_attention();
         g_configured[dev] = true;
     }
     return FA_OK;
@@ -1318,6 +1319,30 @@ extern "C" int fa_op_kv_append(const uint16_t* k, const uint16_t* v, int M, int 
     a.n_layers = n_layers; a.Hkv = kHkv; a.pos = pos; a.slot = slot; a.block_table = bt; a.bt_stride = bt_stride;
     a.n_pages = n_pages; a.pool = reinterpret_cast<__half*>(pool); a.err = err;
     fa::launch_kv_append_raw(a, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_prefill_attention(const float* q, int M, const int* pos, const int* slot, const int* bt,
+                                       int bt_stride, int n_pages, const uint16_t* pool_layer, const int* tiles,
+                                       int n_tiles, uint16_t* out16, uint16_t* out16_lo, float* out32, int* err,
+                                       void* stream) {
+    if (!q || !pos || !slot || !bt || !pool_layer || !tiles || M <= 0 || n_tiles <= 0 || n_pages <= 0 ||
+        bt_stride <= 0 || (!out16 && !out32))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "null or non-positive argument");
+    if ((reinterpret_cast<uintptr_t>(pool_layer) & 15) || (reinterpret_cast<uintptr_t>(tiles) & 7))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "pool must be 16-byte and tiles 8-byte aligned");
+    if (int rc = ensure_configured()) return rc;
+    CUtensorMap tm;
+    if (!fa::make_pool_map(&tm, pool_layer, (long long)n_pages * kHkv * 2 * fa::kPageTokens))
+        return set_err(nullptr, FA_ERR_CUDA, "cannot build the page-pool tensor map");
+    fa::PrefillAttnArgs a{};
+    a.q = q; a.block_table = bt; a.bt_stride = bt_stride; a.n_pages = n_pages; a.slot = slot; a.pos = pos;
+    a.M = M; a.Hq = kHq; a.Hkv = kHkv; a.tiles = reinterpret_cast<const int2*>(tiles); a.n_tiles = n_tiles;
+    a.pool_row0 = 0;
+    a.out16 = reinterpret_cast<__half*>(out16); a.out16_lo = reinterpret_cast<__half*>(out16_lo);
+    a.out32 = out32; a.err = err;
+    fa::launch_prefill_attention(tm, a, (cudaStream_t)stream);
     OP_CK(cudaGetLastError());
     return FA_OK;
 }

@@ -3,6 +3,8 @@
 
 #include "fa_common.cuh"
 
+#include <cuda.h>
+
 namespace fa {
 
 // ---------------------------------------------------------------- k_append.cu --
@@ -67,6 +69,33 @@ size_t attn_smem_bytes();
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s);
 // Split combine; only needed when n_splits > 1.
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s);
+
+// ------------------------------------------------------------ k_prefill_attn.cu --
+// Kernel (2b): causal attention of prefill tiles on the tensor cores. A tile is up to
+// 64 consecutive rows of one sequence with non-decreasing positions; each CTA takes
+// one (KV head, tile) and attends its rows to keys [0, pos[row]].
+struct PrefillAttnArgs {
+    const float* q;          // [M][Hq][128], already scaled by 1/sqrt(128)
+    const int* block_table;
+    int bt_stride;
+    int n_pages;
+    const int* slot;         // [M]
+    const int* pos;          // [M]
+    int M, Hq, Hkv;
+    const int2* tiles;       // [n_tiles] (first row, rows <= 64)
+    int n_tiles;
+    int pool_row0;           // row of this layer's page 0 in the pool tensor map
+    __half* out16;
+    __half* out16_lo;
+    float* out32;
+    int* err;
+};
+size_t prefill_attn_smem_bytes();
+void configure_prefill_attention();
+// Tensor map over a page pool viewed as [total_rows][128] f16 (one row = one token of
+// one head's K or V), 16-row x 64-column boxes, 128 B swizzle.
+bool make_pool_map(CUtensorMap* tm, const void* pool, long long total_rows);
+void launch_prefill_attention(const CUtensorMap& tm_pool, const PrefillAttnArgs& a, cudaStream_t s);
 
 // ------------------------------------------------------------------ k_gemm.cu --
 // Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T

@@ -26,6 +26,7 @@
 // Every mbarrier wait is bounded in time; a wait that gives up records an error
 // and the CTA drains its copies and MMAs before freeing TMEM.
 #include "fa_kernels.cuh"
+#include "tc_common.cuh"
 
 #include <cuda.h>
 
@@ -60,65 +61,14 @@ struct TcSmem {
     int consumed;
 };
 
-// UMMA shared-memory descriptor: K-major tile of 128 B rows in 128 B swizzle
-// atoms (8 rows x 128 B = 1 KiB apart), descriptor version 1.
-__device__ __forceinline__ uint64_t smem_desc(const void* p) {
-    const uint32_t a = smem_u32(p);
-    uint64_t d = 0;
-    d |= (uint64_t)((a & 0x3FFFFu) >> 4);
-    d |= (uint64_t)1 << 16;                 // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset: next 8-row group
-    d |= (uint64_t)1 << 46;                 // descriptor version
-    d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
-    return d;
-}
+__device__ __forceinline__ uint64_t smem_desc(const void* p) { return smem_desc_k128(p); }
 
 // Instruction descriptor: kind::f16, A/B f16 K-major, D f32, M=128, N=128.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t kIdesc = idesc_f16(BM, BN, false, false);
 
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
-        : "memory");
+    tc_mma_f16(tmem_d, da, db, kIdesc, accumulate);
 }
-
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
-}
-
-#define TMEM_LD_X32(taddr, v)                                                                                  \
-    asm volatile(                                                                                              \
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"       \
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                             \
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),       \
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), \
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),           \
-          "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),           \
-          "=r"(v[30]), "=r"(v[31])                                                                             \
-        : "r"(taddr))
 
 struct TcArgs {
     int M, N, K, n_split, epilogue, has_lo;
@@ -327,7 +277,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+}  // namespace
+
 // ------------------------------------------------------------- tensor maps --
+namespace {
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -346,7 +300,9 @@ EncodeTiledFn encoder() {
 }
 
 // 2-D f16 row-major [rows][cols] map with a (box_cols x box_rows) box.
-bool make_map(CUtensorMap* tm, const void* base, int cols, int rows, int box_cols, int box_rows, bool swizzle) {
+}  // namespace
+
+bool make_map(CUtensorMap* tm, const void* base, int cols, long long rows, int box_cols, int box_rows, bool swizzle) {
     EncodeTiledFn enc = encoder();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -358,7 +314,7 @@ bool make_map(CUtensorMap* tm, const void* base, int cols, int rows, int box_col
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
+bool tensor_maps_available() { return encoder() != nullptr; }
 
 size_t gemm_tc_smem_bytes() { return sizeof(TcSmem) + 1024; }
 

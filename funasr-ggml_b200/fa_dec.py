@@ -110,6 +110,7 @@ def lib():
         "fa_gguf_find_tensor": ([ctypes.c_char_p, ctypes.c_char_p, _P, _P, _P, _P], _I),
         "fa_op_attention_plan": ([_P, _I, _I, _P, _P], _I),
         "fa_op_gemm_plan": ([_I, _I, _I, _I, _I, _P], _I),
+        "fa_op_prefill_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_paged_attention_noalloc": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P], _I),
         "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _I, _I, _P, _I, _P], _I),
@@ -374,6 +375,14 @@ def op_attention_plan(n_kv, n_sm=148):
     pps, ns = ctypes.c_int(), ctypes.c_int()
     _check(lib().fa_op_attention_plan(a.ctypes.data, len(a), n_sm, ctypes.byref(pps), ctypes.byref(ns)))
     return pps.value, ns.value
+
+
+def op_prefill_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, tiles, n_tiles, out16=0, out32=0, err=0,
+                         stream=0, out16_lo=0):
+    """Kernel (2b): causal tensor-core attention over prefill tiles (first row, rows)."""
+    _check(lib().fa_op_prefill_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, tiles, n_tiles,
+                                         out16 or None, out16_lo or None, out32 or None, err or None,
+                                         stream or None))
 
 
 def op_gemm_plan(M, N, K, variant=0, n_sm=148):

@@ -210,6 +210,17 @@ FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, 
                           const int* block_table_dev, int bt_stride, int n_pages, const uint16_t* pool_layer_dev,
                           int pages_per_split, int n_splits, void* scratch_dev, uint16_t* out16_dev,
                           uint16_t* out16_lo_dev, float* out32_dev, int* err_dev, void* stream);
+/* Kernel (2b): causal attention of prefill tiles on the tensor cores (tcgen05, TMEM,
+ * TMA). tiles_dev holds n_tiles pairs (first row, rows) of rows of the q/pos/slot
+ * arrays: up to 64 consecutive rows of one sequence with non-decreasing positions;
+ * each row m attends to tokens [0, pos[m]] of sequence slot[m]. Output as for
+ * fa_op_paged_attention. A bad tile or position sets FA error bit 4 (kernel error
+ * word) and that tile writes nothing. pool_layer_dev 16-byte aligned. */
+FA_API int fa_op_prefill_attention(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
+                                   const int* block_table_dev, int bt_stride, int n_pages,
+                                   const uint16_t* pool_layer_dev, const int* tiles_dev, int n_tiles,
+                                   uint16_t* out16_dev, uint16_t* out16_lo_dev, float* out32_dev, int* err_dev,
+                                   void* stream);
 /* fa_op_paged_attention without the scratch argument: nothing is allocated, by the
  * library or the caller. No counterpart in the reference; it exists for callers that
  * cannot call cudaMalloc (an embedding runtime that owns all device memory, a process
