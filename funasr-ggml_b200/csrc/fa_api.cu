@@ -21,6 +21,7 @@
 #include "funasr_dec.h"
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -153,7 +154,16 @@ struct fa_ctx {
     bool use_graphs = true;
     bool use_pdl = true;       // programmatic dependent launch between the step's kernels
     int gemm_variant = 0;      // 0: tcgen05 kernel, 1: mma.sync kernel
-    std::map<uint64_t, cudaGraphExec_t> graphs;
+    struct GraphEntry {
+        cudaGraphExec_t exec;
+        int launches;
+    };
+    std::map<std::array<int, 12>, GraphEntry> graphs;
+    // prefill tiles (first row, rows) and the rows left to the decode kernel
+    int2* pf_tiles = nullptr;
+    int* dec_rows = nullptr;
+    CUtensorMap pool_map{};
+    bool pool_map_ok = false;
 
     bool prof = false;
     std::vector<cudaEvent_t> prof_ev;   // pairs per attention launch
@@ -339,8 +349,11 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
         dev_alloc(ctx, &ctx->row_pos, sizeof(int) * R) || dev_alloc(ctx, &ctx->next_dev, sizeof(int) * R) ||
         dev_alloc(ctx, &ctx->upd_idx, sizeof(int) * ctx->max_updates * 64) ||
         dev_alloc(ctx, &ctx->upd_page, sizeof(int) * ctx->max_updates * 64) ||
-        dev_alloc(ctx, &ctx->err_dev, sizeof(int)))
+        dev_alloc(ctx, &ctx->err_dev, sizeof(int)) || dev_alloc(ctx, &ctx->pf_tiles, sizeof(int2) * R) ||
+        dev_alloc(ctx, &ctx->dec_rows, sizeof(int) * R))
         return fail();
+    ctx->pool_map_ok = fa::make_pool_map(&ctx->pool_map, ctx->pool,
+                                         (long long)d.n_layers * n_pages * kHkv * 2 * fa::kPageTokens);
     ctx->max_updates *= 64;
     ctx->xn_lo = ctx->xn16 + (size_t)R * std::max(d.hidden, d.ffn);
     ctx->attn_lo = ctx->attn16 + (size_t)R * kHq * kD;
@@ -349,7 +362,7 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
         set_err(ctx, FA_ERR_CUDA, "memset err");
         return fail();
     }
-    const size_t h_ints = 3 * (size_t)R + 2 * (size_t)ctx->max_updates;
+    const size_t h_ints = 6 * (size_t)R + 2 * (size_t)ctx->max_updates;   // + tiles (2R) and decode rows (R)
     if (cudaMallocHost(&ctx->h_rows, sizeof(int) * h_ints) != cudaSuccess ||
         cudaMallocHost(&ctx->h_next, sizeof(int) * (size_t)R * 4096) != cudaSuccess ||
         cudaMallocHost(&ctx->h_err, sizeof(int)) != cudaSuccess) {
@@ -364,7 +377,7 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
 }
 
 static void clear_graphs(fa_ctx* ctx) {
-    for (auto& kv : ctx->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : ctx->graphs) cudaGraphExecDestroy(kv.second.exec);
     ctx->graphs.clear();
 }
 
@@ -669,7 +682,7 @@ static int upload_updates(fa_ctx* ctx, const std::vector<int>& ui, const std::ve
     size_t off = 0;
     while (off < ui.size()) {
         const int n = (int)std::min<size_t>(ui.size() - off, (size_t)ctx->max_updates);
-        int* hi = ctx->h_rows + 3 * ctx->d.max_rows;
+        int* hi = ctx->h_rows + 6 * ctx->d.max_rows;
         std::memcpy(hi, ui.data() + off, sizeof(int) * n);
         std::memcpy(hi + ctx->max_updates, up.data() + off, sizeof(int) * n);
         FA_CK(cudaMemcpyAsync(ctx->upd_idx, hi, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
@@ -689,17 +702,21 @@ namespace {
 struct StepPlan {
     int M = 0;
     int s_qkv = 1, s_o = 1, s_gu = 1, s_dn = 1;
-    int pps = 32;        // attention pages per split
+    int pps = 32;        // attention pages per split (decode kernel)
     int n_splits = 1;
+    int n_dec = 0;       // rows for the decode kernel (all M rows when there are no tiles)
+    int n_tiles = 0;     // prefill tiles for the tensor-core kernel
     bool embeds = false; // input rows already in x
     bool logits = false;
     bool prof = false;
-    uint64_t key() const {
-        return (uint64_t)M | ((uint64_t)n_splits << 13) | ((uint64_t)pps << 25) | ((uint64_t)embeds << 33) |
-               ((uint64_t)logits << 34) | ((uint64_t)prof << 35) | ((uint64_t)s_qkv << 36) | ((uint64_t)s_o << 42) |
-               ((uint64_t)s_gu << 48) | ((uint64_t)s_dn << 54);
+    std::array<int, 12> key() const {
+        return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, (int)embeds, (int)logits, (int)prof};
     }
 };
+
+// Rows of one sequence at consecutive positions that form a run at least this long
+// go to the tensor-core prefill kernel in tiles of up to 64 rows.
+constexpr int kPrefillMinRun = 16;
 
 }  // namespace
 
@@ -734,7 +751,10 @@ static void attention_split(const std::vector<int>& row_pages, int n_sm, int max
     *n_splits_out = (max_pages + best - 1) / best;
 }
 
-static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits) {
+// row_len: context length of each row given to the decode kernel (all rows, or the
+// rows outside prefill tiles); n_tiles: prefill tiles of the step.
+static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits,
+                          int n_tiles = 0) {
     const fa_model_desc& d = ctx->d;
     StepPlan p;
     p.M = M;
@@ -746,9 +766,14 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     p.s_o = pick(d.hidden, kHq * kD);
     p.s_gu = pick(2 * d.ffn, d.hidden);
     p.s_dn = pick(d.hidden, d.ffn);
-    std::vector<int> row_pages(row_len.size());
-    for (size_t i = 0; i < row_len.size(); ++i) row_pages[i] = (row_len[i] + fa::kPageTokens - 1) / fa::kPageTokens;
-    attention_split(row_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits);
+    p.n_dec = (int)row_len.size();
+    p.n_tiles = n_tiles;
+    if (p.n_dec > 0) {
+        std::vector<int> row_pages(row_len.size());
+        for (size_t i = 0; i < row_len.size(); ++i)
+            row_pages[i] = (row_len[i] + fa::kPageTokens - 1) / fa::kPageTokens;
+        attention_split(row_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits);
+    }
     p.embeds = embeds;
     p.logits = logits;
     p.prof = ctx->prof;
@@ -817,18 +842,31 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         a.q_scale = 1.0f / std::sqrt((float)kD);
         a.rope = ctx->rope; a.max_pos = d.max_ctx; a.pool_layer = pool_l; a.q_out = ctx->q_rot; a.err = ctx->err_dev;
         fa::launch_qknorm_rope_append(a, s);
-        fa::AttnArgs at{};
-        at.q = ctx->q_rot; at.pool_layer = pool_l; at.block_table = ctx->bt_dev; at.bt_stride = ctx->bt_stride;
-        at.n_pages = ctx->n_pages; at.slot = ctx->row_slot; at.pos = ctx->row_pos; at.M = M; at.Hq = kHq;
-        at.Hkv = kHkv; at.pages_per_split = p.pps; at.n_splits = p.n_splits; at.part_o = ctx->att_po;
-        at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out16_lo = ctx->attn_lo; at.out32 = nullptr;
-        at.err = ctx->err_dev;
         const bool prof_l = p.prof && (l == 0 || l == d.n_layers / 2 || l == d.n_layers - 1);
         if (prof_l) record_prof(ctx, 2 * l, capturing);
-        fa::launch_paged_attention(at, s);
-        ++n;
-        if (p.n_splits > 1) {
-            fa::launch_attn_combine(at, s);
+        if (p.n_dec > 0) {
+            fa::AttnArgs at{};
+            at.q = ctx->q_rot; at.pool_layer = pool_l; at.block_table = ctx->bt_dev; at.bt_stride = ctx->bt_stride;
+            at.n_pages = ctx->n_pages; at.slot = ctx->row_slot; at.pos = ctx->row_pos; at.M = p.n_dec;
+            at.rows = p.n_tiles > 0 ? ctx->dec_rows : nullptr; at.Hq = kHq;
+            at.Hkv = kHkv; at.pages_per_split = p.pps; at.n_splits = p.n_splits; at.part_o = ctx->att_po;
+            at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out16_lo = ctx->attn_lo; at.out32 = nullptr;
+            at.err = ctx->err_dev;
+            fa::launch_paged_attention(at, s);
+            ++n;
+            if (p.n_splits > 1) {
+                fa::launch_attn_combine(at, s);
+                ++n;
+            }
+        }
+        if (p.n_tiles > 0) {
+            fa::PrefillAttnArgs pa{};
+            pa.q = ctx->q_rot; pa.block_table = ctx->bt_dev; pa.bt_stride = ctx->bt_stride; pa.n_pages = ctx->n_pages;
+            pa.slot = ctx->row_slot; pa.pos = ctx->row_pos; pa.M = M; pa.Hq = kHq; pa.Hkv = kHkv;
+            pa.tiles = ctx->pf_tiles; pa.n_tiles = p.n_tiles;
+            pa.pool_row0 = l * ctx->n_pages * kHkv * 2 * fa::kPageTokens;
+            pa.out16 = ctx->attn16; pa.out16_lo = ctx->attn_lo; pa.out32 = nullptr; pa.err = ctx->err_dev;
+            fa::launch_prefill_attention(ctx->pool_map, pa, s);
             ++n;
         }
         if (prof_l) record_prof(ctx, 2 * l + 1, capturing);
@@ -893,13 +931,10 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
         cudaGraphDestroy(graph);
         if (e != cudaSuccess) return set_err(ctx, FA_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
         if (ctx->graphs.size() > 64) clear_graphs(ctx);
-        it = ctx->graphs.emplace(p.key(), exec).first;
-        ctx->last_launches = n;
-    } else {
-        // launch count is a function of the plan
-        ctx->last_launches = (p.embeds ? 0 : 1) + ctx->d.n_layers * (9 + (p.n_splits > 1 ? 1 : 0)) + 3;
+        it = ctx->graphs.emplace(p.key(), fa_ctx::GraphEntry{exec, n}).first;
     }
-    FA_CK(cudaGraphLaunch(it->second, ctx->stream));
+    ctx->last_launches = it->second.launches;
+    FA_CK(cudaGraphLaunch(it->second.exec, ctx->stream));
     ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
     return FA_OK;
 }
@@ -956,15 +991,44 @@ extern "C" int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int
         h[M + i] = seq_ids[i];
         h[2 * M + i] = pos[i];
     }
+    // runs of >= kPrefillMinRun rows of one sequence at consecutive positions become
+    // tensor-core prefill tiles; the other rows stay with the decode kernel
+    int* h_tiles = h + 3 * M;
+    int* h_dec = h + 5 * M;
+    int n_tiles = 0, n_dec = 0;
+    std::vector<int> dec_len;
+    for (int i = 0; i < M;) {
+        int j = i + 1;
+        while (j < M && seq_ids[j] == seq_ids[i] && pos[j] == pos[j - 1] + 1) ++j;
+        if (ctx->pool_map_ok && j - i >= kPrefillMinRun) {
+            for (int t = i; t < j; t += 64) {
+                h_tiles[2 * n_tiles] = t;
+                h_tiles[2 * n_tiles + 1] = std::min(64, j - t);
+                ++n_tiles;
+            }
+        } else {
+            for (int t = i; t < j; ++t) {
+                h_dec[n_dec++] = t;
+                dec_len.push_back(row_len[t]);
+            }
+        }
+        i = j;
+    }
     int rc = FA_OK;
     auto body = [&]() -> int {
         FA_CK(cudaMemcpyAsync(ctx->row_tok, h, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
         FA_CK(cudaMemcpyAsync(ctx->row_slot, h + M, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
         FA_CK(cudaMemcpyAsync(ctx->row_pos, h + 2 * M, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
+        if (n_tiles > 0) {
+            FA_CK(cudaMemcpyAsync(ctx->pf_tiles, h_tiles, sizeof(int2) * n_tiles, cudaMemcpyHostToDevice, ctx->stream));
+            if (n_dec > 0)
+                FA_CK(cudaMemcpyAsync(ctx->dec_rows, h_dec, sizeof(int) * n_dec, cudaMemcpyHostToDevice, ctx->stream));
+        }
         if (int r = upload_updates(ctx, ui, up)) return r;
         if (embeds)
             FA_CK(cudaMemcpyAsync(ctx->x, embeds, sizeof(float) * M * d.hidden, cudaMemcpyHostToDevice, ctx->stream));
-        StepPlan p = make_plan(ctx, M, row_len, embeds != nullptr, logits != nullptr);
+        StepPlan p = n_tiles > 0 ? make_plan(ctx, M, dec_len, embeds != nullptr, logits != nullptr, n_tiles)
+                                 : make_plan(ctx, M, row_len, embeds != nullptr, logits != nullptr);
         if (int r = run_step(ctx, p)) return r;
         FA_CK(cudaMemcpyAsync(ctx->h_next, ctx->next_dev, sizeof(int) * M, cudaMemcpyDeviceToHost, ctx->stream));
         if (logits)

@@ -54,7 +54,8 @@ struct AttnArgs {
     int bt_stride;
     int n_pages;
     const int* slot;         // [M]
-    const int* pos;          // [M]; row m attends to tokens [0, pos[m]]
+    const int* pos;          // [rows]; row m attends to tokens [0, pos[m]]
+    const int* rows;         // [M] rows to attend (grid.z index -> row), or nullptr: rows 0..M-1
     int M, Hq, Hkv;
     int pages_per_split;     // pages one CTA reads
     int n_splits;            // grid.x; splits beyond a row's length exit at once

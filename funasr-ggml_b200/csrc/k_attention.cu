@@ -105,11 +105,11 @@ __global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
     AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
     const int split = blockIdx.x;
     const int h = blockIdx.y;
-    const int m = blockIdx.z;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     pdl_trigger();
     pdl_wait();
+    const int m = a.rows ? a.rows[blockIdx.z] : (int)blockIdx.z;
 
     const int n_kv = a.pos[m] + 1;
     const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
 __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
     pdl_trigger();
     pdl_wait();
-    const int m = blockIdx.x / a.Hq;
+    const int m = a.rows ? a.rows[blockIdx.x / a.Hq] : (int)(blockIdx.x / a.Hq);
     const int H = blockIdx.x % a.Hq;
     const int d = threadIdx.x;
     const int n_kv = a.pos[m] + 1;
