@@ -1394,8 +1394,10 @@ extern "C" int fa_op_prefill_attention(const float* q, int M, const int* pos, co
     if (!q || !pos || !slot || !bt || !pool_layer || !tiles || M <= 0 || n_tiles <= 0 || n_pages <= 0 ||
         bt_stride <= 0 || (!out16 && !out32))
         return set_err(nullptr, FA_ERR_INVALID_ARG, "null or non-positive argument");
-    if ((reinterpret_cast<uintptr_t>(pool_layer) & 15) || (reinterpret_cast<uintptr_t>(tiles) & 7))
-        return set_err(nullptr, FA_ERR_INVALID_ARG, "pool must be 16-byte and tiles 8-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(pool_layer) & 15) || (reinterpret_cast<uintptr_t>(tiles) & 7) ||
+        (reinterpret_cast<uintptr_t>(out16) & 15) || (reinterpret_cast<uintptr_t>(out16_lo) & 15) ||
+        (reinterpret_cast<uintptr_t>(out32) & 15) || (reinterpret_cast<uintptr_t>(q) & 15))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "q, pool and outputs must be 16-byte, tiles 8-byte aligned");
     if (int rc = ensure_configured()) return rc;
     CUtensorMap tm;
     if (!fa::make_pool_map(&tm, pool_layer, (long long)n_pages * kHkv * 2 * fa::kPageTokens))

@@ -43,6 +43,7 @@ constexpr uint32_t STAGE_BYTES = 4 * 2 * 2 * BOX_BYTES; // 4 pages x (K, V) x 2 
 constexpr uint32_t TMEM_COLS = 256;                     // S0 [0,64) S1 [64,128) O [128,256)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;                        // lazy-max threshold, log2 units
+constexpr int PAGE_LIST = 2048;                         // block-table entries staged in shared memory
 
 struct PfSmem {
     __half q_hi[2][128 * 64];       // [dim half][128 query vectors][64 dims], swizzled
@@ -51,6 +52,7 @@ struct PfSmem {
     __half v[PST][2][KB * 64];
     __half p_hi[128 * 64];          // [128 query vectors][64 tokens]
     __half p_lo[128 * 64];
+    int pages[PAGE_LIST];           // the tile's block-table entries [0, last page]
     uint64_t kv_full[PST];
     uint64_t kv_empty[PST];
     uint64_t s_full[2];
@@ -74,13 +76,25 @@ __device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
     return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
 }
 
-__device__ __forceinline__ void store_pf(const PrefillAttnArgs& a, size_t o, float v) {
+// Eight consecutive outputs from offset o (a multiple of 8): 16 B stores of the f16
+// pair and/or two 16 B stores of f32.
+__device__ __forceinline__ void store_pf8(const PrefillAttnArgs& a, size_t o, const float (&v)[8]) {
     if (a.out16) {
-        const __half h = __float2half_rn(v);
-        a.out16[o] = h;
-        if (a.out16_lo) a.out16_lo[o] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const __half h0 = __float2half_rn(v[2 * e]), h1 = __float2half_rn(v[2 * e + 1]);
+            hi[e] = pack_h2(h0, h1);
+            lo[e] = pack_h2(__float2half_rn(__fsub_rn(v[2 * e], __half2float(h0))),
+                            __float2half_rn(__fsub_rn(v[2 * e + 1], __half2float(h1))));
+        }
+        *reinterpret_cast<uint4*>(a.out16 + o) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        if (a.out16_lo) *reinterpret_cast<uint4*>(a.out16_lo + o) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
-    if (a.out32) a.out32[o] = v;
+    if (a.out32) {
+        *reinterpret_cast<float4*>(a.out32 + o) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(a.out32 + o + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    }
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -135,9 +149,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (bad) {
         // nothing issued: fall through to the TMEM release
     } else if (warp == 0) {
+        const int* bt = a.block_table + (size_t)slot * a.bt_stride;
+        const int last_page = pos_last / kPageTokens;
+        for (int i = lane; i <= last_page && i < PAGE_LIST; i += 32) S.pages[i] = bt[i];
+        __syncwarp();
         if (lane == 0) {
-            const int* bt = a.block_table + (size_t)slot * a.bt_stride;
-            const int last_page = pos_last / kPageTokens;
             bool ok = true;
             for (int j = 0; j < n_blocks; ++j) {
                 const int s = j % PST;
@@ -148,7 +164,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mbar_arrive_expect_tx(&S.kv_full[s], STAGE_BYTES);
                 for (int q = 0; q < 4; ++q) {
                     // pages past the last one repeat it: finite data under a zero weight
-                    int pg = bt[min(j * 4 + q, last_page)];
+                    const int pi = min(j * 4 + q, last_page);
+                    int pg = pi < PAGE_LIST ? S.pages[pi] : bt[pi];
                     if (pg < 0 || pg >= a.n_pages) {
                         record_error(a.err, kDevErrBadPage);
                         pg = 0;
@@ -219,33 +236,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int row = row0 + r;
         const int pos_r = live ? a.pos[row] : -1;
         const int H = 2 * h + hq;
-        // stage Q (pre-scaled by 1/sqrt(128)) as an f16 pair, swizzled K-major
+        // stage Q (pre-scaled by 1/sqrt(128)) as an f16 pair, swizzled K-major: each
+        // warp loads its 32 query vectors, one 512 B vector per instruction (lane l
+        // takes dims 4l..4l+3), eight loads in flight at a time
         {
-            const float* qg = a.q + ((size_t)(live ? row : row0) * a.Hq + H) * D;
+            const int hf = lane >> 4;               // dims 64*hf ..
+            const int chunk = (lane & 15) >> 1;     // 16 B chunk within the 128 B row
+            const uint32_t sub = (uint32_t)(lane & 1) * 8;
 #pragma unroll 1
-            for (int c = 0; c < 16; ++c) {          // 16 chunks of 8 dims
-                float x[8];
-                if (live) {
-                    const float4 u = *reinterpret_cast<const float4*>(qg + 8 * c);
-                    const float4 w = *reinterpret_cast<const float4*>(qg + 8 * c + 4);
-                    x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w; x[4] = w.x; x[5] = w.y; x[6] = w.z; x[7] = w.w;
-                } else {
+            for (int v0 = 0; v0 < 32; v0 += 8) {
+                float4 x[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) x[e] = 0.0f;
+                for (int k = 0; k < 8; ++k) {
+                    const int tv = 32 * q + v0 + k;            // query vector = TMEM lane
+                    const int rr = tv & 63;
+                    x[k] = rr < n_rows ? *reinterpret_cast<const float4*>(
+                                             a.q + ((size_t)(row0 + rr) * a.Hq + 2 * h + (tv >> 6)) * D + 4 * lane)
+                                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 }
-                uint32_t hi[4], lo[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const __half h0 = __float2half_rn(x[2 * e]), h1 = __float2half_rn(x[2 * e + 1]);
-                    hi[e] = pack_h2(h0, h1);
-                    lo[e] = pack_h2(__float2half_rn(__fsub_rn(x[2 * e], __half2float(h0))),
-                                    __float2half_rn(__fsub_rn(x[2 * e + 1], __half2float(h1))));
+                for (int k = 0; k < 8; ++k) {
+                    const int tv = 32 * q + v0 + k;
+                    const __half h0 = __float2half_rn(x[k].x), h1 = __float2half_rn(x[k].y);
+                    const __half h2 = __float2half_rn(x[k].z), h3 = __float2half_rn(x[k].w);
+                    const uint2 hi = make_uint2(pack_h2(h0, h1), pack_h2(h2, h3));
+                    const uint2 lo = make_uint2(pack_h2(__float2half_rn(__fsub_rn(x[k].x, __half2float(h0))),
+                                                        __float2half_rn(__fsub_rn(x[k].y, __half2float(h1)))),
+                                                pack_h2(__float2half_rn(__fsub_rn(x[k].z, __half2float(h2))),
+                                                        __float2half_rn(__fsub_rn(x[k].w, __half2float(h3)))));
+                    const uint32_t off = sw128(tv, chunk) + sub;
+                    *reinterpret_cast<uint2*>(reinterpret_cast<unsigned char*>(S.q_hi[hf]) + off) = hi;
+                    *reinterpret_cast<uint2*>(reinterpret_cast<unsigned char*>(S.q_lo[hf]) + off) = lo;
                 }
-                const uint32_t off = sw128(t, c & 7);
-                *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(S.q_hi[c >> 3]) + off) =
-                    make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(S.q_lo[c >> 3]) + off) =
-                    make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
             fence_proxy_async_smem();
             mbar_arrive(&S.q_ready);
@@ -345,7 +367,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_wait_ld();
                 if (live) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) store_pf(a, obase + c + e, __uint_as_float(ov[e]) * inv);
+                    for (int e = 0; e < 32; e += 8) {
+                        float o[8];
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) o[k] = __uint_as_float(ov[e + k]) * inv;
+                        store_pf8(a, obase + c + e, o);
+                    }
                 }
             }
         }

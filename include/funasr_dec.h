@@ -215,7 +215,7 @@ FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, 
  * arrays: up to 64 consecutive rows of one sequence with non-decreasing positions;
  * each row m attends to tokens [0, pos[m]] of sequence slot[m]. Output as for
  * fa_op_paged_attention. A bad tile or position sets FA error bit 4 (kernel error
- * word) and that tile writes nothing. pool_layer_dev 16-byte aligned. */
+ * word) and that tile writes nothing. q, pool and outputs 16-byte aligned. */
 FA_API int fa_op_prefill_attention(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
                                    const int* block_table_dev, int bt_stride, int n_pages,
                                    const uint16_t* pool_layer_dev, const int* tiles_dev, int n_tiles,
