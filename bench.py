@@ -440,12 +440,13 @@ def run_prefill(a):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for rows, e in calls:
-            nxt, _ = dec.forward(rows, embeds=e)
             ends = {}
             for i, s in enumerate(rows):
                 ends[s] = i
-            for s, i in ends.items():
-                firsts[s] = int(nxt[i])
+            # only each stream's last row goes through lm_head
+            nxt, _ = dec.forward_rows(rows, list(ends.values()), embeds=e)
+            for s, v in zip(ends.keys(), nxt):
+                firsts[s] = int(v)
         t1 = time.perf_counter()
         ids, dev_ms = dec.generate(sids, [firsts[s] for s in sids], n_new)
         t2 = time.perf_counter()

@@ -162,6 +162,7 @@ struct fa_ctx {
     // prefill tiles (first row, rows) and the rows left to the decode kernel
     int2* pf_tiles = nullptr;
     int* dec_rows = nullptr;
+    int* out_rows = nullptr;     // rows whose next id / logits a step returns (when not all)
     CUtensorMap pool_map{};
     bool pool_map_ok = false;
 
@@ -350,7 +351,7 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
         dev_alloc(ctx, &ctx->upd_idx, sizeof(int) * ctx->max_updates * 64) ||
         dev_alloc(ctx, &ctx->upd_page, sizeof(int) * ctx->max_updates * 64) ||
         dev_alloc(ctx, &ctx->err_dev, sizeof(int)) || dev_alloc(ctx, &ctx->pf_tiles, sizeof(int2) * R) ||
-        dev_alloc(ctx, &ctx->dec_rows, sizeof(int) * R))
+        dev_alloc(ctx, &ctx->dec_rows, sizeof(int) * R) || dev_alloc(ctx, &ctx->out_rows, sizeof(int) * R))
         return fail();
     ctx->pool_map_ok = fa::make_pool_map(&ctx->pool_map, ctx->pool,
                                          (long long)d.n_layers * n_pages * kHkv * 2 * fa::kPageTokens);
@@ -362,7 +363,8 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
         set_err(ctx, FA_ERR_CUDA, "memset err");
         return fail();
     }
-    const size_t h_ints = 6 * (size_t)R + 2 * (size_t)ctx->max_updates;   // + tiles (2R) and decode rows (R)
+    // tok | slot | pos | tiles (2R) | decode rows | output rows | updates
+    const size_t h_ints = 7 * (size_t)R + 2 * (size_t)ctx->max_updates;
     if (cudaMallocHost(&ctx->h_rows, sizeof(int) * h_ints) != cudaSuccess ||
         cudaMallocHost(&ctx->h_next, sizeof(int) * (size_t)R * 4096) != cudaSuccess ||
         cudaMallocHost(&ctx->h_err, sizeof(int)) != cudaSuccess) {
@@ -682,7 +684,7 @@ static int upload_updates(fa_ctx* ctx, const std::vector<int>& ui, const std::ve
     size_t off = 0;
     while (off < ui.size()) {
         const int n = (int)std::min<size_t>(ui.size() - off, (size_t)ctx->max_updates);
-        int* hi = ctx->h_rows + 6 * ctx->d.max_rows;
+        int* hi = ctx->h_rows + 7 * ctx->d.max_rows;
         std::memcpy(hi, ui.data() + off, sizeof(int) * n);
         std::memcpy(hi + ctx->max_updates, up.data() + off, sizeof(int) * n);
         FA_CK(cudaMemcpyAsync(ctx->upd_idx, hi, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
@@ -706,11 +708,13 @@ struct StepPlan {
     int n_splits = 1;
     int n_dec = 0;       // rows for the decode kernel (all M rows when there are no tiles)
     int n_tiles = 0;     // prefill tiles for the tensor-core kernel
+    int n_out = -1;      // rows through lm_head: -1 all (with token feedback), else the listed rows
     bool embeds = false; // input rows already in x
     bool logits = false;
     bool prof = false;
     std::array<int, 12> key() const {
-        return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, (int)embeds, (int)logits, (int)prof};
+        return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, n_out, (int)embeds * 2 + (int)logits,
+                (int)prof};
     }
 };
 
@@ -888,13 +892,20 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         prev_part = ctx->part;
         prev_n = p.s_dn;
     }
-    fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
+    // final norm and lm_head: all rows (feeding each row's argmax back as its next
+    // token), or only the listed rows, compacted, or none
+    const bool all = p.n_out < 0;
+    const int Mo = all ? M : p.n_out;
+    if (Mo == 0) return n;
+    fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s,
+                                Mo, all ? nullptr : ctx->out_rows);
     fa::GemmArgs g{};
-    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = ctx->lm_q; g.M = M; g.N = d.vocab; g.K = H;
+    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = ctx->lm_q; g.M = Mo; g.N = d.vocab; g.K = H;
     g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = p.logits ? ctx->logits_dev : nullptr;
     g.amax_val = ctx->amax_v; g.amax_idx = ctx->amax_i;
     run_gemm(ctx, g);
-    fa::launch_argmax_reduce(ctx->amax_v, ctx->amax_i, M, d.vocab / 64, ctx->next_dev, ctx->row_tok, ctx->row_pos, s);
+    fa::launch_argmax_reduce(ctx->amax_v, ctx->amax_i, Mo, d.vocab / 64, ctx->next_dev, all ? ctx->row_tok : nullptr,
+                             all ? ctx->row_pos : nullptr, s);
     n += 3;
     return n;
 }
@@ -955,15 +966,26 @@ static int check_device_error(fa_ctx* ctx) {
 
 extern "C" int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
                           int* next_ids, float* logits) {
+    return fa_forward_rows(ctx, n_rows, seq_ids, token_ids, embeds, -1, nullptr, next_ids, logits);
+}
+
+extern "C" int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
+                               int n_out, const int* out_rows, int* next_ids, float* logits) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     if (!ctx->loaded) return set_err(ctx, FA_ERR_NOT_READY, "weights not loaded");
     if (n_rows <= 0 || n_rows > ctx->d.max_rows || !seq_ids)
         return set_err(ctx, FA_ERR_CAPACITY, "n_rows must be in [1, max_rows]");
     if ((token_ids == nullptr) == (embeds == nullptr))
         return set_err(ctx, FA_ERR_INVALID_ARG, "give exactly one of token_ids and embeds");
+    if (n_out > n_rows || (n_out > 0 && !out_rows))
+        return set_err(ctx, FA_ERR_INVALID_ARG, "n_out must be <= n_rows, with out_rows when n_out > 0");
+    for (int k = 0; k < n_out; ++k)
+        if (out_rows[k] < 0 || out_rows[k] >= n_rows)
+            return set_err(ctx, FA_ERR_INVALID_ARG, "out_rows entry outside [0, n_rows)");
     cudaSetDevice(ctx->device);
     const fa_model_desc& d = ctx->d;
     const int M = n_rows;
+    const int Mo = n_out < 0 ? M : n_out;
     // positions: consecutive per sequence in row order
     std::unordered_map<int, int> extra;
     std::vector<int> pos(M), row_len(M);
@@ -995,6 +1017,8 @@ extern "C" int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int
     // tensor-core prefill tiles; the other rows stay with the decode kernel
     int* h_tiles = h + 3 * M;
     int* h_dec = h + 5 * M;
+    int* h_out = h + 6 * M;
+    for (int k = 0; k < n_out; ++k) h_out[k] = out_rows[k];
     int n_tiles = 0, n_dec = 0;
     std::vector<int> dec_len;
     for (int i = 0; i < M;) {
@@ -1024,15 +1048,19 @@ extern "C" int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int
             if (n_dec > 0)
                 FA_CK(cudaMemcpyAsync(ctx->dec_rows, h_dec, sizeof(int) * n_dec, cudaMemcpyHostToDevice, ctx->stream));
         }
+        if (n_out > 0)
+            FA_CK(cudaMemcpyAsync(ctx->out_rows, h_out, sizeof(int) * n_out, cudaMemcpyHostToDevice, ctx->stream));
         if (int r = upload_updates(ctx, ui, up)) return r;
         if (embeds)
             FA_CK(cudaMemcpyAsync(ctx->x, embeds, sizeof(float) * M * d.hidden, cudaMemcpyHostToDevice, ctx->stream));
         StepPlan p = n_tiles > 0 ? make_plan(ctx, M, dec_len, embeds != nullptr, logits != nullptr, n_tiles)
                                  : make_plan(ctx, M, row_len, embeds != nullptr, logits != nullptr);
+        p.n_out = n_out < 0 ? -1 : n_out;
         if (int r = run_step(ctx, p)) return r;
-        FA_CK(cudaMemcpyAsync(ctx->h_next, ctx->next_dev, sizeof(int) * M, cudaMemcpyDeviceToHost, ctx->stream));
-        if (logits)
-            FA_CK(cudaMemcpyAsync(logits, ctx->logits_dev, sizeof(float) * M * d.vocab, cudaMemcpyDeviceToHost,
+        if (Mo > 0)
+            FA_CK(cudaMemcpyAsync(ctx->h_next, ctx->next_dev, sizeof(int) * Mo, cudaMemcpyDeviceToHost, ctx->stream));
+        if (logits && Mo > 0)
+            FA_CK(cudaMemcpyAsync(logits, ctx->logits_dev, sizeof(float) * Mo * d.vocab, cudaMemcpyDeviceToHost,
                                   ctx->stream));
         return check_device_error(ctx);
     };
@@ -1047,7 +1075,7 @@ extern "C" int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int
         return rc;
     }
     for (int i = 0; i < M; ++i) ctx->seqs[seq_ids[i]].len += 1;
-    if (next_ids) std::memcpy(next_ids, ctx->h_next, sizeof(int) * M);
+    if (next_ids && Mo > 0) std::memcpy(next_ids, ctx->h_next, sizeof(int) * Mo);
     return FA_OK;
 }
 
@@ -1056,20 +1084,17 @@ extern "C" int fa_prefill(fa_ctx* ctx, int seq_id, const float* embeds, int n_to
     if (int rc = check_seq(ctx, seq_id)) return rc;
     if (!embeds || n_tok <= 0) return set_err(ctx, FA_ERR_INVALID_ARG, "embeds and n_tok > 0 required");
     const int R = ctx->d.max_rows;
-    std::vector<int> ids(R, seq_id), nx(R);
-    std::vector<float> lg;
+    std::vector<int> ids(R, seq_id);
     for (int off = 0; off < n_tok; off += R) {
         const int m = std::min(R, n_tok - off);
         const bool last = off + m == n_tok;
-        if (last && last_logits) lg.resize((size_t)m * ctx->d.vocab);
-        if (int rc = fa_forward(ctx, m, ids.data(), nullptr, embeds + (size_t)off * ctx->d.hidden, nx.data(),
-                                last && last_logits ? lg.data() : nullptr))
+        const int last_row = m - 1;
+        int nx = 0;
+        // lm_head only for the last row of the last chunk
+        if (int rc = fa_forward_rows(ctx, m, ids.data(), nullptr, embeds + (size_t)off * ctx->d.hidden, last ? 1 : 0,
+                                     last ? &last_row : nullptr, &nx, last ? last_logits : nullptr))
             return rc;
-        if (last) {
-            if (next_id) *next_id = nx[m - 1];
-            if (last_logits)
-                std::memcpy(last_logits, lg.data() + (size_t)(m - 1) * ctx->d.vocab, sizeof(float) * ctx->d.vocab);
-        }
+        if (last && next_id) *next_id = nx;
     }
     return FA_OK;
 }

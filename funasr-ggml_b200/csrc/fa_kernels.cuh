@@ -125,9 +125,11 @@ size_t gemm_tc_smem_bytes();
 void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds,
                   int M, int vocab, float* x, int* err, cudaStream_t s);
 // Activations for the GEMMs leave their producer as an f16 pair: hi = f16(y), lo = f16(y - hi).
-// x[m] += sum_s part[s][m] (n_part may be 0); (hi, lo)[m] = split(rmsnorm(x[m]) * w)
+// x[m] += sum_s part[s][m] (n_part may be 0); (hi, lo)[m] = split(rmsnorm(x[m]) * w).
+// With rows: only rows[k] (k < n_out) are processed and written to output row k.
 void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w,
-                             float eps, __half* xn_hi, __half* xn_lo, cudaStream_t s);
+                             float eps, __half* xn_hi, __half* xn_lo, cudaStream_t s, int n_out = -1,
+                             const int* rows = nullptr);
 // (hi, lo)[m][j] = split(silu(g) * u), g and u summed over n_part partials of the gate|up GEMM
 void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s);
 // next[m] = first column of the row maximum over n_tiles partial maxima; optional feedback

@@ -89,11 +89,11 @@ __device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, in
 // One CTA per row; thread t owns float4 groups t, t+256, ... (hidden <= 4096).
 __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const float* part, int n_part, int M,
                                                                int hidden, const float* w, float eps,
-                                                               __half* xn_hi, __half* xn_lo) {
+                                                               __half* xn_hi, __half* xn_lo, const int* rows) {
     __shared__ double sh[8];
     pdl_trigger();
     pdl_wait();
-    const int m = blockIdx.x;
+    const int m = rows ? rows[blockIdx.x] : (int)blockIdx.x;   // source row; output row blockIdx.x
     const int n4 = hidden / 4;
     float4* xr = reinterpret_cast<float4*>(x + (size_t)m * hidden);
     float4 v[4];
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const f
         const int i = threadIdx.x + 256 * c;
         if (i >= n4) break;
         const float4 ww = reinterpret_cast<const float4*>(w)[i];
-        const size_t o = (size_t)m * hidden + 4 * (size_t)i;
+        const size_t o = (size_t)blockIdx.x * hidden + 4 * (size_t)i;
         split_store(__fmul_rn(__fmul_rn(v[c].x, scale), ww.x), xn_hi, xn_lo, o);
         split_store(__fmul_rn(__fmul_rn(v[c].y, scale), ww.y), xn_hi, xn_lo, o + 1);
         split_store(__fmul_rn(__fmul_rn(v[c].z, scale), ww.z), xn_hi, xn_lo, o + 2);
@@ -251,8 +251,10 @@ void launch_embed(const void* table, int table_type, int hidden, const int* toke
 }
 
 void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w, float eps,
-                             __half* xn_hi, __half* xn_lo, cudaStream_t s) {
-    launch_k(residual_rmsnorm_kernel, dim3(M), dim3(256), 0, s, x, part, n_part, M, hidden, w, eps, xn_hi, xn_lo);
+                             __half* xn_hi, __half* xn_lo, cudaStream_t s, int n_out, const int* rows) {
+    if (n_out < 0) n_out = M;
+    launch_k(residual_rmsnorm_kernel, dim3(n_out), dim3(256), 0, s, x, part, n_part, M, hidden, w, eps, xn_hi, xn_lo,
+             rows);
 }
 
 void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s) {

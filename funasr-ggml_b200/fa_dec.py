@@ -90,6 +90,7 @@ def lib():
         "fa_seq_length": ([_P, _I, _P], _I),
         "fa_seq_truncate": ([_P, _I, _I], _I),
         "fa_seq_block_table": ([_P, _I, _P, _I, _P], _I),
+        "fa_forward_rows": ([_P, _I, _P, _P, _P, _I, _P, _P, _P], _I),
         "fa_forward": ([_P, _I, _P, _P, _P, _P, _P], _I),
         "fa_prefill": ([_P, _I, _P, _I, _P, _P], _I),
         "fa_decode_step": ([_P, _I, _P, _P, _P, _P], _I),
@@ -286,6 +287,19 @@ class Decoder:
         lg = np.zeros((M, self.vocab), np.float32) if want_logits else None
         self._c(lib().fa_forward(self.ctx, M, _p(sids), _p(tok), _p(emb), _p(nxt), _p(lg)))
         return nxt, lg
+
+    def forward_rows(self, seq_ids, out_rows, tokens=None, embeds=None, want_logits=False):
+        """forward() returning next ids (and logits) of the rows in out_rows only."""
+        sids = _i32(seq_ids)
+        M = len(sids)
+        rows = _i32(out_rows)
+        tok = None if tokens is None else _i32(tokens)
+        emb = None if embeds is None else np.ascontiguousarray(embeds, np.float32)
+        nxt = np.zeros(max(len(rows), 1), np.int32)
+        lg = np.zeros((max(len(rows), 1), self.vocab), np.float32) if want_logits else None
+        self._c(lib().fa_forward_rows(self.ctx, M, _p(sids), _p(tok), _p(emb), len(rows), _p(rows) if len(rows) else None,
+                                      _p(nxt), _p(lg)))
+        return nxt[:len(rows)], (lg[:len(rows)] if want_logits else None)
 
     def decode_step(self, seq_ids, tokens, want_logits=False):
         sids = _i32(seq_ids)

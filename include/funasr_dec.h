@@ -145,6 +145,12 @@ FA_API int fa_seq_block_table(const fa_ctx* ctx, int seq_id, int* pages, int max
  * logits [n_rows][vocab] f32. */
 FA_API int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
                int* next_ids, float* logits);
+/* fa_forward returning the outputs of selected rows only: next_ids [n_out] and logits
+ * [n_out][vocab] belong to rows out_rows[0..n_out); only those rows go through the final
+ * norm and lm_head. n_out = 0: no outputs (a prefill chunk whose last row is not the
+ * sequence's last); n_out = -1: all rows, as fa_forward. */
+FA_API int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
+                           int n_out, const int* out_rows, int* next_ids, float* logits);
 /* Prefill n_tok embedding rows of one sequence in chunks of max_rows
  * (pipeline/pipeline.cpp:405 -> GPURunner::forward_gpu_tensor); next_id/last_logits
  * describe the last row. */

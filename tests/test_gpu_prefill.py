@@ -113,3 +113,27 @@ def test_decoder_forward_with_prefill_tiles_matches_oracle(torch_cuda):
         bt = dec.block_table(s)
         assert np.array_equal(bt, od.block_table[s, :len(bt)])
     dec.close()
+
+
+def test_forward_rows_outputs_equal_full_forward(torch_cuda):
+    """fa_forward_rows runs lm_head on the listed rows only; their next ids and logits
+    equal those of a full fa_forward of the same rows (rows are independent in every
+    kernel after attention), and n_out = 0 still appends every row."""
+    import fa_synth
+    cfg = fa_synth.small_config(n_layers=2, hidden=256, ffn=512, vocab=2048)
+    w = fa_synth.make_weights(cfg, seed=41)
+    dec = fa_dec.Decoder(0, **fa_synth.decoder_desc(cfg, max_ctx=512, n_pages=128, max_seqs=8, max_rows=128))
+    dec.load_weights(w)
+    rng = np.random.default_rng(3)
+    a, b, c, d = (dec.seq_open(512) for _ in range(4))
+    rows_a = [a] * 40 + [c] * 3
+    rows_b = [b] * 40 + [d] * 3
+    emb = fa_synth.audio_embeds(rng, len(rows_a), cfg["hidden"])
+    n_full, lg_full = dec.forward(rows_a, embeds=emb, want_logits=True)
+    sel = [39, 42, 0]
+    n_sel, lg_sel = dec.forward_rows(rows_b, sel, embeds=emb, want_logits=True)
+    assert np.array_equal(n_sel, n_full[sel])
+    assert np.array_equal(lg_sel, lg_full[sel])
+    n0, _ = dec.forward_rows([a] * 5, [], embeds=emb[:5])
+    assert len(n0) == 0 and dec.seq_length(a) == 45
+    dec.close()
