@@ -430,6 +430,12 @@ extern "C" int fa_set_pdl(fa_ctx* ctx, int enable) {
     return FA_OK;
 }
 
+extern "C" int fa_ctx_desc(const fa_ctx* ctx, fa_model_desc* desc) {
+    if (!ctx || !desc) return set_err(ctx, FA_ERR_INVALID_ARG, "fa_ctx_desc: bad argument");
+    *desc = ctx->d;
+    return FA_OK;
+}
+
 extern "C" int fa_pool_info(const fa_ctx* ctx, int* n_pages, int* n_free, size_t* page_bytes) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     if (n_pages) *n_pages = ctx->n_pages;
@@ -975,8 +981,7 @@ extern "C" int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, cons
     if (!ctx->loaded) return set_err(ctx, FA_ERR_NOT_READY, "weights not loaded");
     if (n_rows <= 0 || n_rows > ctx->d.max_rows || !seq_ids)
         return set_err(ctx, FA_ERR_CAPACITY, "n_rows must be in [1, max_rows]");
-    if ((token_ids == nullptr) == (embeds == nullptr))
-        return set_err(ctx, FA_ERR_INVALID_ARG, "give exactly one of token_ids and embeds");
+    if (!token_ids && !embeds) return set_err(ctx, FA_ERR_INVALID_ARG, "give token_ids and/or embeds");
     if (n_out > n_rows || (n_out > 0 && !out_rows))
         return set_err(ctx, FA_ERR_INVALID_ARG, "n_out must be <= n_rows, with out_rows when n_out > 0");
     for (int k = 0; k < n_out; ++k)
@@ -991,7 +996,7 @@ extern "C" int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, cons
     std::vector<int> pos(M), row_len(M);
     for (int i = 0; i < M; ++i) {
         if (int rc = check_seq(ctx, seq_ids[i])) return rc;
-        if (token_ids && (token_ids[i] < 0 || token_ids[i] >= d.vocab))
+        if (token_ids && !(token_ids[i] == -1 && embeds) && (token_ids[i] < 0 || token_ids[i] >= d.vocab))
             return set_err(ctx, FA_ERR_INVALID_ARG, "token id out of range");
         const Seq& s = ctx->seqs[seq_ids[i]];
         const int k = extra[seq_ids[i]]++;
@@ -1053,8 +1058,10 @@ extern "C" int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, cons
         if (int r = upload_updates(ctx, ui, up)) return r;
         if (embeds)
             FA_CK(cudaMemcpyAsync(ctx->x, embeds, sizeof(float) * M * d.hidden, cudaMemcpyHostToDevice, ctx->stream));
-        StepPlan p = n_tiles > 0 ? make_plan(ctx, M, dec_len, embeds != nullptr, logits != nullptr, n_tiles)
-                                 : make_plan(ctx, M, row_len, embeds != nullptr, logits != nullptr);
+        // embeddings only: x is the input; with token ids too, rows with id -1 keep their embedding
+        const bool x_ready = embeds && !token_ids;
+        StepPlan p = n_tiles > 0 ? make_plan(ctx, M, dec_len, x_ready, logits != nullptr, n_tiles)
+                                 : make_plan(ctx, M, row_len, x_ready, logits != nullptr);
         p.n_out = n_out < 0 ? -1 : n_out;
         if (int r = run_step(ctx, p)) return r;
         if (Mo > 0)

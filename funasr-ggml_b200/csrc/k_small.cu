@@ -46,6 +46,7 @@ __global__ void __launch_bounds__(256) embed_kernel(const void* table, int table
         return;
     }
     const int tok = tokens[m];
+    if (tok == -1) return;   // the row was loaded from embeddings
     if (tok < 0 || tok >= vocab) {
         if (threadIdx.x == 0) record_error(err, kDevErrBadPage);
         for (int i = threadIdx.x; i < hidden; i += blockDim.x) dst[i] = 0.0f;

@@ -24,6 +24,8 @@ ERRORS = {
     -1: "INVALID_ARG", -2: "CUDA", -3: "OOM", -4: "POOL_EXHAUSTED", -5: "SEQ", -6: "CAPACITY",
     -7: "WEIGHTS", -8: "TIMEOUT", -9: "NOT_READY", -10: "DEVICE",
 }
+FA_ERR_INVALID_ARG = -1
+FA_ERR_CUDA = -2
 FA_ERR_POOL_EXHAUSTED = -4
 FA_ERR_SEQ = -5
 FA_ERR_CAPACITY = -6
@@ -52,6 +54,21 @@ class _Desc(ctypes.Structure):
 class _TensorView(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char_p), ("type", ctypes.c_int), ("ne", ctypes.c_int64 * 2),
                 ("data", ctypes.c_void_p), ("nbytes", ctypes.c_size_t)]
+
+
+class _SchedConfig(ctypes.Structure):
+    _fields_ = [("max_batch_rows", ctypes.c_int), ("prefill_chunk", ctypes.c_int), ("max_running", ctypes.c_int),
+                ("eos_id", ctypes.c_int)]
+
+
+class _SchedEvent(ctypes.Structure):
+    _fields_ = [("tag", ctypes.c_int64), ("token", ctypes.c_int), ("finished", ctypes.c_int)]
+
+
+class _SchedStats(ctypes.Structure):
+    _fields_ = [("steps", ctypes.c_long), ("rows", ctypes.c_long), ("prompt_rows", ctypes.c_long),
+                ("tokens", ctypes.c_long), ("finished", ctypes.c_long), ("waiting", ctypes.c_int),
+                ("running", ctypes.c_int), ("reserved_pages", ctypes.c_long), ("total_pages", ctypes.c_long)]
 
 
 _lib = None
@@ -91,6 +108,13 @@ def lib():
         "fa_seq_truncate": ([_P, _I, _I], _I),
         "fa_seq_block_table": ([_P, _I, _P, _I, _P], _I),
         "fa_forward_rows": ([_P, _I, _P, _P, _P, _I, _P, _P, _P], _I),
+        "fa_ctx_desc": ([_P, _P], _I),
+        "fa_sched_create": ([_P, _P], _P),
+        "fa_sched_destroy": ([_P], None),
+        "fa_sched_submit": ([_P, ctypes.c_int64, _P, _P, _I, _I], _I),
+        "fa_sched_step": ([_P, _P, _I, _P], _I),
+        "fa_sched_idle": ([_P], _I),
+        "fa_sched_get_stats": ([_P, _P], _I),
         "fa_forward": ([_P, _I, _P, _P, _P, _P, _P], _I),
         "fa_prefill": ([_P, _I, _P, _I, _P, _P], _I),
         "fa_decode_step": ([_P, _I, _P, _P, _P, _P], _I),
@@ -429,6 +453,54 @@ def op_argmax_scratch_bytes(M, N) -> int:
 def op_q8_gemm_argmax(a16, a16_lo, M, K, w16, N, scratch, nxt, logits=0, variant=0, stream=0):
     _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, w16, N, scratch, nxt, logits or None, variant,
                                       stream or None))
+
+
+# ------------------------------------------------------ continuous batching --
+class Scheduler:
+    """fa_sched_*: streams submitted with a prompt (token ids or embeddings) and a
+    token budget; each step() runs one batched forward and returns the generated
+    (tag, token, finished) events."""
+
+    def __init__(self, decoder, max_batch_rows=512, prefill_chunk=512, max_running=256, eos_id=-1,
+                 max_events=4096):
+        cfg = _SchedConfig(max_batch_rows, prefill_chunk, max_running, eos_id)
+        self.dec = decoder
+        ctx = decoder.ctx if decoder is not None else None
+        self.s = lib().fa_sched_create(ctx, ctypes.byref(cfg))
+        if not self.s:
+            raise FaError(FA_ERR_INVALID_ARG, last_error(None))
+        self._ev = (_SchedEvent * max_events)()
+        self._n = max_events
+
+    def submit(self, tag: int, max_new: int, ids=None, embeds=None):
+        i = None if ids is None else _i32(ids)
+        e = None if embeds is None else np.ascontiguousarray(embeds, np.float32)
+        n = len(i) if i is not None else len(e)
+        _check(lib().fa_sched_submit(self.s, int(tag), _p(i), _p(e), n, int(max_new)), self.dec.ctx)
+
+    def step(self):
+        n = ctypes.c_int()
+        _check(lib().fa_sched_step(self.s, self._ev, self._n, ctypes.byref(n)), self.dec.ctx)
+        return [(self._ev[k].tag, self._ev[k].token, bool(self._ev[k].finished)) for k in range(n.value)]
+
+    def idle(self) -> bool:
+        return bool(lib().fa_sched_idle(self.s))
+
+    def stats(self) -> dict:
+        st = _SchedStats()
+        _check(lib().fa_sched_get_stats(self.s, ctypes.byref(st)))
+        return {k: getattr(st, k) for k, _ in _SchedStats._fields_}
+
+    def close(self):
+        if getattr(self, "s", None):
+            lib().fa_sched_destroy(self.s)
+            self.s = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ------------------------------------------------------ host page allocator --

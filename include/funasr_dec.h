@@ -122,6 +122,8 @@ FA_API int fa_set_gemm_variant(fa_ctx* ctx, int variant);
 FA_API int fa_set_pdl(fa_ctx* ctx, int enable);
 /* 1 = launch each step as a captured CUDA graph (default), 0 = direct launches. */
 FA_API int fa_set_graphs(fa_ctx* ctx, int enable);
+/* The descriptor the context runs with (n_pages resolved from kv_bytes). */
+FA_API int fa_ctx_desc(const fa_ctx* ctx, fa_model_desc* desc);
 /* Pool geometry: pages, free pages, bytes of one page across all layers. */
 FA_API int fa_pool_info(const fa_ctx* ctx, int* n_pages, int* n_free, size_t* page_bytes_all_layers);
 
@@ -148,7 +150,9 @@ FA_API int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* to
 /* fa_forward returning the outputs of selected rows only: next_ids [n_out] and logits
  * [n_out][vocab] belong to rows out_rows[0..n_out); only those rows go through the final
  * norm and lm_head. n_out = 0: no outputs (a prefill chunk whose last row is not the
- * sequence's last); n_out = -1: all rows, as fa_forward. */
+ * sequence's last); n_out = -1: all rows, as fa_forward. Token ids and embeddings may
+ * be mixed: with both given, a row whose token id is -1 takes its embeds row (a stream's
+ * audio frames next to other streams' tokens in one batch). */
 FA_API int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
                            int n_out, const int* out_rows, int* next_ids, float* logits);
 /* Prefill n_tok embedding rows of one sequence in chunks of max_rows
@@ -164,6 +168,43 @@ FA_API int fa_decode_step(fa_ctx* ctx, int n_seq, const int* seq_ids, const int*
  * n_steps steps on the device, CUDA events on the library stream, H2D/D2H excluded. */
 FA_API int fa_generate(fa_ctx* ctx, int n_seq, const int* seq_ids, const int* first_tokens, int n_steps, int* out_ids,
                 float* device_ms);
+
+/* ---- continuous batching: many streams, one forward per step ----
+ * New (the reference decodes one utterance at a time, pipeline/pipeline.cpp:434-451).
+ * Streams are admitted first come first served when a sequence slot is free and the
+ * page pool can hold the whole stream (prompt + max_new tokens), so a running stream
+ * never meets an exhausted pool. Each step runs one forward over one decode row per
+ * stream past its prompt plus prompt chunks (prefill_chunk rows per stream) of streams
+ * still in prefill, up to max_batch_rows; a stream ends after max_new tokens or at
+ * eos_id, and its pages return to the pool. The scheduler uses the context's sequence
+ * slots and the pages free when it is created. One host thread per scheduler. */
+typedef struct fa_sched fa_sched;
+typedef struct fa_sched_config {
+    int max_batch_rows;  /* rows per forward, <= the context's max_rows */
+    int prefill_chunk;   /* prompt rows of one stream per forward */
+    int max_running;     /* streams admitted at once, <= max_seqs */
+    int eos_id;          /* end-of-sequence id (151645 for Qwen3), -1 to ignore */
+} fa_sched_config;
+typedef struct fa_sched_event {
+    int64_t tag;         /* the stream's tag from fa_sched_submit */
+    int token;           /* generated token id; -1 when the stream failed */
+    int finished;        /* 1 on the stream's last event */
+} fa_sched_event;
+typedef struct fa_sched_stats {
+    long steps, rows, prompt_rows, tokens, finished;
+    int waiting, running;
+    long reserved_pages, total_pages;
+} fa_sched_stats;
+FA_API fa_sched* fa_sched_create(fa_ctx* ctx, const fa_sched_config* cfg);
+FA_API void fa_sched_destroy(fa_sched* s);
+/* Queue a stream: prompt as token ids or as embedding rows [n_prompt][hidden] (one of the two). */
+FA_API int fa_sched_submit(fa_sched* s, int64_t tag, const int* prompt_ids, const float* prompt_embeds, int n_prompt,
+                           int max_new);
+/* Run one step (when no undelivered events remain) and deliver up to max_events events. */
+FA_API int fa_sched_step(fa_sched* s, fa_sched_event* events, int max_events, int* n_events);
+/* 1 when no stream is waiting or running and every event was delivered. */
+FA_API int fa_sched_idle(const fa_sched* s);
+FA_API int fa_sched_get_stats(const fa_sched* s, fa_sched_stats* out);
 
 /* ---- pages ---- */
 /* Copy pages of one layer ([n][kv_heads][2][16][head_dim] f16 bit patterns) to the host. */
