@@ -50,10 +50,15 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between kernels")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "gemm", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "gemm", "prefill", "serve"],
                     help="attention: kernel (2) alone over one layer's pages at the same batch and context; "
                          "gemm: the decode step's weight GEMMs alone; prefill: batched chunked prefill of "
-                         "16 utterances then 64 greedy tokens each")
+                         "16 utterances then 64 greedy tokens each; serve: continuous batching of --streams "
+                         "streams with Poisson arrivals")
+    ap.add_argument("--streams", type=int, default=1024, help="serve: streams over all GPUs")
+    ap.add_argument("--arrival-rate", type=float, default=100.0, help="serve: streams per second (Poisson)")
+    ap.add_argument("--kv-gb", type=float, default=160.0, help="serve: page pool per GPU, GB")
+    ap.add_argument("--serve-seconds", type=float, default=60.0, help="serve: wall-clock budget of the timed run")
     return ap.parse_args()
 
 
@@ -479,6 +484,91 @@ def run_prefill(a):
     fa_multi.shutdown()
 
 
+# --------------------------------------------------- continuous batching --
+def run_serve(a):
+    """Continuous batching (fa_sched_*): --streams streams over all GPUs, sharded
+    across ranks with no collectives; prompt lengths log-uniform in [200, 6000] tokens,
+    output lengths uniform in [16, 512] (EOS ignored), Poisson arrivals at
+    --arrival-rate streams/s over all GPUs, a --kv-gb page pool per GPU. Each step
+    runs one forward over every running stream's next token plus up to 512 prompt rows.
+    Reports generated and processed tokens/s over the run (wall clock, max over ranks;
+    the run stops after --serve-seconds even with streams left), time to first token
+    and the peak number of concurrent streams."""
+    import torch
+    import fa_dec
+
+    rank, local, world = fa_multi.init("nccl")
+    torch.cuda.set_device(local)
+    cfg = fa_synth.QWEN3_06B
+    w = fa_synth.make_weights(cfg, seed=1)
+    rng = np.random.default_rng(2024)
+    n = a.streams
+    plen = np.exp(rng.uniform(np.log(200), np.log(6000), n)).astype(np.int64)
+    olen = rng.integers(16, 513, n)
+    arrive = np.cumsum(rng.exponential(1.0 / a.arrival_rate, n))
+    mine = fa_multi.shard(list(range(n)), rank, world)
+    page_bytes = 28 * 8 * 2 * 16 * 128 * 2
+    n_pages = int(a.kv_gb * 1e9 // page_bytes)
+    max_ctx = int((plen.max() + olen.max() + 31) // 16 * 16)
+    dec = fa_dec.Decoder(local, **fa_synth.decoder_desc(cfg, max_ctx=max_ctx, n_pages=n_pages,
+                                                        max_seqs=max(len(mine), 1), max_rows=1024))
+    dec.load_weights(w)
+    dec.set_graphs(False)          # every step has its own shape
+    prompts = {i: rng.integers(0, cfg["vocab"], int(plen[i])).astype(np.int32) for i in mine}
+
+    # warm-up: a few short streams through the same path
+    sch = fa_dec.Scheduler(dec, max_batch_rows=1024, prefill_chunk=512, max_running=1024, eos_id=-1)
+    for k in range(4):
+        sch.submit(-1 - k, 8, ids=rng.integers(0, cfg["vocab"], 300).astype(np.int32))
+    while not sch.idle():
+        sch.step()
+    sch.close()
+
+    sch = fa_dec.Scheduler(dec, max_batch_rows=1024, prefill_chunk=512, max_running=1024, eos_id=-1)
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    t0 = time.perf_counter()
+    nxt, first, gen, peak_run = 0, {}, 0, 0
+    order = sorted(mine, key=lambda i: arrive[i])
+    while (nxt < len(order) or not sch.idle()) and time.perf_counter() - t0 < a.serve_seconds:
+        now = time.perf_counter() - t0
+        while nxt < len(order) and arrive[order[nxt]] <= now:
+            i = order[nxt]
+            sch.submit(i, int(olen[i]), ids=prompts[i])
+            nxt += 1
+        if sch.idle():
+            time.sleep(max(0.0, min(0.01, arrive[order[nxt]] - now)))
+            continue
+        for tag, tok, fin in sch.step():
+            gen += 1
+            if tag not in first:
+                first[tag] = time.perf_counter() - t0 - arrive[tag]
+        peak_run = max(peak_run, sch.stats()["running"])
+    el = time.perf_counter() - t0
+    st = sch.stats()
+    sch.close()
+    dec.close()
+    el_max = fa_multi.reduce(el, "max")
+    gen_all = fa_multi.reduce(gen, "sum")
+    rows_all = fa_multi.reduce(st["rows"], "sum")
+    ttft = np.array(list(first.values())) if first else np.zeros(1)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "continuous-batching generated tokens/s", "value": gen_all / el_max, "unit": "tokens/s",
+            "n_gpus": world, "steps": int(st["steps"]), "warmup": 1, "ms_per_step": el * 1e3 / max(st["steps"], 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic: seeded random-init Q8_0 weights, random prompt token ids",
+            "config": {"workload": f"{n} streams, prompts log-U[200,6000], outputs U[16,512], Poisson "
+                                   f"{a.arrival_rate}/s, {a.kv_gb} GB pages per GPU, <= 1024 rows per step",
+                       "streams": n, "finished_streams_rank0": int(st["finished"]),
+                       "processed_tokens_per_s": rows_all / el_max, "elapsed_s": el_max,
+                       "ttft_p50_s": float(np.percentile(ttft, 50)), "ttft_p99_s": float(np.percentile(ttft, 99)),
+                       "peak_running_rank0": peak_run, "pages_per_gpu": n_pages},
+            "gpu_launches": None,
+        }), flush=True)
+    fa_multi.shutdown()
+
+
 # -------------------------------------------------------------- reference --
 def run_reference(a):
     """The reference's CPU path (ggml) cannot be built here, so its restatement (the
@@ -538,5 +628,7 @@ if __name__ == "__main__":
         run_gemm(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "serve":
+        run_serve(args)
     else:
         run_ours(args)
