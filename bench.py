@@ -128,6 +128,8 @@ def cpu_oracle_sample(cfg, w, ctx, budget_s, rows=2, seed=0):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     oracle.build()
+    # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    oracle.set_num_threads(len(os.sched_getaffinity(0)))
     pages = (ctx + 16 + 15) // 16
     od = oracle.OracleDecoder(cfg, w, n_pages=rows * pages, max_seqs=rows, max_pages_per_seq=pages,
                               max_pos=ctx + 16, mode=oracle.MODE_GGML_CPU)
@@ -582,6 +584,7 @@ def run_reference(a):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     oracle.build()
+    oracle.set_num_threads(len(os.sched_getaffinity(0)))   # torchrun sets OMP_NUM_THREADS=1
     rows = 2
     ctx = a.ctx
     n_steps = a.warmup + a.steps
