@@ -733,14 +733,14 @@ constexpr int kPrefillMinRun = 16;
 // Attention work split for rows of row_pages[i] pages each: the pages per CTA (a
 // multiple of 4, one per warp and round) that minimise the estimated time
 //   waves * (pps + 2) + (2 if any row is split)
-// where waves = ceil(CTAs / (2 * n_sm)) (2 CTAs fit on an SM), a CTA costs its pages
+// where waves = ceil(CTAs / (kAttnCtasPerSm * n_sm)), a CTA costs its pages
 // plus about 2 pages' worth of set-up, and merging split partials about 2 more; at
 // most max_splits splits per row.
 static void attention_split(const std::vector<int>& row_pages, int n_sm, int max_splits, int* pps_out,
                             int* n_splits_out) {
     int max_pages = 1;
     for (int pg : row_pages) max_pages = std::max(max_pages, pg);
-    const long long slots = 2LL * n_sm;
+    const long long slots = (long long)fa::kAttnCtasPerSm * n_sm;
     long long best_cost = -1;
     int best = 0;
     for (int pps = 4; pps <= 256; pps += 4) {

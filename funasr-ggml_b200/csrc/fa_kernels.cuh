@@ -68,6 +68,10 @@ struct AttnArgs {
 };
 size_t attn_smem_bytes();
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s);
+// Pipeline depth of each warp's page ring and the CTAs that fit on one SM (shared
+// memory: 4 warps x kAttnStages x 8 KiB per CTA).
+constexpr int kAttnStages = 2;
+constexpr int kAttnCtasPerSm = 3;
 // Split combine; only needed when n_splits > 1.
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s);
 

@@ -36,7 +36,7 @@ namespace {
 
 constexpr int D = 128;
 constexpr int WARPS = 4;
-constexpr int STAGES = 3;
+constexpr int STAGES = kAttnStages;
 constexpr int TILE_HALVES = 2 * kPageTokens * D;   // K then V of one head in one page
 constexpr uint32_t TILE_BYTES = TILE_HALVES * 2;   // 8192
 constexpr float kLog2e = 1.4426950408889634f;
@@ -100,7 +100,7 @@ __device__ __forceinline__ void store_out(const AttnArgs& a, size_t o, float v) 
     if (a.out32) a.out32[o] = v;
 }
 
-__global__ void __launch_bounds__(128, 2) paged_attn_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
     const int split = blockIdx.x;
