@@ -1445,6 +1445,14 @@ extern "C" int fa_op_prefill_attention(const float* q, int M, const int* pos, co
     return FA_OK;
 }
 
+extern "C" int fa_op_wait_selftest(int limit_us, int* err_dev, void* stream) {
+    if (limit_us <= 0 || limit_us > 1000000 || !err_dev)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "limit_us in (0, 1e6] and err_dev required");
+    fa::launch_wait_selftest(err_dev, (unsigned long long)limit_us * 1000ull, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
 extern "C" int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages_per_split, int* n_splits) {
     if (!n_kv || M <= 0 || n_sm <= 0 || !pages_per_split || !n_splits)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_attention_plan: bad argument");

@@ -141,6 +141,8 @@ void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, 
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,
                           int* feed_pos, cudaStream_t s);
 void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* upd_page, int n, cudaStream_t s);
+// One CTA waits on an mbarrier that is never completed, for limit_ns: sets kDevErrTimeout.
+void launch_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t s);
 // GGUF Q8_0 rows [N][K/32][34 B] -> W [N][K] f16 with W = f16(f32(d) * q), rows landing at
 // destination row r0 + n (Wq, Wk, Wv and gate, up are stacked that way).
 void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_w, cudaStream_t s);

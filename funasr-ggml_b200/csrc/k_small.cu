@@ -244,6 +244,22 @@ __global__ void __launch_bounds__(256) read_pages_kernel(const __half* pool_laye
     for (size_t k = threadIdx.x; k < n16; k += 256) d[k] = s[k];
 }
 
+// Self-test of the bounded waits every pipelined kernel uses: one CTA arms an
+// mbarrier for a byte count that no copy will ever deliver and waits on it with a
+// short limit. The wait must give up, record kDevErrTimeout and let the kernel
+// return normally, leaving the context usable.
+__global__ void wait_selftest_kernel(int* err, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar, 16);   // 16 bytes that never arrive
+    }
+    __syncthreads();
+    const bool got = mbar_wait_bounded(&bar, 0, limit_ns);
+    if (!got && threadIdx.x == 0) record_error(err, kDevErrTimeout);
+}
+
 }  // namespace
 
 void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds, int M,
@@ -296,6 +312,10 @@ void launch_read_pages(const __half* pool_layer, const int* pages, int n, __half
     if (n <= 0) return;
     const size_t page_elems = (size_t)8 * 2 * kPageTokens * 128;
     read_pages_kernel<<<n, 256, 0, s>>>(pool_layer, pages, page_elems, out);
+}
+
+void launch_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t s) {
+    wait_selftest_kernel<<<1, 32, 0, s>>>(err, limit_ns);
 }
 
 }  // namespace fa

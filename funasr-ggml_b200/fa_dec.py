@@ -135,6 +135,7 @@ def lib():
         "fa_gguf_find_tensor": ([ctypes.c_char_p, ctypes.c_char_p, _P, _P, _P, _P], _I),
         "fa_op_attention_plan": ([_P, _I, _I, _P, _P], _I),
         "fa_op_gemm_plan": ([_I, _I, _I, _I, _I, _P], _I),
+        "fa_op_wait_selftest": ([_I, _P, _P], _I),
         "fa_op_prefill_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_paged_attention_noalloc": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P], _I),
         "fa_op_repack_q8": ([_P, _I, _I, _P, _P], _I),
@@ -421,6 +422,11 @@ def op_prefill_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, tiles, n
     _check(lib().fa_op_prefill_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, tiles, n_tiles,
                                          out16 or None, out16_lo or None, out32 or None, err or None,
                                          stream or None))
+
+
+def op_wait_selftest(limit_us, err, stream=0):
+    """A bounded mbarrier wait that must run out (nothing completes the barrier)."""
+    _check(lib().fa_op_wait_selftest(int(limit_us), err, stream or None))
 
 
 def op_gemm_plan(M, N, K, variant=0, n_sm=148):

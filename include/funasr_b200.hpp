@@ -16,7 +16,8 @@
 //   - KVCache::k_tensor()/v_tensor() (ggml views of the f32 cache) become
 //     read_layer(), which returns the f16 cache of one layer as [n_past][kv_dim];
 //   - GPURunner::forward_tokens() adds the embedding lookup on the device.
-// BatchDecoder is new: many sequences on one GPU, one batched step for all of them.
+// BatchDecoder and Scheduler are new: many sequences on one GPU, one batched step for
+// all of them (Scheduler adds admission, prompt chunking and page release).
 //
 // Not thread-safe per GPUContext; use one host thread per GPU, as the reference does.
 #ifndef FUNASR_B200_HPP
@@ -410,6 +411,66 @@ private:
         return false;
     }
     GPUContext& ctx_;
+    std::string err_;
+};
+
+// Continuous batching over a GPUContext's sequence slots and page pool (fa_sched_*):
+// streams are submitted with a prompt and a token budget; each step() runs one batched
+// forward and returns the tokens it produced as (tag, token, finished) events.
+class Scheduler {
+public:
+    struct Config {
+        int max_batch_rows = 512;
+        int prefill_chunk = 512;
+        int max_running = 256;
+        int eos_id = 151645;   // tokenizer.ggml.eos_token_id of the FunASR model; -1: none
+    };
+
+    Scheduler(GPUContext& ctx, const Config& cfg) : ctx_(ctx) {
+        fa_sched_config c{cfg.max_batch_rows, cfg.prefill_chunk, cfg.max_running, cfg.eos_id};
+        s_ = fa_sched_create(ctx.handle(), &c);
+        if (!s_) err_ = fa_last_error(nullptr);
+    }
+    ~Scheduler() {
+        if (s_) fa_sched_destroy(s_);
+    }
+    Scheduler(const Scheduler&) = delete;
+    Scheduler& operator=(const Scheduler&) = delete;
+
+    bool ok() const { return s_ != nullptr; }
+    bool submit_tokens(int64_t tag, const std::vector<int>& ids, int max_new) {
+        return check(fa_sched_submit(s_, tag, ids.data(), nullptr, (int)ids.size(), max_new));
+    }
+    // embeds: n_prompt rows of embedding_length f32 (e.g. the adaptor's output)
+    bool submit_embeds(int64_t tag, const float* embeds, int n_prompt, int max_new) {
+        return check(fa_sched_submit(s_, tag, nullptr, embeds, n_prompt, max_new));
+    }
+    bool step(std::vector<fa_sched_event>& events, int max_events = 4096) {
+        events.resize((size_t)max_events);
+        int n = 0;
+        if (!check(fa_sched_step(s_, events.data(), max_events, &n))) {
+            events.clear();
+            return false;
+        }
+        events.resize((size_t)n);
+        return true;
+    }
+    bool idle() const { return fa_sched_idle(s_) == 1; }
+    fa_sched_stats stats() const {
+        fa_sched_stats st{};
+        fa_sched_get_stats(s_, &st);
+        return st;
+    }
+    const std::string& last_error() const { return err_; }
+
+private:
+    bool check(int rc) {
+        if (rc == FA_OK) return true;
+        err_ = fa_last_error(ctx_.handle());
+        return false;
+    }
+    GPUContext& ctx_;
+    fa_sched* s_ = nullptr;
     std::string err_;
 };
 

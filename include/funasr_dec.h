@@ -309,6 +309,12 @@ FA_API int fa_palloc_n_free(const fa_palloc* pa);
 /* Applies compaction to the allocator and returns the moves (src[i] -> dst[i]); *n_moves. */
 FA_API int fa_palloc_compact(fa_palloc* pa, int* src, int* dst, int max_moves, int* n_moves);
 
+/* Failure detection without a fault: one CTA waits, with a limit of limit_us
+ * microseconds, on an mbarrier that nothing completes, the same bounded wait every
+ * pipelined kernel uses. The wait gives up, sets bit 1 (timeout) in *err_dev and the
+ * kernel returns, leaving the context usable. */
+FA_API int fa_op_wait_selftest(int limit_us, int* err_dev, void* stream);
+
 /* Library version string. */
 FA_API const char* fa_version(void);
 

@@ -11,7 +11,8 @@
 // prompt.f32 holds n_prompt rows of embedding_length f32 (the adaptor's output in the
 // full pipeline). out.bin receives, in order: n_new int32 greedy ids, vocab f32 logits of
 // the last step, n_past x kv_dim u16 layer-0 K, the same for V, then the same ids again
-// from a second utterance decoded by BatchDecoder on a second sequence (n_new int32).
+// from the utterance decoded by BatchDecoder on a second sequence (n_new int32) and by the
+// Scheduler (n_new int32).
 // Exit codes: 0 ok, 1 usage / input, 2 GPU init failed, 3 forward failed, 4 check failed.
 #include "funasr_b200.hpp"
 
@@ -102,7 +103,7 @@ int main(int argc, char** argv) {
         CHECK(again == logits);
     }
 
-    // 6. the same utterance as a second stream through BatchDecoder; KVCache views it
+    // 6. the same utterance as a second stream through BatchDecoder
     BatchDecoder batch(ctx);
     const int s = batch.open(512);
     CHECK(s >= 0);
@@ -120,7 +121,35 @@ int main(int argc, char** argv) {
     CHECK(len == n_prompt + n_new);
     CHECK(batch.close(s));
 
-    // 7. clear_kv_cache empties the context's own sequence
+    // 7. the same utterance through the scheduler, one prompt chunk (graphs off: every
+    //    scheduled step has its own shape)
+    std::vector<int> ids3;
+    {
+        fa_set_graphs(ctx.handle(), 0);
+        Scheduler::Config sc;
+        sc.max_batch_rows = 64;
+        sc.prefill_chunk = 64;
+        sc.max_running = 1;
+        sc.eos_id = -1;
+        Scheduler sch(ctx, sc);
+        CHECK(sch.ok());
+        CHECK(sch.submit_embeds(7, prompt.data(), n_prompt, n_new));
+        std::vector<fa_sched_event> ev;
+        int guard = 0;
+        while (!sch.idle()) {
+            CHECK(sch.step(ev));
+            for (const auto& e : ev) {
+                CHECK(e.tag == 7 && e.token >= 0);
+                ids3.push_back(e.token);
+            }
+            CHECK(++guard < 10000);
+        }
+        CHECK((int)ids3.size() == n_new);
+        CHECK(sch.stats().finished == 1);
+        fa_set_graphs(ctx.handle(), 1);
+    }
+
+    // 8. clear_kv_cache empties the context's own sequence
     ctx.clear_kv_cache();
     CHECK(ctx.kv_cache().n_past == 0);
 
@@ -130,6 +159,7 @@ int main(int argc, char** argv) {
     out.write(reinterpret_cast<const char*>(k0.data()), (std::streamsize)(k0.size() * 2));
     out.write(reinterpret_cast<const char*>(v0.data()), (std::streamsize)(v0.size() * 2));
     out.write(reinterpret_cast<const char*>(ids2.data()), (std::streamsize)(ids2.size() * sizeof(int)));
+    out.write(reinterpret_cast<const char*>(ids3.data()), (std::streamsize)(ids3.size() * sizeof(int)));
     std::printf("OK\n");
     return 0;
 }

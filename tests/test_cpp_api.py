@@ -61,6 +61,7 @@ def test_cpp_api_decode_matches_oracle(program, tmp_path, torch_cuda):
     v0 = np.frombuffer(raw, np.uint16, n_past * kvd, off).reshape(n_past, kvd)
     off += 2 * n_past * kvd
     ids2 = np.frombuffer(raw, np.int32, n_new, off)
+    ids3 = np.frombuffer(raw, np.int32, n_new, off + 4 * n_new)
 
     od = oracle.OracleDecoder(CFG, w, n_pages=64, max_seqs=1, max_pages_per_seq=64, max_pos=4096,
                               mode=oracle.MODE_W16)
@@ -74,6 +75,7 @@ def test_cpp_api_decode_matches_oracle(program, tmp_path, torch_cuda):
         tok = int(nx[0])
     assert np.mean(ids == np.array(o_ids)) >= 0.99, (ids, o_ids)
     assert np.array_equal(ids2, ids), "BatchDecoder stream differs from GPURunner stream"
+    assert np.array_equal(ids3, ids), "Scheduler stream differs from GPURunner stream"
     assert_close(logits, lg[0], what="last-step logits")
     # layer-0 cache in [pos][kv_dim] order from the oracle's pages
     pages = od.pool[0].reshape(-1, CFG["n_kv_heads"], 2, 16, CFG["head_dim"])

@@ -326,3 +326,20 @@ def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2, variant):
                              variant)
     torch.cuda.synchronize()
     assert nxt.cpu().numpy().tolist() == [j1] * M
+
+
+# ------------------------------------------------------- failure detection --
+def test_bounded_wait_gives_up_and_leaves_the_context_usable(torch_cuda):
+    """An mbarrier wait that nothing completes gives up after its limit and reports a
+    timeout in the kernel error word; the next kernel on the same context runs."""
+    torch = torch_cuda
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    import time
+    t0 = time.perf_counter()
+    fa_dec.op_wait_selftest(20000, err.data_ptr())          # 20 ms
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 5.0
+    assert int(err.item()) & 1
+    rng = np.random.default_rng(77)
+    o32, _, ref = _attention_case(torch, rng, [40, 300], 8)
+    assert_close(o32, ref, max_abs_tol=1e-4, rel_rms_tol=1e-5, what="attention after a timed-out wait")
