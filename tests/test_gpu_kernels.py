@@ -256,6 +256,8 @@ def _split_f16(x):
 @pytest.mark.parametrize("M,N,K,split", [
     (1, 1024, 1024, 1), (5, 4096, 1024, 4), (16, 1024, 2048, 8), (17, 2048, 1024, 2),
     (64, 6144, 1024, 4), (128, 1024, 3072, 12), (200, 1024, 1024, 1), (300, 512, 2048, 2),
+    # prefill-size row counts, ragged last row tile
+    (256, 4096, 1024, 1), (400, 6144, 1024, 2), (513, 1024, 3072, 4),
 ])
 def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
     torch = torch_cuda
@@ -281,10 +283,11 @@ def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
 
 
 @pytest.mark.parametrize("variant", [0, 1])
-def test_lm_head_argmax_full_vocab(torch_cuda, variant):
+@pytest.mark.parametrize("M,N", [(7, 151936), (300, 4096)])
+def test_lm_head_argmax_full_vocab(torch_cuda, variant, M, N):
     torch = torch_cuda
     rng = np.random.default_rng(3)
-    M, N, K = 7, 151936, 1024
+    K = 1024
     raw, w16 = _q8_device(torch, rng, N, K)
     hi, lo, a_eff = _split_f16(rng.standard_normal((M, K)).astype(np.float32))
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
