@@ -93,6 +93,11 @@ static int ensure_configured() {
     return FA_OK;
 }
 
+namespace fa {
+// Kernel attributes (dynamic shared memory) of the current device, set once.
+int ensure_device_configured() { return ensure_configured(); }
+}  // namespace fa
+
 struct fa_ctx {
     int device = 0;
     fa_model_desc d{};
@@ -192,6 +197,7 @@ namespace fa {
 // defined in other translation units.
 int report_op_error(int code, const char* msg) { return set_err(nullptr, code, msg); }
 int report_ctx_error(const fa_ctx* ctx, int code, const char* msg) { return set_err(ctx, code, msg); }
+int ensure_device_configured();
 }  // namespace fa
 
 template <typename T>
@@ -322,7 +328,8 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
                 tab[(size_t)p * (kD / 2) + i] = make_float2((float)std::cos(th), (float)std::sin(th));
             }
         if (dev_alloc(ctx, &ctx->rope, sizeof(float2) * tab.size())) return fail();
-        if (cudaMemcpy(ctx->rope, tab.data(), sizeof(float2) * tab.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        if (cudaMemcpy(ctx->rope, tab.data(), sizeof(float2) * tab.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaDeviceSynchronize() != cudaSuccess) {
             set_err(ctx, FA_ERR_CUDA, "rope table upload");
             return fail();
         }
@@ -588,6 +595,9 @@ extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n
         return FA_OK;
     };
     rc = run();
+    // host -> device copies from pageable memory can return before their DMA lands, and
+    // the library's stream does not order after them: wait for every copy here
+    if (cudaDeviceSynchronize() != cudaSuccess && rc == FA_OK) rc = set_err(ctx, FA_ERR_CUDA, "weight upload");
     cudaFree(staging);
     if (rc == FA_OK) ctx->loaded = true;
     return rc;
@@ -1057,7 +1067,7 @@ extern "C" int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, cons
             FA_CK(cudaMemcpyAsync(ctx->out_rows, h_out, sizeof(int) * n_out, cudaMemcpyHostToDevice, ctx->stream));
         if (int r = upload_updates(ctx, ui, up)) return r;
         if (embeds)
-            FA_CK(cudaMemcpyAsync(ctx->x, embeds, sizeof(float) * M * d.hidden, cudaMemcpyHostToDevice, ctx->stream));
+            FA_CK(cudaMemcpyAsync(ctx->x, embeds, sizeof(float) * M * d.hidden, cudaMemcpyDefault, ctx->stream));
         // embeddings only: x is the input; with token ids too, rows with id -1 keep their embedding
         const bool x_ready = embeds && !token_ids;
         StepPlan p = n_tiles > 0 ? make_plan(ctx, M, dec_len, x_ready, logits != nullptr, n_tiles)

@@ -102,6 +102,20 @@ void configure_prefill_attention();
 bool make_pool_map(CUtensorMap* tm, const void* pool, long long total_rows);
 void launch_prefill_attention(const CUtensorMap& tm_pool, const PrefillAttnArgs& a, cudaStream_t s);
 
+// --------------------------------------------------------------- k_encoder.cu --
+// Audio encoder / adaptor steps around the GEMMs (x rows are frames).
+void launch_enc_scale(const float* in, int T, int d, int ld, float scale, float* x, cudaStream_t s);
+void launch_enc_resid_ln(float* x, int d, int ld_x, const float* part, int n_part, int T, const float* bias,
+                         const float* mem, int residual, const float* ln_w, const float* ln_b, float eps,
+                         int ln_in_place, __half* out_hi, __half* out_lo, int ld_out, cudaStream_t s);
+void launch_enc_bias_act(const float* part, int n_part, int T, int n, const float* bias, int relu, float* y32,
+                         __half* y_hi, __half* y_lo, int n_sm, cudaStream_t s);
+void launch_enc_fsmn(const float* qkv, int T, int d, const float* w, int K, int pad, float* mem, cudaStream_t s);
+size_t enc_attention_smem(int max_T);
+void configure_encoder(int max_T);
+void launch_enc_attention(const float* qkv, int T, int d, int n_heads, __half* out_hi, __half* out_lo, int max_T,
+                          cudaStream_t s);
+
 // ------------------------------------------------------------------ k_gemm.cu --
 // Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T
 enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1 };

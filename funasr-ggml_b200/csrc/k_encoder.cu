@@ -1,0 +1,248 @@
+// Audio encoder (SANM) and adaptor kernels: the elementwise, normalisation, FSMN and
+// attention steps around the tensor-core GEMMs of compute/encoder_ops.cpp and
+// compute/adaptor_ops.cpp. Rows are frames: x [T][d] row-major, fp32 residual stream;
+// GEMM inputs leave their producer as an f16 pair (hi, lo) like the decoder's.
+#include "fa_kernels.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace fa {
+
+namespace {
+
+__device__ __forceinline__ void split_store_h(float v, __half* hi, __half* lo, size_t o) {
+    const __half h = __float2half_rn(v);
+    hi[o] = h;
+    lo[o] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+}
+
+template <int NT>
+__device__ __forceinline__ double block_sum_d(double v, double* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    double t = 0.0;
+    for (int i = 0; i < NT / 32; ++i) t += sh[i];
+    return t;
+}
+
+// x[t] = scale * in[t] (d columns), zero columns d..ld-1 of the padded copy.
+__global__ void __launch_bounds__(256) enc_scale_kernel(const float* in, int d, int ld, float scale, float* x) {
+    const int t = blockIdx.x;
+    for (int i = threadIdx.x; i < ld; i += 256)
+        x[(size_t)t * ld + i] = i < d ? in[(size_t)t * d + i] * scale : 0.0f;
+}
+
+// One CTA per row. With n_part >= 0 the row is first updated:
+//   x = (residual ? x : 0) + sum_s part[s] + bias (+ mem)
+// Then, with ln_w, y = LayerNorm(x) * w + b (ggml_norm: mean and variance over the d
+// columns, eps inside the root), written back into x when ln_in_place, and as an f16
+// pair [T][ld_out] when out_hi. Without ln_w the pair holds x itself.
+__global__ void __launch_bounds__(256) enc_resid_ln_kernel(float* x, int d, int ld_x, const float* part, int n_part,
+                                                           int T, const float* bias, const float* mem, int residual,
+                                                           const float* ln_w, const float* ln_b, float eps,
+                                                           int ln_in_place, __half* out_hi, __half* out_lo,
+                                                           int ld_out) {
+    __shared__ double sh[8];
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    float* xr = x + (size_t)t * ld_x;
+    constexpr int PER = 8;   // columns per thread (d <= 2048)
+    float v[PER];
+    double s = 0.0;
+#pragma unroll
+    for (int c = 0; c < PER; ++c) {
+        const int i = threadIdx.x + 256 * c;
+        v[c] = 0.0f;
+        if (i >= d) continue;
+        float a = xr[i];
+        if (n_part >= 0) {
+            float acc = residual ? a : 0.0f;
+            for (int p = 0; p < n_part; ++p) acc = __fadd_rn(acc, part[((size_t)p * T + t) * d + i]);
+            if (bias) acc = __fadd_rn(acc, bias[i]);
+            if (mem) acc = __fadd_rn(acc, mem[(size_t)t * d + i]);
+            a = acc;
+            if (!ln_w || !ln_in_place) xr[i] = a;
+        }
+        v[c] = a;
+        s += (double)a;
+    }
+    if (!ln_w) {
+        if (out_hi)
+#pragma unroll
+            for (int c = 0; c < PER; ++c) {
+                const int i = threadIdx.x + 256 * c;
+                if (i < d) split_store_h(v[c], out_hi, out_lo, (size_t)t * ld_out + i);
+            }
+        return;
+    }
+    s = block_sum_d<256>(s, sh);
+    const double mean = s / d;
+    double q = 0.0;
+#pragma unroll
+    for (int c = 0; c < PER; ++c) {
+        const int i = threadIdx.x + 256 * c;
+        if (i < d) q += ((double)v[c] - mean) * ((double)v[c] - mean);
+    }
+    q = block_sum_d<256>(q, sh);
+    const float inv = (float)(1.0 / sqrt(q / d + (double)eps));
+    const float mf = (float)mean;
+#pragma unroll
+    for (int c = 0; c < PER; ++c) {
+        const int i = threadIdx.x + 256 * c;
+        if (i >= d) continue;
+        const float y = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[c], mf), inv), ln_w[i]), ln_b[i]);
+        if (ln_in_place) xr[i] = y;
+        if (out_hi) split_store_h(y, out_hi, out_lo, (size_t)t * ld_out + i);
+    }
+}
+
+// y = sum_s part[s] + bias, optionally ReLU; to fp32 (y32) and/or an f16 pair.
+__global__ void __launch_bounds__(256) enc_bias_act_kernel(const float* part, int n_part, int T, int n,
+                                                           const float* bias, int relu, float* y32, __half* y_hi,
+                                                           __half* y_lo) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t total = (size_t)T * n;
+    for (size_t e = blockIdx.x * (size_t)256 + threadIdx.x; e < total; e += (size_t)gridDim.x * 256) {
+        const int i = (int)(e % n);
+        float acc = 0.0f;
+        for (int p = 0; p < n_part; ++p) acc = __fadd_rn(acc, part[(size_t)p * total + e]);
+        acc = __fadd_rn(acc, bias[i]);
+        if (relu) acc = fmaxf(acc, 0.0f);
+        if (y32) y32[e] = acc;
+        if (y_hi) split_store_h(acc, y_hi, y_lo, e);
+    }
+}
+
+// FSMN memory on v = qkv[:, 2d:3d]: mem[t][c] = v[t][c] + sum_k v[t + k - pad][c] * w[c][k]
+// (zero outside [0, T)); taps w [d][K].
+__global__ void __launch_bounds__(256) enc_fsmn_kernel(const float* qkv, int T, int d, const float* w, int K, int pad,
+                                                       float* mem) {
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < d; c += 256) {
+        const float* vcol = qkv + 2 * d + c;
+        float acc = vcol[(size_t)t * 3 * d];
+        for (int k = 0; k < K; ++k) {
+            const int s = t + k - pad;
+            if (s >= 0 && s < T) acc = fmaf(vcol[(size_t)s * 3 * d], w[(size_t)c * K + k], acc);
+        }
+        mem[(size_t)t * d + c] = acc;
+    }
+}
+
+// Bidirectional multi-head attention over T frames, head_dim 128. CTA = (16 query
+// rows, head), 128 threads: scores of the 16 rows against all keys in shared memory
+// (fp32), softmax per row, then thread j accumulates output dim j for the 16 rows.
+constexpr int ATT_ROWS = 16;
+constexpr int HD = 128;
+
+__global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, int T, int d, int n_heads,
+                                                            __half* out_hi, __half* out_lo, int max_T) {
+    extern __shared__ float sm[];
+    float* qs = sm;                                  // [16][128]
+    float* sc = sm + ATT_ROWS * HD;                  // [16][max_T]
+    pdl_trigger();
+    pdl_wait();
+    const int h = blockIdx.y;
+    const int r0 = blockIdx.x * ATT_ROWS;
+    const int nr = min(ATT_ROWS, T - r0);
+    const int ld = 3 * d;
+    const float scale = 1.0f / sqrtf((float)HD);
+    for (int e = threadIdx.x; e < ATT_ROWS * HD; e += 128) {
+        const int r = e / HD, j = e % HD;
+        qs[e] = r < nr ? qkv[(size_t)(r0 + r) * ld + h * HD + j] * scale : 0.0f;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // scores: warp w takes keys w, w+4, ...; lanes split the 128 dims
+    for (int t = warp; t < T; t += 4) {
+        const float4 kv = *reinterpret_cast<const float4*>(qkv + (size_t)t * ld + d + h * HD + 4 * lane);
+        for (int r = 0; r < nr; ++r) {
+            const float4 qv = *reinterpret_cast<const float4*>(qs + r * HD + 4 * lane);
+            float p = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+            if (lane == 0) sc[r * max_T + t] = p;
+        }
+    }
+    __syncthreads();
+    // softmax per row: warp w takes rows w, w+4, ...
+    for (int r = warp; r < nr; r += 4) {
+        float* row = sc + r * max_T;
+        float m = -INFINITY;
+        for (int t = lane; t < T; t += 32) m = fmaxf(m, row[t]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float s = 0.0f;
+        for (int t = lane; t < T; t += 32) {
+            const float e = expf(row[t] - m);
+            row[t] = e;
+            s += e;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float inv = 1.0f / s;
+        for (int t = lane; t < T; t += 32) row[t] *= inv;
+    }
+    __syncthreads();
+    // output: thread j owns head dim j of the 16 rows
+    const int j = threadIdx.x;
+    float acc[ATT_ROWS];
+#pragma unroll
+    for (int r = 0; r < ATT_ROWS; ++r) acc[r] = 0.0f;
+    for (int t = 0; t < T; ++t) {
+        const float v = qkv[(size_t)t * ld + 2 * d + h * HD + j];
+#pragma unroll
+        for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(sc[r * max_T + t], v, acc[r]);
+    }
+    for (int r = 0; r < nr; ++r) split_store_h(acc[r], out_hi, out_lo, (size_t)(r0 + r) * d + h * HD + j);
+}
+
+}  // namespace
+
+void launch_enc_scale(const float* in, int T, int d, int ld, float scale, float* x, cudaStream_t s) {
+    enc_scale_kernel<<<T, 256, 0, s>>>(in, d, ld, scale, x);
+}
+
+void launch_enc_resid_ln(float* x, int d, int ld_x, const float* part, int n_part, int T, const float* bias,
+                         const float* mem, int residual, const float* ln_w, const float* ln_b, float eps,
+                         int ln_in_place, __half* out_hi, __half* out_lo, int ld_out, cudaStream_t s) {
+    launch_k(enc_resid_ln_kernel, dim3(T), dim3(256), 0, s, x, d, ld_x, part, n_part, T, bias, mem, residual, ln_w,
+             ln_b, eps, ln_in_place, out_hi, out_lo, ld_out);
+}
+
+void launch_enc_bias_act(const float* part, int n_part, int T, int n, const float* bias, int relu, float* y32,
+                         __half* y_hi, __half* y_lo, int n_sm, cudaStream_t s) {
+    const size_t total = (size_t)T * n;
+    int blocks = (int)std::min<size_t>((total + 255) / 256, (size_t)n_sm * 8);
+    if (blocks < 1) blocks = 1;
+    launch_k(enc_bias_act_kernel, dim3(blocks), dim3(256), 0, s, part, n_part, T, n, bias, relu, y32, y_hi, y_lo);
+}
+
+void launch_enc_fsmn(const float* qkv, int T, int d, const float* w, int K, int pad, float* mem, cudaStream_t s) {
+    launch_k(enc_fsmn_kernel, dim3(T), dim3(256), 0, s, qkv, T, d, w, K, pad, mem);
+}
+
+size_t enc_attention_smem(int max_T) { return sizeof(float) * (size_t)ATT_ROWS * (HD + max_T); }
+
+void configure_encoder(int max_T) {
+    cudaFuncSetAttribute(enc_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)enc_attention_smem(max_T));
+}
+
+void launch_enc_attention(const float* qkv, int T, int d, int n_heads, __half* out_hi, __half* out_lo, int max_T,
+                          cudaStream_t s) {
+    dim3 grid((T + ATT_ROWS - 1) / ATT_ROWS, n_heads);
+    launch_k(enc_attention_kernel, grid, dim3(128), enc_attention_smem(max_T), s, qkv, T, d, n_heads, out_hi, out_lo,
+             max_T);
+}
+
+}  // namespace fa

@@ -56,6 +56,13 @@ class _TensorView(ctypes.Structure):
                 ("data", ctypes.c_void_p), ("nbytes", ctypes.c_size_t)]
 
 
+class _EncoderDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in (
+        "input_dim", "output_size", "attention_heads", "linear_units", "num_blocks", "tp_blocks", "kernel_size",
+        "sanm_shift", "adaptor_hidden", "adaptor_output", "adaptor_blocks", "adaptor_heads", "adaptor_ffn",
+        "max_frames")]
+
+
 class _SchedConfig(ctypes.Structure):
     _fields_ = [("max_batch_rows", ctypes.c_int), ("prefill_chunk", ctypes.c_int), ("max_running", ctypes.c_int),
                 ("eos_id", ctypes.c_int)]
@@ -109,6 +116,12 @@ def lib():
         "fa_seq_block_table": ([_P, _I, _P, _I, _P], _I),
         "fa_forward_rows": ([_P, _I, _P, _P, _P, _I, _P, _P, _P], _I),
         "fa_ctx_desc": ([_P, _P], _I),
+        "fa_encoder_default_desc": ([_P], None),
+        "fa_encoder_create": ([_I, _P], _P),
+        "fa_encoder_destroy": ([_P], None),
+        "fa_encoder_load_weights": ([_P, _P, _I], _I),
+        "fa_encoder_forward": ([_P, _P, _I, _P], _I),
+        "fa_encoder_forward_dev": ([_P, _P, _I, _P, _P], _I),
         "fa_sched_create": ([_P, _P], _P),
         "fa_sched_destroy": ([_P], None),
         "fa_sched_submit": ([_P, ctypes.c_int64, _P, _P, _I, _I], _I),
@@ -459,6 +472,60 @@ def op_argmax_scratch_bytes(M, N) -> int:
 def op_q8_gemm_argmax(a16, a16_lo, M, K, w16, N, scratch, nxt, logits=0, variant=0, stream=0):
     _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, w16, N, scratch, nxt, logits or None, variant,
                                       stream or None))
+
+
+# ---------------------------------------------------------------- encoder --
+def _views(weights):
+    views = (_TensorView * len(weights))()
+    keep = []
+    for i, (name, (t, ne, arr)) in enumerate(weights.items()):
+        arr = np.ascontiguousarray(arr)
+        nb = name.encode()
+        keep += [arr, nb]
+        views[i].name = nb
+        views[i].type = t
+        views[i].ne[0] = int(ne[0])
+        views[i].ne[1] = int(ne[1]) if len(ne) > 1 else 1
+        views[i].data = arr.ctypes.data
+        views[i].nbytes = arr.nbytes
+    return views, keep
+
+
+class Encoder:
+    """fa_encoder_*: SANM encoder + adaptor on one GPU, LFR features -> decoder embeddings."""
+
+    def __init__(self, device: int = 0, **desc):
+        self.desc = _EncoderDesc()
+        lib().fa_encoder_default_desc(ctypes.byref(self.desc))
+        for k, v in desc.items():
+            setattr(self.desc, k, v)
+        self.e = lib().fa_encoder_create(device, ctypes.byref(self.desc))
+        if not self.e:
+            raise FaError(FA_ERR_CUDA, last_error(None))
+
+    def load_weights(self, weights):
+        views, keep = _views(weights)
+        _check(lib().fa_encoder_load_weights(self.e, views, len(weights)))
+
+    def forward(self, lfr: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(lfr, np.float32)
+        out = np.zeros((x.shape[0], self.desc.adaptor_output), np.float32)
+        _check(lib().fa_encoder_forward(self.e, _p(x), x.shape[0], _p(out)))
+        return out
+
+    def forward_dev(self, lfr_ptr: int, T: int, out_ptr: int, stream: int = 0):
+        _check(lib().fa_encoder_forward_dev(self.e, lfr_ptr, T, out_ptr, stream or None))
+
+    def close(self):
+        if getattr(self, "e", None):
+            lib().fa_encoder_destroy(self.e)
+            self.e = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ------------------------------------------------------ continuous batching --

@@ -86,3 +86,82 @@ def decoder_desc(cfg: dict, **over) -> dict:
 def audio_embeds(rng: np.random.Generator, n: int, hidden: int, scale: float = 1.0) -> np.ndarray:
     """Stand-in for adaptor output frames [n][hidden] (the encoder is out of scope)."""
     return (rng.standard_normal((n, hidden), dtype=np.float32) * scale).astype(np.float32)
+
+
+# ------------------------------------------------------------ encoder --
+ENCODER = dict(input_dim=560, output_size=512, attention_heads=4, linear_units=2048, num_blocks=50, tp_blocks=20,
+               kernel_size=11, sanm_shift=0)
+ADAPTOR = dict(input_dim=512, hidden_dim=2048, output_dim=1024, num_blocks=2, attention_heads=8, ffn_dim=256)
+
+
+def make_encoder_weights(ecfg: dict = ENCODER, acfg: dict = ADAPTOR, seed: int = 0,
+                         d_range=(0.0002, 0.001)) -> Dict[str, Tuple[int, Tuple[int, int], np.ndarray]]:
+    """Random-init SANM encoder + adaptor weights in the reference's GGUF layout
+    (model/loader.cpp:21-80,135-200) and types (tools/hf_convert_ggml_q8.py:308-323):
+    2-D weights whose input dimension is a multiple of 32 are Q8_0, the others
+    (encoder0's 560-wide projections) and the FSMN taps are F16, norms and biases F32.
+    The default scales give weights of standard deviation ~1/sqrt(fan-in)."""
+    rng = np.random.default_rng(seed)
+    lo, hi = d_range
+    w = {}
+
+    def mat(name, n, k):
+        if k % 32 == 0:
+            w[name] = (TYPE_Q8_0, (k, n), q8_0_random(rng, n, k, lo, hi))
+        else:
+            x = (rng.standard_normal((n, k)) / np.sqrt(k)).astype(np.float16)
+            w[name] = (TYPE_F16, (k, n), x.view(np.uint16))
+
+    def vec(name, n, mean, std):
+        w[name] = (TYPE_F32, (n, 1), (mean + std * rng.standard_normal(n)).astype(np.float32))
+
+    def layer(p, d_in, d):
+        vec(p + ".norm1.weight", d_in, 1.0, 0.1)
+        vec(p + ".norm1.bias", d_in, 0.0, 0.1)
+        for nm in ("linear_q", "linear_k", "linear_v"):
+            mat(p + f".self_attn.{nm}.weight", d, d_in)
+            vec(p + f".self_attn.{nm}.bias", d, 0.0, 0.05)
+        mat(p + ".self_attn.linear_out.weight", d, d)
+        vec(p + ".self_attn.linear_out.bias", d, 0.0, 0.05)
+        taps = (rng.standard_normal((d, ecfg["kernel_size"])) * 0.1).astype(np.float16)
+        w[p + ".self_attn.fsmn_block.weight"] = (TYPE_F16, (ecfg["kernel_size"], d), taps.view(np.uint16))
+        vec(p + ".norm2.weight", d, 1.0, 0.1)
+        vec(p + ".norm2.bias", d, 0.0, 0.1)
+        mat(p + ".feed_forward.w_1.weight", ecfg["linear_units"], d)
+        vec(p + ".feed_forward.w_1.bias", ecfg["linear_units"], 0.0, 0.05)
+        mat(p + ".feed_forward.w_2.weight", d, ecfg["linear_units"])
+        vec(p + ".feed_forward.w_2.bias", d, 0.0, 0.05)
+
+    d = ecfg["output_size"]
+    layer("audio_encoder.encoders0.0", ecfg["input_dim"], d)
+    for i in range(ecfg["num_blocks"] - 1):
+        layer(f"audio_encoder.encoders.{i}", d, d)
+    for nm in ("after_norm", "tp_norm"):
+        vec(f"audio_encoder.{nm}.weight", d, 1.0, 0.1)
+        vec(f"audio_encoder.{nm}.bias", d, 0.0, 0.1)
+    for i in range(ecfg["tp_blocks"]):
+        layer(f"audio_encoder.tp_encoders.{i}", d, d)
+    D = acfg["output_dim"]
+    mat("audio_adaptor.linear1.weight", acfg["hidden_dim"], acfg["input_dim"])
+    vec("audio_adaptor.linear1.bias", acfg["hidden_dim"], 0.0, 0.05)
+    mat("audio_adaptor.linear2.weight", D, acfg["hidden_dim"])
+    vec("audio_adaptor.linear2.bias", D, 0.0, 0.05)
+    for i in range(acfg["num_blocks"]):
+        p = f"audio_adaptor.blocks.{i}"
+        vec(p + ".norm1.weight", D, 1.0, 0.1)
+        vec(p + ".norm1.bias", D, 0.0, 0.1)
+        for nm in ("linear_q", "linear_k", "linear_v", "linear_out"):
+            mat(p + f".self_attn.{nm}.weight", D, D)
+            vec(p + f".self_attn.{nm}.bias", D, 0.0, 0.05)
+        vec(p + ".norm2.weight", D, 1.0, 0.1)
+        vec(p + ".norm2.bias", D, 0.0, 0.1)
+        mat(p + ".feed_forward.w_1.weight", acfg["ffn_dim"], D)
+        vec(p + ".feed_forward.w_1.bias", acfg["ffn_dim"], 0.0, 0.05)
+        mat(p + ".feed_forward.w_2.weight", D, acfg["ffn_dim"])
+        vec(p + ".feed_forward.w_2.bias", D, 0.0, 0.05)
+    return w
+
+
+def lfr_features(rng: np.random.Generator, T: int, dim: int = 560) -> np.ndarray:
+    """Stand-in for LFR-stacked log-mel frames [T][560] (the front end is out of scope)."""
+    return (rng.standard_normal((T, dim)) * 2.0 - 4.0).astype(np.float32)

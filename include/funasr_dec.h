@@ -142,7 +142,8 @@ FA_API int fa_seq_block_table(const fa_ctx* ctx, int seq_id, int* pages, int max
  * Rows of one sequence take consecutive positions in row order (chunked prefill);
  * every row's K/V is in the cache before any row's attention, so a prefill chunk is
  * causal within itself. Inputs: token_ids [n_rows] (embedding lookup on the device) or
- * embeds [n_rows][hidden] f32 (audio frames; exactly one of the two).
+ * embeds [n_rows][hidden] f32 (audio frames; exactly one of the two), in host or device
+ * memory (the encoder's output can be passed as it is).
  * Outputs (optional): next_ids [n_rows] = argmax of each row's logits (first maximum),
  * logits [n_rows][vocab] f32. */
 FA_API int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
@@ -314,6 +315,39 @@ FA_API int fa_palloc_compact(fa_palloc* pa, int* src, int* dst, int max_moves, i
  * pipelined kernel uses. The wait gives up, sets bit 1 (timeout) in *err_dev and the
  * kernel returns, leaving the context usable. */
 FA_API int fa_op_wait_selftest(int limit_us, int* err_dev, void* stream);
+
+/* ---- audio encoder (SANM) + adaptor: the producer of the prefill embeddings ----
+ * Replaces compute/encoder_adaptor_gpu.hpp:27-677 (GPUEncoderAdaptorRunner::forward_on_gpu
+ * :88-191) with the graphs of compute/encoder_ops.cpp:17-290 and compute/adaptor_ops.cpp:11-149.
+ * Input: LFR features [T][input_dim] f32 (the front end's output); output: decoder input
+ * embeddings [T][adaptor_output] f32, ready for fa_prefill / fa_forward (which accept
+ * device pointers too). Weights: audio_encoder.* and audio_adaptor.* tensors
+ * (model/loader.cpp:21-80,135-200), 2-D ones Q8_0, F16, BF16 or F32. */
+typedef struct fa_encoder fa_encoder;
+typedef struct fa_encoder_desc {
+    int input_dim;       /* 560 = 80 mels x LFR 7 */
+    int output_size;     /* 512, attention_heads x 128 */
+    int attention_heads; /* 4 */
+    int linear_units;    /* 2048 */
+    int num_blocks;      /* 50: encoder0 + 49 */
+    int tp_blocks;       /* 20 */
+    int kernel_size;     /* FSMN taps, 11 */
+    int sanm_shift;      /* 0 */
+    int adaptor_hidden;  /* 2048 */
+    int adaptor_output;  /* 1024 = decoder hidden, adaptor_heads x 128 */
+    int adaptor_blocks;  /* 2 */
+    int adaptor_heads;   /* 8 */
+    int adaptor_ffn;     /* 256 */
+    int max_frames;      /* longest input, <= 4096 */
+} fa_encoder_desc;
+FA_API void fa_encoder_default_desc(fa_encoder_desc* desc);
+FA_API fa_encoder* fa_encoder_create(int device, const fa_encoder_desc* desc); /* NULL: fa_last_error(NULL) */
+FA_API void fa_encoder_destroy(fa_encoder* e);
+FA_API int fa_encoder_load_weights(fa_encoder* e, const fa_tensor_view* tensors, int n);
+/* Host in, host out; synchronous. */
+FA_API int fa_encoder_forward(fa_encoder* e, const float* lfr, int T, float* embeds);
+/* Device (or host) pointers, on `stream` (NULL: the encoder's stream); returns when done. */
+FA_API int fa_encoder_forward_dev(fa_encoder* e, const float* lfr_dev, int T, float* embeds_dev, void* stream);
 
 /* Library version string. */
 FA_API const char* fa_version(void);
