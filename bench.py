@@ -50,11 +50,13 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between kernels")
-    ap.add_argument("--workload", default="decode", choices=["decode", "attention", "gemm", "prefill", "serve"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "attention", "gemm", "prefill", "serve", "pipeline"],
                     help="attention: kernel (2) alone over one layer's pages at the same batch and context; "
                          "gemm: the decode step's weight GEMMs alone; prefill: batched chunked prefill of "
                          "16 utterances then 64 greedy tokens each; serve: continuous batching of --streams "
-                         "streams with Poisson arrivals")
+                         "streams with Poisson arrivals; pipeline: one 5 s utterance through the encoder, "
+                         "adaptor, prefill and 32 greedy tokens")
     ap.add_argument("--streams", type=int, default=1024, help="serve: streams over all GPUs")
     ap.add_argument("--arrival-rate", type=float, default=100.0, help="serve: streams per second (Poisson)")
     ap.add_argument("--kv-gb", type=float, default=160.0, help="serve: page pool per GPU, GB")
@@ -571,6 +573,94 @@ def run_serve(a):
     fa_multi.shutdown()
 
 
+# --------------------------------------------------------- one utterance --
+def run_pipeline(a):
+    """One utterance end to end on the GPU (the front end excluded): 5 s of audio as 82
+    LFR frames of 560 features (stand-in values), the full SANM encoder (50 + 20
+    layers) and adaptor, a prefill of 16 prompt tokens + 82 audio frames + 14 prompt
+    tokens, then exactly 32 greedy tokens (EOS ignored), batch 1, random-init Q8_0
+    weights everywhere. Reports the latency per utterance and the real-time factor;
+    the CPU restatement of the same work runs beside it on the host cores."""
+    import torch
+    import fa_dec
+
+    rank, local, world = fa_multi.init("nccl")
+    torch.cuda.set_device(local)
+    cfg = fa_synth.QWEN3_06B
+    w = fa_synth.make_weights(cfg, seed=1)
+    we = fa_synth.make_encoder_weights(seed=2)
+    rng = np.random.default_rng(rank)
+    T, n_new = 82, 32
+    lfr = fa_synth.lfr_features(rng, T)
+    table = w["llm.model.embed_tokens.weight"][2].reshape(cfg["vocab"], cfg["hidden"])
+    pre, suf = rng.integers(0, cfg["vocab"], 16), rng.integers(0, cfg["vocab"], 14)
+    emb_pre = (table[pre].astype(np.uint32) << 16).view(np.float32)
+    emb_suf = (table[suf].astype(np.uint32) << 16).view(np.float32)
+    enc = fa_dec.Encoder(local, max_frames=256)
+    enc.load_weights(we)
+    dec = fa_dec.Decoder(local, **fa_synth.decoder_desc(cfg, max_ctx=512, n_pages=64, max_seqs=2, max_rows=256))
+    dec.load_weights(w)
+
+    def utterance():
+        audio = enc.forward(lfr)
+        rows = np.concatenate([emb_pre, audio, emb_suf]).astype(np.float32)
+        s = dec.seq_open(512)
+        first, _ = dec.prefill(s, rows)
+        toks = [first]
+        for _ in range(n_new - 1):
+            nx, _ = dec.decode_step([s], [toks[-1]])
+            toks.append(int(nx[0]))
+        dec.seq_close(s)
+        return toks
+
+    for _ in range(max(a.warmup, 1)):
+        utterance()
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    K = max(a.steps, 1)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        toks = utterance()
+    ms = (time.perf_counter() - t0) * 1e3 / K
+    ms = fa_multi.reduce(ms, "max")
+    cpu = None
+    if rank == 0 and not a.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        import encoder as enc_oracle
+        oracle.build()
+        oracle.set_num_threads(len(os.sched_getaffinity(0)))
+        t1 = time.perf_counter()
+        audio = enc_oracle.adaptor_forward(we, enc_oracle.encoder_forward(we, lfr))
+        rows = np.concatenate([emb_pre, audio, emb_suf]).astype(np.float32)
+        od = oracle.OracleDecoder(cfg, w, n_pages=16, max_seqs=1, max_pages_per_seq=16, max_pos=256,
+                                  mode=oracle.MODE_GGML_CPU)
+        od.seq_open(0)
+        _, nx = od.forward([0] * len(rows), embeds=rows, want_logits=False)
+        tok = int(nx[-1])
+        for _ in range(n_new - 1):
+            _, nx = od.forward([0], tokens=[tok], want_logits=False)
+            tok = int(nx[0])
+        cpu_ms = (time.perf_counter() - t1) * 1e3
+        cpu = {"value": cpu_ms, "unit": "ms per utterance", "cores": oracle.num_threads(), "kind": "port",
+               "sample": "one utterance: encoder + adaptor in numpy float64, decoder prefill + 32 tokens in the "
+                         "C++ oracle (ggml-CPU arithmetic); CPU restatement of the reference (ggml unavailable)"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "utterance latency, encoder + adaptor + prefill + 32 greedy tokens", "value": ms,
+            "unit": "ms", "n_gpus": world, "steps": K, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic: random-init Q8_0 encoder, adaptor and decoder; stand-in LFR frames",
+            "config": {"workload": "5 s utterance: 82 LFR frames x 560, SANM 50+20 layers, adaptor, 112-row "
+                                   "prefill, 32 greedy tokens, batch 1",
+                       "rtf": ms / 5000.0},
+            "cpu_baseline": cpu, "gpu_launches": None,
+        }), flush=True)
+    enc.close()
+    dec.close()
+    fa_multi.shutdown()
+
+
 # -------------------------------------------------------------- reference --
 def run_reference(a):
     """The reference's CPU path (ggml) cannot be built here, so its restatement (the
@@ -633,5 +723,7 @@ if __name__ == "__main__":
         run_prefill(args)
     elif args.workload == "serve":
         run_serve(args)
+    elif args.workload == "pipeline":
+        run_pipeline(args)
     else:
         run_ours(args)

@@ -10,6 +10,7 @@
 //   GPURunner    compute/gpu_runner.hpp:22-236         warmup, forward, argmax, is_warmed_up
 //   KVCache      compute/kv_cache.hpp:25-168           init, clear, free, n_past, n_ctx, n_layers,
 //                                                      kv_dim, is_initialized, set_n_past
+//   GPUEncoderAdaptorRunner compute/encoder_adaptor_gpu.hpp:27-191  init, forward_on_gpu
 // Deviations, all forced by ggml's absence or by the paged cache:
 //   - weights come as GGUF tensor views or a GGUF file path instead of LLMWeights
 //     (ggml_tensor pointers);
@@ -411,6 +412,58 @@ private:
         return false;
     }
     GPUContext& ctx_;
+    std::string err_;
+};
+
+// The audio encoder + adaptor (compute/encoder_adaptor_gpu.hpp:27-677): LFR features
+// [frames][input_dim] -> decoder input embeddings [frames][adaptor_output], kept on the
+// device (forward_on_gpu, the reference's name) or copied to the host (forward).
+class GPUEncoderAdaptorRunner {
+public:
+    GPUEncoderAdaptorRunner() = default;
+    ~GPUEncoderAdaptorRunner() { release(); }
+    GPUEncoderAdaptorRunner(const GPUEncoderAdaptorRunner&) = delete;
+    GPUEncoderAdaptorRunner& operator=(const GPUEncoderAdaptorRunner&) = delete;
+
+    // weights: the audio_encoder.* and audio_adaptor.* GGUF tensors (host memory)
+    bool init(const std::vector<fa_tensor_view>& weights, int max_frames = 1024, int gpu_id = 0) {
+        release();
+        fa_encoder_desc d;
+        fa_encoder_default_desc(&d);
+        d.max_frames = max_frames;
+        e_ = fa_encoder_create(gpu_id, &d);
+        if (!e_) return fail();
+        if (fa_encoder_load_weights(e_, weights.data(), (int)weights.size()) != FA_OK) return fail();
+        desc_ = d;
+        return true;
+    }
+    // embeds_dev: frames x adaptor_output f32 on the device (e.g. straight into fa_prefill)
+    bool forward_on_gpu(const float* lfr_dev, int input_dim, int frames, float* embeds_dev, int& out_frames) {
+        out_frames = 0;
+        if (!e_ || input_dim != desc_.input_dim) return false;
+        if (fa_encoder_forward_dev(e_, lfr_dev, frames, embeds_dev, nullptr) != FA_OK) return fail();
+        out_frames = frames;
+        return true;
+    }
+    bool forward(const float* lfr, int input_dim, int frames, std::vector<float>& embeds) {
+        if (!e_ || input_dim != desc_.input_dim) return false;
+        embeds.resize((size_t)frames * desc_.adaptor_output);
+        return fa_encoder_forward(e_, lfr, frames, embeds.data()) == FA_OK || fail();
+    }
+    int output_dim() const { return desc_.adaptor_output; }
+    const std::string& last_error() const { return err_; }
+
+private:
+    bool fail() {
+        err_ = fa_last_error(nullptr);
+        return false;
+    }
+    void release() {
+        if (e_) fa_encoder_destroy(e_);
+        e_ = nullptr;
+    }
+    fa_encoder* e_ = nullptr;
+    fa_encoder_desc desc_{};
     std::string err_;
 };
 
