@@ -601,16 +601,25 @@ def run_pipeline(a):
     dec = fa_dec.Decoder(local, **fa_synth.decoder_desc(cfg, max_ctx=512, n_pages=64, max_seqs=2, max_rows=256))
     dec.load_weights(w)
 
+    parts = {"encoder_ms": 0.0, "prefill_ms": 0.0, "decode_ms": 0.0}
+
     def utterance():
+        t0 = time.perf_counter()
         audio = enc.forward(lfr)
+        t1 = time.perf_counter()
         rows = np.concatenate([emb_pre, audio, emb_suf]).astype(np.float32)
         s = dec.seq_open(512)
         first, _ = dec.prefill(s, rows)
+        t2 = time.perf_counter()
         toks = [first]
         for _ in range(n_new - 1):
             nx, _ = dec.decode_step([s], [toks[-1]])
             toks.append(int(nx[0]))
         dec.seq_close(s)
+        t3 = time.perf_counter()
+        parts["encoder_ms"] += (t1 - t0) * 1e3
+        parts["prefill_ms"] += (t2 - t1) * 1e3
+        parts["decode_ms"] += (t3 - t2) * 1e3
         return toks
 
     for _ in range(max(a.warmup, 1)):
@@ -618,6 +627,8 @@ def run_pipeline(a):
     torch.cuda.synchronize()
     fa_multi.barrier()
     K = max(a.steps, 1)
+    for k in parts:
+        parts[k] = 0.0
     t0 = time.perf_counter()
     for _ in range(K):
         toks = utterance()
@@ -653,7 +664,7 @@ def run_pipeline(a):
             "data": "synthetic: random-init Q8_0 encoder, adaptor and decoder; stand-in LFR frames",
             "config": {"workload": "5 s utterance: 82 LFR frames x 560, SANM 50+20 layers, adaptor, 112-row "
                                    "prefill, 32 greedy tokens, batch 1",
-                       "rtf": ms / 5000.0},
+                       "rtf": ms / 5000.0, **{k: v / K for k, v in parts.items()}},
             "cpu_baseline": cpu, "gpu_launches": None,
         }), flush=True)
     enc.close()

@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -81,6 +82,15 @@ struct fa_encoder {
     size_t part_elems = 0;
     int* err_dev = nullptr;
     int* h_err = nullptr;
+    // utterance layout of the rows: seg[t] = (first, end) row of row t's utterance;
+    // attention tiles (first row, rows, utterance start, utterance length)
+    int2* seg_dev = nullptr;
+    int4* tiles_dev = nullptr;
+    int2* h_seg = nullptr;
+    int4* h_tiles = nullptr;
+    int max_tiles = 0;
+    bool use_graphs = true;
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;   // (rows, tiles) -> the whole forward
 
     template <typename T>
     int alloc(T** p, size_t bytes) {
@@ -95,8 +105,11 @@ struct fa_encoder {
     }
     ~fa_encoder() {
         if (device >= 0) cudaSetDevice(device);
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         for (void* p : allocs) cudaFree(p);
         if (h_err) cudaFreeHost(h_err);
+        if (h_seg) cudaFreeHost(h_seg);
+        if (h_tiles) cudaFreeHost(h_tiles);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -247,7 +260,7 @@ int gemm(fa_encoder* e, const __half* a, const __half* a_lo, int T, const Lin& L
     return g.n_split;
 }
 
-void enc_layer(fa_encoder* e, const EncLayer& L, int T, bool residual, const float* x_in, int ld_in) {
+void enc_layer(fa_encoder* e, const EncLayer& L, int T, int n_tiles, bool residual, const float* x_in, int ld_in) {
     const fa_encoder_desc& d = e->d;
     const int D = d.output_size;
     cudaStream_t s = e->stream;
@@ -259,8 +272,9 @@ void enc_layer(fa_encoder* e, const EncLayer& L, int T, bool residual, const flo
                             L.n1b, 1e-5f, 0, in_hi, in_lo, L.qkv.kp, s);
     int sp = gemm(e, in_hi, in_lo, T, L.qkv);
     fa::launch_enc_bias_act(e->part, sp, T, L.qkv.n, L.qkv.b, 0, e->qkv, nullptr, nullptr, e->n_sm, s);
-    fa::launch_enc_fsmn(e->qkv, T, D, L.fsmn, d.kernel_size, (d.kernel_size - 1) / 2 - d.sanm_shift, e->mem, s);
-    fa::launch_enc_attention(e->qkv, T, D, d.attention_heads, e->att, e->att_lo, d.max_frames, s);
+    fa::launch_enc_fsmn(e->qkv, T, e->seg_dev, D, L.fsmn, d.kernel_size, (d.kernel_size - 1) / 2 - d.sanm_shift,
+                        e->mem, s);
+    fa::launch_enc_attention(e->qkv, e->tiles_dev, n_tiles, D, d.attention_heads, e->att, e->att_lo, d.max_frames, s);
     sp = gemm(e, e->att, e->att_lo, T, L.out);
     // x = (x) + out + bias + memory, then norm2
     fa::launch_enc_resid_ln(e->x, D, D, e->part, sp, T, L.out.b, e->mem, residual ? 1 : 0, L.n2w, L.n2b, 1e-5f, 0,
@@ -272,7 +286,7 @@ void enc_layer(fa_encoder* e, const EncLayer& L, int T, bool residual, const flo
                             nullptr, 0, s);
 }
 
-void ada_block(fa_encoder* e, const AdaBlock& B, int T) {
+void ada_block(fa_encoder* e, const AdaBlock& B, int T, int n_tiles) {
     const fa_encoder_desc& d = e->d;
     const int D = d.adaptor_output;
     cudaStream_t s = e->stream;
@@ -280,7 +294,7 @@ void ada_block(fa_encoder* e, const AdaBlock& B, int T) {
                             D, s);
     int sp = gemm(e, e->xn, e->xn_lo, T, B.qkv);
     fa::launch_enc_bias_act(e->part, sp, T, B.qkv.n, B.qkv.b, 0, e->qkv, nullptr, nullptr, e->n_sm, s);
-    fa::launch_enc_attention(e->qkv, T, D, d.adaptor_heads, e->att, e->att_lo, d.max_frames, s);
+    fa::launch_enc_attention(e->qkv, e->tiles_dev, n_tiles, D, d.adaptor_heads, e->att, e->att_lo, d.max_frames, s);
     sp = gemm(e, e->att, e->att_lo, T, B.out);
     fa::launch_enc_resid_ln(e->x, D, D, e->part, sp, T, B.out.b, nullptr, 1, B.n2w, B.n2b, 1e-12f, 0, e->xn, e->xn_lo,
                             D, s);
@@ -364,6 +378,7 @@ extern "C" fa_encoder* fa_encoder_create(int device, const fa_encoder_desc* desc
             part = std::max(part, (size_t)sp * m * sh[0]);
         }
     e->part_elems = part;
+    e->max_tiles = 2 * T;
     if (e->alloc(&e->in_raw, sizeof(float) * (size_t)T * d.input_dim) || e->alloc(&e->in0, sizeof(float) * (size_t)T * kin) ||
         e->alloc(&e->x, sizeof(float) * (size_t)T * std::max(d.output_size, d.adaptor_output)) ||
         e->alloc(&e->qkv, sizeof(float) * (size_t)T * nmax) || e->alloc(&e->mem, sizeof(float) * (size_t)T * d.output_size) ||
@@ -374,6 +389,9 @@ extern "C" fa_encoder* fa_encoder_create(int device, const fa_encoder_desc* desc
         e->alloc(&e->hid, sizeof(__half) * (size_t)T * std::max(d.linear_units, d.adaptor_hidden)) ||
         e->alloc(&e->hid_lo, sizeof(__half) * (size_t)T * std::max(d.linear_units, d.adaptor_hidden)) ||
         e->alloc(&e->xn0, sizeof(__half) * (size_t)T * kin) || e->alloc(&e->xn0_lo, sizeof(__half) * (size_t)T * kin) ||
+        e->alloc(&e->seg_dev, sizeof(int2) * (size_t)T) || e->alloc(&e->tiles_dev, sizeof(int4) * (size_t)2 * T) ||
+        cudaMallocHost(&e->h_seg, sizeof(int2) * (size_t)T) != cudaSuccess ||
+        cudaMallocHost(&e->h_tiles, sizeof(int4) * (size_t)2 * T) != cudaSuccess ||
         e->alloc(&e->err_dev, sizeof(int)) || cudaMallocHost(&e->h_err, sizeof(int)) != cudaSuccess) {
         delete e;
         return nullptr;
@@ -441,27 +459,20 @@ extern "C" int fa_encoder_load_weights(fa_encoder* e, const fa_tensor_view* tens
     return rc;
 }
 
-// Device in, device out: lfr [T][input_dim] f32 -> embeds [T][adaptor_output] f32, on `stream`
-// (NULL: the encoder's own stream, synchronised before returning).
-extern "C" int fa_encoder_forward_dev(fa_encoder* e, const float* lfr_dev, int T, float* embeds_dev, void* stream) {
-    if (!e || !lfr_dev || !embeds_dev) return fail("fa_encoder_forward: bad argument", FA_ERR_INVALID_ARG);
-    if (!e->loaded) return fail("encoder weights not loaded", FA_ERR_NOT_READY);
-    if (T < 1 || T > e->d.max_frames)
-        return fail("fa_encoder_forward: T must be in [1, max_frames = " + std::to_string(e->d.max_frames) + "]",
-                    FA_ERR_CAPACITY);
-    cudaSetDevice(e->device);
+// The whole encoder + adaptor over the rows in in_raw (T rows, n_tiles attention tiles
+// in tiles_dev), leaving the embeddings in x. Launch order only; no synchronisation.
+static void enqueue(fa_encoder* e, int T, int n_tiles, cudaStream_t s) {
     const fa_encoder_desc& d = e->d;
-    cudaStream_t saved = e->stream;
-    if (stream) e->stream = (cudaStream_t)stream;
-    cudaStream_t s = e->stream;
     const int kin = pad64(d.input_dim);
+    cudaStream_t saved = e->stream;
+    e->stream = s;
     fa::set_launch_pdl(true);
-    fa::launch_enc_scale(lfr_dev, T, d.input_dim, kin, std::sqrt((float)d.output_size), e->in0, s);
-    enc_layer(e, e->e0, T, false, e->in0, kin);
-    for (const auto& L : e->main_l) enc_layer(e, L, T, true, e->x, d.output_size);
+    fa::launch_enc_scale(e->in_raw, T, d.input_dim, kin, std::sqrt((float)d.output_size), e->in0, s);
+    enc_layer(e, e->e0, T, n_tiles, false, e->in0, kin);
+    for (const auto& L : e->main_l) enc_layer(e, L, T, n_tiles, true, e->x, d.output_size);
     fa::launch_enc_resid_ln(e->x, d.output_size, d.output_size, nullptr, -1, T, nullptr, nullptr, 0, e->after_w,
                             e->after_b, 1e-5f, 1, nullptr, nullptr, 0, s);
-    for (const auto& L : e->tp_l) enc_layer(e, L, T, true, e->x, d.output_size);
+    for (const auto& L : e->tp_l) enc_layer(e, L, T, n_tiles, true, e->x, d.output_size);
     // tp_norm in place; its f16 pair is the adaptor's input
     fa::launch_enc_resid_ln(e->x, d.output_size, d.output_size, nullptr, -1, T, nullptr, nullptr, 0, e->tp_w, e->tp_b,
                             1e-5f, 1, e->xn, e->xn_lo, d.output_size, s);
@@ -470,31 +481,96 @@ extern "C" int fa_encoder_forward_dev(fa_encoder* e, const float* lfr_dev, int T
     sp = gemm(e, e->hid, e->hid_lo, T, e->lin2);
     fa::launch_enc_resid_ln(e->x, d.adaptor_output, d.adaptor_output, e->part, sp, T, e->lin2.b, nullptr, 0, nullptr,
                             nullptr, 0.0f, 0, nullptr, nullptr, 0, s);
-    for (const auto& B : e->blocks) ada_block(e, B, T);
+    for (const auto& B : e->blocks) ada_block(e, B, T, n_tiles);
     fa::set_launch_pdl(false);
-    cudaError_t ce = cudaMemcpyAsync(embeds_dev, e->x, sizeof(float) * (size_t)T * d.adaptor_output,
-                                     cudaMemcpyDefault, s);
-    if (ce == cudaSuccess) ce = cudaGetLastError();
+    e->stream = saved;
+}
+
+// n_utt utterances of frames[i] rows each, concatenated: lfr [sum][input_dim] f32 in, embeds
+// [sum][adaptor_output] f32 out; host or device pointers. The forward of a row layout
+// (rows, tiles) is captured once as a CUDA graph and replayed.
+extern "C" int fa_encoder_forward_batch(fa_encoder* e, int n_utt, const int* frames, const float* lfr, float* embeds,
+                                        void* stream) {
+    if (!e || n_utt < 1 || !frames || !lfr || !embeds)
+        return fail("fa_encoder_forward_batch: bad argument", FA_ERR_INVALID_ARG);
+    if (!e->loaded) return fail("encoder weights not loaded", FA_ERR_NOT_READY);
+    long total = 0;
+    for (int i = 0; i < n_utt; ++i) {
+        if (frames[i] < 1) return fail("fa_encoder_forward_batch: every utterance needs >= 1 frame", FA_ERR_INVALID_ARG);
+        total += frames[i];
+    }
+    if (total > e->d.max_frames)
+        return fail("fa_encoder_forward_batch: " + std::to_string(total) + " frames in all, max_frames = " +
+                        std::to_string(e->d.max_frames),
+                    FA_ERR_CAPACITY);
+    cudaSetDevice(e->device);
+    const fa_encoder_desc& d = e->d;
+    const int T = (int)total;
+    int n_tiles = 0;
+    for (int i = 0, r = 0; i < n_utt; r += frames[i], ++i) {
+        for (int t = 0; t < frames[i]; ++t) e->h_seg[r + t] = make_int2(r, r + frames[i]);
+        for (int t = 0; t < frames[i]; t += fa::kEncAttRows)
+            e->h_tiles[n_tiles++] = make_int4(r + t, std::min(fa::kEncAttRows, frames[i] - t), r, frames[i]);
+    }
+    cudaStream_t s = stream ? (cudaStream_t)stream : e->stream;
+    cudaError_t ce = cudaMemcpyAsync(e->seg_dev, e->h_seg, sizeof(int2) * T, cudaMemcpyHostToDevice, s);
+    if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync(e->tiles_dev, e->h_tiles, sizeof(int4) * n_tiles, cudaMemcpyHostToDevice, s);
+    if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync(e->in_raw, lfr, sizeof(float) * (size_t)T * d.input_dim, cudaMemcpyDefault, s);
+    if (ce != cudaSuccess) return fail(std::string("encoder input: ") + cudaGetErrorString(ce), FA_ERR_CUDA);
+    if (e->use_graphs) {
+        auto key = std::make_pair(T, n_tiles);
+        auto it = e->graphs.find(key);
+        if (it == e->graphs.end()) {
+            cudaGraph_t g = nullptr;
+            ce = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+            if (ce == cudaSuccess) {
+                enqueue(e, T, n_tiles, s);
+                ce = cudaStreamEndCapture(s, &g);
+            }
+            cudaGraphExec_t ex = nullptr;
+            if (ce == cudaSuccess) ce = cudaGraphInstantiate(&ex, g, 0);
+            if (g) cudaGraphDestroy(g);
+            if (ce != cudaSuccess) return fail(std::string("encoder graph: ") + cudaGetErrorString(ce), FA_ERR_CUDA);
+            if (e->graphs.size() >= 32) {
+                for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+                e->graphs.clear();
+            }
+            it = e->graphs.emplace(key, ex).first;
+        }
+        ce = cudaGraphLaunch(it->second, s);
+    } else {
+        enqueue(e, T, n_tiles, s);
+        ce = cudaGetLastError();
+    }
+    if (ce == cudaSuccess)
+        ce = cudaMemcpyAsync(embeds, e->x, sizeof(float) * (size_t)T * d.adaptor_output, cudaMemcpyDefault, s);
     if (ce == cudaSuccess) ce = cudaMemcpyAsync(e->h_err, e->err_dev, sizeof(int), cudaMemcpyDeviceToHost, s);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
-    e->stream = saved;
     if (ce != cudaSuccess) return fail(std::string("encoder forward: ") + cudaGetErrorString(ce), FA_ERR_CUDA);
     if (*e->h_err) {
         cudaMemsetAsync(e->err_dev, 0, sizeof(int), s);
+        cudaStreamSynchronize(s);
         return fail("encoder: a bounded device wait gave up", FA_ERR_TIMEOUT);
     }
     return FA_OK;
 }
 
-// Host in, host out (staged through the encoder's device buffers).
+// One utterance, device (or host) pointers, on `stream` (NULL: the encoder's stream);
+// returns when done.
+extern "C" int fa_encoder_forward_dev(fa_encoder* e, const float* lfr_dev, int T, float* embeds_dev, void* stream) {
+    if (T < 1) return fail("fa_encoder_forward: T must be >= 1", FA_ERR_INVALID_ARG);
+    return fa_encoder_forward_batch(e, 1, &T, lfr_dev, embeds_dev, stream);
+}
+
+// One utterance, host in, host out.
 extern "C" int fa_encoder_forward(fa_encoder* e, const float* lfr, int T, float* embeds) {
-    if (!e || !lfr || !embeds) return fail("fa_encoder_forward: bad argument", FA_ERR_INVALID_ARG);
-    if (T < 1 || T > e->d.max_frames)
-        return fail("fa_encoder_forward: T must be in [1, max_frames = " + std::to_string(e->d.max_frames) + "]",
-                    FA_ERR_CAPACITY);
-    cudaSetDevice(e->device);
-    if (cudaMemcpyAsync(e->in_raw, lfr, sizeof(float) * (size_t)T * e->d.input_dim, cudaMemcpyHostToDevice,
-                        e->stream) != cudaSuccess)
-        return fail("fa_encoder_forward: upload", FA_ERR_CUDA);
-    return fa_encoder_forward_dev(e, e->in_raw, T, embeds, nullptr);
+    return fa_encoder_forward_dev(e, lfr, T, embeds, nullptr);
+}
+
+extern "C" int fa_encoder_set_graphs(fa_encoder* e, int enable) {
+    if (!e) return fail("fa_encoder_set_graphs: NULL encoder", FA_ERR_INVALID_ARG);
+    e->use_graphs = enable != 0;
+    return FA_OK;
 }

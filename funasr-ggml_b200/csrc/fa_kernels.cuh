@@ -110,11 +110,15 @@ void launch_enc_resid_ln(float* x, int d, int ld_x, const float* part, int n_par
                          int ln_in_place, __half* out_hi, __half* out_lo, int ld_out, cudaStream_t s);
 void launch_enc_bias_act(const float* part, int n_part, int T, int n, const float* bias, int relu, float* y32,
                          __half* y_hi, __half* y_lo, int n_sm, cudaStream_t s);
-void launch_enc_fsmn(const float* qkv, int T, int d, const float* w, int K, int pad, float* mem, cudaStream_t s);
+// seg[t] = (first, end) rows of row t's utterance
+void launch_enc_fsmn(const float* qkv, int T, const int2* seg, int d, const float* w, int K, int pad, float* mem,
+                     cudaStream_t s);
 size_t enc_attention_smem(int max_T);
 void configure_encoder(int max_T);
-void launch_enc_attention(const float* qkv, int T, int d, int n_heads, __half* out_hi, __half* out_lo, int max_T,
-                          cudaStream_t s);
+// tiles[i] = (first row, rows <= 16, utterance's first row, utterance length <= max_T)
+void launch_enc_attention(const float* qkv, const int4* tiles, int n_tiles, int d, int n_heads, __half* out_hi,
+                          __half* out_lo, int max_T, cudaStream_t s);
+constexpr int kEncAttRows = 16;
 
 // ------------------------------------------------------------------ k_gemm.cu --
 // Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T

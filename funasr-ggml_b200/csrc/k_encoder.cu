@@ -121,30 +121,32 @@ __global__ void __launch_bounds__(256) enc_bias_act_kernel(const float* part, in
 }
 
 // FSMN memory on v = qkv[:, 2d:3d]: mem[t][c] = v[t][c] + sum_k v[t + k - pad][c] * w[c][k]
-// (zero outside [0, T)); taps w [d][K].
-__global__ void __launch_bounds__(256) enc_fsmn_kernel(const float* qkv, int T, int d, const float* w, int K, int pad,
-                                                       float* mem) {
+// (zero outside the row's utterance, rows [seg[t].x, seg[t].y)); taps w [d][K].
+__global__ void __launch_bounds__(256) enc_fsmn_kernel(const float* qkv, const int2* seg, int d, const float* w, int K,
+                                                       int pad, float* mem) {
     pdl_trigger();
     pdl_wait();
     const int t = blockIdx.x;
+    const int2 sg = seg[t];
     for (int c = threadIdx.x; c < d; c += 256) {
         const float* vcol = qkv + 2 * d + c;
         float acc = vcol[(size_t)t * 3 * d];
         for (int k = 0; k < K; ++k) {
             const int s = t + k - pad;
-            if (s >= 0 && s < T) acc = fmaf(vcol[(size_t)s * 3 * d], w[(size_t)c * K + k], acc);
+            if (s >= sg.x && s < sg.y) acc = fmaf(vcol[(size_t)s * 3 * d], w[(size_t)c * K + k], acc);
         }
         mem[(size_t)t * d + c] = acc;
     }
 }
 
-// Bidirectional multi-head attention over T frames, head_dim 128. CTA = (16 query
-// rows, head), 128 threads: scores of the 16 rows against all keys in shared memory
-// (fp32), softmax per row, then thread j accumulates output dim j for the 16 rows.
+// Bidirectional multi-head attention within each utterance, head_dim 128. CTA = (tile,
+// head), 128 threads; a tile (first row, rows <= 16, utterance start, utterance length)
+// lies in one utterance: scores of its rows against the utterance's keys in shared
+// memory (fp32), softmax per row, then thread j accumulates output dim j of the rows.
 constexpr int ATT_ROWS = 16;
 constexpr int HD = 128;
 
-__global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, int T, int d, int n_heads,
+__global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, const int4* tiles, int d,
                                                             __half* out_hi, __half* out_lo, int max_T) {
     extern __shared__ float sm[];
     float* qs = sm;                                  // [16][128]
@@ -152,8 +154,11 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, in
     pdl_trigger();
     pdl_wait();
     const int h = blockIdx.y;
-    const int r0 = blockIdx.x * ATT_ROWS;
-    const int nr = min(ATT_ROWS, T - r0);
+    const int4 tl = tiles[blockIdx.x];
+    const int r0 = tl.x;
+    const int nr = tl.y;
+    const int k0 = tl.z;                             // the utterance's rows [k0, k0 + T)
+    const int T = tl.w;
     const int ld = 3 * d;
     const float scale = 1.0f / sqrtf((float)HD);
     for (int e = threadIdx.x; e < ATT_ROWS * HD; e += 128) {
@@ -164,7 +169,7 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, in
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // scores: warp w takes keys w, w+4, ...; lanes split the 128 dims
     for (int t = warp; t < T; t += 4) {
-        const float4 kv = *reinterpret_cast<const float4*>(qkv + (size_t)t * ld + d + h * HD + 4 * lane);
+        const float4 kv = *reinterpret_cast<const float4*>(qkv + (size_t)(k0 + t) * ld + d + h * HD + 4 * lane);
         for (int r = 0; r < nr; ++r) {
             const float4 qv = *reinterpret_cast<const float4*>(qs + r * HD + 4 * lane);
             float p = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
@@ -199,7 +204,7 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, in
 #pragma unroll
     for (int r = 0; r < ATT_ROWS; ++r) acc[r] = 0.0f;
     for (int t = 0; t < T; ++t) {
-        const float v = qkv[(size_t)t * ld + 2 * d + h * HD + j];
+        const float v = qkv[(size_t)(k0 + t) * ld + 2 * d + h * HD + j];
 #pragma unroll
         for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(sc[r * max_T + t], v, acc[r]);
     }
@@ -227,8 +232,9 @@ void launch_enc_bias_act(const float* part, int n_part, int T, int n, const floa
     launch_k(enc_bias_act_kernel, dim3(blocks), dim3(256), 0, s, part, n_part, T, n, bias, relu, y32, y_hi, y_lo);
 }
 
-void launch_enc_fsmn(const float* qkv, int T, int d, const float* w, int K, int pad, float* mem, cudaStream_t s) {
-    launch_k(enc_fsmn_kernel, dim3(T), dim3(256), 0, s, qkv, T, d, w, K, pad, mem);
+void launch_enc_fsmn(const float* qkv, int T, const int2* seg, int d, const float* w, int K, int pad, float* mem,
+                     cudaStream_t s) {
+    launch_k(enc_fsmn_kernel, dim3(T), dim3(256), 0, s, qkv, seg, d, w, K, pad, mem);
 }
 
 size_t enc_attention_smem(int max_T) { return sizeof(float) * (size_t)ATT_ROWS * (HD + max_T); }
@@ -238,11 +244,10 @@ void configure_encoder(int max_T) {
                          (int)enc_attention_smem(max_T));
 }
 
-void launch_enc_attention(const float* qkv, int T, int d, int n_heads, __half* out_hi, __half* out_lo, int max_T,
-                          cudaStream_t s) {
-    dim3 grid((T + ATT_ROWS - 1) / ATT_ROWS, n_heads);
-    launch_k(enc_attention_kernel, grid, dim3(128), enc_attention_smem(max_T), s, qkv, T, d, n_heads, out_hi, out_lo,
-             max_T);
+void launch_enc_attention(const float* qkv, const int4* tiles, int n_tiles, int d, int n_heads, __half* out_hi,
+                          __half* out_lo, int max_T, cudaStream_t s) {
+    launch_k(enc_attention_kernel, dim3(n_tiles, n_heads), dim3(128), enc_attention_smem(max_T), s, qkv, tiles, d,
+             out_hi, out_lo, max_T);
 }
 
 }  // namespace fa

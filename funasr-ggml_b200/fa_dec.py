@@ -122,6 +122,8 @@ def lib():
         "fa_encoder_load_weights": ([_P, _P, _I], _I),
         "fa_encoder_forward": ([_P, _P, _I, _P], _I),
         "fa_encoder_forward_dev": ([_P, _P, _I, _P, _P], _I),
+        "fa_encoder_forward_batch": ([_P, _I, _P, _P, _P, _P], _I),
+        "fa_encoder_set_graphs": ([_P, _I], _I),
         "fa_sched_create": ([_P, _P], _P),
         "fa_sched_destroy": ([_P], None),
         "fa_sched_submit": ([_P, ctypes.c_int64, _P, _P, _I, _I], _I),
@@ -512,6 +514,17 @@ class Encoder:
         out = np.zeros((x.shape[0], self.desc.adaptor_output), np.float32)
         _check(lib().fa_encoder_forward(self.e, _p(x), x.shape[0], _p(out)))
         return out
+
+    def forward_batch(self, utterances):
+        """Several utterances in one pass: list of [T_i][input_dim] -> list of [T_i][adaptor_output]."""
+        frames = np.array([len(u) for u in utterances], np.int32)
+        x = np.ascontiguousarray(np.concatenate(utterances), np.float32)
+        out = np.zeros((x.shape[0], self.desc.adaptor_output), np.float32)
+        _check(lib().fa_encoder_forward_batch(self.e, len(frames), _p(frames), _p(x), _p(out), None))
+        return np.split(out, np.cumsum(frames)[:-1])
+
+    def set_graphs(self, enable: bool):
+        _check(lib().fa_encoder_set_graphs(self.e, int(bool(enable))))
 
     def forward_dev(self, lfr_ptr: int, T: int, out_ptr: int, stream: int = 0):
         _check(lib().fa_encoder_forward_dev(self.e, lfr_ptr, T, out_ptr, stream or None))

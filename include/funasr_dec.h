@@ -348,6 +348,14 @@ FA_API int fa_encoder_load_weights(fa_encoder* e, const fa_tensor_view* tensors,
 FA_API int fa_encoder_forward(fa_encoder* e, const float* lfr, int T, float* embeds);
 /* Device (or host) pointers, on `stream` (NULL: the encoder's stream); returns when done. */
 FA_API int fa_encoder_forward_dev(fa_encoder* e, const float* lfr_dev, int T, float* embeds_dev, void* stream);
+/* n_utt utterances at once (frames[i] rows each, concatenated in lfr and embeds; host or
+ * device pointers): every kernel runs over all rows, attention and the FSMN stay within
+ * each utterance. Sum of frames <= max_frames. Each row layout is captured once as a
+ * CUDA graph and replayed. */
+FA_API int fa_encoder_forward_batch(fa_encoder* e, int n_utt, const int* frames, const float* lfr, float* embeds,
+                                    void* stream);
+/* 1 = replay captured CUDA graphs (default), 0 = direct launches. */
+FA_API int fa_encoder_set_graphs(fa_encoder* e, int enable);
 
 /* Library version string. */
 FA_API const char* fa_version(void);
