@@ -332,10 +332,10 @@ extern "C" fa_encoder* fa_encoder_create(int device, const fa_encoder_desc* desc
     }
     const fa_encoder_desc& d = *desc;
     if (d.output_size != d.attention_heads * 128 || d.adaptor_output != d.adaptor_heads * 128 || d.num_blocks < 1 ||
-        d.tp_blocks < 0 || d.kernel_size < 1 || d.max_frames < 1 || d.max_frames > 4096 || d.input_dim < 1 ||
+        d.tp_blocks < 0 || d.kernel_size < 1 || d.max_frames < 1 || d.max_frames > fa::kEncMaxFrames || d.input_dim < 1 ||
         d.input_dim > 2048 || d.output_size % 128 || d.linear_units % 128 || d.adaptor_hidden % 128 ||
         d.adaptor_ffn % 128 || d.output_size > 2048 || d.adaptor_output > 2048) {
-        fail("fa_encoder_create: unsupported geometry (head_dim 128, widths multiples of 128, <= 4096 frames)",
+        fail("fa_encoder_create: unsupported geometry (head_dim 128, widths multiples of 128, <= 3000 frames)",
              FA_ERR_INVALID_ARG);
         return nullptr;
     }

@@ -141,16 +141,21 @@ __global__ void __launch_bounds__(256) enc_fsmn_kernel(const float* qkv, const i
 
 // Bidirectional multi-head attention within each utterance, head_dim 128. CTA = (tile,
 // head), 128 threads; a tile (first row, rows <= 16, utterance start, utterance length)
-// lies in one utterance: scores of its rows against the utterance's keys in shared
-// memory (fp32), softmax per row, then thread j accumulates output dim j of the rows.
+// lies in one utterance. Keys and values pass through shared memory 32 at a time
+// (coalesced loads): scores of the tile's rows against every key of the utterance
+// (fp32, kept in shared memory), softmax per row, then thread j accumulates output dim
+// j of the rows over the value chunks.
 constexpr int ATT_ROWS = 16;
 constexpr int HD = 128;
+constexpr int KCH = 32;                  // keys per chunk
+constexpr int KLD = HD + 4;              // padded row of a staged key / value (floats)
 
 __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, const int4* tiles, int d,
                                                             __half* out_hi, __half* out_lo, int max_T) {
     extern __shared__ float sm[];
     float* qs = sm;                                  // [16][128]
-    float* sc = sm + ATT_ROWS * HD;                  // [16][max_T]
+    float* kv = qs + ATT_ROWS * HD;                  // [32][KLD] staged keys, then values
+    float* sc = kv + KCH * KLD;                      // [16][max_T]
     pdl_trigger();
     pdl_wait();
     const int h = blockIdx.y;
@@ -161,22 +166,37 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
     const int T = tl.w;
     const int ld = 3 * d;
     const float scale = 1.0f / sqrtf((float)HD);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < ATT_ROWS * HD; e += 128) {
         const int r = e / HD, j = e % HD;
         qs[e] = r < nr ? qkv[(size_t)(r0 + r) * ld + h * HD + j] * scale : 0.0f;
     }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // scores: warp w takes keys w, w+4, ...; lanes split the 128 dims
-    for (int t = warp; t < T; t += 4) {
-        const float4 kv = *reinterpret_cast<const float4*>(qkv + (size_t)(k0 + t) * ld + d + h * HD + 4 * lane);
-        for (int r = 0; r < nr; ++r) {
-            const float4 qv = *reinterpret_cast<const float4*>(qs + r * HD + 4 * lane);
-            float p = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-            if (lane == 0) sc[r * max_T + t] = p;
+    // scores: per chunk, lane = key, warp w takes rows w, w+4, w+8, w+12
+    for (int c0 = 0; c0 < T; c0 += KCH) {
+        const int nk = min(KCH, T - c0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < KCH * (HD / 4); e += 128) {
+            const int kk = e / (HD / 4), j4 = e % (HD / 4);
+            const float4 v = kk < nk ? *reinterpret_cast<const float4*>(qkv + (size_t)(k0 + c0 + kk) * ld + d +
+                                                                       h * HD + 4 * j4)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(kv + kk * KLD + 4 * j4) = v;
         }
+        __syncthreads();
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* kr = kv + lane * KLD;
+#pragma unroll 4
+        for (int j = 0; j < HD; j += 4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 q4 = *reinterpret_cast<const float4*>(qs + (warp + 4 * i) * HD + j);
+                acc[i] = fmaf(q4.x, k4.x, fmaf(q4.y, k4.y, fmaf(q4.z, k4.z, fmaf(q4.w, k4.w, acc[i]))));
+            }
+        }
+        if (lane < nk)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sc[(warp + 4 * i) * max_T + c0 + lane] = acc[i];
     }
     __syncthreads();
     // softmax per row: warp w takes rows w, w+4, ...
@@ -186,27 +206,38 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
         for (int t = lane; t < T; t += 32) m = fmaxf(m, row[t]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float s = 0.0f;
+        float ssum = 0.0f;
         for (int t = lane; t < T; t += 32) {
-            const float e = expf(row[t] - m);
-            row[t] = e;
-            s += e;
+            const float ex = expf(row[t] - m);
+            row[t] = ex;
+            ssum += ex;
         }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        const float inv = 1.0f / s;
+        for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+        const float inv = 1.0f / ssum;
         for (int t = lane; t < T; t += 32) row[t] *= inv;
     }
-    __syncthreads();
-    // output: thread j owns head dim j of the 16 rows
+    // output: thread j owns head dim j of the rows; values staged per chunk
     const int j = threadIdx.x;
     float acc[ATT_ROWS];
 #pragma unroll
     for (int r = 0; r < ATT_ROWS; ++r) acc[r] = 0.0f;
-    for (int t = 0; t < T; ++t) {
-        const float v = qkv[(size_t)(k0 + t) * ld + 2 * d + h * HD + j];
+    for (int c0 = 0; c0 < T; c0 += KCH) {
+        const int nk = min(KCH, T - c0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < KCH * (HD / 4); e += 128) {
+            const int kk = e / (HD / 4), j4 = e % (HD / 4);
+            const float4 v = kk < nk ? *reinterpret_cast<const float4*>(qkv + (size_t)(k0 + c0 + kk) * ld + 2 * d +
+                                                                       h * HD + 4 * j4)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(kv + kk * KLD + 4 * j4) = v;
+        }
+        __syncthreads();
+        for (int kk = 0; kk < nk; ++kk) {
+            const float v = kv[kk * KLD + j];
 #pragma unroll
-        for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(sc[r * max_T + t], v, acc[r]);
+            for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(sc[r * max_T + c0 + kk], v, acc[r]);
+        }
     }
     for (int r = 0; r < nr; ++r) split_store_h(acc[r], out_hi, out_lo, (size_t)(r0 + r) * d + h * HD + j);
 }
@@ -237,11 +268,13 @@ void launch_enc_fsmn(const float* qkv, int T, const int2* seg, int d, const floa
     launch_k(enc_fsmn_kernel, dim3(T), dim3(256), 0, s, qkv, seg, d, w, K, pad, mem);
 }
 
-size_t enc_attention_smem(int max_T) { return sizeof(float) * (size_t)ATT_ROWS * (HD + max_T); }
+size_t enc_attention_smem(int max_T) { return sizeof(float) * ((size_t)ATT_ROWS * (HD + max_T) + KCH * KLD); }
 
-void configure_encoder(int max_T) {
+// The attention kernel's shared memory holds a tile's scores against max_T keys: sized
+// once per device for the longest utterance any encoder accepts (kEncMaxFrames).
+void configure_encoder(int) {
     cudaFuncSetAttribute(enc_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)enc_attention_smem(max_T));
+                         (int)enc_attention_smem(kEncMaxFrames));
 }
 
 void launch_enc_attention(const float* qkv, const int4* tiles, int n_tiles, int d, int n_heads, __half* out_hi,

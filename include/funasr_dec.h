@@ -338,7 +338,7 @@ typedef struct fa_encoder_desc {
     int adaptor_blocks;  /* 2 */
     int adaptor_heads;   /* 8 */
     int adaptor_ffn;     /* 256 */
-    int max_frames;      /* longest input, <= 4096 */
+    int max_frames;      /* frames per call (one utterance or a batch), <= 3000 */
 } fa_encoder_desc;
 FA_API void fa_encoder_default_desc(fa_encoder_desc* desc);
 FA_API fa_encoder* fa_encoder_create(int device, const fa_encoder_desc* desc); /* NULL: fa_last_error(NULL) */
