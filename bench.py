@@ -51,12 +51,15 @@ def parse():
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between kernels")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "attention", "gemm", "prefill", "serve", "pipeline"],
+                    choices=["decode", "attention", "gemm", "prefill", "serve", "pipeline", "append"],
                     help="attention: kernel (2) alone over one layer's pages at the same batch and context; "
                          "gemm: the decode step's weight GEMMs alone; prefill: batched chunked prefill of "
                          "16 utterances then 64 greedy tokens each; serve: continuous batching of --streams "
                          "streams with Poisson arrivals; pipeline: one 5 s utterance through the encoder, "
-                         "adaptor, prefill and 32 greedy tokens")
+                         "adaptor, prefill and 32 greedy tokens; append: the paged KV append + gather of "
+                         "32 sequences over 28 layers")
+    ap.add_argument("--append-layers", type=int, default=28,
+                    help="append: layers in the pool (28 is the workload; fewer only for small profiler captures)")
     ap.add_argument("--streams", type=int, default=1024, help="serve: streams over all GPUs")
     ap.add_argument("--arrival-rate", type=float, default=100.0, help="serve: streams per second (Poisson)")
     ap.add_argument("--kv-gb", type=float, default=160.0, help="serve: page pool per GPU, GB")
@@ -697,7 +700,205 @@ def run_pipeline(a):
     fa_multi.shutdown()
 
 
+# ------------------------------------------------- KV append + gather --
+APPEND_METRIC = "KV append + gather GB/s (32 sequences, 28 layers, f16 pages of 16 tokens)"
+
+
+def _append_case(rank, steps_total, L=28):
+    """The append + gather workload: 32 sequences with contexts ~U[64, 1024], block tables
+    cut from a random permutation of a 4096-page pool, positions, lengths and slab row
+    offsets of every step."""
+    rng = np.random.default_rng(2024 + rank)
+    n_pages, n_seq = 4096, 32
+    ctx0 = rng.integers(64, 1025, n_seq).astype(np.int32)
+    bt_stride = (1024 + steps_total + 15) // 16
+    if n_seq * bt_stride > n_pages:
+        raise SystemExit(f"append workload: warmup + steps must stay below {n_pages // n_seq * 16 - 1039}")
+    bt = rng.permutation(n_pages)[: n_seq * bt_stride].reshape(n_seq, bt_stride).astype(np.int32)
+    s = np.arange(steps_total, dtype=np.int32)[:, None]
+    pos = ctx0[None, :] + s                              # token written at step s
+    n_kv = pos + 1                                       # tokens gathered after it
+    row0 = np.concatenate([np.zeros((steps_total, 1), np.int64), np.cumsum(n_kv, 1)[:, :-1]], 1).astype(np.int32)
+    return L, n_pages, n_seq, ctx0, bt, bt_stride, pos.astype(np.int32), n_kv.astype(np.int32), row0
+
+
+def _append_bytes(n_seq, n_kv_step, L=28):
+    """Algorithmic bytes of one step: the appended K/V read and written once, every
+    gathered token read from its page and written to the slabs once."""
+    return 2 * n_seq * L * KV_BYTES_PER_TOKEN_LAYER + 2 * int(n_kv_step.sum()) * L * KV_BYTES_PER_TOKEN_LAYER
+
+
+def cpu_append_sample(budget_s, n_steps_max=256):
+    """The oracle's append (C) and gather (numpy) on the same workload, one host thread,
+    for about budget_s seconds. Returns GB/s, steps done, seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    oracle.build()
+    L, n_pages, n_seq, ctx0, bt, bt_stride, pos, n_kv, row0 = _append_case(0, n_steps_max)
+    pool = np.zeros((L, n_pages, 8 * 2 * 16 * 128), np.uint16)
+    rng = np.random.default_rng(5)
+    slots = np.arange(n_seq, dtype=np.int32)
+    done, nbytes, el = 0, 0, 0.0          # el counts append + gather only, not input generation
+    while done < n_steps_max and el < budget_s:
+        k = oracle.f32_to_f16_bits(rng.standard_normal((n_seq, L, 8, 128)).astype(np.float32))
+        v = oracle.f32_to_f16_bits(rng.standard_normal((n_seq, L, 8, 128)).astype(np.float32))
+        t1 = time.perf_counter()
+        oracle.kv_append_raw(k, v, slots, pos[done], bt, pool, L, n_pages)
+        oracle.kv_gather(pool, bt, slots, n_kv[done], row0[done], int(n_kv[done].sum()))
+        el += time.perf_counter() - t1
+        nbytes += _append_bytes(n_seq, n_kv[done])
+        done += 1
+    return nbytes / el / 1e9, done, el
+
+
+def run_append(a):
+    """Paged KV append + gather on its own: each step appends one token per sequence in
+    all 28 layers (K/V ~N(0,1) f16, through fa_op_kv_append) and then gathers every
+    sequence's K/V over its whole length into head-major slabs [28][8][rows][128]
+    (fa_op_kv_gather), the layout the reference's attention reads. Prints GB/s of
+    algorithmic bytes."""
+    import torch
+    import fa_dec
+
+    rank, local, world = fa_multi.init("nccl")
+    torch.cuda.set_device(local)
+    K, W = a.steps, a.warmup
+    E = a.e2e_steps
+    steps_total = W + K + E
+    L, n_pages, n_seq, ctx0, bt, bt_stride, pos, n_kv, row0 = _append_case(rank, steps_total, a.append_layers)
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(rank)
+    pool = torch.empty((L, n_pages, 8 * 2 * 16 * 128), dtype=torch.float16, device=dev)
+    for l in range(L):
+        pool[l].normal_(generator=g)
+    pool = pool.view(torch.int16)
+    kv_shape = (W + K, n_seq, L, 8, 128)
+    k_in = torch.randn(kv_shape, dtype=torch.float16, device=dev, generator=g).view(torch.int16)
+    v_in = torch.randn(kv_shape, dtype=torch.float16, device=dev, generator=g).view(torch.int16)
+    max_rows = int(n_kv.sum(1).max())
+    k_out = torch.empty((L, 8, max_rows, 128), dtype=torch.int16, device=dev)
+    v_out = torch.empty_like(k_out)
+    d_bt = torch.from_numpy(bt).to(dev)
+    d_pos, d_nkv, d_row0 = (torch.from_numpy(x).to(dev) for x in (pos, n_kv, row0))
+    slot = torch.arange(n_seq, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def append(i, kp, vp):
+        fa_dec.op_kv_append(kp, vp, n_seq, L, d_pos[i].data_ptr(), slot.data_ptr(), d_bt.data_ptr(), bt_stride,
+                            n_pages, pool.data_ptr(), err.data_ptr(), stream)
+
+    def gather(i):
+        fa_dec.op_kv_gather(pool.data_ptr(), L, n_pages, d_bt.data_ptr(), bt_stride, slot.data_ptr(),
+                            d_nkv[i].data_ptr(), d_row0[i].data_ptr(), n_seq, bt_stride, max_rows,
+                            k_out.data_ptr(), v_out.data_ptr(), err.data_ptr(), stream)
+
+    for i in range(W):
+        append(i, k_in[i].data_ptr(), v_in[i].data_ptr())
+        gather(i)
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    for j in range(K):
+        i = W + j
+        ev[j][0].record()
+        append(i, k_in[i].data_ptr(), v_in[i].data_ptr())
+        ev[j][1].record()
+        gather(i)
+        ev[j][2].record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    fa_multi.barrier()
+    assert int(err.item()) == 0, "append or gather reported a device error"
+    ms = fa_multi.reduce(ev[0][0].elapsed_time(ev[-1][2]), "max")
+    step_bytes = [_append_bytes(n_seq, n_kv[W + j], L) for j in range(K)]
+    value = sum(step_bytes) * world / (ms / 1e3) / 1e9
+    gather_ms = sum(ev[j][1].elapsed_time(ev[j][2]) for j in range(K))
+    append_ms = sum(ev[j][0].elapsed_time(ev[j][1]) for j in range(K))
+    gather_bytes = sum(2 * int(n_kv[W + j].sum()) * L * KV_BYTES_PER_TOKEN_LAYER for j in range(K))
+    achieved = gather_bytes / (gather_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # e2e: the step's K/V come from pinned host memory each step, the error word goes back
+    k_host = torch.randn((E, n_seq, L, 8, 128), dtype=torch.float16).view(torch.int16).pin_memory()
+    v_host = torch.randn((E, n_seq, L, 8, 128), dtype=torch.float16).view(torch.int16).pin_memory()
+    k_dev = torch.empty((n_seq, L, 8, 128), dtype=torch.int16, device=dev)
+    v_dev = torch.empty_like(k_dev)
+    err_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    torch.cuda.synchronize()
+    fa_multi.barrier()
+    t0 = time.perf_counter()
+    e2e_bytes = 0
+    for j in range(E):
+        i = W + K + j
+        k_dev.copy_(k_host[j], non_blocking=True)
+        v_dev.copy_(v_host[j], non_blocking=True)
+        append(i, k_dev.data_ptr(), v_dev.data_ptr())
+        gather(i)
+        err_host.copy_(err, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        if int(err_host.item()) != 0:
+            raise RuntimeError("append or gather reported a device error")
+        e2e_bytes += _append_bytes(n_seq, n_kv[i], L)
+    e2e_s = fa_multi.reduce(time.perf_counter() - t0, "max")
+    e2e_value = e2e_bytes * world / e2e_s / 1e9
+    all_clocks = fa_multi.gather(clocks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline and L == 28:
+        del pool, k_in, v_in
+        v, n_done, el = cpu_append_sample(a.cpu_budget_s)
+        cpu = {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"the first {n_done} steps of the same workload (32 sequences, 28 layers) through the "
+                         f"oracle's append and gather in {el:.1f} s, one thread"}
+    if rank == 0:
+        reasons = sorted(set(r for c in all_clocks for r in c.get("reasons", [])))
+        print(json.dumps({
+            "metric": APPEND_METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic: N(0,1) f16 K/V and pages, seeded contexts and block tables",
+            "config": {"workload": f"isolated paged KV append + gather: 32 sequences at contexts ~U[64,1024], {L} "
+                                   "layers x 8 KV heads x 128 f16, pages of 16 tokens, block tables from a random "
+                                   "permutation of a 4096-page pool, 1 token appended per sequence per step, every "
+                                   "sequence gathered over its whole length each step",
+                       "append_ms_per_step": append_ms / K, "gather_ms_per_step": gather_ms / K,
+                       "layers": L, "l2": "no flush: each step gathers ~100 MB per layer from a 268 MB-per-layer "
+                                          "pool, 2.9 GB and 7.5 GB at 28 layers, far above L2"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "kernel": "kv_gather_kernel", "peak_kind": peak_kind,
+                         "bytes_per_launch": gather_bytes / K, "ms_per_launch": gather_ms / K},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": 2 * n_seq * L * 8 * 128 * 2,
+                    "d2h_bytes_per_step": 4, "steps": E},
+            "gpu_launches": 2 * K,
+            "clocks": {"sm_mhz": all_clocks[0].get("sm_mhz"), "sm_max_mhz": all_clocks[0].get("sm_max_mhz"),
+                       "reasons": reasons},
+        }), flush=True)
+    fa_multi.shutdown()
+
+
 # -------------------------------------------------------------- reference --
+def run_append_reference(a):
+    """The append + gather workload through the oracle on the host cores (the reference's
+    ggml CPU path cannot be built here), about --cpu-budget-s seconds of steps."""
+    v, n_done, el = cpu_append_sample(a.cpu_budget_s, n_steps_max=max(a.steps, 1))
+    print(json.dumps({
+        "impl": "reference", "metric": APPEND_METRIC, "value": v, "unit": "GB/s", "n_gpus": a.gpus,
+        "steps": n_done, "warmup": 0, "ms_per_step": el * 1e3 / n_done, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: N(0,1) f16 K/V, seeded contexts and block tables",
+        "config": {"workload": "isolated paged KV append + gather: 32 sequences at contexts ~U[64,1024], 28 layers "
+                               "x 8 KV heads x 128 f16, pages of 16 tokens, 1 token appended per sequence per step, "
+                               "every sequence gathered over its whole length each step"},
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
+                         "sample": f"the first {n_done} steps in {el:.1f} s through the oracle's append and gather"},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_reference(a):
     """The reference's CPU path (ggml) cannot be built here, so its restatement (the
     oracle, ggml-CPU arithmetic, all host threads) is timed on the same config: each
@@ -705,6 +906,8 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", 0))
     if rank != 0:
         return
+    if a.workload == "append":
+        return run_append_reference(a)
     cfg = fa_synth.QWEN3_06B
     w = fa_synth.make_weights(cfg, seed=1)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -761,5 +964,7 @@ if __name__ == "__main__":
         run_serve(args)
     elif args.workload == "pipeline":
         run_pipeline(args)
+    elif args.workload == "append":
+        run_append(args)
     else:
         run_ours(args)

@@ -1429,6 +1429,27 @@ extern "C" int fa_op_kv_append(const uint16_t* k, const uint16_t* v, int M, int 
     return FA_OK;
 }
 
+extern "C" int fa_op_kv_gather(const uint16_t* pool, int n_layers, int n_pages, const int* bt, int bt_stride,
+                               const int* slot, const int* n_kv, const int* row0, int M, int max_pages,
+                               int total_rows, uint16_t* k_out, uint16_t* v_out, int* err, void* stream) {
+    if (!pool || !bt || !slot || !n_kv || !row0 || !k_out || !v_out || M <= 0 || n_layers <= 0 ||
+        n_pages <= 0 || max_pages <= 0 || total_rows <= 0 || bt_stride < max_pages)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "null or non-positive argument, or bt_stride < max_pages");
+    if (M > 65535 || n_layers > 65535)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "M and n_layers are limited to 65535");
+    if ((reinterpret_cast<uintptr_t>(pool) & 15) || (reinterpret_cast<uintptr_t>(k_out) & 15) ||
+        (reinterpret_cast<uintptr_t>(v_out) & 15))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "pool and outputs must be 16-byte aligned");
+    fa::GatherArgs a{};
+    a.pool = reinterpret_cast<const __half*>(pool); a.n_layers = n_layers; a.n_pages = n_pages; a.Hkv = kHkv;
+    a.block_table = bt; a.bt_stride = bt_stride; a.slot = slot; a.n_kv = n_kv; a.row0 = row0; a.M = M;
+    a.max_pages = max_pages; a.total_rows = total_rows; a.k_out = reinterpret_cast<__half*>(k_out);
+    a.v_out = reinterpret_cast<__half*>(v_out); a.err = err;
+    fa::launch_kv_gather(a, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
 extern "C" int fa_op_prefill_attention(const float* q, int M, const int* pos, const int* slot, const int* bt,
                                        int bt_stride, int n_pages, const uint16_t* pool_layer, const int* tiles,
                                        int n_tiles, uint16_t* out16, uint16_t* out16_lo, float* out32, int* err,

@@ -29,6 +29,7 @@ constexpr int kQBytes = 34;        // Q8_0 block bytes
 constexpr int kDevErrTimeout = 1;     // a bounded mbarrier wait gave up
 constexpr int kDevErrBadPage = 2;     // block table entry outside the pool
 constexpr int kDevErrBadPos = 4;      // position outside the RoPE table
+constexpr int kDevErrBadLen = 8;      // sequence length or output row range outside its bounds
 
 // Upper bound for one mbarrier wait, in nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;

@@ -45,6 +45,24 @@ struct RawAppendArgs {
 };
 void launch_kv_append_raw(const RawAppendArgs& a, cudaStream_t s);
 
+// KV gather: tokens [0, n_kv[m]) of sequence slot[m], every layer, from the pages into
+// head-major slabs k_out / v_out [n_layers][Hkv][total_rows][128], sequence m at rows
+// [row0[m], row0[m] + n_kv[m]) of each head's plane. Hkv <= 8.
+struct GatherArgs {
+    const __half* pool;      // [n_layers][n_pages][Hkv][2][16][128]
+    int n_layers, n_pages, Hkv;
+    const int* block_table;
+    int bt_stride;
+    const int* slot;         // [M]
+    const int* n_kv;         // [M]
+    const int* row0;         // [M]
+    int M, max_pages, total_rows;
+    __half* k_out;
+    __half* v_out;
+    int* err;
+};
+void launch_kv_gather(const GatherArgs& a, cudaStream_t s);
+
 // ------------------------------------------------------------- k_attention.cu --
 // Kernel (2): paged GQA decode attention (head_dim 128, 2 query heads per KV head).
 struct AttnArgs {

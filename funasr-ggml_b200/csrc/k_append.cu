@@ -135,7 +135,51 @@ __global__ void __launch_bounds__(256) kv_append_raw_kernel(RawAppendArgs a) {
     reinterpret_cast<uint4*>(d)[c] = reinterpret_cast<const uint4*>(s)[c];
 }
 
+// Gather: one CTA copies one page of one sequence in one layer (64 KiB: 8 heads x K|V x
+// 16 tokens x 128) into the head-major slabs. Each (head, K|V) part of a page is 4 KiB of
+// consecutive tokens and lands as 4 KiB of consecutive rows, so every warp access is 512 B
+// contiguous on both sides; a thread issues its 16 loads before any store.
+__global__ void __launch_bounds__(256) kv_gather_kernel(GatherArgs a) {
+    const int pi = blockIdx.x, m = blockIdx.y, l = blockIdx.z;
+    const int n_kv = a.n_kv[m], row0 = a.row0[m];
+    if (n_kv < 0 || n_kv > a.max_pages * kPageTokens || row0 < 0 || row0 + n_kv > a.total_rows) {
+        if (pi == 0 && l == 0 && threadIdx.x == 0) record_error(a.err, kDevErrBadLen);
+        return;
+    }
+    const int t0 = pi * kPageTokens;
+    if (t0 >= n_kv) return;
+    const int page = a.block_table[(size_t)a.slot[m] * a.bt_stride + pi];
+    if (page < 0 || page >= a.n_pages) {
+        if (threadIdx.x == 0) record_error(a.err, kDevErrBadPage);
+        return;
+    }
+    const int nt = min(kPageTokens, n_kv - t0);
+    const int t = threadIdx.x >> 4;         // token within the page
+    const int c = threadIdx.x & 15;         // 16 B column within the 256 B row
+    const size_t page_vec = (size_t)a.Hkv * 2 * kPageTokens * D / 8;
+    const uint4* src = reinterpret_cast<const uint4*>(a.pool) + ((size_t)l * a.n_pages + page) * page_vec;
+    if (t >= nt) return;
+    uint4 r[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        if (j < 2 * a.Hkv) r[j] = src[(size_t)j * kPageTokens * (D / 8) + threadIdx.x];
+    const size_t row = (size_t)row0 + t0 + t;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        if (j >= 2 * a.Hkv) break;
+        const int h = j >> 1;
+        __half* out = (j & 1) ? a.v_out : a.k_out;
+        uint4* dst = reinterpret_cast<uint4*>(out + (((size_t)l * a.Hkv + h) * a.total_rows + row) * D);
+        dst[c] = r[j];
+    }
+}
+
 }  // namespace
+
+void launch_kv_gather(const GatherArgs& a, cudaStream_t s) {
+    dim3 grid(a.max_pages, a.M, a.n_layers);
+    kv_gather_kernel<<<grid, 256, 0, s>>>(a);
+}
 
 void launch_qknorm_rope_append(const AppendArgs& a, cudaStream_t s) {
     const int n_vec = a.Hq + 2 * a.Hkv;

@@ -143,6 +143,7 @@ def lib():
         "fa_step_launches": ([_P, _P], _I),
         "fa_op_qknorm_rope_append": ([_P, _I, _P, _P, _P, _I, _I, _P, _P, ctypes.c_float, _P, _I, _P, _P, _P, _P], _I),
         "fa_op_kv_append": ([_P, _P, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P], _I),
+        "fa_op_kv_gather": ([_P, _I, _I, _P, _I, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P], _I),
         "fa_op_attention_scratch_bytes": ([_I, _I], ctypes.c_size_t),
         "fa_op_paged_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P], _I),
         "fa_gguf_read_desc": ([ctypes.c_char_p, _P], _I),
@@ -410,6 +411,14 @@ def op_qknorm_rope_append(qkv, M, pos, slot, bt, bt_stride, n_pages, qn, kn, eps
 def op_kv_append(k, v, M, n_layers, pos, slot, bt, bt_stride, n_pages, pool, err=0, stream=0):
     _check(lib().fa_op_kv_append(k, v, M, n_layers, pos, slot, bt, bt_stride, n_pages, pool, err or None,
                                  stream or None))
+
+
+def op_kv_gather(pool, n_layers, n_pages, bt, bt_stride, slot, n_kv, row0, M, max_pages, total_rows, k_out, v_out,
+                 err=0, stream=0):
+    """Head-major K/V slabs [n_layers][8][total_rows][128] of the tokens [0, n_kv[m]) of
+    sequences slot[m] (device pointers throughout)."""
+    _check(lib().fa_op_kv_gather(pool, n_layers, n_pages, bt, bt_stride, slot, n_kv, row0, M, max_pages, total_rows,
+                                 k_out, v_out, err or None, stream or None))
 
 
 def op_attention_scratch_bytes(M, n_splits) -> int:

@@ -246,6 +246,16 @@ FA_API int fa_op_qknorm_rope_append(const float* qkv_dev, int M, const int* pos_
 FA_API int fa_op_kv_append(const uint16_t* k_dev, const uint16_t* v_dev, int M, int n_layers, const int* pos_dev,
                     const int* slot_dev, const int* block_table_dev, int bt_stride, int n_pages,
                     uint16_t* pool_dev, int* err_dev, void* stream);
+/* KV gather (compute/llm_ops_gpu.cpp:97-105: the view of a layer's cache over n_kv
+ * tokens, reshaped to [128, 8, n_kv] and made contiguous as [8][n_kv][128]). Copies
+ * tokens [0, n_kv[m]) of sequence slot[m] in every layer from the pool into k_out_dev /
+ * v_out_dev [n_layers][8][total_rows][128] f16, sequence m at rows [row0[m],
+ * row0[m] + n_kv[m]) of each head plane; rows no sequence covers are left as they are.
+ * n_kv[m] <= 16 * max_pages. Bad lengths or row ranges set error bit 8, bad pages bit 2. */
+FA_API int fa_op_kv_gather(const uint16_t* pool_dev, int n_layers, int n_pages, const int* block_table_dev,
+                           int bt_stride, const int* slot_dev, const int* n_kv_dev, const int* row0_dev, int M,
+                           int max_pages, int total_rows, uint16_t* k_out_dev, uint16_t* v_out_dev, int* err_dev,
+                           void* stream);
 /* Kernel (2): paged GQA decode attention (compute/llm_ops_gpu.cpp:98-143). Row m attends
  * to tokens [0, pos[m]] of sequence slot[m]. q [M][16][128] f32 (pre-scaled).
  * Output [M][2048] as f32 and/or as an f16 pair (out16 = f16(o), out16_lo = f16(o - out16),

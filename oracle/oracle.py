@@ -178,6 +178,33 @@ def kv_append_raw(k16, v16, slot, pos, block_table, pool, n_layers, n_pages,
                            n_kv_heads, head_dim, page_tokens, _ptr(pool))
 
 
+def kv_gather(pool, block_table, slot, n_kv, row0, total_rows, out_k=None, out_v=None,
+              n_kv_heads=8, head_dim=128, page_tokens=16):
+    """Head-major K/V slabs of the tokens [0, n_kv[m]) of sequences slot[m].
+
+    Restates compute/llm_ops_gpu.cpp:97-105: the view of a layer's cache over n_kv
+    tokens ([n_kv][8*128], token-major), reshaped to [128, 8, n_kv] and made contiguous
+    as [8][n_kv][128] (ggml_cont of the 0,2,1,3 permutation), here read through the
+    block table. pool: [n_layers][n_pages][Hkv][2][16][128] uint16. Returns k, v
+    [n_layers][Hkv][total_rows][128] uint16 with sequence m at rows row0[m]...; rows no
+    sequence covers keep out_k / out_v's values (zeros when not given)."""
+    pool = np.asarray(pool)
+    L = pool.shape[0]
+    P = pool.reshape(L, pool.shape[1], n_kv_heads, 2, page_tokens, head_dim)
+    k = np.zeros((L, n_kv_heads, total_rows, head_dim), np.uint16) if out_k is None else out_k
+    v = np.zeros((L, n_kv_heads, total_rows, head_dim), np.uint16) if out_v is None else out_v
+    bt = np.asarray(block_table)
+    for m in range(len(slot)):
+        n = int(n_kv[m])
+        toks = np.arange(n)
+        pg = bt[slot[m], toks // page_tokens]
+        r = slice(int(row0[m]), int(row0[m]) + n)
+        # the split advanced indices come first: [n][L][Hkv][D] -> [L][Hkv][n][D]
+        k[:, :, r] = P[:, pg, :, 0, toks % page_tokens].transpose(1, 2, 0, 3)
+        v[:, :, r] = P[:, pg, :, 1, toks % page_tokens].transpose(1, 2, 0, 3)
+    return k, v
+
+
 def paged_attention(q, slot, n_kv, block_table, pool_layer, n_heads=16, n_kv_heads=8,
                     head_dim=128, page_tokens=16):
     q = _c(q, np.float32)

@@ -123,6 +123,72 @@ def test_raw_append_cfg1_pages_byte_identical(torch_cuda):
     # nothing outside the touched pages was written
     untouched = np.setdiff1d(np.arange(n_pages), touched)
     assert int(d_pool.index_select(1, torch.from_numpy(untouched.astype(np.int64)).cuda()).abs().sum().item()) == 0
+    # the gather side of the same workload: 8 of the sequences read back over their whole
+    # length, in head-major slabs, equal the oracle's gather of the oracle's pages
+    pick = np.array([3, 0, 31, 17, 8, 22, 5, 12], np.int32)
+    n_kv = (ctx0[pick] + steps).astype(np.int32)
+    row0 = np.concatenate([[0], np.cumsum(n_kv)[:-1]]).astype(np.int32)
+    total = int(n_kv.sum())
+    d_k = torch.zeros((L, 8, total, 128), dtype=torch.int16, device="cuda")
+    d_v = torch.zeros_like(d_k)
+    d_pick, d_nkv, d_row0 = dev(torch, pick), dev(torch, n_kv), dev(torch, row0)
+    fa_dec.op_kv_gather(d_pool.data_ptr(), L, n_pages, d_bt.data_ptr(), bt_stride, d_pick.data_ptr(),
+                        d_nkv.data_ptr(), d_row0.data_ptr(), len(pick), bt_stride, total, d_k.data_ptr(),
+                        d_v.data_ptr(), d_err.data_ptr())
+    torch.cuda.synchronize()
+    assert int(d_err.item()) == 0
+    gk, gv = oracle.kv_gather(pool_ref, bt, pick, n_kv, row0, total)
+    assert np.array_equal(_u16(d_k), gk)
+    assert np.array_equal(_u16(d_v), gv)
+
+
+def test_kv_gather_ragged_and_bounds(torch_cuda):
+    """Lengths 0, 1, 15, 16, 17, 255, 256 and random ones, sequences gathered in any slot
+    order into a slab with gaps: the rows equal the oracle's, the gaps keep their
+    sentinel, and a length beyond max_pages or a page outside the pool sets its error bit
+    and writes nothing for that sequence."""
+    torch = torch_cuda
+    rng = np.random.default_rng(77)
+    L, n_pages, max_pages = 5, 600, 20
+    lens = np.array([0, 1, 15, 16, 17, 255, 256, 320, 3, 100, 200, 33], np.int32)
+    n_seq = len(lens)
+    bt = rng.permutation(n_pages)[: n_seq * max_pages].reshape(n_seq, max_pages).astype(np.int32)
+    pool = rng.integers(0, 1 << 16, (L, n_pages, PAGE_ELEMS), dtype=np.uint16)
+    d_pool, d_bt = dev(torch, _i16(pool)), dev(torch, bt)
+    order = rng.permutation(n_seq).astype(np.int32)
+    n_kv = lens[order]
+    row0 = (np.concatenate([[0], np.cumsum(n_kv + 5)[:-1]]) + 3).astype(np.int32)   # gaps of 5 rows
+    total = int(row0[-1] + n_kv[-1] + 7)
+    sentinel = 0x7C01                                           # an f16 NaN pattern nothing writes
+    d_k = torch.full((L, 8, total, 128), sentinel, dtype=torch.int16, device="cuda")
+    d_v = torch.full_like(d_k, sentinel)
+    d_err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = [dev(torch, x) for x in (order, n_kv, row0)]
+    fa_dec.op_kv_gather(d_pool.data_ptr(), L, n_pages, d_bt.data_ptr(), max_pages, a[0].data_ptr(), a[1].data_ptr(),
+                        a[2].data_ptr(), n_seq, max_pages, total, d_k.data_ptr(), d_v.data_ptr(), d_err.data_ptr())
+    torch.cuda.synchronize()
+    assert int(d_err.item()) == 0
+    want_k = np.full((L, 8, total, 128), sentinel, np.uint16)
+    want_v = want_k.copy()
+    oracle.kv_gather(pool, bt, order, n_kv, row0, total, out_k=want_k, out_v=want_v)
+    assert np.array_equal(_u16(d_k), want_k)
+    assert np.array_equal(_u16(d_v), want_v)
+
+    # a length past max_pages * 16 (bit 8) and a page outside the pool (bit 2)
+    bad_bt = bt.copy()
+    bad_bt[1, 0] = n_pages + 3
+    cases = [(np.array([0], np.int32), np.array([max_pages * 16 + 1], np.int32), bt, 8),
+             (np.array([1], np.int32), np.array([1], np.int32), bad_bt, 2)]
+    for slot_, nkv_, bt_, bit in cases:
+        d_err.zero_()
+        d_k.fill_(sentinel)
+        b = [dev(torch, x) for x in (slot_, nkv_, np.zeros(1, np.int32), bt_)]
+        fa_dec.op_kv_gather(d_pool.data_ptr(), L, n_pages, b[3].data_ptr(), max_pages, b[0].data_ptr(),
+                            b[1].data_ptr(), b[2].data_ptr(), 1, max_pages, total, d_k.data_ptr(), d_v.data_ptr(),
+                            d_err.data_ptr())
+        torch.cuda.synchronize()
+        assert int(d_err.item()) == bit
+        assert bool((d_k == sentinel).all().item())
 
 
 # ------------------------------------------------------------------- kernel 2 --

@@ -108,6 +108,39 @@ def test_paged_attention_matches_dense():
             assert np.allclose(out[m, H * 128:(H + 1) * 128], p @ V, atol=1e-6)
 
 
+def test_paged_append_then_gather_equals_contiguous_cache_view():
+    """The reference keeps each layer's cache as one token-major slab [n_ctx][8*128],
+    writes step n's K/V at row n (llm_ops_gpu.cpp:82-93) and reads [0, n_kv) back as
+    [8][n_kv][128] (:97-105). Appending the same tokens to scattered pages and gathering
+    them must give exactly that array."""
+    rng = np.random.default_rng(11)
+    L, n_pages, PT, D, H = 3, 64, 16, 128, 8
+    lens = np.array([1, 16, 17, 70], np.int32)
+    bt_stride = 6
+    bt = rng.permutation(n_pages)[: 4 * bt_stride].reshape(4, bt_stride).astype(np.int32)
+    pool = np.zeros((L, n_pages, H * 2 * PT * D), np.uint16)
+    slabs_k = [np.zeros((L, int(n), H * D), np.uint16) for n in lens]
+    slabs_v = [np.zeros((L, int(n), H * D), np.uint16) for n in lens]
+    for step in range(int(lens.max())):
+        live = np.nonzero(lens > step)[0]
+        k = oracle.f32_to_f16_bits(rng.standard_normal((len(live), L, H, D)).astype(np.float32))
+        v = oracle.f32_to_f16_bits(rng.standard_normal((len(live), L, H, D)).astype(np.float32))
+        oracle.kv_append_raw(k, v, live.astype(np.int32), np.full(len(live), step, np.int32), bt, pool, L, n_pages)
+        for i, m in enumerate(live):
+            slabs_k[m][:, step] = k[i].reshape(L, H * D)
+            slabs_v[m][:, step] = v[i].reshape(L, H * D)
+    order = np.array([2, 0, 3, 1], np.int32)            # slots in any order, rows packed
+    n_kv = lens[order]
+    row0 = np.concatenate([[0], np.cumsum(n_kv)[:-1]]).astype(np.int32)
+    gk, gv = oracle.kv_gather(pool, bt, order, n_kv, row0, int(n_kv.sum()))
+    for i, m in enumerate(order):
+        r = slice(row0[i], row0[i] + n_kv[i])
+        want_k = slabs_k[m].reshape(L, -1, H, D).transpose(0, 2, 1, 3)
+        want_v = slabs_v[m].reshape(L, -1, H, D).transpose(0, 2, 1, 3)
+        assert np.array_equal(gk[:, :, r], want_k)
+        assert np.array_equal(gv[:, :, r], want_v)
+
+
 def test_ggml_cpu_mode_is_a_coarser_approximation():
     """The reference's CPU backend quantises activations to Q8_0; the oracle restates it
     (mode 2). It stays within a few percent of exact arithmetic on the golden model."""
