@@ -821,6 +821,13 @@ def run_append(a):
     gather_bytes = sum(2 * int(n_kv[W + j].sum()) * L * KV_BYTES_PER_TOKEN_LAYER for j in range(K))
     achieved = gather_bytes / (gather_ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "gather_traffic.json")
+    if os.path.exists(tf):
+        with open(tf) as f:
+            t = json.load(f)
+        # DRAM bytes scale with the algorithmic bytes (layers x tokens gathered)
+        traffic = t["dram_bytes_per_launch"] * (gather_bytes / K) / t["algorithmic_bytes_per_launch"]
 
     # e2e: the step's K/V come from pinned host memory each step, the error word goes back
     k_host = torch.randn((E, n_seq, L, 8, 128), dtype=torch.float16).view(torch.int16).pin_memory()
@@ -865,10 +872,10 @@ def run_append(a):
                                    "permutation of a 4096-page pool, 1 token appended per sequence per step, every "
                                    "sequence gathered over its whole length each step",
                        "append_ms_per_step": append_ms / K, "gather_ms_per_step": gather_ms / K,
-                       "layers": L, "l2": "no flush: each step gathers ~100 MB per layer from a 268 MB-per-layer "
-                                          "pool, 2.9 GB and 7.5 GB at 28 layers, far above L2"},
+                       "layers": L, "l2": "no flush: each step reads 67-100 MB of pages per layer (1.9-2.8 GB at 28 "
+                                          "layers) out of a 268 MB-per-layer pool and writes as much, far above L2"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None, "kernel": "kv_gather_kernel", "peak_kind": peak_kind,
+                         "traffic": traffic, "kernel": "kv_gather_kernel", "peak_kind": peak_kind,
                          "bytes_per_launch": gather_bytes / K, "ms_per_launch": gather_ms / K},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": 2 * n_seq * L * 8 * 128 * 2,
