@@ -158,7 +158,8 @@ struct fa_ctx {
 
     bool use_graphs = true;
     bool use_pdl = true;       // programmatic dependent launch between the step's kernels
-    int gemm_variant = 0;      // 0: tcgen05 kernel, 1: mma.sync kernel
+    int gemm_variant = 0;      // 0: CUDA-core kernel up to 2 rows, else tcgen05; 1: mma.sync; 2: tcgen05;
+                               // 3: CUDA-core kernel up to 8 rows, else tcgen05
     struct GraphEntry {
         cudaGraphExec_t exec;
         int launches;
@@ -418,7 +419,7 @@ extern "C" int fa_set_stream(fa_ctx* ctx, void* stream) {
 
 extern "C" int fa_set_gemm_variant(fa_ctx* ctx, int variant) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
-    if (variant != 0 && variant != 1) return set_err(ctx, FA_ERR_INVALID_ARG, "variant must be 0 or 1");
+    if (variant < 0 || variant > 3) return set_err(ctx, FA_ERR_INVALID_ARG, "variant must be 0, 1, 2 or 3");
     ctx->gemm_variant = variant;
     clear_graphs(ctx);
     return FA_OK;
@@ -728,9 +729,10 @@ struct StepPlan {
     bool embeds = false; // input rows already in x
     bool logits = false;
     bool prof = false;
+    bool fuse_swiglu = false;  // gate/up GEMM on the small-M kernel writes SwiGLU's output itself
     std::array<int, 12> key() const {
-        return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, n_out, (int)embeds * 2 + (int)logits,
-                (int)prof};
+        return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, n_out,
+                (int)fuse_swiglu * 4 + (int)embeds * 2 + (int)logits, (int)prof};
     }
 };
 
@@ -771,6 +773,11 @@ static void attention_split(const std::vector<int>& row_pages, int n_sm, int max
     *n_splits_out = (max_pages + best - 1) / best;
 }
 
+// Whether a GEMM of M rows goes to the CUDA-core kernel under a GEMM variant.
+static bool gemv_rows(int variant, int M) {
+    return (variant == 0 && M <= fa::kGemvAutoRows) || (variant == 3 && M <= fa::kGemvMaxRows);
+}
+
 // row_len: context length of each row given to the decode kernel (all rows, or the
 // rows outside prefill tiles); n_tiles: prefill tiles of the step.
 static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits,
@@ -779,13 +786,15 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     StepPlan p;
     p.M = M;
     auto pick = [&](int n, int k) {
-        return ctx->gemm_variant == 0 && n % 128 == 0 ? fa::gemm_tc_pick_split(M, n, k, ctx->n_sm)
+        if (gemv_rows(ctx->gemm_variant, M) && fa::gemv_shape_supported(M, n, k, fa::kEpiStoreF32)) return 1;
+        return ctx->gemm_variant != 1 && n % 128 == 0 ? fa::gemm_tc_pick_split(M, n, k, ctx->n_sm)
                                                        : fa::gemm_pick_split(M, n, k, ctx->n_sm);
     };
     p.s_qkv = pick((kHq + 2 * kHkv) * kD, d.hidden);
     p.s_o = pick(d.hidden, kHq * kD);
     p.s_gu = pick(2 * d.ffn, d.hidden);
     p.s_dn = pick(d.hidden, d.ffn);
+    p.fuse_swiglu = gemv_rows(ctx->gemm_variant, M) && fa::gemv_shape_supported(M, 2 * d.ffn, d.hidden, fa::kEpiSwiglu);
     p.n_dec = (int)row_len.size();
     p.n_tiles = n_tiles;
     if (p.n_dec > 0) {
@@ -826,11 +835,15 @@ static void record_prof(fa_ctx* ctx, int idx, bool capturing) {
     else cudaEventRecord(ctx->prof_ev[idx], ctx->stream);
 }
 
-// One Q8_0 GEMM launch on the selected implementation (tcgen05 unless the caller
-// chose the mma.sync cross-check variant or the shape is outside the tcgen05 kernel).
+// One Q8_0 GEMM launch on the selected implementation: the CUDA-core kernel for a few
+// rows (variants 0 and 3, make_plan gives those shapes n_split 1), else tcgen05; the
+// mma.sync cross-check kernel for variant 1 or a shape outside both.
 static void run_gemm(fa_ctx* ctx, const fa::GemmArgs& g) {
-    if (ctx->gemm_variant == 0 && fa::gemm_tc_supported(g) && fa::launch_q8_gemm_tc(g, ctx->err_dev, ctx->stream))
-        return;
+    const int v = ctx->gemm_variant;
+    if (v != 1) {
+        if (gemv_rows(v, g.M) && fa::launch_q8_gemv(g, ctx->stream)) return;
+        if (fa::gemm_tc_supported(g) && fa::launch_q8_gemm_tc(g, ctx->err_dev, ctx->stream)) return;
+    }
     fa::launch_q8_gemm(g, ctx->stream);
 }
 
@@ -897,9 +910,16 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         fa::launch_residual_rmsnorm(ctx->x, ctx->part, p.s_o, M, H, w.post_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         g = fa::GemmArgs{};
         g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = w.gu_q; g.M = M; g.N = 2 * F; g.K = H;
-        g.n_split = p.s_gu; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
-        run_gemm(ctx, g);
-        fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s);
+        g.n_split = p.s_gu;
+        if (p.fuse_swiglu) {
+            g.epilogue = fa::kEpiSwiglu; g.H = ctx->h16; g.H_lo = ctx->h_lo;
+            fa::launch_q8_gemv(g, s);
+            --n;
+        } else {
+            g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
+            run_gemm(ctx, g);
+            fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s);
+        }
         g = fa::GemmArgs{};
         g.A = ctx->h16; g.A_lo = ctx->h_lo; g.Wh = w.dn_q; g.M = M; g.N = H; g.K = F;
         g.n_split = p.s_dn; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
@@ -1531,20 +1551,27 @@ extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, uint16_t* w16, 
 }
 
 static int op_gemm(const fa::GemmArgs& g, int variant, cudaStream_t s) {
-    if (variant == 0) {
+    if (variant < 0 || variant > 3) return set_err(nullptr, FA_ERR_INVALID_ARG, "variant must be 0, 1, 2 or 3");
+    if (variant == 1) {
+        fa::launch_q8_gemm(g, s);
+    } else if (variant == 3) {
+        if (!fa::launch_q8_gemv(g, s)) return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the CUDA-core kernel");
+    } else if (variant == 0 && gemv_rows(0, g.M) && fa::launch_q8_gemv(g, s)) {
+        // taken by the CUDA-core kernel
+    } else {
         if (!fa::gemm_tc_supported(g)) return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the tcgen05 kernel");
         if (!fa::launch_q8_gemm_tc(g, nullptr, s)) return set_err(nullptr, FA_ERR_CUDA, "tensor map encoding failed");
-    } else {
-        fa::launch_q8_gemm(g, s);
     }
     OP_CK(cudaGetLastError());
     return FA_OK;
 }
 
 extern "C" int fa_op_gemm_plan(int M, int N, int K, int variant, int n_sm, int* n_split) {
-    if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_sm <= 0 || !n_split || (variant != 0 && variant != 1))
+    if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_sm <= 0 || !n_split || variant < 0 || variant > 3)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_gemm_plan: bad argument");
-    *n_split = variant == 0 && N % 128 == 0 ? fa::gemm_tc_pick_split(M, N, K, n_sm) : fa::gemm_pick_split(M, N, K, n_sm);
+    if (gemv_rows(variant, M) && fa::gemv_shape_supported(M, N, K, fa::kEpiStoreF32)) *n_split = 1;
+    else if (variant != 1 && N % 128 == 0) *n_split = fa::gemm_tc_pick_split(M, N, K, n_sm);
+    else *n_split = fa::gemm_pick_split(M, N, K, n_sm);
     return FA_OK;
 }
 
@@ -1559,6 +1586,32 @@ extern "C" int fa_op_q8_gemm(const uint16_t* a16, const uint16_t* a16_lo, int M,
     g.Wh = reinterpret_cast<const __half*>(w16);
     g.M = M; g.N = N; g.K = K; g.n_split = n_split; g.epilogue = fa::kEpiStoreF32; g.C = c;
     return op_gemm(g, variant, (cudaStream_t)stream);
+}
+
+extern "C" int fa_op_q8_gemm_swiglu(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const uint16_t* w16,
+                                    int N, uint16_t* h16, uint16_t* h_lo, void* stream) {
+    if (!a16 || !w16 || !h16 || M <= 0 || N <= 0 || K <= 0)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "null or non-positive argument");
+    if (int rc = ensure_configured()) return rc;
+    fa::GemmArgs g{};
+    g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo);
+    g.Wh = reinterpret_cast<const __half*>(w16);
+    g.M = M; g.N = N; g.K = K; g.n_split = 1; g.epilogue = fa::kEpiSwiglu;
+    g.H = reinterpret_cast<__half*>(h16); g.H_lo = reinterpret_cast<__half*>(h_lo);
+    if (!fa::launch_q8_gemv(g, (cudaStream_t)stream))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the small-M kernel");
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_swiglu(const float* part, int n_part, int M, int ffn, uint16_t* h16, uint16_t* h_lo,
+                            void* stream) {
+    if (!part || !h16 || n_part <= 0 || M <= 0 || ffn <= 0 || ffn % 4)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "need partials, n_part > 0, M > 0 and ffn a multiple of 4");
+    fa::launch_swiglu(part, n_part, M, ffn, reinterpret_cast<__half*>(h16), reinterpret_cast<__half*>(h_lo),
+                      (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
 }
 
 extern "C" size_t fa_op_argmax_scratch_bytes(int M, int N) {

@@ -120,6 +120,18 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// y as the f16 pair the GEMMs read: hi = f16(y), lo = f16(y - hi) (lo may be omitted)
+__device__ __forceinline__ void split_store(float y, __half* hi, __half* lo, size_t i) {
+    const __half h = __float2half_rn(y);
+    hi[i] = h;
+    if (lo) lo[i] = __float2half_rn(__fsub_rn(y, __half2float(h)));
+}
+
+// SwiGLU of one gate / up pair: silu(g) * u = g / (1 + exp(-g)) * u
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 __device__ __forceinline__ void record_error(int* err, int code) {
     if (err) atomicOr(err, code);
 }

@@ -141,7 +141,9 @@ constexpr int kEncMaxFrames = 3000;   // frames per utterance and per batched pa
 
 // ------------------------------------------------------------------ k_gemm.cu --
 // Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T
-enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1 };
+// kEpiSwiglu (small-M kernel only): W stacks gate rows [0, N/2) over up rows [N/2, N) and
+// the result is written as the f16 pair of silu(gate) * up, [M][N/2].
+enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1, kEpiSwiglu = 2 };
 struct GemmArgs {
     const __half* A;         // [M][K] f16 activations (hi part)
     const __half* A_lo;      // [M][K] f16 remainder x - hi, or nullptr (plain f16 activations)
@@ -152,6 +154,8 @@ struct GemmArgs {
     float* C;                // kEpiStoreF32: [n_split][M][N] partials (n_split == 1: the result)
     float* amax_val;         // kEpiArgmax: [M][N/64] per-tile row maxima
     int* amax_idx;           //             [M][N/64] first column holding them
+    __half* H;               // kEpiSwiglu: [M][N/2] hi part
+    __half* H_lo;            //             [M][N/2] lo part (may be nullptr)
 };
 // mma.sync (m16n8k16) implementation; the cross-check variant.
 void launch_q8_gemm(const GemmArgs& g, cudaStream_t s);
@@ -161,6 +165,13 @@ bool gemm_tc_supported(const GemmArgs& g);
 int gemm_tc_pick_split(int M, int N, int K, int n_sm);
 bool launch_q8_gemm_tc(const GemmArgs& g, int* err, cudaStream_t s);
 size_t gemm_tc_smem_bytes();
+// CUDA-core small-M kernel (k_gemv.cu): M <= kGemvMaxRows, n_split 1, K a multiple of 256;
+// the store epilogue needs N a multiple of 4, the argmax epilogue N a multiple of 64 and
+// K <= 1024. The decoder uses it by default up to kGemvAutoRows rows.
+constexpr int kGemvMaxRows = 8;
+constexpr int kGemvAutoRows = 2;
+bool gemv_shape_supported(int M, int N, int K, int epilogue);
+bool launch_q8_gemv(const GemmArgs& g, cudaStream_t s);   // false: shape or pointers not taken
 
 // ----------------------------------------------------------------- k_small.cu --
 void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds,

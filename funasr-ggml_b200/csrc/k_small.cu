@@ -62,12 +62,6 @@ __global__ void __launch_bounds__(256) embed_kernel(const void* table, int table
     }
 }
 
-__device__ __forceinline__ void split_store(float y, __half* hi, __half* lo, size_t i) {
-    const __half h = __float2half_rn(y);
-    hi[i] = h;
-    if (lo) lo[i] = __float2half_rn(__fsub_rn(y, __half2float(h)));
-}
-
 // Sum of n_part split-K partials of one float4 column group, in partial order; the
 // loads of a group of 8 partials are all issued before the first add.
 __device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, int n_part) {
@@ -129,10 +123,6 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const f
         split_store(__fmul_rn(__fmul_rn(v[c].z, scale), ww.z), xn_hi, xn_lo, o + 2);
         split_store(__fmul_rn(__fmul_rn(v[c].w, scale), ww.w), xn_hi, xn_lo, o + 3);
     }
-}
-
-__device__ __forceinline__ float silu_mul(float g, float u) {
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
 }
 
 // Thread per float4 group of one row's ffn outputs.

@@ -158,6 +158,8 @@ def lib():
         "fa_op_q8_gemm": ([_P, _P, _I, _I, _P, _I, _I, _P, _I, _P], _I),
         "fa_op_argmax_scratch_bytes": ([_I, _I], ctypes.c_size_t),
         "fa_op_q8_gemm_argmax": ([_P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _P], _I),
+        "fa_op_q8_gemm_swiglu": ([_P, _P, _I, _I, _P, _I, _P, _P, _P], _I),
+        "fa_op_swiglu": ([_P, _I, _I, _I, _P, _P, _P], _I),
         "fa_palloc_create": ([_I], _P),
         "fa_palloc_destroy": ([_P], None),
         "fa_palloc_alloc": ([_P], _I),
@@ -280,7 +282,8 @@ class Decoder:
         self._c(lib().fa_set_stream(self.ctx, stream_ptr))
 
     def set_gemm_variant(self, variant: int):
-        """0: tcgen05 GEMM (default), 1: mma.sync GEMM (cross-check)."""
+        """0: small-M CUDA-core GEMM up to 2 rows, else tcgen05 (default); 1: mma.sync GEMM
+        (cross-check); 2: tcgen05 at every M; 3: small-M kernel up to 8 rows."""
         self._c(lib().fa_set_gemm_variant(self.ctx, int(variant)))
 
     def set_pdl(self, enable: bool):
@@ -474,6 +477,14 @@ def op_repack_q8(raw, N, K, w16, stream=0):
 
 def op_q8_gemm(a16, a16_lo, M, K, w16, N, n_split, c, variant=0, stream=0):
     _check(lib().fa_op_q8_gemm(a16, a16_lo or None, M, K, w16, N, n_split, c, variant, stream or None))
+
+
+def op_q8_gemm_swiglu(a16, a16_lo, M, K, w16, N, h16, h_lo, stream=0):
+    _check(lib().fa_op_q8_gemm_swiglu(a16, a16_lo or None, M, K, w16, N, h16, h_lo or None, stream or None))
+
+
+def op_swiglu(part, n_part, M, ffn, h16, h_lo, stream=0):
+    _check(lib().fa_op_swiglu(part, n_part, M, ffn, h16, h_lo or None, stream or None))
 
 
 def op_argmax_scratch_bytes(M, N) -> int:

@@ -114,8 +114,9 @@ FA_API int fa_load_gguf(fa_ctx* ctx, const char* path);
 /* Run the library's work on `cuda_stream` (a cudaStream_t of this device); NULL restores
  * the library's own stream. */
 FA_API int fa_set_stream(fa_ctx* ctx, void* cuda_stream);
-/* GEMM implementation: 0 = tcgen05/TMEM/TMA kernel (default), 1 = mma.sync kernel (same
- * arithmetic; kept to cross-check the default). */
+/* GEMM implementation: 0 = default: the CUDA-core small-M kernel for steps of up to 2
+ * rows, the tcgen05/TMEM/TMA kernel otherwise; 1 = mma.sync kernel (same arithmetic; kept
+ * to cross-check); 2 = tcgen05 kernel at every M; 3 = the small-M kernel up to 8 rows. */
 FA_API int fa_set_gemm_variant(fa_ctx* ctx, int variant);
 /* 1 = programmatic dependent launch between a step's kernels (default): each kernel's
  * prologue overlaps the previous kernel's tail. 0 = plain stream order. */
@@ -296,12 +297,24 @@ FA_API int fa_op_paged_attention_noalloc(const float* q_dev, int M, const int* p
  * A [M][K] as an f16 pair a16 + a16_lo (a16_lo may be NULL: plain f16 activations);
  * W [N][K] f16 = f16(d * q) per Q8_0 block (fa_op_repack_q8 builds it from GGUF blocks).
  * n_split > 1 writes partials [n_split][M][N] (their sum is C).
- * variant: 0 = tcgen05 kernel (N a multiple of 128), 1 = mma.sync kernel. */
+ * variant: 0 = the small-M CUDA-core kernel when M <= 2 and n_split == 1 (K a multiple of
+ * 256), else tcgen05 (N a multiple of 128); 1 = mma.sync kernel; 2 = tcgen05 kernel;
+ * 3 = small-M kernel (M <= 8, n_split 1, K a multiple of 256, N of 4; with argmax N of 64
+ * and K <= 1024). */
 FA_API int fa_op_repack_q8(const uint8_t* gguf_q8_dev, int N, int K, uint16_t* w16_dev, void* stream);
 /* The split-K factor the decoder uses for an M x N x K GEMM of `variant` on n_sm SMs (host only). */
 FA_API int fa_op_gemm_plan(int M, int N, int K, int variant, int n_sm, int* n_split);
 FA_API int fa_op_q8_gemm(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K, const uint16_t* w16_dev,
                          int N, int n_split, float* c_dev, int variant, void* stream);
+/* Gate/up GEMM with SwiGLU in its epilogue (compute/llm_ops_gpu.cpp:177-180), small-M
+ * kernel only (M <= 8, K a multiple of 256): w16 stacks the gate rows [0, N/2) over the up
+ * rows [N/2, N); h16 / h_lo [M][N/2] receive the f16 pair of silu(gate) * up. */
+FA_API int fa_op_q8_gemm_swiglu(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K,
+                                const uint16_t* w16_dev, int N, uint16_t* h16_dev, uint16_t* h_lo_dev, void* stream);
+/* SwiGLU of split-K partials part [n_part][M][2*ffn] (gate columns then up columns) into the
+ * f16 pair h16 / h_lo [M][ffn]: the decoder's separate SwiGLU kernel. */
+FA_API int fa_op_swiglu(const float* part_dev, int n_part, int M, int ffn, uint16_t* h16_dev, uint16_t* h_lo_dev,
+                        void* stream);
 /* lm_head with fused argmax: next [M] = first column of each row's maximum; logits optional. */
 FA_API size_t fa_op_argmax_scratch_bytes(int M, int N);
 FA_API int fa_op_q8_gemm_argmax(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K,

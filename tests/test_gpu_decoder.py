@@ -300,3 +300,46 @@ def test_qwen3_06b_benchmark_scale_rel_rms(torch_cuda):
         t = g_next
     assert np.mean(agree) >= 0.99
     dec.close()
+
+
+@pytest.mark.parametrize("n_seq", [1, 3])
+def test_small_batch_gemm_variants_agree(torch_cuda, small_w, n_seq):
+    """Decode steps of 1 or 3 rows through the three GEMM choices: variant 0 (the small-M
+    CUDA-core kernel with SwiGLU in its epilogue up to 2 rows, tcgen05 above), 2 (tcgen05
+    for every GEMM) and 3 (small-M kernel up to 8 rows). All stay within the logits bar of
+    the oracle, differ from each other only by fp32 summation order, and pick the same
+    greedy tokens."""
+    w = small_w
+    rng = np.random.default_rng(21)
+    L = 12
+    prompt = rng.integers(0, CFG["vocab"], (n_seq, L))
+    runs = {}
+    for variant in (0, 2, 3):
+        dec = _decoder(w, CFG)
+        dec.set_gemm_variant(variant)
+        sids = [dec.seq_open(MAX_CTX) for _ in range(n_seq)]
+        nxt, _ = dec.forward(np.repeat(sids, L), tokens=prompt.reshape(-1))
+        toks = nxt[L - 1::L]
+        first = toks
+        lgs, ids = [], []
+        for _ in range(6):
+            toks, lg = dec.decode_step(sids, toks, want_logits=True)
+            lgs.append(lg)
+            ids.append(toks)
+        runs[variant] = (np.stack(lgs), np.stack(ids), first)
+        dec.close()
+    od = oracle.OracleDecoder(CFG, w, n_pages=256, max_seqs=16, max_pages_per_seq=MAX_CTX // 16, max_pos=MAX_CTX,
+                              mode=oracle.MODE_W16)
+    for s in range(n_seq):
+        od.seq_open(s)
+    od.forward(np.repeat(np.arange(n_seq), L), tokens=prompt.reshape(-1))
+    toks = runs[0][2]
+    for step in range(6):
+        # the oracle follows the GPU's tokens so a flipped near-tie cannot derail the comparison
+        o_lg, _ = od.forward(list(range(n_seq)), tokens=toks)
+        for variant in (0, 2, 3):
+            assert_close(runs[variant][0][step], o_lg, what=f"variant {variant} step {step}")
+        toks = runs[0][1][step]
+    for variant in (2, 3):
+        assert rel_rms(runs[variant][0], runs[0][0]) < 1e-4
+        assert np.mean(runs[variant][1] == runs[0][1]) >= 0.99

@@ -318,7 +318,7 @@ def _split_f16(x):
     return hi, lo, oracle.f16_bits_to_f32(hi) + oracle.f16_bits_to_f32(lo)
 
 
-@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("variant", [0, 1, 2])
 @pytest.mark.parametrize("M,N,K,split", [
     (1, 1024, 1024, 1), (5, 4096, 1024, 4), (16, 1024, 2048, 8), (17, 2048, 1024, 2),
     (64, 6144, 1024, 4), (128, 1024, 3072, 12), (200, 1024, 1024, 1), (300, 512, 2048, 2),
@@ -348,9 +348,99 @@ def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
     assert rel_rms(c.sum(0).cpu().numpy(), ref16) < 5e-6
 
 
-@pytest.mark.parametrize("variant", [0, 1])
-@pytest.mark.parametrize("M,N", [(7, 151936), (300, 4096)])
+@pytest.mark.parametrize("M,N,K", [
+    (1, 4096, 1024), (2, 1024, 2048), (3, 6144, 1024), (4, 1024, 3072), (5, 4096, 1024), (8, 1024, 3072),
+    (1, 768, 512), (6, 64, 256), (8, 2048, 4096), (2, 151936, 1024),
+])
+def test_small_m_gemm_matches_oracle(torch_cuda, M, N, K):
+    """The CUDA-core kernel (variant 3) on the decoder's shapes and odd ones: fp32 result
+    against the oracle's double sum, with and without the lo plane."""
+    torch = torch_cuda
+    rng = np.random.default_rng(M * 11 + N + K)
+    raw, w16 = _q8_device(torch, rng, N, K)
+    a = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    hi, lo, a_eff = _split_f16(a)
+    d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
+    assert fa_dec.op_gemm_plan(M, N, K, variant=3) == 1
+    c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, 1, c.data_ptr(), 3)
+    torch.cuda.synchronize()
+    got = c.cpu().numpy()
+    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
+    assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
+    assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
+    c.zero_()
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), 0, M, K, w16.data_ptr(), N, 1, c.data_ptr(), 3)
+    torch.cuda.synchronize()
+    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, oracle.MODE_W16)
+    assert rel_rms(c.cpu().numpy(), ref16) < 5e-6
+
+
+@pytest.mark.parametrize("M,F,K", [(1, 3072, 1024), (2, 3072, 1024), (5, 512, 256), (8, 1536, 2048)])
+def test_small_m_gemm_swiglu_equals_separate_kernels(torch_cuda, M, F, K):
+    """Gate/up GEMM with SwiGLU in its epilogue: the same bits as the small-M GEMM followed
+    by the decoder's SwiGLU kernel, and within f16-pair precision of the oracle."""
+    torch = torch_cuda
+    rng = np.random.default_rng(M + F + K)
+    raw, w16 = _q8_device(torch, rng, 2 * F, K)
+    hi, lo, a_eff = _split_f16(rng.standard_normal((M, K)).astype(np.float32))
+    d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
+    h16 = torch.zeros((M, F), dtype=torch.int16, device="cuda")
+    h_lo = torch.zeros_like(h16)
+    fa_dec.op_q8_gemm_swiglu(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), 2 * F, h16.data_ptr(),
+                             h_lo.data_ptr())
+    c = torch.zeros((M, 2 * F), dtype=torch.float32, device="cuda")
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), 2 * F, 1, c.data_ptr(), 3)
+    r16 = torch.zeros_like(h16)
+    r_lo = torch.zeros_like(h16)
+    fa_dec.op_swiglu(c.data_ptr(), 1, M, F, r16.data_ptr(), r_lo.data_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(h16, r16) and torch.equal(h_lo, r_lo)
+    gu = oracle.gemm_q8(a_eff, raw, 2 * F, oracle.MODE_W16).astype(np.float64)
+    g, u = gu[:, :F], gu[:, F:]
+    want = g / (1.0 + np.exp(-g)) * u
+    got = oracle.f16_bits_to_f32(_u16(h16)).astype(np.float64) + oracle.f16_bits_to_f32(_u16(h_lo))
+    assert rel_rms(got, want) < 5e-6, rel_rms(got, want)
+
+
+def test_small_m_gemm_rows_do_not_depend_on_m(torch_cuda):
+    """A row's result is the same bits whether it is computed alone or among 2..8 rows, so
+    batching sequences together does not change any sequence's logits."""
+    torch = torch_cuda
+    rng = np.random.default_rng(5)
+    N, K = 4096, 1024
+    raw, w16 = _q8_device(torch, rng, N, K)
+    hi, lo, _ = _split_f16((rng.standard_normal((8, K)) * 3).astype(np.float32))
+    d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
+    outs = {}
+    for M in (1, 2, 3, 4, 8):
+        c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, 1, c.data_ptr(), 3)
+        torch.cuda.synchronize()
+        outs[M] = c.cpu().numpy()
+    for M in (2, 3, 4, 8):
+        assert np.array_equal(outs[M][0].view(np.uint32), outs[1][0].view(np.uint32))
+        assert np.array_equal(outs[M][:2].view(np.uint32), outs[2].view(np.uint32))
+
+
+def test_small_m_gemm_rejects_shapes_it_does_not_take(torch_cuda):
+    torch = torch_cuda
+    a = torch.zeros((9, 1024), dtype=torch.int16, device="cuda")
+    w = torch.zeros((1024, 1024), dtype=torch.int16, device="cuda")
+    c = torch.zeros((9, 1024), dtype=torch.float32, device="cuda")
+    for M, K, split in ((9, 1024, 1), (4, 320, 1), (4, 1024, 2)):
+        with pytest.raises(RuntimeError):
+            fa_dec.op_q8_gemm(a.data_ptr(), 0, M, K, w.data_ptr(), 1024, split, c.data_ptr(), 3)
+    # variant 0 sends what the small-M kernel does not take to tcgen05
+    fa_dec.op_q8_gemm(a.data_ptr(), 0, 4, 1024, w.data_ptr(), 1024, 2, c.data_ptr(), 0)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("variant", [0, 1, 3])
+@pytest.mark.parametrize("M,N", [(7, 151936), (300, 4096), (1, 151936), (4, 151936)])
 def test_lm_head_argmax_full_vocab(torch_cuda, variant, M, N):
+    if variant == 3 and M > 8:
+        pytest.skip("the small-M kernel takes at most 8 rows")
     torch = torch_cuda
     rng = np.random.default_rng(3)
     K = 1024
@@ -370,7 +460,7 @@ def test_lm_head_argmax_full_vocab(torch_cuda, variant, M, N):
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(logits.cpu().numpy()))
 
 
-@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
 @pytest.mark.parametrize("j1,j2", [(1000, 70000), (64 * 5 + 3, 64 * 5 + 40), (0, 151935)])
 def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2, variant):
     torch = torch_cuda
