@@ -9,30 +9,11 @@
 //   repack_q8        : GGUF Q8_0 blocks -> f16(d * q) weight matrix
 //   page_copy / fill_random / read_pages / apply_bt_updates : page-pool maintenance
 #include "fa_kernels.cuh"
+#include "k_norm.cuh"
 
 namespace fa {
 
 namespace {
-
-template <int NT>
-__device__ __forceinline__ double block_sum_double(double v, double* sh) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) sh[warp] = v;
-    __syncthreads();
-    double t = 0.0;
-    if (threadIdx.x < 32) {
-        t = threadIdx.x < NT / 32 ? sh[threadIdx.x] : 0.0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (threadIdx.x == 0) sh[0] = t;
-    }
-    __syncthreads();
-    t = sh[0];
-    __syncthreads();
-    return t;
-}
 
 __global__ void __launch_bounds__(256) embed_kernel(const void* table, int table_type, int hidden,
                                                     const int* tokens, const float* embeds, int vocab,
@@ -62,26 +43,7 @@ __global__ void __launch_bounds__(256) embed_kernel(const void* table, int table
     }
 }
 
-// Sum of n_part split-K partials of one float4 column group, in partial order; the
-// loads of a group of 8 partials are all issued before the first add.
-__device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, int n_part) {
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 < n_part; s0 += 8) {
-        float4 t[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (s0 + u < n_part) t[u] = p[(size_t)(s0 + u) * stride4];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (s0 + u < n_part) {
-                o.x = __fadd_rn(o.x, t[u].x); o.y = __fadd_rn(o.y, t[u].y);
-                o.z = __fadd_rn(o.z, t[u].z); o.w = __fadd_rn(o.w, t[u].w);
-            }
-    }
-    return o;
-}
-
-// One CTA per row; thread t owns float4 groups t, t+256, ... (hidden <= 4096).
+// One CTA per row (residual_norm_row's 256-thread order).
 __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const float* part, int n_part, int M,
                                                                int hidden, const float* w, float eps,
                                                                __half* xn_hi, __half* xn_lo, const int* rows) {
@@ -90,39 +52,11 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const f
     pdl_wait();
     const int m = rows ? rows[blockIdx.x] : (int)blockIdx.x;   // source row; output row blockIdx.x
     const int n4 = hidden / 4;
-    float4* xr = reinterpret_cast<float4*>(x + (size_t)m * hidden);
-    float4 v[4];
-    double ss = 0.0;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const int i = threadIdx.x + 256 * c;
-        if (i >= n4) break;
-        float4 a = xr[i];
-        if (n_part > 0) {
-            const float4 o = sum_parts4(reinterpret_cast<const float4*>(part) + (size_t)m * n4 + i,
-                                        (size_t)M * n4, n_part);
-            a.x = __fadd_rn(a.x, o.x); a.y = __fadd_rn(a.y, o.y);
-            a.z = __fadd_rn(a.z, o.z); a.w = __fadd_rn(a.w, o.w);
-            xr[i] = a;
-        }
-        v[c] = a;
-        ss += (double)__fmul_rn(a.x, a.x) + (double)__fmul_rn(a.y, a.y) + (double)__fmul_rn(a.z, a.z) +
-              (double)__fmul_rn(a.w, a.w);
-    }
-    ss = block_sum_double<256>(ss, sh);
-    const float mean = (float)(ss / (double)hidden);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const int i = threadIdx.x + 256 * c;
-        if (i >= n4) break;
-        const float4 ww = reinterpret_cast<const float4*>(w)[i];
-        const size_t o = (size_t)blockIdx.x * hidden + 4 * (size_t)i;
-        split_store(__fmul_rn(__fmul_rn(v[c].x, scale), ww.x), xn_hi, xn_lo, o);
-        split_store(__fmul_rn(__fmul_rn(v[c].y, scale), ww.y), xn_hi, xn_lo, o + 1);
-        split_store(__fmul_rn(__fmul_rn(v[c].z, scale), ww.z), xn_hi, xn_lo, o + 2);
-        split_store(__fmul_rn(__fmul_rn(v[c].w, scale), ww.w), xn_hi, xn_lo, o + 3);
-    }
+    float* xr = x + (size_t)m * hidden;
+    const size_t o = (size_t)blockIdx.x * hidden;
+    residual_norm_row(xr, reinterpret_cast<const float4*>(part) + (size_t)m * n4, (size_t)M * n4, n_part, hidden, w,
+                      eps, n_part > 0 ? xr : nullptr, sh,
+                      [&](int j, float y) { split_store(y, xn_hi, xn_lo, o + j); });
 }
 
 // Thread per float4 group of one row's ffn outputs.
