@@ -77,6 +77,7 @@ namespace fa {
 void configure_attention();
 void configure_gemm();
 void configure_gemm_tc();
+void configure_gemm_tc_skinny();
 }  // namespace fa
 
 static int ensure_configured() {
@@ -87,6 +88,7 @@ static int ensure_configured() {
         fa::configure_attention();
         fa::configure_gemm();
         fa::configure_gemm_tc();
+        fa::configure_gemm_tc_skinny();
         fa::configure_prefill_attention();
         g_configured[dev] = true;
     }
@@ -158,8 +160,9 @@ struct fa_ctx {
 
     bool use_graphs = true;
     bool use_pdl = true;       // programmatic dependent launch between the step's kernels
-    int gemm_variant = 0;      // 0: CUDA-core kernel up to 2 rows, else tcgen05; 1: mma.sync; 2: tcgen05;
-                               // 3: CUDA-core kernel up to 8 rows, else tcgen05
+    int gemm_variant = 0;      // 0: CUDA-core kernel up to 2 rows, swapped tcgen05 up to 128 (lm_head: 32),
+                               // 128-row-tile tcgen05 above; 1: mma.sync; 2: 128-row-tile tcgen05;
+                               // 3: CUDA-core up to 8 rows, else 2; 4: swapped tcgen05 up to 128, else 2
     struct GraphEntry {
         cudaGraphExec_t exec;
         int launches;
@@ -419,7 +422,7 @@ extern "C" int fa_set_stream(fa_ctx* ctx, void* stream) {
 
 extern "C" int fa_set_gemm_variant(fa_ctx* ctx, int variant) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
-    if (variant < 0 || variant > 3) return set_err(ctx, FA_ERR_INVALID_ARG, "variant must be 0, 1, 2 or 3");
+    if (variant < 0 || variant > 4) return set_err(ctx, FA_ERR_INVALID_ARG, "variant must be 0 to 4");
     ctx->gemm_variant = variant;
     clear_graphs(ctx);
     return FA_OK;
@@ -779,6 +782,12 @@ static bool gemv_rows(int variant, int M) {
     return (variant == 0 && M <= fa::kGemvAutoRows) || (variant == 3 && M <= fa::kGemvMaxRows);
 }
 
+// Whether a GEMM of M rows goes to the swapped (few-row) tcgen05 kernel.
+static bool skinny_rows(int variant, int M, int epilogue = fa::kEpiStoreF32) {
+    const int auto_rows = epilogue == fa::kEpiArgmax ? fa::kSkinnyArgmaxAutoRows : fa::kSkinnyAutoRows;
+    return (variant == 0 && M > fa::kGemvAutoRows && M <= auto_rows) || (variant == 4 && M <= fa::kSkinnyMaxRows);
+}
+
 // row_len: context length of each row given to the decode kernel (all rows, or the
 // rows outside prefill tiles); n_tiles: prefill tiles of the step.
 static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits,
@@ -788,6 +797,7 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     p.M = M;
     auto pick = [&](int n, int k) {
         if (gemv_rows(ctx->gemm_variant, M) && fa::gemv_shape_supported(M, n, k, fa::kEpiStoreF32)) return 1;
+        if (skinny_rows(ctx->gemm_variant, M) && n % 128 == 0) return fa::gemm_tc_skinny_pick_split(M, n, k, ctx->n_sm);
         return ctx->gemm_variant != 1 && n % 128 == 0 ? fa::gemm_tc_pick_split(M, n, k, ctx->n_sm)
                                                        : fa::gemm_pick_split(M, n, k, ctx->n_sm);
     };
@@ -843,6 +853,7 @@ static void run_gemm(fa_ctx* ctx, const fa::GemmArgs& g) {
     const int v = ctx->gemm_variant;
     if (v != 1) {
         if (gemv_rows(v, g.M) && fa::launch_q8_gemv(g, ctx->stream)) return;
+        if (skinny_rows(v, g.M, g.epilogue) && fa::launch_q8_gemm_tc_skinny(g, ctx->err_dev, ctx->stream)) return;
         if (fa::gemm_tc_supported(g) && fa::launch_q8_gemm_tc(g, ctx->err_dev, ctx->stream)) return;
     }
     fa::launch_q8_gemm(g, ctx->stream);
@@ -1552,13 +1563,18 @@ extern "C" int fa_op_repack_q8(const uint8_t* raw, int N, int K, uint16_t* w16, 
 }
 
 static int op_gemm(const fa::GemmArgs& g, int variant, cudaStream_t s) {
-    if (variant < 0 || variant > 3) return set_err(nullptr, FA_ERR_INVALID_ARG, "variant must be 0, 1, 2 or 3");
+    if (variant < 0 || variant > 4) return set_err(nullptr, FA_ERR_INVALID_ARG, "variant must be 0 to 4");
     if (variant == 1) {
         fa::launch_q8_gemm(g, s);
     } else if (variant == 3) {
         if (!fa::launch_q8_gemv(g, s)) return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the CUDA-core kernel");
+    } else if (variant == 4) {
+        if (!fa::launch_q8_gemm_tc_skinny(g, nullptr, s))
+            return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the few-row tcgen05 kernel");
     } else if (variant == 0 && gemv_rows(0, g.M) && fa::launch_q8_gemv(g, s)) {
         // taken by the CUDA-core kernel
+    } else if (variant == 0 && skinny_rows(0, g.M, g.epilogue) && fa::launch_q8_gemm_tc_skinny(g, nullptr, s)) {
+        // taken by the few-row tcgen05 kernel
     } else {
         if (!fa::gemm_tc_supported(g)) return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the tcgen05 kernel");
         if (!fa::launch_q8_gemm_tc(g, nullptr, s)) return set_err(nullptr, FA_ERR_CUDA, "tensor map encoding failed");
@@ -1568,9 +1584,10 @@ static int op_gemm(const fa::GemmArgs& g, int variant, cudaStream_t s) {
 }
 
 extern "C" int fa_op_gemm_plan(int M, int N, int K, int variant, int n_sm, int* n_split) {
-    if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_sm <= 0 || !n_split || variant < 0 || variant > 3)
+    if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64 || n_sm <= 0 || !n_split || variant < 0 || variant > 4)
         return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_gemm_plan: bad argument");
     if (gemv_rows(variant, M) && fa::gemv_shape_supported(M, N, K, fa::kEpiStoreF32)) *n_split = 1;
+    else if (skinny_rows(variant, M) && N % 128 == 0) *n_split = fa::gemm_tc_skinny_pick_split(M, N, K, n_sm);
     else if (variant != 1 && N % 128 == 0) *n_split = fa::gemm_tc_pick_split(M, N, K, n_sm);
     else *n_split = fa::gemm_pick_split(M, N, K, n_sm);
     return FA_OK;

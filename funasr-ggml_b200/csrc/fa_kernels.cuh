@@ -165,6 +165,17 @@ bool gemm_tc_supported(const GemmArgs& g);
 int gemm_tc_pick_split(int M, int N, int K, int n_sm);
 bool launch_q8_gemm_tc(const GemmArgs& g, int* err, cudaStream_t s);
 size_t gemm_tc_smem_bytes();
+// tcgen05 kernel with the operands swapped for steps of up to kSkinnyMaxRows rows
+// (k_gemm_tc_skinny.cu): weights on the MMA's 128-row side, activations on its N side.
+constexpr int kSkinnyMaxRows = 128;
+// The default GEMM choice uses it up to this many rows (layer GEMMs: 10-25 % faster than the
+// 128-row-tile kernel at 4-128 rows), and for the lm_head argmax only up to 32 rows (its
+// per-row warp reductions make it slower than the 128-row-tile epilogue above that).
+constexpr int kSkinnyAutoRows = 128;
+constexpr int kSkinnyArgmaxAutoRows = 32;
+bool gemm_tc_skinny_supported(const GemmArgs& g);
+int gemm_tc_skinny_pick_split(int M, int N, int K, int n_sm);
+bool launch_q8_gemm_tc_skinny(const GemmArgs& g, int* err, cudaStream_t s);
 // CUDA-core small-M kernel (k_gemv.cu): M <= kGemvMaxRows, n_split 1, K a multiple of 256;
 // the store epilogue needs N a multiple of 4, the argmax epilogue N a multiple of 64 and
 // K <= 1024. The decoder uses it by default up to kGemvAutoRows rows.

@@ -282,8 +282,10 @@ class Decoder:
         self._c(lib().fa_set_stream(self.ctx, stream_ptr))
 
     def set_gemm_variant(self, variant: int):
-        """0: small-M CUDA-core GEMM up to 2 rows, else tcgen05 (default); 1: mma.sync GEMM
-        (cross-check); 2: tcgen05 at every M; 3: small-M kernel up to 8 rows."""
+        """0 (default): small-M CUDA-core GEMM up to 2 rows, swapped tcgen05 up to 128 (lm_head
+        argmax up to 32), the 128-row-tile tcgen05 GEMM above; 1: mma.sync GEMM (cross-check);
+        2: 128-row-tile tcgen05 at every M; 3: small-M kernel up to 8 rows; 4: swapped tcgen05
+        up to 128 rows."""
         self._c(lib().fa_set_gemm_variant(self.ctx, int(variant)))
 
     def set_pdl(self, enable: bool):

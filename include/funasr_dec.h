@@ -115,8 +115,11 @@ FA_API int fa_load_gguf(fa_ctx* ctx, const char* path);
  * the library's own stream. */
 FA_API int fa_set_stream(fa_ctx* ctx, void* cuda_stream);
 /* GEMM implementation: 0 = default: the CUDA-core small-M kernel for steps of up to 2
- * rows, the tcgen05/TMEM/TMA kernel otherwise; 1 = mma.sync kernel (same arithmetic; kept
- * to cross-check); 2 = tcgen05 kernel at every M; 3 = the small-M kernel up to 8 rows. */
+ * rows, the tcgen05 kernel with swapped operands (weights on the MMA's 128-row side) up
+ * to 128 rows (the lm_head argmax up to 32), the tcgen05/TMEM/TMA kernel with 128-row
+ * activation tiles above; 1 = mma.sync kernel (same arithmetic; kept to cross-check);
+ * 2 = the 128-row-tile tcgen05 kernel at every M; 3 = the small-M kernel up to 8 rows,
+ * else as 2; 4 = the swapped tcgen05 kernel up to 128 rows, else as 2. */
 FA_API int fa_set_gemm_variant(fa_ctx* ctx, int variant);
 /* 1 = programmatic dependent launch between a step's kernels (default): each kernel's
  * prologue overlaps the previous kernel's tail. 0 = plain stream order. */
@@ -298,9 +301,10 @@ FA_API int fa_op_paged_attention_noalloc(const float* q_dev, int M, const int* p
  * W [N][K] f16 = f16(d * q) per Q8_0 block (fa_op_repack_q8 builds it from GGUF blocks).
  * n_split > 1 writes partials [n_split][M][N] (their sum is C).
  * variant: 0 = the small-M CUDA-core kernel when M <= 2 and n_split == 1 (K a multiple of
- * 256), else tcgen05 (N a multiple of 128); 1 = mma.sync kernel; 2 = tcgen05 kernel;
- * 3 = small-M kernel (M <= 8, n_split 1, K a multiple of 256, N of 4; with argmax N of 64
- * and K <= 1024). */
+ * 256), the swapped tcgen05 kernel when M <= 128 (with argmax M <= 32), else the 128-row-
+ * tile tcgen05 kernel (N a multiple of 128); 1 = mma.sync kernel; 2 = 128-row-tile tcgen05
+ * kernel; 3 = small-M kernel (M <= 8, n_split 1, K a multiple of 256, N of 4; with argmax N
+ * of 64 and K <= 1024); 4 = swapped tcgen05 kernel (M <= 128, N a multiple of 128). */
 FA_API int fa_op_repack_q8(const uint8_t* gguf_q8_dev, int N, int K, uint16_t* w16_dev, void* stream);
 /* The split-K factor the decoder uses for an M x N x K GEMM of `variant` on n_sm SMs (host only). */
 FA_API int fa_op_gemm_plan(int M, int N, int K, int variant, int n_sm, int* n_split);

@@ -302,19 +302,19 @@ def test_qwen3_06b_benchmark_scale_rel_rms(torch_cuda):
     dec.close()
 
 
-@pytest.mark.parametrize("n_seq", [1, 3])
+@pytest.mark.parametrize("n_seq", [1, 3, 16])
 def test_small_batch_gemm_variants_agree(torch_cuda, small_w, n_seq):
-    """Decode steps of 1 or 3 rows through the three GEMM choices: variant 0 (the small-M
-    CUDA-core kernel with SwiGLU in its epilogue up to 2 rows, tcgen05 above), 2 (tcgen05
-    for every GEMM) and 3 (small-M kernel up to 8 rows). All stay within the logits bar of
-    the oracle, differ from each other only by fp32 summation order, and pick the same
-    greedy tokens."""
+    """Decode steps of 1, 3 or 16 rows through the GEMM choices: variant 0 (the small-M
+    CUDA-core kernel with SwiGLU in its epilogue up to 2 rows, the swapped tcgen05 kernel up
+    to 64), 2 (128-row-tile tcgen05 for every GEMM), 3 (small-M kernel up to 8 rows) and 4
+    (swapped tcgen05 up to 64 rows). All stay within the logits bar of the oracle, differ
+    from each other only by fp32 summation order, and pick the same greedy tokens."""
     w = small_w
     rng = np.random.default_rng(21)
-    L = 12
+    L = 12 if n_seq <= 3 else 8            # the prefill forward stays within 128 rows
     prompt = rng.integers(0, CFG["vocab"], (n_seq, L))
     runs = {}
-    for variant in (0, 2, 3):
+    for variant in (0, 2, 3, 4):
         dec = _decoder(w, CFG)
         dec.set_gemm_variant(variant)
         sids = [dec.seq_open(MAX_CTX) for _ in range(n_seq)]
@@ -337,9 +337,9 @@ def test_small_batch_gemm_variants_agree(torch_cuda, small_w, n_seq):
     for step in range(6):
         # the oracle follows the GPU's tokens so a flipped near-tie cannot derail the comparison
         o_lg, _ = od.forward(list(range(n_seq)), tokens=toks)
-        for variant in (0, 2, 3):
+        for variant in (0, 2, 3, 4):
             assert_close(runs[variant][0][step], o_lg, what=f"variant {variant} step {step}")
         toks = runs[0][1][step]
-    for variant in (2, 3):
+    for variant in (2, 3, 4):
         assert rel_rms(runs[variant][0], runs[0][0]) < 1e-4
         assert np.mean(runs[variant][1] == runs[0][1]) >= 0.99

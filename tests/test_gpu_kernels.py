@@ -318,7 +318,7 @@ def _split_f16(x):
     return hi, lo, oracle.f16_bits_to_f32(hi) + oracle.f16_bits_to_f32(lo)
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("variant", [0, 1, 2, 4])
 @pytest.mark.parametrize("M,N,K,split", [
     (1, 1024, 1024, 1), (5, 4096, 1024, 4), (16, 1024, 2048, 8), (17, 2048, 1024, 2),
     (64, 6144, 1024, 4), (128, 1024, 3072, 12), (200, 1024, 1024, 1), (300, 512, 2048, 2),
@@ -326,6 +326,8 @@ def _split_f16(x):
     (256, 4096, 1024, 1), (400, 6144, 1024, 2), (513, 1024, 3072, 4),
 ])
 def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
+    if variant == 4 and M > 128:
+        pytest.skip("the swapped tcgen05 kernel takes at most 128 rows")
     torch = torch_cuda
     rng = np.random.default_rng(M * 7 + N + K)
     raw, w16 = _q8_device(torch, rng, N, K)
@@ -403,6 +405,27 @@ def test_small_m_gemm_swiglu_equals_separate_kernels(torch_cuda, M, F, K):
     assert rel_rms(got, want) < 5e-6, rel_rms(got, want)
 
 
+@pytest.mark.parametrize("M,N,K", [(3, 4096, 1024), (16, 1024, 3072), (17, 6144, 1024), (32, 1024, 2048),
+                                   (33, 4096, 1024), (64, 1024, 3072), (9, 256, 512), (65, 4096, 1024),
+                                   (128, 1024, 3072), (100, 6144, 1024)])
+def test_few_row_tcgen05_gemm_matches_oracle(torch_cuda, M, N, K):
+    """The swapped tcgen05 kernel (variant 4) at each activation tile width (16, 32, 64,
+    128 rows) and the planner's split, against the oracle's double sum."""
+    torch = torch_cuda
+    rng = np.random.default_rng(M * 13 + N + K)
+    raw, w16 = _q8_device(torch, rng, N, K)
+    hi, lo, a_eff = _split_f16((rng.standard_normal((M, K)) * 3).astype(np.float32))
+    d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
+    split = fa_dec.op_gemm_plan(M, N, K, variant=4)
+    c = torch.zeros((split, M, N), dtype=torch.float32, device="cuda")
+    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, split, c.data_ptr(), 4)
+    torch.cuda.synchronize()
+    got = c.sum(0).cpu().numpy()
+    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
+    assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
+    assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
+
+
 def test_small_m_gemm_rows_do_not_depend_on_m(torch_cuda):
     """A row's result is the same bits whether it is computed alone or among 2..8 rows, so
     batching sequences together does not change any sequence's logits."""
@@ -436,11 +459,11 @@ def test_small_m_gemm_rejects_shapes_it_does_not_take(torch_cuda):
     torch.cuda.synchronize()
 
 
-@pytest.mark.parametrize("variant", [0, 1, 3])
-@pytest.mark.parametrize("M,N", [(7, 151936), (300, 4096), (1, 151936), (4, 151936)])
+@pytest.mark.parametrize("variant", [0, 1, 3, 4])
+@pytest.mark.parametrize("M,N", [(7, 151936), (300, 4096), (1, 151936), (4, 151936), (40, 151936), (128, 151936)])
 def test_lm_head_argmax_full_vocab(torch_cuda, variant, M, N):
-    if variant == 3 and M > 8:
-        pytest.skip("the small-M kernel takes at most 8 rows")
+    if (variant == 3 and M > 8) or (variant == 4 and M > 128):
+        pytest.skip("outside the kernel's row range")
     torch = torch_cuda
     rng = np.random.default_rng(3)
     K = 1024
@@ -460,8 +483,8 @@ def test_lm_head_argmax_full_vocab(torch_cuda, variant, M, N):
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(logits.cpu().numpy()))
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3])
-@pytest.mark.parametrize("j1,j2", [(1000, 70000), (64 * 5 + 3, 64 * 5 + 40), (0, 151935)])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("j1,j2", [(1000, 70000), (64 * 5 + 3, 64 * 5 + 40), (0, 151935), (64 * 7 + 31, 64 * 7 + 32)])
 def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2, variant):
     torch = torch_cuda
     M, N, K = 3, 151936, 1024
