@@ -130,17 +130,18 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- CPU baseline --
-def cpu_oracle_sample(cfg, w, ctx, budget_s, rows=2, seed=0):
+def cpu_oracle_sample(cfg, w, ctx, budget_s, rows=2, seed=0, max_new=1024):
     """Oracle decode steps (ggml-CPU arithmetic: Q8_0 activations) for `rows` sequences
-    at `ctx` tokens of synthetic cache, repeated for about budget_s seconds."""
+    at `ctx` tokens of synthetic cache, repeated for about budget_s seconds (at most
+    max_new tokens per sequence)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     oracle.build()
     # all host threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
     oracle.set_num_threads(len(os.sched_getaffinity(0)))
-    pages = (ctx + 16 + 15) // 16
+    pages = (ctx + max_new + 15) // 16
     od = oracle.OracleDecoder(cfg, w, n_pages=rows * pages, max_seqs=rows, max_pages_per_seq=pages,
-                              max_pos=ctx + 16, mode=oracle.MODE_GGML_CPU)
+                              max_pos=ctx + max_new, mode=oracle.MODE_GGML_CPU)
     rng = np.random.default_rng(seed)
     for s in range(rows):
         od.seq_open(s)
@@ -156,7 +157,7 @@ def cpu_oracle_sample(cfg, w, ctx, budget_s, rows=2, seed=0):
         toks = nxt
         n_tok += rows
         el = time.perf_counter() - t0
-        if el >= budget_s or od.seq_len[0] >= ctx + 15:
+        if el >= budget_s or od.seq_len[0] >= ctx + max_new - 1:
             break
     return n_tok / el, oracle.num_threads(), n_tok, el
 
