@@ -118,6 +118,13 @@ namespace {
 
 int fail(const std::string& m, int code = FA_ERR_WEIGHTS) { return fa::report_op_error(code, m.c_str()); }
 
+// Split-K factor of an encoder GEMM of T rows (the kernel gemm() picks for it)
+int enc_split(int T, int n, int kp, int n_sm) {
+    if (n % 128) return fa::gemm_pick_split(T, n, kp, n_sm);
+    return T <= fa::kSkinnyAutoRows ? fa::gemm_tc_skinny_pick_split(T, n, kp, n_sm)
+                                    : fa::gemm_tc_pick_split(T, n, kp, n_sm);
+}
+
 using TMap = std::unordered_map<std::string, const fa_tensor_view*>;
 
 const fa_tensor_view* get(const TMap& m, const std::string& name, std::string& err) {
@@ -248,13 +255,15 @@ int load_ada_block(fa_encoder* e, const TMap& m, const std::string& p, AdaBlock&
     return FA_OK;
 }
 
-// C[split][T][n] = A[T][kp] . W^T on the tensor cores (mma.sync kernel when N is not a
-// multiple of 128); returns the split count.
+// C[split][T][n] = A[T][kp] . W^T on the tensor cores: the swapped-operand kernel up to
+// 128 rows (one utterance of up to ~13 s), the 128-row-tile kernel above, the mma.sync
+// kernel when N is not a multiple of 128; returns the split count.
 int gemm(fa_encoder* e, const __half* a, const __half* a_lo, int T, const Lin& L) {
     fa::GemmArgs g{};
     g.A = a; g.A_lo = a_lo; g.Wh = L.w; g.M = T; g.N = L.n; g.K = L.kp; g.epilogue = fa::kEpiStoreF32; g.C = e->part;
+    g.n_split = enc_split(T, L.n, L.kp, e->n_sm);
     const bool tc = L.n % 128 == 0;
-    g.n_split = tc ? fa::gemm_tc_pick_split(T, L.n, L.kp, e->n_sm) : fa::gemm_pick_split(T, L.n, L.kp, e->n_sm);
+    if (tc && T <= fa::kSkinnyAutoRows && fa::launch_q8_gemm_tc_skinny(g, e->err_dev, e->stream)) return g.n_split;
     if (!(tc && fa::gemm_tc_supported(g) && fa::launch_q8_gemm_tc(g, e->err_dev, e->stream)))
         fa::launch_q8_gemm(g, e->stream);
     return g.n_split;
@@ -374,7 +383,7 @@ extern "C" fa_encoder* fa_encoder_create(int device, const fa_encoder_desc* desc
     for (int m = 1; m <= T; ++m)
         for (const auto& sh : shapes) {
             const int kp = pad64(sh[1]);
-            const int sp = fa::gemm_tc_pick_split(m, sh[0], kp, e->n_sm);
+            const int sp = enc_split(m, sh[0], kp, e->n_sm);
             part = std::max(part, (size_t)sp * m * sh[0]);
         }
     e->part_elems = part;
