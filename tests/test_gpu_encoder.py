@@ -89,6 +89,21 @@ def prefill_ptr(dec, sid, ptr, n):
     return nxt.value, lg
 
 
+def test_batch_of_512_rows_or_more_matches_oracle(torch_cuda, small_w):
+    """A pass of >= 512 rows takes the warp-per-row LayerNorm and the 4-wide bias kernel;
+    each utterance still matches the oracle and its own smaller pass."""
+    e = _enc(SMALL, small_w, max_frames=1024)
+    rng = np.random.default_rng(12)
+    utts = [fa_synth.lfr_features(rng, n) for n in (150, 249, 3, 120, 91)]
+    assert sum(len(u) for u in utts) >= 512
+    batch = e.forward_batch(utts)
+    for u, b in zip(utts, batch):
+        ref = enc_oracle.adaptor_forward(small_w, enc_oracle.encoder_forward(small_w, u, SMALL))
+        assert rel_rms(b, ref) < 1e-4
+        assert rel_rms(b, e.forward(u)) < 1e-5
+    e.close()
+
+
 def test_batched_utterances_equal_separate_runs(torch_cuda, small_w):
     """Several utterances in one pass (block-diagonal attention, FSMN within each
     utterance) give each utterance's own result; graphs and direct launches agree."""
