@@ -29,7 +29,7 @@
 //              blocks (roundf), integer block dots, f32 sum of
 //              isum * (d_w * d_x) over blocks            (GEMM mode 2)
 //
-// Decisions this oracle defines (shared with the CUDA path, stated in DESIGN.md):
+// Decisions this oracle defines (the CUDA path makes the same ones):
 //   * KV cache is f16 in pages of 16 tokens: page layout per layer is
 //     [kv_head][K|V][token 16][head_dim], 64 KiB at 8 heads x 128 dims.
 //     Token p of a sequence lives in page block_table[slot][p/16], slot p%16.
