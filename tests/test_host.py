@@ -98,3 +98,34 @@ def test_compaction_matches_oracle_plan():
         assert mine.n_free() == n - len(live)
         if len(live) < n:
             assert mine.alloc() == len(live)
+
+
+def test_gemm_planner_choices():
+    """The split-K factors the decoder plans (host only): one row block per small-M step,
+    the swapped-operand kernel's splits for the decode shapes, and large-M GEMMs kept
+    whole once the epilogue is counted."""
+    shapes = {"qkv": (4096, 1024), "o": (1024, 2048), "gu": (6144, 1024), "dn": (1024, 3072)}
+    plan = lambda M, nm, v=0: fa_dec.op_gemm_plan(M, *shapes[nm], variant=v)
+    # 1-2 rows: the CUDA-core kernel, no split
+    assert [plan(1, nm) for nm in shapes] == [1, 1, 1, 1]
+    assert [plan(2, nm) for nm in shapes] == [1, 1, 1, 1]
+    # 128 rows: the decode step's splits (one unit per SM, 96 for gate/up)
+    assert [plan(128, nm) for nm in shapes] == [4, 16, 2, 16]
+    assert [plan(16, nm) for nm in shapes] == [4, 16, 2, 16]
+    # 2048 and 4096 rows: whole K per unit
+    assert [plan(2048, nm) for nm in shapes] == [1, 1, 1, 1]
+    assert [plan(4096, nm) for nm in shapes] == [1, 1, 1, 1]
+    # the small-M kernel alone (variant 3) also needs no split; mma.sync plans its own
+    assert plan(8, "qkv", 3) == 1
+    assert plan(128, "qkv", 1) >= 1
+
+
+def test_attention_planner_choices():
+    """Pages per CTA and splits of the decode attention: 128 rows at 2048 tokens split in
+    three (seven waves of 3 CTAs per SM); a short single row is not split (a merge launch
+    costs more than the pages it saves)."""
+    pps, ns = fa_dec.op_attention_plan(np.full(128, 2048, np.int32))
+    assert (pps, ns) == (44, 3)
+    assert fa_dec.op_attention_plan(np.array([112], np.int32))[1] == 1
+    pps, ns = fa_dec.op_attention_plan(np.array([4096], np.int32))
+    assert ns > 1 and pps * ns >= 4096 // 16
