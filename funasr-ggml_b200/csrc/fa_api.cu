@@ -1540,6 +1540,8 @@ extern "C" int fa_op_paged_attention(const float* q, int M, const int* pos, cons
     if (!q || !pos || !slot || !bt || !pool_layer || M <= 0 || pps <= 0 || n_splits <= 0 || (!out16 && !out32))
         return set_err(nullptr, FA_ERR_INVALID_ARG, "null or non-positive argument");
     if (n_splits > 1 && !scratch) return set_err(nullptr, FA_ERR_INVALID_ARG, "scratch required when n_splits > 1");
+    if (n_splits > 1 && (reinterpret_cast<uintptr_t>(scratch) & 15))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "scratch must be 16-byte aligned");
     if (int rc = ensure_configured()) return rc;
     fa::AttnArgs a{};
     a.q = q; a.pool_layer = reinterpret_cast<const __half*>(pool_layer); a.block_table = bt; a.bt_stride = bt_stride;

@@ -319,28 +319,41 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
     }
 }
 
-__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
+// Merge of the split partials: a warp per (row, query head), lane l owning dims 4l..4l+3.
+// The split maxima are read by the lanes together; every output then sums its splits in
+// split order, the same arithmetic as one thread per dim.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     pdl_trigger();
     pdl_wait();
-    const int m = a.rows ? a.rows[blockIdx.x / a.Hq] : (int)(blockIdx.x / a.Hq);
-    const int H = blockIdx.x % a.Hq;
-    const int d = threadIdx.x;
+    const int w = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (w >= a.M * a.Hq) return;
+    const int m = a.rows ? a.rows[w / a.Hq] : w / a.Hq;
+    const int H = w % a.Hq;
     const int n_kv = a.pos[m] + 1;
     const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
     const int n_valid = min(a.n_splits, (n_row_pages + a.pages_per_split - 1) / a.pages_per_split);
     const size_t base = ((size_t)m * a.Hq + H) * a.n_splits;
     float M = -INFINITY;
-    for (int s = 0; s < n_valid; ++s) M = fmaxf(M, a.part_ml[(base + s) * 2]);
-    float L = 0.0f, O = 0.0f;
+    for (int s = lane; s < n_valid; s += 32) M = fmaxf(M, a.part_ml[(base + s) * 2]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.0f;
+    float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (M != -INFINITY) {
         for (int s = 0; s < n_valid; ++s) {
             const float sc = exp2f(a.part_ml[(base + s) * 2] - M);
             L += a.part_ml[(base + s) * 2 + 1] * sc;
-            O += a.part_o[(base + s) * D + d] * sc;
+            const float4 o4 = reinterpret_cast<const float4*>(a.part_o + (base + s) * D)[lane];
+            O[0] += o4.x * sc;
+            O[1] += o4.y * sc;
+            O[2] += o4.z * sc;
+            O[3] += o4.w * sc;
         }
     }
-    const float v = L > 0.0f ? O / L : 0.0f;
-    store_out(a, (size_t)m * a.Hq * D + (size_t)H * D + d, v);
+    const size_t o = (size_t)m * a.Hq * D + (size_t)H * D + 4 * lane;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) store_out(a, o + j, L > 0.0f ? O[j] / L : 0.0f);
 }
 
 }  // namespace
@@ -358,7 +371,7 @@ void launch_paged_attention(const AttnArgs& a, cudaStream_t s) {
 }
 
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s) {
-    launch_k(attn_combine_kernel, dim3(a.M * a.Hq), dim3(128), 0, s, a);
+    launch_k(attn_combine_kernel, dim3((a.M * a.Hq + 7) / 8), dim3(256), 0, s, a);
 }
 
 // ---------------------------------------------------- allocation-free variant --

@@ -264,7 +264,8 @@ FA_API int fa_op_kv_gather(const uint16_t* pool_dev, int n_layers, int n_pages, 
  * to tokens [0, pos[m]] of sequence slot[m]. q [M][16][128] f32 (pre-scaled).
  * Output [M][2048] as f32 and/or as an f16 pair (out16 = f16(o), out16_lo = f16(o - out16),
  * the form the next GEMM reads). scratch_dev holds the split-K partials:
- * fa_op_attention_scratch_bytes(M, n_splits) bytes (may be NULL when n_splits == 1). */
+ * fa_op_attention_scratch_bytes(M, n_splits) bytes, 16-byte aligned (may be NULL when
+ * n_splits == 1). */
 FA_API size_t fa_op_attention_scratch_bytes(int M, int n_splits);
 /* The split the decoder uses for rows with contexts n_kv[M] on n_sm SMs (host only). */
 FA_API int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages_per_split, int* n_splits);
