@@ -32,16 +32,18 @@ __device__ __forceinline__ double block_sum_double(double v, double* sh) {
 }
 
 // Sum of n_part split-K partials of one float4 column group, in partial order; the
-// loads of a group of 8 partials are all issued before the first add.
+// loads of a group of G partials are all issued before the first add (the same sum for
+// every G; a larger G shortens the chain of load rounds and costs registers).
+template <int G = 8>
 __device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, int n_part) {
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 < n_part; s0 += 8) {
-        float4 t[8];
+    for (int s0 = 0; s0 < n_part; s0 += G) {
+        float4 t[G];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < G; ++u)
             if (s0 + u < n_part) t[u] = p[(size_t)(s0 + u) * stride4];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < G; ++u)
             if (s0 + u < n_part) {
                 o.x = __fadd_rn(o.x, t[u].x); o.y = __fadd_rn(o.y, t[u].y);
                 o.z = __fadd_rn(o.z, t[u].z); o.w = __fadd_rn(o.w, t[u].w);
@@ -56,7 +58,7 @@ __device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, in
 // squares summed in double, and emit(j, y) for every column j. Threads [0, 256) each own
 // the float4 groups t, t + 256, ... (hidden <= 4096, a multiple of 4); every thread of the
 // block must call it (it synchronises), and sh needs one double per warp.
-template <typename Emit>
+template <int G = 8, typename Emit>
 __device__ __forceinline__ void residual_norm_row(const float* x_row, const float4* part4, size_t stride4, int n_part,
                                                   int hidden, const float* w, float eps, float* x_out_row, double* sh,
                                                   Emit emit) {
@@ -70,7 +72,7 @@ __device__ __forceinline__ void residual_norm_row(const float* x_row, const floa
         if (!owner || i >= n4) break;
         float4 a = reinterpret_cast<const float4*>(x_row)[i];
         if (n_part > 0) {
-            const float4 o = sum_parts4(part4 + i, stride4, n_part);
+            const float4 o = sum_parts4<G>(part4 + i, stride4, n_part);
             a.x = __fadd_rn(a.x, o.x); a.y = __fadd_rn(a.y, o.y);
             a.z = __fadd_rn(a.z, o.z); a.w = __fadd_rn(a.w, o.w);
         }

@@ -43,7 +43,9 @@ __global__ void __launch_bounds__(256) embed_kernel(const void* table, int table
     }
 }
 
-// One CTA per row (residual_norm_row's 256-thread order).
+// One CTA per row (residual_norm_row's 256-thread order); G partials' loads in flight per
+// round (16 for the decode step's split-16 projections, 8 otherwise: 136 vs ~80 registers).
+template <int G>
 __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const float* part, int n_part, int M,
                                                                int hidden, const float* w, float eps,
                                                                __half* xn_hi, __half* xn_lo, const int* rows) {
@@ -54,7 +56,7 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const f
     const int n4 = hidden / 4;
     float* xr = x + (size_t)m * hidden;
     const size_t o = (size_t)blockIdx.x * hidden;
-    residual_norm_row(xr, reinterpret_cast<const float4*>(part) + (size_t)m * n4, (size_t)M * n4, n_part, hidden, w,
+    residual_norm_row<G>(xr, reinterpret_cast<const float4*>(part) + (size_t)m * n4, (size_t)M * n4, n_part, hidden, w,
                       eps, n_part > 0 ? xr : nullptr, sh,
                       [&](int j, float y) { split_store(y, xn_hi, xn_lo, o + j); });
 }
@@ -194,8 +196,12 @@ void launch_embed(const void* table, int table_type, int hidden, const int* toke
 void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w, float eps,
                              __half* xn_hi, __half* xn_lo, cudaStream_t s, int n_out, const int* rows) {
     if (n_out < 0) n_out = M;
-    launch_k(residual_rmsnorm_kernel, dim3(n_out), dim3(256), 0, s, x, part, n_part, M, hidden, w, eps, xn_hi, xn_lo,
-             rows);
+    if (n_part > 8)
+        launch_k(residual_rmsnorm_kernel<16>, dim3(n_out), dim3(256), 0, s, x, part, n_part, M, hidden, w, eps, xn_hi,
+                 xn_lo, rows);
+    else
+        launch_k(residual_rmsnorm_kernel<8>, dim3(n_out), dim3(256), 0, s, x, part, n_part, M, hidden, w, eps, xn_hi,
+                 xn_lo, rows);
 }
 
 void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s) {
