@@ -49,6 +49,27 @@ def test_op_entry_points_validate_arguments():
     assert fa_dec.op_attention_scratch_bytes(128, 4) == 128 * 16 * 4 * 130 * 4
 
 
+@pytest.mark.parametrize("call", [
+    # gather: null pool, non-positive sizes, block-table stride below max_pages
+    lambda: fa_dec.op_kv_gather(0, 28, 16, 8, 4, 8, 8, 8, 1, 4, 64, 8, 8),
+    lambda: fa_dec.op_kv_gather(16, 28, 16, 8, 4, 8, 8, 8, 0, 4, 64, 16, 16),
+    lambda: fa_dec.op_kv_gather(16, 28, 16, 8, 2, 8, 8, 8, 1, 4, 64, 16, 16),
+    # gather: a pool or slab address that is not 16-byte aligned
+    lambda: fa_dec.op_kv_gather(24, 28, 16, 8, 4, 8, 8, 8, 1, 4, 64, 16, 16),
+    # split-K partials of the paged attention need a 16-byte aligned scratch
+    lambda: fa_dec.op_paged_attention(16, 1, 16, 16, 16, 4, 16, 16, 4, 2, 24, out16=16),
+    # a GEMM variant outside 0..4, and the plan of one
+    lambda: fa_dec.op_gemm_plan(16, 1024, 1024, variant=5),
+    # the fused SwiGLU GEMM and the SwiGLU kernel reject missing buffers before touching a GPU
+    lambda: fa_dec.op_q8_gemm_swiglu(0, 0, 1, 1024, 16, 2048, 16, 16),
+    lambda: fa_dec.op_swiglu(0, 1, 1, 1024, 16, 16),
+])
+def test_new_op_entry_points_reject_bad_arguments(call):
+    with pytest.raises(fa_dec.FaError) as e:
+        call()
+    assert "INVALID_ARG" in str(e.value)
+
+
 def test_allocator_matches_oracle_policy():
     rng = np.random.default_rng(0)
     n = 300
