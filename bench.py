@@ -348,7 +348,7 @@ def run_gemm(a):
     """The weight GEMMs of one decode step on their own: for each of the 28 layers the
     QKV (4096 x 1024), o_proj (1024 x 2048), gate/up (6144 x 1024) and down (1024 x 3072)
     GEMMs, then lm_head (151936 x 1024) with its argmax, all at M = batch rows, with
-    each layer's own f16 weights (1.27 GB in all, so weights come from HBM as in the
+    each layer's own f16 weights (1.19 GB in all, so weights come from HBM as in the
     decoder) and the decoder's split-K choice. Prints the weight-read GB/s."""
     import torch
     import fa_dec
@@ -404,7 +404,7 @@ def run_gemm(a):
             "data": "synthetic: random f16 weights and activations",
             "config": {"workload": f"{L} layers x (QKV, o_proj, gate/up, down) + lm_head with argmax at M={M}",
                        "splits": splits, "weight_bytes": wbytes,
-                       "l2": "no flush: 1.27 GB of distinct weights per step"},
+                       "l2": "no flush: 1.19 GB of distinct weights per step"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "peak_kind": peak_kind},
             "gpu_launches": K * (4 * L + 2),
