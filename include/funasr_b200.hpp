@@ -27,7 +27,9 @@
 #include "funasr_dec.h"
 
 #include <algorithm>
+#include <cstdint>
 #include <cstdio>
+#include <cstring>
 #include <string>
 #include <utility>
 #include <vector>
@@ -284,6 +286,41 @@ private:
 
 // The CPU KVCache's interface (compute/kv_cache.hpp) over one paged sequence of a
 // GPUContext: a second utterance stream next to the context's own.
+// IEEE binary32 -> binary16 bits, round to nearest, ties to even (the cast the cache
+// applies to every K/V value), with overflow to infinity and gradual underflow.
+inline uint16_t f32_to_f16_bits(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) return (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0u));   // inf, nan
+    if (ax >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u);                                        // rounds past max
+    if (ax < 0x38800000u) {                                                                          // f16 subnormal
+        if (ax < 0x33000000u) return (uint16_t)sign;                                                  // below half the least
+        const int shift = 126 - (int)(ax >> 23);             // 14 ... 24
+        const uint32_t m = (ax & 0x7fffffu) | 0x800000u;
+        uint32_t r = m >> shift;
+        const uint32_t rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (r & 1u))) ++r;
+        return (uint16_t)(sign | r);
+    }
+    uint32_t r = ((ax - 0x38000000u) >> 13);                 // rebias exponent, keep 10 mantissa bits
+    const uint32_t rem = ax & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) ++r;    // may carry into the exponent: still correct
+    return (uint16_t)(sign | r);
+}
+
+// What k_tensor() / v_tensor() return. The reference hands out ggml tensors of its
+// contiguous f32 cache; ggml is absent here and the cache lives in device pages, so this
+// is a handle on one sequence's K (or V) pages: read(layer) copies a layer out as the
+// reference laid it out, [n_past][kv_dim] (f16 bits).
+class KVCache;
+struct KVTensorView {
+    const KVCache* cache = nullptr;
+    bool is_v = false;
+    bool read(int layer, std::vector<uint16_t>& out) const;
+};
+
 class KVCache {
 public:
     KVCache() = default;
@@ -300,9 +337,11 @@ public:
     }
     void clear() {
         if (ctx_) fa_seq_truncate(ctx_->handle(), seq_, 0);
+        pending_.assign(pending_.size(), Pending{});
     }
     void free() {
         if (ctx_) fa_seq_close(ctx_->handle(), seq_);
+        pending_.clear();
         ctx_ = nullptr;
         seq_ = -1;
     }
@@ -320,6 +359,42 @@ public:
         if (ctx_ && n >= 0 && n <= n_past()) fa_seq_truncate(ctx_->handle(), seq_, n);
     }
     int seq_id() const { return seq_; }
+
+    // The step's K and V of one layer as the reference's forward hands them over
+    // (compute/kv_cache.hpp:68-74): host f32 [seq_len][kv_dim], held until commit().
+    void set_pending(int layer, const float* k, const float* v) {
+        if (layer < 0 || layer >= n_layers()) return;
+        if ((int)pending_.size() < n_layers()) pending_.resize((size_t)n_layers());
+        pending_[(size_t)layer] = {k, v};
+    }
+    // Writes the pending K/V of every layer at positions [n_past, n_past + seq_len)
+    // (compute/kv_cache.hpp:80-97) and drops the pending pointers: each value cast to
+    // f16 (round to nearest even) into the sequence's pages. The cache must hold at least
+    // n_past tokens; later ones are dropped first (the pages are appended in order). A
+    // layer with nothing pending gets zeros there, the value the reference's cleared cache
+    // holds. False when the context reports an error (fa_last_error).
+    bool commit(int n_past, int seq_len) {
+        if (!ctx_ || seq_len <= 0 || n_past < 0 || n_past > this->n_past()) return false;
+        if (n_past < this->n_past() && fa_seq_truncate(ctx_->handle(), seq_, n_past) != FA_OK) return false;
+        const int L = n_layers(), kvd = kv_dim();
+        std::vector<uint16_t> k((size_t)seq_len * L * kvd, 0), v((size_t)seq_len * L * kvd, 0);
+        for (int l = 0; l < L && l < (int)pending_.size(); ++l) {
+            const Pending& p = pending_[(size_t)l];
+            if (!p.k || !p.v) continue;
+            for (int t = 0; t < seq_len; ++t)
+                for (int i = 0; i < kvd; ++i) {
+                    const size_t o = ((size_t)t * L + l) * kvd + i;
+                    k[o] = f32_to_f16_bits(p.k[(size_t)t * kvd + i]);
+                    v[o] = f32_to_f16_bits(p.v[(size_t)t * kvd + i]);
+                }
+        }
+        pending_.assign(pending_.size(), Pending{});
+        const std::vector<int> rows((size_t)seq_len, seq_);
+        return fa_kv_append(ctx_->handle(), seq_len, rows.data(), k.data(), v.data()) == FA_OK;
+    }
+    // The reference's tensor accessors (compute/kv_cache.hpp:146-147), as device views.
+    KVTensorView k_tensor() const { return {this, false}; }
+    KVTensorView v_tensor() const { return {this, true}; }
 
     std::vector<int> block_table() const {
         std::vector<int> pages;
@@ -363,10 +438,22 @@ public:
     }
 
 private:
+    struct Pending {
+        const float* k = nullptr;
+        const float* v = nullptr;
+    };
     GPUContext* ctx_ = nullptr;
     int seq_ = -1;
     int n_ctx_ = 0;
+    std::vector<Pending> pending_;
 };
+
+inline bool KVTensorView::read(int layer, std::vector<uint16_t>& out) const {
+    std::vector<uint16_t> k, v;
+    if (!cache || !cache->read_layer(layer, k, v)) return false;
+    out = is_v ? std::move(v) : std::move(k);
+    return true;
+}
 
 // Many utterance streams on one GPU: open a sequence per stream, prefill it, then
 // advance every live stream by one greedy token per step() call.

@@ -103,6 +103,48 @@ int main(int argc, char** argv) {
         CHECK(again == logits);
     }
 
+    // 5b. the reference's KVCache step contract on a cache of its own: set_pending per
+    //     layer, commit at n_past, read back through k_tensor() / v_tensor(); a rewind
+    //     commit overwrites; a layer with nothing pending reads zeros
+    {
+        KVCache kv;
+        CHECK(kv.init(ctx, 64));
+        const int L = kv.n_layers(), kvd = kv.kv_dim(), T = 20;
+        std::vector<std::vector<float>> kf((size_t)L), vf((size_t)L);
+        for (int l = 0; l < L; ++l) {
+            kf[(size_t)l].resize((size_t)T * kvd);
+            vf[(size_t)l].resize((size_t)T * kvd);
+            for (size_t i = 0; i < kf[(size_t)l].size(); ++i) {
+                kf[(size_t)l][i] = std::sin(0.001f * (float)(i + 7 * l)) * 3.0f;
+                vf[(size_t)l][i] = std::cos(0.002f * (float)(i + 5 * l)) * 0.01f;
+            }
+            kv.set_pending(l, kf[(size_t)l].data(), vf[(size_t)l].data());
+        }
+        CHECK(kv.commit(0, T));
+        CHECK(kv.n_past() == T);
+        for (int l = 0; l < L; ++l) {
+            std::vector<uint16_t> kr, vr;
+            CHECK(kv.k_tensor().read(l, kr) && kv.v_tensor().read(l, vr));
+            CHECK(kr.size() == (size_t)T * kvd && vr.size() == (size_t)T * kvd);
+            for (size_t i = 0; i < kr.size(); ++i) {
+                CHECK(kr[i] == f32_to_f16_bits(kf[(size_t)l][i]));
+                CHECK(vr[i] == f32_to_f16_bits(vf[(size_t)l][i]));
+            }
+        }
+        // rewind to 10 and commit 3 new tokens for layer 0 only
+        std::vector<float> k3((size_t)3 * kvd, 1.5f), v3((size_t)3 * kvd, -2.0f);
+        kv.set_pending(0, k3.data(), v3.data());
+        CHECK(kv.commit(10, 3));
+        CHECK(kv.n_past() == 13);
+        std::vector<uint16_t> kr0, kr1;
+        CHECK(kv.k_tensor().read(0, kr0) && kv.k_tensor().read(L - 1, kr1));
+        CHECK(kr0[(size_t)5 * kvd] == f32_to_f16_bits(kf[0][(size_t)5 * kvd]));
+        CHECK(kr0[(size_t)11 * kvd] == f32_to_f16_bits(1.5f));
+        CHECK(kr1[(size_t)11 * kvd] == 0);
+        CHECK(!kv.commit(20, 1));   // past the cached length
+        kv.free();
+    }
+
     // 6. the same utterance as a second stream through BatchDecoder
     BatchDecoder batch(ctx);
     const int s = batch.open(512);

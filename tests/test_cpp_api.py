@@ -30,6 +30,36 @@ def program(tmp_path_factory):
     return exe
 
 
+def test_host_f16_cast_matches_ieee(tmp_path):
+    """KVCache::commit casts the reference's f32 K/V with funasr_b200::f32_to_f16_bits:
+    round to nearest even, gradual underflow, overflow to infinity, NaN kept."""
+    exe = str(tmp_path / "f16cast")
+    r = subprocess.run(["g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+                        os.path.join(HERE, "cpp", "test_f16_cast.cpp"), "-o", exe], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    rng = np.random.default_rng(3)
+    edge = np.array([0.0, -0.0, 1.0, -1.0, 65504.0, 65519.99, 65520.0, 1e9, -1e9, np.inf, -np.inf,
+                     6.1035156e-05, 6.0975552e-05, 5.9604645e-08, 2.9802322e-08, 2.9802326e-08, 1e-12,
+                     1.0 + 2.0 ** -11, 1.0 + 3 * 2.0 ** -11, 2049.0, 2051.0, 0.1, 1 / 3], np.float32)
+    ticks = (np.arange(1, 1 << 14, dtype=np.uint32) << 13).view(np.float32)   # exact ties and neighbours
+    x = np.concatenate([edge, rng.standard_normal(200000).astype(np.float32) * 10,
+                        rng.standard_normal(50000).astype(np.float32) * 1e-5, ticks, np.nextafter(ticks, 0)]
+                       ).astype(np.float32)
+    (tmp_path / "in.bin").write_bytes(x.tobytes())
+    r = subprocess.run([exe, str(tmp_path / "in.bin"), str(tmp_path / "out.bin")], capture_output=True, timeout=60)
+    assert r.returncode == 0
+    got = np.frombuffer((tmp_path / "out.bin").read_bytes(), np.uint16)
+    with np.errstate(over="ignore"):
+        want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, want), np.nonzero(got != want)[0][:10]
+    nan = subprocess.run([exe, str(tmp_path / "nan.bin"), str(tmp_path / "nan_out.bin")], capture_output=True)
+    assert nan.returncode == 2                                      # missing input file
+    (tmp_path / "nan.bin").write_bytes(np.array([np.nan], np.float32).tobytes())
+    subprocess.run([exe, str(tmp_path / "nan.bin"), str(tmp_path / "nan_out.bin")], check=True)
+    h = int(np.frombuffer((tmp_path / "nan_out.bin").read_bytes(), np.uint16)[0])
+    assert (h & 0x7c00) == 0x7c00 and (h & 0x3ff) != 0
+
+
 def test_program_builds_and_reports_a_bad_model_path(program, tmp_path):
     r = subprocess.run([program, str(tmp_path / "absent.gguf"), "/dev/null", "1", "1", str(tmp_path / "o")],
                        capture_output=True, text=True, timeout=120)
