@@ -137,7 +137,7 @@ void configure_encoder(int max_T);
 void launch_enc_attention(const float* qkv, const int4* tiles, int n_tiles, int d, int n_heads, __half* out_hi,
                           __half* out_lo, int max_T, cudaStream_t s);
 constexpr int kEncAttRows = 16;
-constexpr int kEncMaxFrames = 3000;   // frames per utterance and per batched pass (scores fit in shared memory)
+constexpr int kEncMaxFrames = 3000;   // frames per utterance and per batched pass (the encoder's row buffers)
 
 // ------------------------------------------------------------------ k_gemm.cu --
 // Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T

@@ -274,21 +274,40 @@ __global__ void __launch_bounds__(256) enc_fsmn_kernel(const float* qkv, const i
 
 // Bidirectional multi-head attention within each utterance, head_dim 128. CTA = (tile,
 // head), 128 threads; a tile (first row, rows <= 16, utterance start, utterance length)
-// lies in one utterance. Keys and values pass through shared memory 32 at a time
-// (coalesced loads): scores of the tile's rows against every key of the utterance
-// (fp32, kept in shared memory), softmax per row, then thread j accumulates output dim
-// j of the rows over the value chunks.
+// lies in one utterance. One pass over the utterance's keys in chunks of 32 with an
+// online softmax: the keys and values of the next NST chunks are in flight (cp.async into
+// a ring) while a chunk is used. Warp w scores rows w, w+4, w+8, w+12 against the chunk
+// (lane = key), updates each row's running max and sum and leaves the chunk's
+// probabilities in shared memory; thread j then rescales its output dim j of the 16
+// rows and adds the chunk's values. fp32 throughout; exp of scores minus the running max.
 constexpr int ATT_ROWS = 16;
 constexpr int HD = 128;
 constexpr int KCH = 32;                  // keys per chunk
 constexpr int KLD = HD + 4;              // padded row of a staged key / value (floats)
+constexpr int NST = 3;                   // chunks in flight
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool full) {
+    // 16 bytes from global to shared memory; with full == false the destination is zeroed
+    const int n = full ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(n)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_older() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(NST - 1) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, const int4* tiles, int d,
                                                             __half* out_hi, __half* out_lo, int max_T) {
-    extern __shared__ float sm[];
-    float* qs = sm;                                  // [16][128]
-    float* kv = qs + ATT_ROWS * HD;                  // [32][KLD] staged keys, then values
-    float* sc = kv + KCH * KLD;                      // [16][max_T]
+    extern __shared__ __align__(16) float sm[];
+    float* qs = sm;                                  // [16][128] scaled queries
+    float* ks = qs + ATT_ROWS * HD;                  // [NST][32][KLD] keys
+    float* vs = ks + NST * KCH * KLD;                // [NST][32][KLD] values
+    float* ps = vs + NST * KCH * KLD;                // [16][32] the chunk's probabilities
+    float* al = ps + ATT_ROWS * KCH;                 // [16] rescale of the running output
+    float* ls = al + ATT_ROWS;                       // [16] final row sums
+    (void)max_T;
     pdl_trigger();
     pdl_wait();
     const int h = blockIdx.y;
@@ -300,79 +319,91 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
     const int ld = 3 * d;
     const float scale = 1.0f / sqrtf((float)HD);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_chunks = (T + KCH - 1) / KCH;
+
+    // chunk c into ring slot c % NST (rows past the utterance read as zeros); one copy
+    // group per call, empty past the last chunk, so group counts stay uniform
+    auto issue = [&](int c) {
+        if (c < n_chunks) {
+            const int slot = c % NST, c0 = c * KCH;
+            for (int e = threadIdx.x; e < KCH * (HD / 4); e += 128) {
+                const int kk = e / (HD / 4), j4 = e % (HD / 4);
+                const bool ok = c0 + kk < T;
+                const float* src = qkv + (size_t)(k0 + (ok ? c0 + kk : 0)) * ld + h * HD + 4 * j4;
+                cp_async16(ks + (slot * KCH + kk) * KLD + 4 * j4, src + d, ok);
+                cp_async16(vs + (slot * KCH + kk) * KLD + 4 * j4, src + 2 * d, ok);
+            }
+        }
+        cp_async_commit();
+    };
+    for (int c = 0; c < NST; ++c) issue(c);
     for (int e = threadIdx.x; e < ATT_ROWS * HD; e += 128) {
         const int r = e / HD, j = e % HD;
         qs[e] = r < nr ? qkv[(size_t)(r0 + r) * ld + h * HD + j] * scale : 0.0f;
     }
-    // scores: per chunk, lane = key, warp w takes rows w, w+4, w+8, w+12
-    for (int c0 = 0; c0 < T; c0 += KCH) {
-        const int nk = min(KCH, T - c0);
-        __syncthreads();
-        for (int e = threadIdx.x; e < KCH * (HD / 4); e += 128) {
-            const int kk = e / (HD / 4), j4 = e % (HD / 4);
-            const float4 v = kk < nk ? *reinterpret_cast<const float4*>(qkv + (size_t)(k0 + c0 + kk) * ld + d +
-                                                                       h * HD + 4 * j4)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(kv + kk * KLD + 4 * j4) = v;
-        }
-        __syncthreads();
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const float* kr = kv + lane * KLD;
-#pragma unroll 4
-        for (int j = 0; j < HD; j += 4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(kr + j);
+
+    float m_run[4], l_run[4];                        // rows warp + 4i; every lane holds the same values
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float4 q4 = *reinterpret_cast<const float4*>(qs + (warp + 4 * i) * HD + j);
-                acc[i] = fmaf(q4.x, k4.x, fmaf(q4.y, k4.y, fmaf(q4.z, k4.z, fmaf(q4.w, k4.w, acc[i]))));
-            }
-        }
-        if (lane < nk)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sc[(warp + 4 * i) * max_T + c0 + lane] = acc[i];
+    for (int i = 0; i < 4; ++i) {
+        m_run[i] = -INFINITY;
+        l_run[i] = 0.0f;
     }
-    __syncthreads();
-    // softmax per row: warp w takes rows w, w+4, ...
-    for (int r = warp; r < nr; r += 4) {
-        float* row = sc + r * max_T;
-        float m = -INFINITY;
-        for (int t = lane; t < T; t += 32) m = fmaxf(m, row[t]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float ssum = 0.0f;
-        for (int t = lane; t < T; t += 32) {
-            const float ex = expf(row[t] - m);
-            row[t] = ex;
-            ssum += ex;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-        const float inv = 1.0f / ssum;
-        for (int t = lane; t < T; t += 32) row[t] *= inv;
-    }
-    // output: thread j owns head dim j of the rows; values staged per chunk
-    const int j = threadIdx.x;
+    const int j = threadIdx.x;                       // output dim of this thread
     float acc[ATT_ROWS];
 #pragma unroll
     for (int r = 0; r < ATT_ROWS; ++r) acc[r] = 0.0f;
-    for (int c0 = 0; c0 < T; c0 += KCH) {
-        const int nk = min(KCH, T - c0);
-        __syncthreads();
-        for (int e = threadIdx.x; e < KCH * (HD / 4); e += 128) {
-            const int kk = e / (HD / 4), j4 = e % (HD / 4);
-            const float4 v = kk < nk ? *reinterpret_cast<const float4*>(qkv + (size_t)(k0 + c0 + kk) * ld + 2 * d +
-                                                                       h * HD + 4 * j4)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(kv + kk * KLD + 4 * j4) = v;
-        }
-        __syncthreads();
-        for (int kk = 0; kk < nk; ++kk) {
-            const float v = kv[kk * KLD + j];
+
+    for (int c = 0; c < n_chunks; ++c) {
+        cp_async_wait_older();                       // this thread's copies of chunk c have landed
+        __syncthreads();                             // ... and every thread's; the queries too
+        const int slot = c % NST, nk = min(KCH, T - c * KCH);
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* kr = ks + (slot * KCH + lane) * KLD;
+#pragma unroll 4
+        for (int jj = 0; jj < HD; jj += 4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(kr + jj);
 #pragma unroll
-            for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(sc[r * max_T + c0 + kk], v, acc[r]);
+            for (int i = 0; i < 4; ++i) {
+                const float4 q4 = *reinterpret_cast<const float4*>(qs + (warp + 4 * i) * HD + jj);
+                sc[i] = fmaf(q4.x, k4.x, fmaf(q4.y, k4.y, fmaf(q4.z, k4.z, fmaf(q4.w, k4.w, sc[i]))));
+            }
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int r = warp + 4 * i;
+            const float sv = lane < nk ? sc[i] : -INFINITY;
+            float cm = sv;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+            const float mn = fmaxf(m_run[i], cm);    // finite: every chunk holds at least one key
+            const float a = m_run[i] == -INFINITY ? 0.0f : expf(m_run[i] - mn);
+            const float p = lane < nk ? expf(sv - mn) : 0.0f;
+            float psum = p;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+            l_run[i] = l_run[i] * a + psum;
+            m_run[i] = mn;
+            ps[r * KCH + lane] = p;
+            if (lane == 0) al[r] = a;
+        }
+        __syncthreads();
+        const float* vr = vs + slot * KCH * KLD + j;
+#pragma unroll
+        for (int r = 0; r < ATT_ROWS; ++r) acc[r] *= al[r];
+        for (int kk = 0; kk < nk; ++kk) {
+            const float v = vr[kk * KLD];
+#pragma unroll
+            for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(ps[r * KCH + kk], v, acc[r]);
+        }
+        __syncthreads();                             // every thread is done with slot c % NST
+        issue(c + NST);
     }
-    for (int r = 0; r < nr; ++r) split_store_h(acc[r], out_hi, out_lo, (size_t)(r0 + r) * d + h * HD + j);
+    cp_async_wait_all();                             // only empty groups remain; none outlives the CTA
+    if (lane == 0)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ls[warp + 4 * i] = l_run[i];
+    __syncthreads();
+    for (int r = 0; r < nr; ++r) split_store_h(acc[r] / ls[r], out_hi, out_lo, (size_t)(r0 + r) * d + h * HD + j);
 }
 
 }  // namespace
@@ -425,10 +456,13 @@ void launch_enc_fsmn(const float* qkv, int T, const int2* seg, int d, const floa
     launch_k(enc_fsmn_kernel, dim3(T), dim3(256), 0, s, qkv, seg, d, w, K, pad, mem);
 }
 
-size_t enc_attention_smem(int max_T) { return sizeof(float) * ((size_t)ATT_ROWS * (HD + max_T) + KCH * KLD); }
+size_t enc_attention_smem(int max_T) {
+    (void)max_T;   // the online softmax keeps no per-key scores
+    return sizeof(float) * ((size_t)ATT_ROWS * HD + 2 * NST * KCH * KLD + ATT_ROWS * KCH + 2 * ATT_ROWS);
+}
 
-// The attention kernel's shared memory holds a tile's scores against max_T keys: sized
-// once per device for the longest utterance any encoder accepts (kEncMaxFrames).
+// The attention kernel's shared memory (queries, the key / value ring, one chunk's
+// probabilities: 109 KiB) does not depend on the utterance length; opt in once per device.
 void configure_encoder(int) {
     cudaFuncSetAttribute(enc_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)enc_attention_smem(kEncMaxFrames));
