@@ -74,7 +74,7 @@ void set_launch_pdl(bool on) { t_launch_pdl = on; }
 
 // Kernel attribute set-up, once per device (before any graph capture).
 namespace fa {
-void configure_attention();
+cudaError_t configure_attention();
 void configure_gemm();
 void configure_gemm_tc();
 void configure_gemm_tc_skinny();

@@ -9,8 +9,8 @@
 //
 // Work split: one CTA per (split of `pages_per_split` pages, KV head, row).
 // 4 warps; warp w owns pages w, w+4, ... of the split. Each warp streams its
-// pages through a private 3-stage shared-memory ring: lane 0 issues one 8 KiB
-// cp.async.bulk (TMA bulk copy, K and V of this head in this page) per stage,
+// pages through a private kAttnStages-deep (2) shared-memory ring: lane 0 issues one
+// 8 KiB cp.async.bulk (TMA bulk copy, K and V of this head in this page) per stage,
 // completion is counted on an mbarrier, every wait is bounded in time.
 // Compute per page (lane = (token parity par, 8-dim chunk c)):
 //   QK  : 8 x 16 B shared loads, 16 fp32 FMAs each, then a 16-lane transpose
@@ -90,6 +90,13 @@ __device__ __forceinline__ float transpose_reduce16(float (&v)[16], int lane) {
     return v[0];
 }
 
+// The row's context must be 1 .. bt_stride * 16 tokens and pages_per_split * n_splits
+// must reach its last page; otherwise the kernel and the merge leave the row untouched.
+__device__ __forceinline__ bool row_len_bad(const AttnArgs& a, int n_kv, int n_row_pages) {
+    return n_kv <= 0 || n_row_pages > a.bt_stride ||
+           (long long)a.pages_per_split * a.n_splits < (long long)n_row_pages;
+}
+
 // Output as f32 and/or as the (hi, lo) f16 pair the o_proj GEMM consumes.
 __device__ __forceinline__ void store_out(const AttnArgs& a, size_t o, float v) {
     if (a.out16) {
@@ -113,6 +120,13 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
 
     const int n_kv = a.pos[m] + 1;
     const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
+    // A row whose position is negative, whose pages run past its block-table row, or
+    // whose pages the splits do not all cover is an argument error: flag it (once, from
+    // split 0) and write nothing for the row.
+    if (row_len_bad(a, n_kv, n_row_pages)) {
+        if (split == 0 && threadIdx.x == 0) record_error(a.err, kDevErrBadLen);
+        return;
+    }
     const int p_begin = split * a.pages_per_split;
     if (p_begin >= n_row_pages) return;                 // uniform for the CTA
     const int p_end = min(n_row_pages, p_begin + a.pages_per_split);
@@ -332,6 +346,7 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     const int H = w % a.Hq;
     const int n_kv = a.pos[m] + 1;
     const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
+    if (row_len_bad(a, n_kv, n_row_pages)) return;      // flagged by the attention kernel
     const int n_valid = min(a.n_splits, (n_row_pages + a.pages_per_split - 1) / a.pages_per_split);
     const size_t base = ((size_t)m * a.Hq + H) * a.n_splits;
     float M = -INFINITY;
@@ -361,8 +376,9 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
 size_t attn_smem_bytes() { return sizeof(AttnSmem); }
 
 // Opt the kernel into its dynamic shared memory on the current device.
-void configure_attention() {
-    cudaFuncSetAttribute(paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(AttnSmem));
+cudaError_t configure_attention() {
+    return cudaFuncSetAttribute(paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(AttnSmem));
 }
 
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s) {
@@ -395,9 +411,12 @@ void* g_noalloc_ptr[64] = {};   // device address of g_attn_scratch per device
 
 // The first call on a device looks up the buffer's device address there
 // (cudaGetSymbolAddress) and sets the kernel's shared-memory limit; make that first
-// call before any stream capture. All calls share the one buffer, so calls whose
-// work overlaps on the GPU (other streams, other host threads) race on it. Nothing
-// in it needs to start at zero: a call writes every partial it later reads.
+// call before any stream capture. The address is cached per device for the life of
+// the process: a cudaDeviceReset() destroys the context it belongs to, so do not
+// call this entry point on a device after resetting it. All calls share the one
+// buffer, so calls whose work overlaps on the GPU (other streams, other host
+// threads) race on it. Nothing in it needs to start at zero: a call writes every
+// partial it later reads.
 extern "C" FA_API int fa_op_paged_attention_noalloc(const float* q, int M, const int* pos, const int* slot,
                                                     const int* bt, int bt_stride, int n_pages,
                                                     const uint16_t* pool_layer, int pps, int n_splits,
@@ -429,8 +448,14 @@ extern "C" FA_API int fa_op_paged_attention_noalloc(const float* q, int M, const
                                         cudaGetErrorString(e);
                 return report_op_error(FA_ERR_CUDA, msg.c_str());
             }
-            configure_attention();
-            g_noalloc_ptr[dev] = p;
+            const cudaError_t ec = configure_attention();
+            if (ec != cudaSuccess) {
+                cudaGetLastError();
+                const std::string msg = std::string("fa_op_paged_attention_noalloc: shared-memory limit: ") +
+                                        cudaGetErrorString(ec);
+                return report_op_error(FA_ERR_CUDA, msg.c_str());
+            }
+            g_noalloc_ptr[dev] = p;   // cached only once both set-up calls succeeded
         }
         base = g_noalloc_ptr[dev];
     }

@@ -265,7 +265,9 @@ FA_API int fa_op_kv_gather(const uint16_t* pool_dev, int n_layers, int n_pages, 
  * Output [M][2048] as f32 and/or as an f16 pair (out16 = f16(o), out16_lo = f16(o - out16),
  * the form the next GEMM reads). scratch_dev holds the split-K partials:
  * fa_op_attention_scratch_bytes(M, n_splits) bytes, 16-byte aligned (may be NULL when
- * n_splits == 1). */
+ * n_splits == 1). A row with pos < 0, with more pages than bt_stride, or whose pages
+ * pages_per_split * n_splits does not cover sets error bit 8 and is not written; a page
+ * id outside [0, n_pages) sets bit 2. */
 FA_API size_t fa_op_attention_scratch_bytes(int M, int n_splits);
 /* The split the decoder uses for rows with contexts n_kv[M] on n_sm SMs (host only). */
 FA_API int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages_per_split, int* n_splits);
@@ -290,8 +292,10 @@ FA_API int fa_op_prefill_attention(const float* q_dev, int M, const int* pos_dev
  * that forbids allocation once started). The split-K partials go to one 8 MiB buffer
  * built into the library (held on every GPU that loads it until exit), so
  * M * n_splits <= 1008 (FA_ERR_CAPACITY otherwise). The first call on a device sets
- * the buffer up; make it before any stream capture. Calls share the buffer: calls
- * that overlap on the GPU race. */
+ * the buffer up; make it before any stream capture (and not after a cudaDeviceReset
+ * of that device: the cached address belongs to the destroyed context). Calls share
+ * the buffer: calls that overlap on the GPU race. Row and page checks as for
+ * fa_op_paged_attention. */
 FA_API int fa_op_paged_attention_noalloc(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
                                          const int* block_table_dev, int bt_stride, int n_pages,
                                          const uint16_t* pool_layer_dev, int pages_per_split, int n_splits,

@@ -1,7 +1,7 @@
 """Generate the golden fixtures that pin the CPU oracle.
 
 Run in the build container (needs the reference tree and transformers):
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the FunASR-GGML source tree>
 
 1. q8_0_codec.npz — inputs and the bytes produced by the reference converter's own
    Q8_0 quantiser, FunAsr.quantize_q8_0 in tools/hf_convert_ggml_q8.py:354-381,
@@ -149,6 +149,8 @@ def hf_small():
 
 
 if __name__ == "__main__":
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the FunASR-GGML source tree>")
+    ref = sys.argv[1]
     q8_codec(ref)
     hf_small()

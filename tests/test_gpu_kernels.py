@@ -239,6 +239,46 @@ def test_paged_attention_sharp_softmax(torch_cuda):
     assert_close(o32, ref, max_abs_tol=1e-3, rel_rms_tol=1e-5, what="attention f32")
 
 
+@pytest.mark.parametrize("case", ["too_few_splits", "pos_past_block_table", "negative_pos"])
+def test_paged_attention_rejects_bad_rows(torch_cuda, case):
+    """A row the kernel cannot serve sets error bit 8 and keeps its old output; the other
+    rows are still computed."""
+    torch = torch_cuda
+    rng = np.random.default_rng(12)
+    n_pages, bt_stride = 256, 8
+    M = 3
+    n_kv = np.array([100, 37, 128], np.int32)            # 7, 3 and 8 pages
+    pps, n_splits = 4, 2
+    if case == "too_few_splits":
+        pps = 3                                          # 6 pages covered; row 0 and 2 need more
+    bt = np.stack([rng.choice(n_pages, bt_stride, replace=False) for _ in range(M)]).astype(np.int32)
+    pool = oracle.f32_to_f16_bits(rng.standard_normal((n_pages, PAGE_ELEMS)).astype(np.float32))
+    q = (rng.standard_normal((M, 16, 128)) * 0.3).astype(np.float32)
+    slot = np.arange(M, dtype=np.int32)
+    pos = n_kv - 1
+    bad = {0, 2} if case == "too_few_splits" else {0}
+    if case == "pos_past_block_table":
+        pos[0] = bt_stride * 16                          # page 8 of an 8-entry row
+    if case == "negative_pos":
+        pos[0] = -5
+    ref = oracle.paged_attention(q, slot, n_kv, bt, pool)
+    d = [dev(torch, a) for a in (q, pos, slot, bt, _i16(pool))]
+    out32 = torch.full((M, 2048), 3.0, dtype=torch.float32, device="cuda")
+    scratch = torch.zeros(fa_dec.op_attention_scratch_bytes(M, n_splits), dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    fa_dec.op_paged_attention(d[0].data_ptr(), M, d[1].data_ptr(), d[2].data_ptr(), d[3].data_ptr(), bt_stride,
+                              n_pages, d[4].data_ptr(), pps, n_splits, scratch.data_ptr(), 0, out32.data_ptr(),
+                              err.data_ptr())
+    torch.cuda.synchronize()
+    assert int(err.item()) == 8
+    got = out32.cpu().numpy()
+    for m in range(M):
+        if m in bad:
+            assert (got[m] == 3.0).all(), m
+        else:
+            assert_close(got[m], ref[m], max_abs_tol=1e-4, rel_rms_tol=1e-5, what=f"row {m}")
+
+
 def test_paged_attention_full_size_batch128_ctx2048(torch_cuda):
     """B=128 rows at 2048-2175 tokens (one layer of the steady-state decode shape); all
     rows checked for finiteness, 12 sampled rows against the oracle."""
