@@ -348,8 +348,9 @@ def run_gemm(a):
     """The weight GEMMs of one decode step on their own: for each of the 28 layers the
     QKV (4096 x 1024), o_proj (1024 x 2048), gate/up (6144 x 1024) and down (1024 x 3072)
     GEMMs, then lm_head (151936 x 1024) with its argmax, all at M = batch rows, with
-    each layer's own f16 weights (1.19 GB in all, so weights come from HBM as in the
-    decoder) and the decoder's split-K choice. Prints the weight-read GB/s."""
+    each layer's own Q8_0 weights in the decoder's plane form (0.633 GB of q and scales
+    read per step, so weights come from HBM as in the decoder) and the decoder's split-K
+    choice. Prints the weight-read GB/s (algorithmic: 34 B per 32 weights)."""
     import torch
     import fa_dec
 
@@ -362,8 +363,18 @@ def run_gemm(a):
     shapes = [("qkv", 4096, H), ("o", H, 2048), ("gate_up", 2 * F, H), ("down", H, F)]
     n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
     splits = {nm: fa_dec.op_gemm_plan(M, n, k, 0, n_sm) for nm, n, k in shapes}
-    weights = [{nm: (torch.randn(n, k, device=dev) * 0.02).half() for nm, n, k in shapes} for _ in range(L)]
-    lm = (torch.randn(V, H, device=dev) * 0.02).half()
+    def planes(n, k):
+        """Q8_0 planes: q int8 [n][k], scales f16 [k/32][n] and [n][k/32] ~U(0.001, 0.02)."""
+        buf = torch.empty(fa_dec.op_q8_planes_bytes(n, k), dtype=torch.uint8, device=dev)
+        buf[:n * k].view(torch.int8).copy_(torch.randint(-127, 128, (n * k,), dtype=torch.int8, device=dev))
+        d = (torch.rand(k // 32, n, device=dev) * 0.019 + 0.001).half()
+        nd = n * k // 32
+        buf[n * k:n * k + 2 * nd].view(torch.float16).copy_(d.reshape(-1))
+        buf[n * k + 2 * nd:].view(torch.float16).copy_(d.t().contiguous().reshape(-1))
+        return buf
+
+    weights = [{nm: planes(n, k) for nm, n, k in shapes} for _ in range(L)]
+    lm = planes(V, H)
     a_hi = (torch.randn(M, max(F, 2048), device=dev)).half()
     a_lo = (torch.randn(M, max(F, 2048), device=dev) * 1e-4).half()
     part = torch.empty(max(splits.values()) * M * 2 * F, dtype=torch.float32, device=dev)
@@ -374,10 +385,10 @@ def run_gemm(a):
     def step():
         for l in range(L):
             for nm, n, k in shapes:
-                fa_dec.op_q8_gemm(a_hi.data_ptr(), a_lo.data_ptr(), M, k, weights[l][nm].data_ptr(), n, splits[nm],
-                                  part.data_ptr(), 0, stream)
-        fa_dec.op_q8_gemm_argmax(a_hi.data_ptr(), a_lo.data_ptr(), M, H, lm.data_ptr(), V, am_scr.data_ptr(),
-                                 nxt.data_ptr(), 0, 0, stream)
+                fa_dec.op_q8p_gemm(a_hi.data_ptr(), a_lo.data_ptr(), M, k, weights[l][nm].data_ptr(), n,
+                                   splits[nm], part.data_ptr(), 0, stream)
+        fa_dec.op_q8p_gemm_argmax(a_hi.data_ptr(), a_lo.data_ptr(), M, H, lm.data_ptr(), V, am_scr.data_ptr(),
+                                  nxt.data_ptr(), 0, 0, stream)
 
     for _ in range(W):
         step()
@@ -393,18 +404,18 @@ def run_gemm(a):
     torch.cuda.synchronize()
     clocks = sampler.stop()
     ms = fa_multi.reduce(e0.elapsed_time(e1), "max") / K
-    wbytes = sum(n * k * 2 for _, n, k in shapes) * L + V * H * 2
+    wbytes = (sum(n * k for _, n, k in shapes) * L + V * H) * 34 // 32
     gbs = wbytes / (ms / 1e3) / 1e9
     peak, peak_kind = measured_peaks()
     if rank == 0:
         print(json.dumps({
             "metric": "decode-step weight GEMMs, weight-read GB/s", "value": gbs * world, "unit": "GB/s",
             "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16 (hi/lo activations x f16(d*q) weights)",
-            "data": "synthetic: random f16 weights and activations",
+            "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 x f16 pair (exact d*q, fp32 sums)",
+            "data": "synthetic: random Q8_0 weights (scales U(0.001, 0.02)) and activations",
             "config": {"workload": f"{L} layers x (QKV, o_proj, gate/up, down) + lm_head with argmax at M={M}",
                        "splits": splits, "weight_bytes": wbytes,
-                       "l2": "no flush: 1.19 GB of distinct weights per step"},
+                       "l2": "no flush: 0.63 GB of distinct Q8_0 weights per step"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "peak_kind": peak_kind},
             "gpu_launches": K * (4 * L + 2),
@@ -522,8 +533,8 @@ def run_prefill(a):
 
 # --------------------------------------------------- continuous batching --
 def run_serve(a):
-    """Continuous batching (fa_sched_*): --streams streams over all GPUs, sharded
-    across ranks with no collectives; prompt lengths log-uniform in [200, 6000] tokens,
+    """Continuous batching (fa_sched_*): --streams streams over all GPUs, each given at
+    its arrival to the rank with the fewest outstanding KV pages (no collectives); prompt lengths log-uniform in [200, 6000] tokens,
     output lengths uniform in [16, 512] (EOS ignored), Poisson arrivals at
     --arrival-rate streams/s over all GPUs, a --kv-gb page pool per GPU. Each step
     runs one forward over every running stream's next token plus prompt chunks of up to
@@ -543,7 +554,9 @@ def run_serve(a):
     plen = np.exp(rng.uniform(np.log(200), np.log(6000), n)).astype(np.int64)
     olen = rng.integers(16, 513, n)
     arrive = np.cumsum(rng.exponential(1.0 / a.arrival_rate, n))
-    mine = fa_multi.shard(list(range(n)), rank, world)
+    # streams go to the rank with the fewest outstanding KV pages at their arrival
+    owner = fa_multi.dispatch_by_pages(arrive, plen, olen, world)
+    mine = [int(i) for i in np.flatnonzero(owner == rank)]
     page_bytes = 28 * 8 * 2 * 16 * 128 * 2
     n_pages = int(a.kv_gb * 1e9 // page_bytes)
     max_ctx = int((plen.max() + olen.max() + 31) // 16 * 16)

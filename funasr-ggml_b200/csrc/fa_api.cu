@@ -18,6 +18,7 @@
 // elementwise op folded into a neighbour.
 #include "fa_kernels.cuh"
 #include "page_alloc.hpp"
+#include "nvtx_range.hpp"
 #include "funasr_dec.h"
 
 #include <algorithm>
@@ -35,12 +36,13 @@ namespace {
 
 thread_local std::string g_err;
 
-// Q8_0 weights on the device as f16(d * q) [N][K].
+// Q8_0 weights on the device as q / d_t / d_r planes (q8_planes.cuh), one buffer per
+// (stacked) matrix: the GGUF bytes rearranged, nothing rounded.
 struct LayerW {
-    __half* qkv_q = nullptr;
-    __half* o_q = nullptr;
-    __half* gu_q = nullptr;
-    __half* dn_q = nullptr;
+    unsigned char* qkv_q = nullptr;
+    unsigned char* o_q = nullptr;
+    unsigned char* gu_q = nullptr;
+    unsigned char* dn_q = nullptr;
     float* in_norm = nullptr;
     float* post_norm = nullptr;
     float* q_norm = nullptr;
@@ -113,7 +115,7 @@ struct fa_ctx {
     void* embed = nullptr;
     int embed_type = FA_TYPE_BF16;
     float* final_norm = nullptr;
-    __half* lm_q = nullptr;
+    unsigned char* lm_q = nullptr;
     std::vector<void*> dev_allocs;
 
     __half* pool = nullptr;
@@ -513,10 +515,12 @@ static int upload_vec_f32(fa_ctx* ctx, const fa_tensor_view* v, float** dst) {
     return FA_OK;
 }
 
-// Expand a GGUF Q8_0 tensor with N rows of K into f16(d * q) rows at row offset r0.
-static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, __half* w) {
+// Split a GGUF Q8_0 tensor with N rows of K into the planes of a stacked matrix of
+// n_total rows, at row offset r0.
+static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, int n_total,
+                     unsigned char* planes) {
     FA_CK(cudaMemcpyAsync(staging, v->data, v->nbytes, cudaMemcpyHostToDevice, ctx->stream));
-    fa::launch_repack_q8(staging, N, K, r0, w, ctx->stream);
+    fa::launch_repack_q8_planes(staging, N, K, r0, n_total, planes, ctx->stream);
     FA_CK(cudaGetLastError());
     FA_CK(cudaStreamSynchronize(ctx->stream));
     return FA_OK;
@@ -574,24 +578,24 @@ extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n
             LayerW& w = ctx->L[l];
             LV& t = lv[l];
             int r;
-            if ((r = dev_alloc(ctx, &w.qkv_q, (size_t)QKV * H * 2)) || (r = dev_alloc(ctx, &w.o_q, (size_t)H * QD * 2)) ||
-                (r = dev_alloc(ctx, &w.gu_q, (size_t)2 * F * H * 2)) || (r = dev_alloc(ctx, &w.dn_q, (size_t)H * F * 2)))
+            if ((r = dev_alloc(ctx, &w.qkv_q, fa::q8p_bytes(QKV, H))) || (r = dev_alloc(ctx, &w.o_q, fa::q8p_bytes(H, QD))) ||
+                (r = dev_alloc(ctx, &w.gu_q, fa::q8p_bytes(2 * F, H))) || (r = dev_alloc(ctx, &w.dn_q, fa::q8p_bytes(H, F))))
                 return r;
-            if ((r = upload_q8(ctx, t.q, staging, QD, H, 0, w.qkv_q)) ||
-                (r = upload_q8(ctx, t.k, staging, KD, H, QD, w.qkv_q)) ||
-                (r = upload_q8(ctx, t.v, staging, KD, H, QD + KD, w.qkv_q)) ||
-                (r = upload_q8(ctx, t.o, staging, H, QD, 0, w.o_q)) ||
-                (r = upload_q8(ctx, t.g, staging, F, H, 0, w.gu_q)) ||
-                (r = upload_q8(ctx, t.u, staging, F, H, F, w.gu_q)) ||
-                (r = upload_q8(ctx, t.dn, staging, H, F, 0, w.dn_q)))
+            if ((r = upload_q8(ctx, t.q, staging, QD, H, 0, QKV, w.qkv_q)) ||
+                (r = upload_q8(ctx, t.k, staging, KD, H, QD, QKV, w.qkv_q)) ||
+                (r = upload_q8(ctx, t.v, staging, KD, H, QD + KD, QKV, w.qkv_q)) ||
+                (r = upload_q8(ctx, t.o, staging, H, QD, 0, H, w.o_q)) ||
+                (r = upload_q8(ctx, t.g, staging, F, H, 0, 2 * F, w.gu_q)) ||
+                (r = upload_q8(ctx, t.u, staging, F, H, F, 2 * F, w.gu_q)) ||
+                (r = upload_q8(ctx, t.dn, staging, H, F, 0, H, w.dn_q)))
                 return r;
             if ((r = upload_vec_f32(ctx, t.qn, &w.q_norm)) || (r = upload_vec_f32(ctx, t.kn, &w.k_norm)) ||
                 (r = upload_vec_f32(ctx, t.in, &w.in_norm)) || (r = upload_vec_f32(ctx, t.post, &w.post_norm)))
                 return r;
         }
         int r;
-        if ((r = dev_alloc(ctx, &ctx->lm_q, (size_t)V * H * 2))) return r;
-        if ((r = upload_q8(ctx, lm, staging, V, H, 0, ctx->lm_q))) return r;
+        if ((r = dev_alloc(ctx, &ctx->lm_q, fa::q8p_bytes(V, H)))) return r;
+        if ((r = upload_q8(ctx, lm, staging, V, H, 0, V, ctx->lm_q))) return r;
         if ((r = upload_vec_f32(ctx, fnorm, &ctx->final_norm))) return r;
         if ((r = dev_alloc(ctx, (uint8_t**)&ctx->embed, emb->nbytes))) return r;
         FA_CK(cudaMemcpy(ctx->embed, emb->data, emb->nbytes, cudaMemcpyHostToDevice));
@@ -782,8 +786,11 @@ static bool gemv_rows(int variant, int M) {
     return (variant == 0 && M <= fa::kGemvAutoRows) || (variant == 3 && M <= fa::kGemvMaxRows);
 }
 
-// Whether a GEMM of M rows goes to the swapped (few-row) tcgen05 kernel.
-static bool skinny_rows(int variant, int M, int epilogue = fa::kEpiStoreF32) {
+// Whether a GEMM of M rows goes to the swapped tcgen05 kernel. With Q8_0 planes (the
+// decoder's weights) it takes every M above the CUDA-core kernel's rows, in 128-row
+// activation tiles; with f16 weights it takes one tile of up to 128 rows.
+static bool skinny_rows(int variant, int M, int epilogue = fa::kEpiStoreF32, bool q8 = true) {
+    if (q8) return (variant == 0 && M > fa::kGemvAutoRows) || variant == 4;
     const int auto_rows = epilogue == fa::kEpiArgmax ? fa::kSkinnyArgmaxAutoRows : fa::kSkinnyAutoRows;
     return (variant == 0 && M > fa::kGemvAutoRows && M <= auto_rows) || (variant == 4 && M <= fa::kSkinnyMaxRows);
 }
@@ -853,7 +860,9 @@ static void run_gemm(fa_ctx* ctx, const fa::GemmArgs& g) {
     const int v = ctx->gemm_variant;
     if (v != 1) {
         if (gemv_rows(v, g.M) && fa::launch_q8_gemv(g, ctx->stream)) return;
-        if (skinny_rows(v, g.M, g.epilogue) && fa::launch_q8_gemm_tc_skinny(g, ctx->err_dev, ctx->stream)) return;
+        if (skinny_rows(v, g.M, g.epilogue, g.W8.q != nullptr) &&
+            fa::launch_q8_gemm_tc_skinny(g, ctx->err_dev, ctx->stream))
+            return;
         if (fa::gemm_tc_supported(g) && fa::launch_q8_gemm_tc(g, ctx->err_dev, ctx->stream)) return;
     }
     fa::launch_q8_gemm(g, ctx->stream);
@@ -877,7 +886,7 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         __half* pool_l = ctx->pool + (size_t)l * ctx->layer_stride;
         fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, w.in_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         fa::GemmArgs g{};
-        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = w.qkv_q; g.M = M; g.N = QKV; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(w.qkv_q, QKV, H); g.M = M; g.N = QKV; g.K = H;
         g.n_split = p.s_qkv; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         run_gemm(ctx, g);
         fa::AppendArgs a{};
@@ -916,12 +925,13 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         }
         if (prof_l) record_prof(ctx, 2 * l + 1, capturing);
         g = fa::GemmArgs{};
-        g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.Wh = w.o_q; g.M = M; g.N = H; g.K = kHq * kD;
+        g.A = ctx->attn16; g.A_lo = ctx->attn_lo; g.W8 = fa::q8p_view(w.o_q, H, kHq * kD); g.M = M; g.N = H;
+        g.K = kHq * kD;
         g.n_split = p.s_o; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         run_gemm(ctx, g);
         fa::launch_residual_rmsnorm(ctx->x, ctx->part, p.s_o, M, H, w.post_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         g = fa::GemmArgs{};
-        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = w.gu_q; g.M = M; g.N = 2 * F; g.K = H;
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(w.gu_q, 2 * F, H); g.M = M; g.N = 2 * F; g.K = H;
         g.n_split = p.s_gu;
         if (p.fuse_swiglu) {
             g.epilogue = fa::kEpiSwiglu; g.H = ctx->h16; g.H_lo = ctx->h_lo;
@@ -933,7 +943,7 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
             fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s);
         }
         g = fa::GemmArgs{};
-        g.A = ctx->h16; g.A_lo = ctx->h_lo; g.Wh = w.dn_q; g.M = M; g.N = H; g.K = F;
+        g.A = ctx->h16; g.A_lo = ctx->h_lo; g.W8 = fa::q8p_view(w.dn_q, H, F); g.M = M; g.N = H; g.K = F;
         g.n_split = p.s_dn; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
         run_gemm(ctx, g);
         n += 8;
@@ -948,7 +958,8 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s,
                                 Mo, all ? nullptr : ctx->out_rows);
     fa::GemmArgs g{};
-    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.Wh = ctx->lm_q; g.M = Mo; g.N = d.vocab; g.K = H;
+    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(ctx->lm_q, d.vocab, H); g.M = Mo; g.N = d.vocab;
+    g.K = H;
     g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = p.logits ? ctx->logits_dev : nullptr;
     g.amax_val = ctx->amax_v; g.amax_idx = ctx->amax_i;
     run_gemm(ctx, g);
@@ -967,6 +978,7 @@ static int enqueue_step_pdl(fa_ctx* ctx, const StepPlan& p, bool capturing) {
 }
 
 static int run_step(fa_ctx* ctx, const StepPlan& p) {
+    fa::NvtxRange nv("fa step");
     if (p.prof)
         if (int rc = ensure_prof_events(ctx)) return rc;
     if (!ctx->use_graphs) {
@@ -977,6 +989,7 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
     }
     auto it = ctx->graphs.find(p.key());
     if (it == ctx->graphs.end()) {
+        fa::NvtxRange nv_cap("fa step graph capture");
         FA_CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
         const int n = enqueue_step_pdl(ctx, p, true);
         cudaGraph_t graph = nullptr;
@@ -1019,6 +1032,7 @@ extern "C" int fa_forward(fa_ctx* ctx, int n_rows, const int* seq_ids, const int
 
 extern "C" int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, const int* token_ids, const float* embeds,
                                int n_out, const int* out_rows, int* next_ids, float* logits) {
+    fa::NvtxRange nv("fa_forward_rows");
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     if (!ctx->loaded) return set_err(ctx, FA_ERR_NOT_READY, "weights not loaded");
     if (n_rows <= 0 || n_rows > ctx->d.max_rows || !seq_ids)
@@ -1160,6 +1174,7 @@ extern "C" int fa_decode_step(fa_ctx* ctx, int n_seq, const int* seq_ids, const 
 
 extern "C" int fa_generate(fa_ctx* ctx, int n_seq, const int* seq_ids, const int* first_tokens, int n_steps,
                            int* out_ids, float* device_ms) {
+    fa::NvtxRange nv("fa_generate");
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     if (!ctx->loaded) return set_err(ctx, FA_ERR_NOT_READY, "weights not loaded");
     if (n_seq <= 0 || n_seq > ctx->d.max_rows || !seq_ids || !first_tokens || n_steps <= 0)
@@ -1575,7 +1590,8 @@ static int op_gemm(const fa::GemmArgs& g, int variant, cudaStream_t s) {
             return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the few-row tcgen05 kernel");
     } else if (variant == 0 && gemv_rows(0, g.M) && fa::launch_q8_gemv(g, s)) {
         // taken by the CUDA-core kernel
-    } else if (variant == 0 && skinny_rows(0, g.M, g.epilogue) && fa::launch_q8_gemm_tc_skinny(g, nullptr, s)) {
+    } else if (variant == 0 && skinny_rows(0, g.M, g.epilogue, g.W8.q != nullptr) &&
+               fa::launch_q8_gemm_tc_skinny(g, nullptr, s)) {
         // taken by the few-row tcgen05 kernel
     } else {
         if (!fa::gemm_tc_supported(g)) return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the tcgen05 kernel");
@@ -1648,6 +1664,77 @@ extern "C" int fa_op_q8_gemm_argmax(const uint16_t* a16, const uint16_t* a16_lo,
     g.A = reinterpret_cast<const __half*>(a16); g.A_lo = reinterpret_cast<const __half*>(a16_lo);
     g.Wh = reinterpret_cast<const __half*>(w16);
     g.M = M; g.N = N; g.K = K; g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = logits;
+    g.amax_val = reinterpret_cast<float*>(scratch);
+    g.amax_idx = reinterpret_cast<int*>(g.amax_val + (size_t)M * (N / 64));
+    if (int rc = op_gemm(g, variant, (cudaStream_t)stream)) return rc;
+    fa::launch_argmax_reduce(g.amax_val, g.amax_idx, M, N / 64, next, nullptr, nullptr, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+// Q8_0 planes (the decoder's weight form): the same GEMMs reading q / d_t / d_r.
+extern "C" size_t fa_op_q8_planes_bytes(int N, int K) {
+    if (N <= 0 || K <= 0 || N % 4 || K % 64) return 0;
+    return fa::q8p_bytes(N, K);
+}
+
+extern "C" int fa_op_repack_q8_planes(const uint8_t* raw, int N, int K, void* planes, void* stream) {
+    if (!raw || !planes || N <= 0 || K <= 0 || N % 4 || K % 64)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "need N a multiple of 4 and K of 64");
+    if (reinterpret_cast<uintptr_t>(planes) & 255)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "planes must be 256-byte aligned");
+    fa::launch_repack_q8_planes(raw, N, K, 0, N, planes, (cudaStream_t)stream);
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+static int q8p_args(const void* a16, const void* planes, int M, int N, int K, fa::GemmArgs* g) {
+    if (!a16 || !planes || M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 64)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "need N, K multiples of 64");
+    if (reinterpret_cast<uintptr_t>(planes) & 255)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "planes must be 256-byte aligned");
+    *g = fa::GemmArgs{};
+    g->A = reinterpret_cast<const __half*>(a16);
+    g->W8 = fa::q8p_view(planes, N, K);
+    g->M = M; g->N = N; g->K = K;
+    return FA_OK;
+}
+
+extern "C" int fa_op_q8p_gemm(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const void* planes, int N,
+                              int n_split, float* c, int variant, void* stream) {
+    fa::GemmArgs g;
+    if (int rc = q8p_args(a16, planes, M, N, K, &g)) return rc;
+    if (!c || n_split <= 0 || (K / 64) % n_split)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "need an output and n_split dividing K/64");
+    if (int rc = ensure_configured()) return rc;
+    g.A_lo = reinterpret_cast<const __half*>(a16_lo);
+    g.n_split = n_split; g.epilogue = fa::kEpiStoreF32; g.C = c;
+    return op_gemm(g, variant, (cudaStream_t)stream);
+}
+
+extern "C" int fa_op_q8p_gemm_swiglu(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const void* planes,
+                                     int N, uint16_t* h16, uint16_t* h_lo, void* stream) {
+    fa::GemmArgs g;
+    if (int rc = q8p_args(a16, planes, M, N, K, &g)) return rc;
+    if (!h16) return set_err(nullptr, FA_ERR_INVALID_ARG, "h16 is NULL");
+    if (int rc = ensure_configured()) return rc;
+    g.A_lo = reinterpret_cast<const __half*>(a16_lo);
+    g.n_split = 1; g.epilogue = fa::kEpiSwiglu;
+    g.H = reinterpret_cast<__half*>(h16); g.H_lo = reinterpret_cast<__half*>(h_lo);
+    if (!fa::launch_q8_gemv(g, (cudaStream_t)stream))
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "shape outside the small-M kernel");
+    OP_CK(cudaGetLastError());
+    return FA_OK;
+}
+
+extern "C" int fa_op_q8p_gemm_argmax(const uint16_t* a16, const uint16_t* a16_lo, int M, int K, const void* planes,
+                                     int N, void* scratch, int* next, float* logits, int variant, void* stream) {
+    fa::GemmArgs g;
+    if (int rc = q8p_args(a16, planes, M, N, K, &g)) return rc;
+    if (!scratch || !next) return set_err(nullptr, FA_ERR_INVALID_ARG, "bad arguments");
+    if (int rc = ensure_configured()) return rc;
+    g.A_lo = reinterpret_cast<const __half*>(a16_lo);
+    g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = logits;
     g.amax_val = reinterpret_cast<float*>(scratch);
     g.amax_idx = reinterpret_cast<int*>(g.amax_val + (size_t)M * (N / 64));
     if (int rc = op_gemm(g, variant, (cudaStream_t)stream)) return rc;

@@ -10,6 +10,7 @@
 //   + residual
 // The GEMMs are the decoder's tcgen05 kernel (f16(d*q) weights, activations as an
 // f16 pair); encoder0's 560-wide input is zero-padded to 576 columns.
+#include "nvtx_range.hpp"
 #include "fa_kernels.cuh"
 #include "funasr_dec.h"
 
@@ -500,6 +501,7 @@ static void enqueue(fa_encoder* e, int T, int n_tiles, cudaStream_t s) {
 // (rows, tiles) is captured once as a CUDA graph and replayed.
 extern "C" int fa_encoder_forward_batch(fa_encoder* e, int n_utt, const int* frames, const float* lfr, float* embeds,
                                         void* stream) {
+    fa::NvtxRange nv("fa_encoder_forward_batch");
     if (!e || n_utt < 1 || !frames || !lfr || !embeds)
         return fail("fa_encoder_forward_batch: bad argument", FA_ERR_INVALID_ARG);
     if (!e->loaded) return fail("encoder weights not loaded", FA_ERR_NOT_READY);

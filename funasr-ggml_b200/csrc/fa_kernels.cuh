@@ -2,6 +2,7 @@
 #pragma once
 
 #include "fa_common.cuh"
+#include "q8_planes.cuh"
 
 #include <cuda.h>
 
@@ -147,7 +148,8 @@ enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1, kEpiSwiglu = 2 };
 struct GemmArgs {
     const __half* A;         // [M][K] f16 activations (hi part)
     const __half* A_lo;      // [M][K] f16 remainder x - hi, or nullptr (plain f16 activations)
-    const __half* Wh;        // [N][K] f16(d * q): Q8_0 weights rounded once to f16 at load time
+    const __half* Wh;        // [N][K] f16 weights (the encoder's f16(d * q)), read when W8.q is null
+    Q8Planes W8;             // Q8_0 weights as q / d_t / d_r planes (the decoder's): exact d * q
     int M, N, K;
     int n_split;             // split-K factor (grid.z); K/n_split multiple of 64
     int epilogue;
@@ -178,10 +180,11 @@ int gemm_tc_skinny_pick_split(int M, int N, int K, int n_sm);
 bool launch_q8_gemm_tc_skinny(const GemmArgs& g, int* err, cudaStream_t s);
 // CUDA-core small-M kernel (k_gemv.cu): M <= kGemvMaxRows, n_split 1, K a multiple of 256;
 // the store epilogue needs N a multiple of 4, the argmax epilogue N a multiple of 64 and
-// K <= 1024. The decoder uses it by default up to kGemvAutoRows rows.
+// K <= 1024 (f16 weights) or K <= 2048 (Q8_0 planes, K a multiple of 512) or K == 256. The
+// decoder uses it by default up to kGemvAutoRows rows.
 constexpr int kGemvMaxRows = 8;
 constexpr int kGemvAutoRows = 2;
-bool gemv_shape_supported(int M, int N, int K, int epilogue);
+bool gemv_shape_supported(int M, int N, int K, int epilogue, bool q8 = true);
 bool launch_q8_gemv(const GemmArgs& g, cudaStream_t s);   // false: shape or pointers not taken
 
 // ----------------------------------------------------------------- k_small.cu --

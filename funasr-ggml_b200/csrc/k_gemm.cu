@@ -5,12 +5,13 @@
 // :206 lm_head). At decode batch B the weight stream is read once per step for
 // all B rows, so the op is a skinny GEMM C[B][N] = A[B][K] . W[N][K]^T.
 //
-// Arithmetic (the oracle's GEMM mode 1, same as k_gemm_tc.cu): activations
-// arrive as an f16 pair (hi, lo) with hi + lo = x to ~22 bits, so the product is
-// a smooth function of them (a single f16 rounding of the activations makes the
-// decoder output jump by ~3e-4 relative under 1e-7 input noise, which no parity
-// tolerance survives); the weights are f16(d*q), rounded once at load time;
-// products are exact and accumulate in fp32.
+// Arithmetic (same as k_gemm_tc.cu): activations arrive as an f16 pair (hi, lo)
+// with hi + lo = x to ~22 bits, so the product is a smooth function of them (a
+// single f16 rounding of the activations makes the decoder output jump by ~3e-4
+// relative under 1e-7 input noise, which no parity tolerance survives). Weights
+// are the decoder's Q8_0 planes, each stage's q tile expanded into the exact f16
+// pair W_hi + W_lo = d*q (q8_planes.cuh; three MMAs per product: Wh.ah, Wh.al,
+// Wl.ah), or the encoder's f16 weights (two MMAs); products accumulate in fp32.
 //
 // This is the legacy-tensor-core (mma.sync m16n8k16) implementation, kept as the
 // cross-check of the tcgen05 kernel in k_gemm_tc.cu, which is the default.
@@ -43,7 +44,7 @@ struct Cfg {
     static constexpr int MT = WTM / 16;
     static constexpr int NT = WTN / 8;
     static constexpr int A_STAGE = BM * A_LD;        // halves
-    static constexpr int Q_STAGE = BN * B_LD * 2;    // bytes (f16 weight tile, padded rows)
+    static constexpr int Q_STAGE = 2 * BN * B_LD * 2;   // bytes (f16 weight tile hi, then lo; padded rows)
     static constexpr size_t SMEM = (size_t)STAGES * (2 * A_STAGE * 2 + Q_STAGE) + (size_t)BM * WN * 8;
     static_assert(WTM % 16 == 0 && WTN % 8 == 0, "warp tile");
     static_assert(NT % 2 == 0, "B fragments are loaded two n8 tiles at a time");
@@ -63,7 +64,7 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-template <int BM, int WM, int WN>
+template <int BM, int WM, int WN, bool Q8>
 __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const GemmArgs g) {
     using C = Cfg<BM, WM, WN>;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -99,7 +100,17 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
         __half* q_dst = reinterpret_cast<__half*>(Qs + st * C::Q_STAGE);
         for (int ch = tid; ch < BN * 8; ch += C::THREADS) {
             const int r = ch >> 3, cc = ch & 7;
-            cp_async16(q_dst + r * B_LD + cc * 8, g.Wh + (size_t)(n0 + r) * g.K + k0 + cc * 8, true);
+            if constexpr (Q8) {
+                // 8 int8 values of one block and its scale -> the exact f16 pair, stored directly
+                const uint2 qv = __ldg(reinterpret_cast<const uint2*>(g.W8.q + (size_t)(n0 + r) * g.K + k0 + cc * 8));
+                const __half dv = g.W8.d_r[(size_t)(n0 + r) * (g.K / kQK) + (k0 + cc * 8) / kQK];
+                uint4 h, l;
+                q8x8_to_hilo(qv.x, qv.y, __halves2half2(dv, dv), h, l);
+                *reinterpret_cast<uint4*>(q_dst + r * B_LD + cc * 8) = h;
+                *reinterpret_cast<uint4*>(q_dst + BN * B_LD + r * B_LD + cc * 8) = l;
+            } else {
+                cp_async16(q_dst + r * B_LD + cc * 8, g.Wh + (size_t)(n0 + r) * g.K + k0 + cc * 8, true);
+            }
         }
     };
 
@@ -140,9 +151,10 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
             }
 #pragma unroll
             for (int np = 0; np < C::NT / 2; ++np) {
-                uint32_t bf[4];
+                uint32_t bf[4], bl[4];
                 const int r = wn * C::WTN + np * 16 + (lane & 7) + ((lane >> 4) << 3);
                 ldmatrix_x4(bf, Bs + r * B_LD + kk * 16 + ((lane >> 3) & 1) * 8);
+                if constexpr (Q8) ldmatrix_x4(bl, Bs + BN * B_LD + r * B_LD + kk * 16 + ((lane >> 3) & 1) * 8);
 #pragma unroll
                 for (int mt = 0; mt < C::MT; ++mt) {
                     mma16816(acc[mt][2 * np], ah[mt], bf[0], bf[1]);
@@ -150,6 +162,10 @@ __global__ void __launch_bounds__(Cfg<BM, WM, WN>::THREADS) q8_gemm_kernel(const
                     if (has_lo) {
                         mma16816(acc[mt][2 * np], al[mt], bf[0], bf[1]);
                         mma16816(acc[mt][2 * np + 1], al[mt], bf[2], bf[3]);
+                    }
+                    if constexpr (Q8) {
+                        mma16816(acc[mt][2 * np], ah[mt], bl[0], bl[1]);
+                        mma16816(acc[mt][2 * np + 1], ah[mt], bl[2], bl[3]);
                     }
                 }
             }
@@ -226,12 +242,15 @@ template <int BM, int WM, int WN>
 void launch_cfg(const GemmArgs& g, cudaStream_t s) {
     using C = Cfg<BM, WM, WN>;
     dim3 grid(g.N / BN, (g.M + BM - 1) / BM, g.n_split);
-    launch_k(q8_gemm_kernel<BM, WM, WN>, grid, dim3(C::THREADS), C::SMEM, s, g);
+    if (g.W8.q) launch_k(q8_gemm_kernel<BM, WM, WN, true>, grid, dim3(C::THREADS), C::SMEM, s, g);
+    else launch_k(q8_gemm_kernel<BM, WM, WN, false>, grid, dim3(C::THREADS), C::SMEM, s, g);
 }
 
 template <int BM, int WM, int WN>
 void configure_cfg() {
-    cudaFuncSetAttribute(q8_gemm_kernel<BM, WM, WN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(q8_gemm_kernel<BM, WM, WN, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)Cfg<BM, WM, WN>::SMEM);
+    cudaFuncSetAttribute(q8_gemm_kernel<BM, WM, WN, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)Cfg<BM, WM, WN>::SMEM);
 }
 

@@ -4,23 +4,30 @@
 //     C^T[N][M] = W[N][K] . A[M][K]^T,   the MMA's M side = 128 weight rows,
 //                                        its N side = the activation rows (16 ... 128)
 //
-// Same arithmetic as k_gemm_tc.cu (f16(d*q) weights, the activation as an f16 hi/lo pair,
-// fp32 accumulation in TMEM) and the same outputs (fp32 split-K partials [split][M][N],
-// or per-64-column row maxima for the lm_head argmax). Why swap: with 128-row activation
+// Two weight forms. The decoder's: Q8_0 planes (q int8 [N][K], block scales d_t), exact
+// d*q expanded in shared memory into an f16 pair (W_hi + W_lo, q8_planes.cuh), so a
+// product is W_hi*a_hi + W_hi*a_lo + W_lo*a_hi (the dropped W_lo*a_lo is below 2^-22 of
+// it) and the kernel streams 34/32 B per weight from HBM. The encoder's: f16 weights
+// [N][K] (one rounding at load), W*a_hi + W*a_lo. Accumulation is fp32 in TMEM; outputs
+// are fp32 split-K partials [split][M][N] or per-64-column row maxima for the lm_head
+// argmax. Why swap: with 128-row activation
 // tiles a step of 16 rows still pays for a 128 x 128 fp32 accumulator per unit (64 KiB of
 // epilogue and partials) and for 64 KiB of activation copies per stage pair; here a unit's
 // accumulator is 128 x BNA (8-32 KiB up to 64 rows), a stage holds 16 KiB of weights and
 // BNA rows of activations, so six stages fit and each SM keeps ~96 KiB of weights in flight.
 //
-// Persistent, one CTA per SM, units = (128 weight rows, K chunk). 6 warps:
-//   warp 0      TMA producer: the weight tile (64 K x 128 rows) and the activation hi /
-//               lo tiles (64 K x BNA rows; rows past M read as zeros) per stage, 128 B
-//               swizzled; the first stages' weight copies go out before the wait on the
-//               previous kernel
+// Persistent, one CTA per SM, units = (128 weight rows, K chunk). 6 warps (10 for Q8_0):
+//   warp 0      TMA producer: the weight tile (64 K x 128 rows: f16 128 B swizzled, or
+//               the q tile 64 B x 128 rows and its 2 x 128 scales) and the activation hi /
+//               lo tiles (64 K x BNA rows; rows past M read as zeros) per stage; the first
+//               stages' weight copies go out before the wait on the previous kernel
 //   warp 1      TMEM (two BNA-column accumulators) and tcgen05.mma kind::f16, M=128,
-//               N=BNA, K=16, hi and lo into one accumulator
+//               N=BNA, K=16, every product of a stage into one accumulator
 //   warps 2..5  epilogue: TMEM lanes 32*(warp%4).. are weight rows, columns are
 //               activation rows; each warp writes 128 B runs of one activation row
+//   warps 6..9  (Q8_0) expand each stage's q tile, a weight row per thread, into the
+//               W_hi / W_lo pair in a TMEM slot (tcgen05.st) that the MMAs read as their
+//               A operand; the raw stage and the slot are released when those MMAs complete
 // Every mbarrier wait is bounded; a wait that gives up records an error and the CTA
 // drains its copies and MMAs before freeing TMEM.
 #include "fa_kernels.cuh"
@@ -34,23 +41,36 @@ namespace {
 
 constexpr int WM = 128;             // weight rows per unit
 constexpr int BK = 64;
-constexpr int THREADS = 64 + 128;
+constexpr int CONV_THREADS = 128;   // Q8_0: warps 6..9 expand q into the f16 pair
 
-// stages of the ring: 6 of 16 KiB weights + BNA-row activation pairs up to 64 rows (at
-// most 192 KiB), 4 at 128 rows (48 KiB each)
+template <bool Q8>
+__host__ __device__ constexpr int threads_for() {
+    return Q8 ? 64 + 128 + CONV_THREADS : 64 + 128;
+}
+
+// f16 weights: one ring, 6 stages of 16 KiB weights + BNA-row activation pairs up to 64
+// rows (at most 192 KiB), 4 at 128 rows (48 KiB each).
 template <int BNA>
 __host__ __device__ constexpr int stages_for() {
     return BNA <= 64 ? 6 : 4;
 }
+// Q8_0 weights: a shared-memory ring of raw stages (q 8 KiB + scales 512 B + activation
+// pair), about 200 KiB deep, and the expanded W_hi / W_lo tiles in tensor memory (the MMA's
+// A operand read from TMEM): 4 slots of 64 columns (32 for hi, 32 for lo: 128 rows x 64 K
+// f16, two per column) above the accumulators.
+template <int BNA>
+__host__ __device__ constexpr int raw_stages_q8() {
+    return BNA <= 16 ? 16 : BNA <= 32 ? 12 : BNA <= 64 ? 8 : 5;
+}
+constexpr int kConvSlots = 4;
+constexpr uint32_t kConvCol0 = 256;             // first TMEM column of the expanded slots
+constexpr uint32_t kConvSlotCols = 64;
 constexpr uint32_t W_BYTES = WM * BK * 2;
+constexpr uint32_t Q_BYTES = WM * BK;           // int8 q tile
+constexpr uint32_t D_BYTES = 2 * WM * 2;        // f16 scales of 2 blocks x 128 rows
 
-template <int BNA, int STAGES = stages_for<BNA>()>
-struct SkSmem {
-    __half w[STAGES][WM * BK];      // 16 KiB each; every operand buffer is a multiple of 1 KiB
-    __half a_hi[STAGES][BNA * BK];
-    __half a_lo[STAGES][BNA * BK];
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+template <int BNA>
+struct SkEpi {
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drain;
@@ -63,14 +83,78 @@ struct SkSmem {
     int consumed;
 };
 
+template <int BNA, bool Q8>
+struct SkSmem;
+
 template <int BNA>
+struct SkSmem<BNA, false> {
+    static constexpr int STAGES = stages_for<BNA>();
+    __half w[STAGES][WM * BK];      // 16 KiB each; every operand buffer is a multiple of 1 KiB
+    __half a_hi[STAGES][BNA * BK];
+    __half a_lo[STAGES][BNA * BK];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    SkEpi<BNA> e;
+};
+
+template <int BNA>
+struct SkSmem<BNA, true> {
+    static constexpr int STAGES = raw_stages_q8<BNA>();
+    static constexpr int CSTAGES = kConvSlots;
+    __half a_hi[STAGES][BNA * BK];
+    __half a_lo[STAGES][BNA * BK];
+    int8_t q[STAGES][WM * BK];      // 64 B rows, 64 B swizzle (conflict-free row reads)
+    __half d[STAGES][2 * WM];
+    uint64_t full[STAGES];          // raw stage landed (q, scales, activations)
+    uint64_t empty[STAGES];         // its MMAs are done: the producer may refill it
+    uint64_t cfull[CSTAGES];        // expanded slot written (128 converter arrivals)
+    uint64_t cempty[CSTAGES];       // its MMAs are done: the converters may overwrite it
+    SkEpi<BNA> e;
+};
+
+template <int BNA, bool Q8>
 __host__ __device__ constexpr uint32_t tmem_cols() {
-    return 2 * BNA < 32 ? 32u : (uint32_t)(2 * BNA);
+    return Q8 ? 512u : (2 * BNA < 32 ? 32u : (uint32_t)(2 * BNA));
+}
+
+// tcgen05.mma with the A operand (M = 128 rows, K = 16: 8 columns of f16 pairs) in TMEM.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// One row (TMEM lane) of a raw stage -> the f16 pair of its 64 weights in TMEM slot columns
+// [col, col + 32) (hi) and [col + 32, col + 64) (lo). The q row is read with the 64 B
+// swizzle its TMA box was written with: chunk c of row r sits at chunk c ^ ((r >> 1) & 3).
+__device__ __forceinline__ void q8_row_to_tmem(const int8_t* q, const __half* d, int r, uint32_t taddr) {
+    uint32_t hi[32], lo[32];
+    const unsigned char* row = reinterpret_cast<const unsigned char*>(q) + r * 64;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 v = lds128(row + ((c ^ ((r >> 1) & 3)) << 4));
+        const __half dv = d[(c >> 1) * WM + r];
+        const __half2 d2 = __halves2half2(dv, dv);
+        uint4 h0, l0, h1, l1;
+        q8x8_to_hilo(v.x, v.y, d2, h0, l0);
+        q8x8_to_hilo(v.z, v.w, d2, h1, l1);
+        hi[8 * c + 0] = h0.x; hi[8 * c + 1] = h0.y; hi[8 * c + 2] = h0.z; hi[8 * c + 3] = h0.w;
+        hi[8 * c + 4] = h1.x; hi[8 * c + 5] = h1.y; hi[8 * c + 6] = h1.z; hi[8 * c + 7] = h1.w;
+        lo[8 * c + 0] = l0.x; lo[8 * c + 1] = l0.y; lo[8 * c + 2] = l0.z; lo[8 * c + 3] = l0.w;
+        lo[8 * c + 4] = l1.x; lo[8 * c + 5] = l1.y; lo[8 * c + 6] = l1.z; lo[8 * c + 7] = l1.w;
+    }
+    TMEM_ST_X32(taddr, hi);
+    TMEM_ST_X32(taddr + 32, lo);
 }
 
 struct SkArgs {
     int M, N, K, n_split, epilogue, has_lo;
-    int n_units;
+    int n_wtiles;                   // N / 128 weight tiles
+    int n_units;                    // weight tiles x splits x activation tiles of BNA rows
     float* C;
     float* amax_val;
     int* amax_idx;
@@ -79,16 +163,54 @@ struct SkArgs {
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int BNA>
-__global__ void __launch_bounds__(THREADS, 1)
+// v[m] (m < 32): this lane's value (weight row n) for activation row m. Five butterfly rounds
+// halve the rows each lane keeps, taking the first maximum (larger value, then lower row)
+// of each pair; lane l ends with the maximum over the warp's 32 weight rows for activation
+// row l. NaN never wins (it enters as -inf with an index no row has).
+__device__ __forceinline__ void warp_argmax32_transpose(const uint32_t (&vb)[32], int n, int lane, float& out_v,
+                                                        int& out_i) {
+    float v[32];
+    int ix[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+        v[k] = __uint_as_float(vb[k]);
+        ix[k] = n;
+        if (!(v[k] > -INFINITY)) { v[k] = -INFINITY; ix[k] = 0x7fffffff; }
+    }
+#pragma unroll
+    for (int c = 16; c > 0; c >>= 1) {
+        const bool b = (lane & c) != 0;
+#pragma unroll
+        for (int k = 0; k < c; ++k) {
+            float keep = b ? v[k + c] : v[k];
+            int keep_i = b ? ix[k + c] : ix[k];
+            const float send = b ? v[k] : v[k + c];
+            const int send_i = b ? ix[k] : ix[k + c];
+            const float rv = __shfl_xor_sync(0xffffffffu, send, c);
+            const int ri = __shfl_xor_sync(0xffffffffu, send_i, c);
+            if (rv > keep || (rv == keep && ri < keep_i)) { keep = rv; keep_i = ri; }
+            v[k] = keep;
+            ix[k] = keep_i;
+        }
+    }
+    out_v = v[0];
+    out_i = ix[0];
+}
+
+// tm_w: the f16 weights [N][K] (128 B swizzle), or for Q8_0 the q plane [N][K] uint8;
+// tm_d: Q8_0 only, the d_t plane [K/32][N] f16 (2 x 128 boxes).
+template <int BNA, bool Q8, bool AM>
+__global__ void __launch_bounds__(threads_for<Q8>(), 1)
     q8_gemm_tc_skinny_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
-                             const __grid_constant__ CUtensorMap tm_w, const SkArgs g) {
+                             const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_d,
+                             const SkArgs g) {
     extern __shared__ unsigned char smem_raw[];
-    SkSmem<BNA>& S =
-        *reinterpret_cast<SkSmem<BNA>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    using Smem = SkSmem<BNA, Q8>;
+    Smem& S = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    SkEpi<BNA>& E = S.e;
     constexpr uint32_t kIdesc = idesc_f16(WM, BNA, false, false);
-    constexpr uint32_t TCOLS = tmem_cols<BNA>();
-    constexpr int STAGES = stages_for<BNA>();
+    constexpr uint32_t TCOLS = tmem_cols<BNA, Q8>();
+    constexpr int STAGES = Smem::STAGES;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int k_unit = g.K / g.n_split;
@@ -98,22 +220,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_prefetch_desc(&tm_a_hi);
         tma_prefetch_desc(&tm_a_lo);
         tma_prefetch_desc(&tm_w);
+        if constexpr (Q8) tma_prefetch_desc(&tm_d);
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&S.tfull[b], 1);
-            mbar_init(&S.tempty[b], 128);
+        if constexpr (Q8) {
+            for (int s = 0; s < Smem::CSTAGES; ++s) {
+                mbar_init(&S.cfull[s], CONV_THREADS);
+                mbar_init(&S.cempty[s], 1);
+            }
         }
-        mbar_init(&S.drain, 1);
-        S.err = 0;
-        S.issued = 0;
-        S.consumed = 0;
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&E.tfull[b], 1);
+            mbar_init(&E.tempty[b], 128);
+        }
+        mbar_init(&E.drain, 1);
+        E.err = 0;
+        E.issued = 0;
+        E.consumed = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem_base)),
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&E.tmem_base)),
                      "r"(TCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -121,35 +250,48 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = S.tmem_base;
+    const uint32_t tmem = E.tmem_base;
     pdl_trigger();
+
+    int my_units = 0;
+    for (int u = blockIdx.x; u < g.n_units; u += gridDim.x) ++my_units;
+    const int total = my_units * n_iters;
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t bytes = W_BYTES + (uint32_t)(BNA * BK * 2) * (g.has_lo ? 2u : 1u);
-            int my_units = 0;
-            for (int u = blockIdx.x; u < g.n_units; u += gridDim.x) ++my_units;
-            const int total = my_units * n_iters;
-            auto coords = [&](int it, int& k, int& n0) {
+            const uint32_t a_bytes = (uint32_t)(BNA * BK * 2) * (g.has_lo ? 2u : 1u);
+            const uint32_t bytes = (Q8 ? Q_BYTES + D_BYTES : W_BYTES) + a_bytes;
+            auto coords = [&](int it, int& k, int& n0, int& m0) {
                 const int u = blockIdx.x + (it / n_iters) * gridDim.x;
+                const int t = u / g.n_split;
                 k = (u % g.n_split) * k_unit + (it % n_iters) * BK;
-                n0 = (u / g.n_split) * WM;
+                n0 = (t % g.n_wtiles) * WM;
+                m0 = (t / g.n_wtiles) * BNA;
+            };
+            auto load_w = [&](int it, int s) {
+                int k, n0, m0;
+                coords(it, k, n0, m0);
+                if constexpr (Q8) {
+                    tma_load_2d(S.q[s], &tm_w, k, n0, &S.full[s]);
+                    tma_load_2d(S.d[s], &tm_d, n0, k / kQK, &S.full[s]);
+                } else {
+                    tma_load_2d(S.w[s], &tm_w, k, n0, &S.full[s]);
+                }
+            };
+            auto load_a = [&](int it, int s) {
+                int k, n0, m0;
+                coords(it, k, n0, m0);
+                tma_load_2d(S.a_hi[s], &tm_a_hi, k, m0, &S.full[s]);
+                if (g.has_lo) tma_load_2d(S.a_lo[s], &tm_a_lo, k, m0, &S.full[s]);
             };
             const int pre = total < STAGES ? total : STAGES;
             for (int it = 0; it < pre; ++it) {
-                int k, n0;
-                coords(it, k, n0);
                 mbar_arrive_expect_tx(&S.full[it], bytes);
-                tma_load_2d(S.w[it], &tm_w, k, n0, &S.full[it]);
+                load_w(it, it);
             }
             pdl_wait();
-            for (int it = 0; it < pre; ++it) {
-                int k, n0;
-                coords(it, k, n0);
-                tma_load_2d(S.a_hi[it], &tm_a_hi, k, 0, &S.full[it]);
-                if (g.has_lo) tma_load_2d(S.a_lo[it], &tm_a_lo, k, 0, &S.full[it]);
-            }
-            S.issued = pre;
+            for (int it = 0; it < pre; ++it) load_a(it, it);
+            E.issued = pre;
             bool ok = true;
             for (int it = pre; it < total; ++it) {
                 const int s = it % STAGES;
@@ -157,15 +299,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     ok = false;
                     break;
                 }
-                int k, n0;
-                coords(it, k, n0);
                 mbar_arrive_expect_tx(&S.full[s], bytes);
-                tma_load_2d(S.w[s], &tm_w, k, n0, &S.full[s]);
-                tma_load_2d(S.a_hi[s], &tm_a_hi, k, 0, &S.full[s]);
-                if (g.has_lo) tma_load_2d(S.a_lo[s], &tm_a_lo, k, 0, &S.full[s]);
-                S.issued = it + 1;
+                load_w(it, s);
+                load_a(it, s);
+                E.issued = it + 1;
             }
-            if (!ok) S.err = 1;
+            if (!ok) E.err = 1;
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -174,7 +313,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             int it = 0, j = 0;
             for (int u = blockIdx.x; u < g.n_units && ok; u += gridDim.x, ++j) {
                 const int buf = j & 1;
-                if (j >= 2 && !mbar_wait_bounded(&S.tempty[buf], (uint32_t)((j >> 1) - 1) & 1u)) {
+                if (j >= 2 && !mbar_wait_bounded(&E.tempty[buf], (uint32_t)((j >> 1) - 1) & 1u)) {
                     ok = false;
                     break;
                 }
@@ -183,43 +322,93 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int i = 0; i < n_iters; ++i, ++it) {
                     const int s = it % STAGES;
                     if (!mbar_wait_bounded(&S.full[s], (uint32_t)(it / STAGES) & 1u)) { ok = false; break; }
-                    S.consumed = it + 1;
-                    tc_fence_after();
+                    if constexpr (Q8) {
+                        const int cs = it % Smem::CSTAGES;
+                        if (!mbar_wait_bounded(&S.cfull[cs], (uint32_t)(it / Smem::CSTAGES) & 1u)) {
+                            ok = false;
+                            break;
+                        }
+                        E.consumed = it + 1;
+                        tc_fence_after();
+                        const uint32_t w_hi = tmem + kConvCol0 + (uint32_t)cs * kConvSlotCols;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint32_t koff = (uint32_t)(kk * 32) >> 4;   // bytes / 16
-                        const uint64_t dw = smem_desc_k128(S.w[s]) + koff;
-                        tc_mma_f16(d_tmem, dw, smem_desc_k128(S.a_hi[s]) + koff, kIdesc, (i > 0 || kk > 0) ? 1u : 0u);
-                        if (g.has_lo) tc_mma_f16(d_tmem, dw, smem_desc_k128(S.a_lo[s]) + koff, kIdesc, 1u);
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint32_t koff = (uint32_t)(kk * 32) >> 4;   // bytes / 16
+                            const uint32_t wh = w_hi + (uint32_t)(kk * 8);    // 8 columns per K16
+                            const uint64_t dah = smem_desc_k128(S.a_hi[s]) + koff;
+                            tc_mma_f16_ts(d_tmem, wh, dah, kIdesc, (i > 0 || kk > 0) ? 1u : 0u);
+                            if (g.has_lo) tc_mma_f16_ts(d_tmem, wh, smem_desc_k128(S.a_lo[s]) + koff, kIdesc, 1u);
+                            tc_mma_f16_ts(d_tmem, wh + 32, dah, kIdesc, 1u);
+                        }
+                        tc_commit(&S.empty[s]);
+                        tc_commit(&S.cempty[cs]);
+                    } else {
+                        E.consumed = it + 1;
+                        tc_fence_after();
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint32_t koff = (uint32_t)(kk * 32) >> 4;   // bytes / 16
+                            const uint64_t dw = smem_desc_k128(S.w[s]) + koff;
+                            tc_mma_f16(d_tmem, dw, smem_desc_k128(S.a_hi[s]) + koff, kIdesc,
+                                       (i > 0 || kk > 0) ? 1u : 0u);
+                            if (g.has_lo) tc_mma_f16(d_tmem, dw, smem_desc_k128(S.a_lo[s]) + koff, kIdesc, 1u);
+                        }
+                        tc_commit(&S.empty[s]);
                     }
-                    tc_commit(&S.empty[s]);
                 }
                 if (!ok) break;
-                tc_commit(&S.tfull[buf]);
+                tc_commit(&E.tfull[buf]);
             }
-            if (!ok) S.err = 1;
-            tc_commit(&S.drain);
-            if (!mbar_wait_bounded(&S.drain, 0)) S.err = 1;
+            if (!ok) E.err = 1;
+            tc_commit(&E.drain);
+            if (!mbar_wait_bounded(&E.drain, 0)) E.err = 1;
         }
         __syncwarp();
+    } else if (warp >= 6) {
+        if constexpr (Q8) {
+            // converters: raw stage it (q, scales) -> TMEM slot it % CSTAGES; a warp may only
+            // reach its own quarter of the lanes, so thread (warp w, lane l) expands weight
+            // row 32 * (w % 4) + l
+            const int r = 32 * (warp & 3) + lane;
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+            for (int it = 0; it < total; ++it) {
+                const int s = it % STAGES;
+                const int cs = it % Smem::CSTAGES;
+                bool got = mbar_wait_bounded(&S.full[s], (uint32_t)(it / STAGES) & 1u);
+                if (got && it >= Smem::CSTAGES)
+                    got = mbar_wait_bounded(&S.cempty[cs], (uint32_t)((it / Smem::CSTAGES) - 1) & 1u);
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0) E.err = 1;
+                    break;
+                }
+                tc_fence_after();
+                q8_row_to_tmem(S.q[s], S.d[s], r, lane_base + kConvCol0 + (uint32_t)cs * kConvSlotCols);
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&S.cfull[cs]);
+            }
+        }
     } else {
         const int q = warp & 3;                 // TMEM lanes 32q..32q+31: weight rows of this warp
         int j = 0;
         for (int u = blockIdx.x; u < g.n_units; u += gridDim.x, ++j) {
             const int split = u % g.n_split;
-            const int n0 = (u / g.n_split) * WM;
+            const int t = u / g.n_split;
+            const int n0 = (t % g.n_wtiles) * WM;
+            const int m0 = (t / g.n_wtiles) * BNA;
+            const int rows = min(BNA, g.M - m0);  // activation rows of this unit
             const int buf = j & 1;
-            const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&S.tfull[buf], (uint32_t)(j >> 1) & 1u));
-            if (g.epilogue == kEpiArgmax) {
+            const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&E.tfull[buf], (uint32_t)(j >> 1) & 1u));
+            if (AM) {
                 // the four warps meet at named barriers below: they leave together or not at all
-                if (lane == 0) S.got[q] = got ? 1 : 0;
+                if (lane == 0) E.got[q] = got ? 1 : 0;
                 epi_bar();
-                if (!(S.got[0] & S.got[1] & S.got[2] & S.got[3])) {
-                    if (lane == 0) S.err = 1;
+                if (!(E.got[0] & E.got[1] & E.got[2] & E.got[3])) {
+                    if (lane == 0) E.err = 1;
                     break;
                 }
             } else if (!got) {
-                if (lane == 0) S.err = 1;
+                if (lane == 0) E.err = 1;
                 break;
             }
             tc_fence_after();
@@ -227,55 +416,65 @@ __global__ void __launch_bounds__(THREADS, 1)
             constexpr int CH = BNA < 32 ? BNA : 32;
             const int n = n0 + q * 32 + lane;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BNA);
-            float* out = g.C ? g.C + (g.epilogue == kEpiStoreF32 ? (size_t)split * g.M * g.N : 0) + n : nullptr;
+            float* out = g.C ? g.C + (AM ? 0 : (size_t)split * g.M * g.N) +
+                                   (size_t)m0 * g.N + n
+                             : nullptr;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BNA && c0 < g.M; c0 += CH) {
-                uint32_t v[CH];
+            for (int c0 = 0; c0 < BNA && c0 < rows; c0 += CH) {
+                uint32_t cur[CH];
                 if constexpr (CH == 16) {
-                    TMEM_LD_X16(tbase + c0, v);
+                    TMEM_LD_X16(tbase + c0, cur);
                 } else {
-                    TMEM_LD_X32(tbase + c0, v);
+                    TMEM_LD_X32(tbase + c0, cur);
                 }
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                tmem_wait_ld();
                 if (out) {
 #pragma unroll
                     for (int m = 0; m < CH; ++m)
-                        if (c0 + m < g.M) out[(size_t)(c0 + m) * g.N] = __uint_as_float(v[m]);
+                        if (c0 + m < rows) out[(size_t)(c0 + m) * g.N] = __uint_as_float(cur[m]);
                 }
-                if (g.epilogue == kEpiArgmax) {
-                    // per activation row: first maximum over this warp's 32 weight rows; NaN never wins
+                if constexpr (AM) {
+                    if constexpr (CH == 32) {
+                        // first maximum over this warp's 32 weight rows for all 32 activation
+                        // rows at once: lane l ends with activation row c0 + l
+                        float bv;
+                        int bi;
+                        warp_argmax32_transpose(cur, n, lane, bv, bi);
+                        if (c0 + lane < rows) { E.amax_v[q][c0 + lane] = bv; E.amax_i[q][c0 + lane] = bi; }
+                    } else {
 #pragma unroll
-                    for (int m = 0; m < CH; ++m) {
-                        if (c0 + m >= g.M) break;
-                        float bv = __uint_as_float(v[m]);
-                        int bi = n;
-                        if (!(bv > -INFINITY)) { bv = -INFINITY; bi = 0x7fffffff; }
+                        for (int m = 0; m < CH; ++m) {
+                            if (c0 + m >= rows) break;
+                            float bv = __uint_as_float(cur[m]);
+                            int bi = n;
+                            if (!(bv > -INFINITY)) { bv = -INFINITY; bi = 0x7fffffff; }
 #pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) {
-                            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                            for (int o = 16; o > 0; o >>= 1) {
+                                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                            }
+                            if (lane == 0) { E.amax_v[q][c0 + m] = bv; E.amax_i[q][c0 + m] = bi; }
                         }
-                        if (lane == 0) { S.amax_v[q][c0 + m] = bv; S.amax_i[q][c0 + m] = bi; }
                     }
                 }
             }
             tc_fence_before();
-            mbar_arrive(&S.tempty[buf]);
-            if (g.epilogue == kEpiArgmax) {
+            mbar_arrive(&E.tempty[buf]);
+            if (AM) {
                 // then over the two warps of each 64-row half
                 epi_bar();
-                for (int t = threadIdx.x - 64; t < 2 * BNA; t += 128) {
-                    const int h = t / BNA, m = t % BNA;
-                    if (m < g.M) {
-                        float bv = S.amax_v[2 * h][m];
-                        int bi = S.amax_i[2 * h][m];
-                        const float ov = S.amax_v[2 * h + 1][m];
-                        const int oi = S.amax_i[2 * h + 1][m];
+                for (int tt = threadIdx.x - 64; tt < 2 * BNA; tt += 128) {
+                    const int h = tt / BNA, m = tt % BNA;
+                    if (m < rows) {
+                        float bv = E.amax_v[2 * h][m];
+                        int bi = E.amax_i[2 * h][m];
+                        const float ov = E.amax_v[2 * h + 1][m];
+                        const int oi = E.amax_i[2 * h + 1][m];
                         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
                         const int n_tiles = g.N / 64;
-                        g.amax_val[(size_t)m * n_tiles + n0 / 64 + h] = bv;
-                        g.amax_idx[(size_t)m * n_tiles + n0 / 64 + h] = bi;
+                        g.amax_val[(size_t)(m0 + m) * n_tiles + n0 / 64 + h] = bv;
+                        g.amax_idx[(size_t)(m0 + m) * n_tiles + n0 / 64 + h] = bi;
                     }
                 }
                 epi_bar();
@@ -283,10 +482,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     }
     __syncthreads();
-    if (S.err) {
+    if (E.err) {
         if (threadIdx.x == 0) {
             record_error(g.err, kDevErrTimeout);
-            for (int it = S.consumed; it < S.issued; ++it)
+            for (int it = E.consumed; it < E.issued; ++it)
                 (void)mbar_wait_bounded(&S.full[it % STAGES], (uint32_t)(it / STAGES) & 1u);
         }
         __syncthreads();
@@ -297,41 +496,73 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-template <int BNA>
+template <int BNA, bool Q8>
 size_t skinny_smem() {
-    return sizeof(SkSmem<BNA>) + 1024;
+    return sizeof(SkSmem<BNA, Q8>) + 1024;
 }
 
-template <int BNA>
+template <int BNA, bool Q8>
 bool launch_bna(const GemmArgs& g, int* err, cudaStream_t s, int n_sm) {
-    CUtensorMap ta, tl, tw;
+    CUtensorMap ta, tl, tw, td;
     if (!make_map(&ta, g.A, g.K, g.M, BK, BNA, true)) return false;
     if (!make_map(&tl, g.A_lo ? g.A_lo : g.A, g.K, g.M, BK, BNA, true)) return false;
-    if (!make_map(&tw, g.Wh, g.K, g.N, BK, WM, true)) return false;
+    if constexpr (Q8) {
+        if (!make_map_u8(&tw, g.W8.q, g.K, g.N, BK, WM, true)) return false;
+        if (!make_map(&td, g.W8.d_t, g.N, g.K / kQK, WM, 2, false)) return false;
+    } else {
+        if (!make_map(&tw, g.Wh, g.K, g.N, BK, WM, true)) return false;
+        td = tw;
+    }
     SkArgs a{};
     a.M = g.M; a.N = g.N; a.K = g.K; a.n_split = g.n_split; a.epilogue = g.epilogue; a.has_lo = g.A_lo != nullptr;
-    a.n_units = (g.N / WM) * g.n_split;
+    a.n_wtiles = g.N / WM;
+    a.n_units = a.n_wtiles * g.n_split * ((g.M + BNA - 1) / BNA);
     a.C = g.C; a.amax_val = g.amax_val; a.amax_idx = g.amax_idx; a.err = err;
     const int grid = a.n_units < n_sm ? a.n_units : n_sm;
-    launch_k(q8_gemm_tc_skinny_kernel<BNA>, dim3(grid), dim3(THREADS), skinny_smem<BNA>(), s, ta, tl, tw, a);
+    if (g.epilogue == kEpiArgmax)
+        launch_k(q8_gemm_tc_skinny_kernel<BNA, Q8, true>, dim3(grid), dim3(threads_for<Q8>()), skinny_smem<BNA, Q8>(),
+                 s, ta, tl, tw, td, a);
+    else
+        launch_k(q8_gemm_tc_skinny_kernel<BNA, Q8, false>, dim3(grid), dim3(threads_for<Q8>()), skinny_smem<BNA, Q8>(),
+                 s, ta, tl, tw, td, a);
     return true;
+}
+
+template <bool Q8>
+bool launch_rows(const GemmArgs& g, int* err, cudaStream_t s, int sms) {
+    if (g.M <= 16) return launch_bna<16, Q8>(g, err, s, sms);
+    if (g.M <= 32) return launch_bna<32, Q8>(g, err, s, sms);
+    if (g.M <= 64) return launch_bna<64, Q8>(g, err, s, sms);
+    return launch_bna<128, Q8>(g, err, s, sms);
+}
+
+template <int BNA, bool Q8>
+void set_smem_attr() {
+    static_assert(sizeof(SkSmem<BNA, Q8>) + 1024 <= 232448, "shared memory per CTA");
+    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)skinny_smem<BNA, Q8>());
+    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)skinny_smem<BNA, Q8>());
 }
 
 }  // namespace
 
 void configure_gemm_tc_skinny() {
-    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)skinny_smem<16>());
-    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)skinny_smem<32>());
-    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)skinny_smem<64>());
-    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)skinny_smem<128>());
+    set_smem_attr<16, false>();
+    set_smem_attr<32, false>();
+    set_smem_attr<64, false>();
+    set_smem_attr<128, false>();
+    set_smem_attr<16, true>();
+    set_smem_attr<32, true>();
+    set_smem_attr<64, true>();
+    set_smem_attr<128, true>();
 }
 
 bool gemm_tc_skinny_supported(const GemmArgs& g) {
-    return g.Wh != nullptr && g.A != nullptr && g.M >= 1 && g.M <= kSkinnyMaxRows && g.N % WM == 0 &&
+    const bool w_ok = g.W8.q ? (g.W8.d_t != nullptr) : (g.Wh != nullptr);
+    // f16 weights: one activation tile of up to 128 rows; Q8_0 planes: any number of
+    // 128-row activation tiles (the units then cover every (weight tile, activation tile))
+    return w_ok && g.A != nullptr && g.M >= 1 && (g.W8.q || g.M <= kSkinnyMaxRows) && g.N % WM == 0 &&
            g.K % BK == 0 && g.n_split > 0 && (g.K / g.n_split) % BK == 0 &&
            (g.epilogue == kEpiStoreF32 ? g.C != nullptr
                                        : g.epilogue == kEpiArgmax && g.n_split == 1 && g.amax_val && g.amax_idx) &&
@@ -339,10 +570,14 @@ bool gemm_tc_skinny_supported(const GemmArgs& g) {
 }
 
 // Split-K factor: the divisor S of K/64 (K/S >= 128) minimising rounds * (32-wide K blocks
-// per unit + 2 fill + 2 epilogue), rounds = ceil(units / SMs), units = N/128 * S.
+// per unit + 2 fill + epilogue), rounds = ceil(units / SMs), units = N/128 * S * activation
+// tiles. The epilogue counts 2 blocks for one activation tile (a decode step) and 8 when
+// there are several (a prefill forward), where split partials of full tiles cost more than
+// the waves they save.
 int gemm_tc_skinny_pick_split(int M, int N, int K, int n_sm) {
-    (void)M;
-    const int tiles = N / WM;
+    const int m_tiles = (M + kSkinnyMaxRows - 1) / kSkinnyMaxRows;
+    const int tiles = N / WM * m_tiles;
+    const int epi = m_tiles > 1 ? 8 : 2;
     const int kb = K / BK;
     int best = 1;
     long best_cost = -1;
@@ -350,7 +585,7 @@ int gemm_tc_skinny_pick_split(int M, int N, int K, int n_sm) {
         if (kb % sp || (sp > 1 && K / sp < 128)) continue;
         const long units = (long)tiles * sp;
         const long rounds = (units + n_sm - 1) / n_sm;
-        const long cost = rounds * (K / sp / kQK + 2 + 2);
+        const long cost = rounds * (K / sp / kQK + 2 + epi);
         if (best_cost < 0 || cost < best_cost) { best = sp; best_cost = cost; }
     }
     return best;
@@ -363,10 +598,7 @@ bool launch_q8_gemm_tc_skinny(const GemmArgs& g, int* err, cudaStream_t s) {
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && n_sm[dev] == 0) cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev);
     const int sms = (dev >= 0 && dev < 64 && n_sm[dev] > 0) ? n_sm[dev] : 148;
-    if (g.M <= 16) return launch_bna<16>(g, err, s, sms);
-    if (g.M <= 32) return launch_bna<32>(g, err, s, sms);
-    if (g.M <= 64) return launch_bna<64>(g, err, s, sms);
-    return launch_bna<128>(g, err, s, sms);
+    return g.W8.q ? launch_rows<true>(g, err, s, sms) : launch_rows<false>(g, err, s, sms);
 }
 
 }  // namespace fa

@@ -1,6 +1,12 @@
 // Kernel (4), small-M form: the Q8_0 GEMM of a decode step with at most 8 rows, on the
 // CUDA cores. C[m][n] = sum_k x[m][k] * W[n][k], x = hi + lo (the activation pair the
-// tcgen05 kernel reads; their f32 sum is exact), W = f16(d * q) [N][K] row-major.
+// tcgen05 kernel reads; their f32 sum is exact).
+//
+// Weights: the decoder's Q8_0 planes (q int8 [N][K] and the row-major scales d_r
+// [N][K/32], q8_planes.cuh): a lane loads 16 (or 8) int8 values of a row, all in one Q8_0
+// block, and accumulates sum_k q*x of them in fp32 before one multiply by the block's d,
+// so every weight is the exact d * q and the kernel streams 34/32 B per weight. The
+// encoder's f16 weights [N][K] take the same structure with 8 f16 per lane.
 //
 // Same role as the tcgen05 kernel (compute/llm_ops_gpu.cpp:53-55,149,177-180,206: every
 // ggml_mul_mat of the decoder), same epilogues: fp32 results [M][N] (one "partial"), or
@@ -9,28 +15,31 @@
 // 177-180, ggml_silu(gate) * up), which saves the separate SwiGLU launch.
 //
 // Why a second kernel: with one token per sequence and few sequences the product is a
-// matrix-vector product. Its floor is the weight read, 2 B per weight (4-13 MB per layer
-// GEMM, under 2 us at HBM rate), and the tcgen05 kernel's fixed costs (TMEM allocation,
-// barrier set-up, a 128-row tile pipeline, a split-K partial round trip) dominate it.
-// Here a warp owns a block of 4 weight rows x (K / ks) columns: it issues all of its
-// 16 B weight loads before waiting on the previous kernel (the weights do not depend on
-// it), then reads the activations, accumulates 4 x M dot products in fp32, reduces them
-// over its lanes, and ks warps of one row block add their sums in a fixed order, so
-// results do not depend on timing.
+// matrix-vector product. Its floor is the weight read (2-7 MB of Q8_0 per layer GEMM,
+// about a microsecond at HBM rate), and the tcgen05 kernel's fixed costs (TMEM
+// allocation, barrier set-up, a 128-row tile pipeline, a split-K partial round trip)
+// dominate it. Here a warp owns a block of 4 weight rows x (K / ks) columns: it issues
+// all of its weight loads before waiting on the previous kernel (the weights do not
+// depend on it), then reads the activations, accumulates 4 x M dot products in fp32,
+// reduces them over its lanes, and ks warps of one row block add their sums in a fixed
+// order, so results do not depend on timing.
 #include "fa_kernels.cuh"
+
+#include <type_traits>
 
 namespace fa {
 
 namespace {
 
 constexpr int kRowsPerWarp = 4;
-constexpr int kSlice = 256;          // K columns one warp-wide 16 B load covers
 constexpr int kMaxWarps = 16;
 
 struct GemvArgs {
     const __half* A;
     const __half* A_lo;
-    const __half* W;
+    const __half* W;                 // f16 weights, or nullptr
+    const int8_t* Wq;                // Q8_0 planes: q [N][K] and d_r [N][K/32]
+    const __half* Wd;
     int M, N, K;
     int ks;                          // warps sharing one row block's K range
     int G;                           // row blocks per CTA
@@ -52,9 +61,18 @@ __device__ __forceinline__ void h8_to_f32(const uint4& u, float* f) {
     }
 }
 
+// Weights per lane per slice: WPL = 8 (f16: one 16 B load; Q8_0: 8 B) or 16 (Q8_0: 16 B).
+// A slice is the 32 * WPL columns one warp-wide load covers.
+template <bool Q8, int WPL>
+struct WLoad {
+    using T = typename std::conditional<(!Q8 || WPL == 16), uint4, uint2>::type;
+};
+
 // MM: rows of activations the registers hold (>= a.M); NS: K slices per warp
-template <int MM, int NS>
+template <int MM, int NS, bool Q8, int WPL>
 __global__ void __launch_bounds__(kMaxWarps * 32) gemv_kernel(const GemvArgs a) {
+    using WT = typename WLoad<Q8, WPL>::T;
+    constexpr int kSlice = 32 * WPL;
     __shared__ float red[kMaxWarps * kRowsPerWarp * MM];
     pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -65,14 +83,23 @@ __global__ void __launch_bounds__(kMaxWarps * 32) gemv_kernel(const GemvArgs a) 
     const int n0 = !swiglu ? blockIdx.x * (a.G * kRowsPerWarp) + g * kRowsPerWarp
                  : g < half_g ? (blockIdx.x * half_g + g) * kRowsPerWarp
                               : a.N / 2 + (blockIdx.x * half_g + g - half_g) * kRowsPerWarp;
-    const int k0 = c * (NS * kSlice) + lane * 8;
+    const int k0 = c * (NS * kSlice) + lane * WPL;
 
-    uint4 w[NS][kRowsPerWarp];
+    WT w[NS][kRowsPerWarp];
+    float dsc[NS][kRowsPerWarp];
 #pragma unroll
     for (int s = 0; s < NS; ++s)
 #pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r)
-            w[s][r] = __ldg(reinterpret_cast<const uint4*>(a.W + (size_t)(n0 + r) * a.K + k0 + s * kSlice));
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            const size_t e = (size_t)(n0 + r) * a.K + k0 + s * kSlice;
+            if constexpr (Q8) {
+                w[s][r] = __ldg(reinterpret_cast<const WT*>(a.Wq + e));
+                dsc[s][r] = __half2float(a.Wd[(size_t)(n0 + r) * (a.K / kQK) + (k0 + s * kSlice) / kQK]);
+            } else {
+                w[s][r] = __ldg(reinterpret_cast<const WT*>(a.W + e));
+                dsc[s][r] = 1.0f;
+            }
+        }
     pdl_wait();
 
     float acc[kRowsPerWarp][MM];
@@ -80,26 +107,50 @@ __global__ void __launch_bounds__(kMaxWarps * 32) gemv_kernel(const GemvArgs a) 
     for (int r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll
         for (int m = 0; m < MM; ++m) acc[r][m] = 0.0f;
+    constexpr int XV = Q8 ? WPL : 8;     // activation values per lane per slice
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
-        float wf[kRowsPerWarp][8];
+        float wf[kRowsPerWarp][XV];
 #pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) h8_to_f32(w[s][r], wf[r]);
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+            if constexpr (Q8) {
+                // int8 -> f32 exactly without the (quarter-rate) integer conversion: the byte
+                // q + 128 under the exponent of 2^23 reads as 2^23 + q + 128
+                const uint32_t* wb = reinterpret_cast<const uint32_t*>(&w[s][r]);
+#pragma unroll
+                for (int j4 = 0; j4 < XV / 4; ++j4) {
+                    const uint32_t u = wb[j4] ^ 0x80808080u;
+#pragma unroll
+                    for (int b = 0; b < 4; ++b)
+                        wf[r][4 * j4 + b] =
+                            __int_as_float((int)__byte_perm(u, 0x4B000000u, 0x7540u + (unsigned)b)) - 8388736.0f;
+                }
+            } else {
+                h8_to_f32(w[s][r], wf[r]);
+            }
+        }
 #pragma unroll
         for (int m = 0; m < MM; ++m) {
             if (m < a.M) {
                 const size_t off = (size_t)m * a.K + k0 + s * kSlice;
-                float x[8], xl[8];
-                h8_to_f32(*reinterpret_cast<const uint4*>(a.A + off), x);
-                if (a.A_lo) {
-                    h8_to_f32(*reinterpret_cast<const uint4*>(a.A_lo + off), xl);
+                float x[XV];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) x[j] += xl[j];
+                for (int h = 0; h < XV / 8; ++h) {
+                    h8_to_f32(*reinterpret_cast<const uint4*>(a.A + off + 8 * h), x + 8 * h);
+                    if (a.A_lo) {
+                        float xl[8];
+                        h8_to_f32(*reinterpret_cast<const uint4*>(a.A_lo + off + 8 * h), xl);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) x[8 * h + j] += xl[j];
+                    }
                 }
 #pragma unroll
-                for (int r = 0; r < kRowsPerWarp; ++r)
+                for (int r = 0; r < kRowsPerWarp; ++r) {
+                    float sq = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[r][m] = fmaf(wf[r][j], x[j], acc[r][m]);
+                    for (int j = 0; j < XV; ++j) sq = fmaf(wf[r][j], x[j], sq);
+                    acc[r][m] = Q8 ? fmaf(dsc[s][r], sq, acc[r][m]) : acc[r][m] + sq;
+                }
             }
         }
     }
@@ -166,21 +217,33 @@ __global__ void __launch_bounds__(kMaxWarps * 32) gemv_kernel(const GemvArgs a) 
     }
 }
 
-template <int MM>
+template <int MM, bool Q8, int WPL>
 void launch_mm(const GemvArgs& a, int ns, cudaStream_t s) {
     const dim3 grid(a.N / (a.G * kRowsPerWarp)), block(a.ks * a.G * 32);   // SwiGLU: N / 2 over G / 2 blocks
-    if (ns == 1) launch_k(gemv_kernel<MM, 1>, grid, block, 0, s, a);
-    else if (ns == 2) launch_k(gemv_kernel<MM, 2>, grid, block, 0, s, a);
-    else launch_k(gemv_kernel<MM, 4>, grid, block, 0, s, a);
+    if (ns == 1) launch_k(gemv_kernel<MM, 1, Q8, WPL>, grid, block, 0, s, a);
+    else if (ns == 2) launch_k(gemv_kernel<MM, 2, Q8, WPL>, grid, block, 0, s, a);
+    else launch_k(gemv_kernel<MM, 4, Q8, WPL>, grid, block, 0, s, a);
+}
+
+template <bool Q8, int WPL>
+void launch_form(const GemvArgs& a, int ns, cudaStream_t s) {
+    if (a.M == 1) launch_mm<1, Q8, WPL>(a, ns, s);
+    else if (a.M == 2) launch_mm<2, Q8, WPL>(a, ns, s);
+    else if (a.M <= 4) launch_mm<4, Q8, WPL>(a, ns, s);
+    else launch_mm<8, Q8, WPL>(a, ns, s);
 }
 
 }  // namespace
 
+// Weights per lane per slice: 8 f16, or 16 int8 of Q8_0 when K allows (8 otherwise).
+static int wpl_for(bool q8, int K) { return q8 && K % 512 == 0 ? 16 : 8; }
+
 // Chooses (ks, G, slices per warp) for a shape, or returns false when the kernel does not
 // take it. Store epilogue: the fewest warps per row block that still give >= 4096 warps
-// (enough 16 B loads in flight to cover HBM latency), else the most the shape allows.
+// (enough loads in flight to cover HBM latency), else the most the shape allows.
 // Argmax epilogue: 64 rows per CTA (16 row blocks) and one warp per row block.
-static bool shape_config(int M, int N, int K, int epilogue, int* ks_out, int* G_out, int* ns_out) {
+static bool shape_config(int M, int N, int K, int epilogue, bool q8, int* ks_out, int* G_out, int* ns_out) {
+    const int kSlice = 32 * wpl_for(q8, K);
     if (M < 1 || M > kGemvMaxRows || N <= 0 || K <= 0 || K % kSlice) return false;
     const int n_sl = K / kSlice;
     if (epilogue == kEpiArgmax) {
@@ -221,28 +284,29 @@ static bool shape_config(int M, int N, int K, int epilogue, int* ks_out, int* G_
 }
 
 static bool gemv_config(const GemmArgs& g, int* ks, int* G, int* ns) {
-    if (g.n_split != 1 || !g.Wh || !g.A) return false;
+    const bool q8 = g.W8.q != nullptr;
+    if (g.n_split != 1 || !g.A || (q8 ? !g.W8.d_r : !g.Wh)) return false;
     if (g.epilogue == kEpiArgmax ? (!g.amax_val || !g.amax_idx) : g.epilogue == kEpiSwiglu ? !g.H : !g.C)
         return false;
-    return shape_config(g.M, g.N, g.K, g.epilogue, ks, G, ns);
+    return shape_config(g.M, g.N, g.K, g.epilogue, q8, ks, G, ns);
 }
 
-bool gemv_shape_supported(int M, int N, int K, int epilogue) {
+bool gemv_shape_supported(int M, int N, int K, int epilogue, bool q8) {
     int ks, G, ns;
-    return shape_config(M, N, K, epilogue, &ks, &G, &ns);
+    return shape_config(M, N, K, epilogue, q8, &ks, &G, &ns);
 }
 
 bool launch_q8_gemv(const GemmArgs& g, cudaStream_t s) {
     int ks, G, ns;
     if (!gemv_config(g, &ks, &G, &ns)) return false;
     GemvArgs a{};
-    a.A = g.A; a.A_lo = g.A_lo; a.W = g.Wh; a.M = g.M; a.N = g.N; a.K = g.K; a.ks = ks; a.G = G;
+    a.A = g.A; a.A_lo = g.A_lo; a.W = g.Wh; a.Wq = g.W8.q; a.Wd = g.W8.d_r;
+    a.M = g.M; a.N = g.N; a.K = g.K; a.ks = ks; a.G = G;
     a.epilogue = g.epilogue; a.C = g.epilogue == kEpiSwiglu ? nullptr : g.C; a.amax_val = g.amax_val;
     a.amax_idx = g.amax_idx; a.H = g.H; a.H_lo = g.H_lo;
-    if (g.M == 1) launch_mm<1>(a, ns, s);
-    else if (g.M == 2) launch_mm<2>(a, ns, s);
-    else if (g.M <= 4) launch_mm<4>(a, ns, s);
-    else launch_mm<8>(a, ns, s);
+    if (!g.W8.q) launch_form<false, 8>(a, ns, s);
+    else if (wpl_for(true, g.K) == 16) launch_form<true, 16>(a, ns, s);
+    else launch_form<true, 8>(a, ns, s);
     return true;
 }
 

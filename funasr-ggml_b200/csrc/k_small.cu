@@ -6,9 +6,11 @@
 //                      f16(rms_norm(x) * w) for the next GEMM (gpu_rms_norm, :16-25)
 //   swiglu           : f16(silu(gate) * up) from the gate/up GEMM partials (:177-180)
 //   argmax_reduce    : first maximum over lm_head tiles (compute/gpu_runner.hpp:108-118)
-//   repack_q8        : GGUF Q8_0 blocks -> f16(d * q) weight matrix
+//   repack_q8        : GGUF Q8_0 blocks -> f16(d * q) weight matrix (the encoder's weights)
+//   repack_q8_planes : GGUF Q8_0 blocks -> the q / d_t / d_r planes the decoder GEMMs read
 //   page_copy / fill_random / read_pages / apply_bt_updates : page-pool maintenance
 #include "fa_kernels.cuh"
+#include "q8_planes.cuh"
 #include "k_norm.cuh"
 
 namespace fa {
@@ -132,6 +134,23 @@ __global__ void repack_q8_kernel(const uint8_t* raw, int N, int K, int r0, __hal
     for (int j = 0; j < kQK; ++j) w[j] = __float2half_rn(__fmul_rn(d, (float)(int8_t)blk[2 + j]));
 }
 
+// One thread per Q8_0 block: the 32 values go to q row r0 + n, the scale to both
+// scale planes (block-major d_t with row length n_total, row-major d_r).
+__global__ void repack_q8_planes_kernel(const uint8_t* raw, int N, int K, int r0, int n_total, int8_t* q,
+                                        __half* d_t, __half* d_r) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nb = K / kQK;
+    if (i >= (size_t)N * nb) return;
+    const int n = (int)(i / nb), b = (int)(i % nb);
+    const uint8_t* blk = raw + i * kQBytes;
+    const __half d = __ushort_as_half((uint16_t)blk[0] | ((uint16_t)blk[1] << 8));
+    d_t[(size_t)b * n_total + r0 + n] = d;
+    d_r[(size_t)(r0 + n) * nb + b] = d;
+    int8_t* dst = q + (size_t)(r0 + n) * K + (size_t)b * kQK;
+#pragma unroll
+    for (int j = 0; j < kQK; ++j) dst[j] = (int8_t)blk[2 + j];
+}
+
 __global__ void __launch_bounds__(256) page_copy_kernel(__half* pool, size_t layer_stride, const int* src,
                                                         const int* dst, size_t page_elems) {
     const int i = blockIdx.x, l = blockIdx.y;
@@ -222,6 +241,14 @@ void launch_apply_bt_updates(int* block_table, const int* upd_idx, const int* up
 void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_w, cudaStream_t s) {
     const size_t n = (size_t)N * (K / kQK);
     repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, N, K, r0, dst_w);
+}
+
+void launch_repack_q8_planes(const uint8_t* raw, int N, int K, int r0, int n_total, void* planes, cudaStream_t s) {
+    const size_t n = (size_t)N * (K / kQK);
+    unsigned char* b = static_cast<unsigned char*>(planes);
+    repack_q8_planes_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        raw, N, K, r0, n_total, reinterpret_cast<int8_t*>(b), reinterpret_cast<__half*>(b + q8p_dt_offset(n_total, K)),
+        reinterpret_cast<__half*>(b + q8p_dr_offset(n_total, K)));
 }
 
 void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,

@@ -1,5 +1,6 @@
 // Continuous-batching scheduler on a decoder context: SchedCore's policy bound to the
 // C ABI of the decoder (sequences, fa_forward_rows), exported as fa_sched_*.
+#include "nvtx_range.hpp"
 #include "funasr_dec.h"
 #include "sched_core.hpp"
 
@@ -87,6 +88,7 @@ extern "C" int fa_sched_submit(fa_sched* s, int64_t tag, const int* prompt_ids, 
 }
 
 extern "C" int fa_sched_step(fa_sched* s, fa_sched_event* events, int max_events, int* n_events) {
+    fa::NvtxRange nv("fa_sched_step");
     if (!s || (max_events > 0 && !events) || !n_events)
         return fa::report_op_error(FA_ERR_INVALID_ARG, "fa_sched_step: bad argument");
     // events not yet handed out come first; a step runs only when none are left

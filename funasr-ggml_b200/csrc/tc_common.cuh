@@ -112,6 +112,10 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // 128 B swizzle when `swizzle`. False when the driver entry point is missing or the
 // encoder rejects the arguments.
 bool make_map(CUtensorMap* tm, const void* base, int cols, long long rows, int box_cols, int box_rows, bool swizzle);
+// The same over a uint8 [rows][cols] array (the q plane of Q8_0 weights), plain or with the
+// 64 B swizzle (for 64-byte box rows: 16 B chunk c of row r lands at chunk c ^ ((r >> 1) & 3)).
+bool make_map_u8(CUtensorMap* tm, const void* base, int cols, long long rows, int box_cols, int box_rows,
+                 bool swizzle64);
 bool tensor_maps_available();
 
 }  // namespace fa

@@ -160,6 +160,11 @@ def lib():
         "fa_op_q8_gemm_argmax": ([_P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _P], _I),
         "fa_op_q8_gemm_swiglu": ([_P, _P, _I, _I, _P, _I, _P, _P, _P], _I),
         "fa_op_swiglu": ([_P, _I, _I, _I, _P, _P, _P], _I),
+        "fa_op_q8_planes_bytes": ([_I, _I], ctypes.c_size_t),
+        "fa_op_repack_q8_planes": ([_P, _I, _I, _P, _P], _I),
+        "fa_op_q8p_gemm": ([_P, _P, _I, _I, _P, _I, _I, _P, _I, _P], _I),
+        "fa_op_q8p_gemm_argmax": ([_P, _P, _I, _I, _P, _I, _P, _P, _P, _I, _P], _I),
+        "fa_op_q8p_gemm_swiglu": ([_P, _P, _I, _I, _P, _I, _P, _P, _P], _I),
         "fa_palloc_create": ([_I], _P),
         "fa_palloc_destroy": ([_P], None),
         "fa_palloc_alloc": ([_P], _I),
@@ -496,6 +501,29 @@ def op_argmax_scratch_bytes(M, N) -> int:
 def op_q8_gemm_argmax(a16, a16_lo, M, K, w16, N, scratch, nxt, logits=0, variant=0, stream=0):
     _check(lib().fa_op_q8_gemm_argmax(a16, a16_lo or None, M, K, w16, N, scratch, nxt, logits or None, variant,
                                       stream or None))
+
+
+def op_q8_planes_bytes(N, K) -> int:
+    """Bytes of the Q8_0 planes (q int8 [N][K], scales f16 [K/32][N] and [N][K/32])."""
+    return int(lib().fa_op_q8_planes_bytes(N, K))
+
+
+def op_repack_q8_planes(raw, N, K, planes, stream=0):
+    """GGUF Q8_0 blocks [N][K/32][34 B] on the device -> the planes the decoder GEMMs read."""
+    _check(lib().fa_op_repack_q8_planes(raw, N, K, planes, stream or None))
+
+
+def op_q8p_gemm(a16, a16_lo, M, K, planes, N, n_split, c, variant=0, stream=0):
+    _check(lib().fa_op_q8p_gemm(a16, a16_lo or None, M, K, planes, N, n_split, c, variant, stream or None))
+
+
+def op_q8p_gemm_swiglu(a16, a16_lo, M, K, planes, N, h16, h_lo, stream=0):
+    _check(lib().fa_op_q8p_gemm_swiglu(a16, a16_lo or None, M, K, planes, N, h16, h_lo or None, stream or None))
+
+
+def op_q8p_gemm_argmax(a16, a16_lo, M, K, planes, N, scratch, nxt, logits=0, variant=0, stream=0):
+    _check(lib().fa_op_q8p_gemm_argmax(a16, a16_lo or None, M, K, planes, N, scratch, nxt, logits or None, variant,
+                                       stream or None))
 
 
 # ---------------------------------------------------------------- encoder --

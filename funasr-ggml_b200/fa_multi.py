@@ -1,7 +1,9 @@
 """Multi-GPU plumbing for independent utterance streams (no data-path collectives).
 
 Streams never interact, so the GPUs of one box each hold a weight replica and their
-own page pool, and a host dispatcher gives each rank its share of the streams.
+own page pool, and a host dispatcher gives each rank its share of the streams: a
+contiguous split for equal streams (the decode benchmark), and the least-outstanding-
+KV-pages rule for streams of mixed lengths (continuous batching).
 torch.distributed (NCCL on GPUs, gloo in CPU tests) is used only for the start
 barrier and for max/sum reductions of the timing numbers.
 """
@@ -76,6 +78,37 @@ def shard(items: Sequence, rank: int, world: int) -> list:
     lo = rank * n // world
     hi = (rank + 1) * n // world
     return list(items[lo:hi])
+
+
+def dispatch_by_pages(arrive, prompt_len, out_len, world: int, token_s: float = 0.02, page_tokens: int = 16):
+    """Host dispatcher of independent streams: each stream, in arrival order, goes to the
+    rank with the fewest outstanding KV pages at its arrival (ties to the lowest rank).
+    A stream holds ceil((prompt + output) / page_tokens) pages from its arrival until its
+    estimated finish, arrival + output * token_s (one token per decode step). Every rank
+    computes the same assignment from the same seeded stream list, so nothing crosses
+    between ranks. Returns the owning rank of each stream."""
+    import heapq
+
+    import numpy as np
+    arrive = np.asarray(arrive, np.float64)
+    plen = np.asarray(prompt_len, np.int64)
+    olen = np.asarray(out_len, np.int64)
+    n = len(arrive)
+    owner = np.empty(n, np.int64)
+    load = [0] * world
+    live = [[] for _ in range(world)]          # per rank: heap of (finish time, pages)
+    for i in np.argsort(arrive, kind="stable"):
+        t = arrive[i]
+        for r in range(world):
+            h = live[r]
+            while h and h[0][0] <= t:
+                load[r] -= heapq.heappop(h)[1]
+        r = min(range(world), key=lambda k: (load[k], k))
+        pages = int((plen[i] + olen[i] + page_tokens - 1) // page_tokens)
+        load[r] += pages
+        heapq.heappush(live[r], (t + float(olen[i]) * token_s, pages))
+        owner[i] = r
+    return owner
 
 
 def shutdown():

@@ -302,8 +302,13 @@ FA_API int fa_op_paged_attention_noalloc(const float* q_dev, int M, const int* p
                                          uint16_t* out16_dev, uint16_t* out16_lo_dev, float* out32_dev, int* err_dev,
                                          void* stream);
 /* Kernel (4): Q8_0 GEMM C = A . W^T (compute/llm_ops_gpu.cpp:53-55,149,177-180,206).
- * A [M][K] as an f16 pair a16 + a16_lo (a16_lo may be NULL: plain f16 activations);
- * W [N][K] f16 = f16(d * q) per Q8_0 block (fa_op_repack_q8 builds it from GGUF blocks).
+ * A [M][K] as an f16 pair a16 + a16_lo (a16_lo may be NULL: plain f16 activations).
+ * Two weight forms. fa_op_q8p_*: the decoder's, Q8_0 planes built by
+ * fa_op_repack_q8_planes from GGUF blocks [N][K/32][34 B] (tools/hf_convert_ggml_q8.py:
+ * 354-381): q int8 [N][K], then the block scales twice, f16 [K/32][N] and f16 [N][K/32],
+ * in one 256-byte aligned buffer of fa_op_q8_planes_bytes(N, K) bytes (N a multiple of
+ * 4, K of 64); every weight is the exact d * q. fa_op_q8_gemm*: W [N][K] f16, e.g.
+ * f16(d * q) from fa_op_repack_q8 (the encoder's form).
  * n_split > 1 writes partials [n_split][M][N] (their sum is C).
  * variant: 0 = the small-M CUDA-core kernel when M <= 2 and n_split == 1 (K a multiple of
  * 256), the swapped tcgen05 kernel when M <= 128 (with argmax M <= 32), else the 128-row-
@@ -329,6 +334,16 @@ FA_API size_t fa_op_argmax_scratch_bytes(int M, int N);
 FA_API int fa_op_q8_gemm_argmax(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K,
                                 const uint16_t* w16_dev, int N, void* scratch_dev, int* next_dev, float* logits_dev,
                                 int variant, void* stream);
+/* The same three GEMMs on Q8_0 planes (the form the decoder's layers and lm_head use). */
+FA_API size_t fa_op_q8_planes_bytes(int N, int K);
+FA_API int fa_op_repack_q8_planes(const uint8_t* gguf_q8_dev, int N, int K, void* planes_dev, void* stream);
+FA_API int fa_op_q8p_gemm(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K, const void* planes_dev,
+                          int N, int n_split, float* c_dev, int variant, void* stream);
+FA_API int fa_op_q8p_gemm_swiglu(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K,
+                                 const void* planes_dev, int N, uint16_t* h16_dev, uint16_t* h_lo_dev, void* stream);
+FA_API int fa_op_q8p_gemm_argmax(const uint16_t* a16_dev, const uint16_t* a16_lo_dev, int M, int K,
+                                 const void* planes_dev, int N, void* scratch_dev, int* next_dev, float* logits_dev,
+                                 int variant, void* stream);
 
 /* ---- host-only page allocator (no GPU needed): the policy behind fa_seq_* ----
  * Lowest free page id first; compaction moves the highest live page into the lowest

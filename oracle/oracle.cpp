@@ -36,11 +36,12 @@
 //     f32 -> f16 is round-to-nearest-even.
 //   * RoPE cos/sin: theta computed in double, cos/sin in double, rounded to f32
 //     once into a table [pos][i] (the same table the CUDA path uploads).
-//   * GEMM mode 1 (the CUDA path's arithmetic): f32 activations times the Q8_0
-//     weights expanded once to f16, W = f16(f32(d) * q), sums in wide precision.
-//     (The CUDA path carries the activations as an f16 hi/lo pair, ~22 bits.)
-//     Mode 0 is the same with the exact weights d*q; mode 2 is the ggml CPU
-//     backend's Q8_0-activation arithmetic.
+//   * GEMM mode 0 (the decoder CUDA path's arithmetic): f32 activations times the
+//     exact Q8_0 weights d*q, sums in wide precision. (The CUDA path carries the
+//     activations as an f16 hi/lo pair, ~22 bits, and each weight as the exact f16
+//     pair of d*q.) Mode 1 rounds each weight once to f16, W = f16(f32(d) * q): the
+//     f16 weight form the encoder's GEMMs read. Mode 2 is the ggml CPU backend's
+//     Q8_0-activation arithmetic.
 //   * Attention scores, softmax and PV are computed in double here.
 //
 // Parity pins: the Q8_0 codec is pinned byte-for-byte against the reference
@@ -227,8 +228,9 @@ void or_rmsnorm(const float* x, const float* w, int rows, int n, float eps, floa
 }
 
 // ---- Q8_0 matmul: C[M][N] = A[M][K] . W[N][K]^T --------------------------------
-// mode 0: f32 activations x exactly dequantised weights d*q, double accumulation.
-// mode 1: f32 activations x f16(d*q) weights, double accumulation (the CUDA path).
+// mode 0: f32 activations x exactly dequantised weights d*q, double accumulation
+//         (the decoder CUDA path).
+// mode 1: f32 activations x f16(d*q) weights, double accumulation (the f16 weight form).
 // mode 2: ggml CPU backend: Q8_0 activations, integer block dots, f32 block sum.
 void or_gemm_q8(const float* A, int M, int K, const uint8_t* W, int N, int mode, float* C) {
     const int nb = K / QK;

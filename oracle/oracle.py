@@ -23,8 +23,8 @@ _LIB_PATH = os.path.join(_HERE, "liboracle.so")
 _lib = None
 
 # GEMM arithmetic modes of or_gemm_q8 / or_decoder_forward.
-MODE_EXACT = 0      # f32 activations x exactly dequantised weights d*q
-MODE_W16 = 1        # f32 activations x f16(d*q) weights: the CUDA path's arithmetic
+MODE_EXACT = 0      # f32 activations x exactly dequantised weights d*q: the decoder CUDA path
+MODE_W16 = 1        # f32 activations x f16(d*q) weights: the f16 weight form (the encoder's GEMMs)
 MODE_GGML_CPU = 2   # ggml CPU backend: Q8_0 activations, integer block dots
 
 QK8_0 = 32
@@ -141,7 +141,7 @@ def rmsnorm(x: np.ndarray, w: Optional[np.ndarray], eps: float = 1e-5) -> np.nda
     return out
 
 
-def gemm_q8(a: np.ndarray, w_q8: np.ndarray, n: int, mode: int = MODE_W16) -> np.ndarray:
+def gemm_q8(a: np.ndarray, w_q8: np.ndarray, n: int, mode: int = MODE_EXACT) -> np.ndarray:
     a = _c(a, np.float32)
     M, K = a.shape
     w_q8 = _c(w_q8, np.uint8)
@@ -254,7 +254,7 @@ class OracleDecoder:
     """
 
     def __init__(self, cfg, weights, n_pages: int, max_seqs: int, max_pages_per_seq: int,
-                 max_pos: int, mode: int = MODE_W16):
+                 max_pos: int, mode: int = MODE_EXACT):
         self.cfg = cfg
         self.mode = mode
         L = cfg["n_layers"]
@@ -325,6 +325,17 @@ class OracleDecoder:
             p = self.alloc.alloc()
             self.block_table[slot, len(pages)] = p
             pages.append(p)
+
+    def adopt(self, slot: int, length: int, pages_by_layer):
+        """Take over a cached sequence: `length` tokens whose pages (allocated here by the
+        same lowest-first policy) get the given contents, pages_by_layer[l] = [n][page_elems]
+        f16 bits in block-table order. Returns the slot's page ids."""
+        self._reserve(slot, length)
+        self.seq_len[slot] = length
+        pages = self.seq_pages[slot]
+        for l, arr in enumerate(pages_by_layer):
+            self.pool[l, pages] = np.asarray(arr, np.uint16).reshape(len(pages), self.page_elems)
+        return list(pages)
 
     def forward(self, slots: Sequence[int], tokens=None, embeds=None, want_logits=True):
         """One forward over rows; each row appends one token to its sequence."""

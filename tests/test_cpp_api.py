@@ -94,7 +94,7 @@ def test_cpp_api_decode_matches_oracle(program, tmp_path, torch_cuda):
     ids3 = np.frombuffer(raw, np.int32, n_new, off + 4 * n_new)
 
     od = oracle.OracleDecoder(CFG, w, n_pages=64, max_seqs=1, max_pages_per_seq=64, max_pos=4096,
-                              mode=oracle.MODE_W16)
+                              mode=oracle.MODE_EXACT)
     od.seq_open(0)
     lg, nx = od.forward([0] * n_prompt, embeds=prompt)
     o_ids = []

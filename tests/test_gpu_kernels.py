@@ -323,6 +323,47 @@ def _q8_device(torch, rng, N, K):
     return raw, w16
 
 
+# The two weight forms the GEMMs read: "q8p", the decoder's Q8_0 planes (every weight the
+# exact d*q, checked against the oracle's exact mode), and "f16", f16(d*q) (the encoder's
+# form, checked against the oracle's W16 mode).
+FORMS = ["q8p", "f16"]
+
+
+def _weights(torch, raw, N, K, form):
+    """Device weights of GGUF Q8_0 bytes `raw` [N][K/32*34] in `form`, and the oracle mode."""
+    d_raw = dev(torch, raw)
+    if form == "f16":
+        w = torch.zeros((N, K), dtype=torch.int16, device="cuda")
+        fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, w.data_ptr())
+        return w, oracle.MODE_W16
+    w = torch.zeros(fa_dec.op_q8_planes_bytes(N, K), dtype=torch.uint8, device="cuda")
+    fa_dec.op_repack_q8_planes(d_raw.data_ptr(), N, K, w.data_ptr())
+    return w, oracle.MODE_EXACT
+
+
+def _gemm(form, a_hi, a_lo, M, K, w, N, split, c, variant):
+    f = fa_dec.op_q8p_gemm if form == "q8p" else fa_dec.op_q8_gemm
+    f(a_hi, a_lo, M, K, w, N, split, c, variant)
+
+
+def test_repack_planes_keep_every_gguf_byte(torch_cuda):
+    """q [N][K], the scales block-major [K/32][N] and row-major [N][K/32]: the GGUF bytes moved."""
+    torch = torch_cuda
+    rng = np.random.default_rng(1)
+    N, K = 192, 512
+    raw = fa_synth.q8_0_random(rng, N, K)
+    w, _ = _weights(torch, raw, N, K, "q8p")
+    torch.cuda.synchronize()
+    got = w.cpu().numpy()
+    assert got.nbytes == N * K + N * (K // 32) * 4
+    blocks = raw.reshape(N, K // 32, 34)
+    d = blocks[:, :, :2].copy().view(np.uint16)[:, :, 0]
+    assert np.array_equal(got[:N * K].view(np.int8).reshape(N, K), blocks[:, :, 2:].view(np.int8).reshape(N, K))
+    d_t = got[N * K:N * K + N * K // 16].view(np.uint16).reshape(K // 32, N)
+    d_r = got[N * K + N * K // 16:].view(np.uint16).reshape(N, K // 32)
+    assert np.array_equal(d_t, d.T) and np.array_equal(d_r, d)
+
+
 def test_repack_rounds_d_times_q_to_f16(torch_cuda):
     rng = np.random.default_rng(0)
     raw, w16 = _q8_device(torch_cuda, rng, 128, 256)
@@ -334,19 +375,21 @@ def test_repack_rounds_d_times_q_to_f16(torch_cuda):
     assert np.array_equal(w16.cpu().numpy().view(np.uint16), want)
 
 
-def test_tcgen05_gemm_single_tile(torch_cuda):
+@pytest.mark.parametrize("form", FORMS)
+def test_tcgen05_gemm_single_tile(torch_cuda, form):
     """One CTA (128 x 128 tile, K = 64) of the tcgen05 kernel: the smallest case."""
     torch = torch_cuda
     rng = np.random.default_rng(42)
     M, N, K = 128, 128, 64
-    raw, w16 = _q8_device(torch, rng, N, K)
+    raw = fa_synth.q8_0_random(rng, N, K)
+    w, mode = _weights(torch, raw, N, K, form)
     a = rng.standard_normal((M, K)).astype(np.float32)
     hi, lo, a_eff = _split_f16(a)
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     c = torch.zeros((1, M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, 1, c.data_ptr(), 0)
+    _gemm(form, d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), N, 1, c.data_ptr(), 0)
     torch.cuda.synchronize()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
+    ref = oracle.gemm_q8(a_eff, raw, N, mode)
     got = c[0].cpu().numpy()
     assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
 
@@ -358,6 +401,7 @@ def _split_f16(x):
     return hi, lo, oracle.f16_bits_to_f32(hi) + oracle.f16_bits_to_f32(lo)
 
 
+@pytest.mark.parametrize("form", FORMS)
 @pytest.mark.parametrize("variant", [0, 1, 2, 4])
 @pytest.mark.parametrize("M,N,K,split", [
     (1, 1024, 1024, 1), (5, 4096, 1024, 4), (16, 1024, 2048, 8), (17, 2048, 1024, 2),
@@ -365,28 +409,29 @@ def _split_f16(x):
     # prefill-size row counts, ragged last row tile
     (256, 4096, 1024, 1), (400, 6144, 1024, 2), (513, 1024, 3072, 4),
 ])
-def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
-    if variant == 4 and M > 128:
-        pytest.skip("the swapped tcgen05 kernel takes at most 128 rows")
+def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant, form):
+    if variant == 4 and M > 128 and form == "f16":
+        pytest.skip("with f16 weights the swapped tcgen05 kernel takes at most 128 rows")
     torch = torch_cuda
     rng = np.random.default_rng(M * 7 + N + K)
-    raw, w16 = _q8_device(torch, rng, N, K)
+    raw = fa_synth.q8_0_random(rng, N, K)
+    w, mode = _weights(torch, raw, N, K, form)
     a = (rng.standard_normal((M, K)) * 3).astype(np.float32)
     hi, lo, a_eff = _split_f16(a)
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     c = torch.zeros((split, M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, split, c.data_ptr(), variant)
+    _gemm(form, d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), N, split, c.data_ptr(), variant)
     torch.cuda.synchronize()
     got = c.sum(0).cpu().numpy()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
+    ref = oracle.gemm_q8(a_eff, raw, N, mode)
     # fp32 accumulation over K (up to 3072) against a double-precision sum: ~sqrt(K) * 2^-24
     assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
     assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
     # without the lo plane the result is the f16-activation product
     c.zero_()
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), 0, M, K, w16.data_ptr(), N, split, c.data_ptr(), variant)
+    _gemm(form, d_hi.data_ptr(), 0, M, K, w.data_ptr(), N, split, c.data_ptr(), variant)
     torch.cuda.synchronize()
-    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, oracle.MODE_W16)
+    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, mode)
     assert rel_rms(c.sum(0).cpu().numpy(), ref16) < 5e-6
 
 
@@ -394,51 +439,55 @@ def test_q8_gemm_matches_oracle(torch_cuda, M, N, K, split, variant):
     (1, 4096, 1024), (2, 1024, 2048), (3, 6144, 1024), (4, 1024, 3072), (5, 4096, 1024), (8, 1024, 3072),
     (1, 768, 512), (6, 64, 256), (8, 2048, 4096), (2, 151936, 1024),
 ])
-def test_small_m_gemm_matches_oracle(torch_cuda, M, N, K):
+@pytest.mark.parametrize("form", FORMS)
+def test_small_m_gemm_matches_oracle(torch_cuda, M, N, K, form):
     """The CUDA-core kernel (variant 3) on the decoder's shapes and odd ones: fp32 result
     against the oracle's double sum, with and without the lo plane."""
     torch = torch_cuda
     rng = np.random.default_rng(M * 11 + N + K)
-    raw, w16 = _q8_device(torch, rng, N, K)
+    raw = fa_synth.q8_0_random(rng, N, K)
+    w, mode = _weights(torch, raw, N, K, form)
     a = (rng.standard_normal((M, K)) * 3).astype(np.float32)
     hi, lo, a_eff = _split_f16(a)
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     assert fa_dec.op_gemm_plan(M, N, K, variant=3) == 1
     c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, 1, c.data_ptr(), 3)
+    _gemm(form, d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), N, 1, c.data_ptr(), 3)
     torch.cuda.synchronize()
     got = c.cpu().numpy()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
+    ref = oracle.gemm_q8(a_eff, raw, N, mode)
     assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
     assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
     c.zero_()
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), 0, M, K, w16.data_ptr(), N, 1, c.data_ptr(), 3)
+    _gemm(form, d_hi.data_ptr(), 0, M, K, w.data_ptr(), N, 1, c.data_ptr(), 3)
     torch.cuda.synchronize()
-    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, oracle.MODE_W16)
+    ref16 = oracle.gemm_q8(oracle.f16_bits_to_f32(hi), raw, N, mode)
     assert rel_rms(c.cpu().numpy(), ref16) < 5e-6
 
 
 @pytest.mark.parametrize("M,F,K", [(1, 3072, 1024), (2, 3072, 1024), (5, 512, 256), (8, 1536, 2048)])
-def test_small_m_gemm_swiglu_equals_separate_kernels(torch_cuda, M, F, K):
+@pytest.mark.parametrize("form", FORMS)
+def test_small_m_gemm_swiglu_equals_separate_kernels(torch_cuda, M, F, K, form):
     """Gate/up GEMM with SwiGLU in its epilogue: the same bits as the small-M GEMM followed
     by the decoder's SwiGLU kernel, and within f16-pair precision of the oracle."""
     torch = torch_cuda
     rng = np.random.default_rng(M + F + K)
-    raw, w16 = _q8_device(torch, rng, 2 * F, K)
+    raw = fa_synth.q8_0_random(rng, 2 * F, K)
+    w, mode = _weights(torch, raw, 2 * F, K, form)
     hi, lo, a_eff = _split_f16(rng.standard_normal((M, K)).astype(np.float32))
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     h16 = torch.zeros((M, F), dtype=torch.int16, device="cuda")
     h_lo = torch.zeros_like(h16)
-    fa_dec.op_q8_gemm_swiglu(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), 2 * F, h16.data_ptr(),
-                             h_lo.data_ptr())
+    sw = fa_dec.op_q8p_gemm_swiglu if form == "q8p" else fa_dec.op_q8_gemm_swiglu
+    sw(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), 2 * F, h16.data_ptr(), h_lo.data_ptr())
     c = torch.zeros((M, 2 * F), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), 2 * F, 1, c.data_ptr(), 3)
+    _gemm(form, d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), 2 * F, 1, c.data_ptr(), 3)
     r16 = torch.zeros_like(h16)
     r_lo = torch.zeros_like(h16)
     fa_dec.op_swiglu(c.data_ptr(), 1, M, F, r16.data_ptr(), r_lo.data_ptr())
     torch.cuda.synchronize()
     assert torch.equal(h16, r16) and torch.equal(h_lo, r_lo)
-    gu = oracle.gemm_q8(a_eff, raw, 2 * F, oracle.MODE_W16).astype(np.float64)
+    gu = oracle.gemm_q8(a_eff, raw, 2 * F, mode).astype(np.float64)
     g, u = gu[:, :F], gu[:, F:]
     want = g / (1.0 + np.exp(-g)) * u
     got = oracle.f16_bits_to_f32(_u16(h16)).astype(np.float64) + oracle.f16_bits_to_f32(_u16(h_lo))
@@ -448,37 +497,40 @@ def test_small_m_gemm_swiglu_equals_separate_kernels(torch_cuda, M, F, K):
 @pytest.mark.parametrize("M,N,K", [(3, 4096, 1024), (16, 1024, 3072), (17, 6144, 1024), (32, 1024, 2048),
                                    (33, 4096, 1024), (64, 1024, 3072), (9, 256, 512), (65, 4096, 1024),
                                    (128, 1024, 3072), (100, 6144, 1024)])
-def test_few_row_tcgen05_gemm_matches_oracle(torch_cuda, M, N, K):
+@pytest.mark.parametrize("form", FORMS)
+def test_few_row_tcgen05_gemm_matches_oracle(torch_cuda, M, N, K, form):
     """The swapped tcgen05 kernel (variant 4) at each activation tile width (16, 32, 64,
     128 rows) and the planner's split, against the oracle's double sum."""
     torch = torch_cuda
     rng = np.random.default_rng(M * 13 + N + K)
-    raw, w16 = _q8_device(torch, rng, N, K)
+    raw = fa_synth.q8_0_random(rng, N, K)
+    w, mode = _weights(torch, raw, N, K, form)
     hi, lo, a_eff = _split_f16((rng.standard_normal((M, K)) * 3).astype(np.float32))
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     split = fa_dec.op_gemm_plan(M, N, K, variant=4)
     c = torch.zeros((split, M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, split, c.data_ptr(), 4)
+    _gemm(form, d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), N, split, c.data_ptr(), 4)
     torch.cuda.synchronize()
     got = c.sum(0).cpu().numpy()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
+    ref = oracle.gemm_q8(a_eff, raw, N, mode)
     assert rel_rms(got, ref) < 5e-6, rel_rms(got, ref)
     assert max_abs(got, ref) < 2e-5 * np.abs(ref).max()
 
 
-def test_small_m_gemm_rows_do_not_depend_on_m(torch_cuda):
+@pytest.mark.parametrize("form", FORMS)
+def test_small_m_gemm_rows_do_not_depend_on_m(torch_cuda, form):
     """A row's result is the same bits whether it is computed alone or among 2..8 rows, so
     batching sequences together does not change any sequence's logits."""
     torch = torch_cuda
     rng = np.random.default_rng(5)
     N, K = 4096, 1024
-    raw, w16 = _q8_device(torch, rng, N, K)
+    w, _ = _weights(torch, fa_synth.q8_0_random(rng, N, K), N, K, form)
     hi, lo, _ = _split_f16((rng.standard_normal((8, K)) * 3).astype(np.float32))
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     outs = {}
     for M in (1, 2, 3, 4, 8):
         c = torch.zeros((M, N), dtype=torch.float32, device="cuda")
-        fa_dec.op_q8_gemm(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N, 1, c.data_ptr(), 3)
+        _gemm(form, d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), N, 1, c.data_ptr(), 3)
         torch.cuda.synchronize()
         outs[M] = c.cpu().numpy()
     for M in (2, 3, 4, 8):
@@ -499,33 +551,37 @@ def test_small_m_gemm_rejects_shapes_it_does_not_take(torch_cuda):
     torch.cuda.synchronize()
 
 
+@pytest.mark.parametrize("form", FORMS)
 @pytest.mark.parametrize("variant", [0, 1, 3, 4])
 @pytest.mark.parametrize("M,N", [(7, 151936), (300, 4096), (1, 151936), (4, 151936), (40, 151936), (128, 151936)])
-def test_lm_head_argmax_full_vocab(torch_cuda, variant, M, N):
-    if (variant == 3 and M > 8) or (variant == 4 and M > 128):
+def test_lm_head_argmax_full_vocab(torch_cuda, variant, M, N, form):
+    if (variant == 3 and M > 8) or (variant == 4 and M > 128 and form == "f16"):
         pytest.skip("outside the kernel's row range")
     torch = torch_cuda
     rng = np.random.default_rng(3)
     K = 1024
-    raw, w16 = _q8_device(torch, rng, N, K)
+    raw = fa_synth.q8_0_random(rng, N, K)
+    w, mode = _weights(torch, raw, N, K, form)
     hi, lo, a_eff = _split_f16(rng.standard_normal((M, K)).astype(np.float32))
     d_hi, d_lo = dev(torch, _i16(hi)), dev(torch, _i16(lo))
     scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
     nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
     logits = torch.zeros((M, N), dtype=torch.float32, device="cuda")
-    fa_dec.op_q8_gemm_argmax(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w16.data_ptr(), N,
-                             scratch.data_ptr(), nxt.data_ptr(), logits.data_ptr(), variant)
+    am = fa_dec.op_q8p_gemm_argmax if form == "q8p" else fa_dec.op_q8_gemm_argmax
+    am(d_hi.data_ptr(), d_lo.data_ptr(), M, K, w.data_ptr(), N, scratch.data_ptr(), nxt.data_ptr(),
+       logits.data_ptr(), variant)
     torch.cuda.synchronize()
-    ref = oracle.gemm_q8(a_eff, raw, N, oracle.MODE_W16)
+    ref = oracle.gemm_q8(a_eff, raw, N, mode)
     assert rel_rms(logits.cpu().numpy(), ref) < 5e-6
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(ref))
     # the kernel's argmax is the first maximum of its own logits
     assert np.array_equal(nxt.cpu().numpy(), oracle.argmax_rows(logits.cpu().numpy()))
 
 
+@pytest.mark.parametrize("form", FORMS)
 @pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("j1,j2", [(1000, 70000), (64 * 5 + 3, 64 * 5 + 40), (0, 151935), (64 * 7 + 31, 64 * 7 + 32)])
-def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2, variant):
+def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2, variant, form):
     torch = torch_cuda
     M, N, K = 3, 151936, 1024
     nb = K // 32
@@ -537,15 +593,13 @@ def test_lm_head_argmax_ties_pick_first(torch_cuda, j1, j2, variant):
         blocks[j, :, 0:2] = big
         blocks[j, :, 2:] = np.uint8(127)
     raw = blocks.reshape(N, nb * 34)
-    d_raw = dev(torch, raw)
-    w16 = torch.zeros((N, K), dtype=torch.int16, device="cuda")
-    fa_dec.op_repack_q8(d_raw.data_ptr(), N, K, w16.data_ptr())
+    w, _ = _weights(torch, raw, N, K, form)
     a16 = oracle.f32_to_f16_bits(np.full((M, K), 0.5, np.float32))
     d_a = dev(torch, _i16(a16))
     scratch = torch.zeros(fa_dec.op_argmax_scratch_bytes(M, N), dtype=torch.uint8, device="cuda")
     nxt = torch.zeros(M, dtype=torch.int32, device="cuda")
-    fa_dec.op_q8_gemm_argmax(d_a.data_ptr(), 0, M, K, w16.data_ptr(), N, scratch.data_ptr(), nxt.data_ptr(), 0,
-                             variant)
+    am = fa_dec.op_q8p_gemm_argmax if form == "q8p" else fa_dec.op_q8_gemm_argmax
+    am(d_a.data_ptr(), 0, M, K, w.data_ptr(), N, scratch.data_ptr(), nxt.data_ptr(), 0, variant)
     torch.cuda.synchronize()
     assert nxt.cpu().numpy().tolist() == [j1] * M
 

@@ -85,7 +85,7 @@ def test_decoder_forward_with_prefill_tiles_matches_oracle(torch_cuda):
     dec = fa_dec.Decoder(0, **fa_synth.decoder_desc(cfg, max_ctx=1024, n_pages=256, max_seqs=8, max_rows=256))
     dec.load_weights(w)
     od = oracle.OracleDecoder(cfg, w, n_pages=256, max_seqs=8, max_pages_per_seq=64, max_pos=1024,
-                              mode=oracle.MODE_W16)
+                              mode=oracle.MODE_EXACT)
     rng = np.random.default_rng(12)
     sids = [dec.seq_open(1024) for _ in range(3)]
     for s in sids:

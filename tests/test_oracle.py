@@ -181,3 +181,21 @@ def test_f16_weights_stay_close_to_exact_weights():
     rr = lambda a: float(np.sqrt(((a - ref) ** 2).mean() / (ref ** 2).mean()))
     assert rr(outs[oracle.MODE_W16]) < 2e-3
     assert rr(outs[oracle.MODE_W16]) < 0.2 * rr(outs[oracle.MODE_GGML_CPU])
+
+
+def test_encoder_oracle_matches_independent_torch_formulation():
+    """oracle/encoder.py (numpy restatement of compute/encoder_ops.cpp:17-290 and
+    compute/adaptor_ops.cpp:11-149) against the fixture of make_encoder_golden.py: the same
+    graphs in PyTorch float64 with gguf-py's Q8_0 dequantiser, a depthwise Conv1d for the
+    FSMN memory and scaled_dot_product_attention, on a 3 + 2-layer encoder at 5 and 21
+    frames. Both are float64, so they agree to rounding."""
+    import encoder
+    import make_encoder_golden as g
+    h = np.load(make_golden.os.path.join(make_golden.HERE, "encoder_small.npz"))
+    w = fa_synth.make_encoder_weights(g.ENC_CFG, seed=int(h["seed"]))
+    assert make_golden.weights_checksum(w) == str(h["checksum"]), "synthetic encoder weight stream changed"
+    for T in g.FRAMES:
+        enc = encoder.encoder_forward(w, h[f"x{T}"], g.ENC_CFG, w16=False)
+        ada = encoder.adaptor_forward(w, enc, w16=False)
+        for got, ref in ((enc, h[f"enc{T}"]), (ada, h[f"ada{T}"])):
+            assert np.abs(got - ref).max() <= 1e-12 * np.abs(ref).max(), T
