@@ -161,6 +161,11 @@ struct fa_ctx {
     int* h_err = nullptr;
 
     bool use_graphs = true;
+    // bit 0: QKV + kernel (1), bit 1: gate/up + SwiGLU, finished in the tcgen05 GEMM's
+    // clusters. Default 2: the QKV form measured slower (its per-row norm / RoPE / append
+    // tail runs on 4 warps per SM, where the separate kernel spreads it over every SM)
+    int fuse_epilogues = 2;
+    bool enqueue_failed = false; // a planned launch declined its arguments while a step was enqueued
     bool use_pdl = true;       // programmatic dependent launch between the step's kernels
     int gemm_variant = 0;      // 0: CUDA-core kernel up to 2 rows, swapped tcgen05 up to 128 (lm_head: 32),
                                // 128-row-tile tcgen05 above; 1: mma.sync; 2: 128-row-tile tcgen05;
@@ -430,6 +435,14 @@ extern "C" int fa_set_gemm_variant(fa_ctx* ctx, int variant) {
     return FA_OK;
 }
 
+extern "C" int fa_set_fused_epilogues(fa_ctx* ctx, int enable) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    if (enable < 0 || enable > 3) return set_err(ctx, FA_ERR_INVALID_ARG, "fused epilogue mask must be 0 to 3");
+    ctx->fuse_epilogues = enable;
+    clear_graphs(ctx);
+    return FA_OK;
+}
+
 extern "C" int fa_set_graphs(fa_ctx* ctx, int enable) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     ctx->use_graphs = enable != 0;
@@ -518,9 +531,9 @@ static int upload_vec_f32(fa_ctx* ctx, const fa_tensor_view* v, float** dst) {
 // Split a GGUF Q8_0 tensor with N rows of K into the planes of a stacked matrix of
 // n_total rows, at row offset r0.
 static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int N, int K, int r0, int n_total,
-                     unsigned char* planes) {
+                     unsigned char* planes, int interleave = 0) {
     FA_CK(cudaMemcpyAsync(staging, v->data, v->nbytes, cudaMemcpyHostToDevice, ctx->stream));
-    fa::launch_repack_q8_planes(staging, N, K, r0, n_total, planes, ctx->stream);
+    fa::launch_repack_q8_planes(staging, N, K, r0, n_total, planes, ctx->stream, interleave);
     FA_CK(cudaGetLastError());
     FA_CK(cudaStreamSynchronize(ctx->stream));
     return FA_OK;
@@ -585,8 +598,10 @@ extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n
                 (r = upload_q8(ctx, t.k, staging, KD, H, QD, QKV, w.qkv_q)) ||
                 (r = upload_q8(ctx, t.v, staging, KD, H, QD + KD, QKV, w.qkv_q)) ||
                 (r = upload_q8(ctx, t.o, staging, H, QD, 0, H, w.o_q)) ||
-                (r = upload_q8(ctx, t.g, staging, F, H, 0, 2 * F, w.gu_q)) ||
-                (r = upload_q8(ctx, t.u, staging, F, H, F, 2 * F, w.gu_q)) ||
+                // gate and up rows in blocks of 64: rows [128 b, 128 b + 64) are gate rows
+                // [64 b, 64 b + 64), the next 64 the up rows of the same outputs
+                (r = upload_q8(ctx, t.g, staging, F, H, 0, 2 * F, w.gu_q, 64)) ||
+                (r = upload_q8(ctx, t.u, staging, F, H, 64, 2 * F, w.gu_q, 64)) ||
                 (r = upload_q8(ctx, t.dn, staging, H, F, 0, H, w.dn_q)))
                 return r;
             if ((r = upload_vec_f32(ctx, t.qn, &w.q_norm)) || (r = upload_vec_f32(ctx, t.kn, &w.k_norm)) ||
@@ -737,9 +752,12 @@ struct StepPlan {
     bool logits = false;
     bool prof = false;
     bool fuse_swiglu = false;  // gate/up GEMM on the small-M kernel writes SwiGLU's output itself
+    bool fuse_gu_tc = false;   // gate/up GEMM on the tcgen05 kernel finishes SwiGLU in its clusters
+    bool fuse_qkv = false;     // QKV GEMM on the tcgen05 kernel finishes kernel (1) in its clusters
     std::array<int, 12> key() const {
         return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, n_out,
-                (int)fuse_swiglu * 4 + (int)embeds * 2 + (int)logits, (int)prof};
+                (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 + (int)fuse_swiglu * 4 + (int)embeds * 2 + (int)logits,
+                (int)prof};
     }
 };
 
@@ -813,6 +831,12 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     p.s_gu = pick(2 * d.ffn, d.hidden);
     p.s_dn = pick(d.hidden, d.ffn);
     p.fuse_swiglu = gemv_rows(ctx->gemm_variant, M) && fa::gemv_shape_supported(M, 2 * d.ffn, d.hidden, fa::kEpiSwiglu);
+    // one-tile steps on the tcgen05 kernel: QKV finishes kernel (1) and gate/up finishes
+    // SwiGLU inside clusters of their split CTAs (no partials, no separate launches)
+    const bool tc = !gemv_rows(ctx->gemm_variant, M) && skinny_rows(ctx->gemm_variant, M);
+    p.fuse_qkv = tc && (ctx->fuse_epilogues & 1) &&
+                 fa::skinny_fusable(M, (kHq + 2 * kHkv) * kD, d.hidden, p.s_qkv, ctx->n_sm);
+    p.fuse_gu_tc = tc && (ctx->fuse_epilogues & 2) && fa::skinny_fusable(M, 2 * d.ffn, d.hidden, p.s_gu, ctx->n_sm);
     p.n_dec = (int)row_len.size();
     p.n_tiles = n_tiles;
     if (p.n_dec > 0) {
@@ -886,16 +910,23 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         __half* pool_l = ctx->pool + (size_t)l * ctx->layer_stride;
         fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, w.in_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s);
         fa::GemmArgs g{};
-        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(w.qkv_q, QKV, H); g.M = M; g.N = QKV; g.K = H;
-        g.n_split = p.s_qkv; g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
-        run_gemm(ctx, g);
         fa::AppendArgs a{};
         a.qkv_part = ctx->part; a.n_part = p.s_qkv; a.M = M; a.pos = ctx->row_pos; a.slot = ctx->row_slot;
         a.block_table = ctx->bt_dev; a.bt_stride = ctx->bt_stride; a.n_pages = ctx->n_pages;
         a.qn_w = w.q_norm; a.kn_w = w.k_norm; a.Hq = kHq; a.Hkv = kHkv; a.eps = d.rms_eps;
         a.q_scale = 1.0f / std::sqrt((float)kD);
         a.rope = ctx->rope; a.max_pos = d.max_ctx; a.pool_layer = pool_l; a.q_out = ctx->q_rot; a.err = ctx->err_dev;
-        fa::launch_qknorm_rope_append(a, s);
+        g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(w.qkv_q, QKV, H); g.M = M; g.N = QKV; g.K = H;
+        g.n_split = p.s_qkv;
+        if (p.fuse_qkv) {
+            g.epilogue = fa::kEpiQkvAppend; g.app = &a;
+            if (!fa::launch_q8_gemm_tc_skinny(g, ctx->err_dev, s)) ctx->enqueue_failed = true;
+            --n;
+        } else {
+            g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
+            run_gemm(ctx, g);
+            fa::launch_qknorm_rope_append(a, s);
+        }
         const bool prof_l = p.prof && (l == 0 || l == d.n_layers / 2 || l == d.n_layers - 1);
         if (prof_l) record_prof(ctx, 2 * l, capturing);
         if (p.n_dec > 0) {
@@ -933,14 +964,16 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         g = fa::GemmArgs{};
         g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(w.gu_q, 2 * F, H); g.M = M; g.N = 2 * F; g.K = H;
         g.n_split = p.s_gu;
-        if (p.fuse_swiglu) {
+        g.swiglu_interleave64 = 1;     // gate / up rows stacked in blocks of 64 (upload_q8)
+        if (p.fuse_swiglu || p.fuse_gu_tc) {
             g.epilogue = fa::kEpiSwiglu; g.H = ctx->h16; g.H_lo = ctx->h_lo;
-            fa::launch_q8_gemv(g, s);
+            const bool ok = p.fuse_swiglu ? fa::launch_q8_gemv(g, s) : fa::launch_q8_gemm_tc_skinny(g, ctx->err_dev, s);
+            if (!ok) ctx->enqueue_failed = true;
             --n;
         } else {
             g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
             run_gemm(ctx, g);
-            fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s);
+            fa::launch_swiglu(ctx->part, p.s_gu, M, F, ctx->h16, ctx->h_lo, s, true);
         }
         g = fa::GemmArgs{};
         g.A = ctx->h16; g.A_lo = ctx->h_lo; g.W8 = fa::q8p_view(w.dn_q, H, F); g.M = M; g.N = H; g.K = F;
@@ -972,6 +1005,7 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
 // enqueue_step with programmatic dependent launch between its kernels when enabled
 static int enqueue_step_pdl(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     fa::set_launch_pdl(ctx->use_pdl);
+    ctx->enqueue_failed = false;
     const int n = enqueue_step(ctx, p, capturing);
     fa::set_launch_pdl(false);
     return n;
@@ -983,6 +1017,7 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
         if (int rc = ensure_prof_events(ctx)) return rc;
     if (!ctx->use_graphs) {
         ctx->last_launches = enqueue_step_pdl(ctx, p, false);
+        if (ctx->enqueue_failed) return set_err(ctx, FA_ERR_CUDA, "a fused GEMM launch declined its arguments");
         FA_CK(cudaGetLastError());
         ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
         return FA_OK;
@@ -994,9 +1029,10 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
         const int n = enqueue_step_pdl(ctx, p, true);
         cudaGraph_t graph = nullptr;
         cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
-        if (e != cudaSuccess) {
+        if (e != cudaSuccess || ctx->enqueue_failed) {
             if (graph) cudaGraphDestroy(graph);
-            return set_err(ctx, FA_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+            return set_err(ctx, FA_ERR_CUDA, ctx->enqueue_failed ? std::string("a fused GEMM launch declined its arguments")
+                                                                  : std::string("graph capture: ") + cudaGetErrorString(e));
         }
         cudaGraphExec_t exec = nullptr;
         e = cudaGraphInstantiate(&exec, graph, 0);

@@ -144,7 +144,10 @@ constexpr int kEncMaxFrames = 3000;   // frames per utterance and per batched pa
 // Kernel (4): Q8_0 weight GEMM on the tensor cores.  C[M][N] = A[M][K] . W[N][K]^T
 // kEpiSwiglu (small-M kernel only): W stacks gate rows [0, N/2) over up rows [N/2, N) and
 // the result is written as the f16 pair of silu(gate) * up, [M][N/2].
-enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1, kEpiSwiglu = 2 };
+// kEpiQkvAppend (swapped tcgen05 kernel, Q8_0, skinny_fusable shapes): the QKV GEMM finishes
+// kernel (1) itself (per-head RMSNorm, RoPE, q out, K / V into the pages) from *app.
+// kEpiSwiglu on the swapped kernel needs swiglu_interleave64 and skinny_fusable shapes.
+enum GemmEpilogue { kEpiStoreF32 = 0, kEpiArgmax = 1, kEpiSwiglu = 2, kEpiQkvAppend = 3 };
 struct GemmArgs {
     const __half* A;         // [M][K] f16 activations (hi part)
     const __half* A_lo;      // [M][K] f16 remainder x - hi, or nullptr (plain f16 activations)
@@ -158,6 +161,9 @@ struct GemmArgs {
     int* amax_idx;           //             [M][N/64] first column holding them
     __half* H;               // kEpiSwiglu: [M][N/2] hi part
     __half* H_lo;            //             [M][N/2] lo part (may be nullptr)
+    int swiglu_interleave64; // kEpiSwiglu: W stacks blocks of 64 gate rows and the 64 up rows of
+                             // the same columns (the decoder's layout) instead of gate over up
+    const struct AppendArgs* app;   // kEpiQkvAppend: kernel (1)'s arguments (qkv_part unused)
 };
 // mma.sync (m16n8k16) implementation; the cross-check variant.
 void launch_q8_gemm(const GemmArgs& g, cudaStream_t s);
@@ -176,6 +182,8 @@ constexpr int kSkinnyMaxRows = 128;
 constexpr int kSkinnyAutoRows = 128;
 constexpr int kSkinnyArgmaxAutoRows = 32;
 bool gemm_tc_skinny_supported(const GemmArgs& g);
+int skinny_tile_rows(int M);      // activation rows per tile the kernel takes for Q8_0 weights
+bool skinny_fusable(int M, int N, int K, int n_split, int n_sm);   // the fused epilogues apply
 int gemm_tc_skinny_pick_split(int M, int N, int K, int n_sm);
 bool launch_q8_gemm_tc_skinny(const GemmArgs& g, int* err, cudaStream_t s);
 // CUDA-core small-M kernel (k_gemv.cu): M <= kGemvMaxRows, n_split 1, K a multiple of 256;
@@ -196,8 +204,11 @@ void launch_embed(const void* table, int table_type, int hidden, const int* toke
 void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int hidden, const float* w,
                              float eps, __half* xn_hi, __half* xn_lo, cudaStream_t s, int n_out = -1,
                              const int* rows = nullptr);
-// (hi, lo)[m][j] = split(silu(g) * u), g and u summed over n_part partials of the gate|up GEMM
-void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s);
+// (hi, lo)[m][j] = split(silu(g) * u), g and u summed over n_part partials of the gate|up GEMM:
+// gate columns [0, ffn) and up columns [ffn, 2 ffn), or with interleave64 the decoder's
+// stacking, 64 gate columns then the 64 up columns of the same outputs, block after block
+void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s,
+                   bool interleave64 = false);
 // next[m] = first column of the row maximum over n_tiles partial maxima; optional feedback
 // of the token into tokens[m] and pos[m] += 1 for device-fed generation.
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,

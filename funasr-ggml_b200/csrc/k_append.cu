@@ -18,6 +18,7 @@
 // (l, l+64) and (l+32, l+96) stay in one lane. Memory-bound on nothing: a few KB
 // per row; it exists to avoid ~10 ggml launches and the f32 cache round trip.
 #include "fa_kernels.cuh"
+#include "k_append.cuh"
 
 namespace fa {
 
@@ -56,57 +57,7 @@ __global__ void __launch_bounds__(256) qknorm_rope_append_kernel(AppendArgs a) {
                 for (int k = 0; k < 4; ++k) x[k] = __fadd_rn(x[k], t[u][k]);
     }
 
-    const int pos = a.pos[m];
-    const bool is_q = j < a.Hq;
-    const bool is_k = !is_q && j < a.Hq + a.Hkv;
-    if (pos < 0 || pos >= a.max_pos) {
-        if (lane == 0) record_error(a.err, kDevErrBadPos);
-        return;
-    }
-
-    if (is_q || is_k) {
-        double ss = 0.0;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) ss += (double)__fmul_rn(x[k], x[k]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float mean = (float)(ss / (double)D);
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-        const float* w = is_q ? a.qn_w : a.kn_w;
-        float y[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) y[k] = __fmul_rn(__fmul_rn(x[k], scale), w[lane + 32 * k]);
-        const float2* cs = a.rope + (size_t)pos * (D / 2);
-        // pair (y[0], y[2]) uses rotation index lane, pair (y[1], y[3]) index lane + 32
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const float2 r = cs[lane + 32 * k];
-            const float x0 = y[k], x1 = y[k + 2];
-            y[k] = __fsub_rn(__fmul_rn(x0, r.x), __fmul_rn(x1, r.y));
-            y[k + 2] = __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x));
-        }
-        if (is_q) {
-            float* dst = a.q_out + ((size_t)m * a.Hq + j) * D;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = __fmul_rn(y[k], a.q_scale);
-            return;
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) x[k] = y[k];
-    }
-
-    // K (rotated) or V (as projected) into the page of this row's token.
-    const int h = is_k ? (j - a.Hq) : (j - a.Hq - a.Hkv);
-    const int kv = is_k ? 0 : 1;
-    const int page = a.block_table[(size_t)a.slot[m] * a.bt_stride + pos / kPageTokens];
-    if (page < 0 || page >= a.n_pages) {
-        if (lane == 0) record_error(a.err, kDevErrBadPage);
-        return;
-    }
-    __half* dst = a.pool_layer + (size_t)page * a.Hkv * 2 * kPageTokens * D +
-                  ((size_t)(h * 2 + kv) * kPageTokens + pos % kPageTokens) * D;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = __float2half_rn(x[k]);
+    qkv_head_finish(a, m, j, lane, x);
 }
 
 // Raw append: one warp copies one (row, layer, head) pair of 256 B K and 256 B V rows.

@@ -31,9 +31,12 @@
 // Every mbarrier wait is bounded; a wait that gives up records an error and the CTA
 // drains its copies and MMAs before freeing TMEM.
 #include "fa_kernels.cuh"
+#include "k_append.cuh"
 #include "tc_common.cuh"
 
 #include <cuda.h>
+
+#include <utility>
 
 namespace fa {
 
@@ -74,6 +77,7 @@ struct SkEpi {
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drain;
+    uint64_t rbar;                  // fused epilogues: the cluster peers' partial rows have arrived
     float amax_v[4][BNA];
     int amax_i[4][BNA];
     int got[4];                     // argmax epilogue: each warp's accumulator wait succeeded
@@ -151,8 +155,22 @@ __device__ __forceinline__ void q8_row_to_tmem(const int8_t* q, const __half* d,
     TMEM_ST_X32(taddr + 32, lo);
 }
 
+// Epilogue forms (template parameter EPI): fp32 split-K partials, lm_head per-tile argmax,
+// and two that finish the product inside a cluster of the n_split CTAs of one weight tile
+// (one unit per CTA): each CTA stages its partial tile in shared memory, and after a
+// cluster barrier CTA r sums rows [r, r+1) * BNA / n_split over the cluster's tiles
+// (distributed shared memory, split order) and applies the next op itself:
+//   EPI_QKV     the tile is one head vector of the QKV projection: per-head RMSNorm, RoPE,
+//               q to q_out, K / V into their pages (kernel (1), k_append.cuh)
+//   EPI_SWIGLU  the tile is 64 gate rows and the 64 up rows of the same outputs: SwiGLU,
+//               written as the down GEMM's f16 pair
+constexpr int EPI_STORE = 0, EPI_ARGMAX = 1, EPI_QKV = 2, EPI_SWIGLU = 3;
+
 struct SkArgs {
     int M, N, K, n_split, epilogue, has_lo;
+    AppendArgs app;                 // EPI_QKV
+    __half* H;                      // EPI_SWIGLU: [M][N/2] hi / lo
+    __half* H_lo;
     int n_wtiles;                   // N / 128 weight tiles
     int n_units;                    // weight tiles x splits x activation tiles of BNA rows
     float* C;
@@ -199,7 +217,30 @@ __device__ __forceinline__ void warp_argmax32_transpose(const uint32_t (&vb)[32]
 
 // tm_w: the f16 weights [N][K] (128 B swizzle), or for Q8_0 the q plane [N][K] uint8;
 // tm_d: Q8_0 only, the d_t plane [K/32][N] f16 (2 x 128 boxes).
-template <int BNA, bool Q8, bool AM>
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+    return out;
+}
+
+__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+template <int BNA, bool Q8, int EPI>
 __global__ void __launch_bounds__(threads_for<Q8>(), 1)
     q8_gemm_tc_skinny_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
                              const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_d,
@@ -236,6 +277,7 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
             mbar_init(&E.tempty[b], 128);
         }
         mbar_init(&E.drain, 1);
+        mbar_init(&E.rbar, 1);
         E.err = 0;
         E.issued = 0;
         E.consumed = 0;
@@ -252,6 +294,12 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
     tc_fence_after();
     const uint32_t tmem = E.tmem_base;
     pdl_trigger();
+
+    // EPI_QKV: the epilogue warps finish up to kPreRows rows each with the rows' metadata
+    // (position, page, rotation, norm weights) loaded during the MMAs
+    constexpr int kPreRows = 8;
+    HeadRowMeta meta[kPreRows];
+    const bool qkv_pre = EPI == EPI_QKV && (BNA / g.n_split + 3) / 4 <= kPreRows;
 
     int my_units = 0;
     for (int u = blockIdx.x; u < g.n_units; u += gridDim.x) ++my_units;
@@ -390,6 +438,27 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
         }
     } else {
         const int q = warp & 3;                 // TMEM lanes 32q..32q+31: weight rows of this warp
+        if constexpr (EPI == EPI_QKV) {
+            if (qkv_pre) {
+                // the metadata may come from the previous kernels: wait for them first
+                pdl_wait();
+                const int rpr = BNA / g.n_split;
+                const int t = blockIdx.x / g.n_split;
+                const int mrow0 = (t / g.n_wtiles) * BNA + (int)cluster_rank() * rpr;
+#pragma unroll
+                for (int r = 0; r < kPreRows; ++r) {
+                    const int i = (warp - 2) + 4 * r;
+                    if (i < rpr && mrow0 + i < g.M) meta[r] = qkv_head_meta(g.app, mrow0 + i, (t % g.n_wtiles), lane);
+                }
+                // consume the values here, so the loads (and the ones that depend on them) are
+                // issued and complete now, while the MMAs run, not where they are first used
+#pragma unroll
+                for (int r = 0; r < kPreRows; ++r)
+                    asm volatile("" ::"r"(meta[r].pos), "r"(meta[r].page), "f"(meta[r].rot[0].x), "f"(meta[r].rot[0].y),
+                                 "f"(meta[r].rot[1].x), "f"(meta[r].rot[1].y), "f"(meta[r].w[0]), "f"(meta[r].w[1]),
+                                 "f"(meta[r].w[2]), "f"(meta[r].w[3]));
+            }
+        }
         int j = 0;
         for (int u = blockIdx.x; u < g.n_units; u += gridDim.x, ++j) {
             const int split = u % g.n_split;
@@ -399,7 +468,7 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
             const int rows = min(BNA, g.M - m0);  // activation rows of this unit
             const int buf = j & 1;
             const bool got = __all_sync(0xffffffffu, mbar_wait_bounded(&E.tfull[buf], (uint32_t)(j >> 1) & 1u));
-            if (AM) {
+            if (EPI == EPI_ARGMAX) {
                 // the four warps meet at named barriers below: they leave together or not at all
                 if (lane == 0) E.got[q] = got ? 1 : 0;
                 epi_bar();
@@ -416,9 +485,15 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
             constexpr int CH = BNA < 32 ? BNA : 32;
             const int n = n0 + q * 32 + lane;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BNA);
-            float* out = g.C ? g.C + (AM ? 0 : (size_t)split * g.M * g.N) +
-                                   (size_t)m0 * g.N + n
-                             : nullptr;
+            constexpr bool FUSED = EPI == EPI_QKV || EPI == EPI_SWIGLU;
+            float* out = !FUSED && g.C ? g.C + (EPI == EPI_ARGMAX ? 0 : (size_t)split * g.M * g.N) +
+                                             (size_t)m0 * g.N + n
+                                       : nullptr;
+            // fused forms: the partial tile goes to shared memory [row][128 weight rows], over
+            // the raw ring (every stage of this CTA's one unit has been consumed by now; the
+            // proxy fence orders these writes after the tensor cores' reads of that memory)
+            float* stage = reinterpret_cast<float*>(&S.a_hi[0][0]);
+            if constexpr (FUSED) fence_proxy_async_smem();
 #pragma unroll 1
             for (int c0 = 0; c0 < BNA && c0 < rows; c0 += CH) {
                 uint32_t cur[CH];
@@ -433,7 +508,11 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
                     for (int m = 0; m < CH; ++m)
                         if (c0 + m < rows) out[(size_t)(c0 + m) * g.N] = __uint_as_float(cur[m]);
                 }
-                if constexpr (AM) {
+                if constexpr (FUSED) {
+#pragma unroll
+                    for (int m = 0; m < CH; ++m) stage[(c0 + m) * WM + q * 32 + lane] = __uint_as_float(cur[m]);
+                }
+                if constexpr (EPI == EPI_ARGMAX) {
                     if constexpr (CH == 32) {
                         // first maximum over this warp's 32 weight rows for all 32 activation
                         // rows at once: lane l ends with activation row c0 + l
@@ -459,9 +538,10 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
                     }
                 }
             }
+            if constexpr (FUSED) fence_proxy_async_smem();   // the staged tile is read by bulk copies
             tc_fence_before();
             mbar_arrive(&E.tempty[buf]);
-            if (AM) {
+            if (EPI == EPI_ARGMAX) {
                 // then over the two warps of each 64-row half
                 epi_bar();
                 for (int tt = threadIdx.x - 64; tt < 2 * BNA; tt += 128) {
@@ -490,6 +570,108 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
         }
         __syncthreads();
     }
+    if constexpr (EPI == EPI_QKV || EPI == EPI_SWIGLU) {
+        static_assert(Q8 && Smem::STAGES >= 4, "the staged tile lives over the raw ring of the Q8_0 form");
+        // Each CTA owns rows [rank, rank + 1) * rpr of the tile. After one cluster barrier
+        // (every CTA has staged its partial tile and its MMAs are done with the ring), CTA s
+        // pushes its partial rows of CTA r into r's receive slot s with one bulk copy; CTA r
+        // waits (bounded) for the bytes, then sums the partials in split order from its own
+        // shared memory. Every thread of every CTA passes the barrier, errors or not, and a
+        // CTA leaves only after its outgoing copies have read their source and its incoming
+        // copies have landed.
+        const int cs = g.n_split;
+        const uint32_t rank = cluster_rank();
+        const int t = blockIdx.x / g.n_split;
+        const int n0 = (t % g.n_wtiles) * WM;
+        const int m0 = (t / g.n_wtiles) * BNA;
+        const int rpr = BNA / cs;                          // rows this CTA finishes
+        const uint32_t slot_bytes = (uint32_t)rpr * WM * 4;
+        const float* stage = reinterpret_cast<const float*>(&S.a_hi[0][0]);
+        float* recv = reinterpret_cast<float*>(&S.a_lo[0][0]);
+        if (threadIdx.x == 0) mbar_arrive_expect_tx(&E.rbar, (uint32_t)(cs - 1) * slot_bytes);
+        cluster_sync_all();
+        if (threadIdx.x == 0) {
+            for (int r = 1; r < cs; ++r) {
+                const uint32_t peer = (rank + (uint32_t)r) % (uint32_t)cs;
+                const uint32_t dst = dsmem_addr(recv + (size_t)rank * rpr * WM, peer);
+                const uint32_t bar = dsmem_addr(&E.rbar, peer);
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        dst),
+                    "r"(smem_u32(stage + (size_t)peer * rpr * WM)), "r"(slot_bytes), "r"(bar)
+                    : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        const bool got = mbar_wait_bounded(&E.rbar, 0);
+        if (!got && lane == 0) E.err = 1;
+        if (got && !E.err) {
+            // partial s of local row i: this CTA's own staging for s == rank, else slot s
+            auto row = [&](int sp, int i) -> const float* {
+                return sp == (int)rank ? stage + (size_t)(rank * rpr + i) * WM : recv + (size_t)(sp * rpr + i) * WM;
+            };
+            if constexpr (EPI == EPI_QKV) {
+                if (qkv_pre) {
+                    if (warp >= 2 && warp < 6) {
+                        // the warp's rows ew, ew + 4, ... two at a time, side by side; a rolled
+                        // loop: this code runs once per launch, so its size costs instruction
+                        // fetches from L2, and a second unrolled copy would cost them again
+                        const int ew = warp - 2;
+                        constexpr int RB = 2;
+#pragma unroll 1
+                        for (int r0 = 0; r0 < kPreRows; r0 += RB) {
+                            float x[RB][4];
+                            int mr[RB];
+                            bool live[RB];
+#pragma unroll
+                            for (int r = 0; r < RB; ++r) {
+                                const int i = ew + 4 * (r0 + r);
+                                mr[r] = m0 + (int)rank * rpr + i;
+                                live[r] = i < rpr && mr[r] < g.M;
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) x[r][k] = 0.0f;
+                                if (!live[r]) continue;
+                                for (int sp = 0; sp < cs; ++sp) {
+                                    const float* src = row(sp, i) + lane;
+#pragma unroll
+                                    for (int k = 0; k < 4; ++k) x[r][k] = __fadd_rn(x[r][k], src[32 * k]);
+                                }
+                            }
+                            qkv_head_apply_rows<RB>(g.app, &meta[r0], mr, n0 / WM, lane, x, live);
+                        }
+                    }
+                } else {
+                    for (int i = warp; i < rpr && m0 + (int)rank * rpr + i < g.M; i += threads_for<Q8>() / 32) {
+                        float x[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        for (int sp = 0; sp < cs; ++sp) {
+                            const float* src = row(sp, i) + lane;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) x[k] = __fadd_rn(x[k], src[32 * k]);
+                        }
+                        qkv_head_finish(g.app, m0 + (int)rank * rpr + i, n0 / WM, lane, x);
+                    }
+                }
+            } else {
+                const int F = g.N / 2;
+                for (int i = warp; i < rpr && m0 + (int)rank * rpr + i < g.M; i += threads_for<Q8>() / 32) {
+                    float gs[2] = {0.0f, 0.0f}, us[2] = {0.0f, 0.0f};
+                    for (int sp = 0; sp < cs; ++sp) {
+                        const float* src = row(sp, i) + lane;
+#pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            gs[k] = __fadd_rn(gs[k], src[32 * k]);
+                            us[k] = __fadd_rn(us[k], src[64 + 32 * k]);
+                        }
+                    }
+                    const size_t o = (size_t)(m0 + (int)rank * rpr + i) * F + n0 / 2 + lane;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) split_store(silu_mul(gs[k], us[k]), g.H, g.H_lo, o + 32 * k);
+                }
+            }
+        }
+        if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncthreads();
+    }
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
@@ -499,6 +681,33 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
 template <int BNA, bool Q8>
 size_t skinny_smem() {
     return sizeof(SkSmem<BNA, Q8>) + 1024;
+}
+
+// launch_k with a cluster of `cluster` CTAs along x (and programmatic dependent launch when
+// the step enables it)
+template <typename... KArgs, typename... Args>
+cudaError_t launch_clustered(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             int cluster, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+    if (launch_pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 template <int BNA, bool Q8>
@@ -519,33 +728,79 @@ bool launch_bna(const GemmArgs& g, int* err, cudaStream_t s, int n_sm) {
     a.n_units = a.n_wtiles * g.n_split * ((g.M + BNA - 1) / BNA);
     a.C = g.C; a.amax_val = g.amax_val; a.amax_idx = g.amax_idx; a.err = err;
     const int grid = a.n_units < n_sm ? a.n_units : n_sm;
-    if (g.epilogue == kEpiArgmax)
-        launch_k(q8_gemm_tc_skinny_kernel<BNA, Q8, true>, dim3(grid), dim3(threads_for<Q8>()), skinny_smem<BNA, Q8>(),
-                 s, ta, tl, tw, td, a);
-    else
-        launch_k(q8_gemm_tc_skinny_kernel<BNA, Q8, false>, dim3(grid), dim3(threads_for<Q8>()), skinny_smem<BNA, Q8>(),
-                 s, ta, tl, tw, td, a);
+    const dim3 blk(threads_for<Q8>());
+    const size_t sm = skinny_smem<BNA, Q8>();
+    if (g.epilogue == kEpiArgmax) {
+        launch_k(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_ARGMAX>, dim3(grid), blk, sm, s, ta, tl, tw, td, a);
+    } else if (g.epilogue == kEpiStoreF32) {
+        launch_k(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_STORE>, dim3(grid), blk, sm, s, ta, tl, tw, td, a);
+    } else if constexpr (Q8) {
+        // fused forms: one unit per CTA, clusters of the n_split CTAs of each weight tile
+        if (!skinny_fusable(g.M, g.N, g.K, g.n_split, n_sm)) return false;
+        if (g.epilogue == kEpiQkvAppend) {
+            if (!g.app) return false;
+            a.app = *g.app;
+            launch_clustered(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_QKV>, dim3(a.n_units), blk, sm, s, g.n_split, ta,
+                             tl, tw, td, a);
+        } else if (g.epilogue == kEpiSwiglu) {
+            if (!g.H || !g.swiglu_interleave64) return false;
+            a.H = g.H;
+            a.H_lo = g.H_lo;
+            launch_clustered(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_SWIGLU>, dim3(a.n_units), blk, sm, s, g.n_split,
+                             ta, tl, tw, td, a);
+        } else {
+            return false;
+        }
+    } else {
+        return false;
+    }
     return true;
 }
 
 template <bool Q8>
 bool launch_rows(const GemmArgs& g, int* err, cudaStream_t s, int sms) {
-    if (g.M <= 16) return launch_bna<16, Q8>(g, err, s, sms);
-    if (g.M <= 32) return launch_bna<32, Q8>(g, err, s, sms);
-    if (g.M <= 64) return launch_bna<64, Q8>(g, err, s, sms);
-    return launch_bna<128, Q8>(g, err, s, sms);
+    switch (Q8 ? skinny_tile_rows(g.M) : (g.M <= 16 ? 16 : g.M <= 32 ? 32 : g.M <= 64 ? 64 : 128)) {
+        case 16: return launch_bna<16, Q8>(g, err, s, sms);
+        case 32: return launch_bna<32, Q8>(g, err, s, sms);
+        case 64: return launch_bna<64, Q8>(g, err, s, sms);
+        default: return launch_bna<128, Q8>(g, err, s, sms);
+    }
 }
 
 template <int BNA, bool Q8>
 void set_smem_attr() {
     static_assert(sizeof(SkSmem<BNA, Q8>) + 1024 <= 232448, "shared memory per CTA");
-    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)skinny_smem<BNA, Q8>());
-    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)skinny_smem<BNA, Q8>());
+    if constexpr (Q8) {
+        cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)skinny_smem<BNA, Q8>());
+        cudaFuncSetAttribute(q8_gemm_tc_skinny_kernel<BNA, Q8, EPI_SWIGLU>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)skinny_smem<BNA, Q8>());
+    }
 }
 
 }  // namespace
+
+// Whether the fused epilogues take a GEMM: Q8_0 weights, one activation tile (M <= 128),
+// one unit per CTA (weight tiles x n_split <= SMs) and a cluster of n_split CTAs (1 to 8)
+// that divides the tile's rows.
+bool skinny_fusable(int M, int N, int K, int n_split, int n_sm) {
+    if (M < 1 || M > kSkinnyMaxRows || N % WM || K % BK || n_split < 1 || n_split > 8 || (K / n_split) % BK)
+        return false;
+    if (n_split & (n_split - 1)) return false;
+    const int bna = skinny_tile_rows(M);
+    return (N / WM) * n_split <= n_sm && bna % n_split == 0;
+}
+
+// Activation rows per tile for Q8_0 weights: the smallest of 16 / 32 / 64 / 128 that holds
+// M, and 128-row tiles above 128 rows. (Two 64-row tiles at 65-128 rows, which would halve
+// the split-K partials, measured slower: the weight tile is then expanded twice.)
+int skinny_tile_rows(int M) {
+    return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+}
 
 void configure_gemm_tc_skinny() {
     set_smem_attr<16, false>();
@@ -564,8 +819,11 @@ bool gemm_tc_skinny_supported(const GemmArgs& g) {
     // 128-row activation tiles (the units then cover every (weight tile, activation tile))
     return w_ok && g.A != nullptr && g.M >= 1 && (g.W8.q || g.M <= kSkinnyMaxRows) && g.N % WM == 0 &&
            g.K % BK == 0 && g.n_split > 0 && (g.K / g.n_split) % BK == 0 &&
-           (g.epilogue == kEpiStoreF32 ? g.C != nullptr
-                                       : g.epilogue == kEpiArgmax && g.n_split == 1 && g.amax_val && g.amax_idx) &&
+           (g.epilogue == kEpiStoreF32    ? g.C != nullptr
+            : g.epilogue == kEpiArgmax    ? g.n_split == 1 && g.amax_val && g.amax_idx
+            : g.epilogue == kEpiQkvAppend ? g.W8.q && g.app != nullptr
+            : g.epilogue == kEpiSwiglu    ? g.W8.q && g.H && g.swiglu_interleave64
+                                          : false) &&
            tensor_maps_available();
 }
 
@@ -575,9 +833,10 @@ bool gemm_tc_skinny_supported(const GemmArgs& g) {
 // there are several (a prefill forward), where split partials of full tiles cost more than
 // the waves they save.
 int gemm_tc_skinny_pick_split(int M, int N, int K, int n_sm) {
-    const int m_tiles = (M + kSkinnyMaxRows - 1) / kSkinnyMaxRows;
+    const int bna = skinny_tile_rows(M);
+    const int m_tiles = (M + bna - 1) / bna;
     const int tiles = N / WM * m_tiles;
-    const int epi = m_tiles > 1 ? 8 : 2;
+    const int epi = M > kSkinnyMaxRows ? 8 : 2;
     const int kb = K / BK;
     int best = 1;
     long best_cost = -1;

@@ -44,6 +44,7 @@ struct GemvArgs {
     int ks;                          // warps sharing one row block's K range
     int G;                           // row blocks per CTA
     int epilogue;
+    int interleave64;                // SwiGLU: gate / up rows stacked in blocks of 64 each
     float* C;
     float* amax_val;
     int* amax_idx;
@@ -80,9 +81,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32) gemv_kernel(const GemvArgs a) 
     // SwiGLU: the first G/2 row blocks are gate rows, the others the up rows of the same columns
     const bool swiglu = a.epilogue == kEpiSwiglu;
     const int half_g = a.G / 2;
+    // (with interleave64: output column f of the gate rows is weight row (f/64)*128 + f%64,
+    // its up row 64 further; a block of 4 rows never crosses a 64-row boundary)
+    const int f0 = (blockIdx.x * half_g + (g < half_g ? g : g - half_g)) * kRowsPerWarp;
     const int n0 = !swiglu ? blockIdx.x * (a.G * kRowsPerWarp) + g * kRowsPerWarp
-                 : g < half_g ? (blockIdx.x * half_g + g) * kRowsPerWarp
-                              : a.N / 2 + (blockIdx.x * half_g + g - half_g) * kRowsPerWarp;
+                 : a.interleave64 ? (f0 / 64) * 128 + f0 % 64 + (g < half_g ? 0 : 64)
+                 : g < half_g ? f0 : a.N / 2 + f0;
     const int k0 = c * (NS * kSlice) + lane * WPL;
 
     WT w[NS][kRowsPerWarp];
@@ -302,7 +306,8 @@ bool launch_q8_gemv(const GemmArgs& g, cudaStream_t s) {
     GemvArgs a{};
     a.A = g.A; a.A_lo = g.A_lo; a.W = g.Wh; a.Wq = g.W8.q; a.Wd = g.W8.d_r;
     a.M = g.M; a.N = g.N; a.K = g.K; a.ks = ks; a.G = G;
-    a.epilogue = g.epilogue; a.C = g.epilogue == kEpiSwiglu ? nullptr : g.C; a.amax_val = g.amax_val;
+    a.epilogue = g.epilogue; a.interleave64 = g.swiglu_interleave64;
+    a.C = g.epilogue == kEpiSwiglu ? nullptr : g.C; a.amax_val = g.amax_val;
     a.amax_idx = g.amax_idx; a.H = g.H; a.H_lo = g.H_lo;
     if (!g.W8.q) launch_form<false, 8>(a, ns, s);
     else if (wpl_for(true, g.K) == 16) launch_form<true, 16>(a, ns, s);

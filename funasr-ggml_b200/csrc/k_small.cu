@@ -63,9 +63,11 @@ __global__ void __launch_bounds__(256) residual_rmsnorm_kernel(float* x, const f
                       [&](int j, float y) { split_store(y, xn_hi, xn_lo, o + j); });
 }
 
-// Thread per float4 group of one row's ffn outputs.
+// Thread per float4 group of one row's ffn outputs. Columns of a partial row: gate
+// [0, ffn) then up [ffn, 2 ffn), or with interleave64 blocks of 64 gate columns followed by
+// the 64 up columns of the same outputs (the decoder's stacking of the gate/up weights).
 __global__ void __launch_bounds__(256) swiglu_kernel(const float* part, int n_part, int M, int ffn,
-                                                     __half* h_hi, __half* h_lo) {
+                                                     __half* h_hi, __half* h_lo, int interleave64) {
     pdl_trigger();
     pdl_wait();
     const size_t idx = (size_t)blockIdx.x * 256 + threadIdx.x;
@@ -74,8 +76,10 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const float* part, int n_pa
     const int m = (int)(idx / f4), j = (int)(idx % f4);
     const float4* p = reinterpret_cast<const float4*>(part) + (size_t)m * 2 * f4;
     const size_t stride4 = (size_t)M * 2 * f4;
-    const float4 g = sum_parts4(p + j, stride4, n_part);
-    const float4 u = sum_parts4(p + f4 + j, stride4, n_part);
+    const int gj = interleave64 ? (j / 16) * 32 + j % 16 : j;
+    const int uj = interleave64 ? gj + 16 : f4 + j;
+    const float4 g = sum_parts4(p + gj, stride4, n_part);
+    const float4 u = sum_parts4(p + uj, stride4, n_part);
     const size_t o = (size_t)m * ffn + 4 * (size_t)j;
     split_store(silu_mul(g.x, u.x), h_hi, h_lo, o);
     split_store(silu_mul(g.y, u.y), h_hi, h_lo, o + 1);
@@ -137,11 +141,13 @@ __global__ void repack_q8_kernel(const uint8_t* raw, int N, int K, int r0, __hal
 // One thread per Q8_0 block: the 32 values go to q row r0 + n, the scale to both
 // scale planes (block-major d_t with row length n_total, row-major d_r).
 __global__ void repack_q8_planes_kernel(const uint8_t* raw, int N, int K, int r0, int n_total, int8_t* q,
-                                        __half* d_t, __half* d_r) {
+                                        __half* d_t, __half* d_r, int ileave) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int nb = K / kQK;
     if (i >= (size_t)N * nb) return;
-    const int n = (int)(i / nb), b = (int)(i % nb);
+    const int n_src = (int)(i / nb), b = (int)(i % nb);
+    // row n_src lands at r0 + n_src, or with ileave at r0 + blocks of ileave rows spaced 2 * ileave
+    const int n = ileave ? (n_src / ileave) * 2 * ileave + n_src % ileave : n_src;
     const uint8_t* blk = raw + i * kQBytes;
     const __half d = __ushort_as_half((uint16_t)blk[0] | ((uint16_t)blk[1] << 8));
     d_t[(size_t)b * n_total + r0 + n] = d;
@@ -223,9 +229,11 @@ void launch_residual_rmsnorm(float* x, const float* part, int n_part, int M, int
                  xn_lo, rows);
 }
 
-void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s) {
+void launch_swiglu(const float* part, int n_part, int M, int ffn, __half* h_hi, __half* h_lo, cudaStream_t s,
+                   bool interleave64) {
     const size_t n = (size_t)M * (ffn / 4);
-    launch_k(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part, n_part, M, ffn, h_hi, h_lo);
+    launch_k(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, part, n_part, M, ffn, h_hi, h_lo,
+             interleave64 ? 1 : 0);
 }
 
 void launch_argmax_reduce(const float* val, const int* idx, int M, int n_tiles, int* next, int* feed_tokens,
@@ -243,12 +251,13 @@ void launch_repack_q8(const uint8_t* raw, int N, int K, int r0, __half* dst_w, c
     repack_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(raw, N, K, r0, dst_w);
 }
 
-void launch_repack_q8_planes(const uint8_t* raw, int N, int K, int r0, int n_total, void* planes, cudaStream_t s) {
+void launch_repack_q8_planes(const uint8_t* raw, int N, int K, int r0, int n_total, void* planes, cudaStream_t s,
+                             int interleave) {
     const size_t n = (size_t)N * (K / kQK);
     unsigned char* b = static_cast<unsigned char*>(planes);
     repack_q8_planes_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         raw, N, K, r0, n_total, reinterpret_cast<int8_t*>(b), reinterpret_cast<__half*>(b + q8p_dt_offset(n_total, K)),
-        reinterpret_cast<__half*>(b + q8p_dr_offset(n_total, K)));
+        reinterpret_cast<__half*>(b + q8p_dr_offset(n_total, K)), interleave);
 }
 
 void launch_page_copy(__half* pool, size_t layer_stride, int n_layers, const int* src, const int* dst, int n,

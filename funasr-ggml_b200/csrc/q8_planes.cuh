@@ -110,7 +110,9 @@ __device__ __forceinline__ void q8_stage_to_hilo(const int8_t* q, const __half* 
 }
 
 // Host: repack GGUF Q8_0 blocks [N][K/32][34 B] into the planes of a stacked matrix of
-// n_total rows at row offset r0 (k_small.cu).
-void launch_repack_q8_planes(const uint8_t* raw, int N, int K, int r0, int n_total, void* planes, cudaStream_t s);
+// n_total rows at row offset r0 (k_small.cu); with interleave > 0 source row n goes to
+// r0 + (n / interleave) * 2 * interleave + n % interleave (two matrices in alternating blocks).
+void launch_repack_q8_planes(const uint8_t* raw, int N, int K, int r0, int n_total, void* planes, cudaStream_t s,
+                             int interleave = 0);
 
 }  // namespace fa

@@ -107,6 +107,7 @@ def lib():
         "fa_set_stream": ([_P, _P], _I),
         "fa_set_graphs": ([_P, _I], _I),
         "fa_set_gemm_variant": ([_P, _I], _I),
+        "fa_set_fused_epilogues": ([_P, _I], _I),
         "fa_set_pdl": ([_P, _I], _I),
         "fa_pool_info": ([_P, _P, _P, _P], _I),
         "fa_seq_open": ([_P, _I, _P], _I),
@@ -287,11 +288,16 @@ class Decoder:
         self._c(lib().fa_set_stream(self.ctx, stream_ptr))
 
     def set_gemm_variant(self, variant: int):
-        """0 (default): small-M CUDA-core GEMM up to 2 rows, swapped tcgen05 up to 128 (lm_head
-        argmax up to 32), the 128-row-tile tcgen05 GEMM above; 1: mma.sync GEMM (cross-check);
-        2: 128-row-tile tcgen05 at every M; 3: small-M kernel up to 8 rows; 4: swapped tcgen05
-        up to 128 rows."""
+        """0 (default): small-M CUDA-core GEMM up to 2 rows, the swapped tcgen05 GEMM above (in
+        128-row activation tiles); 1: mma.sync GEMM (cross-check); 2: 128-row-tile tcgen05 at
+        every M; 3: small-M kernel up to 8 rows; 4: swapped tcgen05 at every M."""
         self._c(lib().fa_set_gemm_variant(self.ctx, int(variant)))
+
+    def set_fused_epilogues(self, mask: int):
+        """Mask of projections finished inside the tcgen05 GEMM: 1 = QKV with per-head
+        norm/RoPE/append, 2 = gate/up with SwiGLU (default 2); 0 = separate kernels. Same
+        bits either way."""
+        self._c(lib().fa_set_fused_epilogues(self.ctx, int(mask)))
 
     def set_pdl(self, enable: bool):
         self._c(lib().fa_set_pdl(self.ctx, int(enable)))

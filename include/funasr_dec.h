@@ -115,12 +115,19 @@ FA_API int fa_load_gguf(fa_ctx* ctx, const char* path);
  * the library's own stream. */
 FA_API int fa_set_stream(fa_ctx* ctx, void* cuda_stream);
 /* GEMM implementation: 0 = default: the CUDA-core small-M kernel for steps of up to 2
- * rows, the tcgen05 kernel with swapped operands (weights on the MMA's 128-row side) up
- * to 128 rows (the lm_head argmax up to 32), the tcgen05/TMEM/TMA kernel with 128-row
- * activation tiles above; 1 = mma.sync kernel (same arithmetic; kept to cross-check);
- * 2 = the 128-row-tile tcgen05 kernel at every M; 3 = the small-M kernel up to 8 rows,
- * else as 2; 4 = the swapped tcgen05 kernel up to 128 rows, else as 2. */
+ * rows, the tcgen05 kernel with swapped operands (weights on the MMA's 128-row side,
+ * expanded from Q8_0 into TMEM) above, in 128-row activation tiles; 1 = mma.sync kernel
+ * (same arithmetic; kept to cross-check); 2 = the 128-row-tile tcgen05 kernel at every M;
+ * 3 = the small-M kernel up to 8 rows, else as 2; 4 = the swapped tcgen05 kernel at every
+ * M. */
 FA_API int fa_set_gemm_variant(fa_ctx* ctx, int variant);
+/* Which projections of steps of up to 128 rows on the swapped tcgen05 kernel finish their
+ * next op inside the GEMM, in clusters of its split-K CTAs (a mask): bit 0 = the QKV
+ * projection with kernel (1) (per-head norm, RoPE, K/V append), bit 1 = the gate/up
+ * projection with SwiGLU. Default 2 (SwiGLU only); 0 = separate kernels. The results are
+ * the same bits either way. No counterpart in the reference (ggml runs each node
+ * separately, compute/llm_ops_gpu.cpp:53-96,177-180). */
+FA_API int fa_set_fused_epilogues(fa_ctx* ctx, int mask);
 /* 1 = programmatic dependent launch between a step's kernels (default): each kernel's
  * prologue overlaps the previous kernel's tail. 0 = plain stream order. */
 FA_API int fa_set_pdl(fa_ctx* ctx, int enable);

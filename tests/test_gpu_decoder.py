@@ -149,6 +149,41 @@ def test_gemm_variants_agree_end_to_end(torch_cuda, small_w):
     assert_close(outs[0], outs[1], max_abs_tol=2e-3, rel_rms_tol=1e-5, what="tcgen05 vs mma.sync")
 
 
+@pytest.mark.parametrize("n_seq", [3, 16, 100])
+def test_fused_gemm_epilogues_give_the_same_bits(torch_cuda, small_w, n_seq):
+    """QKV with kernel (1) and gate/up with SwiGLU finished inside the tcgen05 GEMM's clusters
+    (split-K partials pushed between the cluster's CTAs by bulk copies and summed in split
+    order), each alone and both, against the separate kernels: identical logits, tokens and
+    K/V pages, at 3, 16 and 100 rows a step."""
+    w = small_w
+    rng = np.random.default_rng(31 + n_seq)
+    L = 8
+    prompt = rng.integers(0, CFG["vocab"], (n_seq, L))
+    out = {}
+    for fused in (3, 2, 1, 0):
+        dec = _decoder(w, CFG, n_pages=1024, max_seqs=128, max_rows=1024)
+        dec.set_fused_epilogues(fused)
+        sids = [dec.seq_open(MAX_CTX) for _ in range(n_seq)]
+        nxt, lg0 = dec.forward(np.repeat(sids, L), tokens=prompt.reshape(-1), want_logits=True)
+        toks = nxt[L - 1::L]
+        lgs, ids = [lg0], []
+        for _ in range(4):
+            toks, lg = dec.decode_step(sids, toks, want_logits=True)
+            lgs.append(lg)
+            ids.append(toks)
+        pages = [dec.kv_read_pages(l, np.concatenate([dec.block_table(x) for x in sids]))
+                 for l in (0, CFG["n_layers"] - 1)]
+        out[fused] = (lgs, ids, pages)
+        dec.close()
+    for mask in (3, 2, 1):
+        for a, b in zip(out[mask][0], out[0][0]):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), mask
+        for a, b in zip(out[mask][1], out[0][1]):
+            assert np.array_equal(a, b), mask
+        for a, b in zip(out[mask][2], out[0][2]):
+            assert np.array_equal(a, b), mask
+
+
 def test_pool_exhaustion_rolls_back(torch_cuda, small_w):
     dec = _decoder(small_w, CFG, n_pages=4)
     a = dec.seq_open(MAX_CTX)
