@@ -45,10 +45,29 @@ struct AttnSmem {
     __half tiles[WARPS][STAGES][TILE_HALVES];
     uint64_t bars[WARPS][STAGES];
     float q[2][D];
-    float pbuf[WARPS][32];
+    float2 pbuf[WARPS][32];         // each p twice: the PV products take it as a packed pair
     float acc[WARPS][2][D];
     float ml[WARPS][4];
 };
+
+// Two fp32 fused multiply-adds in one instruction (sm_100 packs a pair of fp32 lanes): each
+// half is the same correctly rounded fma as fmaf, so results do not change.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
+          "l"(*reinterpret_cast<unsigned long long*>(&c)));
+    return *reinterpret_cast<float2*>(&r);
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
+    return *reinterpret_cast<float2*>(&r);
+}
 
 __device__ __forceinline__ void load8(const __half* p, float (&f)[8]) {
     const uint4 v = lds128(p);
@@ -160,16 +179,19 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
 
     const int c = lane & 15;
     const int par = lane >> 4;
-    float q0[8], q1[8];
+    // q of both heads for this lane's 8 dims, each value twice: a QK product runs two
+    // tokens' dot products side by side (packed fp32 pairs), in the same order as one at a time
+    float2 q0[8], q1[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        q0[k] = S.q[0][8 * c + k];
-        q1[k] = S.q[1][8 * c + k];
+        q0[k] = make_float2(S.q[0][8 * c + k], S.q[0][8 * c + k]);
+        q1[k] = make_float2(S.q[1][8 * c + k], S.q[1][8 * c + k]);
     }
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-    float acc0[8], acc1[8];
+    // PV accumulators of the lane's 8 dims as 4 packed pairs per head
+    float2 acc0[4], acc1[4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) { acc0[k] = 0.0f; acc1[k] = 0.0f; }
+    for (int k = 0; k < 4; ++k) { acc0[k] = make_float2(0.0f, 0.0f); acc1[k] = make_float2(0.0f, 0.0f); }
 
     const size_t page_elems = (size_t)a.Hkv * TILE_HALVES;
     const __half* head_base = a.pool_layer + (size_t)h * TILE_HALVES;
@@ -199,17 +221,22 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
 
         float part[16];
 #pragma unroll
-        for (int ii = 0; ii < 8; ++ii) {
-            float f[8];
-            load8(Kt + (2 * ii + par) * D + 8 * c, f);
-            float s0 = 0.0f, s1 = 0.0f;
+        for (int ii = 0; ii < 8; ii += 2) {
+            // tokens 2ii+par and 2(ii+1)+par side by side
+            float fa[8], fb[8];
+            load8(Kt + (2 * ii + par) * D + 8 * c, fa);
+            load8(Kt + (2 * ii + 2 + par) * D + 8 * c, fb);
+            float2 s0 = make_float2(0.0f, 0.0f), s1 = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                s0 = fmaf(q0[k], f[k], s0);
-                s1 = fmaf(q1[k], f[k], s1);
+                const float2 kk = make_float2(fa[k], fb[k]);
+                s0 = ffma2(q0[k], kk, s0);
+                s1 = ffma2(q1[k], kk, s1);
             }
-            part[2 * ii] = s0;
-            part[2 * ii + 1] = s1;
+            part[2 * ii] = s0.x;
+            part[2 * ii + 1] = s1.x;
+            part[2 * ii + 2] = s0.y;
+            part[2 * ii + 3] = s1.y;
         }
         const float tot = transpose_reduce16(part, lane);
         const int r = lane & 15;
@@ -235,29 +262,34 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
         m0 = mn0;
         m1 = mn1;
 
-        S.pbuf[warp][lane] = p;   // lane index = par*16 + 2*ii + hh
+        S.pbuf[warp][lane] = make_float2(p, p);   // lane index = par*16 + 2*ii + hh
         __syncwarp();
-        float pv[16];
+        float2 pv[16];
         {
             const float4* pb = reinterpret_cast<const float4*>(&S.pbuf[warp][par * 16]);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < 8; ++k) {
                 const float4 t = pb[k];
-                pv[4 * k] = t.x; pv[4 * k + 1] = t.y; pv[4 * k + 2] = t.z; pv[4 * k + 3] = t.w;
+                pv[2 * k] = make_float2(t.x, t.y);
+                pv[2 * k + 1] = make_float2(t.z, t.w);
             }
         }
+        {
+            const float2 a0 = make_float2(al0, al0), a1 = make_float2(al1, al1);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) { acc0[k] *= al0; acc1[k] *= al1; }
+            for (int k = 0; k < 4; ++k) { acc0[k] = fmul2(acc0[k], a0); acc1[k] = fmul2(acc1[k], a1); }
+        }
 #pragma unroll
         for (int ii = 0; ii < 8; ++ii) {
             if (2 * ii + par < nvalid) {
                 float f[8];
                 load8(Vt + (2 * ii + par) * D + 8 * c, f);
-                const float pa = pv[2 * ii], pb = pv[2 * ii + 1];
+                const float2 pa = pv[2 * ii], pb = pv[2 * ii + 1];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    acc0[k] = fmaf(pa, f[k], acc0[k]);
-                    acc1[k] = fmaf(pb, f[k], acc1[k]);
+                for (int k = 0; k < 4; ++k) {
+                    const float2 vv = make_float2(f[2 * k], f[2 * k + 1]);
+                    acc0[k] = ffma2(pa, vv, acc0[k]);
+                    acc1[k] = ffma2(pb, vv, acc1[k]);
                 }
             }
         }
@@ -282,19 +314,25 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
         m0 = m1 = -INFINITY;
         l0 = l1 = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) { acc0[k] = 0.0f; acc1[k] = 0.0f; }
+        for (int k = 0; k < 4; ++k) { acc0[k] = make_float2(0.0f, 0.0f); acc1[k] = make_float2(0.0f, 0.0f); }
     }
 
+    float o0[8], o1[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        o0[2 * k] = acc0[k].x; o0[2 * k + 1] = acc0[k].y;
+        o1[2 * k] = acc1[k].x; o1[2 * k + 1] = acc1[k].y;
+    }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        acc0[k] += __shfl_xor_sync(0xffffffffu, acc0[k], 16);
-        acc1[k] += __shfl_xor_sync(0xffffffffu, acc1[k], 16);
+        o0[k] += __shfl_xor_sync(0xffffffffu, o0[k], 16);
+        o1[k] += __shfl_xor_sync(0xffffffffu, o1[k], 16);
     }
     if (lane < 16) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            S.acc[warp][0][8 * c + k] = acc0[k];
-            S.acc[warp][1][8 * c + k] = acc1[k];
+            S.acc[warp][0][8 * c + k] = o0[k];
+            S.acc[warp][1][8 * c + k] = o1[k];
         }
     }
     if (lane == 0) {
