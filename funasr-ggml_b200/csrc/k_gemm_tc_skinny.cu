@@ -25,7 +25,7 @@
 //               N=BNA, K=16, every product of a stage into one accumulator
 //   warps 2..5  epilogue: TMEM lanes 32*(warp%4).. are weight rows, columns are
 //               activation rows; each warp writes 128 B runs of one activation row
-//   warps 6..9  (Q8_0) expand each stage's q tile, a weight row per thread, into the
+//   warps 6..13 (Q8_0) expand each stage's q tile, half a weight row per thread, into the
 //               W_hi / W_lo pair in a TMEM slot (tcgen05.st) that the MMAs read as their
 //               A operand; the raw stage and the slot are released when those MMAs complete
 // Every mbarrier wait is bounded; a wait that gives up records an error and the CTA
@@ -44,7 +44,7 @@ namespace {
 
 constexpr int WM = 128;             // weight rows per unit
 constexpr int BK = 64;
-constexpr int CONV_THREADS = 128;   // Q8_0: warps 6..9 expand q into the f16 pair
+constexpr int CONV_THREADS = 256;   // Q8_0: warps 6..13 expand q into the f16 pair
 
 template <bool Q8>
 __host__ __device__ constexpr int threads_for() {
@@ -132,34 +132,36 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, 
         : "memory");
 }
 
-// One row (TMEM lane) of a raw stage -> the f16 pair of its 64 weights in TMEM slot columns
-// [col, col + 32) (hi) and [col + 32, col + 64) (lo). The q row is read with the 64 B
-// swizzle its TMA box was written with: chunk c of row r sits at chunk c ^ ((r >> 1) & 3).
-__device__ __forceinline__ void q8_row_to_tmem(const int8_t* q, const __half* d, int r, uint32_t taddr) {
-    uint32_t hi[32], lo[32];
+// Half a row (32 of the stage's 64 K values, half h) of a raw stage -> the f16 pair of those
+// weights in TMEM slot columns [col + 16h, col + 16h + 16) (hi) and [col + 32 + 16h, ...)
+// (lo). The q row is read with the 64 B swizzle its TMA box was written with: chunk c of
+// row r sits at chunk c ^ ((r >> 1) & 3).
+__device__ __forceinline__ void q8_halfrow_to_tmem(const int8_t* q, const __half* d, int r, int h, uint32_t taddr) {
+    uint32_t hi[16], lo[16];
     const unsigned char* row = reinterpret_cast<const unsigned char*>(q) + r * 64;
+    const __half dv = d[h * WM + r];              // K [32h, 32h + 32) is Q8_0 block h of the stage
+    const __half2 d2 = __halves2half2(dv, dv);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * h + cc;
         const uint4 v = lds128(row + ((c ^ ((r >> 1) & 3)) << 4));
-        const __half dv = d[(c >> 1) * WM + r];
-        const __half2 d2 = __halves2half2(dv, dv);
         uint4 h0, l0, h1, l1;
         q8x8_to_hilo(v.x, v.y, d2, h0, l0);
         q8x8_to_hilo(v.z, v.w, d2, h1, l1);
-        hi[8 * c + 0] = h0.x; hi[8 * c + 1] = h0.y; hi[8 * c + 2] = h0.z; hi[8 * c + 3] = h0.w;
-        hi[8 * c + 4] = h1.x; hi[8 * c + 5] = h1.y; hi[8 * c + 6] = h1.z; hi[8 * c + 7] = h1.w;
-        lo[8 * c + 0] = l0.x; lo[8 * c + 1] = l0.y; lo[8 * c + 2] = l0.z; lo[8 * c + 3] = l0.w;
-        lo[8 * c + 4] = l1.x; lo[8 * c + 5] = l1.y; lo[8 * c + 6] = l1.z; lo[8 * c + 7] = l1.w;
+        hi[8 * cc + 0] = h0.x; hi[8 * cc + 1] = h0.y; hi[8 * cc + 2] = h0.z; hi[8 * cc + 3] = h0.w;
+        hi[8 * cc + 4] = h1.x; hi[8 * cc + 5] = h1.y; hi[8 * cc + 6] = h1.z; hi[8 * cc + 7] = h1.w;
+        lo[8 * cc + 0] = l0.x; lo[8 * cc + 1] = l0.y; lo[8 * cc + 2] = l0.z; lo[8 * cc + 3] = l0.w;
+        lo[8 * cc + 4] = l1.x; lo[8 * cc + 5] = l1.y; lo[8 * cc + 6] = l1.z; lo[8 * cc + 7] = l1.w;
     }
-    TMEM_ST_X32(taddr, hi);
-    TMEM_ST_X32(taddr + 32, lo);
+    TMEM_ST_X16(taddr + 16u * h, hi);
+    TMEM_ST_X16(taddr + 32u + 16u * h, lo);
 }
 
 // Epilogue forms (template parameter EPI): fp32 split-K partials, lm_head per-tile argmax,
 // and two that finish the product inside a cluster of the n_split CTAs of one weight tile
-// (one unit per CTA): each CTA stages its partial tile in shared memory, and after a
-// cluster barrier CTA r sums rows [r, r+1) * BNA / n_split over the cluster's tiles
-// (distributed shared memory, split order) and applies the next op itself:
+// (one unit per CTA): each CTA stages its partial tile in shared memory, the CTAs exchange
+// the rows each finishes (bulk copies between their shared memories) and each sums its
+// rows over the cluster's tiles in split order and applies the next op itself:
 //   EPI_QKV     the tile is one head vector of the QKV projection: per-head RMSNorm, RoPE,
 //               q to q_out, K / V into their pages (kernel (1), k_append.cuh)
 //   EPI_SWIGLU  the tile is 64 gate rows and the 64 up rows of the same outputs: SwiGLU,
@@ -232,12 +234,6 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
     uint32_t out;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
     return out;
-}
-
-__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
 }
 
 template <int BNA, bool Q8, int EPI>
@@ -415,9 +411,10 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
     } else if (warp >= 6) {
         if constexpr (Q8) {
             // converters: raw stage it (q, scales) -> TMEM slot it % CSTAGES; a warp may only
-            // reach its own quarter of the lanes, so thread (warp w, lane l) expands weight
-            // row 32 * (w % 4) + l
+            // reach its own quarter of the lanes, so thread (warp w, lane l) expands half h =
+            // (w - 6) / 4 (K values [32h, 32h + 32)) of weight row 32 * (w % 4) + l
             const int r = 32 * (warp & 3) + lane;
+            const int half = (warp - 6) >> 2;
             const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
             for (int it = 0; it < total; ++it) {
                 const int s = it % STAGES;
@@ -430,7 +427,7 @@ __global__ void __launch_bounds__(threads_for<Q8>(), 1)
                     break;
                 }
                 tc_fence_after();
-                q8_row_to_tmem(S.q[s], S.d[s], r, lane_base + kConvCol0 + (uint32_t)cs * kConvSlotCols);
+                q8_halfrow_to_tmem(S.q[s], S.d[s], r, half, lane_base + kConvCol0 + (uint32_t)cs * kConvSlotCols);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&S.cfull[cs]);

@@ -108,6 +108,13 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
         "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])                     \
         : "memory")
 
+#define TMEM_ST_X16(taddr, v)                                                                                  \
+    asm volatile(                                                                                              \
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" \
+        ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),    \
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])             \
+        : "memory")
+
 // Host: 2-D f16 row-major [rows][cols] tensor map with a (box_cols x box_rows) box,
 // 128 B swizzle when `swizzle`. False when the driver entry point is missing or the
 // encoder rejects the arguments.
