@@ -23,7 +23,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libfunasr_dec.so")
 INCLUDE = os.path.join(ROOT, "include")
 
-SOURCES = ["fa_api.cu", "k_append.cu", "k_attention.cu", "k_prefill_attn.cu", "k_gemm.cu", "k_gemm_tc.cu", "k_gemm_tc_skinny.cu", "k_gemv.cu", "k_small.cu",
+SOURCES = ["fa_api.cu", "k_append.cu", "k_attention.cu", "k_prefill_attn.cu", "k_gemm.cu", "k_gemm_tc.cu", "k_gemm_tc_skinny.cu", "k_gemv.cu", "k_row_step.cu", "k_small.cu",
            "gguf_file.cpp", "scheduler.cpp", "k_encoder.cu", "fa_encoder.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

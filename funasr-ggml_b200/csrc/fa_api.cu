@@ -92,6 +92,7 @@ static int ensure_configured() {
         fa::configure_gemm_tc();
         fa::configure_gemm_tc_skinny();
         fa::configure_prefill_attention();
+        fa::configure_row_step();
         g_configured[dev] = true;
     }
     return FA_OK;
@@ -167,6 +168,16 @@ struct fa_ctx {
     int fuse_epilogues = 2;
     bool enqueue_failed = false; // a planned launch declined its arguments while a step was enqueued
     bool use_pdl = true;       // programmatic dependent launch between the step's kernels
+    // one-row steps as one persistent kernel (k_row_step.cu) when the shapes allow it
+    bool row_step_on = true;
+    bool row_ready = false;    // buffers and the layer table below exist
+    fa::RowGemm row_gm[4] = {};
+    fa::RowLayer* row_layers = nullptr;
+    float* x_b = nullptr;
+    fa::RowCtl* row_ctl = nullptr;
+    int row_absent_cta = -1;   // failure test (fa_set_row_step_fault)
+    unsigned long long row_wait_ns = fa::kWaitLimitNs;
+    std::string enqueue_msg;   // why a planned launch failed while a step was enqueued
     int gemm_variant = 0;      // 0: CUDA-core kernel up to 2 rows, swapped tcgen05 up to 128 (lm_head: 32),
                                // 128-row-tile tcgen05 above; 1: mma.sync; 2: 128-row-tile tcgen05;
                                // 3: CUDA-core up to 8 rows, else 2; 4: swapped tcgen05 up to 128, else 2
@@ -443,6 +454,21 @@ extern "C" int fa_set_fused_epilogues(fa_ctx* ctx, int enable) {
     return FA_OK;
 }
 
+extern "C" int fa_set_row_step(fa_ctx* ctx, int enable) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    ctx->row_step_on = enable != 0;
+    clear_graphs(ctx);
+    return FA_OK;
+}
+
+extern "C" int fa_set_row_step_fault(fa_ctx* ctx, int absent_cta, int wait_us) {
+    if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
+    ctx->row_absent_cta = absent_cta < 0 ? -1 : absent_cta;
+    ctx->row_wait_ns = wait_us > 0 ? (unsigned long long)wait_us * 1000ull : fa::kWaitLimitNs;
+    clear_graphs(ctx);
+    return FA_OK;
+}
+
 extern "C" int fa_set_graphs(fa_ctx* ctx, int enable) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
     ctx->use_graphs = enable != 0;
@@ -539,6 +565,32 @@ static int upload_q8(fa_ctx* ctx, const fa_tensor_view* v, uint8_t* staging, int
     return FA_OK;
 }
 
+// Buffers and the per-layer weight table of the one-row step kernel, when it takes the
+// model's shapes (else one-row steps run launch by launch).
+static int setup_row_step(fa_ctx* ctx) {
+    const fa_model_desc& d = ctx->d;
+    if (!fa::row_step_shapes(d.hidden, d.ffn, ctx->n_sm, ctx->row_gm)) return FA_OK;
+    int attr = 0;
+    if (cudaDeviceGetAttribute(&attr, cudaDevAttrCooperativeLaunch, ctx->device) != cudaSuccess || !attr) {
+        cudaGetLastError();
+        return FA_OK;
+    }
+    std::vector<fa::RowLayer> tab(d.n_layers);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const LayerW& w = ctx->L[l];
+        tab[l].w[0] = w.qkv_q; tab[l].w[1] = w.o_q; tab[l].w[2] = w.gu_q; tab[l].w[3] = w.dn_q;
+        tab[l].in_norm = w.in_norm; tab[l].post_norm = w.post_norm; tab[l].q_norm = w.q_norm; tab[l].k_norm = w.k_norm;
+    }
+    int r;
+    if ((r = dev_alloc(ctx, &ctx->row_layers, sizeof(fa::RowLayer) * tab.size())) ||
+        (r = dev_alloc(ctx, &ctx->x_b, sizeof(float) * d.hidden)) || (r = dev_alloc(ctx, &ctx->row_ctl, sizeof(fa::RowCtl))))
+        return r;
+    FA_CK(cudaMemcpy(ctx->row_layers, tab.data(), sizeof(fa::RowLayer) * tab.size(), cudaMemcpyHostToDevice));
+    FA_CK(cudaMemset(ctx->row_ctl, 0, sizeof(fa::RowCtl)));
+    ctx->row_ready = true;
+    return FA_OK;
+}
+
 extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n) {
     if (!ctx || (!tensors && n > 0)) return set_err(ctx, FA_ERR_INVALID_ARG, "bad arguments");
     if (ctx->loaded) return set_err(ctx, FA_ERR_INVALID_ARG, "weights already loaded");
@@ -615,7 +667,7 @@ extern "C" int fa_load_weights(fa_ctx* ctx, const fa_tensor_view* tensors, int n
         if ((r = dev_alloc(ctx, (uint8_t**)&ctx->embed, emb->nbytes))) return r;
         FA_CK(cudaMemcpy(ctx->embed, emb->data, emb->nbytes, cudaMemcpyHostToDevice));
         ctx->embed_type = emb->type;
-        return FA_OK;
+        return setup_row_step(ctx);
     };
     rc = run();
     // host -> device copies from pageable memory can return before their DMA lands, and
@@ -754,9 +806,11 @@ struct StepPlan {
     bool fuse_swiglu = false;  // gate/up GEMM on the small-M kernel writes SwiGLU's output itself
     bool fuse_gu_tc = false;   // gate/up GEMM on the tcgen05 kernel finishes SwiGLU in its clusters
     bool fuse_qkv = false;     // QKV GEMM on the tcgen05 kernel finishes kernel (1) in its clusters
+    bool row_step = false;     // one row: the persistent step kernel, then lm_head and argmax
     std::array<int, 12> key() const {
         return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, n_out,
-                (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 + (int)fuse_swiglu * 4 + (int)embeds * 2 + (int)logits,
+                (int)row_step * 32 + (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 + (int)fuse_swiglu * 4 +
+                    (int)embeds * 2 + (int)logits,
                 (int)prof};
     }
 };
@@ -848,6 +902,9 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     p.embeds = embeds;
     p.logits = logits;
     p.prof = ctx->prof;
+    // one decode row, CUDA-core GEMM arithmetic, every attention item on its own SM
+    p.row_step = ctx->row_ready && ctx->row_step_on && M == 1 && n_tiles == 0 && p.n_dec == 1 && !p.prof &&
+                 gemv_rows(ctx->gemm_variant, 1) && p.n_splits * kHkv <= ctx->n_sm;
     return p;
 }
 
@@ -892,8 +949,12 @@ static void run_gemm(fa_ctx* ctx, const fa::GemmArgs& g) {
     fa::launch_q8_gemm(g, ctx->stream);
 }
 
+static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p);
+static int enqueue_lm_head(fa_ctx* ctx, const StepPlan& p, int Mo);
+
 // Enqueue the kernels of one forward step. Returns the number of launches.
 static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
+    if (p.row_step) return enqueue_row_step(ctx, p);
     const fa_model_desc& d = ctx->d;
     cudaStream_t s = ctx->stream;
     const int M = p.M, H = d.hidden, F = d.ffn;
@@ -990,25 +1051,70 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     if (Mo == 0) return n;
     fa::launch_residual_rmsnorm(ctx->x, prev_part, prev_n, M, H, ctx->final_norm, d.rms_eps, ctx->xn16, ctx->xn_lo, s,
                                 Mo, all ? nullptr : ctx->out_rows);
+    n += 1 + enqueue_lm_head(ctx, p, Mo);
+    return n;
+}
+
+// The final lm_head GEMM (fused per-tile argmax, logits when asked) and the argmax reduce
+// of the Mo output rows, from the final norm's pair in xn16 / xn_lo.
+static int enqueue_lm_head(fa_ctx* ctx, const StepPlan& p, int Mo) {
+    const fa_model_desc& d = ctx->d;
+    const bool all = p.n_out < 0;
     fa::GemmArgs g{};
-    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(ctx->lm_q, d.vocab, H); g.M = Mo; g.N = d.vocab;
-    g.K = H;
+    g.A = ctx->xn16; g.A_lo = ctx->xn_lo; g.W8 = fa::q8p_view(ctx->lm_q, d.vocab, d.hidden); g.M = Mo; g.N = d.vocab;
+    g.K = d.hidden;
     g.n_split = 1; g.epilogue = fa::kEpiArgmax; g.C = p.logits ? ctx->logits_dev : nullptr;
     g.amax_val = ctx->amax_v; g.amax_idx = ctx->amax_i;
     run_gemm(ctx, g);
     fa::launch_argmax_reduce(ctx->amax_v, ctx->amax_i, Mo, d.vocab / 64, ctx->next_dev, all ? ctx->row_tok : nullptr,
-                             all ? ctx->row_pos : nullptr, s);
-    n += 3;
-    return n;
+                             all ? ctx->row_pos : nullptr, ctx->stream);
+    return 2;
+}
+
+// One row: the persistent step kernel (embedding, every layer, the final norm) as a
+// cooperative launch, then the lm_head and the argmax reduce.
+static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p) {
+    const fa_model_desc& d = ctx->d;
+    fa::RowStepArgs a{};
+    a.layers = ctx->row_layers; a.n_layers = d.n_layers; a.hidden = d.hidden; a.ffn = d.ffn;
+    for (int i = 0; i < 4; ++i) a.gm[i] = ctx->row_gm[i];
+    a.eps = d.rms_eps; a.q_scale = 1.0f / std::sqrt((float)kD);
+    a.embed = ctx->embed; a.embed_type = ctx->embed_type; a.vocab = d.vocab; a.x_ready = p.embeds ? 1 : 0;
+    a.tok = ctx->row_tok; a.slot = ctx->row_slot; a.pos = ctx->row_pos;
+    a.block_table = ctx->bt_dev; a.bt_stride = ctx->bt_stride; a.n_pages = ctx->n_pages;
+    a.pool = ctx->pool; a.layer_stride = ctx->layer_stride; a.rope = ctx->rope; a.max_pos = d.max_ctx;
+    a.x_a = ctx->x; a.x_b = ctx->x_b;
+    a.qkv = ctx->part; a.part_o = ctx->part + (kHq + 2 * kHkv) * kD; a.part_dn = a.part_o + d.hidden;
+    a.attn16 = ctx->attn16; a.attn_lo = ctx->attn_lo; a.h16 = ctx->h16; a.h_lo = ctx->h_lo;
+    a.att_po = ctx->att_po; a.att_pml = ctx->att_pml; a.pps = p.pps; a.n_splits = p.n_splits;
+    a.final_norm = ctx->final_norm; a.xn16 = ctx->xn16; a.xn_lo = ctx->xn_lo;
+    a.ctl = ctx->row_ctl; a.err = ctx->err_dev;
+    a.wait_ns = ctx->row_wait_ns; a.absent_cta = ctx->row_absent_cta;
+    const bool pdl = fa::launch_pdl_enabled();
+    fa::set_launch_pdl(false);
+    const cudaError_t e = fa::launch_row_step(a, ctx->n_sm, ctx->stream);
+    fa::set_launch_pdl(pdl);
+    if (e != cudaSuccess) {
+        ctx->enqueue_failed = true;
+        ctx->enqueue_msg = std::string("one-row step kernel launch: ") + cudaGetErrorString(e);
+        return 1;
+    }
+    const int Mo = p.n_out < 0 ? 1 : p.n_out;
+    return 1 + (Mo > 0 ? enqueue_lm_head(ctx, p, Mo) : 0);
 }
 
 // enqueue_step with programmatic dependent launch between its kernels when enabled
 static int enqueue_step_pdl(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     fa::set_launch_pdl(ctx->use_pdl);
     ctx->enqueue_failed = false;
+    ctx->enqueue_msg.clear();
     const int n = enqueue_step(ctx, p, capturing);
     fa::set_launch_pdl(false);
     return n;
+}
+
+static std::string enqueue_error(const fa_ctx* ctx) {
+    return ctx->enqueue_msg.empty() ? std::string("a fused GEMM launch declined its arguments") : ctx->enqueue_msg;
 }
 
 static int run_step(fa_ctx* ctx, const StepPlan& p) {
@@ -1017,7 +1123,7 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
         if (int rc = ensure_prof_events(ctx)) return rc;
     if (!ctx->use_graphs) {
         ctx->last_launches = enqueue_step_pdl(ctx, p, false);
-        if (ctx->enqueue_failed) return set_err(ctx, FA_ERR_CUDA, "a fused GEMM launch declined its arguments");
+        if (ctx->enqueue_failed) return set_err(ctx, FA_ERR_CUDA, enqueue_error(ctx));
         FA_CK(cudaGetLastError());
         ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
         return FA_OK;
@@ -1031,7 +1137,7 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
         cudaError_t e = cudaStreamEndCapture(ctx->stream, &graph);
         if (e != cudaSuccess || ctx->enqueue_failed) {
             if (graph) cudaGraphDestroy(graph);
-            return set_err(ctx, FA_ERR_CUDA, ctx->enqueue_failed ? std::string("a fused GEMM launch declined its arguments")
+            return set_err(ctx, FA_ERR_CUDA, ctx->enqueue_failed ? enqueue_error(ctx)
                                                                   : std::string("graph capture: ") + cudaGetErrorString(e));
         }
         cudaGraphExec_t exec = nullptr;
@@ -1053,6 +1159,8 @@ static int check_device_error(fa_ctx* ctx) {
     if (*ctx->h_err) {
         const int e = *ctx->h_err;
         cudaMemsetAsync(ctx->err_dev, 0, sizeof(int), ctx->stream);
+        // a one-row step that gave up leaves its barrier counter mid-way: start it afresh
+        if (ctx->row_ctl) cudaMemsetAsync(ctx->row_ctl, 0, sizeof(fa::RowCtl), ctx->stream);
         cudaStreamSynchronize(ctx->stream);
         if (e & fa::kDevErrTimeout) return set_err(ctx, FA_ERR_TIMEOUT, "a bounded device wait gave up");
         return set_err(ctx, FA_ERR_DEVICE, "kernel reported error bits " + std::to_string(e) +

@@ -194,6 +194,75 @@ constexpr int kGemvMaxRows = 8;
 constexpr int kGemvAutoRows = 2;
 bool gemv_shape_supported(int M, int N, int K, int epilogue, bool q8 = true);
 bool launch_q8_gemv(const GemmArgs& g, cudaStream_t s);   // false: shape or pointers not taken
+// How the CUDA-core kernel splits a Q8_0 GEMM with 16 weights per lane (K a multiple of 512):
+// ks warps share a block of 4 weight rows, each taking ns slices of 512 columns. False when
+// the kernel would not take the shape that way.
+bool gemv_q8_split(int M, int N, int K, int epilogue, int* ks, int* ns);
+
+// --------------------------------------------------------------- k_row_step.cu --
+// The decode step of one row (one sequence, one token) as one persistent cooperative
+// kernel: embedding, every layer and the final norm; the lm_head GEMV and the argmax
+// reduce follow as ordinary launches. Same arithmetic, same bits as the launch-per-op step
+// with the CUDA-core GEMMs.
+struct RowLayer {
+    const unsigned char* w[4];   // Q8_0 planes of QKV, o_proj, gate|up (64-row blocks), down
+    const float* in_norm;
+    const float* post_norm;
+    const float* q_norm;
+    const float* k_norm;
+};
+struct RowGemm {
+    int N, K, ks;                // ks warps x 512 columns cover K (one slice each)
+    int swiglu;                  // gate / up pairs, 64-row interleave, SwiGLU output
+};
+struct RowCtl {
+    unsigned long long bar;      // grid barrier arrivals (a multiple of the grid between launches)
+    int abort;                   // a barrier wait ran out: every CTA leaves
+    int att_cnt[8];              // attention splits finished per KV head (reset by the last one)
+};
+struct RowStepArgs {
+    const RowLayer* layers;
+    int n_layers, hidden, ffn;
+    RowGemm gm[4];
+    float eps, q_scale;
+    const void* embed;
+    int embed_type, vocab;
+    int x_ready;                 // x_a already holds the row's input (embeddings given)
+    const int* tok;
+    const int* slot;
+    const int* pos;
+    const int* block_table;
+    int bt_stride, n_pages;
+    __half* pool;
+    size_t layer_stride;         // elements between layers of the pool
+    const float2* rope;
+    int max_pos;
+    float* x_a;                  // residual stream, ping-pong between the two norms
+    float* x_b;
+    float* qkv;                  // [(Hq + 2 Hkv) * 128]
+    float* part_o;               // [hidden]
+    float* part_dn;              // [hidden]
+    __half* attn16;
+    __half* attn_lo;
+    __half* h16;
+    __half* h_lo;
+    float* att_po;
+    float* att_pml;
+    int pps, n_splits;
+    const float* final_norm;
+    __half* xn16;                // final norm output, the lm_head's input pair
+    __half* xn_lo;
+    RowCtl* ctl;
+    int* err;
+    unsigned long long wait_ns;  // limit of one grid-barrier wait
+    int absent_cta;              // failure test: this CTA leaves at once (never arrives); -1 = none
+};
+// Fills gm[] for a model's shapes; false when the kernel does not take them.
+bool row_step_shapes(int hidden, int ffn, int grid, RowGemm* gm);
+size_t row_step_smem_bytes(int hidden, int ffn);
+cudaError_t configure_row_step();
+// grid: one CTA per SM (a cooperative launch: all CTAs resident, or the launch fails)
+cudaError_t launch_row_step(const RowStepArgs& a, int grid, cudaStream_t s);
 
 // ----------------------------------------------------------------- k_small.cu --
 void launch_embed(const void* table, int table_type, int hidden, const int* tokens, const float* embeds,

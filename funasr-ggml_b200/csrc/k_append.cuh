@@ -45,8 +45,10 @@ __device__ __forceinline__ HeadRowMeta qkv_head_meta(const AppendArgs& a, int m,
     return h;
 }
 
+// q_dst (optional): where a q head goes instead of a.q_out (128 floats, any address space);
+// kv_dst (optional): a second copy of a K / V head's 128 f16 values besides the page.
 __device__ __forceinline__ void qkv_head_apply(const AppendArgs& a, const HeadRowMeta& h, int m, int j, int lane,
-                                               float (&x)[4]) {
+                                               float (&x)[4], float* q_dst = nullptr, __half* kv_dst = nullptr) {
     constexpr int D = 128;
     const int pos = h.pos;
     const bool is_q = j < a.Hq;
@@ -76,7 +78,7 @@ __device__ __forceinline__ void qkv_head_apply(const AppendArgs& a, const HeadRo
             y[k + 2] = __fadd_rn(__fmul_rn(x0, r.y), __fmul_rn(x1, r.x));
         }
         if (is_q) {
-            float* dst = a.q_out + ((size_t)m * a.Hq + j) * D;
+            float* dst = q_dst ? q_dst : a.q_out + ((size_t)m * a.Hq + j) * D;
 #pragma unroll
             for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = __fmul_rn(y[k], a.q_scale);
             return;
@@ -96,7 +98,11 @@ __device__ __forceinline__ void qkv_head_apply(const AppendArgs& a, const HeadRo
     __half* dst = a.pool_layer + (size_t)page * a.Hkv * 2 * kPageTokens * D +
                   ((size_t)(hh * 2 + kv) * kPageTokens + pos % kPageTokens) * D;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) dst[lane + 32 * k] = __float2half_rn(x[k]);
+    for (int k = 0; k < 4; ++k) {
+        const __half v = __float2half_rn(x[k]);
+        dst[lane + 32 * k] = v;
+        if (kv_dst) kv_dst[lane + 32 * k] = v;
+    }
 }
 
 // qkv_head_apply for R rows of the same head vector at once (row r live when live[r]): the

@@ -300,6 +300,12 @@ bool gemv_shape_supported(int M, int N, int K, int epilogue, bool q8) {
     return shape_config(M, N, K, epilogue, q8, &ks, &G, &ns);
 }
 
+bool gemv_q8_split(int M, int N, int K, int epilogue, int* ks, int* ns) {
+    int G;
+    if (wpl_for(true, K) != 16) return false;
+    return shape_config(M, N, K, epilogue, true, ks, &G, ns);
+}
+
 bool launch_q8_gemv(const GemmArgs& g, cudaStream_t s) {
     int ks, G, ns;
     if (!gemv_config(g, &ks, &G, &ns)) return false;

@@ -34,14 +34,18 @@ __device__ __forceinline__ double block_sum_double(double v, double* sh) {
 // Sum of n_part split-K partials of one float4 column group, in partial order; the
 // loads of a group of G partials are all issued before the first add (the same sum for
 // every G; a larger G shortens the chain of load rounds and costs registers).
-template <int G = 8>
+// CG: load at L2 (ld.global.cg), for partials written by other CTAs of the same kernel.
+template <int G = 8, bool CG = false>
 __device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, int n_part) {
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s0 = 0; s0 < n_part; s0 += G) {
         float4 t[G];
 #pragma unroll
         for (int u = 0; u < G; ++u)
-            if (s0 + u < n_part) t[u] = p[(size_t)(s0 + u) * stride4];
+            if (s0 + u < n_part) {
+                if constexpr (CG) t[u] = __ldcg(p + (size_t)(s0 + u) * stride4);
+                else t[u] = p[(size_t)(s0 + u) * stride4];
+            }
 #pragma unroll
         for (int u = 0; u < G; ++u)
             if (s0 + u < n_part) {
@@ -57,8 +61,10 @@ __device__ __forceinline__ float4 sum_parts4(const float4* p, size_t stride4, in
 // x_row) receives a; then y = (a * scale) * w, scale = 1 / sqrt(mean(a^2) + eps) with the
 // squares summed in double, and emit(j, y) for every column j. Threads [0, 256) each own
 // the float4 groups t, t + 256, ... (hidden <= 4096, a multiple of 4); every thread of the
-// block must call it (it synchronises), and sh needs one double per warp.
-template <int G = 8, typename Emit>
+// block must call it (it synchronises), and sh needs one double per warp. CG: x_row (a
+// global address then) and the partials are read at L2, for values other CTAs of the same
+// kernel wrote.
+template <int G = 8, bool CG = false, typename Emit>
 __device__ __forceinline__ void residual_norm_row(const float* x_row, const float4* part4, size_t stride4, int n_part,
                                                   int hidden, const float* w, float eps, float* x_out_row, double* sh,
                                                   Emit emit) {
@@ -70,9 +76,11 @@ __device__ __forceinline__ void residual_norm_row(const float* x_row, const floa
     for (int c = 0; c < 4; ++c) {
         const int i = threadIdx.x + 256 * c;
         if (!owner || i >= n4) break;
-        float4 a = reinterpret_cast<const float4*>(x_row)[i];
+        float4 a;
+        if constexpr (CG) a = __ldcg(reinterpret_cast<const float4*>(x_row) + i);
+        else a = reinterpret_cast<const float4*>(x_row)[i];
         if (n_part > 0) {
-            const float4 o = sum_parts4<G>(part4 + i, stride4, n_part);
+            const float4 o = sum_parts4<G, CG>(part4 + i, stride4, n_part);
             a.x = __fadd_rn(a.x, o.x); a.y = __fadd_rn(a.y, o.y);
             a.z = __fadd_rn(a.z, o.z); a.w = __fadd_rn(a.w, o.w);
         }

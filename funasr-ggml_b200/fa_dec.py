@@ -109,6 +109,8 @@ def lib():
         "fa_set_gemm_variant": ([_P, _I], _I),
         "fa_set_fused_epilogues": ([_P, _I], _I),
         "fa_set_pdl": ([_P, _I], _I),
+        "fa_set_row_step": ([_P, _I], _I),
+        "fa_set_row_step_fault": ([_P, _I, _I], _I),
         "fa_pool_info": ([_P, _P, _P, _P], _I),
         "fa_seq_open": ([_P, _I, _P], _I),
         "fa_seq_close": ([_P, _I], _I),
@@ -298,6 +300,16 @@ class Decoder:
         norm/RoPE/append, 2 = gate/up with SwiGLU (default 2); 0 = separate kernels. Same
         bits either way."""
         self._c(lib().fa_set_fused_epilogues(self.ctx, int(mask)))
+
+    def set_row_step(self, enable: bool):
+        """One-row decode steps as one persistent kernel (default on; same bits as launch by
+        launch)."""
+        self._c(lib().fa_set_row_step(self.ctx, int(enable)))
+
+    def set_row_step_fault(self, absent_cta: int, wait_us: int = 0):
+        """Failure test: CTA absent_cta of the one-row step kernel never reaches its barriers,
+        so the step gives up after wait_us and returns FA_ERR_TIMEOUT (-1: off)."""
+        self._c(lib().fa_set_row_step_fault(self.ctx, int(absent_cta), int(wait_us)))
 
     def set_pdl(self, enable: bool):
         self._c(lib().fa_set_pdl(self.ctx, int(enable)))

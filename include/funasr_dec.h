@@ -131,6 +131,17 @@ FA_API int fa_set_fused_epilogues(fa_ctx* ctx, int mask);
 /* 1 = programmatic dependent launch between a step's kernels (default): each kernel's
  * prologue overlaps the previous kernel's tail. 0 = plain stream order. */
 FA_API int fa_set_pdl(fa_ctx* ctx, int enable);
+/* 1 (default) = a step of one decode row (one sequence, one token) runs as one persistent
+ * kernel over every SM (embedding, all layers, final norm; grid barriers between a layer's
+ * phases) followed by the lm_head and argmax launches, when the model's shapes allow it and
+ * the GEMM variant is 0 or 3; 0 = launch by launch. Same bits either way. Replaces the
+ * reference's per-token graph launch of compute/llm_ops_gpu.cpp:155-207 for one stream. */
+FA_API int fa_set_row_step(fa_ctx* ctx, int enable);
+/* Failure test of the one-row step kernel's grid barriers: with absent_cta >= 0 that CTA
+ * leaves at once, so the others' barrier waits run out after wait_us microseconds (<= 0:
+ * the default 2 s); every CTA then leaves, the step returns FA_ERR_TIMEOUT and the context
+ * stays usable. absent_cta = -1 turns it off. No reference counterpart. */
+FA_API int fa_set_row_step_fault(fa_ctx* ctx, int absent_cta, int wait_us);
 /* 1 = launch each step as a captured CUDA graph (default), 0 = direct launches. */
 FA_API int fa_set_graphs(fa_ctx* ctx, int enable);
 /* The descriptor the context runs with (n_pages resolved from kv_bytes). */
