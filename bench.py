@@ -198,6 +198,7 @@ def run_ours(a):
     clocks = sampler.stop()
     fa_multi.barrier()
     attn_ms, n_att = dec.profile_attention()
+    row_ms = dec.profile_row_step()
     launches = dec.step_launches()
     dec.profile(False)
     max_ms = fa_multi.reduce(dev_ms, "max")
@@ -216,6 +217,22 @@ def run_ours(a):
             t = json.load(f)
         # bytes scale with the (row, token) pairs read per launch
         traffic = t["dram_bytes_per_launch"] * (B * n_kv_last) / (t["rows"] * t["n_kv"])
+
+    kernel, bytes_per_launch, ms_per_launch = "paged_attn_kernel (+attn_combine)", att_bytes, att_launch_ms
+    if row_ms > 0:
+        # one row: the persistent step kernel is the step; its algorithmic bytes are every
+        # layer's Q8_0 weights (q and row-major scale planes, 34 B per 32 weights) and the
+        # row's K/V pages, each read once
+        wq = sum(n * k for n, k in ((4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072)))
+        bytes_per_launch = cfg["n_layers"] * (wq * 34 // 32 + B * n_kv_last * KV_BYTES_PER_TOKEN_LAYER)
+        ms_per_launch = row_ms
+        kernel = "row_step_kernel (one-row step: 28 layers, persistent)"
+        achieved = bytes_per_launch / (row_ms / 1e3) / 1e9
+        traffic = None
+        tf = os.path.join(ROOT, "profiles", "row_step_traffic.json")
+        if os.path.exists(tf):
+            with open(tf) as f:
+                traffic = json.load(f)["dram_bytes_per_launch"]
 
     # e2e through the public step call, host ids in and out every step
     toks = ids[-1]
@@ -255,8 +272,8 @@ def run_ours(a):
                        "parallelism": f"independent replicas x{world}, no collectives"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "paged_attn_kernel (+attn_combine)", "peak_kind": peak_kind,
-                         "bytes_per_launch": att_bytes, "ms_per_launch": att_launch_ms},
+                         "kernel": kernel, "peak_kind": peak_kind,
+                         "bytes_per_launch": bytes_per_launch, "ms_per_launch": ms_per_launch},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": B * 12,
                     "d2h_bytes_per_step": B * 4 + 4, "steps": E},

@@ -173,7 +173,8 @@ struct fa_ctx {
     bool row_ready = false;    // buffers and the layer table below exist
     fa::RowGemm row_gm[4] = {};
     fa::RowLayer* row_layers = nullptr;
-    float* x_b = nullptr;
+    unsigned long long* row_words = nullptr;   // the phases' tagged words (row_step_words)
+    size_t row_words_n = 0;
     fa::RowCtl* row_ctl = nullptr;
     int row_absent_cta = -1;   // failure test (fa_set_row_step_fault)
     unsigned long long row_wait_ns = fa::kWaitLimitNs;
@@ -196,6 +197,7 @@ struct fa_ctx {
     bool prof = false;
     std::vector<cudaEvent_t> prof_ev;   // pairs per attention launch
     int prof_n = 0;
+    bool prof_row = false;     // the last profiled step ran the one-row step kernel
     int last_launches = 0;
     cudaEvent_t ev_t0 = nullptr, ev_t1 = nullptr;
 };
@@ -583,10 +585,13 @@ static int setup_row_step(fa_ctx* ctx) {
     }
     int r;
     if ((r = dev_alloc(ctx, &ctx->row_layers, sizeof(fa::RowLayer) * tab.size())) ||
-        (r = dev_alloc(ctx, &ctx->x_b, sizeof(float) * d.hidden)) || (r = dev_alloc(ctx, &ctx->row_ctl, sizeof(fa::RowCtl))))
+        (r = dev_alloc(ctx, &ctx->row_words, sizeof(unsigned long long) * fa::row_step_words(d.hidden, d.ffn))) ||
+        (r = dev_alloc(ctx, &ctx->row_ctl, sizeof(fa::RowCtl))))
         return r;
     FA_CK(cudaMemcpy(ctx->row_layers, tab.data(), sizeof(fa::RowLayer) * tab.size(), cudaMemcpyHostToDevice));
+    ctx->row_words_n = fa::row_step_words(d.hidden, d.ffn);
     FA_CK(cudaMemset(ctx->row_ctl, 0, sizeof(fa::RowCtl)));
+    FA_CK(cudaMemset(ctx->row_words, 0, sizeof(unsigned long long) * ctx->row_words_n));
     ctx->row_ready = true;
     return FA_OK;
 }
@@ -903,7 +908,7 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
     p.logits = logits;
     p.prof = ctx->prof;
     // one decode row, CUDA-core GEMM arithmetic, every attention item on its own SM
-    p.row_step = ctx->row_ready && ctx->row_step_on && M == 1 && n_tiles == 0 && p.n_dec == 1 && !p.prof &&
+    p.row_step = ctx->row_ready && ctx->row_step_on && M == 1 && n_tiles == 0 && p.n_dec == 1 &&
                  gemv_rows(ctx->gemm_variant, 1) && p.n_splits * kHkv <= ctx->n_sm;
     return p;
 }
@@ -949,12 +954,12 @@ static void run_gemm(fa_ctx* ctx, const fa::GemmArgs& g) {
     fa::launch_q8_gemm(g, ctx->stream);
 }
 
-static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p);
+static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p, bool capturing);
 static int enqueue_lm_head(fa_ctx* ctx, const StepPlan& p, int Mo);
 
 // Enqueue the kernels of one forward step. Returns the number of launches.
 static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
-    if (p.row_step) return enqueue_row_step(ctx, p);
+    if (p.row_step) return enqueue_row_step(ctx, p, capturing);
     const fa_model_desc& d = ctx->d;
     cudaStream_t s = ctx->stream;
     const int M = p.M, H = d.hidden, F = d.ffn;
@@ -1072,8 +1077,9 @@ static int enqueue_lm_head(fa_ctx* ctx, const StepPlan& p, int Mo) {
 }
 
 // One row: the persistent step kernel (embedding, every layer, the final norm) as a
-// cooperative launch, then the lm_head and the argmax reduce.
-static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p) {
+// cooperative launch, then the lm_head and the argmax reduce. Profiling brackets the
+// persistent kernel with events 0 and 1.
+static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     const fa_model_desc& d = ctx->d;
     fa::RowStepArgs a{};
     a.layers = ctx->row_layers; a.n_layers = d.n_layers; a.hidden = d.hidden; a.ffn = d.ffn;
@@ -1083,16 +1089,18 @@ static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p) {
     a.tok = ctx->row_tok; a.slot = ctx->row_slot; a.pos = ctx->row_pos;
     a.block_table = ctx->bt_dev; a.bt_stride = ctx->bt_stride; a.n_pages = ctx->n_pages;
     a.pool = ctx->pool; a.layer_stride = ctx->layer_stride; a.rope = ctx->rope; a.max_pos = d.max_ctx;
-    a.x_a = ctx->x; a.x_b = ctx->x_b;
-    a.qkv = ctx->part; a.part_o = ctx->part + (kHq + 2 * kHkv) * kD; a.part_dn = a.part_o + d.hidden;
-    a.attn16 = ctx->attn16; a.attn_lo = ctx->attn_lo; a.h16 = ctx->h16; a.h_lo = ctx->h_lo;
+    a.x_a = ctx->x;
+    a.w_qkv = ctx->row_words; a.w_att = a.w_qkv + (kHq + 2 * kHkv) * kD; a.w_o = a.w_att + kHq * kD;
+    a.w_h = a.w_o + d.hidden; a.w_dn = a.w_h + d.ffn;
     a.att_po = ctx->att_po; a.att_pml = ctx->att_pml; a.pps = p.pps; a.n_splits = p.n_splits;
     a.final_norm = ctx->final_norm; a.xn16 = ctx->xn16; a.xn_lo = ctx->xn_lo;
     a.ctl = ctx->row_ctl; a.err = ctx->err_dev;
     a.wait_ns = ctx->row_wait_ns; a.absent_cta = ctx->row_absent_cta;
     const bool pdl = fa::launch_pdl_enabled();
     fa::set_launch_pdl(false);
+    if (p.prof) record_prof(ctx, 0, capturing);
     const cudaError_t e = fa::launch_row_step(a, ctx->n_sm, ctx->stream);
+    if (p.prof) record_prof(ctx, 1, capturing);
     fa::set_launch_pdl(pdl);
     if (e != cudaSuccess) {
         ctx->enqueue_failed = true;
@@ -1125,7 +1133,8 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
         ctx->last_launches = enqueue_step_pdl(ctx, p, false);
         if (ctx->enqueue_failed) return set_err(ctx, FA_ERR_CUDA, enqueue_error(ctx));
         FA_CK(cudaGetLastError());
-        ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
+        ctx->prof_n = p.prof && !p.row_step ? ctx->d.n_layers : 0;
+        ctx->prof_row = p.prof && p.row_step;
         return FA_OK;
     }
     auto it = ctx->graphs.find(p.key());
@@ -1149,7 +1158,8 @@ static int run_step(fa_ctx* ctx, const StepPlan& p) {
     }
     ctx->last_launches = it->second.launches;
     FA_CK(cudaGraphLaunch(it->second.exec, ctx->stream));
-    ctx->prof_n = p.prof ? ctx->d.n_layers : 0;
+    ctx->prof_n = p.prof && !p.row_step ? ctx->d.n_layers : 0;
+    ctx->prof_row = p.prof && p.row_step;
     return FA_OK;
 }
 
@@ -1159,8 +1169,12 @@ static int check_device_error(fa_ctx* ctx) {
     if (*ctx->h_err) {
         const int e = *ctx->h_err;
         cudaMemsetAsync(ctx->err_dev, 0, sizeof(int), ctx->stream);
-        // a one-row step that gave up leaves its barrier counter mid-way: start it afresh
-        if (ctx->row_ctl) cudaMemsetAsync(ctx->row_ctl, 0, sizeof(fa::RowCtl), ctx->stream);
+        // a one-row step that gave up leaves words of its sequence number behind: clear
+        // them and start the numbering afresh
+        if (ctx->row_ctl) {
+            cudaMemsetAsync(ctx->row_ctl, 0, sizeof(fa::RowCtl), ctx->stream);
+            cudaMemsetAsync(ctx->row_words, 0, sizeof(unsigned long long) * ctx->row_words_n, ctx->stream);
+        }
         cudaStreamSynchronize(ctx->stream);
         if (e & fa::kDevErrTimeout) return set_err(ctx, FA_ERR_TIMEOUT, "a bounded device wait gave up");
         return set_err(ctx, FA_ERR_DEVICE, "kernel reported error bits " + std::to_string(e) +
@@ -1573,6 +1587,14 @@ extern "C" int fa_profile_attention(fa_ctx* ctx, float* total_ms, int* n_launche
     }
     if (total_ms) *total_ms = tot;
     if (n_launches) *n_launches = n;
+    return FA_OK;
+}
+
+extern "C" int fa_profile_row_step(fa_ctx* ctx, float* ms) {
+    if (!ctx || !ms) return set_err(ctx, FA_ERR_INVALID_ARG, "bad arguments");
+    FA_CK(cudaStreamSynchronize(ctx->stream));
+    *ms = 0.0f;
+    if (ctx->prof_row) FA_CK(cudaEventElapsedTime(ms, ctx->prof_ev[0], ctx->prof_ev[1]));
     return FA_OK;
 }
 

@@ -216,8 +216,8 @@ struct RowGemm {
     int swiglu;                  // gate / up pairs, 64-row interleave, SwiGLU output
 };
 struct RowCtl {
-    unsigned long long bar;      // grid barrier arrivals (a multiple of the grid between launches)
-    int abort;                   // a barrier wait ran out: every CTA leaves
+    unsigned int seq;            // launches completed: tags of launch k are (k + 1) * layers + layer
+    int abort;                   // a wait ran out: every CTA leaves
     int att_cnt[8];              // attention splits finished per KV head (reset by the last one)
 };
 struct RowStepArgs {
@@ -237,16 +237,14 @@ struct RowStepArgs {
     size_t layer_stride;         // elements between layers of the pool
     const float2* rope;
     int max_pos;
-    float* x_a;                  // residual stream, ping-pong between the two norms
-    float* x_b;
-    float* qkv;                  // [(Hq + 2 Hkv) * 128]
-    float* part_o;               // [hidden]
-    float* part_dn;              // [hidden]
-    __half* attn16;
-    __half* attn_lo;
-    __half* h16;
-    __half* h_lo;
-    float* att_po;
+    float* x_a;                  // the row's input (x_ready), and the final residual on exit
+    // tagged words {value, tag} the phases hand on (row_step_words of them, in this order)
+    unsigned long long* w_qkv;   // [(Hq + 2 Hkv) * 128] f32
+    unsigned long long* w_att;   // [Hq * 128] f16 pair
+    unsigned long long* w_o;     // [hidden] f32
+    unsigned long long* w_h;     // [ffn] f16 pair
+    unsigned long long* w_dn;    // [hidden] f32
+    float* att_po;               // split partials (n_splits > 1)
     float* att_pml;
     int pps, n_splits;
     const float* final_norm;
@@ -254,9 +252,10 @@ struct RowStepArgs {
     __half* xn_lo;
     RowCtl* ctl;
     int* err;
-    unsigned long long wait_ns;  // limit of one grid-barrier wait
-    int absent_cta;              // failure test: this CTA leaves at once (never arrives); -1 = none
+    unsigned long long wait_ns;  // limit of one wait for a word
+    int absent_cta;              // failure test: this CTA leaves at once (its words never come); -1 = none
 };
+size_t row_step_words(int hidden, int ffn);
 // Fills gm[] for a model's shapes; false when the kernel does not take them.
 bool row_step_shapes(int hidden, int ffn, int grid, RowGemm* gm);
 size_t row_step_smem_bytes(int hidden, int ffn);

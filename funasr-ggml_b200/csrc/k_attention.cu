@@ -74,7 +74,9 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
     const int issued = attn::warp_issue_first(S, bt, p_begin, nw, head_base, page_elems, warp, lane);
     attn::warp_pages(a, S, bt, p_begin, nw, issued, n_kv, head_base, page_elems, nullptr, -1, 0, warp, lane);
     __syncthreads();
-    attn::merge_warps(a, S, split, h, m, threadIdx.x);
+    attn::merge_warps(S, threadIdx.x, [&](int hq, float M, float L, float O) {
+        attn::merge_store(a, split, h, m, threadIdx.x, hq, M, L, O);
+    });
 }
 
 // Merge of the split partials: a warp per (row, query head).
@@ -85,7 +87,9 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
     const int lane = threadIdx.x & 31;
     if (w >= a.M * a.Hq) return;
     const int m = a.rows ? a.rows[w / a.Hq] : w / a.Hq;
-    attn::combine_head<false>(a, m, w % a.Hq, lane);
+    const int H = w % a.Hq;
+    const size_t o = (size_t)m * a.Hq * D + (size_t)H * D;
+    attn::combine_head<false>(a, m, H, lane, [&](int d, float v) { attn::store_out(a, o + d, v); });
 }
 
 }  // namespace

@@ -333,9 +333,10 @@ __device__ __forceinline__ void warp_pages(const AttnArgs& a, Smem<STAGES>& S, c
 }
 
 // Merge of the 4 warps' partials (after a barrier over the 4 warps), thread d < 128 of
-// them owning dim d: the output of query heads 2h, 2h+1 of row m, or the split's partial.
-template <int STAGES>
-__device__ __forceinline__ void merge_warps(const AttnArgs& a, const Smem<STAGES>& S, int split, int h, int m, int d) {
+// them owning dim d: for each of the two query heads hq, the maximum M, the sum L and the
+// output O, handed to epi(hq, M, L, O).
+template <int STAGES, typename Epi>
+__device__ __forceinline__ void merge_warps(const Smem<STAGES>& S, int d, Epi epi) {
 #pragma unroll
     for (int hq = 0; hq < 2; ++hq) {
         float M = -INFINITY;
@@ -346,21 +347,28 @@ __device__ __forceinline__ void merge_warps(const AttnArgs& a, const Smem<STAGES
 #pragma unroll
             for (int w = 0; w < WARPS; ++w) {
                 const float sc = exp2f(S.ml[w][hq] - M);
-                L += S.ml[w][2 + hq] * sc;
-                O += S.acc[w][hq][d] * sc;
+                L = fmaf(S.ml[w][2 + hq], sc, L);
+                O = fmaf(S.acc[w][hq][d], sc, O);
             }
         }
-        const int H = 2 * h + hq;
-        if (a.n_splits == 1) {
-            const float v = L > 0.0f ? O / L : 0.0f;
-            store_out(a, (size_t)m * a.Hq * D + (size_t)H * D + d, v);
-        } else {
-            const size_t base = ((size_t)m * a.Hq + H) * a.n_splits + split;
-            a.part_o[base * D + d] = O;
-            if (d == 0) {
-                a.part_ml[base * 2] = M;
-                a.part_ml[base * 2 + 1] = L;
-            }
+        epi(hq, M, L, O);
+    }
+}
+
+// merge_warps' epilogue of kernel (2): the output of query head 2h + hq of row m (one
+// split), or the split's partial.
+__device__ __forceinline__ void merge_store(const AttnArgs& a, int split, int h, int m, int d, int hq, float M, float L,
+                                            float O) {
+    const int H = 2 * h + hq;
+    if (a.n_splits == 1) {
+        const float v = L > 0.0f ? O / L : 0.0f;
+        store_out(a, (size_t)m * a.Hq * D + (size_t)H * D + d, v);
+    } else {
+        const size_t base = ((size_t)m * a.Hq + H) * a.n_splits + split;
+        a.part_o[base * D + d] = O;
+        if (d == 0) {
+            a.part_ml[base * 2] = M;
+            a.part_ml[base * 2 + 1] = L;
         }
     }
 }
@@ -378,10 +386,11 @@ __device__ __forceinline__ float4 ld_part4(const float4* p) {
 
 // Merge of the split partials of (row m, query head H) by one warp, lane l owning dims
 // 4l..4l+3: the split maxima read by the lanes together, then every output sums its splits
-// in split order (the same arithmetic as one thread per dim). CG: read the partials at L2
-// (they were written by other CTAs of the same kernel).
-template <bool CG>
-__device__ __forceinline__ void combine_head(const AttnArgs& a, int m, int H, int lane) {
+// in split order (the same arithmetic as one thread per dim); out(d, value) for each of the
+// lane's dims. CG: read the partials at L2 (they were written by other CTAs of the same
+// kernel).
+template <bool CG, typename Out>
+__device__ __forceinline__ void combine_head(const AttnArgs& a, int m, int H, int lane, Out out) {
     const int n_kv = a.pos[m] + 1;
     const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
     if (row_len_bad(a, n_kv, n_row_pages)) return;      // flagged by the attention kernel
@@ -396,17 +405,16 @@ __device__ __forceinline__ void combine_head(const AttnArgs& a, int m, int H, in
     if (M != -INFINITY) {
         for (int s = 0; s < n_valid; ++s) {
             const float sc = exp2f(ld_part<CG>(a.part_ml + (base + s) * 2) - M);
-            L += ld_part<CG>(a.part_ml + (base + s) * 2 + 1) * sc;
+            L = fmaf(ld_part<CG>(a.part_ml + (base + s) * 2 + 1), sc, L);
             const float4 o4 = ld_part4<CG>(reinterpret_cast<const float4*>(a.part_o + (base + s) * D) + lane);
-            O[0] += o4.x * sc;
-            O[1] += o4.y * sc;
-            O[2] += o4.z * sc;
-            O[3] += o4.w * sc;
+            O[0] = fmaf(o4.x, sc, O[0]);
+            O[1] = fmaf(o4.y, sc, O[1]);
+            O[2] = fmaf(o4.z, sc, O[2]);
+            O[3] = fmaf(o4.w, sc, O[3]);
         }
     }
-    const size_t o = (size_t)m * a.Hq * D + (size_t)H * D + 4 * lane;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) store_out(a, o + j, L > 0.0f ? O[j] / L : 0.0f);
+    for (int j = 0; j < 4; ++j) out(4 * lane + j, L > 0.0f ? O[j] / L : 0.0f);
 }
 
 }  // namespace attn

@@ -110,6 +110,7 @@ def lib():
         "fa_set_fused_epilogues": ([_P, _I], _I),
         "fa_set_pdl": ([_P, _I], _I),
         "fa_set_row_step": ([_P, _I], _I),
+        "fa_profile_row_step": ([_P, _P], _I),
         "fa_set_row_step_fault": ([_P, _I, _I], _I),
         "fa_pool_info": ([_P, _P, _P, _P], _I),
         "fa_seq_open": ([_P, _I, _P], _I),
@@ -422,6 +423,13 @@ class Decoder:
         ms = ctypes.c_float(); n = ctypes.c_int()
         self._c(lib().fa_profile_attention(self.ctx, ctypes.byref(ms), ctypes.byref(n)))
         return ms.value, n.value
+
+    def profile_row_step(self) -> float:
+        """Device ms of the persistent one-row step kernel in the last profiled step (0 if
+        the step ran launch by launch)."""
+        ms = ctypes.c_float()
+        self._c(lib().fa_profile_row_step(self.ctx, ctypes.byref(ms)))
+        return ms.value
 
     def step_launches(self) -> int:
         n = ctypes.c_int()

@@ -132,15 +132,17 @@ FA_API int fa_set_fused_epilogues(fa_ctx* ctx, int mask);
  * prologue overlaps the previous kernel's tail. 0 = plain stream order. */
 FA_API int fa_set_pdl(fa_ctx* ctx, int enable);
 /* 1 (default) = a step of one decode row (one sequence, one token) runs as one persistent
- * kernel over every SM (embedding, all layers, final norm; grid barriers between a layer's
- * phases) followed by the lm_head and argmax launches, when the model's shapes allow it and
+ * kernel over every SM (embedding, all layers, final norm; a layer's phases hand their
+ * values on as tagged words that the next phase polls) followed by the lm_head and argmax
+ * launches, when the model's shapes allow it and
  * the GEMM variant is 0 or 3; 0 = launch by launch. Same bits either way. Replaces the
  * reference's per-token graph launch of compute/llm_ops_gpu.cpp:155-207 for one stream. */
 FA_API int fa_set_row_step(fa_ctx* ctx, int enable);
-/* Failure test of the one-row step kernel's grid barriers: with absent_cta >= 0 that CTA
- * leaves at once, so the others' barrier waits run out after wait_us microseconds (<= 0:
- * the default 2 s); every CTA then leaves, the step returns FA_ERR_TIMEOUT and the context
- * stays usable. absent_cta = -1 turns it off. No reference counterpart. */
+/* Failure test of the one-row step kernel's waits: with absent_cta >= 0 that CTA leaves
+ * at once, so the values of its rows never arrive and the other CTAs' waits run out after
+ * wait_us microseconds (<= 0: the default 2 s); every CTA then leaves, the step returns
+ * FA_ERR_TIMEOUT and the context stays usable. absent_cta = -1 turns it off. No reference
+ * counterpart. */
 FA_API int fa_set_row_step_fault(fa_ctx* ctx, int absent_cta, int wait_us);
 /* 1 = launch each step as a captured CUDA graph (default), 0 = direct launches. */
 FA_API int fa_set_graphs(fa_ctx* ctx, int enable);
@@ -243,12 +245,15 @@ FA_API int fa_kv_fill_synthetic(fa_ctx* ctx, int seq_id, int n_tokens, uint64_t 
 FA_API int fa_pool_compact(fa_ctx* ctx, int* n_moved);
 
 /* ---- measurement ---- */
-/* 1 = bracket the attention launches of layers 0, L/2 and L-1 with CUDA events (taken
- * into graphs when captured). */
+/* 1 = bracket the attention launches of layers 0, L/2 and L-1 with CUDA events, or in a
+ * one-row step the persistent step kernel (events taken into graphs when captured). */
 FA_API int fa_profile(fa_ctx* ctx, int enable);
 /* Those attention launches of the last forward/generate step: summed device ms and count
- * (paged-attention kernel plus its split combine). */
+ * (paged-attention kernel plus its split combine); 0 launches after a one-row step. */
 FA_API int fa_profile_attention(fa_ctx* ctx, float* total_ms, int* n_launches);
+/* Device ms of the persistent step kernel in the last profiled step; 0 when that step was
+ * not a one-row step. */
+FA_API int fa_profile_row_step(fa_ctx* ctx, float* ms);
 /* Kernels launched by the last forward step (all of this library's kernels). */
 FA_API int fa_step_launches(const fa_ctx* ctx, int* n_launches);
 

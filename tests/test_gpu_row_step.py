@@ -1,7 +1,7 @@
 """The one-row decode step as one persistent kernel (k_row_step.cu) against the launch-per-op
 step: same logits bits, same ids, same K/V page bytes, over contexts that take one and
-several attention splits, with token and embedding inputs; and its bounded grid barriers
-(a CTA that never arrives makes the step fail with FA_ERR_TIMEOUT, and the context keeps
+several attention splits, with token and embedding inputs; and its bounded waits (a CTA
+whose values never arrive makes the step fail with FA_ERR_TIMEOUT, and the context keeps
 working). The step's agreement with the oracle is checked at full Qwen3-0.6B geometry by
 test_gpu_decoder.test_qwen3_06b_greedy_decode_batch1, whose batch-1 steps run on it."""
 import numpy as np
@@ -85,7 +85,7 @@ def test_row_step_embedding_input(torch_cuda, w):
 
 
 def test_row_step_barrier_timeout_is_reported_and_recovers(torch_cuda, w):
-    """CTA 5 never arrives: every other CTA's barrier wait gives up after 50 ms, all leave,
+    """CTA 5 leaves at once: the CTAs waiting for its rows give up after 50 ms, all leave,
     the step fails with FA_ERR_TIMEOUT and rolls back; the same step then runs normally and
     gives the launch path's bits."""
     rng = np.random.default_rng(8)
