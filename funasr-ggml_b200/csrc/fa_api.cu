@@ -827,17 +827,19 @@ constexpr int kPrefillMinRun = 16;
 }  // namespace
 
 // Attention work split for rows of row_pages[i] pages each: the pages per CTA (a
-// multiple of 4, one per warp and round) that minimise the estimated time
-//   waves * (pps + 2) + (8 if any row is split)
-// where waves = ceil(CTAs / (kAttnCtasPerSm * n_sm)), a CTA costs its pages plus about
-// 2 pages' worth of set-up, and merging split partials costs a launch of its own, about
-// 8 pages' worth (a unit is ~0.5 us: 128 rows x 2048 tokens run 7 waves of 46 in
-// 173 us; the merge launch takes 4-6 us); at most max_splits splits per row.
+// multiple of 4) that minimise the estimated time
+//   waves * (4 * ceil(pps / warps) + 2) + (8 if any row is split)
+// where warps = fa::attn_warps(rows) per CTA, waves = ceil(CTAs / (CTAs per SM * n_sm)), a
+// CTA costs its rounds of pages (one per warp each) plus about 2 pages' worth of set-up, and
+// merging split partials costs a launch of its own, about 8 pages' worth (a unit is
+// ~0.5 us: 128 rows x 2048 tokens run 7 waves of 46 in 173 us; the merge launch takes
+// 4-6 us); at most max_splits splits per row.
 static void attention_split(const std::vector<int>& row_pages, int n_sm, int max_splits, int* pps_out,
                             int* n_splits_out) {
     int max_pages = 1;
     for (int pg : row_pages) max_pages = std::max(max_pages, pg);
-    const long long slots = (long long)fa::kAttnCtasPerSm * n_sm;
+    const int warps = fa::attn_warps((int)row_pages.size());
+    const long long slots = (long long)(warps == 4 ? fa::kAttnCtasPerSm : 1) * n_sm;
     long long best_cost = -1;
     int best = 0;
     for (int pps = 4; pps <= 256; pps += 4) {
@@ -846,7 +848,7 @@ static void attention_split(const std::vector<int>& row_pages, int n_sm, int max
         long long ctas = 0;
         for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + pps - 1) / pps);
         const long long waves = (ctas + slots - 1) / slots;
-        const long long cost = waves * (pps + 2) + (n_splits > 1 ? 8 : 0);
+        const long long cost = waves * (4 * ((pps + warps - 1) / warps) + 2) + (n_splits > 1 ? 8 : 0);
         if (best_cost < 0 || cost < best_cost) {
             best_cost = cost;
             best = pps;

@@ -91,6 +91,10 @@ void launch_paged_attention(const AttnArgs& a, cudaStream_t s);
 // memory: 4 warps x kAttnStages x 8 KiB per CTA).
 constexpr int kAttnStages = 2;
 constexpr int kAttnCtasPerSm = 3;
+// Steps of at most this many rows run 8 warps per CTA (one CTA per SM), so that a split's
+// pages spread over twice the warps; attn_warps gives the count for M rows.
+constexpr int kAttnWideRows = 2;
+int attn_warps(int M);
 // Split combine; only needed when n_splits > 1.
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s);
 
@@ -254,11 +258,11 @@ struct RowStepArgs {
     int* err;
     unsigned long long wait_ns;  // limit of one wait for a word
     int absent_cta;              // failure test: this CTA leaves at once (its words never come); -1 = none
+    int stage_q_bytes;           // set by launch_row_step
 };
 size_t row_step_words(int hidden, int ffn);
 // Fills gm[] for a model's shapes; false when the kernel does not take them.
 bool row_step_shapes(int hidden, int ffn, int grid, RowGemm* gm);
-size_t row_step_smem_bytes(int hidden, int ffn);
 cudaError_t configure_row_step();
 // grid: one CTA per SM (a cooperative launch: all CTAs resident, or the launch fails)
 cudaError_t launch_row_step(const RowStepArgs& a, int grid, cudaStream_t s);

@@ -27,12 +27,15 @@ namespace fa {
 namespace {
 
 using attn::D;
-using attn::WARPS;
-using AttnSmem = attn::Smem<kAttnStages>;
+template <int NW>
+using AttnSmem = attn::Smem<kAttnStages, NW>;
 
-__global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const AttnArgs a) {
+// NW warps per CTA: 4 (3 CTAs per SM) in general, 8 for steps of at most kAttnWideRows rows,
+// whose few CTAs would otherwise leave each warp several pages in a row.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_attn_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
+    AttnSmem<NW>& S = *reinterpret_cast<AttnSmem<NW>*>(smem_raw);
     const int split = blockIdx.x;
     const int h = blockIdx.y;
     const int warp = threadIdx.x >> 5;
@@ -56,27 +59,28 @@ __global__ void __launch_bounds__(128, kAttnCtasPerSm) paged_attn_kernel(const A
     const int* bt = a.block_table + (size_t)a.slot[m] * a.bt_stride;
 
     if (threadIdx.x == 0) {
-        for (int w = 0; w < WARPS; ++w)
+        for (int w = 0; w < NW; ++w)
             for (int s = 0; s < kAttnStages; ++s) mbar_init(&S.bars[w][s], 1);
         fence_mbar_init();
     }
-    {
+    if (threadIdx.x < D) {
         const float* qg = a.q + ((size_t)m * a.Hq + 2 * h) * D;
         S.q[0][threadIdx.x] = qg[threadIdx.x] * attn::kLog2e;
         S.q[1][threadIdx.x] = qg[D + threadIdx.x] * attn::kLog2e;
     }
     __syncthreads();
 
-    int nw = attn::warp_page_count(p_end - p_begin, warp);
-    nw = attn::warp_check_pages(a, bt, p_begin, nw, warp, lane);
+    int nw = attn::warp_page_count(p_end - p_begin, warp, NW);
+    nw = attn::warp_check_pages(a, bt, p_begin, nw, warp, lane, NW);
     const size_t page_elems = (size_t)a.Hkv * attn::TILE_HALVES;
     const __half* head_base = a.pool_layer + (size_t)h * attn::TILE_HALVES;
     const int issued = attn::warp_issue_first(S, bt, p_begin, nw, head_base, page_elems, warp, lane);
     attn::warp_pages(a, S, bt, p_begin, nw, issued, n_kv, head_base, page_elems, nullptr, -1, 0, warp, lane);
     __syncthreads();
-    attn::merge_warps(S, threadIdx.x, [&](int hq, float M, float L, float O) {
-        attn::merge_store(a, split, h, m, threadIdx.x, hq, M, L, O);
-    });
+    if (threadIdx.x < D)
+        attn::merge_warps(S, threadIdx.x, [&](int hq, float M, float L, float O) {
+            attn::merge_store(a, split, h, m, threadIdx.x, hq, M, L, O);
+        });
 }
 
 // Merge of the split partials: a warp per (row, query head).
@@ -94,17 +98,23 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a) {
 
 }  // namespace
 
-size_t attn_smem_bytes() { return sizeof(AttnSmem); }
+size_t attn_smem_bytes() { return sizeof(AttnSmem<4>); }
 
-// Opt the kernel into its dynamic shared memory on the current device.
+int attn_warps(int M) { return M <= kAttnWideRows ? 8 : 4; }
+
+// Opt the kernels into their dynamic shared memory on the current device.
 cudaError_t configure_attention() {
-    return cudaFuncSetAttribute(paged_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(AttnSmem));
+    const cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)sizeof(AttnSmem<4>));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(paged_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sizeof(AttnSmem<8>));
 }
 
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s) {
     dim3 grid(a.n_splits, a.Hkv, a.M);
-    launch_k(paged_attn_kernel, grid, dim3(128), sizeof(AttnSmem), s, a);
+    if (attn_warps(a.M) == 8) launch_k(paged_attn_kernel<8>, grid, dim3(256), sizeof(AttnSmem<8>), s, a);
+    else launch_k(paged_attn_kernel<4>, grid, dim3(128), sizeof(AttnSmem<4>), s, a);
 }
 
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s) {

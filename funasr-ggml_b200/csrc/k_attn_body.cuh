@@ -2,16 +2,16 @@
 // device functions: the stand-alone kernel (k_attention.cu) and the one-row persistent
 // step (k_row_step.cu) run the same code, so their outputs are the same bits.
 //
-// Four warps; warp w owns pages w, w+4, ... of the split and streams them through a
-// private STAGES-deep shared-memory ring: lane 0 issues one 8 KiB cp.async.bulk (K and V
-// of this head in this page) per stage, completion is counted on an mbarrier and every
-// wait is bounded in time. Compute per page (lane = (token parity par, 8-dim chunk c)):
+// NW warps (4, or 8 for steps of at most two rows); warp w owns pages w, w+NW, ... of the
+// split and streams them through a private STAGES-deep shared-memory ring: lane 0 issues
+// one 8 KiB cp.async.bulk (K and V of this head in this page) per stage, completion is
+// counted on an mbarrier and every wait is bounded in time. Compute per page (lane = (token parity par, 8-dim chunk c)):
 //   QK  : 8 x 16 B shared loads, 16 fp32 FMAs each (two tokens side by side as packed
 //         pairs), then a 16-lane transpose reduction leaves lane r of each half-warp with
 //         the score of (token 2*(r/2)+par, head r%2)
 //   softmax: max and sum by xor shuffles, running (max, sum) per head in log2 units
 //   PV  : p broadcast through shared memory, 8 x 16 B loads, 16 FMAs each
-// The 4 warps then merge in shared memory; with several splits the un-normalised partials
+// The NW warps then merge in shared memory; with several splits the un-normalised partials
 // go to the scratch buffer and the split merge (combine_head) finishes them.
 #pragma once
 
@@ -21,19 +21,18 @@ namespace fa {
 namespace attn {
 
 constexpr int D = 128;
-constexpr int WARPS = 4;
 constexpr int TILE_HALVES = 2 * kPageTokens * D;   // K then V of one head in one page
 constexpr uint32_t TILE_BYTES = TILE_HALVES * 2;   // 8192
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int STAGES>
+template <int STAGES, int NW>
 struct Smem {
-    __half tiles[WARPS][STAGES][TILE_HALVES];
-    uint64_t bars[WARPS][STAGES];
+    __half tiles[NW][STAGES][TILE_HALVES];
+    uint64_t bars[NW][STAGES];
     float q[2][D];
-    float2 pbuf[WARPS][32];         // each p twice: the PV products take it as a packed pair
-    float acc[WARPS][2][D];
-    float ml[WARPS][4];
+    float2 pbuf[NW][32];            // each p twice: the PV products take it as a packed pair
+    float acc[NW][2][D];
+    float ml[NW][4];
 };
 
 // Two fp32 fused multiply-adds in one instruction (sm_100 packs a pair of fp32 lanes): each
@@ -112,18 +111,18 @@ __device__ __forceinline__ void store_out(const AttnArgs& a, size_t o, float v) 
     if (a.out32) a.out32[o] = v;
 }
 
-// Pages warp `warp` owns in a split of `span` pages.
-__device__ __forceinline__ int warp_page_count(int span, int warp) {
-    return span > warp ? (span - warp + WARPS - 1) / WARPS : 0;
+// Pages warp `warp` of nwarps owns in a split of `span` pages.
+__device__ __forceinline__ int warp_page_count(int span, int warp, int nwarps) {
+    return span > warp ? (span - warp + nwarps - 1) / nwarps : 0;
 }
 
 // The warp's pages checked against the pool (all lanes call): 0 and an error flag when
 // any block-table entry is outside it, else nw.
 __device__ __forceinline__ int warp_check_pages(const AttnArgs& a, const int* bt, int p_begin, int nw, int warp,
-                                                int lane) {
+                                                int lane, int nwarps) {
     bool bad = false;
     for (int i = lane; i < nw; i += 32) {
-        const int pg = bt[p_begin + warp + WARPS * i];
+        const int pg = bt[p_begin + warp + nwarps * i];
         bad |= (pg < 0 || pg >= a.n_pages);
     }
     if (__any_sync(0xffffffffu, bad)) {
@@ -135,13 +134,13 @@ __device__ __forceinline__ int warp_check_pages(const AttnArgs& a, const int* bt
 
 // Lane 0 issues the copies of the warp's first min(STAGES, nw) pages; every lane gets
 // the number issued.
-template <int STAGES>
-__device__ __forceinline__ int warp_issue_first(Smem<STAGES>& S, const int* bt, int p_begin, int nw,
+template <int STAGES, int NW>
+__device__ __forceinline__ int warp_issue_first(Smem<STAGES, NW>& S, const int* bt, int p_begin, int nw,
                                                 const __half* head_base, size_t page_elems, int warp, int lane) {
     int issued = 0;
     if (lane == 0) {
         for (; issued < STAGES && issued < nw; ++issued) {
-            const int pg = bt[p_begin + warp + WARPS * issued];
+            const int pg = bt[p_begin + warp + NW * issued];
             mbar_arrive_expect_tx(&S.bars[warp][issued], TILE_BYTES);
             bulk_copy_g2s(S.tiles[warp][issued], head_base + (size_t)pg * page_elems, TILE_BYTES,
                           &S.bars[warp][issued]);
@@ -168,8 +167,8 @@ __device__ __forceinline__ uint32_t ring_phase_after(uint32_t ph0, int nw) {
 // next completes the phase of parity bit s of ph0 (0 for fresh barriers).
 // patch (or nullptr): the K row then the V row (2 x 128 f16) of token patch_t of the
 // warp's page patch_i, written over the page's shared-memory copy once it has landed.
-template <int STAGES>
-__device__ __forceinline__ void warp_pages(const AttnArgs& a, Smem<STAGES>& S, const int* bt, int p_begin, int nw,
+template <int STAGES, int NW>
+__device__ __forceinline__ void warp_pages(const AttnArgs& a, Smem<STAGES, NW>& S, const int* bt, int p_begin, int nw,
                                            int issued, int n_kv, const __half* head_base, size_t page_elems,
                                            const __half* patch, int patch_i, int patch_t, int warp, int lane,
                                            uint32_t ph0 = 0u) {
@@ -197,7 +196,7 @@ __device__ __forceinline__ void warp_pages(const AttnArgs& a, Smem<STAGES>& S, c
         const bool got = mbar_wait_bounded(&S.bars[warp][s], ph);
         if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
 
-        const int t0 = (p_begin + warp + WARPS * i) * kPageTokens;
+        const int t0 = (p_begin + warp + NW * i) * kPageTokens;
         const int nvalid = min(kPageTokens, n_kv - t0);
         __half* Kt = S.tiles[warp][s];
         const __half* Vt = Kt + kPageTokens * D;
@@ -286,7 +285,7 @@ __device__ __forceinline__ void warp_pages(const AttnArgs& a, Smem<STAGES>& S, c
         __syncwarp();
         if (lane == 0 && i + STAGES < nw) {
             fence_proxy_async_smem();
-            const int pg = bt[p_begin + warp + WARPS * (i + STAGES)];
+            const int pg = bt[p_begin + warp + NW * (i + STAGES)];
             mbar_arrive_expect_tx(&S.bars[warp][s], TILE_BYTES);
             bulk_copy_g2s(S.tiles[warp][s], head_base + (size_t)pg * page_elems, TILE_BYTES, &S.bars[warp][s]);
         }
@@ -332,20 +331,20 @@ __device__ __forceinline__ void warp_pages(const AttnArgs& a, Smem<STAGES>& S, c
     }
 }
 
-// Merge of the 4 warps' partials (after a barrier over the 4 warps), thread d < 128 of
-// them owning dim d: for each of the two query heads hq, the maximum M, the sum L and the
-// output O, handed to epi(hq, M, L, O).
-template <int STAGES, typename Epi>
-__device__ __forceinline__ void merge_warps(const Smem<STAGES>& S, int d, Epi epi) {
+// Merge of the NW warps' partials (after a barrier over them), thread d < 128 owning dim
+// d: for each of the two query heads hq, the maximum M, the sum L and the output O (warps
+// in order), handed to epi(hq, M, L, O).
+template <int STAGES, int NW, typename Epi>
+__device__ __forceinline__ void merge_warps(const Smem<STAGES, NW>& S, int d, Epi epi) {
 #pragma unroll
     for (int hq = 0; hq < 2; ++hq) {
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < WARPS; ++w) M = fmaxf(M, S.ml[w][hq]);
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, S.ml[w][hq]);
         float L = 0.0f, O = 0.0f;
         if (M != -INFINITY) {
 #pragma unroll
-            for (int w = 0; w < WARPS; ++w) {
+            for (int w = 0; w < NW; ++w) {
                 const float sc = exp2f(S.ml[w][hq] - M);
                 L = fmaf(S.ml[w][2 + hq], sc, L);
                 O = fmaf(S.acc[w][hq][d], sc, O);

@@ -23,10 +23,12 @@
 // them (each phase needs every row of the one before). Each CTA keeps its own copy of
 // the residual stream in shared memory.
 //
-// The weights of the next phase do not depend on its input: each warp loads its next rows
-// into registers before it polls, and the attention items start their page copies (4-deep
-// rings, barriers initialised once and their phases counted across layers) during the
-// previous layer. The token's own K/V row, computed in phase B, is written to its page and
+// The weights of the next phase do not depend on its input: as soon as a phase's dot
+// products are done, one thread stages the CTA's rows of the next GEMM into shared memory
+// by bulk copies (so the copies leave the load/store unit free for the polls), the next
+// norm's weights follow by cp.async, and the attention items start their page copies
+// (2-deep rings on all 8 warps, barriers initialised once, their phases counted) during
+// the previous layer. The token's own K/V row, computed in phase B, is written to its page and
 // patched into the page's shared-memory copy.
 //
 // Same arithmetic as the launch-per-op step with the CUDA-core GEMMs (k_gemv.cu): a GEMV
@@ -50,22 +52,26 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnitsPerWarp = 4;
 constexpr int kMaxUnits = kWarps * kUnitsPerWarp;
-constexpr int kRowStages = 4;
+constexpr int kRowStages = 2;           // page ring depth: 16 pages per split in flight
 constexpr int kWpl = 16;                 // int8 weights per lane per unit
 constexpr int kSlice = 32 * kWpl;        // columns of a unit
 constexpr int D = 128;
 constexpr int kHq = 16, kHkv = 8;
 constexpr int kQkvN = (kHq + 2 * kHkv) * D;
 constexpr int kPollWords = 16;           // words one thread polls at a time
-using ASmem = attn::Smem<kRowStages>;
+constexpr int kAttnNW = 8;               // the attention item's warps: the whole CTA
+using ASmem = attn::Smem<kRowStages, kAttnNW>;
 
 struct RowSmem {
     ASmem att;
     float red[kMaxUnits][4];
     double sh[kWarps];
     __half newkv[2 * D];       // the token's K row then V row (f16), for the page patch
+    uint64_t wbar;             // completion of the staged weights' bulk copies
     int last;
-    alignas(16) float buf[4];  // act [max(hidden, Hq * 128, ffn)], x [hidden], part [hidden]
+    // act [max(hidden, Hq * 128, ffn)] (permuted, act_index), x [hidden], part [hidden], norm weights [2][hidden],
+    // then the staged weights: q rows [rows][K] int8, then their scales [rows][K / 32] f16
+    alignas(128) float buf[4];
 };
 
 __host__ __device__ inline size_t act_floats(int hidden, int ffn) {
@@ -73,11 +79,9 @@ __host__ __device__ inline size_t act_floats(int hidden, int ffn) {
     return (size_t)(k > kHq * D ? k : kHq * D);
 }
 
-// Weights of a warp's units for the next GEMV phase, held in registers while it polls.
-struct WRegs {
-    uint4 q[kUnitsPerWarp][4];
-    float d[kUnitsPerWarp][4];
-};
+__host__ __device__ inline size_t stage_offset(int hidden, int ffn) {   // bytes from buf, 128-aligned
+    return ((act_floats(hidden, ffn) + 4 * (size_t)hidden) * sizeof(float) + 127) / 128 * 128;
+}
 
 // The CTA's share of a GEMM: row blocks (or gate/up pairs) [b0, b0 + nb) and its units.
 struct Span {
@@ -93,61 +97,97 @@ __device__ __forceinline__ Span cta_span(const RowGemm& g, int cta, int G) {
     return s;
 }
 
-// Unit u of the span -> first weight row n0 and K slice c. SwiGLU units run pair by pair:
-// the ks units of the gate rows of output columns f0..f0+3, then those of their up rows
-// (gate row f is weight row (f/64)*128 + f%64, its up row 64 further).
-__device__ __forceinline__ void unit_rows(const RowGemm& g, const Span& s, int u, int& n0, int& c) {
-    c = u % g.ks;
+// The CTA's share of a GEMM as runs of consecutive weight rows: run(n, rr, cnt) for
+// weight rows [n, n + cnt) that go to staged rows [rr, rr + cnt).
+template <typename Run>
+__device__ __forceinline__ void share_runs(const RowGemm& g, const Span& s, Run run) {
     if (!g.swiglu) {
-        n0 = 4 * (s.b0 + u / g.ks);
-    } else {
-        const int pl = u / (2 * g.ks), which = (u / g.ks) & 1;
-        const int f0 = 4 * (s.b0 + pl);
-        n0 = (f0 / 64) * 128 + f0 % 64 + 64 * which;
+        run(4 * s.b0, 0, 4 * s.nb);
+        return;
+    }
+    // output columns f in [4 b0, 4 (b0 + nb)): gate row (f/64)*128 + f%64, up row 64 further;
+    // consecutive f map to consecutive rows within a 64-block
+    const int f0 = 4 * s.b0, f1 = 4 * (s.b0 + s.nb);
+    for (int fa = f0; fa < f1;) {
+        const int fb = min(f1, (fa / 64 + 1) * 64);
+        for (int which = 0; which < 2; ++which)
+            run((fa / 64) * 128 + fa % 64 + 64 * which, which * 4 * s.nb + (fa - f0), fb - fa);
+        fa = fb;
     }
 }
 
-__device__ __forceinline__ void load_units(WRegs& w, const RowGemm& g, const Span& s, const unsigned char* planes,
-                                           int warp, int lane) {
-    const int8_t* q = reinterpret_cast<const int8_t*>(planes);
-    const __half* dr = reinterpret_cast<const __half*>(planes + q8p_dr_offset(g.N, g.K));
-#pragma unroll
-    for (int i = 0; i < kUnitsPerWarp; ++i) {
-        const int u = warp + kWarps * i;
-        if (u >= s.n_units) break;
-        int n0, c;
-        unit_rows(g, s, u, n0, c);
+// Thread 0: one bulk copy per run of the CTA's share (q rows, then the same rows' scales)
+// into the staging area, completion on bar.
+__device__ __forceinline__ void stage_weights(const RowGemm& g, const Span& s, const unsigned char* planes,
+                                              unsigned char* sq, __half* sd, uint64_t* bar) {
+    const size_t dr_off = q8p_dr_offset(g.N, g.K);
+    const uint32_t rows = (uint32_t)(s.nb * (g.swiglu ? 8 : 4));
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, rows * (uint32_t)(g.K + g.K / 16));
+    share_runs(g, s, [&](int n, int rr, int cnt) {
+        bulk_copy_g2s(sq + (size_t)rr * g.K, planes + (size_t)n * g.K, (uint32_t)(cnt * g.K), bar);
+        bulk_copy_g2s(sd + (size_t)rr * (g.K / kQK), planes + dr_off + (size_t)n * (g.K / 16),
+                      (uint32_t)(cnt * (g.K / 16)), bar);
+    });
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Thread 0: the CTA's shares of one layer's four GEMMs (and its norm weights) into L2, so
+// that their staging copies a phase later find them there.
+__device__ __forceinline__ void prefetch_layer(const RowStepArgs& a, const RowLayer* L, int cta, int G) {
+    for (int i = 0; i < 4; ++i) {
+        const RowGemm& g = a.gm[i];
+        const unsigned char* w = L->w[i];
+        const size_t dr_off = q8p_dr_offset(g.N, g.K);
+        share_runs(g, cta_span(g, cta, G), [&](int n, int, int cnt) {
+            prefetch_l2(w + (size_t)n * g.K, (uint32_t)(cnt * g.K));
+            prefetch_l2(w + dr_off + (size_t)n * (g.K / 16), (uint32_t)(cnt * (g.K / 16)));
+        });
+    }
+    prefetch_l2(L->in_norm, (uint32_t)a.hidden * 4);
+    prefetch_l2(L->post_norm, (uint32_t)a.hidden * 4);
+}
+
+// The activation row in shared memory is stored permuted within each 512-column slice:
+// column c*512 + l*16 + 4h + e (lane l's 16 values, piece h) sits at c*512 + h*128 + l*4 + e,
+// so that the four 16 B loads of a warp's lanes read consecutive chunks (no bank conflict).
+__device__ __forceinline__ int act_index(int j) {
+    return (j & ~511) | (((j >> 2) & 3) << 7) | (((j >> 4) & 31) << 2) | (j & 3);
+}
+
+// Every unit of the warp: 4 dot products of 512 columns of the staged rows with act, the
+// CUDA-core kernel's arithmetic; lane 0 leaves the 4 sums in red[u]. The unit's four rows
+// are consecutive staged rows.
+__device__ __forceinline__ void dot_units(const RowGemm& g, const Span& s, const unsigned char* sq, const __half* sd,
+                                          const float* act, float (*red)[4], int warp, int lane) {
+    const int K = g.K, ks = g.ks;
+#pragma unroll 1
+    for (int u = warp; u < s.n_units; u += kWarps) {
+        const int blk = u / ks;                 // row block (SwiGLU: gate or up block of a pair)
+        const int c = u - blk * ks;             // K slice
+        const int rr0 = g.swiglu ? (blk & 1) * 4 * s.nb + 4 * (blk >> 1) : 4 * blk;
         const int k0 = c * kSlice + lane * kWpl;
+        uint4 q[4];
+        float dsc[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            w.q[i][r] = __ldg(reinterpret_cast<const uint4*>(q + (size_t)(n0 + r) * g.K + k0));
-            w.d[i][r] = __half2float(dr[(size_t)(n0 + r) * (g.K / kQK) + k0 / kQK]);
+            q[r] = lds128(sq + (size_t)(rr0 + r) * K + k0);
+            dsc[r] = __half2float(sd[(size_t)(rr0 + r) * (K / kQK) + k0 / kQK]);
         }
-    }
-}
-
-// Every unit of the warp: 4 dot products of 512 columns with act (shared memory), the
-// CUDA-core kernel's arithmetic; lane 0 leaves the 4 sums in red[u].
-__device__ __forceinline__ void dot_units(const WRegs& w, const RowGemm& g, const Span& s, const float* act,
-                                          float (*red)[4], int warp, int lane) {
-#pragma unroll
-    for (int i = 0; i < kUnitsPerWarp; ++i) {
-        const int u = warp + kWarps * i;
-        if (u >= s.n_units) break;
-        int n0, c;
-        unit_rows(g, s, u, n0, c);
-        const int k0 = c * kSlice + lane * kWpl;
         float x[kWpl];
 #pragma unroll
         for (int h = 0; h < kWpl / 4; ++h) {
-            const float4 t = reinterpret_cast<const float4*>(act + k0)[h];
+            const float4 t = *reinterpret_cast<const float4*>(act + c * kSlice + h * 128 + lane * 4);
             x[4 * h] = t.x; x[4 * h + 1] = t.y; x[4 * h + 2] = t.z; x[4 * h + 3] = t.w;
         }
         float acc[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             // int8 -> f32 exactly: the byte q + 128 under the exponent of 2^23 reads as 2^23 + q + 128
-            const uint32_t* wb = reinterpret_cast<const uint32_t*>(&w.q[i][r]);
+            const uint32_t wb[4] = {q[r].x, q[r].y, q[r].z, q[r].w};
             float wf[kWpl];
 #pragma unroll
             for (int j4 = 0; j4 < kWpl / 4; ++j4) {
@@ -156,11 +196,11 @@ __device__ __forceinline__ void dot_units(const WRegs& w, const RowGemm& g, cons
                 for (int b = 0; b < 4; ++b)
                     wf[4 * j4 + b] = __int_as_float((int)__byte_perm(v, 0x4B000000u, 0x7540u + (unsigned)b)) - 8388736.0f;
             }
-            float sq = 0.0f;
+            float sq_ = 0.0f;
 #pragma unroll
-            for (int j = 0; j < kWpl; ++j) sq = fmaf(wf[j], x[j], sq);
+            for (int j = 0; j < kWpl; ++j) sq_ = fmaf(wf[j], x[j], sq_);
             acc[r] = 0.0f;
-            acc[r] = fmaf(w.d[i][r], sq, acc[r]);
+            acc[r] = fmaf(dsc[r], sq_, acc[r]);
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -170,6 +210,12 @@ __device__ __forceinline__ void dot_units(const WRegs& w, const RowGemm& g, cons
 #pragma unroll
             for (int r = 0; r < 4; ++r) red[u][r] = acc[r];
     }
+}
+
+// Norm weights [n] into shared memory by cp.async (waited for by the next poll).
+__device__ __forceinline__ void prefetch_norm(float* dst, const float* src, int n) {
+    for (int i = 4 * threadIdx.x; i < n; i += 4 * kThreads) cp_async16(dst + i, src + i, true);
+    cp_async_commit();
 }
 
 // ------------------------------------------------------------------ words --
@@ -254,6 +300,7 @@ __device__ __forceinline__ bool poll_words(const RowStepArgs& a, const unsigned 
                              return i < n ? src + i : nullptr;
                          },
                          [&](int u, uint32_t v) { f(i0 + u * kThreads, v); });
+    cp_async_wait<0>();     // this thread's norm-weight prefetch, if any
     return __syncthreads_or(!ok) == 0;
 }
 
@@ -276,7 +323,6 @@ __device__ __forceinline__ void finish_units(const RowGemm& g, const Span& s, co
     }
 }
 
-__device__ __forceinline__ void bar_sync_attn() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -285,6 +331,10 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
     float* act = S.buf;
     float* xr = S.buf + act_floats(a.hidden, a.ffn);   // this CTA's copy of the residual stream
     float* part = xr + Hd;                             // the sum the next norm adds to it
+    float* nrm_in = part + Hd;                         // the layer's norm weights, prefetched
+    float* nrm_post = nrm_in + Hd;
+    unsigned char* sq = reinterpret_cast<unsigned char*>(S.buf) + stage_offset(a.hidden, a.ffn);
+    __half* sd = reinterpret_cast<__half*>(sq + a.stage_q_bytes);
     const int cta = blockIdx.x, G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (cta == a.absent_cta) return;    // failure test: the words of its rows never arrive
@@ -313,10 +363,12 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
     const size_t page_elems = (size_t)kHkv * attn::TILE_HALVES;
 
     if (threadIdx.x == 0) {
-        for (int w = 0; w < attn::WARPS; ++w)
+        for (int w = 0; w < kAttnNW; ++w)
             for (int s = 0; s < kRowStages; ++s) mbar_init(&S.att.bars[w][s], 1);
+        mbar_init(&S.wbar, 1);
         fence_mbar_init();
     }
+    prefetch_norm(nrm_in, a.layers[0].in_norm, Hd);
     // ---- layer 0's input row
     const bool embed_row = !a.x_ready && a.tok[0] != -1;
     if (embed_row) {
@@ -335,169 +387,199 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
     } else {
         for (int i = threadIdx.x; i < Hd; i += kThreads) xr[i] = a.x_a[i];
     }
+    cp_async_wait<0>();
     __syncthreads();
 
-    const Span sp_qkv = cta_span(a.gm[0], cta, G), sp_o = cta_span(a.gm[1], cta, G);
-    const Span sp_gu = cta_span(a.gm[2], cta, G), sp_dn = cta_span(a.gm[3], cta, G);
-    WRegs wr;
-    load_units(wr, a.gm[0], sp_qkv, a.layers[0].w[0], warp, lane);
+    // the staged weights: issued by the last warp's lane 0 (whose warp has no share of the
+    // phases' output rows, so the words go out without waiting for it) as soon as the
+    // buffer is free, waited for by every thread before its dot products
+    const bool issuer = threadIdx.x == kThreads - 32;
+    uint32_t wpar = 0u;
+    bool wpend = false;
+    auto stage = [&](int gi, const unsigned char* planes) {
+        if (issuer) stage_weights(a.gm[gi], cta_span(a.gm[gi], cta, G), planes, sq, sd, &S.wbar);
+        wpend = true;
+    };
+    stage(0, a.layers[0].w[0]);
+    if (issuer) prefetch_layer(a, a.layers, cta, G);
 
-    auto emit_act = [&](int j, float y) { act[j] = pair_value(y); };
-    auto to_part = [&](int i, uint32_t v) { part[i] = __uint_as_float(v); };
+    auto emit_act = [&](int j, float y) { act[act_index(j)] = pair_value(y); };
     // the page ring's barriers are initialised once; bit s = parity of stage s's next phase
     uint32_t ring_ph = 0u;
     int nw = 0, issued = 0;        // this warp's pages of the item and copies in flight
     // The item's page copies of layer l start (attention warps); the ring's shared memory
     // was last read and patched by generic accesses, hence the proxy fence.
     auto start_pages = [&](int l) {
-        if (item && warp < attn::WARPS) {
+        if (item) {
             if (lane == 0) fence_proxy_async_smem();
             __syncwarp();
             const __half* hb = a.pool + (size_t)l * a.layer_stride + (size_t)h * attn::TILE_HALVES;
-            nw = attn::warp_page_count(p_end - p_begin, warp);
-            nw = attn::warp_check_pages(at, bt, p_begin, nw, warp, lane);
+            nw = attn::warp_page_count(p_end - p_begin, warp, kAttnNW);
+            nw = attn::warp_check_pages(at, bt, p_begin, nw, warp, lane, kAttnNW);
             issued = attn::warp_issue_first(S.att, bt, p_begin, nw, hb, page_elems, warp, lane);
         }
     };
-    // nothing may land in shared memory after the CTA has left: wait (bounded) for the
-    // copies in flight
-    auto leave = [&]() {
-        if (item && warp < attn::WARPS)
+    start_pages(0);
+
+    // The layer loop. The four GEMV phases (A: QKV, C: o_proj, D: gate|up, E: down; GEMM gi =
+    // 0..3) run one code path with CTA-uniform parameters, and B (attention) follows A inside
+    // it, so that each piece of code appears once: the kernel's instructions then stay in
+    // the SM's instruction cache from layer to layer.
+    bool ok = true;
+    for (int l = 0; l < a.n_layers && ok; ++l) {
+        const RowLayer* Lp = a.layers + l;
+        const uint32_t tag = tag0 + (uint32_t)l;
+        __half* pool_l = a.pool + (size_t)l * a.layer_stride;
+        at.pool_layer = pool_l;
+
+        for (int gi = 0; gi < 4; ++gi) {
+            // ---- the phase's input: the previous phase's words; the next norm's weights
+            if (gi == 1) prefetch_norm(nrm_post, Lp->post_norm, Hd);
+            if (gi == 3) {
+                if (l + 1 < a.n_layers) prefetch_norm(nrm_in, Lp[1].in_norm, Hd);
+                else if (cta == 0) prefetch_norm(nrm_in, a.final_norm, Hd);
+            }
+            const bool pairs = gi == 1 || gi == 3;   // attention output, SwiGLU output: f16 pairs
+            if (gi != 0 || l > 0) {
+                const unsigned long long* src = gi == 0 ? a.w_dn : gi == 1 ? a.w_att : gi == 2 ? a.w_o : a.w_h;
+                const int n = gi == 1 ? kHq * D : gi == 3 ? a.ffn : Hd;
+                ok = poll_words(a, src, n, gi == 0 ? tag - 1u : tag, [&](int i, uint32_t v) {
+                    if (pairs) act[act_index(i)] = pair_sum(v);
+                    else part[i] = __uint_as_float(v);
+                });
+                if (!ok) break;
+            }
+            if (gi == 0 || gi == 2) {
+                const bool first = gi == 0 && l == 0;   // the embedding row: nothing to add
+                residual_norm_row<8, false>(xr, first ? nullptr : reinterpret_cast<const float4*>(part), 0,
+                                            first ? 0 : 1, Hd, gi == 0 ? nrm_in : nrm_post, a.eps,
+                                            first ? nullptr : xr, S.sh, emit_act);
+            }
+            // ---- the staged weights, the dot products, the next staging, the words out
+            {
+                const bool got = mbar_wait_bounded(&S.wbar, wpar);
+                wpar ^= 1u;
+                wpend = false;
+                if (__syncthreads_or(!got)) {
+                    if (threadIdx.x == 0) {
+                        record_error(a.err, kDevErrTimeout);
+                        atomicExch(&a.ctl->abort, 1);
+                    }
+                    ok = false;
+                    break;
+                }
+            }
+            const RowGemm& g = a.gm[gi];
+            const Span sp = cta_span(g, cta, G);
+            dot_units(g, sp, sq, sd, act, S.red, warp, lane);
+            __syncthreads();
+            if (gi < 3) stage(gi + 1, Lp->w[gi + 1]);
+            else if (l + 1 < a.n_layers) stage(0, Lp[1].w[0]);
+            finish_units(g, sp, S.red, gi == 0 ? a.w_qkv : gi == 1 ? a.w_o : gi == 2 ? a.w_h : a.w_dn, tag);
+            if (gi == 0 && issuer && l + 1 < a.n_layers) prefetch_layer(a, Lp + 1, cta, G);
+            if (gi == 3 && l + 1 < a.n_layers) start_pages(l + 1);
+            if (gi != 0 || !item) continue;
+
+            // ---------------- B: kernel (1) for the item's heads, then attention
+            bool hok = true;
+            if (warp >= 4) {
+                const int v = warp - 4;     // q heads 2h, 2h+1, then K and V of head h
+                const int j = v < 2 ? 2 * h + v : (v == 2 ? kHq + h : kHq + kHkv + h);
+                if (v < 2 || owner) {
+                    AppendArgs app{};
+                    app.n_part = 1; app.M = 1; app.pos = a.pos; app.slot = a.slot;
+                    app.block_table = a.block_table; app.bt_stride = a.bt_stride; app.n_pages = a.n_pages;
+                    app.qn_w = Lp->q_norm; app.kn_w = Lp->k_norm; app.Hq = kHq; app.Hkv = kHkv; app.eps = a.eps;
+                    app.q_scale = a.q_scale; app.rope = a.rope; app.max_pos = a.max_pos;
+                    app.pool_layer = pool_l; app.q_out = nullptr; app.err = a.err;
+                    // the head's norm weights, rotation and page do not depend on the words
+                    const HeadRowMeta meta = qkv_head_meta(app, 0, j, lane);
+                    float x[4];
+                    hok = poll_thread(a, tag,
+                                      [&](int u) -> const unsigned long long* {
+                                          return u < 4 ? a.w_qkv + j * D + lane + 32 * u : nullptr;
+                                      },
+                                      [&](int u, uint32_t w) { x[u] = __fadd_rn(0.0f, __uint_as_float(w)); });
+                    // the lanes poll their own words, but the head's norm shuffles over the
+                    // whole warp: all lanes go on, or none
+                    hok = __all_sync(0xffffffffu, hok);
+                    if (hok)
+                        qkv_head_apply(app, meta, 0, j, lane, x, v < 2 ? S.att.q[v] : nullptr,
+                                       v < 2 ? nullptr : S.newkv + (v - 2) * D);
+                }
+            }
+            if (__syncthreads_or(!hok)) {
+                ok = false;
+                break;
+            }
+            // every warp of the CTA takes pages
+            const int t = threadIdx.x;
+            if (t < D) {
+                S.att.q[0][t] = S.att.q[0][t] * attn::kLog2e;
+                S.att.q[1][t] = S.att.q[1][t] * attn::kLog2e;
+            }
+            __syncthreads();
+            const int rel = p_last - p_begin;
+            const int patch_i = owner && warp == rel % kAttnNW ? rel / kAttnNW : -1;
+            const __half* head_base = pool_l + (size_t)h * attn::TILE_HALVES;
+            attn::warp_pages(at, S.att, bt, p_begin, nw, issued, n_kv, head_base, page_elems,
+                             owner ? S.newkv : nullptr, patch_i, pos % kPageTokens, warp, lane, ring_ph);
+            ring_ph = attn::ring_phase_after<kRowStages>(ring_ph, nw);
+            issued = 0;
+            __syncthreads();
+            if (a.n_splits == 1) {
+                if (t < D)
+                    attn::merge_warps(S.att, t, [&](int hq, float, float Ls, float Os) {
+                        st_word(a.w_att + (2 * h + hq) * D + t, pack_pair(Ls > 0.0f ? Os / Ls : 0.0f), tag);
+                    });
+            } else {
+                // partials to the scratch; the split that finishes last merges the head's
+                // splits and writes its words
+                if (t < D)
+                    attn::merge_warps(S.att, t, [&](int hq, float M, float Ls, float Os) {
+                        attn::merge_store(at, split, h, 0, t, hq, M, Ls, Os);
+                    });
+                __syncthreads();
+                if (t == 0) {
+                    __threadfence();
+                    const int old = atomicAdd(&a.ctl->att_cnt[h], 1);
+                    S.last = old == n_valid - 1;
+                    if (S.last) {
+                        __threadfence();
+                        a.ctl->att_cnt[h] = 0;
+                    }
+                }
+                __syncthreads();
+                if (S.last && warp < 2) {
+                    const int H = 2 * h + warp;
+                    attn::combine_head<true>(at, 0, H, lane, [&](int d, float v) {
+                        st_word(a.w_att + H * D + d, pack_pair(v), tag);
+                    });
+                }
+            }
+        }
+    }
+    if (!ok) {
+        // nothing may land in shared memory after the CTA has left: wait (bounded) for the
+        // copies in flight
+        cp_async_wait<0>();
+        if (wpend) (void)mbar_wait_bounded(&S.wbar, wpar);
+        if (item)
             for (int k = 0; k < issued; ++k) {
                 const int st = k % kRowStages;
                 const bool done = mbar_wait_bounded(&S.att.bars[warp][st],
                                                     ((uint32_t)(k / kRowStages) & 1u) ^ ((ring_ph >> st) & 1u));
                 (void)__all_sync(0xffffffffu, done);
             }
-    };
-    start_pages(0);
-
-    for (int l = 0; l < a.n_layers; ++l) {
-        const RowLayer L = a.layers[l];
-        const uint32_t tag = tag0 + (uint32_t)l;
-        __half* pool_l = a.pool + (size_t)l * a.layer_stride;
-        at.pool_layer = pool_l;
-        const __half* head_base = pool_l + (size_t)h * attn::TILE_HALVES;
-
-        // ---------------- A: norm + QKV (the item's page copies are in flight)
-        if (l == 0) {
-            residual_norm_row<8, false>(xr, nullptr, 0, 0, Hd, L.in_norm, a.eps, nullptr, S.sh, emit_act);
-        } else {
-            if (!poll_words(a, a.w_dn, Hd, tag - 1u, to_part)) return leave();
-            residual_norm_row<8, false>(xr, reinterpret_cast<const float4*>(part), 0, 1, Hd, L.in_norm, a.eps, xr,
-                                        S.sh, emit_act);
-        }
-        __syncthreads();
-        dot_units(wr, a.gm[0], sp_qkv, act, S.red, warp, lane);
-        __syncthreads();
-        finish_units(a.gm[0], sp_qkv, S.red, a.w_qkv, tag);
-
-        // ---------------- B: kernel (1) for the item's heads, then attention
-        if (item) {
-            bool ok = true;
-            if (warp >= 4) {
-                const int v = warp - 4;     // q heads 2h, 2h+1, then K and V of head h
-                const int j = v < 2 ? 2 * h + v : (v == 2 ? kHq + h : kHq + kHkv + h);
-                if (v < 2 || owner) {
-                    float x[4];
-                    ok = poll_thread(a, tag,
-                                     [&](int u) -> const unsigned long long* {
-                                         return u < 4 ? a.w_qkv + j * D + lane + 32 * u : nullptr;
-                                     },
-                                     [&](int u, uint32_t w) { x[u] = __fadd_rn(0.0f, __uint_as_float(w)); });
-                    // the lanes poll their own words, but the head's norm shuffles over the
-                    // whole warp: all lanes go on, or none
-                    ok = __all_sync(0xffffffffu, ok);
-                    if (ok) {
-                        AppendArgs app{};
-                        app.n_part = 1; app.M = 1; app.pos = a.pos; app.slot = a.slot;
-                        app.block_table = a.block_table; app.bt_stride = a.bt_stride; app.n_pages = a.n_pages;
-                        app.qn_w = L.q_norm; app.kn_w = L.k_norm; app.Hq = kHq; app.Hkv = kHkv; app.eps = a.eps;
-                        app.q_scale = a.q_scale; app.rope = a.rope; app.max_pos = a.max_pos;
-                        app.pool_layer = pool_l; app.q_out = nullptr; app.err = a.err;
-                        const HeadRowMeta meta = qkv_head_meta(app, 0, j, lane);
-                        qkv_head_apply(app, meta, 0, j, lane, x, v < 2 ? S.att.q[v] : nullptr,
-                                       v < 2 ? nullptr : S.newkv + (v - 2) * D);
-                    }
-                }
-            }
-            if (__syncthreads_or(!ok)) return leave();
-            if (warp < attn::WARPS) {
-                const int t = threadIdx.x;
-                S.att.q[0][t] = S.att.q[0][t] * attn::kLog2e;
-                S.att.q[1][t] = S.att.q[1][t] * attn::kLog2e;
-                bar_sync_attn();
-                const int rel = p_last - p_begin;
-                const int patch_i = owner && warp == rel % attn::WARPS ? rel / attn::WARPS : -1;
-                attn::warp_pages(at, S.att, bt, p_begin, nw, issued, n_kv, head_base, page_elems,
-                                 owner ? S.newkv : nullptr, patch_i, pos % kPageTokens, warp, lane, ring_ph);
-                ring_ph = attn::ring_phase_after<kRowStages>(ring_ph, nw);
-                issued = 0;
-                bar_sync_attn();
-                if (a.n_splits == 1) {
-                    attn::merge_warps(S.att, t, [&](int hq, float, float Ls, float Os) {
-                        st_word(a.w_att + (2 * h + hq) * D + t, pack_pair(Ls > 0.0f ? Os / Ls : 0.0f), tag);
-                    });
-                } else {
-                    // partials to the scratch; the split that finishes last merges the head's
-                    // splits and writes its words
-                    attn::merge_warps(S.att, t, [&](int hq, float M, float Ls, float Os) {
-                        attn::merge_store(at, split, h, 0, t, hq, M, Ls, Os);
-                    });
-                    bar_sync_attn();
-                    if (t == 0) {
-                        __threadfence();
-                        const int old = atomicAdd(&a.ctl->att_cnt[h], 1);
-                        S.last = old == n_valid - 1;
-                        if (S.last) {
-                            __threadfence();
-                            a.ctl->att_cnt[h] = 0;
-                        }
-                    }
-                    bar_sync_attn();
-                    if (S.last && warp < 2) {
-                        const int H = 2 * h + warp;
-                        attn::combine_head<true>(at, 0, H, lane, [&](int d, float v) {
-                            st_word(a.w_att + H * D + d, pack_pair(v), tag);
-                        });
-                    }
-                }
-            }
-        }
-        load_units(wr, a.gm[1], sp_o, L.w[1], warp, lane);
-
-        // ---------------- C: o_proj
-        if (!poll_words(a, a.w_att, kHq * D, tag, [&](int i, uint32_t v) { act[i] = pair_sum(v); })) return leave();
-        dot_units(wr, a.gm[1], sp_o, act, S.red, warp, lane);
-        __syncthreads();
-        finish_units(a.gm[1], sp_o, S.red, a.w_o, tag);
-        load_units(wr, a.gm[2], sp_gu, L.w[2], warp, lane);
-
-        // ---------------- D: norm + gate|up + SwiGLU
-        if (!poll_words(a, a.w_o, Hd, tag, to_part)) return leave();
-        residual_norm_row<8, false>(xr, reinterpret_cast<const float4*>(part), 0, 1, Hd, L.post_norm, a.eps, xr, S.sh,
-                                    emit_act);
-        __syncthreads();
-        dot_units(wr, a.gm[2], sp_gu, act, S.red, warp, lane);
-        __syncthreads();
-        finish_units(a.gm[2], sp_gu, S.red, a.w_h, tag);
-        load_units(wr, a.gm[3], sp_dn, L.w[3], warp, lane);
-
-        // ---------------- E: down
-        if (!poll_words(a, a.w_h, a.ffn, tag, [&](int i, uint32_t v) { act[i] = pair_sum(v); })) return leave();
-        dot_units(wr, a.gm[3], sp_dn, act, S.red, warp, lane);
-        __syncthreads();
-        finish_units(a.gm[3], sp_dn, S.red, a.w_dn, tag);
-        if (l + 1 < a.n_layers) {
-            load_units(wr, a.gm[0], sp_qkv, a.layers[l + 1].w[0], warp, lane);
-            start_pages(l + 1);
-        }
+        return;
     }
 
     // ---------------- final norm: the lm_head's input pair (CTA 0)
     if (cta != 0) return;
-    if (!poll_words(a, a.w_dn, Hd, tag0 + (uint32_t)a.n_layers - 1u, to_part)) return;
-    residual_norm_row<8, false>(xr, reinterpret_cast<const float4*>(part), 0, 1, Hd, a.final_norm, a.eps, xr, S.sh,
+    if (!poll_words(a, a.w_dn, Hd, tag0 + (uint32_t)a.n_layers - 1u,
+                    [&](int i, uint32_t v) { part[i] = __uint_as_float(v); }))
+        return;
+    residual_norm_row<8, false>(xr, reinterpret_cast<const float4*>(part), 0, 1, Hd, nrm_in, a.eps, xr, S.sh,
                                 [&](int j, float y) { split_store(y, a.xn16, a.xn_lo, (size_t)j); });
     __syncthreads();
     for (int i = threadIdx.x; i < Hd; i += kThreads) a.x_a[i] = xr[i];
@@ -507,6 +589,21 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
 }
 
 }  // namespace
+
+// Bytes of the largest share of q rows one CTA stages (its row blocks of one GEMM x K).
+static size_t stage_q_bytes(const RowGemm* gm, int grid) {
+    size_t m = 0;
+    for (int i = 0; i < 4; ++i) {
+        const int total = gm[i].swiglu ? gm[i].N / 8 : gm[i].N / 4;
+        const size_t rows = (size_t)((total + grid - 1) / grid) * (gm[i].swiglu ? 8 : 4);
+        m = rows * gm[i].K > m ? rows * gm[i].K : m;
+    }
+    return m;
+}
+
+static size_t smem_bytes(int hidden, int ffn, size_t sq_bytes) {
+    return offsetof(RowSmem, buf) + stage_offset(hidden, ffn) + sq_bytes + sq_bytes / 16;
+}
 
 bool row_step_shapes(int hidden, int ffn, int grid, RowGemm* gm) {
     if (hidden <= 0 || hidden > 4096 || hidden % kSlice || ffn % kSlice || grid <= 0) return false;
@@ -528,11 +625,7 @@ bool row_step_shapes(int hidden, int ffn, int grid, RowGemm* gm) {
         const int per_cta = (total + grid - 1) / grid;
         if (per_cta * ks * (g.swiglu ? 2 : 1) > kMaxUnits) return false;
     }
-    return row_step_smem_bytes(hidden, ffn) <= 227 * 1024;
-}
-
-size_t row_step_smem_bytes(int hidden, int ffn) {
-    return offsetof(RowSmem, buf) + sizeof(float) * (act_floats(hidden, ffn) + 2 * (size_t)hidden);
+    return smem_bytes(hidden, ffn, stage_q_bytes(gm, grid)) <= 227 * 1024;
 }
 
 size_t row_step_words(int hidden, int ffn) {
@@ -543,11 +636,13 @@ cudaError_t configure_row_step() {
     return cudaFuncSetAttribute(row_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
-cudaError_t launch_row_step(const RowStepArgs& a, int grid, cudaStream_t s) {
+cudaError_t launch_row_step(const RowStepArgs& args, int grid, cudaStream_t s) {
+    RowStepArgs a = args;
+    a.stage_q_bytes = (int)stage_q_bytes(a.gm, grid);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = row_step_smem_bytes(a.hidden, a.ffn);
+    cfg.dynamicSmemBytes = smem_bytes(a.hidden, a.ffn, (size_t)a.stage_q_bytes);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
