@@ -208,7 +208,7 @@ def run_ours(a):
     n_kv_last = ctx + W + K
     att_bytes = B * n_kv_last * KV_BYTES_PER_TOKEN_LAYER
     att_launch_ms = attn_ms / max(n_att, 1)
-    achieved = att_bytes / (att_launch_ms / 1e3) / 1e9
+    achieved = att_bytes / (att_launch_ms / 1e3) / 1e9 if att_launch_ms > 0 else None
     peak, peak_kind = measured_peaks()
     traffic = None
     tf = os.path.join(ROOT, "profiles", "attention_traffic.json")
@@ -225,8 +225,11 @@ def run_ours(a):
         # row's K/V pages, each read once
         wq = sum(n * k for n, k in ((4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072)))
         bytes_per_launch = cfg["n_layers"] * (wq * 34 // 32 + B * n_kv_last * KV_BYTES_PER_TOKEN_LAYER)
-        ms_per_launch = row_ms
         kernel = "row_step_kernel (one-row step: 28 layers, persistent)"
+        if launches == 1:   # the lm_head runs in the kernel too
+            bytes_per_launch += cfg["vocab"] * cfg["hidden"] * 34 // 32
+            kernel = "row_step_kernel (one-row step: 28 layers + lm_head + argmax, persistent)"
+        ms_per_launch = row_ms
         achieved = bytes_per_launch / (row_ms / 1e3) / 1e9
         traffic = None
         tf = os.path.join(ROOT, "profiles", "row_step_traffic.json")
@@ -271,7 +274,7 @@ def run_ours(a):
                        "l2": "no flush: inputs larger than L2 (KV read per step ~30 GB)",
                        "parallelism": f"independent replicas x{world}, no collectives"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
+                         "frac": achieved / peak if achieved else None, "traffic": traffic,
                          "kernel": kernel, "peak_kind": peak_kind,
                          "bytes_per_launch": bytes_per_launch, "ms_per_launch": ms_per_launch},
             "cpu_baseline": cpu,

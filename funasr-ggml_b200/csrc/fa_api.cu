@@ -1078,9 +1078,10 @@ static int enqueue_lm_head(fa_ctx* ctx, const StepPlan& p, int Mo) {
     return 2;
 }
 
-// One row: the persistent step kernel (embedding, every layer, the final norm) as a
-// cooperative launch, then the lm_head and the argmax reduce. Profiling brackets the
-// persistent kernel with events 0 and 1.
+// One row: the persistent step kernel (embedding, every layer, the final norm and, for
+// hidden 1024, the lm_head and the argmax) as a cooperative launch; otherwise the lm_head
+// and the argmax reduce follow as launches of their own. Profiling brackets the persistent
+// kernel with events 0 and 1.
 static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     const fa_model_desc& d = ctx->d;
     fa::RowStepArgs a{};
@@ -1098,6 +1099,12 @@ static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
     a.final_norm = ctx->final_norm; a.xn16 = ctx->xn16; a.xn_lo = ctx->xn_lo;
     a.ctl = ctx->row_ctl; a.err = ctx->err_dev;
     a.wait_ns = ctx->row_wait_ns; a.absent_cta = ctx->row_absent_cta;
+    const int Mo = p.n_out < 0 ? 1 : p.n_out;
+    const bool lm_here = fa::row_step_lm_fits(d.hidden, d.vocab);
+    a.lm = lm_here && Mo > 0;
+    a.lm_q = ctx->lm_q; a.lm_tiles = d.vocab / 64; a.logits = p.logits ? ctx->logits_dev : nullptr;
+    a.amax_val = ctx->amax_v; a.amax_idx = ctx->amax_i; a.next = ctx->next_dev;
+    a.feed_tok = p.n_out < 0 ? ctx->row_tok : nullptr; a.feed_pos = p.n_out < 0 ? ctx->row_pos : nullptr;
     const bool pdl = fa::launch_pdl_enabled();
     fa::set_launch_pdl(false);
     if (p.prof) record_prof(ctx, 0, capturing);
@@ -1109,8 +1116,7 @@ static int enqueue_row_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         ctx->enqueue_msg = std::string("one-row step kernel launch: ") + cudaGetErrorString(e);
         return 1;
     }
-    const int Mo = p.n_out < 0 ? 1 : p.n_out;
-    return 1 + (Mo > 0 ? enqueue_lm_head(ctx, p, Mo) : 0);
+    return 1 + (Mo > 0 && !lm_here ? enqueue_lm_head(ctx, p, Mo) : 0);
 }
 
 // enqueue_step with programmatic dependent launch between its kernels when enabled

@@ -223,6 +223,7 @@ struct RowCtl {
     unsigned int seq;            // launches completed: tags of launch k are (k + 1) * layers + layer
     int abort;                   // a wait ran out: every CTA leaves
     int att_cnt[8];              // attention splits finished per KV head (reset by the last one)
+    int lm_cnt;                  // CTAs done with their lm_head tiles (reset by the last one)
 };
 struct RowStepArgs {
     const RowLayer* layers;
@@ -254,6 +255,16 @@ struct RowStepArgs {
     const float* final_norm;
     __half* xn16;                // final norm output, the lm_head's input pair
     __half* xn_lo;
+    // lm (row_step_lm_fits): the lm_head and the argmax run in the kernel too
+    int lm;
+    const unsigned char* lm_q;   // lm_head Q8_0 planes [vocab][hidden]
+    int lm_tiles;                // vocab / 64
+    float* logits;               // [vocab] or nullptr
+    float* amax_val;             // [lm_tiles] per-tile maxima and their rows
+    int* amax_idx;
+    int* next;                   // [1] the argmax
+    int* feed_tok;               // or nullptr: the token fed back for the next step
+    int* feed_pos;               //             and its position + 1
     RowCtl* ctl;
     int* err;
     unsigned long long wait_ns;  // limit of one wait for a word
@@ -261,6 +272,7 @@ struct RowStepArgs {
     int stage_q_bytes;           // set by launch_row_step
 };
 size_t row_step_words(int hidden, int ffn);
+bool row_step_lm_fits(int hidden, int vocab);
 // Fills gm[] for a model's shapes; false when the kernel does not take them.
 bool row_step_shapes(int hidden, int ffn, int grid, RowGemm* gm);
 cudaError_t configure_row_step();

@@ -59,6 +59,8 @@ constexpr int D = 128;
 constexpr int kHq = 16, kHkv = 8;
 constexpr int kQkvN = (kHq + 2 * kHkv) * D;
 constexpr int kPollWords = 16;           // words one thread polls at a time
+constexpr int kLmRows = 32;              // lm_head rows per staged chunk: one 4-row block per warp
+constexpr int kLmSlots = 3;              // chunks in flight (in the attention ring's shared memory)
 constexpr int kAttnNW = 8;               // the attention item's warps: the whole CTA
 using ASmem = attn::Smem<kRowStages, kAttnNW>;
 
@@ -68,6 +70,10 @@ struct RowSmem {
     double sh[kWarps];
     __half newkv[2 * D];       // the token's K row then V row (f16), for the page patch
     uint64_t wbar;             // completion of the staged weights' bulk copies
+    uint64_t lmbar[kLmSlots];  // completion of the lm_head chunks
+    float tilev[2][64];        // the logits of a 64-row vocab tile (two tiles alternate)
+    float rv[kWarps];          // the argmax's per-warp results
+    int ri[kWarps];
     int last;
     // act [max(hidden, Hq * 128, ffn)] (permuted, act_index), x [hidden], part [hidden], norm weights [2][hidden],
     // then the staged weights: q rows [rows][K] int8, then their scales [rows][K / 32] f16
@@ -366,6 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
         for (int w = 0; w < kAttnNW; ++w)
             for (int s = 0; s < kRowStages; ++s) mbar_init(&S.att.bars[w][s], 1);
         mbar_init(&S.wbar, 1);
+        for (int k = 0; k < kLmSlots; ++k) mbar_init(&S.lmbar[k], 1);
         fence_mbar_init();
     }
     prefetch_norm(nrm_in, a.layers[0].in_norm, Hd);
@@ -437,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
             if (gi == 1) prefetch_norm(nrm_post, Lp->post_norm, Hd);
             if (gi == 3) {
                 if (l + 1 < a.n_layers) prefetch_norm(nrm_in, Lp[1].in_norm, Hd);
-                else if (cta == 0) prefetch_norm(nrm_in, a.final_norm, Hd);
+                else if (cta == 0 || a.lm) prefetch_norm(nrm_in, a.final_norm, Hd);
             }
             const bool pairs = gi == 1 || gi == 3;   // attention output, SwiGLU output: f16 pairs
             if (gi != 0 || l > 0) {
@@ -574,18 +581,183 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
         return;
     }
 
-    // ---------------- final norm: the lm_head's input pair (CTA 0)
-    if (cta != 0) return;
-    if (!poll_words(a, a.w_dn, Hd, tag0 + (uint32_t)a.n_layers - 1u,
-                    [&](int i, uint32_t v) { part[i] = __uint_as_float(v); }))
+    // ---------------- F: the final norm, then (a.lm) the lm_head and the argmax
+    const uint32_t tag_last = tag0 + (uint32_t)a.n_layers - 1u;
+    if (!a.lm) {
+        // the lm_head runs as its own launch: CTA 0 leaves the final norm's pair for it
+        if (cta != 0) return;
+        if (!poll_words(a, a.w_dn, Hd, tag_last, [&](int i, uint32_t v) { part[i] = __uint_as_float(v); })) return;
+        residual_norm_row<8, false>(xr, reinterpret_cast<const float4*>(part), 0, 1, Hd, nrm_in, a.eps, xr, S.sh,
+                                    [&](int j, float y) { split_store(y, a.xn16, a.xn_lo, (size_t)j); });
+        __syncthreads();
+        for (int i = threadIdx.x; i < Hd; i += kThreads) a.x_a[i] = xr[i];
+        // every CTA read the sequence number at its start, long before this point (its rows
+        // of every phase came before)
+        if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(&a.ctl->seq) = seq + 1u;
         return;
+    }
+    // Every CTA normalises the row itself, then computes the logits of its 64-row vocab
+    // tiles with the CUDA-core lm_head kernel's arithmetic (a warp per 4 rows over all of
+    // K, its 512-column slices in order), streamed through kLmSlots chunks of kLmRows
+    // rows in the attention ring's shared memory; each tile's first maximum goes to
+    // amax_val / amax_idx, and the CTA that finishes last reduces them as the argmax
+    // reduce kernel does.
+    if (!poll_words(a, a.w_dn, Hd, tag_last, [&](int i, uint32_t v) { part[i] = __uint_as_float(v); })) return;
     residual_norm_row<8, false>(xr, reinterpret_cast<const float4*>(part), 0, 1, Hd, nrm_in, a.eps, xr, S.sh,
-                                [&](int j, float y) { split_store(y, a.xn16, a.xn_lo, (size_t)j); });
+                                [&](int j, float y) {
+                                    act[act_index(j)] = pair_value(y);
+                                    if (cta == 0) split_store(y, a.xn16, a.xn_lo, (size_t)j);
+                                });
     __syncthreads();
-    for (int i = threadIdx.x; i < Hd; i += kThreads) a.x_a[i] = xr[i];
-    // every CTA read the sequence number at its start, long before this point (its rows
-    // of every phase came before)
-    if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(&a.ctl->seq) = seq + 1u;
+    if (cta == 0)
+        for (int i = threadIdx.x; i < Hd; i += kThreads) a.x_a[i] = xr[i];
+    {
+        const int K = Hd;
+        const int tile0 = (int)((long long)cta * a.lm_tiles / G);
+        const int tile1 = (int)((long long)(cta + 1) * a.lm_tiles / G);
+        const int n_chunks = 2 * (tile1 - tile0);
+        const uint32_t slot_bytes = (uint32_t)(kLmRows * (K + K / 16));
+        unsigned char* ring = reinterpret_cast<unsigned char*>(&S.att.tiles[0][0][0]);
+        const size_t dr_off = q8p_dr_offset(a.vocab, K);
+        auto issue = [&](int k) {
+            unsigned char* slot = ring + (size_t)(k % kLmSlots) * slot_bytes;
+            const size_t row0 = (size_t)64 * tile0 + (size_t)kLmRows * k;
+            uint64_t* bar = &S.lmbar[k % kLmSlots];
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(bar, slot_bytes);
+            bulk_copy_g2s(slot, a.lm_q + row0 * K, (uint32_t)(kLmRows * K), bar);
+            bulk_copy_g2s(slot + kLmRows * K, a.lm_q + dr_off + row0 * (K / 16), (uint32_t)(kLmRows * K / 16), bar);
+        };
+        if (issuer)
+            for (int k = 0; k < kLmSlots && k < n_chunks; ++k) issue(k);
+        bool lok = true;
+        int k = 0;
+        for (; k < n_chunks; ++k) {
+            const bool got = mbar_wait_bounded(&S.lmbar[k % kLmSlots], (uint32_t)(k / kLmSlots) & 1u);
+            if (__syncthreads_or(!got)) {
+                if (threadIdx.x == 0) record_error(a.err, kDevErrTimeout);
+                lok = false;
+                break;
+            }
+            const unsigned char* slot = ring + (size_t)(k % kLmSlots) * slot_bytes;
+            const __half* dsl = reinterpret_cast<const __half*>(slot + kLmRows * K);
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+            for (int sl = 0; sl < K / kSlice; ++sl) {
+                const int k0 = sl * kSlice + lane * kWpl;
+                float x[kWpl];
+#pragma unroll
+                for (int hh = 0; hh < kWpl / 4; ++hh) {
+                    const float4 t4 = *reinterpret_cast<const float4*>(act + sl * kSlice + hh * 128 + lane * 4);
+                    x[4 * hh] = t4.x; x[4 * hh + 1] = t4.y; x[4 * hh + 2] = t4.z; x[4 * hh + 3] = t4.w;
+                }
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int rr = 4 * warp + r;
+                    const uint4 q = lds128(slot + (size_t)rr * K + k0);
+                    const float dsc = __half2float(dsl[(size_t)rr * (K / kQK) + k0 / kQK]);
+                    const uint32_t wb[4] = {q.x, q.y, q.z, q.w};
+                    float wf[kWpl];
+#pragma unroll
+                    for (int j4 = 0; j4 < kWpl / 4; ++j4) {
+                        const uint32_t v = wb[j4] ^ 0x80808080u;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b)
+                            wf[4 * j4 + b] =
+                                __int_as_float((int)__byte_perm(v, 0x4B000000u, 0x7540u + (unsigned)b)) - 8388736.0f;
+                    }
+                    float sq_ = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < kWpl; ++j) sq_ = fmaf(wf[j], x[j], sq_);
+                    acc[r] = fmaf(dsc, sq_, acc[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+            const int tp = (k >> 1) & 1;
+            if (lane == 0)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    float v = 0.0f;
+                    v += acc[r];
+                    const int rt = (k & 1) * kLmRows + 4 * warp + r;   // row within the tile
+                    S.tilev[tp][rt] = v;
+                    if (a.logits) a.logits[(size_t)64 * tile0 + (size_t)kLmRows * k + 4 * warp + r] = v;
+                }
+            __syncthreads();   // the chunk's slot is free; the tile's values are complete
+            if (issuer && k + kLmSlots < n_chunks) issue(k + kLmSlots);
+            if ((k & 1) && warp == 0) {
+                // the tile's first maximum (NaN never wins), ties to the lower index
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+                const int row_base = 64 * (tile0 + (k >> 1));
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int rr = lane + 32 * hh;
+                    const float v = S.tilev[tp][rr];
+                    if (v > bv) { bv = v; bi = row_base + rr; }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                }
+                if (lane == 0) {
+                    a.amax_val[tile0 + (k >> 1)] = bv;
+                    a.amax_idx[tile0 + (k >> 1)] = bi;
+                }
+            }
+        }
+        if (!lok) {
+            // wait (bounded) for the chunks still in flight before leaving
+            const int issued_to = min(n_chunks, k + kLmSlots);
+            for (int kk = k + 1; kk < issued_to; ++kk)
+                (void)mbar_wait_bounded(&S.lmbar[kk % kLmSlots], (uint32_t)(kk / kLmSlots) & 1u);
+            return;
+        }
+    }
+    // the tile maxima are out: the CTA that finishes last reduces them
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const int old = atomicAdd(&a.ctl->lm_cnt, 1);
+        S.last = old == G - 1;
+        if (S.last) {
+            __threadfence();
+            a.ctl->lm_cnt = 0;
+        }
+    }
+    __syncthreads();
+    if (S.last) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int t = threadIdx.x; t < a.lm_tiles; t += kThreads) {
+            const float v = __ldcg(a.amax_val + t);
+            const int i = __ldcg(a.amax_idx + t);
+            if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) { S.rv[warp] = bv; S.ri[warp] = bi; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int w = 1; w < kWarps; ++w)
+                if (S.rv[w] > bv || (S.rv[w] == bv && S.ri[w] < bi)) { bv = S.rv[w]; bi = S.ri[w]; }
+            // all-NaN or empty rows fall back to index 0, as the reference's scan does
+            if (bi == 0x7fffffff) bi = 0;
+            a.next[0] = bi;
+            if (a.feed_tok) a.feed_tok[0] = bi;
+            if (a.feed_pos) a.feed_pos[0] += 1;
+        }
+    }
+    if (cta == 0 && threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(&a.ctl->seq) = seq + 1u;
 }
 
 }  // namespace
@@ -626,6 +798,13 @@ bool row_step_shapes(int hidden, int ffn, int grid, RowGemm* gm) {
         if (per_cta * ks * (g.swiglu ? 2 : 1) > kMaxUnits) return false;
     }
     return smem_bytes(hidden, ffn, stage_q_bytes(gm, grid)) <= 227 * 1024;
+}
+
+bool row_step_lm_fits(int hidden, int vocab) {
+    // the CUDA-core lm_head's argmax form at one row: one warp per 4 rows over all of K, in
+    // one or two slices of 512 columns
+    return (hidden == 512 || hidden == 1024) && vocab % 64 == 0 &&
+           (size_t)kLmSlots * kLmRows * (hidden + hidden / 16) <= sizeof(((ASmem*)nullptr)->tiles);
 }
 
 size_t row_step_words(int hidden, int ffn) {
