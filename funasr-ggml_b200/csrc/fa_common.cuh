@@ -8,8 +8,9 @@
 //                    copy moves it.
 //   block table    : int32 [seq_slot][page_index]; token p of slot s sits in page
 //                    block_table[s][p / 16] at in-page token p % 16.
-//   Q8_0 weights   : expanded at load time from GGUF blocks ([f16 d][32 x int8]) into
-//                    W [N][K] f16 = f16(d * q), row-major (K contiguous), TMA-able.
+//   Q8_0 weights   : the GGUF blocks ([f16 d][32 x int8]) split into planes, nothing rounded
+//                    (q8_planes.cuh): q int8 [N][K], scales f16 [K/32][N] and [N][K/32].
+//                    The encoder's weights are f16(d * q) [N][K], row-major, TMA-able.
 //   RoPE table     : float2 [pos][head_dim/2] = (cos, sin), computed on the host in double.
 #pragma once
 

@@ -15,8 +15,9 @@
 // Exact dequantisation for the tensor cores: d*q has at most 11 + 7 significant bits, so
 // it is the sum of two f16 values, hi = f16(d*q) and lo = d*q - hi, both exact (lo is a
 // multiple of d's last place and at most 2^6 of them, representable down to the f16
-// subnormals). The kernels expand a tile of q into an f16 (hi, lo) pair in shared memory
-// and multiply it with the activation pair; no weight is rounded.
+// subnormals). The tensor-core kernels expand a tile of q into an f16 (hi, lo) pair (in TMEM
+// as the MMA's A operand, or in shared memory) and multiply it with the activation pair; the
+// CUDA-core kernels sum q * x in fp32 and multiply by d once. No weight is rounded.
 #pragma once
 
 #include "fa_common.cuh"
