@@ -802,6 +802,7 @@ struct StepPlan {
     int s_qkv = 1, s_o = 1, s_gu = 1, s_dn = 1;
     int pps = 32;        // attention pages per split (decode kernel)
     int n_splits = 1;
+    int att_warps = 4;   // warps per attention CTA
     int n_dec = 0;       // rows for the decode kernel (all M rows when there are no tiles)
     int n_tiles = 0;     // prefill tiles for the tensor-core kernel
     int n_out = -1;      // rows through lm_head: -1 all (with token feedback), else the listed rows
@@ -813,7 +814,7 @@ struct StepPlan {
     bool fuse_qkv = false;     // QKV GEMM on the tcgen05 kernel finishes kernel (1) in its clusters
     bool row_step = false;     // one row: the persistent step kernel, then lm_head and argmax
     std::array<int, 12> key() const {
-        return {M, s_qkv, s_o, s_gu, s_dn, pps, n_splits, n_dec, n_tiles, n_out,
+        return {M, s_qkv, s_o, s_gu, s_dn, pps * 16 + att_warps, n_splits, n_dec, n_tiles, n_out,
                 (int)row_step * 32 + (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 + (int)fuse_swiglu * 4 +
                     (int)embeds * 2 + (int)logits,
                 (int)prof};
@@ -826,38 +827,48 @@ constexpr int kPrefillMinRun = 16;
 
 }  // namespace
 
-// Attention work split for rows of row_pages[i] pages each: the pages per CTA (a
-// multiple of 4) that minimise the estimated time
+// Attention work split for rows of row_pages[i] pages each: the CTA form (warps per CTA)
+// and pages per CTA (a multiple of 4) that minimise the estimated time
 //   waves * (4 * ceil(pps / warps) + 2) + (8 if any row is split)
-// where warps = fa::attn_warps(rows) per CTA, waves = ceil(CTAs / (CTAs per SM * n_sm)), a
+// where waves = ceil(CTAs / (CTAs per SM * n_sm)) (3 CTAs of 4 warps or one of 8 per SM), a
 // CTA costs its rounds of pages (one per warp each) plus about 2 pages' worth of set-up, and
 // merging split partials costs a launch of its own, about 8 pages' worth (a unit is
 // ~0.5 us: 128 rows x 2048 tokens run 7 waves of 46 in 173 us; the merge launch takes
-// 4-6 us); at most max_splits splits per row.
+// 4-6 us); at most max_splits splits per row. warps_in = 0 lets the model choose (8 for one
+// row, either form up to kAttnPlanWideRows rows, 4 above); 4 or 8 fixes it.
 static void attention_split(const std::vector<int>& row_pages, int n_sm, int max_splits, int* pps_out,
-                            int* n_splits_out) {
+                            int* n_splits_out, int* warps_out = nullptr, int warps_in = 0) {
     int max_pages = 1;
     for (int pg : row_pages) max_pages = std::max(max_pages, pg);
-    const int warps = fa::attn_warps((int)row_pages.size());
-    const long long slots = (long long)(warps == 4 ? fa::kAttnCtasPerSm : 1) * n_sm;
+    const int rows = (int)row_pages.size();
+    int forms[2] = {4, 8}, n_forms = 2;
+    if (warps_in) { forms[0] = warps_in; n_forms = 1; }
+    else if (rows == 1) { forms[0] = 8; n_forms = 1; }
+    else if (rows > fa::kAttnPlanWideRows) { forms[0] = 4; n_forms = 1; }
     long long best_cost = -1;
-    int best = 0;
-    for (int pps = 4; pps <= 256; pps += 4) {
-        const int n_splits = (max_pages + pps - 1) / pps;
-        if (n_splits > max_splits) continue;
-        long long ctas = 0;
-        for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + pps - 1) / pps);
-        const long long waves = (ctas + slots - 1) / slots;
-        const long long cost = waves * (4 * ((pps + warps - 1) / warps) + 2) + (n_splits > 1 ? 8 : 0);
-        if (best_cost < 0 || cost < best_cost) {
-            best_cost = cost;
-            best = pps;
+    int best = 0, best_w = forms[0];
+    for (int fi = 0; fi < n_forms; ++fi) {
+        const int warps = forms[fi];
+        const long long slots = (long long)(warps == 4 ? fa::kAttnCtasPerSm : 1) * n_sm;
+        for (int pps = 4; pps <= 256; pps += 4) {
+            const int n_splits = (max_pages + pps - 1) / pps;
+            if (n_splits > max_splits) continue;
+            long long ctas = 0;
+            for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + pps - 1) / pps);
+            const long long waves = (ctas + slots - 1) / slots;
+            const long long cost = waves * (4 * ((pps + warps - 1) / warps) + 2) + (n_splits > 1 ? 8 : 0);
+            if (best_cost < 0 || cost < best_cost) {
+                best_cost = cost;
+                best = pps;
+                best_w = warps;
+            }
+            if (n_splits == 1) break;   // larger pps change nothing
         }
-        if (n_splits == 1) break;   // larger pps change nothing
     }
     if (!best) best = (max_pages + max_splits - 1) / max_splits;   // unreachable with pps up to 256
     *pps_out = best;
     *n_splits_out = (max_pages + best - 1) / best;
+    if (warps_out) *warps_out = best_w;
 }
 
 // Whether a GEMM of M rows goes to the CUDA-core kernel under a GEMM variant.
@@ -904,14 +915,14 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
         std::vector<int> row_pages(row_len.size());
         for (size_t i = 0; i < row_len.size(); ++i)
             row_pages[i] = (row_len[i] + fa::kPageTokens - 1) / fa::kPageTokens;
-        attention_split(row_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits);
+        attention_split(row_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits, &p.att_warps);
     }
     p.embeds = embeds;
     p.logits = logits;
     p.prof = ctx->prof;
     // one decode row, CUDA-core GEMM arithmetic, every attention item on its own SM
     p.row_step = ctx->row_ready && ctx->row_step_on && M == 1 && n_tiles == 0 && p.n_dec == 1 &&
-                 gemv_rows(ctx->gemm_variant, 1) && p.n_splits * kHkv <= ctx->n_sm;
+                 gemv_rows(ctx->gemm_variant, 1) && p.att_warps == 8 && p.n_splits * kHkv <= ctx->n_sm;
     return p;
 }
 
@@ -1002,7 +1013,8 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
             at.q = ctx->q_rot; at.pool_layer = pool_l; at.block_table = ctx->bt_dev; at.bt_stride = ctx->bt_stride;
             at.n_pages = ctx->n_pages; at.slot = ctx->row_slot; at.pos = ctx->row_pos; at.M = p.n_dec;
             at.rows = p.n_tiles > 0 ? ctx->dec_rows : nullptr; at.Hq = kHq;
-            at.Hkv = kHkv; at.pages_per_split = p.pps; at.n_splits = p.n_splits; at.part_o = ctx->att_po;
+            at.Hkv = kHkv; at.pages_per_split = p.pps; at.n_splits = p.n_splits; at.warps = p.att_warps;
+            at.part_o = ctx->att_po;
             at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out16_lo = ctx->attn_lo; at.out32 = nullptr;
             at.err = ctx->err_dev;
             fa::launch_paged_attention(at, s);
@@ -1713,7 +1725,7 @@ extern "C" int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages
         if (n_kv[i] <= 0) return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_op_attention_plan: n_kv must be > 0");
         row_pages[i] = (n_kv[i] + fa::kPageTokens - 1) / fa::kPageTokens;
     }
-    attention_split(row_pages, n_sm, 64, pages_per_split, n_splits);
+    attention_split(row_pages, n_sm, 64, pages_per_split, n_splits, nullptr, fa::attn_warps(M));
     return FA_OK;
 }
 

@@ -78,6 +78,7 @@ struct AttnArgs {
     int M, Hq, Hkv;
     int pages_per_split;     // pages one CTA reads
     int n_splits;            // grid.x; splits beyond a row's length exit at once
+    int warps;               // 4 or 8 warps per CTA; 0: attn_warps(M)
     float* part_o;           // [M][Hq][n_splits][128] un-normalised partial outputs
     float* part_ml;          // [M][Hq][n_splits][2]   (running max in log2 units, sum)
     __half* out16;           // [M][Hq*128] final output as f16 hi part, or nullptr
@@ -91,9 +92,12 @@ void launch_paged_attention(const AttnArgs& a, cudaStream_t s);
 // memory: 4 warps x kAttnStages x 8 KiB per CTA).
 constexpr int kAttnStages = 2;
 constexpr int kAttnCtasPerSm = 3;
-// Steps of at most this many rows run 8 warps per CTA (one CTA per SM), so that a split's
-// pages spread over twice the warps; attn_warps gives the count for M rows.
+// Steps of at most this many rows run 8 warps per CTA (one CTA per SM) unless AttnArgs::warps
+// says otherwise, so that a split's pages spread over twice the warps; attn_warps gives that
+// default for M rows (the decoder's planner picks 4 or 8 by its cost model up to
+// kAttnPlanWideRows rows, 8 for one row).
 constexpr int kAttnWideRows = 2;
+constexpr int kAttnPlanWideRows = 64;
 int attn_warps(int M);
 // Split combine; only needed when n_splits > 1.
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s);

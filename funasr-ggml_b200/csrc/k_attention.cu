@@ -113,7 +113,8 @@ cudaError_t configure_attention() {
 
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s) {
     dim3 grid(a.n_splits, a.Hkv, a.M);
-    if (attn_warps(a.M) == 8) launch_k(paged_attn_kernel<8>, grid, dim3(256), sizeof(AttnSmem<8>), s, a);
+    const int warps = a.warps ? a.warps : attn_warps(a.M);
+    if (warps == 8) launch_k(paged_attn_kernel<8>, grid, dim3(256), sizeof(AttnSmem<8>), s, a);
     else launch_k(paged_attn_kernel<4>, grid, dim3(128), sizeof(AttnSmem<4>), s, a);
 }
 
