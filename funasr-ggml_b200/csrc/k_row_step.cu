@@ -4,14 +4,18 @@
 //
 // With one row every launch of the launch-per-op step is latency-bound: a layer's eight
 // launches move 17 MB of Q8_0 weights (2.6 us at HBM rate) in ~34 us. Here one CTA per SM
-// (a cooperative launch, so all CTAs are resident) runs every layer in five phases:
+// (a cooperative launch, so all CTAs are resident) runs every layer in five phases, and
+// then the final one:
 //
 //   A  residual add + RMSNorm (every CTA, redundantly) -> QKV GEMV rows
-//   B  per (split, KV head) item: q/k RMSNorm + RoPE, K/V append, paged attention
-//      (+ split merge by the item that finishes last)
+//   B  per (split, KV head) item: q/k RMSNorm + RoPE, K/V append, paged attention on all 8
+//      warps (+ split merge by the item that finishes last)
 //   C  o_proj GEMV rows
 //   D  residual add + RMSNorm -> gate|up GEMV rows + SwiGLU
 //   E  down GEMV rows
+//   F  final norm (every CTA), lm_head rows of 64-row vocab tiles and their maxima, the
+//      argmax by the CTA that finishes last (hidden 512 or 1024; otherwise the lm_head
+//      runs as its own launch after the kernel)
 //
 // Every value one phase hands to the next travels as a 64-bit word {32-bit value, 32-bit
 // tag}, written with one relaxed store; the tag is this launch's sequence number times
@@ -75,8 +79,9 @@ struct RowSmem {
     float rv[kWarps];          // the argmax's per-warp results
     int ri[kWarps];
     int last;
-    // act [max(hidden, Hq * 128, ffn)] (permuted, act_index), x [hidden], part [hidden], norm weights [2][hidden],
-    // then the staged weights: q rows [rows][K] int8, then their scales [rows][K / 32] f16
+    // act [max(hidden, Hq * 128, ffn)] (permuted, act_index), x [hidden], part [hidden],
+    // norm weights [2][hidden], then the staged weights: q rows [rows][K] int8, then their
+    // scales [rows][K / 32] f16
     alignas(128) float buf[4];
 };
 
@@ -358,7 +363,12 @@ __global__ void __launch_bounds__(kThreads, 1) row_step_kernel(const RowStepArgs
     const int n_kv = pos + 1;
     const int n_row_pages = (n_kv + kPageTokens - 1) / kPageTokens;
     const bool len_bad = attn::row_len_bad(at, n_kv, n_row_pages);
-    if (len_bad && cta == 0 && threadIdx.x == 0) record_error(a.err, kDevErrBadLen);
+    if (len_bad) {
+        // the row's attention would be skipped, so its words would never come: flag the row
+        // and leave before anything is written (the same for every CTA)
+        if (cta == 0 && threadIdx.x == 0) record_error(a.err, kDevErrBadLen);
+        return;
+    }
     const int p_begin = split * a.pps;
     const int p_end = min(n_row_pages, p_begin + a.pps);
     const bool item = cta < a.n_splits * kHkv && !len_bad && p_begin < n_row_pages;
