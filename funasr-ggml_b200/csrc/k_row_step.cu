@@ -37,8 +37,8 @@
 //
 // Same arithmetic as the launch-per-op step with the CUDA-core GEMMs (k_gemv.cu): a GEMV
 // unit is a block of 4 weight rows x 512 columns, lane l holding 16 int8 of each row, the
-// same fp32 FMA chain per lane, the same xor-shuffle reduction, and the ks units of a row
-// block summed in unit order from 0; the norms call residual_norm_row, attention runs the
+// same fp32 FMA chain per lane, a warp reduction that pairs lanes as its xor-shuffle
+// reduction does, and the ks units of a row block summed in unit order from 0; the norms call residual_norm_row, attention runs the
 // body of kernel (2) (k_attn_body.cuh) and kernel (1) is qkv_head_apply. The outputs are
 // the same bits, which the tests check.
 #include "fa_kernels.cuh"
@@ -169,57 +169,78 @@ __device__ __forceinline__ int act_index(int j) {
     return (j & ~511) | (((j >> 2) & 3) << 7) | (((j >> 4) & 31) << 2) | (j & 3);
 }
 
-// Every unit of the warp: 4 dot products of 512 columns of the staged rows with act, the
-// CUDA-core kernel's arithmetic; lane 0 leaves the 4 sums in red[u]. The unit's four rows
-// are consecutive staged rows.
+// Lane sums of unit u: for each of its 4 rows, this lane's 16 columns of the CUDA-core
+// kernel's arithmetic (the fp32 FMA chain, then one multiply-add by the block's scale).
+__device__ __forceinline__ void unit_lane_sums(const RowGemm& g, const Span& s, const unsigned char* sq,
+                                               const __half* sd, const float* act, int u, int lane, float (&acc)[4]) {
+    const int K = g.K;
+    const int blk = u / g.ks;                 // row block (SwiGLU: gate or up block of a pair)
+    const int c = u - blk * g.ks;             // K slice
+    const int rr0 = g.swiglu ? (blk & 1) * 4 * s.nb + 4 * (blk >> 1) : 4 * blk;
+    const int k0 = c * kSlice + lane * kWpl;
+    uint4 q[4];
+    float dsc[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        q[r] = lds128(sq + (size_t)(rr0 + r) * K + k0);
+        dsc[r] = __half2float(sd[(size_t)(rr0 + r) * (K / kQK) + k0 / kQK]);
+    }
+    float x[kWpl];
+#pragma unroll
+    for (int h = 0; h < kWpl / 4; ++h) {
+        const float4 t = *reinterpret_cast<const float4*>(act + c * kSlice + h * 128 + lane * 4);
+        x[4 * h] = t.x; x[4 * h + 1] = t.y; x[4 * h + 2] = t.z; x[4 * h + 3] = t.w;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        // int8 -> f32 exactly: the byte q + 128 under the exponent of 2^23 reads as 2^23 + q + 128
+        const uint32_t wb[4] = {q[r].x, q[r].y, q[r].z, q[r].w};
+        float wf[kWpl];
+#pragma unroll
+        for (int j4 = 0; j4 < kWpl / 4; ++j4) {
+            const uint32_t v = wb[j4] ^ 0x80808080u;
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                wf[4 * j4 + b] = __int_as_float((int)__byte_perm(v, 0x4B000000u, 0x7540u + (unsigned)b)) - 8388736.0f;
+        }
+        float sq_ = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kWpl; ++j) sq_ = fmaf(wf[j], x[j], sq_);
+        acc[r] = 0.0f;
+        acc[r] = fmaf(dsc[r], sq_, acc[r]);
+    }
+}
+
+// Every unit of the warp: 4 dot products of 512 columns of the staged rows with act; the
+// 4 sums of unit u land in red[u]. The unit's four rows are consecutive staged rows. The
+// 4 lane sums are reduced over the warp by halving exchanges (16 and 8 lanes apart, each
+// lane keeping half of the values it holds, then 4, 2, 1 apart): every partial sum pairs
+// the same lanes in the same order as an xor-shuffle reduction of each value over 16, 8,
+// 4, 2, 1 (the CUDA-core kernel's), so the totals are the same bits, with 6 shuffles
+// instead of 20. Lane 8r ends with row r.
 __device__ __forceinline__ void dot_units(const RowGemm& g, const Span& s, const unsigned char* sq, const __half* sd,
                                           const float* act, float (*red)[4], int warp, int lane) {
-    const int K = g.K, ks = g.ks;
 #pragma unroll 1
     for (int u = warp; u < s.n_units; u += kWarps) {
-        const int blk = u / ks;                 // row block (SwiGLU: gate or up block of a pair)
-        const int c = u - blk * ks;             // K slice
-        const int rr0 = g.swiglu ? (blk & 1) * 4 * s.nb + 4 * (blk >> 1) : 4 * blk;
-        const int k0 = c * kSlice + lane * kWpl;
-        uint4 q[4];
-        float dsc[4];
+        float v[4];
+        unit_lane_sums(g, s, sq, sd, act, u, lane, v);
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            q[r] = lds128(sq + (size_t)(rr0 + r) * K + k0);
-            dsc[r] = __half2float(sd[(size_t)(rr0 + r) * (K / kQK) + k0 / kQK]);
+        for (int k = 0; k < 2; ++k) {
+            const bool b = lane & 16;
+            const float keep = b ? v[k + 2] : v[k];
+            const float send = b ? v[k] : v[k + 2];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
         }
-        float x[kWpl];
-#pragma unroll
-        for (int h = 0; h < kWpl / 4; ++h) {
-            const float4 t = *reinterpret_cast<const float4*>(act + c * kSlice + h * 128 + lane * 4);
-            x[4 * h] = t.x; x[4 * h + 1] = t.y; x[4 * h + 2] = t.z; x[4 * h + 3] = t.w;
+        {
+            const bool b = lane & 8;
+            const float keep = b ? v[1] : v[0];
+            const float send = b ? v[0] : v[1];
+            v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
         }
-        float acc[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            // int8 -> f32 exactly: the byte q + 128 under the exponent of 2^23 reads as 2^23 + q + 128
-            const uint32_t wb[4] = {q[r].x, q[r].y, q[r].z, q[r].w};
-            float wf[kWpl];
-#pragma unroll
-            for (int j4 = 0; j4 < kWpl / 4; ++j4) {
-                const uint32_t v = wb[j4] ^ 0x80808080u;
-#pragma unroll
-                for (int b = 0; b < 4; ++b)
-                    wf[4 * j4 + b] = __int_as_float((int)__byte_perm(v, 0x4B000000u, 0x7540u + (unsigned)b)) - 8388736.0f;
-            }
-            float sq_ = 0.0f;
-#pragma unroll
-            for (int j = 0; j < kWpl; ++j) sq_ = fmaf(wf[j], x[j], sq_);
-            acc[r] = 0.0f;
-            acc[r] = fmaf(dsc[r], sq_, acc[r]);
-        }
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-        if (lane == 0)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) red[u][r] = acc[r];
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 4);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+        v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+        if ((lane & 7) == 0) red[u][lane >> 3] = v[0];
     }
 }
 
