@@ -141,6 +141,7 @@ struct fa_ctx {
     __half* h_lo = nullptr;
     float* att_po = nullptr;
     float* att_pml = nullptr;
+    int* att_cnt = nullptr;        // [rows][Hkv] split counters of the in-kernel split merge
     int att_max_splits = 0;
     float* amax_v = nullptr;
     int* amax_i = nullptr;
@@ -165,7 +166,7 @@ struct fa_ctx {
     // bit 0: QKV + kernel (1), bit 1: gate/up + SwiGLU, finished in the tcgen05 GEMM's
     // clusters. Default 2: the QKV form measured slower (its per-row norm / RoPE / append
     // tail runs on 4 warps per SM, where the separate kernel spreads it over every SM)
-    int fuse_epilogues = 2;
+    int fuse_epilogues = 6;
     bool enqueue_failed = false; // a planned launch declined its arguments while a step was enqueued
     bool use_pdl = true;       // programmatic dependent launch between the step's kernels
     // one-row steps as one persistent kernel (k_row_step.cu) when the shapes allow it
@@ -375,6 +376,7 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
         dev_alloc(ctx, &ctx->h16, sizeof(__half) * 2 * R * d.ffn) ||
         dev_alloc(ctx, &ctx->att_po, sizeof(float) * (size_t)R * kHq * ctx->att_max_splits * kD) ||
         dev_alloc(ctx, &ctx->att_pml, sizeof(float) * (size_t)R * kHq * ctx->att_max_splits * 2) ||
+        dev_alloc(ctx, &ctx->att_cnt, sizeof(int) * (size_t)R * kHkv) ||
         dev_alloc(ctx, &ctx->amax_v, sizeof(float) * (size_t)R * (d.vocab / 64)) ||
         dev_alloc(ctx, &ctx->amax_i, sizeof(int) * (size_t)R * (d.vocab / 64)) ||
         dev_alloc(ctx, &ctx->row_tok, sizeof(int) * R) || dev_alloc(ctx, &ctx->row_slot, sizeof(int) * R) ||
@@ -390,7 +392,8 @@ extern "C" fa_ctx* fa_create(int device, const fa_model_desc* desc) {
     ctx->xn_lo = ctx->xn16 + (size_t)R * std::max(d.hidden, d.ffn);
     ctx->attn_lo = ctx->attn16 + (size_t)R * kHq * kD;
     ctx->h_lo = ctx->h16 + (size_t)R * d.ffn;
-    if (cudaMemset(ctx->err_dev, 0, sizeof(int)) != cudaSuccess) {
+    if (cudaMemset(ctx->err_dev, 0, sizeof(int)) != cudaSuccess ||
+        cudaMemset(ctx->att_cnt, 0, sizeof(int) * (size_t)R * kHkv) != cudaSuccess) {
         set_err(ctx, FA_ERR_CUDA, "memset err");
         return fail();
     }
@@ -450,7 +453,7 @@ extern "C" int fa_set_gemm_variant(fa_ctx* ctx, int variant) {
 
 extern "C" int fa_set_fused_epilogues(fa_ctx* ctx, int enable) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
-    if (enable < 0 || enable > 3) return set_err(ctx, FA_ERR_INVALID_ARG, "fused epilogue mask must be 0 to 3");
+    if (enable < 0 || enable > 7) return set_err(ctx, FA_ERR_INVALID_ARG, "fused epilogue mask must be 0 to 7");
     ctx->fuse_epilogues = enable;
     clear_graphs(ctx);
     return FA_OK;
@@ -813,10 +816,11 @@ struct StepPlan {
     bool fuse_gu_tc = false;   // gate/up GEMM on the tcgen05 kernel finishes SwiGLU in its clusters
     bool fuse_qkv = false;     // QKV GEMM on the tcgen05 kernel finishes kernel (1) in its clusters
     bool row_step = false;     // one row: the persistent step kernel, then lm_head and argmax
+    bool att_merge = false;    // the attention kernel merges its splits itself (no combine launch)
     std::array<int, 12> key() const {
         return {M, s_qkv, s_o, s_gu, s_dn, pps * 16 + att_warps, n_splits, n_dec, n_tiles, n_out,
-                (int)row_step * 32 + (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 + (int)fuse_swiglu * 4 +
-                    (int)embeds * 2 + (int)logits,
+                (int)att_merge * 64 + (int)row_step * 32 + (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 +
+                    (int)fuse_swiglu * 4 + (int)embeds * 2 + (int)logits,
                 (int)prof};
     }
 };
@@ -916,6 +920,14 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
         for (size_t i = 0; i < row_len.size(); ++i)
             row_pages[i] = (row_len[i] + fa::kPageTokens - 1) / fa::kPageTokens;
         attention_split(row_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits, &p.att_warps);
+        // the split merge inside the attention kernel when its CTAs fit in one wave: then the
+        // merge launch is the cost it saves; over several waves each CTA's count and the last
+        // split's merge hold back the next wave (measured: 4 rows x 2048 tokens 1.49 -> 1.45
+        // ms per step, 16 x 1024 1.64 -> 1.61; 64 and 128 rows x 2048 2-4 % slower)
+        long long ctas = 0;
+        for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + p.pps - 1) / p.pps);
+        const long long slots = (long long)(p.att_warps == 4 ? fa::kAttnCtasPerSm : 1) * ctx->n_sm;
+        p.att_merge = p.n_splits > 1 && (ctx->fuse_epilogues & 4) && ctas <= slots;
     }
     p.embeds = embeds;
     p.logits = logits;
@@ -1017,9 +1029,10 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
             at.part_o = ctx->att_po;
             at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out16_lo = ctx->attn_lo; at.out32 = nullptr;
             at.err = ctx->err_dev;
+            at.merge_cnt = p.att_merge ? ctx->att_cnt : nullptr;
             fa::launch_paged_attention(at, s);
             ++n;
-            if (p.n_splits > 1) {
+            if (p.n_splits > 1 && !p.att_merge) {
                 fa::launch_attn_combine(at, s);
                 ++n;
             }
@@ -1195,6 +1208,8 @@ static int check_device_error(fa_ctx* ctx) {
             cudaMemsetAsync(ctx->row_ctl, 0, sizeof(fa::RowCtl), ctx->stream);
             cudaMemsetAsync(ctx->row_words, 0, sizeof(unsigned long long) * ctx->row_words_n, ctx->stream);
         }
+        // and the split counters of a step whose attention stopped part-way
+        cudaMemsetAsync(ctx->att_cnt, 0, sizeof(int) * (size_t)ctx->d.max_rows * kHkv, ctx->stream);
         cudaStreamSynchronize(ctx->stream);
         if (e & fa::kDevErrTimeout) return set_err(ctx, FA_ERR_TIMEOUT, "a bounded device wait gave up");
         return set_err(ctx, FA_ERR_DEVICE, "kernel reported error bits " + std::to_string(e) +

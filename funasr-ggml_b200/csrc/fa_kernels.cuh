@@ -85,6 +85,9 @@ struct AttnArgs {
     __half* out16_lo;        // [M][Hq*128] f16 remainder (out - hi), or nullptr
     float* out32;            // [M][Hq*128] final output (f32) or nullptr
     int* err;
+    int* merge_cnt;          // [rows][Hkv] splits done per (row, KV head), zero between launches:
+                             // the split that finishes last merges the head's splits itself;
+                             // nullptr: the merge is launch_attn_combine's
 };
 size_t attn_smem_bytes();
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s);

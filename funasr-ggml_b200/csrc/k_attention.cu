@@ -10,7 +10,8 @@
 // Work split: one CTA per (split of `pages_per_split` pages, KV head, row); the CTA's
 // four warps run the body in k_attn_body.cuh (page ring, scores, online softmax, PV,
 // merge of the warps). With several splits the un-normalised partials go to the scratch
-// buffer and attn_combine merges them.
+// buffer and are merged either by the split of each (row, KV head) that finishes last
+// (AttnArgs::merge_cnt given: the decoder's steps) or by attn_combine (the op entry points).
 //
 // Roofline: HBM. Algorithmic bytes per (row, layer) = n_kv * 8 heads * 2 * 128 * 2 B
 // = n_kv * 4096 B; compute is 4 flop per byte read.
@@ -81,6 +82,28 @@ __global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_a
         attn::merge_warps(S, threadIdx.x, [&](int hq, float M, float L, float O) {
             attn::merge_store(a, split, h, m, threadIdx.x, hq, M, L, O);
         });
+    if (!a.merge_cnt || a.n_splits == 1) return;
+    // The split merge here: the CTA that counts its (row, KV head) last merges the splits
+    // of both query heads (the partials it reads are at L2; the count is reset for the next
+    // launch). No CTA waits for another.
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int n_valid = min(a.n_splits, (n_row_pages + a.pages_per_split - 1) / a.pages_per_split);
+        int* cnt = a.merge_cnt + (size_t)m * a.Hkv + h;
+        __threadfence();
+        last = atomicAdd(cnt, 1) == n_valid - 1;
+        if (last) {
+            __threadfence();
+            *cnt = 0;
+        }
+    }
+    __syncthreads();
+    if (last && warp < 2) {
+        const int H = 2 * h + warp;
+        const size_t o = (size_t)m * a.Hq * D + (size_t)H * D;
+        attn::combine_head<true>(a, m, H, lane, [&](int d, float v) { attn::store_out(a, o + d, v); });
+    }
 }
 
 // Merge of the split partials: a warp per (row, query head).

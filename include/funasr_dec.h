@@ -121,12 +121,14 @@ FA_API int fa_set_stream(fa_ctx* ctx, void* cuda_stream);
  * 3 = the small-M kernel up to 8 rows, else as 2; 4 = the swapped tcgen05 kernel at every
  * M. */
 FA_API int fa_set_gemm_variant(fa_ctx* ctx, int variant);
-/* Which projections of steps of up to 128 rows on the swapped tcgen05 kernel finish their
- * next op inside the GEMM, in clusters of its split-K CTAs (a mask): bit 0 = the QKV
- * projection with kernel (1) (per-head norm, RoPE, K/V append), bit 1 = the gate/up
- * projection with SwiGLU. Default 2 (SwiGLU only); 0 = separate kernels. The results are
- * the same bits either way. No counterpart in the reference (ggml runs each node
- * separately, compute/llm_ops_gpu.cpp:53-96,177-180). */
+/* Which ops of a step finish inside the kernel before them (a mask): bit 0 = the QKV
+ * projection of steps of up to 128 rows on the swapped tcgen05 kernel finishes kernel (1)
+ * (per-head norm, RoPE, K/V append) in clusters of its split-K CTAs; bit 1 = the gate/up
+ * projection finishes SwiGLU the same way; bit 2 = decode attention with several splits
+ * per row merges them in the attention kernel (the split that finishes last for a row and
+ * KV head merges both query heads) instead of a merge launch. Default 6; 0 = separate
+ * kernels. The results are the same bits either way. No counterpart in the reference
+ * (ggml runs each node separately, compute/llm_ops_gpu.cpp:53-96,135-143,177-180). */
 FA_API int fa_set_fused_epilogues(fa_ctx* ctx, int mask);
 /* 1 = programmatic dependent launch between a step's kernels (default): each kernel's
  * prologue overlaps the previous kernel's tail. 0 = plain stream order. */

@@ -184,6 +184,40 @@ def test_fused_gemm_epilogues_give_the_same_bits(torch_cuda, small_w, n_seq):
             assert np.array_equal(a, b), mask
 
 
+@pytest.mark.parametrize("n_seq,lo,hi,fused", [(4, 300, 2001, True), (16, 1024, 1025, True), (128, 300, 2001, False)])
+def test_attention_split_merge_in_kernel_gives_the_same_bits(torch_cuda, small_w, n_seq, lo, hi, fused):
+    """Decode steps over contexts whose attention runs several splits per row: with fused
+    mask bit 2 the split that finishes last merges its (row, KV head) inside the attention
+    kernel when the attention CTAs fit in one wave (4 rows of 300-2000 tokens: 4 splits on
+    one CTA per SM; 16 rows of 1024: 3 splits on three CTAs per SM), one launch fewer per
+    layer; over several waves (128 rows) the merge stays a launch of its own. Logits and
+    tokens over six steps equal the separate merge's bits either way, so the split counters
+    are back at zero after every step."""
+    w = small_w
+    rng = np.random.default_rng(77 + n_seq)
+    lens = rng.integers(lo, hi, n_seq)
+    first = rng.integers(0, CFG["vocab"], n_seq)
+    out = {}
+    for mask in (6, 2):
+        dec = _decoder(w, CFG, n_pages=n_seq * 130 + 16, max_seqs=n_seq, max_rows=n_seq)
+        dec.set_fused_epilogues(mask)
+        sids = [dec.seq_open(MAX_CTX) for _ in range(n_seq)]
+        for s, n in zip(sids, lens):
+            dec.kv_fill_synthetic(s, int(n), seed=int(n))
+        toks, lgs, ids = first, [], []
+        for _ in range(6):
+            toks, lg = dec.decode_step(sids, toks, want_logits=True)
+            lgs.append(lg)
+            ids.append(toks)
+        out[mask] = (lgs, ids, dec.step_launches())
+        dec.close()
+    assert out[2][2] - out[6][2] == (CFG["n_layers"] if fused else 0), (out[2][2], out[6][2])
+    for a, b in zip(out[6][0], out[2][0]):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    for a, b in zip(out[6][1], out[2][1]):
+        assert np.array_equal(a, b)
+
+
 def test_pool_exhaustion_rolls_back(torch_cuda, small_w):
     dec = _decoder(small_w, CFG, n_pages=4)
     a = dec.seq_open(MAX_CTX)
