@@ -218,12 +218,16 @@ def run_ours(a):
         # bytes scale with the (row, token) pairs read per launch
         traffic = t["dram_bytes_per_launch"] * (B * n_kv_last) / (t["rows"] * t["n_kv"])
 
-    kernel, bytes_per_launch, ms_per_launch = "paged_attn_kernel (+attn_combine)", att_bytes, att_launch_ms
+    kernel, bytes_per_launch, ms_per_launch = "paged_attn_kernel (+ split merge)", att_bytes, att_launch_ms
+    # what one step reads: every layer's Q8_0 weights (q and scale planes, 34 B per 32
+    # weights), the lm_head, and the rows' K/V
+    wq = sum(n * k for n, k in ((4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072)))
+    step_bytes = (cfg["n_layers"] * (wq * 34 // 32 + B * (ctx + W) * KV_BYTES_PER_TOKEN_LAYER)
+                  + cfg["vocab"] * cfg["hidden"] * 34 // 32)
     if row_ms > 0:
         # one row: the persistent step kernel is the step; its algorithmic bytes are every
         # layer's Q8_0 weights (q and row-major scale planes, 34 B per 32 weights) and the
         # row's K/V pages, each read once
-        wq = sum(n * k for n, k in ((4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072)))
         bytes_per_launch = cfg["n_layers"] * (wq * 34 // 32 + B * n_kv_last * KV_BYTES_PER_TOKEN_LAYER)
         kernel = "row_step_kernel (one-row step: 28 layers, persistent)"
         if launches == 1:   # the lm_head runs in the kernel too
@@ -271,7 +275,8 @@ def run_ours(a):
             "config": {"workload": f"steady-state paged GQA decode, {B} sequences per GPU at {ctx}-token context "
                                    f"(grows to {ctx + W + K}), Qwen3-0.6B 28 layers 16q/8kv x 128, Q8_0 weights, f16 KV",
                        "batch_per_gpu": B, "ctx": ctx, "page_tokens": 16,
-                       "l2": "no flush: inputs larger than L2 (KV read per step ~30 GB)",
+                       "l2": f"no flush: each step reads {step_bytes / 1e9:.2f} GB (weights, lm_head, K/V), "
+                             f"above the 126 MB L2",
                        "parallelism": f"independent replicas x{world}, no collectives"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak if achieved else None, "traffic": traffic,
