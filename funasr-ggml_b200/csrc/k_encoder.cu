@@ -390,7 +390,18 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
         const float* vr = vs + slot * KCH * KLD + j;
 #pragma unroll
         for (int r = 0; r < ATT_ROWS; ++r) acc[r] *= al[r];
-        for (int kk = 0; kk < nk; ++kk) {
+        // four keys at a time: each row's four probabilities in one 16 B load (the same
+        // address in every thread), the FMAs still in key order
+        int kk = 0;
+        for (; kk + 4 <= nk; kk += 4) {
+            const float v0 = vr[kk * KLD], v1 = vr[(kk + 1) * KLD], v2 = vr[(kk + 2) * KLD], v3 = vr[(kk + 3) * KLD];
+#pragma unroll
+            for (int r = 0; r < ATT_ROWS; ++r) {
+                const float4 p4 = *reinterpret_cast<const float4*>(ps + r * KCH + kk);
+                acc[r] = fmaf(p4.w, v3, fmaf(p4.z, v2, fmaf(p4.y, v1, fmaf(p4.x, v0, acc[r]))));
+            }
+        }
+        for (; kk < nk; ++kk) {
             const float v = vr[kk * KLD];
 #pragma unroll
             for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(ps[r * KCH + kk], v, acc[r]);
