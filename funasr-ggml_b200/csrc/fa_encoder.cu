@@ -270,16 +270,31 @@ int gemm(fa_encoder* e, const __half* a, const __half* a_lo, int T, const Lin& L
     return g.n_split;
 }
 
-void enc_layer(fa_encoder* e, const EncLayer& L, int T, int n_tiles, bool residual, const float* x_in, int ld_in) {
+// The LayerNorm that follows a layer's last residual add, applied by the same launch: the
+// next layer's norm1 (into xn, x kept), or after_norm / tp_norm in place of x. The launch
+// normalises the f32 row it has just written, the values a separate launch would read
+// back, so the results are the same bits with one launch fewer per layer.
+struct LnTail {
+    const float* w = nullptr;
+    const float* b = nullptr;
+    float eps = 0.0f;
+    int in_place = 0;
+    bool to_xn = false;      // the f16 pair into xn / xn_lo
+};
+
+void enc_layer(fa_encoder* e, const EncLayer& L, int T, int n_tiles, bool residual, const float* x_in, int ld_in,
+               bool ln1_done, const LnTail& tail) {
     const fa_encoder_desc& d = e->d;
     const int D = d.output_size;
     cudaStream_t s = e->stream;
-    // norm1 of the layer input (encoder0: the scaled features, 560 of 576 columns)
+    // norm1 of the layer input (encoder0: the scaled features, 560 of 576 columns), unless
+    // the previous layer's last launch left it in xn
     const bool padded = L.qkv.kp != L.d_in;
     __half* in_hi = padded ? e->xn0 : e->xn;
     __half* in_lo = padded ? e->xn0_lo : e->xn_lo;
-    fa::launch_enc_resid_ln(const_cast<float*>(x_in), L.d_in, ld_in, nullptr, -1, T, nullptr, nullptr, 0, L.n1w,
-                            L.n1b, 1e-5f, 0, in_hi, in_lo, L.qkv.kp, s);
+    if (!ln1_done)
+        fa::launch_enc_resid_ln(const_cast<float*>(x_in), L.d_in, ld_in, nullptr, -1, T, nullptr, nullptr, 0, L.n1w,
+                                L.n1b, 1e-5f, 0, in_hi, in_lo, L.qkv.kp, s);
     int sp = gemm(e, in_hi, in_lo, T, L.qkv);
     fa::launch_enc_bias_act(e->part, sp, T, L.qkv.n, L.qkv.b, 0, e->qkv, nullptr, nullptr, e->n_sm, s);
     fa::launch_enc_fsmn(e->qkv, T, e->seg_dev, D, L.fsmn, d.kernel_size, (d.kernel_size - 1) / 2 - d.sanm_shift,
@@ -292,16 +307,17 @@ void enc_layer(fa_encoder* e, const EncLayer& L, int T, int n_tiles, bool residu
     sp = gemm(e, e->xn, e->xn_lo, T, L.w1);
     fa::launch_enc_bias_act(e->part, sp, T, L.w1.n, L.w1.b, 1, nullptr, e->hid, e->hid_lo, e->n_sm, s);
     sp = gemm(e, e->hid, e->hid_lo, T, L.w2);
-    fa::launch_enc_resid_ln(e->x, D, D, e->part, sp, T, L.w2.b, nullptr, 1, nullptr, nullptr, 0.0f, 0, nullptr,
-                            nullptr, 0, s);
+    fa::launch_enc_resid_ln(e->x, D, D, e->part, sp, T, L.w2.b, nullptr, 1, tail.w, tail.b, tail.eps, tail.in_place,
+                            tail.to_xn ? e->xn : nullptr, tail.to_xn ? e->xn_lo : nullptr, tail.to_xn ? D : 0, s);
 }
 
-void ada_block(fa_encoder* e, const AdaBlock& B, int T, int n_tiles) {
+void ada_block(fa_encoder* e, const AdaBlock& B, int T, int n_tiles, bool ln1_done, const LnTail& tail) {
     const fa_encoder_desc& d = e->d;
     const int D = d.adaptor_output;
     cudaStream_t s = e->stream;
-    fa::launch_enc_resid_ln(e->x, D, D, nullptr, -1, T, nullptr, nullptr, 0, B.n1w, B.n1b, 1e-12f, 0, e->xn, e->xn_lo,
-                            D, s);
+    if (!ln1_done)
+        fa::launch_enc_resid_ln(e->x, D, D, nullptr, -1, T, nullptr, nullptr, 0, B.n1w, B.n1b, 1e-12f, 0, e->xn,
+                                e->xn_lo, D, s);
     int sp = gemm(e, e->xn, e->xn_lo, T, B.qkv);
     fa::launch_enc_bias_act(e->part, sp, T, B.qkv.n, B.qkv.b, 0, e->qkv, nullptr, nullptr, e->n_sm, s);
     fa::launch_enc_attention(e->qkv, e->tiles_dev, n_tiles, D, d.adaptor_heads, e->att, e->att_lo, d.max_frames, s);
@@ -311,8 +327,8 @@ void ada_block(fa_encoder* e, const AdaBlock& B, int T, int n_tiles) {
     sp = gemm(e, e->xn, e->xn_lo, T, B.w1);
     fa::launch_enc_bias_act(e->part, sp, T, B.w1.n, B.w1.b, 1, nullptr, e->hid, e->hid_lo, e->n_sm, s);
     sp = gemm(e, e->hid, e->hid_lo, T, B.w2);
-    fa::launch_enc_resid_ln(e->x, D, D, e->part, sp, T, B.w2.b, nullptr, 1, nullptr, nullptr, 0.0f, 0, nullptr,
-                            nullptr, 0, s);
+    fa::launch_enc_resid_ln(e->x, D, D, e->part, sp, T, B.w2.b, nullptr, 1, tail.w, tail.b, tail.eps, tail.in_place,
+                            tail.to_xn ? e->xn : nullptr, tail.to_xn ? e->xn_lo : nullptr, tail.to_xn ? D : 0, s);
 }
 
 }  // namespace
@@ -478,20 +494,36 @@ static void enqueue(fa_encoder* e, int T, int n_tiles, cudaStream_t s) {
     e->stream = s;
     fa::set_launch_pdl(true);
     fa::launch_enc_scale(e->in_raw, T, d.input_dim, kin, std::sqrt((float)d.output_size), e->in0, s);
-    enc_layer(e, e->e0, T, n_tiles, false, e->in0, kin);
-    for (const auto& L : e->main_l) enc_layer(e, L, T, n_tiles, true, e->x, d.output_size);
-    fa::launch_enc_resid_ln(e->x, d.output_size, d.output_size, nullptr, -1, T, nullptr, nullptr, 0, e->after_w,
-                            e->after_b, 1e-5f, 1, nullptr, nullptr, 0, s);
-    for (const auto& L : e->tp_l) enc_layer(e, L, T, n_tiles, true, e->x, d.output_size);
-    // tp_norm in place; its f16 pair is the adaptor's input
-    fa::launch_enc_resid_ln(e->x, d.output_size, d.output_size, nullptr, -1, T, nullptr, nullptr, 0, e->tp_w, e->tp_b,
-                            1e-5f, 1, e->xn, e->xn_lo, d.output_size, s);
+    // each layer's last launch also applies the norm that comes next: the following layer's
+    // norm1, after_norm (in place) after the main layers, tp_norm (in place, and the
+    // adaptor's f16 input) after the tp layers
+    auto norm1_of = [](const EncLayer& L) { return LnTail{L.n1w, L.n1b, 1e-5f, 0, true}; };
+    const LnTail after{e->after_w, e->after_b, 1e-5f, 1, false};
+    const LnTail tp{e->tp_w, e->tp_b, 1e-5f, 1, true};
+    const size_t n_main = e->main_l.size(), n_tp = e->tp_l.size();
+    enc_layer(e, e->e0, T, n_tiles, false, e->in0, kin, false, n_main ? norm1_of(e->main_l[0]) : after);
+    for (size_t i = 0; i < n_main; ++i)
+        enc_layer(e, e->main_l[i], T, n_tiles, true, e->x, d.output_size, true,
+                  i + 1 < n_main ? norm1_of(e->main_l[i + 1]) : after);
+    if (n_tp == 0)   // tp_norm on its own
+        fa::launch_enc_resid_ln(e->x, d.output_size, d.output_size, nullptr, -1, T, nullptr, nullptr, 0, e->tp_w,
+                                e->tp_b, 1e-5f, 1, e->xn, e->xn_lo, d.output_size, s);
+    for (size_t i = 0; i < n_tp; ++i)   // the first one normalises after_norm's output itself
+        enc_layer(e, e->tp_l[i], T, n_tiles, true, e->x, d.output_size, i > 0,
+                  i + 1 < n_tp ? norm1_of(e->tp_l[i + 1]) : tp);
     int sp = gemm(e, e->xn, e->xn_lo, T, e->lin1);
     fa::launch_enc_bias_act(e->part, sp, T, e->lin1.n, e->lin1.b, 1, nullptr, e->hid, e->hid_lo, e->n_sm, s);
     sp = gemm(e, e->hid, e->hid_lo, T, e->lin2);
-    fa::launch_enc_resid_ln(e->x, d.adaptor_output, d.adaptor_output, e->part, sp, T, e->lin2.b, nullptr, 0, nullptr,
-                            nullptr, 0.0f, 0, nullptr, nullptr, 0, s);
-    for (const auto& B : e->blocks) ada_block(e, B, T, n_tiles);
+    // x = lin2 output, then the first block's norm1 in the same launch
+    const size_t n_blk = e->blocks.size();
+    auto ada_norm1 = [](const AdaBlock& B) { return LnTail{B.n1w, B.n1b, 1e-12f, 0, true}; };
+    const LnTail none{};
+    const LnTail t0 = n_blk ? ada_norm1(e->blocks[0]) : none;
+    fa::launch_enc_resid_ln(e->x, d.adaptor_output, d.adaptor_output, e->part, sp, T, e->lin2.b, nullptr, 0, t0.w,
+                            t0.b, t0.eps, 0, t0.to_xn ? e->xn : nullptr, t0.to_xn ? e->xn_lo : nullptr,
+                            t0.to_xn ? d.adaptor_output : 0, s);
+    for (size_t i = 0; i < n_blk; ++i)
+        ada_block(e, e->blocks[i], T, n_tiles, true, i + 1 < n_blk ? ada_norm1(e->blocks[i + 1]) : none);
     fa::set_launch_pdl(false);
     e->stream = saved;
 }
