@@ -297,8 +297,9 @@ class Decoder:
         self._c(lib().fa_set_gemm_variant(self.ctx, int(variant)))
 
     def set_fused_epilogues(self, mask: int):
-        """Mask of projections finished inside the tcgen05 GEMM: 1 = QKV with per-head
-        norm/RoPE/append, 2 = gate/up with SwiGLU (default 2); 0 = separate kernels. Same
+        """Mask of ops finished inside the kernel before them: 1 = QKV GEMM with per-head
+        norm/RoPE/append, 2 = gate/up GEMM with SwiGLU, 4 = decode attention merging its
+        splits itself when its CTAs fit in one wave (default 6); 0 = separate kernels. Same
         bits either way."""
         self._c(lib().fa_set_fused_epilogues(self.ctx, int(mask)))
 
