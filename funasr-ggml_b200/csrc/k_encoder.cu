@@ -273,15 +273,21 @@ __global__ void __launch_bounds__(256) enc_fsmn_kernel(const float* qkv, const i
 }
 
 // Bidirectional multi-head attention within each utterance, head_dim 128. CTA = (tile,
-// head), 128 threads; a tile (first row, rows <= 16, utterance start, utterance length)
-// lies in one utterance. One pass over the utterance's keys in chunks of 32 with an
-// online softmax: the keys and values of the next NST chunks are in flight (cp.async into
-// a ring) while a chunk is used. Warp w scores rows w, w+4, w+8, w+12 against the chunk
-// (lane = key), updates each row's running max and sum and leaves the chunk's
-// probabilities in shared memory; thread j then rescales its output dim j of the 16
-// rows and adds the chunk's values. fp32 throughout; exp of scores minus the running max.
+// head), 8 warps; a tile (first row, rows <= 16, utterance start, utterance length) lies
+// in one utterance. One pass over the utterance's keys in chunks of 32 with an online
+// softmax: the keys and values of the next NST chunks are in flight (cp.async into a ring)
+// while a chunk is used. Warp w scores rows w and w+8 against the chunk (lane = key),
+// updates each row's running max and sum and leaves the chunk's probabilities in shared
+// memory; thread t then rescales output dim t % 128 of rows 8 (t / 128) .. +7 and adds the
+// chunk's values. fp32 throughout; exp of scores minus the running max. (Shared memory
+// allows two CTAs per SM: 8 warps instead of 4 keep twice the loads in flight, with every
+// product, sum and rescale computed in the same order as with 4.)
 constexpr int ATT_ROWS = 16;
+constexpr int ATT_WARPS = 8;
+constexpr int ATT_THREADS = 32 * ATT_WARPS;
 constexpr int HD = 128;
+constexpr int QK_ROWS = ATT_ROWS / ATT_WARPS;            // rows a warp scores
+constexpr int PV_ROWS = ATT_ROWS * HD / ATT_THREADS;     // rows a thread accumulates
 constexpr int KCH = 32;                  // keys per chunk
 constexpr int KLD = HD + 4;              // padded row of a staged key / value (floats)
 constexpr int NST = 3;                   // chunks in flight
@@ -298,7 +304,7 @@ __device__ __forceinline__ void cp_async_wait_older() {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, const int4* tiles, int d,
+__global__ void __launch_bounds__(ATT_THREADS) enc_attention_kernel(const float* qkv, const int4* tiles, int d,
                                                             __half* out_hi, __half* out_lo, int max_T) {
     extern __shared__ __align__(16) float sm[];
     float* qs = sm;                                  // [16][128] scaled queries
@@ -326,7 +332,7 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
     auto issue = [&](int c) {
         if (c < n_chunks) {
             const int slot = c % NST, c0 = c * KCH;
-            for (int e = threadIdx.x; e < KCH * (HD / 4); e += 128) {
+            for (int e = threadIdx.x; e < KCH * (HD / 4); e += ATT_THREADS) {
                 const int kk = e / (HD / 4), j4 = e % (HD / 4);
                 const bool ok = c0 + kk < T;
                 const float* src = qkv + (size_t)(k0 + (ok ? c0 + kk : 0)) * ld + h * HD + 4 * j4;
@@ -337,40 +343,43 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
         cp_async_commit();
     };
     for (int c = 0; c < NST; ++c) issue(c);
-    for (int e = threadIdx.x; e < ATT_ROWS * HD; e += 128) {
+    for (int e = threadIdx.x; e < ATT_ROWS * HD; e += ATT_THREADS) {
         const int r = e / HD, j = e % HD;
         qs[e] = r < nr ? qkv[(size_t)(r0 + r) * ld + h * HD + j] * scale : 0.0f;
     }
 
-    float m_run[4], l_run[4];                        // rows warp + 4i; every lane holds the same values
+    float m_run[QK_ROWS], l_run[QK_ROWS];            // rows warp + 8i; every lane holds the same values
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < QK_ROWS; ++i) {
         m_run[i] = -INFINITY;
         l_run[i] = 0.0f;
     }
-    const int j = threadIdx.x;                       // output dim of this thread
-    float acc[ATT_ROWS];
+    const int j = threadIdx.x & (HD - 1);            // output dim of this thread
+    const int rb = (threadIdx.x / HD) * PV_ROWS;     // its first output row
+    float acc[PV_ROWS];
 #pragma unroll
-    for (int r = 0; r < ATT_ROWS; ++r) acc[r] = 0.0f;
+    for (int r = 0; r < PV_ROWS; ++r) acc[r] = 0.0f;
 
     for (int c = 0; c < n_chunks; ++c) {
         cp_async_wait_older();                       // this thread's copies of chunk c have landed
         __syncthreads();                             // ... and every thread's; the queries too
         const int slot = c % NST, nk = min(KCH, T - c * KCH);
-        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        float sc[QK_ROWS];
+#pragma unroll
+        for (int i = 0; i < QK_ROWS; ++i) sc[i] = 0.0f;
         const float* kr = ks + (slot * KCH + lane) * KLD;
 #pragma unroll 4
         for (int jj = 0; jj < HD; jj += 4) {
             const float4 k4 = *reinterpret_cast<const float4*>(kr + jj);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float4 q4 = *reinterpret_cast<const float4*>(qs + (warp + 4 * i) * HD + jj);
+            for (int i = 0; i < QK_ROWS; ++i) {
+                const float4 q4 = *reinterpret_cast<const float4*>(qs + (warp + ATT_WARPS * i) * HD + jj);
                 sc[i] = fmaf(q4.x, k4.x, fmaf(q4.y, k4.y, fmaf(q4.z, k4.z, fmaf(q4.w, k4.w, sc[i]))));
             }
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = warp + 4 * i;
+        for (int i = 0; i < QK_ROWS; ++i) {
+            const int r = warp + ATT_WARPS * i;
             const float sv = lane < nk ? sc[i] : -INFINITY;
             float cm = sv;
 #pragma unroll
@@ -389,22 +398,22 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
         __syncthreads();
         const float* vr = vs + slot * KCH * KLD + j;
 #pragma unroll
-        for (int r = 0; r < ATT_ROWS; ++r) acc[r] *= al[r];
+        for (int r = 0; r < PV_ROWS; ++r) acc[r] *= al[rb + r];
         // four keys at a time: each row's four probabilities in one 16 B load (the same
-        // address in every thread), the FMAs still in key order
+        // address in every thread of the warp), the FMAs still in key order
         int kk = 0;
         for (; kk + 4 <= nk; kk += 4) {
             const float v0 = vr[kk * KLD], v1 = vr[(kk + 1) * KLD], v2 = vr[(kk + 2) * KLD], v3 = vr[(kk + 3) * KLD];
 #pragma unroll
-            for (int r = 0; r < ATT_ROWS; ++r) {
-                const float4 p4 = *reinterpret_cast<const float4*>(ps + r * KCH + kk);
+            for (int r = 0; r < PV_ROWS; ++r) {
+                const float4 p4 = *reinterpret_cast<const float4*>(ps + (rb + r) * KCH + kk);
                 acc[r] = fmaf(p4.w, v3, fmaf(p4.z, v2, fmaf(p4.y, v1, fmaf(p4.x, v0, acc[r]))));
             }
         }
         for (; kk < nk; ++kk) {
             const float v = vr[kk * KLD];
 #pragma unroll
-            for (int r = 0; r < ATT_ROWS; ++r) acc[r] = fmaf(ps[r * KCH + kk], v, acc[r]);
+            for (int r = 0; r < PV_ROWS; ++r) acc[r] = fmaf(ps[(rb + r) * KCH + kk], v, acc[r]);
         }
         __syncthreads();                             // every thread is done with slot c % NST
         issue(c + NST);
@@ -412,9 +421,12 @@ __global__ void __launch_bounds__(128) enc_attention_kernel(const float* qkv, co
     cp_async_wait_all();                             // only empty groups remain; none outlives the CTA
     if (lane == 0)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) ls[warp + 4 * i] = l_run[i];
+        for (int i = 0; i < QK_ROWS; ++i) ls[warp + ATT_WARPS * i] = l_run[i];
     __syncthreads();
-    for (int r = 0; r < nr; ++r) split_store_h(acc[r] / ls[r], out_hi, out_lo, (size_t)(r0 + r) * d + h * HD + j);
+#pragma unroll
+    for (int r = 0; r < PV_ROWS; ++r)
+        if (rb + r < nr)
+            split_store_h(acc[r] / ls[rb + r], out_hi, out_lo, (size_t)(r0 + rb + r) * d + h * HD + j);
 }
 
 }  // namespace
@@ -481,7 +493,7 @@ void configure_encoder(int) {
 
 void launch_enc_attention(const float* qkv, const int4* tiles, int n_tiles, int d, int n_heads, __half* out_hi,
                           __half* out_lo, int max_T, cudaStream_t s) {
-    launch_k(enc_attention_kernel, dim3(n_tiles, n_heads), dim3(128), enc_attention_smem(max_T), s, qkv, tiles, d,
+    launch_k(enc_attention_kernel, dim3(n_tiles, n_heads), dim3(ATT_THREADS), enc_attention_smem(max_T), s, qkv, tiles, d,
              out_hi, out_lo, max_T);
 }
 
