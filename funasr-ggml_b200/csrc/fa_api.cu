@@ -164,9 +164,10 @@ struct fa_ctx {
 
     bool use_graphs = true;
     // bit 0: QKV + kernel (1), bit 1: gate/up + SwiGLU, finished in the tcgen05 GEMM's
-    // clusters. Default 2: the QKV form measured slower (its per-row norm / RoPE / append
-    // tail runs on 4 warps per SM, where the separate kernel spreads it over every SM)
-    int fuse_epilogues = 6;
+    // clusters; bit 2: split merge inside the attention kernel; bit 3: kernel (1) inside the
+    // attention kernel. Bit 0 is off: the QKV form measured slower (its per-row norm / RoPE /
+    // append tail runs on 4 warps per SM, where the other forms spread it over every SM)
+    int fuse_epilogues = 14;
     bool enqueue_failed = false; // a planned launch declined its arguments while a step was enqueued
     bool use_pdl = true;       // programmatic dependent launch between the step's kernels
     // one-row steps as one persistent kernel (k_row_step.cu) when the shapes allow it
@@ -453,7 +454,7 @@ extern "C" int fa_set_gemm_variant(fa_ctx* ctx, int variant) {
 
 extern "C" int fa_set_fused_epilogues(fa_ctx* ctx, int enable) {
     if (!ctx) return set_err(nullptr, FA_ERR_INVALID_ARG, "ctx is NULL");
-    if (enable < 0 || enable > 7) return set_err(ctx, FA_ERR_INVALID_ARG, "fused epilogue mask must be 0 to 7");
+    if (enable < 0 || enable > 15) return set_err(ctx, FA_ERR_INVALID_ARG, "fused epilogue mask must be 0 to 15");
     ctx->fuse_epilogues = enable;
     clear_graphs(ctx);
     return FA_OK;
@@ -817,9 +818,10 @@ struct StepPlan {
     bool fuse_qkv = false;     // QKV GEMM on the tcgen05 kernel finishes kernel (1) in its clusters
     bool row_step = false;     // one row: the persistent step kernel, then lm_head and argmax
     bool att_merge = false;    // the attention kernel merges its splits itself (no combine launch)
+    bool att_append = false;   // ... and runs kernel (1) for its KV heads (no kernel (1) launch)
     std::array<int, 12> key() const {
         return {M, s_qkv, s_o, s_gu, s_dn, pps * 16 + att_warps, n_splits, n_dec, n_tiles, n_out,
-                (int)att_merge * 64 + (int)row_step * 32 + (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 +
+                (int)att_append * 128 + (int)att_merge * 64 + (int)row_step * 32 + (int)fuse_qkv * 16 + (int)fuse_gu_tc * 8 +
                     (int)fuse_swiglu * 4 + (int)embeds * 2 + (int)logits,
                 (int)prof};
     }
@@ -928,6 +930,9 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
         for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + p.pps - 1) / p.pps);
         const long long slots = (long long)(p.att_warps == 4 ? fa::kAttnCtasPerSm : 1) * ctx->n_sm;
         p.att_merge = p.n_splits > 1 && (ctx->fuse_epilogues & 4) && ctas <= slots;
+        // kernel (1) inside the attention kernel: steps of decode rows only (prefill tiles
+        // need q of every row), when the QKV GEMM does not finish it itself
+        p.att_append = (ctx->fuse_epilogues & 8) && n_tiles == 0 && p.n_dec == M && !p.fuse_qkv;
     }
     p.embeds = embeds;
     p.logits = logits;
@@ -1016,7 +1021,8 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
         } else {
             g.epilogue = fa::kEpiStoreF32; g.C = ctx->part;
             run_gemm(ctx, g);
-            fa::launch_qknorm_rope_append(a, s);
+            if (p.att_append) --n;   // kernel (1) runs inside the attention kernel
+            else fa::launch_qknorm_rope_append(a, s);
         }
         const bool prof_l = p.prof && (l == 0 || l == d.n_layers / 2 || l == d.n_layers - 1);
         if (prof_l) record_prof(ctx, 2 * l, capturing);
@@ -1030,6 +1036,10 @@ static int enqueue_step(fa_ctx* ctx, const StepPlan& p, bool capturing) {
             at.part_ml = ctx->att_pml; at.out16 = ctx->attn16; at.out16_lo = ctx->attn_lo; at.out32 = nullptr;
             at.err = ctx->err_dev;
             at.merge_cnt = p.att_merge ? ctx->att_cnt : nullptr;
+            if (p.att_append) {
+                at.fuse_append = 1;
+                at.app = a;
+            }
             fa::launch_paged_attention(at, s);
             ++n;
             if (p.n_splits > 1 && !p.att_merge) {

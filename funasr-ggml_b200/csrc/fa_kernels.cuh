@@ -88,6 +88,9 @@ struct AttnArgs {
     int* merge_cnt;          // [rows][Hkv] splits done per (row, KV head), zero between launches:
                              // the split that finishes last merges the head's splits itself;
                              // nullptr: the merge is launch_attn_combine's
+    int fuse_append;         // kernel (1) of the rows' KV heads runs here, from app (q unused,
+    AppendArgs app;          // rows 0..M-1): q of both query heads into shared memory, the token's
+                             // K / V into its page by the split that holds the page
 };
 size_t attn_smem_bytes();
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s);

@@ -35,28 +35,8 @@ __global__ void __launch_bounds__(256) qknorm_rope_append_kernel(AppendArgs a) {
     const int j = blockIdx.y * 8 + warp;          // head vector index in the qkv row
     const int n_vec = a.Hq + 2 * a.Hkv;
     if (j >= n_vec) return;
-    const int W = n_vec * D;
-
-    // sum of the split-K partials in partial order; 8 partials' loads in flight at a time
     float x[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) x[k] = 0.0f;
-    const float* base = a.qkv_part + (size_t)m * W + (size_t)j * D + lane;
-    const size_t stride = (size_t)a.M * W;
-    for (int s0 = 0; s0 < a.n_part; s0 += 8) {
-        float t[8][4];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (s0 + u < a.n_part)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) t[u][k] = base[(size_t)(s0 + u) * stride + 32 * k];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-            if (s0 + u < a.n_part)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) x[k] = __fadd_rn(x[k], t[u][k]);
-    }
-
+    qkv_head_sum(a, m, j, lane, x);
     qkv_head_finish(a, m, j, lane, x);
 }
 

@@ -178,6 +178,31 @@ __device__ __forceinline__ void qkv_head_apply_rows(const AppendArgs& a, const H
     }
 }
 
+// The head vector j of row m summed over the QKV GEMM's split-K partials, in partial
+// order with 8 partials' loads in flight at a time (lane l: dims l, l+32, l+64, l+96):
+// kernel (1)'s input, wherever kernel (1) runs.
+__device__ __forceinline__ void qkv_head_sum(const AppendArgs& a, int m, int j, int lane, float (&x)[4]) {
+    constexpr int D = 128;
+    const int W = (a.Hq + 2 * a.Hkv) * D;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) x[k] = 0.0f;
+    const float* base = a.qkv_part + (size_t)m * W + (size_t)j * D + lane;
+    const size_t stride = (size_t)a.M * W;
+    for (int s0 = 0; s0 < a.n_part; s0 += 8) {
+        float t[8][4];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (s0 + u < a.n_part)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) t[u][k] = base[(size_t)(s0 + u) * stride + 32 * k];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (s0 + u < a.n_part)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) x[k] = __fadd_rn(x[k], t[u][k]);
+    }
+}
+
 __device__ __forceinline__ void qkv_head_finish(const AppendArgs& a, int m, int j, int lane, float (&x)[4]) {
     const HeadRowMeta h = qkv_head_meta(a, m, j, lane);
     qkv_head_apply(a, h, m, j, lane, x);

@@ -16,6 +16,7 @@
 // Roofline: HBM. Algorithmic bytes per (row, layer) = n_kv * 8 heads * 2 * 128 * 2 B
 // = n_kv * 4096 B; compute is 4 flop per byte read.
 #include "fa_kernels.cuh"
+#include "k_append.cuh"
 #include "k_attn_body.cuh"
 #include "funasr_dec.h"
 
@@ -64,7 +65,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_a
             for (int s = 0; s < kAttnStages; ++s) mbar_init(&S.bars[w][s], 1);
         fence_mbar_init();
     }
-    if (threadIdx.x < D) {
+    if (!a.fuse_append && threadIdx.x < D) {
         const float* qg = a.q + ((size_t)m * a.Hq + 2 * h) * D;
         S.q[0][threadIdx.x] = qg[threadIdx.x] * attn::kLog2e;
         S.q[1][threadIdx.x] = qg[D + threadIdx.x] * attn::kLog2e;
@@ -76,7 +77,38 @@ __global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_a
     const size_t page_elems = (size_t)a.Hkv * attn::TILE_HALVES;
     const __half* head_base = a.pool_layer + (size_t)h * attn::TILE_HALVES;
     const int issued = attn::warp_issue_first(S, bt, p_begin, nw, head_base, page_elems, warp, lane);
-    attn::warp_pages(a, S, bt, p_begin, nw, issued, n_kv, head_base, page_elems, nullptr, -1, 0, warp, lane);
+    const __half* patch = nullptr;
+    int patch_i = -1;
+    if (a.fuse_append) {
+        // kernel (1) for this KV head while the first pages are in flight: warps 0 and 1
+        // the two query heads (into shared memory), warps 2 and 3 the K and V heads when
+        // this split holds the token's page (written to the page, and kept to patch this
+        // CTA's copy of it, which may have been taken before the write)
+        __shared__ __align__(16) __half newkv[2 * D];
+        const int p_last = n_row_pages - 1;
+        const bool owner = p_last >= p_begin && p_last < p_end;
+        if (warp < 4 && (warp < 2 || owner)) {
+            const int j = warp < 2 ? 2 * h + warp : (warp == 2 ? a.Hq + h : a.Hq + a.Hkv + h);
+            float x[4];
+            qkv_head_sum(a.app, m, j, lane, x);
+            const HeadRowMeta meta = qkv_head_meta(a.app, m, j, lane);
+            qkv_head_apply(a.app, meta, m, j, lane, x, warp < 2 ? S.q[warp] : nullptr,
+                           warp < 2 ? nullptr : newkv + (warp - 2) * D);
+        }
+        __syncthreads();
+        if (threadIdx.x < D) {
+            S.q[0][threadIdx.x] = S.q[0][threadIdx.x] * attn::kLog2e;
+            S.q[1][threadIdx.x] = S.q[1][threadIdx.x] * attn::kLog2e;
+        }
+        __syncthreads();
+        if (owner) {
+            const int rel = p_last - p_begin;
+            patch = newkv;
+            patch_i = warp == rel % NW ? rel / NW : -1;
+        }
+    }
+    attn::warp_pages(a, S, bt, p_begin, nw, issued, n_kv, head_base, page_elems, patch, patch_i,
+                     (n_kv - 1) % kPageTokens, warp, lane);
     __syncthreads();
     if (threadIdx.x < D)
         attn::merge_warps(S, threadIdx.x, [&](int hq, float M, float L, float O) {

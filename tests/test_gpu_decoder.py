@@ -218,6 +218,43 @@ def test_attention_split_merge_in_kernel_gives_the_same_bits(torch_cuda, small_w
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("n_seq,lo,hi", [(2, 20, 60), (3, 14, 18), (4, 300, 2001), (16, 200, 700), (128, 300, 2001)])
+def test_kernel1_inside_attention_gives_the_same_bits(torch_cuda, small_w, n_seq, lo, hi):
+    """Kernel (1) (q/k RMSNorm, RoPE, K/V append) run by the decode attention kernel (fused
+    mask bit 3): every split computes its KV head's two query heads, the split holding the
+    token's page writes K and V to the page and patches its copy of it. Against the separate
+    launch over six steps (contexts crossing page boundaries, one and several splits, one
+    and several waves, 2 rows on the CUDA-core GEMM): one launch fewer per layer, identical
+    logits and tokens, and identical K/V pages in every layer."""
+    w = small_w
+    rng = np.random.default_rng(91 + n_seq)
+    lens = rng.integers(lo, hi, n_seq)
+    first = rng.integers(0, CFG["vocab"], n_seq)
+    out = {}
+    for mask in (14, 6):
+        dec = _decoder(w, CFG, n_pages=n_seq * 130 + 16, max_seqs=n_seq, max_rows=n_seq)
+        dec.set_fused_epilogues(mask)
+        sids = [dec.seq_open(MAX_CTX) for _ in range(n_seq)]
+        for s, n in zip(sids, lens):
+            dec.kv_fill_synthetic(s, int(n), seed=int(n))
+        toks, lgs, ids = first, [], []
+        for _ in range(6):
+            toks, lg = dec.decode_step(sids, toks, want_logits=True)
+            lgs.append(lg)
+            ids.append(toks)
+        pages = np.concatenate([dec.block_table(x) for x in sids])
+        kv = [dec.kv_read_pages(l, pages) for l in range(CFG["n_layers"])]
+        out[mask] = (lgs, ids, kv, dec.step_launches())
+        dec.close()
+    assert out[6][3] - out[14][3] == CFG["n_layers"], (out[6][3], out[14][3])
+    for a, b in zip(out[14][0], out[6][0]):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    for a, b in zip(out[14][1], out[6][1]):
+        assert np.array_equal(a, b)
+    for l in range(CFG["n_layers"]):
+        assert np.array_equal(out[14][2][l], out[6][2][l]), f"layer {l} K/V pages differ"
+
+
 def test_pool_exhaustion_rolls_back(torch_cuda, small_w):
     dec = _decoder(small_w, CFG, n_pages=4)
     a = dec.seq_open(MAX_CTX)
