@@ -892,9 +892,10 @@ static bool skinny_rows(int variant, int M, int epilogue = fa::kEpiStoreF32, boo
 }
 
 // row_len: context length of each row given to the decode kernel (all rows, or the
-// rows outside prefill tiles); n_tiles: prefill tiles of the step.
+// rows outside prefill tiles); n_tiles: prefill tiles of the step; distinct: every row
+// belongs to a sequence of its own.
 static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, bool embeds, bool logits,
-                          int n_tiles = 0) {
+                          int n_tiles = 0, bool distinct = false) {
     const fa_model_desc& d = ctx->d;
     StepPlan p;
     p.M = M;
@@ -930,9 +931,11 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
         for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + p.pps - 1) / p.pps);
         const long long slots = (long long)(p.att_warps == 4 ? fa::kAttnCtasPerSm : 1) * ctx->n_sm;
         p.att_merge = p.n_splits > 1 && (ctx->fuse_epilogues & 4) && ctas <= slots;
-        // kernel (1) inside the attention kernel: steps of decode rows only (prefill tiles
-        // need q of every row), when the QKV GEMM does not finish it itself
-        p.att_append = (ctx->fuse_epilogues & 8) && n_tiles == 0 && p.n_dec == M && !p.fuse_qkv;
+        // kernel (1) inside the attention kernel: steps of decode rows of distinct sequences
+        // only (prefill tiles need q of every row; a row attends over the K / V that earlier
+        // rows of its sequence append in the same step, which another CTA would be writing),
+        // when the QKV GEMM does not finish kernel (1) itself
+        p.att_append = (ctx->fuse_epilogues & 8) && n_tiles == 0 && p.n_dec == M && distinct && !p.fuse_qkv;
     }
     p.embeds = embeds;
     p.logits = logits;
@@ -1320,7 +1323,7 @@ extern "C" int fa_forward_rows(fa_ctx* ctx, int n_rows, const int* seq_ids, cons
         // embeddings only: x is the input; with token ids too, rows with id -1 keep their embedding
         const bool x_ready = embeds && !token_ids;
         StepPlan p = n_tiles > 0 ? make_plan(ctx, M, dec_len, x_ready, logits != nullptr, n_tiles)
-                                 : make_plan(ctx, M, row_len, x_ready, logits != nullptr);
+                                 : make_plan(ctx, M, row_len, x_ready, logits != nullptr, 0, (int)extra.size() == M);
         p.n_out = n_out < 0 ? -1 : n_out;
         if (int r = run_step(ctx, p)) return r;
         if (Mo > 0)
@@ -1416,7 +1419,7 @@ extern "C" int fa_generate(fa_ctx* ctx, int n_seq, const int* seq_ids, const int
         std::vector<int> row_len(n_seq);
         for (int k = 0; k < n_steps; ++k) {
             for (int i = 0; i < n_seq; ++i) row_len[i] = base[i] + k + 1;
-            StepPlan p = make_plan(ctx, n_seq, row_len, false, false);
+            StepPlan p = make_plan(ctx, n_seq, row_len, false, false, 0, true);   // distinct: checked above
             if (int r = run_step(ctx, p)) return r;
             FA_CK(cudaMemcpyAsync(ctx->h_next + (size_t)k * n_seq, ctx->next_dev, sizeof(int) * n_seq,
                                   cudaMemcpyDeviceToHost, ctx->stream));
