@@ -300,7 +300,8 @@ class Decoder:
         """Mask of ops finished inside the kernel before them: 1 = QKV GEMM with per-head
         norm/RoPE/append, 2 = gate/up GEMM with SwiGLU, 4 = decode attention merging its
         splits itself when its CTAs fit in one wave, 8 = decode attention running the per-head
-        norm/RoPE/append itself (default 14); 0 = separate kernels. Same bits either way."""
+        norm/RoPE/append itself in steps of distinct sequences (default 14); 0 = separate
+        kernels. Same bits either way."""
         self._c(lib().fa_set_fused_epilogues(self.ctx, int(mask)))
 
     def set_row_step(self, enable: bool):
