@@ -930,12 +930,18 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
         long long ctas = 0;
         for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + p.pps - 1) / p.pps);
         const long long slots = (long long)(p.att_warps == 4 ? fa::kAttnCtasPerSm : 1) * ctx->n_sm;
-        p.att_merge = p.n_splits > 1 && (ctx->fuse_epilogues & 4) && ctas <= slots;
+        const bool one_wave = ctas <= slots;
+        p.att_merge = p.n_splits > 1 && (ctx->fuse_epilogues & 4) && one_wave;
         // kernel (1) inside the attention kernel: steps of decode rows of distinct sequences
         // only (prefill tiles need q of every row; a row attends over the K / V that earlier
         // rows of its sequence append in the same step, which another CTA would be writing),
-        // when the QKV GEMM does not finish kernel (1) itself
-        p.att_append = (ctx->fuse_epilogues & 8) && n_tiles == 0 && p.n_dec == M && distinct && !p.fuse_qkv;
+        // when the QKV GEMM does not finish kernel (1) itself, and when the attention CTAs fit
+        // in one wave: then the per-CTA kernel (1) work overlaps the first page copies once;
+        // over several waves every wave repeats it (measured: 2 rows x 256 tokens 1.094 ->
+        // 1.045 ms per step, 16 x 1024 1.615 -> 1.587; 128 x 2048 no gain, the attention
+        // launch 5.6 us longer)
+        p.att_append = (ctx->fuse_epilogues & 8) && n_tiles == 0 && p.n_dec == M && distinct && !p.fuse_qkv &&
+                       one_wave;
     }
     p.embeds = embeds;
     p.logits = logits;

@@ -33,8 +33,10 @@ template <int NW>
 using AttnSmem = attn::Smem<kAttnStages, NW>;
 
 // NW warps per CTA: 4 (3 CTAs per SM) in general, 8 for steps of at most kAttnWideRows rows,
-// whose few CTAs would otherwise leave each warp several pages in a row.
-template <int NW>
+// whose few CTAs would otherwise leave each warp several pages in a row. APPEND: the form
+// that runs kernel (1) itself (AttnArgs::fuse_append); a separate instance, so that the
+// plain form's page loop carries no patch branch.
+template <int NW, bool APPEND>
 __global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_attn_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     AttnSmem<NW>& S = *reinterpret_cast<AttnSmem<NW>*>(smem_raw);
@@ -65,7 +67,7 @@ __global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_a
             for (int s = 0; s < kAttnStages; ++s) mbar_init(&S.bars[w][s], 1);
         fence_mbar_init();
     }
-    if (!a.fuse_append && threadIdx.x < D) {
+    if (!APPEND && threadIdx.x < D) {
         const float* qg = a.q + ((size_t)m * a.Hq + 2 * h) * D;
         S.q[0][threadIdx.x] = qg[threadIdx.x] * attn::kLog2e;
         S.q[1][threadIdx.x] = qg[D + threadIdx.x] * attn::kLog2e;
@@ -78,8 +80,8 @@ __global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_a
     const __half* head_base = a.pool_layer + (size_t)h * attn::TILE_HALVES;
     const int issued = attn::warp_issue_first(S, bt, p_begin, nw, head_base, page_elems, warp, lane);
     const __half* patch = nullptr;
-    int patch_i = -1;
-    if (a.fuse_append) {
+    int patch_i = -1, patch_t = 0;
+    if constexpr (APPEND) {
         // kernel (1) for this KV head while the first pages are in flight: warps 0 and 1
         // the two query heads (into shared memory), warps 2 and 3 the K and V heads when
         // this split holds the token's page (written to the page, and kept to patch this
@@ -105,10 +107,11 @@ __global__ void __launch_bounds__(NW * 32, NW == 4 ? kAttnCtasPerSm : 1) paged_a
             const int rel = p_last - p_begin;
             patch = newkv;
             patch_i = warp == rel % NW ? rel / NW : -1;
+            patch_t = (n_kv - 1) % kPageTokens;
         }
     }
-    attn::warp_pages(a, S, bt, p_begin, nw, issued, n_kv, head_base, page_elems, patch, patch_i,
-                     (n_kv - 1) % kPageTokens, warp, lane);
+    attn::warp_pages(a, S, bt, p_begin, nw, issued, n_kv, head_base, page_elems, patch, patch_i, patch_t, warp,
+                     lane);
     __syncthreads();
     if (threadIdx.x < D)
         attn::merge_warps(S, threadIdx.x, [&](int hq, float M, float L, float O) {
@@ -159,18 +162,30 @@ int attn_warps(int M) { return M <= kAttnWideRows ? 8 : 4; }
 
 // Opt the kernels into their dynamic shared memory on the current device.
 cudaError_t configure_attention() {
-    const cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)sizeof(AttnSmem<4>));
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(paged_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)sizeof(AttnSmem<8>));
+    cudaError_t e = cudaFuncSetAttribute(paged_attn_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(AttnSmem<4>));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(paged_attn_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(AttnSmem<4>));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(paged_attn_kernel<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(AttnSmem<8>));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(paged_attn_kernel<8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(AttnSmem<8>));
+    return e;
 }
 
 void launch_paged_attention(const AttnArgs& a, cudaStream_t s) {
     dim3 grid(a.n_splits, a.Hkv, a.M);
     const int warps = a.warps ? a.warps : attn_warps(a.M);
-    if (warps == 8) launch_k(paged_attn_kernel<8>, grid, dim3(256), sizeof(AttnSmem<8>), s, a);
-    else launch_k(paged_attn_kernel<4>, grid, dim3(128), sizeof(AttnSmem<4>), s, a);
+    if (warps == 8) {
+        if (a.fuse_append) launch_k(paged_attn_kernel<8, true>, grid, dim3(256), sizeof(AttnSmem<8>), s, a);
+        else launch_k(paged_attn_kernel<8, false>, grid, dim3(256), sizeof(AttnSmem<8>), s, a);
+    } else {
+        if (a.fuse_append) launch_k(paged_attn_kernel<4, true>, grid, dim3(128), sizeof(AttnSmem<4>), s, a);
+        else launch_k(paged_attn_kernel<4, false>, grid, dim3(128), sizeof(AttnSmem<4>), s, a);
+    }
 }
 
 void launch_attn_combine(const AttnArgs& a, cudaStream_t s) {

@@ -300,7 +300,7 @@ class Decoder:
         """Mask of ops finished inside the kernel before them: 1 = QKV GEMM with per-head
         norm/RoPE/append, 2 = gate/up GEMM with SwiGLU, 4 = decode attention merging its
         splits itself when its CTAs fit in one wave, 8 = decode attention running the per-head
-        norm/RoPE/append itself in steps of distinct sequences (default 14); 0 = separate
+        norm/RoPE/append itself in one-wave steps of distinct sequences (default 14); 0 = separate
         kernels. Same bits either way."""
         self._c(lib().fa_set_fused_epilogues(self.ctx, int(mask)))
 

@@ -127,8 +127,9 @@ FA_API int fa_set_gemm_variant(fa_ctx* ctx, int variant);
  * projection finishes SwiGLU the same way; bit 2 = decode attention with several splits
  * per row merges them in the attention kernel (the split that finishes last for a row and
  * KV head merges both query heads) instead of a merge launch; bit 3 = steps of decode rows
- * of distinct sequences run kernel (1) inside the attention kernel (every split computes
- * its KV head's query heads, the split holding the token's page appends K and V). Default
+ * of distinct sequences whose attention CTAs fit in one wave run kernel (1) inside the
+ * attention kernel (every split computes its KV head's query heads, the split holding the
+ * token's page appends K and V). Default
  * 14; 0 = separate
  * kernels. The results are the same bits either way. No counterpart in the reference
  * (ggml runs each node separately, compute/llm_ops_gpu.cpp:53-96,135-143,177-180). */

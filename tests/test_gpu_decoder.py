@@ -218,14 +218,16 @@ def test_attention_split_merge_in_kernel_gives_the_same_bits(torch_cuda, small_w
         assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("n_seq,lo,hi", [(2, 20, 60), (3, 14, 18), (4, 300, 2001), (16, 200, 700), (128, 300, 2001)])
-def test_kernel1_inside_attention_gives_the_same_bits(torch_cuda, small_w, n_seq, lo, hi):
+@pytest.mark.parametrize("n_seq,lo,hi,fused", [(2, 20, 60, True), (3, 14, 18, True), (4, 300, 2001, True),
+                                               (16, 200, 700, True), (128, 300, 2001, False)])
+def test_kernel1_inside_attention_gives_the_same_bits(torch_cuda, small_w, n_seq, lo, hi, fused):
     """Kernel (1) (q/k RMSNorm, RoPE, K/V append) run by the decode attention kernel (fused
     mask bit 3): every split computes its KV head's two query heads, the split holding the
     token's page writes K and V to the page and patches its copy of it. Against the separate
-    launch over six steps (contexts crossing page boundaries, one and several splits, one
-    and several waves, 2 rows on the CUDA-core GEMM): one launch fewer per layer, identical
-    logits and tokens, and identical K/V pages in every layer."""
+    launch over six steps (contexts crossing page boundaries, one split and up to 15, 2 rows
+    on the CUDA-core GEMM): one launch fewer per layer when the attention CTAs fit in one
+    wave, a launch of its own over several waves (128 rows), and identical logits, tokens and
+    K/V pages in every layer either way."""
     w = small_w
     rng = np.random.default_rng(91 + n_seq)
     lens = rng.integers(lo, hi, n_seq)
@@ -246,13 +248,37 @@ def test_kernel1_inside_attention_gives_the_same_bits(torch_cuda, small_w, n_seq
         kv = [dec.kv_read_pages(l, pages) for l in range(CFG["n_layers"])]
         out[mask] = (lgs, ids, kv, dec.step_launches())
         dec.close()
-    assert out[6][3] - out[14][3] == CFG["n_layers"], (out[6][3], out[14][3])
+    assert out[6][3] - out[14][3] == (CFG["n_layers"] if fused else 0), (out[6][3], out[14][3])
     for a, b in zip(out[14][0], out[6][0]):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
     for a, b in zip(out[14][1], out[6][1]):
         assert np.array_equal(a, b)
     for l in range(CFG["n_layers"]):
         assert np.array_equal(out[14][2][l], out[6][2][l]), f"layer {l} K/V pages differ"
+
+
+def test_kernel1_stays_a_launch_for_rows_of_one_sequence(torch_cuda, small_w):
+    """A forward whose rows include several of one sequence (4 prompts of 10 rows: runs too
+    short for the prefill tiles, so every row goes to the decode attention kernel) keeps
+    kernel (1) as a launch of its own under fused mask bit 3: a row attends over the K/V
+    that the earlier rows of its sequence append in the same forward. Same launch count and
+    the same logits bits as without the bit, twice in a row."""
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, CFG["vocab"], (4, 10))
+    out = {}
+    for mask in (14, 6):
+        dec = _decoder(small_w, CFG)
+        dec.set_fused_epilogues(mask)
+        sids = [dec.seq_open(MAX_CTX) for _ in range(4)]
+        lgs = []
+        for _ in range(2):
+            _, lg = dec.forward(np.repeat(sids, 10), tokens=prompt.reshape(-1), want_logits=True)
+            lgs.append(lg)
+        out[mask] = (lgs, dec.step_launches())
+        dec.close()
+    assert out[14][1] == out[6][1], (out[14][1], out[6][1])
+    for a, b in zip(out[14][0], out[6][0]):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
 def test_pool_exhaustion_rolls_back(torch_cuda, small_w):
