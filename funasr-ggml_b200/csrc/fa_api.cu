@@ -877,6 +877,33 @@ static void attention_split(const std::vector<int>& row_pages, int n_sm, int max
     if (warps_out) *warps_out = best_w;
 }
 
+// The decode attention of a step with rows of row_pages[i] pages: the split (attention_split,
+// CTA form chosen by the cost model) and what the attention kernel finishes itself under the
+// fused-op mask. Both fusions are taken only when the attention CTAs fit in one wave:
+//   merge  (bit 2): the split that counts its (row, KV head) last merges the splits; over
+//          several waves each CTA's count and the last split's merge hold back the next wave
+//          (measured: 4 rows x 2048 tokens 1.49 -> 1.45 ms per step, 16 x 1024 1.64 -> 1.61;
+//          64 and 128 rows x 2048 2-4 % slower);
+//   append (bit 3): kernel (1) for each CTA's KV head, whose per-CTA work then overlaps the
+//          first page copies once, where over several waves every wave repeats it (measured:
+//          2 rows x 256 tokens 1.094 -> 1.045 ms per step, 16 x 1024 1.615 -> 1.587; 128 x 2048
+//          no gain, the attention launch 5.6 us longer). The step adds its own conditions.
+struct AttnChoice {
+    int pps = 0, n_splits = 0, warps = 4;
+    bool merge = false, append = false;
+};
+static AttnChoice plan_attention(const std::vector<int>& row_pages, int n_sm, int max_splits, int mask) {
+    AttnChoice c;
+    attention_split(row_pages, n_sm, max_splits, &c.pps, &c.n_splits, &c.warps);
+    long long ctas = 0;
+    for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + c.pps - 1) / c.pps);
+    const long long slots = (long long)(c.warps == 4 ? fa::kAttnCtasPerSm : 1) * n_sm;
+    const bool one_wave = ctas <= slots;
+    c.merge = c.n_splits > 1 && (mask & 4) && one_wave;
+    c.append = (mask & 8) && one_wave;
+    return c;
+}
+
 // Whether a GEMM of M rows goes to the CUDA-core kernel under a GEMM variant.
 static bool gemv_rows(int variant, int M) {
     return (variant == 0 && M <= fa::kGemvAutoRows) || (variant == 3 && M <= fa::kGemvMaxRows);
@@ -922,26 +949,16 @@ static StepPlan make_plan(fa_ctx* ctx, int M, const std::vector<int>& row_len, b
         std::vector<int> row_pages(row_len.size());
         for (size_t i = 0; i < row_len.size(); ++i)
             row_pages[i] = (row_len[i] + fa::kPageTokens - 1) / fa::kPageTokens;
-        attention_split(row_pages, ctx->n_sm, ctx->att_max_splits, &p.pps, &p.n_splits, &p.att_warps);
-        // the split merge inside the attention kernel when its CTAs fit in one wave: then the
-        // merge launch is the cost it saves; over several waves each CTA's count and the last
-        // split's merge hold back the next wave (measured: 4 rows x 2048 tokens 1.49 -> 1.45
-        // ms per step, 16 x 1024 1.64 -> 1.61; 64 and 128 rows x 2048 2-4 % slower)
-        long long ctas = 0;
-        for (int pg : row_pages) ctas += (long long)kHkv * ((std::max(pg, 1) + p.pps - 1) / p.pps);
-        const long long slots = (long long)(p.att_warps == 4 ? fa::kAttnCtasPerSm : 1) * ctx->n_sm;
-        const bool one_wave = ctas <= slots;
-        p.att_merge = p.n_splits > 1 && (ctx->fuse_epilogues & 4) && one_wave;
+        const AttnChoice c = plan_attention(row_pages, ctx->n_sm, ctx->att_max_splits, ctx->fuse_epilogues);
+        p.pps = c.pps;
+        p.n_splits = c.n_splits;
+        p.att_warps = c.warps;
+        p.att_merge = c.merge;
         // kernel (1) inside the attention kernel: steps of decode rows of distinct sequences
         // only (prefill tiles need q of every row; a row attends over the K / V that earlier
         // rows of its sequence append in the same step, which another CTA would be writing),
-        // when the QKV GEMM does not finish kernel (1) itself, and when the attention CTAs fit
-        // in one wave: then the per-CTA kernel (1) work overlaps the first page copies once;
-        // over several waves every wave repeats it (measured: 2 rows x 256 tokens 1.094 ->
-        // 1.045 ms per step, 16 x 1024 1.615 -> 1.587; 128 x 2048 no gain, the attention
-        // launch 5.6 us longer)
-        p.att_append = (ctx->fuse_epilogues & 8) && n_tiles == 0 && p.n_dec == M && distinct && !p.fuse_qkv &&
-                       one_wave;
+        // when the QKV GEMM does not finish kernel (1) itself
+        p.att_append = c.append && n_tiles == 0 && p.n_dec == M && distinct && !p.fuse_qkv;
     }
     p.embeds = embeds;
     p.logits = logits;
@@ -1760,6 +1777,23 @@ extern "C" int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages
         row_pages[i] = (n_kv[i] + fa::kPageTokens - 1) / fa::kPageTokens;
     }
     attention_split(row_pages, n_sm, 64, pages_per_split, n_splits, nullptr, fa::attn_warps(M));
+    return FA_OK;
+}
+
+extern "C" int fa_step_attention_plan(const int* n_kv, int M, int n_sm, int mask, int* pages_per_split,
+                                      int* n_splits, int* warps, int* fused) {
+    if (!n_kv || M <= 0 || n_sm <= 0 || mask < 0 || mask > 15 || !pages_per_split || !n_splits || !warps || !fused)
+        return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_step_attention_plan: bad argument");
+    std::vector<int> row_pages((size_t)M);
+    for (int i = 0; i < M; ++i) {
+        if (n_kv[i] <= 0) return set_err(nullptr, FA_ERR_INVALID_ARG, "fa_step_attention_plan: n_kv must be > 0");
+        row_pages[i] = (n_kv[i] + fa::kPageTokens - 1) / fa::kPageTokens;
+    }
+    const AttnChoice c = plan_attention(row_pages, n_sm, 64, mask);
+    *pages_per_split = c.pps;
+    *n_splits = c.n_splits;
+    *warps = c.warps;
+    *fused = (c.merge ? 1 : 0) | (c.append ? 2 : 0);
     return FA_OK;
 }
 

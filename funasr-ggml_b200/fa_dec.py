@@ -154,6 +154,7 @@ def lib():
         "fa_load_gguf": ([_P, ctypes.c_char_p], _I),
         "fa_gguf_find_tensor": ([ctypes.c_char_p, ctypes.c_char_p, _P, _P, _P, _P], _I),
         "fa_op_attention_plan": ([_P, _I, _I, _P, _P], _I),
+        "fa_step_attention_plan": ([_P, _I, _I, _I, _P, _P, _P, _P], _I),
         "fa_op_gemm_plan": ([_I, _I, _I, _I, _I, _P], _I),
         "fa_op_wait_selftest": ([_I, _P, _P], _I),
         "fa_op_prefill_attention": ([_P, _I, _P, _P, _P, _I, _I, _P, _P, _I, _P, _P, _P, _P, _P], _I),
@@ -476,6 +477,18 @@ def op_attention_plan(n_kv, n_sm=148):
     pps, ns = ctypes.c_int(), ctypes.c_int()
     _check(lib().fa_op_attention_plan(a.ctypes.data, len(a), n_sm, ctypes.byref(pps), ctypes.byref(ns)))
     return pps.value, ns.value
+
+
+def step_attention_plan(n_kv, n_sm=148, mask=14):
+    """The decoder's attention plan for a step of decode rows with contexts n_kv under fused
+    mask `mask`: dict of pages_per_split, n_splits, warps, merge (the attention kernel merges
+    its splits) and append (it runs kernel (1) for rows of distinct sequences)."""
+    a = np.ascontiguousarray(n_kv, np.int32)
+    pps, ns, w, f = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    _check(lib().fa_step_attention_plan(a.ctypes.data, len(a), n_sm, int(mask), ctypes.byref(pps),
+                                        ctypes.byref(ns), ctypes.byref(w), ctypes.byref(f)))
+    return dict(pages_per_split=pps.value, n_splits=ns.value, warps=w.value, merge=bool(f.value & 1),
+                append=bool(f.value & 2))
 
 
 def op_prefill_attention(q, M, pos, slot, bt, bt_stride, n_pages, pool, tiles, n_tiles, out16=0, out32=0, err=0,

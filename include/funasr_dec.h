@@ -298,8 +298,18 @@ FA_API int fa_op_kv_gather(const uint16_t* pool_dev, int n_layers, int n_pages, 
  * pages_per_split * n_splits does not cover sets error bit 8 and is not written; a page
  * id outside [0, n_pages) sets bit 2. */
 FA_API size_t fa_op_attention_scratch_bytes(int M, int n_splits);
-/* The split the decoder uses for rows with contexts n_kv[M] on n_sm SMs (host only). */
+/* The split for fa_op_paged_attention's CTA form (8 warps for up to 2 rows, else 4) and rows
+ * with contexts n_kv[M] on n_sm SMs (host only). */
 FA_API int fa_op_attention_plan(const int* n_kv, int M, int n_sm, int* pages_per_split, int* n_splits);
+/* The decoder's attention plan for a step of M decode rows with contexts n_kv[M] on n_sm SMs
+ * under fused-op mask `mask` (fa_set_fused_epilogues; host only): pages per split, splits,
+ * warps per CTA (the cost model picks 4 or 8 up to 64 rows), and in *fused bit 0 whether the
+ * attention kernel merges its splits itself, bit 1 whether it runs kernel (1) itself (for
+ * rows of distinct sequences, unless the QKV GEMM finishes kernel (1)). Both fusions need the
+ * attention CTAs to fit in one wave. No counterpart in the reference (ggml plans nothing of
+ * this: compute/llm_ops_gpu.cpp:98-143 builds one attention subgraph per token). */
+FA_API int fa_step_attention_plan(const int* n_kv, int M, int n_sm, int mask, int* pages_per_split, int* n_splits,
+                                  int* warps, int* fused);
 FA_API int fa_op_paged_attention(const float* q_dev, int M, const int* pos_dev, const int* slot_dev,
                           const int* block_table_dev, int bt_stride, int n_pages, const uint16_t* pool_layer_dev,
                           int pages_per_split, int n_splits, void* scratch_dev, uint16_t* out16_dev,

@@ -150,3 +150,29 @@ def test_attention_planner_choices():
     assert fa_dec.op_attention_plan(np.array([112], np.int32))[1] == 1
     pps, ns = fa_dec.op_attention_plan(np.array([4096], np.int32))
     assert ns > 1 and pps * ns >= 4096 // 16
+
+
+def test_step_attention_plan_fuses_only_in_one_wave():
+    """What the decode attention kernel finishes itself (host only): the split merge (bit 2 of
+    the fused-op mask) and kernel (1) (bit 3) only when its CTAs fit in one wave. 128 rows at
+    2048 tokens (3 splits x 8 KV heads x 128 rows = 3,072 CTAs, seven waves) keep both as
+    launches; 16 rows at 1025 tokens (384 CTAs of 4 warps, 3 per SM on 148 SMs), 2 rows at
+    257 and one row at 113 (8 warps, one CTA per SM) fuse; mask 6 leaves kernel (1) a launch."""
+    plan = lambda M, n_kv, mask=14: fa_dec.step_attention_plan(np.full(M, n_kv, np.int32), mask=mask)
+    p = plan(128, 2048)
+    assert (p["pages_per_split"], p["n_splits"], p["warps"]) == (44, 3, 4)
+    assert not p["merge"] and not p["append"]
+    assert not plan(64, 2048)["append"]
+    p = plan(16, 1025)
+    assert p["n_splits"] == 3 and p["warps"] == 4 and p["merge"] and p["append"]
+    p = plan(2, 257)
+    assert p["merge"] and p["append"]
+    p = plan(1, 113)
+    assert (p["n_splits"], p["warps"]) == (1, 8) and not p["merge"] and p["append"]
+    p = plan(16, 1025, mask=6)
+    assert p["merge"] and not p["append"]
+    assert not any(plan(16, 1025, mask=0)[k] for k in ("merge", "append"))
+    for bad in (lambda: plan(4, 100, mask=16), lambda: plan(4, 0)):
+        with pytest.raises(fa_dec.FaError):
+            bad()
+
